@@ -1,0 +1,756 @@
+// loom_oracle.cpp -- TEST INFRASTRUCTURE ONLY: CPU restatement of the
+// reference's CPU kernels for the quantized MoE forward path. It checks the
+// CUDA backend and is the timed CPU baseline; the product never links it.
+//
+// Source followed (ch4r10t33r/loom):
+//   src/gguf/ggml.zig   block formats, quantizers, int8-activation matvecs,
+//                       batched matmul, dequantRow, the row-parallel pool
+//   src/gguf/moe.zig    route()
+//   src/core/tensor.zig softmax / silu / sigmoid / swiglu / rmsnorm
+//   src/gguf/llama.zig  denseFFN + moeRun's weighted accumulation
+//   src/gguf/deepseek.zig  moeFfnBlockRouted / moeFfnBlock call sites
+// Build with -ffp-contract=off (no FMA contraction, as Zig) and no fast-math.
+#include "loom_oracle.h"
+
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <thread>
+#include <vector>
+
+namespace {
+
+constexpr size_t QK_0 = 32;
+constexpr size_t QK_K = 256;
+constexpr size_t Q4_0_BLOCK = 18;
+constexpr size_t Q8_0_BLOCK = 34;
+constexpr size_t Q4_K_BLOCK = 144;
+constexpr size_t Q6_K_BLOCK = 210;
+
+// ggml.zig:260 f16FromBytes: exact widening of an IEEE half.
+inline float f16_bits_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1Fu;
+    uint32_t man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {  // subnormal half -> normal float
+            int e = -1;
+            do {
+                man <<= 1;
+                e++;
+            } while ((man & 0x400u) == 0);
+            man &= 0x3FFu;
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+inline float f16at(const uint8_t *p) { return f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
+
+inline bool finitef(float v) { return std::isfinite(v); }
+
+// ggml.zig:1067-1074 toI8Saturating: non-finite -> 0, round half away from
+// zero, saturate at +-127.
+inline int8_t to_i8_sat(float v) {
+    if (!finitef(v)) return 0;
+    float r = std::round(v);
+    if (r >= 127.0f) return 127;
+    if (r <= -127.0f) return -127;
+    return (int8_t)(int)r;
+}
+
+// ggml.zig:1332-1340 scaleMinK4
+inline void scale_min_k4(int j, const uint8_t *s, int &sc, int &mn) {
+    if (j < 4) {
+        sc = s[j] & 63;
+        mn = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// ---- quantizers ---------------------------------------------------------------
+
+// ggml.zig:776-801 quantizeX256 (one 256-wide block)
+void quant256(const float *src, int8_t *q, float *d_out, int32_t *bsum) {
+    float amax = 0.0f;
+    for (size_t i = 0; i < QK_K; i++)
+        if (finitef(src[i])) amax = std::fmax(amax, std::fabs(src[i]));
+    const float d = amax / 127.0f;
+    const float inv = (d != 0.0f && finitef(d)) ? 1.0f / d : 0.0f;
+    for (size_t s = 0; s < QK_K / 16; s++) {
+        int32_t sum = 0;
+        for (size_t i = 0; i < 16; i++) {
+            int8_t v = to_i8_sat(src[s * 16 + i] * inv);
+            q[s * 16 + i] = v;
+            sum += v;
+        }
+        bsum[s] = sum;
+    }
+    *d_out = finitef(d) ? d : 0.0f;
+}
+
+// ggml.zig:1077-1100 quantizeX (one 32-wide block)
+void quant32(const float *src, int8_t *q, float *d_out, int32_t *sum_out) {
+    float amax = 0.0f;
+    for (size_t i = 0; i < QK_0; i++)
+        if (finitef(src[i])) amax = std::fmax(amax, std::fabs(src[i]));
+    const float d = amax / 127.0f;
+    const float inv = (d != 0.0f && finitef(d)) ? 1.0f / d : 0.0f;
+    int32_t sum = 0;
+    for (size_t i = 0; i < QK_0; i++) {
+        int8_t v = to_i8_sat(src[i] * inv);
+        q[i] = v;
+        sum += v;
+    }
+    *d_out = finitef(d) ? d : 0.0f;
+    *sum_out = sum;
+}
+
+struct XQ {  // quantized activation vector
+    std::vector<int8_t> q;
+    std::vector<float> d;
+    std::vector<int32_t> s;  // bsum16 (K) or sum32 (Q4_0/Q8_0)
+};
+
+bool uses_q8k(int t) { return t == OR_Q4_K || t == OR_Q6_K; }
+
+void quantize(int t, const float *x, size_t cols, XQ &xq) {
+    xq.q.resize(cols);
+    if (uses_q8k(t)) {
+        xq.d.resize(cols / QK_K);
+        xq.s.resize(cols / 16);
+        for (size_t b = 0; b < cols / QK_K; b++)
+            quant256(x + b * QK_K, &xq.q[b * QK_K], &xq.d[b], &xq.s[b * 16]);
+    } else {
+        xq.d.resize(cols / QK_0);
+        xq.s.resize(cols / QK_0);
+        for (size_t b = 0; b < cols / QK_0; b++)
+            quant32(x + b * QK_0, &xq.q[b * QK_0], &xq.d[b], &xq.s[b]);
+    }
+}
+
+// ---- per-block dots ------------------------------------------------------------
+
+inline int32_t dot32(const int8_t *w, const int8_t *x) {
+    int32_t s = 0;
+    for (int i = 0; i < 32; i++) s += (int32_t)w[i] * (int32_t)x[i];
+    return s;
+}
+
+// ggml.zig:882-997 kDecode (q4_k) + :1002-1021 kBlockDot
+inline float q4k_block_dot(const uint8_t *blk, const int8_t *xq, float xd, const int32_t *bsum) {
+    const float d = f16at(blk);
+    const float dmin = f16at(blk + 2);
+    const uint8_t *scales = blk + 4;
+    const uint8_t *qs = blk + 16;
+    int32_t isum = 0, msum = 0;
+    int8_t w[32];
+    for (int j = 0; j < 8; j++) {
+        int sc, mn;
+        scale_min_k4(j, scales, sc, mn);
+        const uint8_t *src = qs + (j / 2) * 32;
+        if (j & 1)
+            for (int i = 0; i < 32; i++) w[i] = (int8_t)(src[i] >> 4);
+        else
+            for (int i = 0; i < 32; i++) w[i] = (int8_t)(src[i] & 0x0F);
+        isum += sc * dot32(w, xq + j * 32);
+        msum += mn * (bsum[2 * j] + bsum[2 * j + 1]);
+    }
+    return xd * (d * (float)isum - dmin * (float)msum);
+}
+
+// ggml.zig:882-997 kDecode (q6_k) + kBlockDot (no min)
+inline float q6k_block_dot(const uint8_t *blk, const int8_t *xq, float xd) {
+    const uint8_t *ql_all = blk;
+    const uint8_t *qh_all = blk + 128;
+    const int8_t *sc = (const int8_t *)(blk + 192);
+    const float d = f16at(blk + 208);
+    int32_t isum = 0;
+    int8_t w[32];
+    for (int half = 0; half < 2; half++) {
+        const uint8_t *ql = ql_all + half * 64;
+        const uint8_t *qh = qh_all + half * 32;
+        for (int gg = 0; gg < 4; gg++) {
+            for (int i = 0; i < 32; i++) {
+                uint8_t a = ql[i], bb = ql[32 + i], h = qh[i];
+                uint8_t q;
+                switch (gg) {
+                    case 0: q = (a & 0x0F) | ((h & 3) << 4); break;
+                    case 1: q = (bb & 0x0F) | (((h >> 2) & 3) << 4); break;
+                    case 2: q = (a >> 4) | (((h >> 4) & 3) << 4); break;
+                    default: q = (bb >> 4) | (((h >> 6) & 3) << 4); break;
+                }
+                w[i] = (int8_t)((int)q - 32);
+            }
+            const int g = half * 4 + gg;
+            int32_t lo = 0, hi = 0;
+            for (int i = 0; i < 16; i++) lo += (int32_t)w[i] * xq[g * 32 + i];
+            for (int i = 16; i < 32; i++) hi += (int32_t)w[i] * xq[g * 32 + i];
+            isum += lo * (int32_t)sc[2 * g] + hi * (int32_t)sc[2 * g + 1];
+        }
+    }
+    return xd * d * (float)isum;
+}
+
+// ggml.zig:1196-1223 matvecQ40Int, one block
+inline float q40_block_dot(const uint8_t *blk, const int8_t *xq, float xd) {
+    const float d = f16at(blk);
+    const uint8_t *qs = blk + 2;
+    int32_t dot = 0, sum = 0;
+    for (int i = 0; i < 16; i++) {
+        int32_t lo = qs[i] & 0x0F, hi = qs[i] >> 4;
+        dot += lo * (int32_t)xq[i] + hi * (int32_t)xq[i + 16];
+        sum += (int32_t)xq[i] + (int32_t)xq[i + 16];
+    }
+    return d * xd * (float)(dot - 8 * sum);
+}
+
+// ggml.zig:1277-1294 matvecQ80Int, one block
+inline float q80_block_dot(const uint8_t *blk, const int8_t *xq, float xd) {
+    const float d = f16at(blk);
+    return d * xd * (float)dot32((const int8_t *)(blk + 2), xq);
+}
+
+// One row against a quantized activation.
+float row_dot(int t, const uint8_t *row, const XQ &xq, size_t cols) {
+    float acc = 0.0f;
+    switch (t) {
+        case OR_Q4_K:
+            for (size_t b = 0; b < cols / QK_K; b++)
+                acc += q4k_block_dot(row + b * Q4_K_BLOCK, &xq.q[b * QK_K], xq.d[b], &xq.s[b * 16]);
+            break;
+        case OR_Q6_K:
+            for (size_t b = 0; b < cols / QK_K; b++)
+                acc += q6k_block_dot(row + b * Q6_K_BLOCK, &xq.q[b * QK_K], xq.d[b]);
+            break;
+        case OR_Q4_0:
+            for (size_t b = 0; b < cols / QK_0; b++)
+                acc += q40_block_dot(row + b * Q4_0_BLOCK, &xq.q[b * QK_0], xq.d[b]);
+            break;
+        case OR_Q8_0:
+            for (size_t b = 0; b < cols / QK_0; b++)
+                acc += q80_block_dot(row + b * Q8_0_BLOCK, &xq.q[b * QK_0], xq.d[b]);
+            break;
+    }
+    return acc;
+}
+
+// ---- pool (ggml.zig:279-398): spin workers, row chunks, submitter works ------
+
+struct Pool {
+    int n = 0;  // live workers (excluding the submitting thread)
+    std::vector<std::thread> threads;
+    std::atomic<bool> quit{false};
+    std::atomic<uint64_t> seq{0};
+    std::atomic<size_t> active{0};
+    std::atomic<size_t> cursor{0};
+    size_t rows = 0, chunk = 0;
+    const std::function<void(size_t, size_t)> *job = nullptr;
+};
+Pool pool;
+constexpr size_t MIN_ROWS_PER_THREAD = 64;  // ggml.zig:263
+constexpr uint32_t SPIN_BEFORE_YIELD = 40000;  // ggml.zig:268
+
+void run_chunks() {
+    for (;;) {
+        size_t start = pool.cursor.fetch_add(pool.chunk, std::memory_order_acq_rel);
+        if (start >= pool.rows) return;
+        size_t end = std::min(start + pool.chunk, pool.rows);
+        (*pool.job)(start, end);
+    }
+}
+
+void worker_main() {
+    uint64_t seen = 0;
+    uint32_t idle = 0;
+    for (;;) {
+        uint64_t s = pool.seq.load(std::memory_order_acquire);
+        if (s == seen) {
+            if (pool.quit.load(std::memory_order_acquire)) return;
+            if (++idle < SPIN_BEFORE_YIELD) {
+#if defined(__x86_64__)
+                __builtin_ia32_pause();
+#endif
+            } else {
+                std::this_thread::yield();
+            }
+            continue;
+        }
+        idle = 0;
+        seen = s;
+        if (pool.quit.load(std::memory_order_acquire)) return;
+        run_chunks();
+        pool.active.fetch_sub(1, std::memory_order_release);
+    }
+}
+
+// Row-parallel execution with the reference's chunking rule (ggml.zig:212-213):
+// chunk = max(64, ceil(rows / (2*(workers+1)))).  Row splitting is exact, so the
+// result is independent of the worker count.
+void parallel_rows(size_t rows, const std::function<void(size_t, size_t)> &fn) {
+    const int workers = pool.n;
+    if (workers == 0 || rows < 2 * MIN_ROWS_PER_THREAD) {
+        fn(0, rows);
+        return;
+    }
+    size_t per = (rows + (workers + 1) * 2 - 1) / ((workers + 1) * 2);
+    if (per < MIN_ROWS_PER_THREAD) per = MIN_ROWS_PER_THREAD;
+    pool.job = &fn;
+    pool.rows = rows;
+    pool.chunk = per;
+    pool.cursor.store(0, std::memory_order_relaxed);
+    pool.active.store(workers, std::memory_order_relaxed);
+    pool.seq.fetch_add(1, std::memory_order_release);
+    run_chunks();
+    uint32_t spins = 0;
+    while (pool.active.load(std::memory_order_acquire) != 0) {
+        if (++spins < SPIN_BEFORE_YIELD) {
+#if defined(__x86_64__)
+            __builtin_ia32_pause();
+#endif
+        } else {
+            std::this_thread::yield();
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t or_block_elems(int t) {
+    switch (t) {
+        case OR_F32: case OR_F16: return 1;
+        case OR_Q4_0: case OR_Q8_0: return QK_0;
+        case OR_Q4_K: case OR_Q6_K: return QK_K;
+    }
+    return 0;
+}
+
+size_t or_block_bytes(int t) {
+    switch (t) {
+        case OR_F32: return 4;
+        case OR_F16: return 2;
+        case OR_Q4_0: return Q4_0_BLOCK;
+        case OR_Q8_0: return Q8_0_BLOCK;
+        case OR_Q4_K: return Q4_K_BLOCK;
+        case OR_Q6_K: return Q6_K_BLOCK;
+    }
+    return 0;
+}
+
+size_t or_row_bytes(int t, size_t n) {
+    size_t be = or_block_elems(t);
+    if (be == 0) return 0;
+    return (n / be) * or_block_bytes(t);
+}
+
+void or_parallel_begin(int n) {
+    if (pool.n != 0) return;
+    int want = n > 32 ? 32 : n;  // MAX_WORKERS, ggml.zig:259
+    if (want <= 1) return;
+    pool.quit.store(false);
+    pool.seq.store(0);
+    pool.active.store(0);
+    for (int i = 0; i + 1 < want; i++) pool.threads.emplace_back(worker_main);
+    pool.n = (int)pool.threads.size();
+}
+
+void or_parallel_end(void) {
+    if (pool.n == 0) return;
+    pool.quit.store(true, std::memory_order_release);
+    pool.seq.fetch_add(1, std::memory_order_release);
+    for (auto &t : pool.threads) t.join();
+    pool.threads.clear();
+    pool.n = 0;
+}
+
+int or_pool_workers(void) { return pool.n; }
+
+// ggml.zig:198-217 dotF32: four 8-lane accumulators, 32 per step, an 8-wide
+// tail into acc0, then (acc0+acc1+acc2+acc3) reduced lane 0..7 in order
+// (@reduce(.Add) lowered as an ordered reduction), then a scalar tail.
+float or_dot_f32(const float *a, const float *b, size_t n) {
+    float acc[4][8] = {};
+    size_t i = 0;
+    for (; i + 32 <= n; i += 32)
+        for (int k = 0; k < 4; k++)
+            for (int j = 0; j < 8; j++) acc[k][j] += a[i + 8 * k + j] * b[i + 8 * k + j];
+    for (; i + 8 <= n; i += 8)
+        for (int j = 0; j < 8; j++) acc[0][j] += a[i + j] * b[i + j];
+    float v[8];
+    for (int j = 0; j < 8; j++) v[j] = ((acc[0][j] + acc[1][j]) + acc[2][j]) + acc[3][j];
+    float r = v[0];
+    for (int j = 1; j < 8; j++) r += v[j];
+    for (; i < n; i++) r += a[i] * b[i];
+    return r;
+}
+
+void or_quantize_x256(const float *x, size_t cols, int8_t *q, float *d, int32_t *bsum) {
+    for (size_t b = 0; b < cols / QK_K; b++) quant256(x + b * QK_K, q + b * QK_K, d + b, bsum + b * 16);
+}
+
+void or_quantize_x32(const float *x, size_t cols, int8_t *q, float *d, int32_t *sum) {
+    for (size_t b = 0; b < cols / QK_0; b++) quant32(x + b * QK_0, q + b * QK_0, d + b, sum + b);
+}
+
+// ggml.zig:1739-1857 dequantRow (f32, q4_0, q8_0, q4_k, q6_k)
+int or_dequant_row(int t, float *out, const uint8_t *data, size_t r, size_t cols) {
+    const size_t rb = or_row_bytes(t, cols);
+    const uint8_t *row = data + r * rb;
+    switch (t) {
+        case OR_F32:
+            std::memcpy(out, row, cols * 4);
+            return 0;
+        case OR_Q4_K:  // dequantBlockQ4K, ggml.zig:1342-1374
+            for (size_t b = 0; b < cols / QK_K; b++) {
+                const uint8_t *blk = row + b * Q4_K_BLOCK;
+                const float d = f16at(blk), dmin = f16at(blk + 2);
+                const uint8_t *scales = blk + 4, *qs = blk + 16;
+                float *v = out + b * QK_K;
+                for (int j = 0; j < 4; j++) {
+                    int sc, mn;
+                    scale_min_k4(2 * j, scales, sc, mn);
+                    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+                    scale_min_k4(2 * j + 1, scales, sc, mn);
+                    const float d2 = d * (float)sc, m2 = dmin * (float)mn;
+                    for (int l = 0; l < 32; l++) {
+                        v[64 * j + l] = d1 * (float)(qs[32 * j + l] & 0x0F) - m1;
+                        v[64 * j + 32 + l] = d2 * (float)(qs[32 * j + l] >> 4) - m2;
+                    }
+                }
+            }
+            return 0;
+        case OR_Q6_K:  // dequantBlockQ6K, ggml.zig:1420-1474
+            for (size_t b = 0; b < cols / QK_K; b++) {
+                const uint8_t *blk = row + b * Q6_K_BLOCK;
+                const float d = f16at(blk + 208);
+                float *v = out + b * QK_K;
+                for (int n = 0; n < 2; n++) {
+                    const uint8_t *ql = blk + 64 * n, *qh = blk + 128 + 32 * n;
+                    const int8_t *sc = (const int8_t *)(blk + 192 + 8 * n);
+                    for (int l = 0; l < 32; l++) {
+                        const int is = l / 16;
+                        const float s1 = d * (float)sc[is], s2 = d * (float)sc[is + 2];
+                        const float s3 = d * (float)sc[is + 4], s4 = d * (float)sc[is + 6];
+                        const uint8_t a = ql[l], bb = ql[l + 32], h = qh[l];
+                        const float q1 = (float)((a & 0x0F) | ((h & 3) << 4));
+                        const float q2 = (float)((bb & 0x0F) | (((h >> 2) & 3) << 4));
+                        const float q3 = (float)((a >> 4) | (((h >> 4) & 3) << 4));
+                        const float q4 = (float)((bb >> 4) | (((h >> 6) & 3) << 4));
+                        v[128 * n + l] = s1 * (q1 - 32.0f);
+                        v[128 * n + l + 32] = s2 * (q2 - 32.0f);
+                        v[128 * n + l + 64] = s3 * (q3 - 32.0f);
+                        v[128 * n + l + 96] = s4 * (q4 - 32.0f);
+                    }
+                }
+            }
+            return 0;
+        case OR_Q4_0:
+            for (size_t b = 0; b < cols / QK_0; b++) {
+                const uint8_t *blk = row + b * Q4_0_BLOCK;
+                const float s = f16at(blk);
+                for (int j = 0; j < 16; j++) {
+                    out[b * 32 + j] = (float)((int)(blk[2 + j] & 0x0F) - 8) * s;
+                    out[b * 32 + j + 16] = (float)((int)(blk[2 + j] >> 4) - 8) * s;
+                }
+            }
+            return 0;
+        case OR_Q8_0:
+            for (size_t b = 0; b < cols / QK_0; b++) {
+                const uint8_t *blk = row + b * Q8_0_BLOCK;
+                const float s = f16at(blk);
+                for (int j = 0; j < 32; j++) out[b * 32 + j] = (float)(int8_t)blk[2 + j] * s;
+            }
+            return 0;
+    }
+    return -1;
+}
+
+// ggml.zig:602-659 matvec/dispatch: the activation is quantized once per call
+// (matvecK256 :1024, matvecQ40Int :1196, matvecQ80Int :1277); rows are
+// independent dots, split over the pool.
+int or_matvec(int t, float *out, const uint8_t *data, const float *x, size_t rows, size_t cols) {
+    if (t == OR_F32) {
+        const float *w = (const float *)data;
+        parallel_rows(rows, [&](size_t r0, size_t r1) {
+            for (size_t r = r0; r < r1; r++) out[r] = or_dot_f32(w + r * cols, x, cols);
+        });
+        return 0;
+    }
+    if (t != OR_Q4_K && t != OR_Q6_K && t != OR_Q4_0 && t != OR_Q8_0) return -1;
+    if (cols % or_block_elems(t) != 0) return -1;
+    XQ xq;
+    quantize(t, x, cols, xq);
+    const size_t rb = or_row_bytes(t, cols);
+    parallel_rows(rows, [&](size_t r0, size_t r1) {
+        for (size_t r = r0; r < r1; r++) out[r] = row_dot(t, data + r * rb, xq, cols);
+    });
+    return 0;
+}
+
+// ggml.zig:504-563 matmul: out[k*rows + r]; bit-identical to n matvecs
+// (the reference's own invariant, test ggml.zig:2132). Each token's activation
+// is quantized once; every row is decoded against all n tokens.
+int or_matmul(int t, float *out, const uint8_t *data, const float *xs, size_t n, size_t rows, size_t cols) {
+    if (t == OR_F32) {
+        for (size_t k = 0; k < n; k++) or_matvec(t, out + k * rows, data, xs + k * cols, rows, cols);
+        return 0;
+    }
+    if (t != OR_Q4_K && t != OR_Q6_K && t != OR_Q4_0 && t != OR_Q8_0) return -1;
+    std::vector<XQ> xq(n);
+    for (size_t k = 0; k < n; k++) quantize(t, xs + k * cols, cols, xq[k]);
+    const size_t rb = or_row_bytes(t, cols);
+    parallel_rows(rows, [&](size_t r0, size_t r1) {
+        for (size_t r = r0; r < r1; r++)
+            for (size_t k = 0; k < n; k++) out[k * rows + r] = row_dot(t, data + r * rb, xq[k], cols);
+    });
+    return 0;
+}
+
+// tensor.zig:18-28
+void or_softmax(float *x, size_t n) {
+    float m = -INFINITY;
+    for (size_t i = 0; i < n; i++) m = std::fmax(m, x[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        x[i] = std::exp(x[i] - m);
+        sum += x[i];
+    }
+    const float inv = 1.0f / sum;
+    for (size_t i = 0; i < n; i++) x[i] *= inv;
+}
+
+float or_silu(float x) { return x / (1.0f + std::exp(-x)); }      // tensor.zig:30
+float or_sigmoid(float x) { return 1.0f / (1.0f + std::exp(-x)); }  // tensor.zig:34
+
+// tensor.zig:9-15
+void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps) {
+    float ss = 0.0f;
+    for (size_t i = 0; i < n; i++) ss += x[i] * x[i];
+    const float scale = 1.0f / std::sqrt(ss / (float)n + eps);
+    for (size_t i = 0; i < n; i++) out[i] = x[i] * scale * w[i];
+}
+
+// moe.zig:106-158 route
+int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
+             int weights_norm, float weights_scale, uint32_t *ids, float *gates) {
+    if (n_expert > 1024 || n_used > 64 || n_used > n_expert) return -1;  // MAX_EXPERTS/MAX_SELECTED, moe.zig:48-49
+    float scores[1024], choice[1024];
+    bool used[1024] = {};
+    if (gating == 2) {
+        for (size_t i = 0; i < n_expert; i++) scores[i] = or_sigmoid(logits[i]);
+    } else {
+        std::memcpy(scores, logits, n_expert * 4);
+        if (gating == 1) or_softmax(scores, n_expert);
+    }
+    std::memcpy(choice, scores, n_expert * 4);
+    if (bias)
+        for (size_t i = 0; i < n_expert; i++) choice[i] += bias[i];
+    for (size_t k = 0; k < n_used; k++) {
+        size_t best = 0;
+        float best_v = -INFINITY;
+        for (size_t e = 0; e < n_expert; e++) {
+            if (!used[e] && choice[e] > best_v) {
+                best_v = choice[e];
+                best = e;
+            }
+        }
+        used[best] = true;
+        ids[k] = (uint32_t)best;
+        gates[k] = scores[best];
+    }
+    if (gating == 3) or_softmax(gates, n_used);
+    if (weights_norm) {
+        float sum = 0.0f;
+        for (size_t k = 0; k < n_used; k++) sum += gates[k];
+        const float denom = std::fmax(sum, 6.103515625e-5f);
+        for (size_t k = 0; k < n_used; k++) gates[k] /= denom;
+    }
+    if (weights_scale != 1.0f)
+        for (size_t k = 0; k < n_used; k++) gates[k] *= weights_scale;
+    return 0;
+}
+
+// llama.zig:952-958 denseFFN then moeRun's `acc += gate * out` (:1397).
+static int dense_ffn(const or_expert &e, const float *normed, size_t dim, float *ffn_out,
+                     std::vector<float> &g, std::vector<float> &u) {
+    g.resize(e.ffn);
+    u.resize(e.ffn);
+    if (or_matvec(e.gate_type, g.data(), e.gate, normed, e.ffn, dim)) return -1;
+    if (or_matvec(e.up_type, u.data(), e.up, normed, e.ffn, dim)) return -1;
+    for (size_t i = 0; i < e.ffn; i++) g[i] = or_silu(g[i]) * u[i];  // tensor.zig:53 swiglu
+    if (or_matvec(e.down_type, ffn_out, e.down, g.data(), dim, e.ffn)) return -1;
+    return 0;
+}
+
+int or_moe_ffn_block(const float *normed, size_t dim, const or_expert *experts, size_t n, float *out) {
+    std::vector<float> g, u, v(dim);
+    for (size_t i = 0; i < dim; i++) out[i] = 0.0f;
+    for (size_t k = 0; k < n; k++) {
+        if (dense_ffn(experts[k], normed, dim, v.data(), g, u)) return -1;
+        for (size_t i = 0; i < dim; i++) out[i] += experts[k].weight * v[i];
+    }
+    return 0;
+}
+
+int or_moe_ffn_routed(const float *normed, size_t dim, const float *logits, const float *bias,
+                      int gate_type, const uint8_t *gate3d, int up_type, const uint8_t *up3d,
+                      int down_type, const uint8_t *down3d, size_t ffn,
+                      const int *shexp_types, const uint8_t *const *shexp, size_t shexp_ffn,
+                      size_t n_expert, size_t n_used, int gating_sigmoid, int weights_norm,
+                      float weights_scale, float *out) {
+    uint32_t ids[64];
+    float gates[64];
+    if (or_route(logits, bias, n_expert, n_used, gating_sigmoid ? 2 : 1, weights_norm, weights_scale, ids, gates))
+        return -1;
+    const size_t gp = ffn * or_row_bytes(gate_type, dim);
+    const size_t up_ = ffn * or_row_bytes(up_type, dim);
+    const size_t dp = dim * or_row_bytes(down_type, ffn);
+    std::vector<or_expert> ex(n_used);
+    for (size_t k = 0; k < n_used; k++) {
+        ex[k] = or_expert{gate_type, up_type, down_type, gate3d + ids[k] * gp, up3d + ids[k] * up_,
+                          down3d + ids[k] * dp, gates[k], ffn};
+    }
+    if (or_moe_ffn_block(normed, dim, ex.data(), n_used, out)) return -1;
+    if (shexp) {  // deepseek.zig:1498-1508: shared expert, added plainly
+        or_expert se{shexp_types[0], shexp_types[1], shexp_types[2], shexp[0], shexp[1], shexp[2], 1.0f, shexp_ffn};
+        std::vector<float> g, u, v(dim);
+        if (dense_ffn(se, normed, dim, v.data(), g, u)) return -1;
+        for (size_t i = 0; i < dim; i++) out[i] += v[i];
+    }
+    return 0;
+}
+
+int or_moe_layer(const float *x, size_t T, size_t dim, const float *router_w, int gate_type,
+                 const uint8_t *gate3d, int up_type, const uint8_t *up3d, int down_type,
+                 const uint8_t *down3d, size_t ffn, size_t n_expert, size_t n_used, int gating,
+                 int weights_norm, float weights_scale, float *out, uint32_t *ids_out) {
+    std::vector<float> logits(n_expert);
+    uint32_t ids[64];
+    float gates[64];
+    const size_t gp = ffn * or_row_bytes(gate_type, dim);
+    const size_t up_ = ffn * or_row_bytes(up_type, dim);
+    const size_t dp = dim * or_row_bytes(down_type, ffn);
+    std::vector<or_expert> ex(n_used);
+    for (size_t t = 0; t < T; t++) {
+        const float *xt = x + t * dim;
+        or_matvec(OR_F32, logits.data(), (const uint8_t *)router_w, xt, n_expert, dim);
+        if (or_route(logits.data(), nullptr, n_expert, n_used, gating, weights_norm, weights_scale, ids, gates))
+            return -1;
+        for (size_t k = 0; k < n_used; k++) {
+            if (ids_out) ids_out[t * n_used + k] = ids[k];
+            ex[k] = or_expert{gate_type, up_type, down_type, gate3d + ids[k] * gp, up3d + ids[k] * up_,
+                              down3d + ids[k] * dp, gates[k], ffn};
+        }
+        if (or_moe_ffn_block(xt, dim, ex.data(), n_used, out + t * dim)) return -1;
+    }
+    return 0;
+}
+
+// ---- seeded synthetic tensors -------------------------------------------------
+// Counter-based: word(seed, i) = splitmix64(seed * K + i). A block b of a
+// quantized tensor draws words [b*16, b*16+16)... (see synth_block).
+
+static inline uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static inline uint64_t word(uint64_t seed, uint64_t i) { return splitmix64(seed * 0xD1B54A32D192ED03ull + i); }
+static inline float unit24(uint64_t w) { return (float)(w >> 40) * (1.0f / 16777216.0f); }
+
+uint16_t or_f32_to_f16_rne(float f) {
+    uint32_t b;
+    std::memcpy(&b, &f, 4);
+    uint32_t sign = (b >> 16) & 0x8000u;
+    int32_t e = (int32_t)((b >> 23) & 0xFF) - 127 + 15;
+    uint32_t m = b & 0x7FFFFFu;
+    if (e <= 0 || e >= 31) return (uint16_t)sign;  // generator only emits normal halves
+    uint32_t h = ((uint32_t)e << 10) | (m >> 13);
+    uint32_t rem = m & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)(sign | h);
+}
+float or_f16_to_f32(uint16_t h) { return f16_bits_to_f32(h); }
+
+// words per block: enough for the largest block (210 B) plus two scale words
+static constexpr uint64_t WPB = 32;
+
+static inline void put_bytes(uint8_t *dst, size_t n, uint64_t seed, uint64_t w0) {
+    for (size_t i = 0; i < n; i += 8) {
+        uint64_t w = word(seed, w0 + i / 8);
+        for (size_t j = 0; j < 8 && i + j < n; j++) dst[i + j] = (uint8_t)(w >> (8 * j));
+    }
+}
+static inline uint16_t rand_scale(uint64_t w, float lo, float span) {
+    float u = unit24(w);
+    float a = span * u;
+    float d = lo + a;
+    return or_f32_to_f16_rne(d);
+}
+
+void or_synth(int type, void *out, uint64_t blk0, uint64_t nblk, uint64_t seed, float sigma) {
+    uint8_t *o = (uint8_t *)out;
+    for (uint64_t i = 0; i < nblk; i++) {
+        const uint64_t b = blk0 + i;
+        const uint64_t w0 = b * WPB;
+        switch (type) {
+            case OR_F32: {
+                uint64_t w[3] = {word(seed, w0), word(seed, w0 + 1), word(seed, w0 + 2)};
+                float s = 0.0f;
+                for (int k = 0; k < 12; k++) s += (float)((w[k / 4] >> (16 * (k % 4))) & 0xFFFF) * (1.0f / 65536.0f);
+                float v = (s - 6.0f) * sigma;
+                std::memcpy(o + i * 4, &v, 4);
+                break;
+            }
+            case OR_Q4_K: {
+                uint8_t *blk = o + i * Q4_K_BLOCK;
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                uint16_t dm = rand_scale(word(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8; blk[2] = dm & 0xFF; blk[3] = dm >> 8;
+                put_bytes(blk + 4, 140, seed, w0 + 2);
+                break;
+            }
+            case OR_Q6_K: {
+                uint8_t *blk = o + i * Q6_K_BLOCK;
+                put_bytes(blk, 192, seed, w0 + 2);
+                uint8_t sc[16];
+                put_bytes(sc, 16, seed, w0 + 26);
+                for (int k = 0; k < 16; k++) blk[192 + k] = (uint8_t)(int8_t)((int)(sc[k] % 64) - 32);
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                blk[208] = d & 0xFF; blk[209] = d >> 8;
+                break;
+            }
+            case OR_Q4_0: {
+                uint8_t *blk = o + i * Q4_0_BLOCK;
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 1.9e-2f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8;
+                put_bytes(blk + 2, 16, seed, w0 + 2);
+                break;
+            }
+            case OR_Q8_0: {
+                uint8_t *blk = o + i * Q8_0_BLOCK;
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8;
+                put_bytes(blk + 2, 32, seed, w0 + 2);
+                break;
+            }
+        }
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,99 @@
+/*
+ * loom_oracle.h -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A CPU restatement, in plain C++, of the reference's CPU kernels for the
+ * quantized MoE forward path (ch4r10t33r/loom, Zig). It is the checker the
+ * CUDA backend is compared against and the timed CPU baseline; it is never
+ * linked into, called by or shipped with the product library.
+ *
+ * Every function cites the reference file:line it restates. Floating-point
+ * operations follow the Zig source one rounding at a time (the build uses
+ * -ffp-contract=off: Zig does not contract a*b-c into an FMA).
+ *
+ * Parity is pinned against the reference's own known-answer tests
+ * (src/gguf/ggml.zig:1906-2210, src/gguf/moe.zig:210-262), which the CPU test
+ * suite replays against this library.
+ */
+#ifndef LOOM_ORACLE_H
+#define LOOM_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids, src/gguf/ggml.zig:23-45 */
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q6_K = 14 };
+
+size_t or_row_bytes(int type, size_t n);          /* ggml.zig:103 rowBytes */
+size_t or_block_elems(int type);                  /* ggml.zig:128 blockElems */
+size_t or_block_bytes(int type);                  /* ggml.zig:157 blockBytes */
+
+/* worker pool, ggml.zig:279-398 (parallelBegin/parallelEnd) */
+void or_parallel_begin(int n);
+void or_parallel_end(void);
+int or_pool_workers(void);
+
+/* kernels */
+int or_dequant_row(int type, float *out, const uint8_t *data, size_t r, size_t cols);      /* ggml.zig:1739 */
+int or_matvec(int type, float *out, const uint8_t *data, const float *x, size_t rows, size_t cols); /* ggml.zig:602 */
+int or_matmul(int type, float *out, const uint8_t *data, const float *xs, size_t n, size_t rows, size_t cols); /* ggml.zig:504 */
+float or_dot_f32(const float *a, const float *b, size_t n);                               /* ggml.zig:198 dotF32 */
+
+/* activation quantizers. ggml.zig:776 quantizeX256: q[cols], d[cols/256], bsum[cols/16];
+ * ggml.zig:1077 quantizeX: q[cols], d[cols/32], sum[cols/32] */
+void or_quantize_x256(const float *x, size_t cols, int8_t *q, float *d, int32_t *bsum);
+void or_quantize_x32(const float *x, size_t cols, int8_t *q, float *d, int32_t *sum);
+
+/* elementwise, src/core/tensor.zig:9-57 */
+void or_softmax(float *x, size_t n);
+float or_silu(float x);
+float or_sigmoid(float x);
+void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps);
+
+/* router, src/gguf/moe.zig:106-158. gating: 1 softmax, 2 sigmoid, 3 softmax_topk */
+int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
+             int weights_norm, float weights_scale, uint32_t *ids, float *gates);
+
+/* One expert as the seam's ExpertRef (src/compute/cpu.zig:23). */
+typedef struct {
+    int gate_type, up_type, down_type;
+    const uint8_t *gate, *up, *down;
+    float weight;
+    size_t ffn;
+} or_expert;
+
+/* moeFfnBlock semantics: out = sum_k weight_k * FFN_k(normed), in list order
+ * (src/gguf/llama.zig:1363-1398 denseFFN + acc loop; deepseek.zig:1405-1442). */
+int or_moe_ffn_block(const float *normed, size_t dim, const or_expert *experts, size_t n, float *out);
+
+/* moeFfnBlockRouted semantics (deepseek.zig:1340-1380 with cpu route +
+ * the host loop): route(logits, bias) -> per selected expert plane FFN ->
+ * weighted sum in selection order -> + shared expert (plain add).
+ * 3D tensors are n_expert contiguous planes. */
+int or_moe_ffn_routed(const float *normed, size_t dim, const float *logits, const float *bias,
+                      int gate_type, const uint8_t *gate3d, int up_type, const uint8_t *up3d,
+                      int down_type, const uint8_t *down3d, size_t ffn,
+                      const int *shexp_types, const uint8_t *const *shexp, size_t shexp_ffn,
+                      size_t n_expert, size_t n_used, int gating_sigmoid, int weights_norm,
+                      float weights_scale, float *out);
+
+/* A whole MoE layer at T tokens (src/gguf/llama.zig:1262-1272 moeLayer):
+ * logits = matvec(f32 router, x_t); route; experts; out_t. Router f32 [n_expert][dim]. */
+int or_moe_layer(const float *x, size_t T, size_t dim, const float *router_w, int gate_type,
+                 const uint8_t *gate3d, int up_type, const uint8_t *up3d, int down_type,
+                 const uint8_t *down3d, size_t ffn, size_t n_expert, size_t n_used, int gating,
+                 int weights_norm, float weights_scale, float *out, uint32_t *ids_out);
+
+/* Seeded synthetic tensors (counter-based, the same generator the CUDA backend
+ * runs on the device): blocks [blk0, blk0+nblk) of a tensor of `type`. For
+ * OR_F32, "blocks" are elements ~ sigma * IrwinHall12. */
+void or_synth(int type, void *out, uint64_t blk0, uint64_t nblk, uint64_t seed, float sigma);
+uint16_t or_f32_to_f16_rne(float f);
+float or_f16_to_f32(uint16_t h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

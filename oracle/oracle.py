@@ -1,0 +1,223 @@
+"""ctypes view of the CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+The oracle (loom_oracle.cpp) restates the reference's CPU kernels
+(ch4r10t33r/loom src/gguf/ggml.zig, src/gguf/moe.zig, src/core/tensor.zig).
+Only the test suite, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+baseline leg use it, and only as the checker / the timed CPU reference. The
+product library never loads it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libloom_oracle.so")
+
+F32, F16, Q4_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 8, 12, 14
+BLOCK_ELEMS = {F32: 1, Q4_0: 32, Q8_0: 32, Q4_K: 256, Q6_K: 256}
+BLOCK_BYTES = {F32: 4, Q4_0: 18, Q8_0: 34, Q4_K: 144, Q6_K: 210}
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        vp, sz, fp = C.c_void_p, C.c_size_t, C.c_float
+        L.or_row_bytes.restype = sz
+        L.or_row_bytes.argtypes = [C.c_int, sz]
+        L.or_dequant_row.argtypes = [C.c_int, vp, vp, sz, sz]
+        L.or_matvec.argtypes = [C.c_int, vp, vp, vp, sz, sz]
+        L.or_matmul.argtypes = [C.c_int, vp, vp, vp, sz, sz, sz]
+        L.or_dot_f32.restype = fp
+        L.or_dot_f32.argtypes = [vp, vp, sz]
+        L.or_quantize_x256.argtypes = [vp, sz, vp, vp, vp]
+        L.or_quantize_x32.argtypes = [vp, sz, vp, vp, vp]
+        L.or_softmax.argtypes = [vp, sz]
+        L.or_silu.restype = fp
+        L.or_silu.argtypes = [fp]
+        L.or_sigmoid.restype = fp
+        L.or_sigmoid.argtypes = [fp]
+        L.or_route.argtypes = [vp, vp, sz, sz, C.c_int, C.c_int, fp, vp, vp]
+        L.or_moe_ffn_block.argtypes = [vp, sz, vp, sz, vp]
+        L.or_moe_ffn_routed.argtypes = [vp, sz, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, sz,
+                                        vp, vp, sz, sz, sz, C.c_int, C.c_int, fp, vp]
+        L.or_moe_layer.argtypes = [vp, sz, sz, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, sz, sz,
+                                   sz, C.c_int, C.c_int, fp, vp, vp]
+        L.or_synth.argtypes = [C.c_int, vp, C.c_uint64, C.c_uint64, C.c_uint64, fp]
+        L.or_f32_to_f16_rne.restype = C.c_uint16
+        L.or_f32_to_f16_rne.argtypes = [fp]
+        L.or_parallel_begin.argtypes = [C.c_int]
+        L.or_pool_workers.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p) if a is not None else None
+
+
+class Expert(C.Structure):
+    _fields_ = [("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+                ("weight", C.c_float), ("ffn", C.c_size_t)]
+
+
+def row_bytes(t: int, n: int) -> int:
+    return int(lib().or_row_bytes(t, n))
+
+
+def parallel_begin(n: int) -> None:
+    lib().or_parallel_begin(n)
+
+
+def parallel_end() -> None:
+    lib().or_parallel_end()
+
+
+def dequant_row(t, data, r, cols):
+    out = np.empty(cols, np.float32)
+    assert lib().or_dequant_row(t, _p(out), _p(data), r, cols) == 0
+    return out
+
+
+def dequant(t, data, rows, cols):
+    return np.stack([dequant_row(t, data, r, cols) for r in range(rows)])
+
+
+def matvec(t, data, x, rows, cols):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(rows, np.float32)
+    assert lib().or_matvec(t, _p(out), _p(data), _p(x), rows, cols) == 0
+    return out
+
+
+def matmul(t, data, xs, rows, cols):
+    xs = np.ascontiguousarray(xs, np.float32)
+    n = xs.shape[0]
+    out = np.empty((n, rows), np.float32)
+    assert lib().or_matmul(t, _p(out), _p(data), _p(xs), n, rows, cols) == 0
+    return out
+
+
+def dot_f32(a, b):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return float(lib().or_dot_f32(_p(a), _p(b), a.size))
+
+
+def quantize_x256(x):
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.size
+    q = np.empty(n, np.int8)
+    d = np.empty(n // 256, np.float32)
+    s = np.empty(n // 16, np.int32)
+    lib().or_quantize_x256(_p(x), n, _p(q), _p(d), _p(s))
+    return q, d, s
+
+
+def quantize_x32(x):
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.size
+    q = np.empty(n, np.int8)
+    d = np.empty(n // 32, np.float32)
+    s = np.empty(n // 32, np.int32)
+    lib().or_quantize_x32(_p(x), n, _p(q), _p(d), _p(s))
+    return q, d, s
+
+
+def softmax(x):
+    x = np.array(x, np.float32)
+    lib().or_softmax(_p(x), x.size)
+    return x
+
+
+def silu(v):
+    return float(lib().or_silu(v))
+
+
+def sigmoid(v):
+    return float(lib().or_sigmoid(v))
+
+
+def route(logits, n_used, gating=1, weights_norm=True, weights_scale=1.0, bias=None):
+    logits = np.ascontiguousarray(logits, np.float32)
+    bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    ids = np.empty(n_used, np.uint32)
+    gates = np.empty(n_used, np.float32)
+    rc = lib().or_route(_p(logits), _p(bias), logits.size, n_used, gating, int(weights_norm),
+                        weights_scale, _p(ids), _p(gates))
+    assert rc == 0
+    return ids, gates
+
+
+def moe_ffn_block(normed, experts, dim):
+    """experts: list of dicts {gate_type, up_type, down_type, gate, up, down, weight, ffn}."""
+    normed = np.ascontiguousarray(normed, np.float32)
+    arr = (Expert * len(experts))()
+    keep = []
+    for i, e in enumerate(experts):
+        keep += [e["gate"], e["up"], e["down"]]
+        arr[i] = Expert(e["gate_type"], e["up_type"], e["down_type"], _p(e["gate"]).value,
+                        _p(e["up"]).value, _p(e["down"]).value, e["weight"], e["ffn"])
+    out = np.empty(dim, np.float32)
+    assert lib().or_moe_ffn_block(_p(normed), dim, C.cast(arr, C.c_void_p), len(experts), _p(out)) == 0
+    return out
+
+
+def moe_ffn_routed(normed, logits, gate, up, down, ffn, n_used, gating_sigmoid=False,
+                   weights_norm=True, weights_scale=1.0, bias=None, shexp=None, shexp_ffn=0):
+    """gate/up/down: (type, bytes) of the full 3D tensors; shexp: 3 x (type, bytes) or None."""
+    normed = np.ascontiguousarray(normed, np.float32)
+    logits = np.ascontiguousarray(logits, np.float32)
+    dim = normed.size
+    out = np.empty(dim, np.float32)
+    st = sp = None
+    if shexp is not None:
+        st = (C.c_int * 3)(*[t for t, _ in shexp])
+        sp = (C.c_void_p * 3)(*[_p(b).value for _, b in shexp])
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    rc = lib().or_moe_ffn_routed(_p(normed), dim, _p(logits), _p(b), gate[0], _p(gate[1]), up[0],
+                                 _p(up[1]), down[0], _p(down[1]), ffn,
+                                 C.cast(st, C.c_void_p) if st else None,
+                                 C.cast(sp, C.c_void_p) if sp else None, shexp_ffn, logits.size,
+                                 n_used, int(gating_sigmoid), int(weights_norm), weights_scale, _p(out))
+    assert rc == 0
+    return out
+
+
+def moe_layer(x, router_w, gate, up, down, ffn, n_expert, n_used, gating=1, weights_norm=True,
+              weights_scale=1.0):
+    x = np.ascontiguousarray(x, np.float32)
+    T, dim = x.shape
+    out = np.empty((T, dim), np.float32)
+    ids = np.empty((T, n_used), np.uint32)
+    rc = lib().or_moe_layer(_p(x), T, dim, _p(router_w), gate[0], _p(gate[1]), up[0], _p(up[1]),
+                            down[0], _p(down[1]), ffn, n_expert, n_used, gating, int(weights_norm),
+                            weights_scale, _p(out), _p(ids))
+    assert rc == 0
+    return out, ids
+
+
+def synth(t, nblk, seed, blk0=0, sigma=1.0):
+    """Seeded synthetic blocks (same generator as the CUDA backend's device synth)."""
+    nbytes = nblk * BLOCK_BYTES[t]
+    out = np.empty(nbytes, np.uint8)
+    lib().or_synth(t, _p(out), blk0, nblk, seed, sigma)
+    return out.view(np.float32) if t == F32 else out
+
+
+def f32_to_f16_rne(v):
+    return int(lib().or_f32_to_f16_rne(v))

@@ -1,0 +1,199 @@
+"""Pins the CPU oracle against the reference's own known-answer tests and
+invariants (ch4r10t33r/loom src/gguf/ggml.zig:1906-2210, src/gguf/moe.zig:210-262,
+src/core/tensor.zig:77-101), and cross-checks it bit for bit against an
+independent numpy restatement of the block decoders."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from tests import npref
+
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "known_answers.json")))
+TYPES = [2, 8, 12, 14]  # q4_0, q8_0, q4_k, q6_k
+
+
+@pytest.mark.parametrize("case", GOLDEN["dequant"], ids=lambda c: c["name"])
+def test_known_answer_dequant(orc, case):
+    blk = np.array(case["block"], np.uint8)
+    vals = orc.dequant_row(case["type"], blk, 0, case["cols"])
+    if "expect_at" in case:
+        for i, v in case["expect_at"].items():
+            assert abs(vals[int(i)] - v) <= case["tol"]
+    if "expect_all" in case:
+        assert np.all(np.abs(vals - case["expect_all"]) <= case["tol"])
+    if "matvec_ones" in case:
+        out = orc.matvec(case["type"], blk, np.ones(case["cols"], np.float32), 1, case["cols"])
+        assert abs(out[0] - case["matvec_ones"]) <= case["matvec_tol"]
+
+
+@pytest.mark.parametrize("case", GOLDEN["route"], ids=lambda c: c["name"])
+def test_known_answer_route(orc, case):
+    ids, gates = orc.route(np.array(case["logits"], np.float32), case["n_used"], case["gating"],
+                           case["norm"], case["scale"],
+                           None if case["bias"] is None else np.array(case["bias"], np.float32))
+    if "expect_ids" in case:
+        assert list(ids) == case["expect_ids"]
+        np.testing.assert_allclose(gates, case["expect_gates"], atol=case["tol"], rtol=0)
+    if "expect_gate_sum" in case:
+        assert abs(gates.sum() - case["expect_gate_sum"]) <= case["tol"]
+    if "expect_gate_sum_below" in case:
+        assert gates.sum() < case["expect_gate_sum_below"]
+
+
+def test_known_answer_softmax(orc):
+    for case in GOLDEN["softmax"]:
+        assert abs(orc.softmax(case["x"]).sum() - case["expect_sum"]) <= case["tol"]
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_dequant_matches_numpy_restatement_bitexact(orc, t):
+    rng = np.random.default_rng(100 + t)
+    rows, cols = 5, 512
+    data = npref.random_blocks(rng, t, rows, cols)
+    got = orc.dequant(t, data, rows, cols)
+    want = npref.DEQUANT[t](data.tobytes(), rows, cols)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("t", TYPES + [0])
+def test_matvec_agrees_with_dequant_row(orc, t):
+    """ggml.zig:2021-2087: matvec vs dequant-then-dot, mass*0.01 for int8 kernels."""
+    rng = np.random.default_rng(0xC0FFEE)
+    cols, rows = 256, 3
+    x = ((rng.random(cols, dtype=np.float32) - 0.5) * 4.0).astype(np.float32)
+    if t == 0:
+        data = rng.standard_normal(rows * cols).astype(np.float32).view(np.uint8)
+    else:
+        data = npref.random_blocks(rng, t, rows, cols)
+    got = orc.matvec(t, data, x, rows, cols)
+    for r in range(rows):
+        row = orc.dequant_row(t, data, r, cols)
+        want = np.float32(0)
+        mass = np.float32(0)
+        for w, xv in zip(row, x):
+            want = np.float32(want + w * xv)
+            mass = np.float32(mass + abs(w * xv))
+        tol = mass * 0.01 if t != 0 else max(abs(want), abs(got[r])) * 1e-4 + 1e-3
+        assert abs(want - got[r]) <= tol, (t, r, got[r], want)
+
+
+def test_q40_q80_within_quant_error(orc):
+    """ggml.zig:1906-1936, with the test's own encoders."""
+    rng = np.random.default_rng(3)
+    rows, cols = 4, 64
+    wf = (rng.random((rows, cols), dtype=np.float32) - 0.5).astype(np.float32)
+    x = (rng.random(cols, dtype=np.float32) - 0.5).astype(np.float32)
+    ref = orc.matvec(0, wf.view(np.uint8).ravel(), x, rows, cols)
+    q4 = np.concatenate([npref.quantize_q40(wf[r]) for r in range(rows)])
+    q8 = np.concatenate([npref.quantize_q80(wf[r]) for r in range(rows)])
+    o4 = orc.matvec(2, q4, x, rows, cols)
+    o8 = orc.matvec(8, q8, x, rows, cols)
+    assert np.all(np.abs(o4 - ref) < 0.6)
+    assert np.all(np.abs(o8 - ref) < 0.05)
+
+
+@pytest.mark.parametrize("t", [12, 14, 8, 2, 0])
+def test_matmul_bit_identical_to_matvec(orc, t):
+    """ggml.zig:2132-2186 with per-token magnitudes differing."""
+    rng = np.random.default_rng(0x5EED)
+    cols, rows = 512, 133
+    if t == 0:
+        data = rng.standard_normal(rows * cols).astype(np.float32).view(np.uint8)
+    else:
+        data = npref.random_blocks(rng, t, rows, cols)
+    for n in (2, 3, 5, 8):
+        xs = np.stack([(rng.random(cols, dtype=np.float32) - 0.5) * (k + 1) for k in range(n)]).astype(np.float32)
+        want = np.stack([orc.matvec(t, data, xs[k], rows, cols) for k in range(n)])
+        got = orc.matmul(t, data, xs, rows, cols)
+        assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+
+
+def test_parallel_bit_identical(orc):
+    """ggml.zig:2089-2130: row splitting never perturbs an element."""
+    rng = np.random.default_rng(0xBEEF)
+    cols, rows = 256, 257
+    x = ((rng.random(cols, dtype=np.float32) - 0.5) * 4.0).astype(np.float32)
+    for t in (14, 12, 0):
+        data = (rng.standard_normal(rows * cols).astype(np.float32).view(np.uint8) if t == 0
+                else npref.random_blocks(rng, t, rows, cols))
+        serial = orc.matvec(t, data, x, rows, cols)
+        orc.parallel_begin(8)
+        try:
+            assert orc.lib().or_pool_workers() > 0
+            for _ in range(4):
+                par = orc.matvec(t, data, x, rows, cols)
+                assert np.array_equal(serial.view(np.uint32), par.view(np.uint32))
+        finally:
+            orc.parallel_end()
+
+
+def test_nonfinite_activations_do_not_trap(orc):
+    """ggml.zig:2188-2210."""
+    x = (np.arange(64) % 7).astype(np.float32)
+    x[0], x[1], x[2] = np.nan, np.inf, -np.inf
+    q, d, s = orc.quantize_x32(x)
+    assert np.all(np.isfinite(d)) and q.min() >= -127 and q.max() <= 127
+    y = np.full(32, np.nan, np.float32)
+    q, d, s = orc.quantize_x32(y)
+    assert d[0] == 0 and np.all(q == 0)
+    q, d, s = orc.quantize_x256(np.full(256, np.nan, np.float32))
+    assert d[0] == 0 and np.all(q == 0) and np.all(s == 0)
+
+
+def test_quantizer_rounding_half_away_from_zero(orc):
+    """toI8Saturating (ggml.zig:1067): @round is half away from zero."""
+    x = np.zeros(32, np.float32)
+    x[0] = 127.0  # d = 1, inv = 1
+    x[1], x[2], x[3], x[4] = 0.5, -0.5, 2.5, -2.5
+    q, d, s = orc.quantize_x32(x)
+    assert d[0] == 1.0
+    assert list(q[:5]) == [127, 1, -1, 3, -3]
+    assert s[0] == 127 + 1 - 1 + 3 - 3
+
+
+def test_route_ties_lowest_index_and_selection_order(orc):
+    """moe.zig:135-146: strict '>' keeps the first maximum."""
+    ids, _ = orc.route(np.array([1.0, 3.0, 3.0, 2.0, 3.0], np.float32), 3, 1, True, 1.0)
+    assert list(ids) == [1, 2, 4]
+
+
+def test_route_renorm_clamp(orc):
+    """moe.zig:149-153: divisor clamped to 6.103515625e-5."""
+    logits = np.full(4, -200.0, np.float32)
+    ids, gates = orc.route(logits, 2, 2, True, 1.0)  # sigmoid(-200) ~ 0
+    assert np.all(np.isfinite(gates))
+
+
+def test_moe_ffn_routed_equals_block(orc):
+    """moeFfnBlockRouted == route + moeFfnBlock over the selected planes."""
+    rng = np.random.default_rng(7)
+    dim, ffn, ne, k = 512, 256, 8, 3
+    gate = npref.random_blocks(rng, 12, ne * ffn, dim)
+    up = npref.random_blocks(rng, 12, ne * ffn, dim)
+    down = npref.random_blocks(rng, 14, ne * dim, ffn)
+    x = rng.standard_normal(dim).astype(np.float32)
+    logits = rng.standard_normal(ne).astype(np.float32)
+    out = orc.moe_ffn_routed(x, logits, (12, gate), (12, up), (14, down), ffn, k)
+    ids, gates = orc.route(logits, k)
+    gp, dp = ffn * orc.row_bytes(12, dim), dim * orc.row_bytes(14, ffn)
+    ex = [dict(gate_type=12, up_type=12, down_type=14, gate=gate[i * gp:(i + 1) * gp],
+               up=up[i * gp:(i + 1) * gp], down=down[i * dp:(i + 1) * dp], weight=float(g), ffn=ffn)
+          for i, g in zip(ids, gates)]
+    want = orc.moe_ffn_block(x, ex, dim)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def test_synth_matches_spec(orc):
+    """The seeded generator emits valid blocks with the configured scale ranges."""
+    b = orc.synth(12, 64, seed=11).reshape(64, 144)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32).ravel()
+    assert d.min() >= 0.00099 and d.max() <= 0.01001
+    b6 = orc.synth(14, 64, seed=11).reshape(64, 210)
+    sc = b6[:, 192:208].view(np.int8)
+    assert sc.min() >= -32 and sc.max() <= 31
+    f = orc.synth(0, 100000, seed=5, sigma=0.02)
+    assert abs(f.std() - 0.02) < 0.002 and abs(f.mean()) < 0.001
+    again = orc.synth(12, 8, seed=11, blk0=10)
+    assert np.array_equal(again, b[10:18].ravel())
