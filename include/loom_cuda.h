@@ -1,0 +1,187 @@
+/*
+ * loom_cuda.h -- C ABI of the B200 (sm_100a) CUDA compute backend for Loom's
+ * quantized Mixture-of-Experts forward path.
+ *
+ * The backend slots in behind Loom's comptime backend seam
+ * (src/compute/backend.zig:28-49) as a `cuda` arm, next to cpu/metal/vulkan.
+ * Each seam entry below cites the reference declaration it replaces; the Zig
+ * binding a maintainer adds is shown in INTEGRATION.md.
+ *
+ * Conventions (the seam's, src/compute/backend.zig and src/vulkan/backend.zig):
+ *  - Host slices are borrowed for the duration of the call; `out` is written
+ *    completely before a call returns LOOM_CUDA_OK.
+ *  - Weights are immutable host byte ranges (GGUF blocks, typically views into
+ *    an mmap). The backend keeps a device copy in its own layout, keyed by the
+ *    host pointer, byte length and type, or addressed inside a registered arena.
+ *  - Status codes: LOOM_CUDA_OK = done; LOOM_CUDA_DECLINED = the backend did
+ *    nothing (unsupported type/shape, not initialised) and the caller runs its
+ *    CPU path -- the seam's "return false"; LOOM_CUDA_ERROR = a CUDA error (the
+ *    message is in loom_cuda_last_error). No CPU fallback exists inside the
+ *    backend.
+ *  - One generation thread calls the backend; it is not reentrant.
+ *
+ * ggml type ids (src/gguf/ggml.zig:23-45): F32 0, Q4_0 2, Q8_0 8, Q4_K 12, Q6_K 14.
+ */
+#ifndef LOOM_CUDA_H
+#define LOOM_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LOOM_CUDA_OK 0
+#define LOOM_CUDA_DECLINED 1
+#define LOOM_CUDA_ERROR 2
+
+enum {
+    LOOM_F32 = 0,
+    LOOM_Q4_0 = 2,
+    LOOM_Q8_0 = 8,
+    LOOM_Q4_K = 12,
+    LOOM_Q6_K = 14
+};
+
+/* WeightRef, src/compute/cpu.zig:21: a weight tensor as the fused entries take it. */
+typedef struct {
+    int ggml_type;
+    const void *data;
+    size_t bytes;
+} loom_weight;
+
+/* ExpertRef, src/compute/cpu.zig:23: one expert of a MoE layer. */
+typedef struct {
+    loom_weight gate, up, down;
+    float weight;
+    size_t ffn;
+} loom_expert;
+
+/* RoutedCfg, src/compute/cpu.zig:61. */
+typedef struct {
+    size_t n_expert;
+    size_t n_used;
+    int gating_sigmoid;
+    int weights_norm;
+    float weights_scale;
+} loom_routed_cfg;
+
+/* ---- lifecycle ------------------------------------------------------------ */
+
+/* Select the device, create the backend's stream and scratch. Replaces the
+ * device bring-up the GPU backends do inside parallelBegin
+ * (src/compute/backend.zig:225-226, src/vulkan/backend.zig parallelBegin). */
+int loom_cuda_init(int device);
+void loom_cuda_shutdown(void);
+/* parallelBegin/parallelEnd (src/compute/backend.zig:225-226): init on first
+ * begin; end is a no-op (the device stays up for the process). */
+void loom_cuda_parallel_begin(size_t n);
+void loom_cuda_parallel_end(void);
+/* MAX_BATCH (src/compute/backend.zig:229): the largest matmul batch taken. */
+size_t loom_cuda_max_batch(void);
+
+/* registerArena (src/compute/backend.zig:98): remember a host mapping; false
+ * (DECLINED) when not initialised. Tensors inside it are then addressed by
+ * offset once materialised. */
+int loom_cuda_register_arena(const void *mem, size_t bytes);
+/* materializeArenas (src/compute/backend.zig:104): copy every registered
+ * mapping to the device; returns the bytes made resident (0 on failure, with
+ * the reason in loom_cuda_arena_error). */
+size_t loom_cuda_materialize_arenas(void);
+/* arena_error (src/compute/backend.zig:118). NULL when none. */
+const char *loom_cuda_arena_error(void);
+/* takeCmdBufCount (src/compute/backend.zig:112): seam submissions since the
+ * last call, then reset. */
+size_t loom_cuda_take_cmdbuf_count(void);
+/* Kernel launches issued by this library since load (never reset). */
+uint64_t loom_cuda_kernel_launches(void);
+/* Copy the last error message into buf (NUL-terminated); returns its length. */
+size_t loom_cuda_last_error(char *buf, size_t len);
+/* Drop every cached device copy of host weights (the Vulkan backend's
+ * clearWeightCache, src/vulkan/backend.zig:159-168). */
+void loom_cuda_clear_weight_cache(void);
+
+/* ---- seam ops (host buffers) ------------------------------------------------ */
+
+/* matvec (src/compute/backend.zig:62 -> cpu.zig:17 ggml.matvec, ggml.zig:602):
+ * out[r] = W[r] . x with int8-quantized activations, bit-identical to the CPU
+ * kernels for Q4_0/Q8_0/Q4_K/Q6_K and to dotF32 for F32. */
+int loom_cuda_matvec(int ggml_type, float *out, const void *w, size_t w_bytes, const float *x, size_t rows,
+                     size_t cols);
+/* matmul (src/compute/backend.zig:66 -> ggml.zig:504): out[k*rows + r],
+ * bit-identical to n matvecs. */
+int loom_cuda_matmul(int ggml_type, float *out, const void *w, size_t w_bytes, const float *xs, size_t n, size_t rows,
+                     size_t cols);
+/* dequantRow (src/compute/backend.zig:69 -> ggml.zig:1739), bit-exact. */
+int loom_cuda_dequant_row(int ggml_type, float *out, const void *w, size_t w_bytes, size_t r, size_t cols);
+/* moeRoute (src/compute/backend.zig:183 -> cpu.zig:86; moe.zig:106 route):
+ * ids_out/gates_out hold n_used entries. */
+int loom_cuda_moe_route(const float *logits, const float *bias, size_t n_expert, uint32_t *ids_out, float *gates_out,
+                        size_t n_used, int gating_sigmoid, int weights_norm, float weights_scale);
+/* moeFfnBlock (src/compute/backend.zig:104 -> cpu.zig:27): out = sum_k
+ * experts[k].weight * FFN_k(normed), in list order (llama.zig:1363-1398). */
+int loom_cuda_moe_ffn_block(const float *normed, size_t dim, const loom_expert *experts, size_t n_experts, float *out);
+/* moeFfnBlockRouted (src/compute/backend.zig:189 -> cpu.zig:68): route from
+ * logits, run the selected planes of the 3D tensors, weighted sum in selection
+ * order, plus the shared expert (shexp3 = NULL when absent), as ONE submission
+ * (deepseek.zig:1340-1380). */
+int loom_cuda_moe_ffn_routed(const float *normed, size_t dim, const float *logits, const float *bias,
+                             loom_weight gate, loom_weight up, loom_weight down, const loom_weight *shexp3, size_t ffn,
+                             size_t shexp_ffn, loom_routed_cfg cfg, float *out);
+
+/* ---- device-resident API (no counterpart in the reference's seam: the
+ * engine-side layer that keeps a whole model on the device) ---------------- */
+
+typedef uint64_t loom_tensor; /* handle to a device-resident tensor in the backend's layout; 0 = none */
+
+/* Upload host GGUF bytes (ggml_type blocks) into a device tensor. */
+int loom_cuda_tensor_upload(int ggml_type, const void *data, size_t bytes, loom_tensor *out);
+/* Create a tensor of nblocks blocks from the seeded counter-based generator
+ * (the synthetic-weight generator the benchmarks use; sigma is the f32
+ * standard deviation). */
+int loom_cuda_tensor_synth(int ggml_type, uint64_t nblocks, uint64_t seed, float sigma, loom_tensor *out);
+/* Read a tensor back as GGUF bytes (bytes = nblocks * block bytes). */
+int loom_cuda_tensor_download(loom_tensor t, void *dst, size_t bytes);
+int loom_cuda_tensor_free(loom_tensor t);
+/* Device bytes a tensor occupies. */
+size_t loom_cuda_tensor_device_bytes(loom_tensor t);
+
+/* One MoE layer over device-resident tensors. router: f32 [n_expert][dim]
+ * (0 = logits are supplied by the caller); gate/up: [n_local][ffn][dim];
+ * down: [n_local][dim][ffn]; shexp: 0 = none. For expert parallelism this rank
+ * holds experts [expert0, expert0 + n_local). */
+typedef struct {
+    size_t dim, ffn, n_expert, n_used;
+    int gating;        /* 1 softmax, 2 sigmoid, 3 softmax_topk (moe.zig:35-42) */
+    int weights_norm;
+    float weights_scale;
+    loom_tensor router, router_bias;
+    loom_tensor gate, up, down;
+    loom_tensor shexp_gate, shexp_up, shexp_down;
+    size_t shexp_ffn;
+    size_t expert0, n_local;
+} loom_moe_desc;
+
+/* d_x: device f32 [T][dim]; d_out: device f32 [T][dim] (d_out = d_residual +
+ * MoE(d_x) when d_residual is non-NULL). d_logits: optional device f32
+ * [T][n_expert] supplied by the caller instead of the router. d_ids: optional
+ * device u32 [T][n_used] that receives the routing. stream: a cudaStream_t or
+ * NULL for the backend's own stream. Asynchronous; launches only (no
+ * allocation) once loom_cuda_reserve covered T. */
+int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
+                          const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream);
+/* Size the scratch for layers up to (dim, ffn, n_expert, n_used) at T tokens so
+ * later forwards never allocate (required before CUDA-graph capture). */
+int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t n_used);
+/* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
+int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
+                            void *stream);
+/* Synchronize the backend's stream. */
+int loom_cuda_sync(void);
+/* The backend's stream (cudaStream_t). */
+void *loom_cuda_stream(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,116 @@
+"""Loads the in-tree CUDA backend library (libloom_cuda.so) and declares the
+C ABI of include/loom_cuda.h for ctypes.
+
+There is no fallback: if the library is missing or cannot be loaded, every
+entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libloom_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "loom_cuda.h")
+
+OK, DECLINED, ERROR = 0, 1, 2
+
+
+class LoomCudaError(RuntimeError):
+    pass
+
+
+class Weight(C.Structure):  # loom_weight (WeightRef, src/compute/cpu.zig:21)
+    _fields_ = [("ggml_type", C.c_int), ("data", C.c_void_p), ("bytes", C.c_size_t)]
+
+
+class ExpertRef(C.Structure):  # loom_expert (ExpertRef, src/compute/cpu.zig:23)
+    _fields_ = [("gate", Weight), ("up", Weight), ("down", Weight), ("weight", C.c_float), ("ffn", C.c_size_t)]
+
+
+class RoutedCfg(C.Structure):  # loom_routed_cfg (RoutedCfg, src/compute/cpu.zig:61)
+    _fields_ = [("n_expert", C.c_size_t), ("n_used", C.c_size_t), ("gating_sigmoid", C.c_int),
+                ("weights_norm", C.c_int), ("weights_scale", C.c_float)]
+
+
+class MoeDesc(C.Structure):  # loom_moe_desc
+    _fields_ = [("dim", C.c_size_t), ("ffn", C.c_size_t), ("n_expert", C.c_size_t), ("n_used", C.c_size_t),
+                ("gating", C.c_int), ("weights_norm", C.c_int), ("weights_scale", C.c_float),
+                ("router", C.c_uint64), ("router_bias", C.c_uint64),
+                ("gate", C.c_uint64), ("up", C.c_uint64), ("down", C.c_uint64),
+                ("shexp_gate", C.c_uint64), ("shexp_up", C.c_uint64), ("shexp_down", C.c_uint64),
+                ("shexp_ffn", C.c_size_t), ("expert0", C.c_size_t), ("n_local", C.c_size_t)]
+
+
+def header_symbols() -> list[str]:
+    """Every function the public header declares."""
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(loom_cuda_\w+)\s*\(", src)))
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise LoomCudaError(f"CUDA backend library not built: {LIB_PATH} (run python -m loom_b200.build)")
+    L = C.CDLL(LIB_PATH)
+    vp, sz, i, f, u64 = C.c_void_p, C.c_size_t, C.c_int, C.c_float, C.c_uint64
+    sig = {
+        "loom_cuda_init": (i, [i]),
+        "loom_cuda_shutdown": (None, []),
+        "loom_cuda_parallel_begin": (None, [sz]),
+        "loom_cuda_parallel_end": (None, []),
+        "loom_cuda_max_batch": (sz, []),
+        "loom_cuda_register_arena": (i, [vp, sz]),
+        "loom_cuda_materialize_arenas": (sz, []),
+        "loom_cuda_arena_error": (C.c_char_p, []),
+        "loom_cuda_take_cmdbuf_count": (sz, []),
+        "loom_cuda_kernel_launches": (u64, []),
+        "loom_cuda_last_error": (sz, [C.c_char_p, sz]),
+        "loom_cuda_clear_weight_cache": (None, []),
+        "loom_cuda_matvec": (i, [i, vp, vp, sz, vp, sz, sz]),
+        "loom_cuda_matmul": (i, [i, vp, vp, sz, vp, sz, sz, sz]),
+        "loom_cuda_dequant_row": (i, [i, vp, vp, sz, sz, sz]),
+        "loom_cuda_moe_route": (i, [vp, vp, sz, vp, vp, sz, i, i, f]),
+        "loom_cuda_moe_ffn_block": (i, [vp, sz, vp, sz, vp]),
+        "loom_cuda_moe_ffn_routed": (i, [vp, sz, vp, vp, Weight, Weight, Weight, vp, sz, sz, RoutedCfg, vp]),
+        "loom_cuda_tensor_upload": (i, [i, vp, sz, C.POINTER(u64)]),
+        "loom_cuda_tensor_synth": (i, [i, u64, u64, f, C.POINTER(u64)]),
+        "loom_cuda_tensor_download": (i, [u64, vp, sz]),
+        "loom_cuda_tensor_free": (i, [u64]),
+        "loom_cuda_tensor_device_bytes": (sz, [u64]),
+        "loom_cuda_moe_forward": (i, [C.POINTER(MoeDesc), vp, sz, vp, vp, vp, vp, vp]),
+        "loom_cuda_reserve": (i, [sz, sz, sz, sz, sz]),
+        "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
+        "loom_cuda_sync": (i, []),
+        "loom_cuda_stream": (vp, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(512)
+    lib().loom_cuda_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str) -> int:
+    """OK -> OK; DECLINED -> DECLINED (caller decides); ERROR -> raise."""
+    if rc == ERROR:
+        raise LoomCudaError(f"{what}: {last_error()}")
+    return rc
+
+
+def must(rc: int, what: str) -> None:
+    if rc != OK:
+        raise LoomCudaError(f"{what}: {'declined' if rc == DECLINED else 'error'}: {last_error()}")

@@ -1,0 +1,615 @@
+// kernels.cu -- dequant, activation quantization, matvec/matmul, router and
+// the MoE expert kernels of the CUDA backend (sm_100a).
+#include <atomic>
+
+#include "kernels.cuh"
+#include "rowdot.cuh"
+
+namespace loom {
+
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launches() { return g_launches.load(); }
+void count_launch() { g_launches.fetch_add(1); }
+
+static inline unsigned cdiv(uint64_t a, uint64_t b) { return (unsigned)((a + b - 1) / b); }
+
+// ---- seeded synthetic tensors ---------------------------------------------------
+// Counter-based generator: word(seed, i) = splitmix64(seed*K + i); block b draws
+// words [32b, 32b+32). The host-side test oracle implements the same function,
+// so any sampled block can be regenerated on the CPU bit for bit.
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint64_t rword(uint64_t seed, uint64_t i) {
+    return splitmix64(seed * 0xD1B54A32D192ED03ull + i);
+}
+__device__ __forceinline__ float unit24(uint64_t w) { return (float)(w >> 40) * (1.0f / 16777216.0f); }
+
+// f32 -> f16 round-to-nearest-even for positive normal-range values (the
+// generator's scale ranges); integer arithmetic, identical on host and device.
+__device__ __forceinline__ uint16_t f32_to_f16_rne(float f) {
+    uint32_t b = __float_as_uint(f);
+    uint32_t sign = (b >> 16) & 0x8000u;
+    int32_t e = (int32_t)((b >> 23) & 0xFF) - 127 + 15;
+    uint32_t m = b & 0x7FFFFFu;
+    if (e <= 0 || e >= 31) return (uint16_t)sign;
+    uint32_t h = ((uint32_t)e << 10) | (m >> 13);
+    uint32_t rem = m & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)(sign | h);
+}
+__device__ __forceinline__ uint16_t rand_scale(uint64_t w, float lo, float span) {
+    return f32_to_f16_rne(fadd(lo, fmul(span, unit24(w))));
+}
+__device__ __forceinline__ void put_bytes(uint8_t *dst, int n, uint64_t seed, uint64_t w0) {
+    for (int i = 0; i < n; i += 8) {
+        uint64_t w = rword(seed, w0 + i / 8);
+        for (int j = 0; j < 8 && i + j < n; j++) dst[i + j] = (uint8_t)(w >> (8 * j));
+    }
+}
+
+__global__ void k_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, uint64_t seed, float sigma) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nblk; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t b = blk0 + i;
+        const uint64_t w0 = b * 32;
+        switch (type) {
+            case T_F32: {
+                uint64_t w[3] = {rword(seed, w0), rword(seed, w0 + 1), rword(seed, w0 + 2)};
+                float s = 0.0f;
+                for (int k = 0; k < 12; k++) s = fadd(s, (float)((w[k / 4] >> (16 * (k % 4))) & 0xFFFF) * (1.0f / 65536.0f));
+                reinterpret_cast<float *>(raw)[i] = fmul(fsub(s, 6.0f), sigma);
+                break;
+            }
+            case T_Q4_K: {
+                uint8_t *blk = raw + i * 144;
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                uint16_t dm = rand_scale(rword(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8; blk[2] = dm & 0xFF; blk[3] = dm >> 8;
+                put_bytes(blk + 4, 140, seed, w0 + 2);
+                break;
+            }
+            case T_Q6_K: {
+                uint8_t *blk = raw + i * 210;
+                put_bytes(blk, 192, seed, w0 + 2);
+                uint8_t sc[16];
+                put_bytes(sc, 16, seed, w0 + 26);
+                for (int k = 0; k < 16; k++) blk[192 + k] = (uint8_t)(int8_t)((int)(sc[k] % 64) - 32);
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                blk[208] = d & 0xFF; blk[209] = d >> 8;
+                break;
+            }
+            case T_Q4_0: {
+                uint8_t *blk = raw + i * 18;
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 1.9e-2f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8;
+                put_bytes(blk + 2, 16, seed, w0 + 2);
+                break;
+            }
+            case T_Q8_0: {
+                uint8_t *blk = raw + i * 34;
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8;
+                put_bytes(blk + 2, 32, seed, w0 + 2);
+                break;
+            }
+        }
+    }
+}
+
+void launch_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, uint64_t seed, float sigma, cudaStream_t st) {
+    if (nblk == 0) return;
+    unsigned g = cdiv(nblk, 256);
+    if (g > 148 * 64) g = 148 * 64;
+    k_synth<<<g, 256, 0, st>>>(type, raw, blk0, nblk, seed, sigma);
+    count_launch();
+}
+
+// ---- GGUF bytes <-> device layout ------------------------------------------------
+
+__global__ void k_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, uint16_t *d, uint64_t nblk) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblk; b += (uint64_t)gridDim.x * blockDim.x) {
+        switch (type) {
+            case T_Q6_K: {
+                const uint8_t *src = raw + b * 210;
+                for (int i = 0; i < 192; i++) q[b * 192 + i] = src[i];
+                for (int i = 0; i < 16; i++) sc[b * 16 + i] = src[192 + i];
+                d[b] = (uint16_t)(src[208] | (src[209] << 8));
+                break;
+            }
+            case T_Q8_0: {
+                const uint8_t *src = raw + b * 34;
+                d[b] = (uint16_t)(src[0] | (src[1] << 8));
+                for (int i = 0; i < 32; i++) q[b * 32 + i] = src[2 + i];
+                break;
+            }
+            case T_Q4_0: {
+                const uint8_t *src = raw + b * 18;
+                d[b] = (uint16_t)(src[0] | (src[1] << 8));
+                for (int i = 0; i < 16; i++) q[b * 16 + i] = src[2 + i];
+                break;
+            }
+        }
+    }
+}
+
+void launch_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, uint16_t *d, uint64_t nblk, cudaStream_t st) {
+    if (nblk == 0) return;
+    unsigned g = cdiv(nblk, 256);
+    if (g > 148 * 64) g = 148 * 64;
+    k_repack<<<g, 256, 0, st>>>(type, raw, q, sc, d, nblk);
+    count_launch();
+}
+
+__global__ void k_unpack(WDev w, uint8_t *raw, uint64_t nblk) {
+    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblk; b += (uint64_t)gridDim.x * blockDim.x) {
+        switch (w.type) {
+            case T_Q4_K:
+                for (int i = 0; i < 144; i++) raw[b * 144 + i] = w.q[b * 144 + i];
+                break;
+            case T_Q6_K: {
+                uint8_t *dst = raw + b * 210;
+                for (int i = 0; i < 192; i++) dst[i] = w.q[b * 192 + i];
+                for (int i = 0; i < 16; i++) dst[192 + i] = w.sc[b * 16 + i];
+                dst[208] = w.d[b] & 0xFF;
+                dst[209] = w.d[b] >> 8;
+                break;
+            }
+            case T_Q8_0: {
+                uint8_t *dst = raw + b * 34;
+                dst[0] = w.d[b] & 0xFF;
+                dst[1] = w.d[b] >> 8;
+                for (int i = 0; i < 32; i++) dst[2 + i] = w.q[b * 32 + i];
+                break;
+            }
+            case T_Q4_0: {
+                uint8_t *dst = raw + b * 18;
+                dst[0] = w.d[b] & 0xFF;
+                dst[1] = w.d[b] >> 8;
+                for (int i = 0; i < 16; i++) dst[2 + i] = w.q[b * 16 + i];
+                break;
+            }
+        }
+    }
+}
+
+void launch_unpack(int type, const WDev &w, uint8_t *raw, uint64_t nblk, cudaStream_t st) {
+    (void)type;
+    if (nblk == 0) return;
+    unsigned g = cdiv(nblk, 256);
+    if (g > 148 * 64) g = 148 * 64;
+    k_unpack<<<g, 256, 0, st>>>(w, raw, nblk);
+    count_launch();
+}
+
+// ---- dequant (bit-exact with dequantRow, ggml.zig:1739-1857) -----------------------
+
+__global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
+    const int be = block_elems(w.type);
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < nelem; e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t gb = gb0 + e / be;
+        const int i = (int)(e % be);
+        float v = 0.0f;
+        switch (w.type) {
+            case T_F32:
+                v = reinterpret_cast<const float *>(w.q)[gb];
+                break;
+            case T_Q4_K: {  // dequantBlockQ4K :1342: (d*sc)*q - (dmin*m)
+                const uint8_t *blk = w.q + gb * 144;
+                const float d = f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+                const float dmin = f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+                const int j = i / 64, l = i % 64;
+                const int sb = 2 * j + (l >= 32);
+                const uint8_t byte = blk[16 + 32 * j + (l & 31)];
+                const int q = l < 32 ? (byte & 0x0F) : (byte >> 4);
+                int sc, mn;
+                scale_min_k4(sb, blk + 4, sc, mn);
+                v = fsub(fmul(fmul(d, (float)sc), (float)q), fmul(dmin, (float)mn));
+                break;
+            }
+            case T_Q6_K: {  // dequantBlockQ6K :1420: (d*sc)*(q-32)
+                const uint8_t *qb = w.q + gb * 192;
+                const int8_t *scs = reinterpret_cast<const int8_t *>(w.sc + gb * 16);
+                const float d = f16_to_f32(w.d[gb]);
+                const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
+                const uint8_t a = qb[64 * n + l], bb = qb[64 * n + 32 + l], h = qb[128 + 32 * n + l];
+                int q;
+                switch (g) {
+                    case 0: q = (a & 0x0F) | ((h & 3) << 4); break;
+                    case 1: q = (bb & 0x0F) | (((h >> 2) & 3) << 4); break;
+                    case 2: q = (a >> 4) | (((h >> 4) & 3) << 4); break;
+                    default: q = (bb >> 4) | (((h >> 6) & 3) << 4); break;
+                }
+                const float s = fmul(d, (float)scs[8 * n + l / 16 + 2 * g]);
+                v = fmul(s, fsub((float)q, 32.0f));
+                break;
+            }
+            case T_Q4_0: {
+                const uint8_t byte = w.q[gb * 16 + (i & 15)];
+                const int q = i < 16 ? (byte & 0x0F) : (byte >> 4);
+                v = fmul((float)(q - 8), f16_to_f32(w.d[gb]));
+                break;
+            }
+            case T_Q8_0:
+                v = fmul((float)(int8_t)w.q[gb * 32 + i], f16_to_f32(w.d[gb]));
+                break;
+        }
+        out[e] = v;
+    }
+}
+
+void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cudaStream_t st) {
+    const uint64_t n = nblk * (uint64_t)block_elems(w.type);
+    if (n == 0) return;
+    unsigned g = cdiv(n, 256);
+    if (g > 148 * 64) g = 148 * 64;
+    k_dequant<<<g, 256, 0, st>>>(w, gb0, n, out);
+    count_launch();
+}
+
+// ---- activation quantization (quantizeX256 :776 / quantizeX :1077) ---------------
+// Each lane holds 8 consecutive values. 256-wide blocks: one warp per block,
+// per-16 sums from lane pairs. 32-wide blocks: four lanes per block, eight
+// blocks per warp.
+
+__device__ __forceinline__ void quant_lane8(const float *src, bool live, int group_lanes, int8_t *qdst, float *ddst,
+                                            int32_t *sdst_pairs, int32_t *sdst_group, int lane) {
+    float v[8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        v[i] = live ? src[i] : 0.0f;
+        if (isfinite(v[i])) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    for (int o = 1; o < group_lanes; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = fdiv(amax, 127.0f);
+    const float inv = (d != 0.0f && isfinite(d)) ? fdiv(1.0f, d) : 0.0f;
+    int sum = 0;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int q = to_i8_sat(fmul(v[i], inv));
+        sum += q;
+        if (i < 4) lo |= ((uint32_t)(q & 0xFF)) << (8 * i);
+        else hi |= ((uint32_t)(q & 0xFF)) << (8 * (i - 4));
+    }
+    if (live) *reinterpret_cast<uint2 *>(qdst) = make_uint2(lo, hi);
+    const int pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
+    if (sdst_pairs && live && (lane & 1) == 0) *sdst_pairs = pair;
+    if (sdst_group) {
+        int gs = sum;
+        for (int o = 1; o < group_lanes; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        if (live && (lane % group_lanes) == 0) *sdst_group = gs;
+    }
+    if (live && (lane % group_lanes) == 0) *ddst = isfinite(d) ? d : 0.0f;
+}
+
+__global__ void k_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d,
+                            int32_t *s, int dstride, int sstride) {
+    const int lane = threadIdx.x & 31;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    if (kind256) {
+        const int nb = cols / 256;
+        for (int item = warp; item < ntok * nb; item += nwarps) {
+            const int t = item / nb, b = item % nb;
+            const int off = b * 256 + lane * 8;
+            quant_lane8(x + (size_t)t * xstride + off, true, 32, q + (size_t)t * cols + off, d + (size_t)t * dstride + b,
+                        s + (size_t)t * sstride + b * 16 + lane / 2, nullptr, lane);
+        }
+    } else {
+        const int nb = cols / 32;
+        const int ng = (nb + 7) / 8;
+        for (int item = warp; item < ntok * ng; item += nwarps) {
+            const int t = item / ng, g = item % ng;
+            const int b = g * 8 + lane / 4;
+            const bool live = b < nb;
+            const int off = b * 32 + (lane & 3) * 8;
+            quant_lane8(x + (size_t)t * xstride + off, live, 4, q + (size_t)t * cols + off, d + (size_t)t * dstride + b,
+                        nullptr, s + (size_t)t * sstride + b, lane);
+        }
+    }
+}
+
+void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d, int32_t *s,
+                      int dstride, int sstride, cudaStream_t st) {
+    const int items = kind256 ? ntok * (cols / 256) : ntok * ((cols / 32 + 7) / 8);
+    if (items == 0) return;
+    const int threads = 128;
+    unsigned g = cdiv((uint64_t)items * 32, threads);
+    if (g > 148 * 16) g = 148 * 16;
+    k_quant_act<<<g, threads, 0, st>>>(x, ntok, cols, xstride, kind256, q, d, s, dstride, sstride);
+    count_launch();
+}
+
+// ---- matvec / matmul (ggml.zig:602 matvec, :504 matmul) ---------------------------
+// One warp per row; the row's blocks are decoded once per group of NT tokens.
+
+constexpr int MM_NT = 4;
+
+__global__ void __launch_bounds__(256) k_mm(WDev w, uint64_t gb_base, int rows, int nb, XQ x, int ntok, float *out) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    for (int t0 = 0; t0 < ntok; t0 += MM_NT) {
+        float acc[MM_NT] = {};
+        const int nt = min(MM_NT, ntok - t0);
+        rowdot<MM_NT>(w, gb_base + (uint64_t)r * nb, nb, x, t0, nt, acc, lane);
+        if (lane == 0)
+            for (int k = 0; k < nt; k++) out[(size_t)(t0 + k) * rows + r] = acc[k];
+    }
+}
+
+void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x, int ntok, float *out, cudaStream_t st) {
+    if (rows == 0 || ntok == 0) return;
+    const int nb = cols / block_elems(w.type);
+    k_mm<<<cdiv(rows, 8), 256, 0, st>>>(w, gb_base, rows, nb, x, ntok, out);
+    count_launch();
+}
+
+__global__ void __launch_bounds__(256) k_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    for (int t = 0; t < ntok; t++) {
+        const float v = rowdot_f32(W + (size_t)r * cols, xs + (size_t)t * cols, cols, lane);
+        if (lane == 0) out[(size_t)t * rows + r] = v;
+    }
+}
+
+void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out, cudaStream_t st) {
+    if (rows == 0 || ntok == 0) return;
+    k_mm_f32<<<cdiv(rows, 8), 256, 0, st>>>(W, rows, cols, xs, ntok, out);
+    count_launch();
+}
+
+// ---- router (moe.zig:106-158 route) ------------------------------------------------
+// One warp per token. Scores and the biased choice live in shared memory;
+// top-k is k rounds of a warp arg-max that keeps the lowest index on ties and
+// never selects a value that is not > -inf (the serial scan's strict '>').
+
+__device__ void route_warp(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
+                           float weights_scale, float *scores, float *choice, int *ids, float *gates, int lane) {
+    if (gating == 2) {
+        for (int e = lane; e < ne; e += 32) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
+    } else if (gating == 1) {
+        float m = -INFINITY;
+        for (int e = lane; e < ne; e += 32) m = fmaxf(m, logits[e]);
+        m = warp_max(m);
+        float sum = 0.0f;
+        for (int e = lane; e < ne; e += 32) {
+            const float v = expf(fsub(logits[e], m));
+            scores[e] = v;
+            sum = fadd(sum, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum = fadd(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        const float inv = fdiv(1.0f, sum);
+        for (int e = lane; e < ne; e += 32) scores[e] = fmul(scores[e], inv);
+    } else {
+        for (int e = lane; e < ne; e += 32) scores[e] = logits[e];
+    }
+    for (int e = lane; e < ne; e += 32) choice[e] = bias ? fadd(scores[e], bias[e]) : scores[e];
+    __syncwarp();
+    for (int k = 0; k < nk; k++) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < ne; e += 32) {
+            const float c = choice[e];
+            if (c > bv) {  // strict: first maximum in this lane's (ascending) run
+                bv = c;
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
+        if (lane == 0) {
+            ids[k] = bi;
+            gates[k] = scores[bi];
+            choice[bi] = -INFINITY;  // used
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        if (gating == 3) {  // softmax over the selected k (tensor.zig:18 softmax)
+            float m = -INFINITY;
+            for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
+            float sum = 0.0f;
+            for (int k = 0; k < nk; k++) {
+                gates[k] = expf(fsub(gates[k], m));
+                sum = fadd(sum, gates[k]);
+            }
+            const float inv = fdiv(1.0f, sum);
+            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], inv);
+        }
+        if (weights_norm) {
+            float sum = 0.0f;
+            for (int k = 0; k < nk; k++) sum = fadd(sum, gates[k]);
+            const float denom = fmaxf(sum, 6.103515625e-5f);
+            for (int k = 0; k < nk; k++) gates[k] = fdiv(gates[k], denom);
+        }
+        if (weights_scale != 1.0f)
+            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], weights_scale);
+    }
+    __syncwarp();
+}
+
+__global__ void k_route(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
+                        float weights_scale, int *ids, float *gates) {
+    extern __shared__ float sm[];
+    const int t = blockIdx.x;
+    route_warp(logits + (size_t)t * ne, bias, ne, nk, gating, weights_norm, weights_scale, sm, sm + ne,
+               ids + (size_t)t * nk, gates + (size_t)t * nk, threadIdx.x);
+}
+
+void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating, int weights_norm,
+                  float weights_scale, int *ids, float *gates, cudaStream_t st) {
+    if (T == 0) return;
+    k_route<<<T, 32, 2 * n_expert * sizeof(float), st>>>(logits, bias, n_expert, n_used, gating, weights_norm,
+                                                         weights_scale, ids, gates);
+    count_launch();
+}
+
+// Route, then expand the selection into per-(token, expert) slots. Slot
+// t*n_used + k is token t's k-th selected expert; the shared expert of token t
+// is slot T*n_used + t. Experts outside this rank's range get ffn = 0.
+__global__ void k_route_slots(const float *logits, const float *bias, int T, RoutedLayerDev L, int *ids, float *gates,
+                              Slot *slots, int act_stride) {
+    extern __shared__ float sm[];
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x;
+    int *tid = ids + (size_t)t * L.n_used;
+    float *tg = gates + (size_t)t * L.n_used;
+    route_warp(logits + (size_t)t * L.n_expert, bias, L.n_expert, L.n_used, L.gating, L.weights_norm, L.weights_scale,
+               sm, sm + L.n_expert, tid, tg, lane);
+    for (int k = lane; k < L.n_used; k += 32) {
+        const int e = tid[k];
+        const int le = e - L.expert0;
+        const bool local = le >= 0 && le < L.n_local;
+        Slot s;
+        s.g = L.g;
+        s.u = L.u;
+        s.dn = L.dn;
+        s.gb_g = local ? (uint64_t)le * L.plane_blk_g : 0;
+        s.gb_u = local ? (uint64_t)le * L.plane_blk_u : 0;
+        s.gb_dn = local ? (uint64_t)le * L.plane_blk_dn : 0;
+        s.ffn = local ? L.ffn : 0;
+        s.token = t;
+        s.weight = tg[k];
+        s.act_off = (t * L.n_used + k) * act_stride;
+        slots[t * L.n_used + k] = s;
+    }
+    if (L.has_shared && lane == 0) {
+        Slot s;
+        s.g = L.sg;
+        s.u = L.su;
+        s.dn = L.sdn;
+        s.gb_g = s.gb_u = s.gb_dn = 0;
+        s.ffn = L.shexp_ffn;
+        s.token = t;
+        s.weight = 1.0f;
+        s.act_off = (T * L.n_used + t) * act_stride;
+        slots[T * L.n_used + t] = s;
+    }
+}
+
+void launch_route_slots(const float *logits, const float *bias, int T, const RoutedLayerDev &L, int *ids, float *gates,
+                        Slot *slots, int act_stride, cudaStream_t st) {
+    if (T == 0) return;
+    k_route_slots<<<T, 32, 2 * L.n_expert * sizeof(float), st>>>(logits, bias, T, L, ids, gates, slots, act_stride);
+    count_launch();
+}
+
+// ---- expert FFN ------------------------------------------------------------------
+// gate/up (+SwiGLU): warp per (slot, row). act = silu(g) * u, silu(g) = g/(1+e^-g)
+// (tensor.zig:30, :53).
+
+__global__ void __launch_bounds__(256) k_gateup(const Slot *__restrict__ slots, int dim, XQ x256, XQ x32, float *act) {
+    const Slot &s = slots[blockIdx.y];
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= s.ffn) return;
+    const XQ &xg = act256(s.g.type) ? x256 : x32;
+    const XQ &xu = act256(s.u.type) ? x256 : x32;
+    const int nbg = dim / block_elems(s.g.type), nbu = dim / block_elems(s.u.type);
+    float g[1] = {0.0f}, u[1] = {0.0f};
+    rowdot<1>(s.g, s.gb_g + (uint64_t)r * nbg, nbg, xg, s.token, 1, g, lane);
+    rowdot<1>(s.u, s.gb_u + (uint64_t)r * nbu, nbu, xu, s.token, 1, u, lane);
+    if (lane == 0) {
+        const float sl = fdiv(g[0], fadd(1.0f, expf(-g[0])));
+        act[s.act_off + r] = fmul(sl, u[0]);
+    }
+}
+
+void launch_gateup(const Slot *slots, int n_slots, int max_ffn, int dim, const XQ &x256, const XQ &x32, float *act,
+                   cudaStream_t st) {
+    if (n_slots == 0) return;
+    dim3 grid(cdiv(max_ffn, 8), n_slots);
+    k_gateup<<<grid, 256, 0, st>>>(slots, dim, x256, x32, act);
+    count_launch();
+}
+
+// Quantize each slot's activation in the format its down projection reads.
+__global__ void k_quant_slots(const Slot *__restrict__ slots, const float *act, int8_t *aq, float *ad, int32_t *as) {
+    const Slot &s = slots[blockIdx.y];
+    if (s.ffn == 0) return;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float *x = act + s.act_off;
+    int8_t *q = aq + s.act_off;
+    float *d = ad + s.act_off / 32;
+    int32_t *sm = as + s.act_off / 16;
+    if (act256(s.dn.type)) {
+        for (int b = warp; b < s.ffn / 256; b += nw)
+            quant_lane8(x + b * 256 + lane * 8, true, 32, q + b * 256 + lane * 8, d + b, sm + b * 16 + lane / 2, nullptr,
+                        lane);
+    } else {
+        const int nb = s.ffn / 32, ng = (nb + 7) / 8;
+        for (int gi = warp; gi < ng; gi += nw) {
+            const int b = gi * 8 + lane / 4;
+            const bool live = b < nb;
+            const int off = b * 32 + (lane & 3) * 8;
+            quant_lane8(x + off, live, 4, q + off, d + b, nullptr, sm + b, lane);
+        }
+    }
+}
+
+void launch_quant_slots(const Slot *slots, int n_slots, int max_ffn, const float *act, int8_t *aq, float *ad, int32_t *as,
+                        cudaStream_t st) {
+    (void)max_ffn;
+    if (n_slots == 0) return;
+    k_quant_slots<<<dim3(1, n_slots), 256, 0, st>>>(slots, act, aq, ad, as);
+    count_launch();
+}
+
+// down + weighted combine: warp per (token, output row); the token's slots are
+// summed in selection order, then the shared expert is added (llama.zig:1397,
+// deepseek.zig:1498-1508).
+__global__ void __launch_bounds__(256) k_down(const Slot *__restrict__ slots, int T, int nk, int has_shared, int dim,
+                                              const int8_t *aq, const float *ad, const int32_t *as, float *out,
+                                              const float *residual) {
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= dim) return;
+    float acc = 0.0f;
+    const int n = nk + (has_shared ? 1 : 0);
+    for (int k = 0; k < n; k++) {
+        const Slot &s = slots[k < nk ? t * nk + k : T * nk + t];
+        if (s.ffn == 0) continue;
+        XQ xa;
+        xa.q = aq + s.act_off;
+        xa.d = ad + s.act_off / 32;
+        xa.s = as + s.act_off / 16;
+        xa.cols = s.ffn;
+        xa.dstride = 0;
+        xa.sstride = 0;
+        xa.kind256 = act256(s.dn.type);
+        const int nb = s.ffn / block_elems(s.dn.type);
+        float y[1] = {0.0f};
+        rowdot<1>(s.dn, s.gb_dn + (uint64_t)r * nb, nb, xa, 0, 1, y, lane);
+        acc = k < nk ? fadd(acc, fmul(s.weight, y[0])) : fadd(acc, y[0]);
+    }
+    if (lane == 0) out[(size_t)t * dim + r] = residual ? fadd(residual[(size_t)t * dim + r], acc) : acc;
+}
+
+void launch_down(const Slot *slots, int T, int nk, int has_shared, int dim, const int8_t *aq, const float *ad,
+                 const int32_t *as, float *out, const float *residual, cudaStream_t st) {
+    if (T == 0) return;
+    dim3 grid(cdiv(dim, 8), T);
+    k_down<<<grid, 256, 0, st>>>(slots, T, nk, has_shared, dim, aq, ad, as, out, residual);
+    count_launch();
+}
+
+}  // namespace loom

@@ -1,0 +1,64 @@
+// kernels.cuh -- device kernels of the CUDA backend and their host launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace loom {
+
+// One routed (or host-listed) expert applied to one token: the unit the MoE
+// kernels iterate over. Mirrors the seam's ExpertRef (src/compute/cpu.zig:23)
+// plus the token it serves and where its activation lives in scratch.
+struct Slot {
+    WDev g, u, dn;        // gate [ffn x dim], up [ffn x dim], down [dim x ffn]
+    uint64_t gb_g, gb_u, gb_dn;  // first block of this expert's plane in each tensor
+    int ffn;
+    int token;
+    float weight;
+    int act_off;          // element offset of this slot's activation in scratch (multiple of 256)
+};
+
+// Routed-layer description the device-side router expands into slots.
+struct RoutedLayerDev {
+    WDev g, u, dn;
+    uint64_t plane_blk_g, plane_blk_u, plane_blk_dn;  // blocks per expert plane
+    int ffn, dim;
+    int n_expert, n_used;
+    int gating;           // 1 softmax, 2 sigmoid, 3 softmax_topk
+    int weights_norm;
+    float weights_scale;
+    int has_shared;
+    WDev sg, su, sdn;     // shared expert (gb offsets 0)
+    int shexp_ffn;
+    int expert0;          // first expert id held by this rank (expert parallelism); 0 otherwise
+    int n_local;          // experts held locally; n_expert when not sharded
+};
+
+// launchers (all asynchronous on `st`)
+void launch_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, uint64_t seed, float sigma, cudaStream_t st);
+void launch_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, uint16_t *d, uint64_t nblk, cudaStream_t st);
+void launch_unpack(int type, const WDev &w, uint8_t *raw, uint64_t nblk, cudaStream_t st);
+void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cudaStream_t st);
+void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d,
+                      int32_t *s, int dstride, int sstride, cudaStream_t st);
+void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x, int ntok, float *out,
+               cudaStream_t st);
+void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out, cudaStream_t st);
+void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating,
+                  int weights_norm, float weights_scale, int *ids, float *gates, cudaStream_t st);
+void launch_route_slots(const float *logits, const float *bias, int T, const RoutedLayerDev &L, int *ids,
+                        float *gates, Slot *slots, int act_stride, cudaStream_t st);
+void launch_gateup(const Slot *slots, int n_slots, int max_ffn, int dim, const XQ &x256, const XQ &x32,
+                   float *act, cudaStream_t st);
+void launch_quant_slots(const Slot *slots, int n_slots, int max_ffn, const float *act, int8_t *aq, float *ad,
+                        int32_t *as, cudaStream_t st);
+void launch_down(const Slot *slots, int T, int nk, int has_shared, int dim, const int8_t *aq, const float *ad,
+                 const int32_t *as, float *out, const float *residual, cudaStream_t st);
+
+// number of kernel launches issued by this library (host-side count)
+uint64_t launches();
+void count_launch();
+
+}  // namespace loom

@@ -1,0 +1,795 @@
+// runtime.cu -- the C ABI of the CUDA backend (include/loom_cuda.h): device
+// and stream ownership, the device weight cache, arenas, scratch, and the
+// host-buffer seam entry points.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/loom_cuda.h"
+#include "kernels.cuh"
+
+using namespace loom;
+
+namespace {
+
+thread_local std::string g_err;
+std::string g_arena_err;
+bool g_inited = false;
+int g_device = -1;
+cudaStream_t g_stream = nullptr;
+size_t g_cmdbufs = 0;
+
+int fail(const char *what, cudaError_t e) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "%s: %s", what, cudaGetErrorString(e));
+    g_err = buf;
+    return LOOM_CUDA_ERROR;
+}
+int decline(const char *why) {
+    g_err = why;
+    return LOOM_CUDA_DECLINED;
+}
+#define CK(call)                                     \
+    do {                                             \
+        cudaError_t e_ = (call);                     \
+        if (e_ != cudaSuccess) return fail(#call, e_); \
+    } while (0)
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+bool type_ok(int t) { return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; }
+
+// ---- device tensors ---------------------------------------------------------------
+
+struct Tensor {
+    int type = 0;
+    uint64_t nblk = 0;
+    uint8_t *base = nullptr;
+    size_t dev_bytes = 0;
+    WDev w{};
+};
+std::unordered_map<uint64_t, Tensor> g_tensors;
+uint64_t g_next_handle = 1;
+
+// weight cache: (host pointer, bytes, type) -> tensor handle
+std::map<std::tuple<const void *, size_t, int>, uint64_t> g_cache;
+
+struct Arena {
+    const uint8_t *host;
+    size_t bytes;
+    uint8_t *dev;
+};
+std::vector<Arena> g_arenas;
+
+// growable device buffer
+struct DBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t n) {
+        if (n <= cap) return 0;
+        if (p) {
+            cudaStreamSynchronize(g_stream);
+            cudaFree(p);
+            p = nullptr;
+            cap = 0;
+        }
+        size_t want = std::max<size_t>(align256(n + n / 4), 256);
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e != cudaSuccess) return fail("cudaMalloc(scratch)", e);
+        cap = want;
+        return 0;
+    }
+    template <class T> T *as() const { return reinterpret_cast<T *>(p); }
+};
+struct HBuf {  // pinned host staging
+    void *p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t n) {
+        if (n <= cap) return 0;
+        if (p) {
+            cudaStreamSynchronize(g_stream);
+            cudaFreeHost(p);
+            p = nullptr;
+            cap = 0;
+        }
+        size_t want = std::max<size_t>(align256(n + n / 4), 4096);
+        cudaError_t e = cudaHostAlloc(&p, want, cudaHostAllocDefault);
+        if (e != cudaSuccess) return fail("cudaHostAlloc(staging)", e);
+        cap = want;
+        return 0;
+    }
+    template <class T> T *as() const { return reinterpret_cast<T *>(p); }
+};
+
+struct Scratch {
+    DBuf xq256_q, xq256_d, xq256_s, xq32_q, xq32_d, xq32_s;
+    DBuf logits, ids, gates, slots, act, aq, ad, as;
+    DBuf io_in, io_out, io_aux, raw;
+    HBuf h_in, h_out;
+} S;
+
+int alloc_tensor(int type, uint64_t nblk, Tensor &t) {
+    t.type = type;
+    t.nblk = nblk;
+    const size_t qb = align256(nblk * (size_t)layout_qbytes(type));
+    const size_t scb = type == T_Q6_K ? align256(nblk * 16) : 0;
+    const size_t db = (type == T_Q6_K || type == T_Q8_0 || type == T_Q4_0) ? align256(nblk * 2) : 0;
+    t.dev_bytes = qb + scb + db;
+    cudaError_t e = cudaMalloc(&t.base, std::max<size_t>(t.dev_bytes, 256));
+    if (e != cudaSuccess) return fail("cudaMalloc(tensor)", e);
+    t.w.type = type;
+    t.w.q = t.base;
+    t.w.sc = scb ? t.base + qb : nullptr;
+    t.w.d = db ? reinterpret_cast<uint16_t *>(t.base + qb + scb) : nullptr;
+    return 0;
+}
+
+// Fill a tensor from GGUF bytes already on the device (`raw_dev`).
+int fill_from_raw_dev(Tensor &t, const uint8_t *raw_dev) {
+    if (t.type == T_F32 || t.type == T_Q4_K) {
+        CK(cudaMemcpyAsync(t.base, raw_dev, t.nblk * (size_t)block_bytes(t.type), cudaMemcpyDeviceToDevice, g_stream));
+    } else {
+        launch_repack(t.type, raw_dev, t.base, const_cast<uint8_t *>(t.w.sc), const_cast<uint16_t *>(t.w.d), t.nblk,
+                      g_stream);
+    }
+    CK(cudaGetLastError());
+    return 0;
+}
+
+const uint8_t *arena_lookup(const void *p, size_t bytes) {
+    const uint8_t *hp = static_cast<const uint8_t *>(p);
+    for (auto &a : g_arenas)
+        if (a.dev && hp >= a.host && hp + bytes <= a.host + a.bytes) return a.dev + (hp - a.host);
+    return nullptr;
+}
+
+int upload_tensor(int type, const void *data, size_t bytes, uint64_t &handle) {
+    const size_t bb = block_bytes(type);
+    if (!type_ok(type) || bb == 0) return decline("unsupported ggml type");
+    if (bytes % bb != 0) return decline("tensor bytes are not a whole number of blocks");
+    Tensor t;
+    if (int rc = alloc_tensor(type, bytes / bb, t)) return rc;
+    const uint8_t *raw_dev = arena_lookup(data, bytes);
+    if (!raw_dev && (type == T_F32 || type == T_Q4_K)) {
+        CK(cudaMemcpyAsync(t.base, data, bytes, cudaMemcpyHostToDevice, g_stream));
+    } else {
+        if (!raw_dev) {
+            if (int rc = S.raw.ensure(bytes)) return rc;
+            CK(cudaMemcpyAsync(S.raw.p, data, bytes, cudaMemcpyHostToDevice, g_stream));
+            raw_dev = S.raw.as<uint8_t>();
+        }
+        if (int rc = fill_from_raw_dev(t, raw_dev)) return rc;
+    }
+    CK(cudaStreamSynchronize(g_stream));  // the host bytes are only borrowed
+    handle = g_next_handle++;
+    g_tensors[handle] = t;
+    return 0;
+}
+
+// Resolve a seam weight (host bytes) to its cached device tensor.
+int resolve(int type, const void *data, size_t bytes, Tensor *&out) {
+    auto key = std::make_tuple(data, bytes, type);
+    auto it = g_cache.find(key);
+    if (it != g_cache.end()) {
+        out = &g_tensors[it->second];
+        return 0;
+    }
+    uint64_t h = 0;
+    if (int rc = upload_tensor(type, data, bytes, h)) return rc;
+    g_cache[key] = h;
+    out = &g_tensors[h];
+    return 0;
+}
+
+Tensor *lookup(loom_tensor h) {
+    auto it = g_tensors.find(h);
+    return it == g_tensors.end() ? nullptr : &it->second;
+}
+
+int need_init() { return g_inited ? 0 : decline("loom_cuda_init has not been called"); }
+
+// Scratch for quantizing T activation vectors of width `cols`.
+int ensure_xq(size_t T, size_t cols) {
+    if (int rc = S.xq256_q.ensure(T * cols)) return rc;
+    if (int rc = S.xq256_d.ensure(T * (cols / 256 + 1) * 4)) return rc;
+    if (int rc = S.xq256_s.ensure(T * (cols / 16 + 1) * 4)) return rc;
+    if (int rc = S.xq32_q.ensure(T * cols)) return rc;
+    if (int rc = S.xq32_d.ensure(T * (cols / 32 + 1) * 4)) return rc;
+    if (int rc = S.xq32_s.ensure(T * (cols / 32 + 1) * 4)) return rc;
+    return 0;
+}
+
+XQ make_xq(bool k256, size_t cols) {
+    XQ x;
+    x.cols = (int)cols;
+    x.kind256 = k256;
+    if (k256) {
+        x.q = S.xq256_q.as<int8_t>();
+        x.d = S.xq256_d.as<float>();
+        x.s = S.xq256_s.as<int32_t>();
+        x.dstride = (int)(cols / 256);
+        x.sstride = (int)(cols / 16);
+    } else {
+        x.q = S.xq32_q.as<int8_t>();
+        x.d = S.xq32_d.as<float>();
+        x.s = S.xq32_s.as<int32_t>();
+        x.dstride = (int)(cols / 32);
+        x.sstride = (int)(cols / 32);
+    }
+    return x;
+}
+
+void quantize_into(const float *x, size_t T, size_t cols, bool k256, cudaStream_t st) {
+    XQ q = make_xq(k256, cols);
+    launch_quant_act(x, (int)T, (int)cols, (int)cols, k256, const_cast<int8_t *>(q.q), const_cast<float *>(q.d),
+                     const_cast<int32_t *>(q.s), q.dstride, q.sstride, st);
+}
+
+int ensure_moe_scratch(size_t T, size_t dim, size_t max_ffn, size_t n_expert, size_t n_slots) {
+    const size_t act_stride = align256(max_ffn);
+    if (int rc = ensure_xq(T, dim)) return rc;
+    if (int rc = S.logits.ensure(T * n_expert * 4)) return rc;
+    if (int rc = S.ids.ensure(n_slots * 4)) return rc;
+    if (int rc = S.gates.ensure(n_slots * 4)) return rc;
+    if (int rc = S.slots.ensure(n_slots * sizeof(Slot))) return rc;
+    if (int rc = S.act.ensure(n_slots * act_stride * 4)) return rc;
+    if (int rc = S.aq.ensure(n_slots * act_stride)) return rc;
+    if (int rc = S.ad.ensure(n_slots * act_stride / 32 * 4 + 64)) return rc;
+    if (int rc = S.as.ensure(n_slots * act_stride / 16 * 4 + 64)) return rc;
+    return 0;
+}
+
+// Run the expert phase for slots already on the device.
+int run_experts(size_t T, size_t dim, int nk, int has_shared, size_t n_slots, size_t max_ffn, bool need256,
+                bool need32, const float *d_x, float *d_out, const float *d_residual, cudaStream_t st) {
+    if (need256) quantize_into(d_x, T, dim, true, st);
+    if (need32) quantize_into(d_x, T, dim, false, st);
+    const Slot *slots = S.slots.as<Slot>();
+    launch_gateup(slots, (int)n_slots, (int)max_ffn, (int)dim, make_xq(true, dim), make_xq(false, dim),
+                  S.act.as<float>(), st);
+    launch_quant_slots(slots, (int)n_slots, (int)max_ffn, S.act.as<float>(), S.aq.as<int8_t>(), S.ad.as<float>(),
+                       S.as.as<int32_t>(), st);
+    launch_down(slots, (int)T, nk, has_shared, (int)dim, S.aq.as<int8_t>(), S.ad.as<float>(), S.as.as<int32_t>(), d_out,
+                d_residual, st);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int check_moe_types(const Tensor *g, const Tensor *u, const Tensor *d) {
+    for (const Tensor *t : {g, u, d})
+        if (!t || t->type == T_F32) return decline("MoE expert tensors must be Q4_0, Q8_0, Q4_K or Q6_K");
+    return 0;
+}
+
+int routed_layer(RoutedLayerDev &L, const Tensor *g, const Tensor *u, const Tensor *dn, size_t dim, size_t ffn,
+                 size_t n_local, const Tensor *sh[3], size_t shexp_ffn) {
+    if (int rc = check_moe_types(g, u, dn)) return rc;
+    const int bg = block_elems(g->type), bu = block_elems(u->type), bd = block_elems(dn->type);
+    if (dim % bg || dim % bu || ffn % bd || ffn % 32) return decline("MoE shape is not a whole number of blocks");
+    const uint64_t pg = ffn * (dim / bg), pu = ffn * (dim / bu), pd = dim * (ffn / bd);
+    if (g->nblk < pg * n_local || u->nblk < pu * n_local || dn->nblk < pd * n_local)
+        return decline("expert tensor smaller than n_expert planes");
+    L.g = g->w;
+    L.u = u->w;
+    L.dn = dn->w;
+    L.plane_blk_g = pg;
+    L.plane_blk_u = pu;
+    L.plane_blk_dn = pd;
+    L.ffn = (int)ffn;
+    L.dim = (int)dim;
+    L.has_shared = 0;
+    L.shexp_ffn = 0;
+    if (sh[0]) {
+        if (int rc = check_moe_types(sh[0], sh[1], sh[2])) return rc;
+        if (dim % block_elems(sh[0]->type) || dim % block_elems(sh[1]->type) ||
+            shexp_ffn % block_elems(sh[2]->type) || shexp_ffn % 32 || shexp_ffn == 0)
+            return decline("shared expert shape is not a whole number of blocks");
+        L.has_shared = 1;
+        L.sg = sh[0]->w;
+        L.su = sh[1]->w;
+        L.sdn = sh[2]->w;
+        L.shexp_ffn = (int)shexp_ffn;
+    }
+    return 0;
+}
+
+bool any_type(const RoutedLayerDev &L, bool k256) {
+    bool r = act256(L.g.type) == k256 || act256(L.u.type) == k256;
+    if (L.has_shared) r = r || act256(L.sg.type) == k256 || act256(L.su.type) == k256;
+    return r;
+}
+
+// Device-side forward of a routed MoE layer (routing on the device).
+int moe_routed_dev(const RoutedLayerDev &L0, size_t T, const float *d_x, const float *d_logits, const float *d_bias,
+                   float *d_out, const float *d_residual, cudaStream_t st) {
+    RoutedLayerDev L = L0;
+    const size_t max_ffn = std::max<size_t>(L.ffn, L.has_shared ? L.shexp_ffn : 0);
+    const size_t n_slots = T * L.n_used + (L.has_shared ? T : 0);
+    if (int rc = ensure_moe_scratch(T, L.dim, max_ffn, L.n_expert, n_slots)) return rc;
+    launch_route_slots(d_logits, d_bias, (int)T, L, S.ids.as<int>(), S.gates.as<float>(), S.slots.as<Slot>(),
+                       (int)align256(max_ffn), st);
+    return run_experts(T, L.dim, L.n_used, L.has_shared, n_slots, max_ffn, any_type(L, true), any_type(L, false), d_x,
+                       d_out, d_residual, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int loom_cuda_init(int device) {
+    if (g_inited) return device == g_device ? LOOM_CUDA_OK : decline("already initialised on another device");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return decline("no CUDA device");
+    if (device < 0 || device >= n) return decline("device index out of range");
+    CK(cudaSetDevice(device));
+    cudaDeviceProp p;
+    CK(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10) return decline("this backend is built for sm_100a (B200)");
+    CK(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking));
+    g_device = device;
+    g_inited = true;
+    return LOOM_CUDA_OK;
+}
+
+void loom_cuda_clear_weight_cache(void) {
+    if (!g_inited) return;
+    cudaStreamSynchronize(g_stream);
+    for (auto &kv : g_cache) {
+        auto it = g_tensors.find(kv.second);
+        if (it != g_tensors.end()) {
+            cudaFree(it->second.base);
+            g_tensors.erase(it);
+        }
+    }
+    g_cache.clear();
+}
+
+void loom_cuda_shutdown(void) {
+    if (!g_inited) return;
+    cudaStreamSynchronize(g_stream);
+    for (auto &kv : g_tensors) cudaFree(kv.second.base);
+    g_tensors.clear();
+    g_cache.clear();
+    for (auto &a : g_arenas)
+        if (a.dev) cudaFree(a.dev);
+    g_arenas.clear();
+    for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
+                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.io_in, &S.io_out, &S.io_aux, &S.raw}) {
+        if (b->p) cudaFree(b->p);
+        b->p = nullptr;
+        b->cap = 0;
+    }
+    for (HBuf *b : {&S.h_in, &S.h_out}) {
+        if (b->p) cudaFreeHost(b->p);
+        b->p = nullptr;
+        b->cap = 0;
+    }
+    cudaStreamDestroy(g_stream);
+    g_stream = nullptr;
+    g_inited = false;
+    g_device = -1;
+}
+
+void loom_cuda_parallel_begin(size_t n) {
+    (void)n;
+    if (!g_inited) loom_cuda_init(0);
+}
+void loom_cuda_parallel_end(void) {}
+size_t loom_cuda_max_batch(void) { return 64; }
+
+int loom_cuda_register_arena(const void *mem, size_t bytes) {
+    if (int rc = need_init()) return rc;
+    if (!mem || bytes == 0) return decline("empty arena");
+    g_arenas.push_back(Arena{static_cast<const uint8_t *>(mem), bytes, nullptr});
+    return LOOM_CUDA_OK;
+}
+
+size_t loom_cuda_materialize_arenas(void) {
+    if (!g_inited) {
+        g_arena_err = "backend not initialised";
+        return 0;
+    }
+    size_t total = 0;
+    for (auto &a : g_arenas) {
+        if (!a.dev) {
+            cudaError_t e = cudaMalloc(&a.dev, a.bytes);
+            if (e != cudaSuccess) {
+                a.dev = nullptr;
+                g_arena_err = std::string("cudaMalloc(arena): ") + cudaGetErrorString(e);
+                return 0;
+            }
+            e = cudaMemcpy(a.dev, a.host, a.bytes, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                cudaFree(a.dev);
+                a.dev = nullptr;
+                g_arena_err = std::string("arena upload: ") + cudaGetErrorString(e);
+                return 0;
+            }
+        }
+        total += a.bytes;
+    }
+    g_arena_err.clear();
+    return total;
+}
+
+const char *loom_cuda_arena_error(void) { return g_arena_err.empty() ? nullptr : g_arena_err.c_str(); }
+
+size_t loom_cuda_take_cmdbuf_count(void) {
+    size_t n = g_cmdbufs;
+    g_cmdbufs = 0;
+    return n;
+}
+
+uint64_t loom_cuda_kernel_launches(void) { return loom::launches(); }
+
+size_t loom_cuda_last_error(char *buf, size_t len) {
+    if (buf && len) {
+        size_t n = std::min(len - 1, g_err.size());
+        memcpy(buf, g_err.data(), n);
+        buf[n] = 0;
+    }
+    return g_err.size();
+}
+
+void *loom_cuda_stream(void) { return g_stream; }
+
+int loom_cuda_sync(void) {
+    if (int rc = need_init()) return rc;
+    CK(cudaStreamSynchronize(g_stream));
+    return LOOM_CUDA_OK;
+}
+
+// ---- seam ops -------------------------------------------------------------------
+
+int loom_cuda_matvec(int type, float *out, const void *w, size_t w_bytes, const float *x, size_t rows, size_t cols) {
+    return loom_cuda_matmul(type, out, w, w_bytes, x, 1, rows, cols);
+}
+
+int loom_cuda_matmul(int type, float *out, const void *w, size_t w_bytes, const float *xs, size_t n, size_t rows,
+                     size_t cols) {
+    if (int rc = need_init()) return rc;
+    if (!type_ok(type)) return decline("unsupported ggml type");
+    const size_t be = block_elems(type);
+    if (cols == 0 || cols % be) return decline("cols is not a whole number of blocks");
+    if (rows > (1u << 30) || cols > (1u << 24) || n > (1u << 20)) return decline("shape out of range");
+    if (w_bytes < rows * (cols / be) * (size_t)block_bytes(type)) return decline("weight slice shorter than rows x cols");
+    if (n == 0 || rows == 0) return LOOM_CUDA_OK;
+    Tensor *t;
+    if (int rc = resolve(type, w, w_bytes, t)) return rc;
+    const size_t in_b = n * cols * 4, out_b = n * rows * 4;
+    if (int rc = S.h_in.ensure(in_b)) return rc;
+    if (int rc = S.h_out.ensure(out_b)) return rc;
+    if (int rc = S.io_in.ensure(in_b)) return rc;
+    if (int rc = S.io_out.ensure(out_b)) return rc;
+    memcpy(S.h_in.p, xs, in_b);
+    CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
+    if (type == T_F32) {
+        launch_mm_f32(reinterpret_cast<const float *>(t->base), (int)rows, (int)cols, S.io_in.as<float>(), (int)n,
+                      S.io_out.as<float>(), g_stream);
+    } else {
+        if (int rc = ensure_xq(n, cols)) return rc;
+        quantize_into(S.io_in.as<float>(), n, cols, act256(type), g_stream);
+        launch_mm(t->w, 0, (int)rows, (int)cols, make_xq(act256(type), cols), (int)n, S.io_out.as<float>(), g_stream);
+    }
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, out_b, cudaMemcpyDeviceToHost, g_stream));
+    CK(cudaStreamSynchronize(g_stream));
+    memcpy(out, S.h_out.p, out_b);
+    g_cmdbufs++;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_dequant_row(int type, float *out, const void *w, size_t w_bytes, size_t r, size_t cols) {
+    if (int rc = need_init()) return rc;
+    if (!type_ok(type)) return decline("unsupported ggml type");
+    const size_t be = block_elems(type);
+    if (cols == 0 || cols % be) return decline("cols is not a whole number of blocks");
+    const size_t rb = (cols / be) * block_bytes(type);
+    if (w_bytes < (r + 1) * rb) return decline("row out of range");
+    Tensor *t;
+    if (int rc = resolve(type, w, w_bytes, t)) return rc;
+    if (int rc = S.io_out.ensure(cols * 4)) return rc;
+    if (int rc = S.h_out.ensure(cols * 4)) return rc;
+    launch_dequant(t->w, (uint64_t)r * (cols / be), cols / be, S.io_out.as<float>(), g_stream);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, cols * 4, cudaMemcpyDeviceToHost, g_stream));
+    CK(cudaStreamSynchronize(g_stream));
+    memcpy(out, S.h_out.p, cols * 4);
+    g_cmdbufs++;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_moe_route(const float *logits, const float *bias, size_t n_expert, uint32_t *ids_out, float *gates_out,
+                        size_t n_used, int gating_sigmoid, int weights_norm, float weights_scale) {
+    if (int rc = need_init()) return rc;
+    if (n_expert == 0 || n_expert > 1024 || n_used == 0 || n_used > 64 || n_used > n_expert)
+        return decline("router shape out of range (moe.zig:48-49)");
+    const size_t in_b = n_expert * 4 * 2, out_b = n_used * 8;
+    if (int rc = S.h_in.ensure(in_b)) return rc;
+    if (int rc = S.h_out.ensure(out_b)) return rc;
+    if (int rc = S.io_in.ensure(in_b)) return rc;
+    if (int rc = S.io_out.ensure(out_b)) return rc;
+    memcpy(S.h_in.p, logits, n_expert * 4);
+    if (bias) memcpy(S.h_in.as<float>() + n_expert, bias, n_expert * 4);
+    CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, bias ? in_b : n_expert * 4, cudaMemcpyHostToDevice, g_stream));
+    int *d_ids = S.io_out.as<int>();
+    float *d_g = S.io_out.as<float>() + n_used;
+    launch_route(S.io_in.as<float>(), bias ? S.io_in.as<float>() + n_expert : nullptr, 1, (int)n_expert, (int)n_used,
+                 gating_sigmoid ? 2 : 1, weights_norm, weights_scale, d_ids, d_g, g_stream);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, out_b, cudaMemcpyDeviceToHost, g_stream));
+    CK(cudaStreamSynchronize(g_stream));
+    memcpy(ids_out, S.h_out.p, n_used * 4);
+    memcpy(gates_out, S.h_out.as<float>() + n_used, n_used * 4);
+    g_cmdbufs++;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_moe_ffn_block(const float *normed, size_t dim, const loom_expert *experts, size_t n, float *out) {
+    if (int rc = need_init()) return rc;
+    if (n == 0 || n > 65) return decline("expert count out of range");
+    if (dim == 0 || dim % 32) return decline("dim is not a whole number of blocks");
+    // Resolve everything before launching anything: a decline leaves no work behind.
+    std::vector<Slot> host(n);
+    size_t max_ffn = 0;
+    bool need256 = false, need32 = false;
+    for (size_t k = 0; k < n; k++) {
+        const loom_expert &e = experts[k];
+        Tensor *g, *u, *d;
+        if (int rc = resolve(e.gate.ggml_type, e.gate.data, e.gate.bytes, g)) return rc;
+        if (int rc = resolve(e.up.ggml_type, e.up.data, e.up.bytes, u)) return rc;
+        if (int rc = resolve(e.down.ggml_type, e.down.data, e.down.bytes, d)) return rc;
+        if (int rc = check_moe_types(g, u, d)) return rc;
+        if (dim % block_elems(g->type) || dim % block_elems(u->type) || e.ffn % block_elems(d->type) || e.ffn % 32 ||
+            e.ffn == 0)
+            return decline("expert shape is not a whole number of blocks");
+        if (g->nblk < e.ffn * (dim / block_elems(g->type)) || u->nblk < e.ffn * (dim / block_elems(u->type)) ||
+            d->nblk < dim * (e.ffn / block_elems(d->type)))
+            return decline("expert slice shorter than its shape");
+        max_ffn = std::max(max_ffn, e.ffn);
+        need256 |= act256(g->type) || act256(u->type);
+        need32 |= !act256(g->type) || !act256(u->type);
+        host[k].g = g->w;
+        host[k].u = u->w;
+        host[k].dn = d->w;
+        host[k].gb_g = host[k].gb_u = host[k].gb_dn = 0;
+        host[k].ffn = (int)e.ffn;
+        host[k].token = 0;
+        host[k].weight = e.weight;
+    }
+    const size_t act_stride = align256(max_ffn);
+    for (size_t k = 0; k < n; k++) host[k].act_off = (int)(k * act_stride);
+    if (int rc = ensure_moe_scratch(1, dim, max_ffn, 1, n)) return rc;
+    const size_t slot_b = n * sizeof(Slot);
+    if (int rc = S.h_in.ensure(align256(slot_b) + dim * 4)) return rc;
+    if (int rc = S.h_out.ensure(dim * 4)) return rc;
+    if (int rc = S.io_in.ensure(dim * 4)) return rc;
+    if (int rc = S.io_out.ensure(dim * 4)) return rc;
+    memcpy(S.h_in.p, host.data(), slot_b);
+    memcpy(S.h_in.as<uint8_t>() + align256(slot_b), normed, dim * 4);
+    CK(cudaMemcpyAsync(S.slots.p, S.h_in.p, slot_b, cudaMemcpyHostToDevice, g_stream));
+    CK(cudaMemcpyAsync(S.io_in.p, S.h_in.as<uint8_t>() + align256(slot_b), dim * 4, cudaMemcpyHostToDevice, g_stream));
+    if (int rc = run_experts(1, dim, (int)n, 0, n, max_ffn, need256, need32, S.io_in.as<float>(), S.io_out.as<float>(),
+                             nullptr, g_stream))
+        return rc;
+    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
+    CK(cudaStreamSynchronize(g_stream));
+    memcpy(out, S.h_out.p, dim * 4);
+    g_cmdbufs++;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_moe_ffn_routed(const float *normed, size_t dim, const float *logits, const float *bias, loom_weight gate,
+                             loom_weight up, loom_weight down, const loom_weight *shexp3, size_t ffn, size_t shexp_ffn,
+                             loom_routed_cfg cfg, float *out) {
+    if (int rc = need_init()) return rc;
+    if (cfg.n_expert == 0 || cfg.n_expert > 1024 || cfg.n_used == 0 || cfg.n_used > 64 || cfg.n_used > cfg.n_expert)
+        return decline("router shape out of range (moe.zig:48-49)");
+    if (dim == 0 || ffn == 0) return decline("empty layer");
+    Tensor *g, *u, *d;
+    if (int rc = resolve(gate.ggml_type, gate.data, gate.bytes, g)) return rc;
+    if (int rc = resolve(up.ggml_type, up.data, up.bytes, u)) return rc;
+    if (int rc = resolve(down.ggml_type, down.data, down.bytes, d)) return rc;
+    const Tensor *sh[3] = {nullptr, nullptr, nullptr};
+    if (shexp3) {
+        for (int i = 0; i < 3; i++) {
+            Tensor *t;
+            if (int rc = resolve(shexp3[i].ggml_type, shexp3[i].data, shexp3[i].bytes, t)) return rc;
+            sh[i] = t;
+        }
+    }
+    RoutedLayerDev L{};
+    if (int rc = routed_layer(L, g, u, d, dim, ffn, cfg.n_expert, sh, shexp_ffn)) return rc;
+    L.n_expert = (int)cfg.n_expert;
+    L.n_used = (int)cfg.n_used;
+    L.gating = cfg.gating_sigmoid ? 2 : 1;
+    L.weights_norm = cfg.weights_norm;
+    L.weights_scale = cfg.weights_scale;
+    L.expert0 = 0;
+    L.n_local = (int)cfg.n_expert;
+    const size_t in_b = (dim + 2 * cfg.n_expert) * 4;
+    if (int rc = S.h_in.ensure(in_b)) return rc;
+    if (int rc = S.h_out.ensure(dim * 4)) return rc;
+    if (int rc = S.io_in.ensure(in_b)) return rc;
+    if (int rc = S.io_out.ensure(dim * 4)) return rc;
+    float *hin = S.h_in.as<float>();
+    memcpy(hin, normed, dim * 4);
+    memcpy(hin + dim, logits, cfg.n_expert * 4);
+    if (bias) memcpy(hin + dim + cfg.n_expert, bias, cfg.n_expert * 4);
+    CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
+    const float *dx = S.io_in.as<float>();
+    if (int rc = moe_routed_dev(L, 1, dx, dx + dim, bias ? dx + dim + cfg.n_expert : nullptr, S.io_out.as<float>(),
+                                nullptr, g_stream))
+        return rc;
+    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
+    CK(cudaStreamSynchronize(g_stream));
+    memcpy(out, S.h_out.p, dim * 4);
+    g_cmdbufs++;
+    return LOOM_CUDA_OK;
+}
+
+// ---- device-resident API ------------------------------------------------------------
+
+int loom_cuda_tensor_upload(int type, const void *data, size_t bytes, loom_tensor *out) {
+    if (int rc = need_init()) return rc;
+    uint64_t h = 0;
+    if (int rc = upload_tensor(type, data, bytes, h)) return rc;
+    *out = h;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_tensor_synth(int type, uint64_t nblk, uint64_t seed, float sigma, loom_tensor *out) {
+    if (int rc = need_init()) return rc;
+    if (!type_ok(type)) return decline("unsupported ggml type");
+    Tensor t;
+    if (int rc = alloc_tensor(type, nblk, t)) return rc;
+    const size_t bb = block_bytes(type);
+    if (type == T_F32 || type == T_Q4_K) {
+        launch_synth(type, t.base, 0, nblk, seed, sigma, g_stream);
+    } else {
+        // generate GGUF bytes in bounded chunks, then repack each into the layout
+        const uint64_t chunk = std::max<uint64_t>(1, (256ull << 20) / bb);
+        if (int rc = S.raw.ensure(std::min<uint64_t>(chunk, nblk) * bb)) {
+            cudaFree(t.base);
+            return rc;
+        }
+        for (uint64_t b0 = 0; b0 < nblk; b0 += chunk) {
+            const uint64_t nb = std::min(chunk, nblk - b0);
+            launch_synth(type, S.raw.as<uint8_t>(), b0, nb, seed, sigma, g_stream);
+            uint8_t *q = t.base + b0 * layout_qbytes(type);
+            uint8_t *sc = t.w.sc ? const_cast<uint8_t *>(t.w.sc) + b0 * 16 : nullptr;
+            uint16_t *d = t.w.d ? const_cast<uint16_t *>(t.w.d) + b0 : nullptr;
+            launch_repack(type, S.raw.as<uint8_t>(), q, sc, d, nb, g_stream);
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) {
+        cudaFree(t.base);
+        return fail("tensor_synth", e);
+    }
+    uint64_t h = g_next_handle++;
+    g_tensors[h] = t;
+    *out = h;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_tensor_download(loom_tensor h, void *dst, size_t bytes) {
+    if (int rc = need_init()) return rc;
+    Tensor *t = lookup(h);
+    if (!t) return decline("unknown tensor");
+    const size_t raw_b = t->nblk * (size_t)block_bytes(t->type);
+    if (bytes != raw_b) return decline("size mismatch");
+    if (t->type == T_F32 || t->type == T_Q4_K) {
+        CK(cudaMemcpyAsync(dst, t->base, raw_b, cudaMemcpyDeviceToHost, g_stream));
+    } else {
+        if (int rc = S.raw.ensure(raw_b)) return rc;
+        launch_unpack(t->type, t->w, S.raw.as<uint8_t>(), t->nblk, g_stream);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(dst, S.raw.p, raw_b, cudaMemcpyDeviceToHost, g_stream));
+    }
+    CK(cudaStreamSynchronize(g_stream));
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_tensor_free(loom_tensor h) {
+    if (int rc = need_init()) return rc;
+    Tensor *t = lookup(h);
+    if (!t) return decline("unknown tensor");
+    CK(cudaStreamSynchronize(g_stream));
+    cudaFree(t->base);
+    for (auto it = g_cache.begin(); it != g_cache.end();)
+        it = it->second == h ? g_cache.erase(it) : std::next(it);
+    g_tensors.erase(h);
+    return LOOM_CUDA_OK;
+}
+
+size_t loom_cuda_tensor_device_bytes(loom_tensor h) {
+    Tensor *t = lookup(h);
+    return t ? t->dev_bytes : 0;
+}
+
+int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t n_used) {
+    if (int rc = need_init()) return rc;
+    const size_t n_slots = T * (n_used + 1);
+    if (int rc = ensure_moe_scratch(T, dim, ffn, n_expert, n_slots)) return rc;
+    CK(cudaStreamSynchronize(g_stream));
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, const float *d_residual,
+                          const float *d_logits, uint32_t *d_ids, void *stream) {
+    if (int rc = need_init()) return rc;
+    if (!desc || T == 0) return decline("empty forward");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    const loom_moe_desc &D = *desc;
+    if (D.n_expert == 0 || D.n_expert > 1024 || D.n_used == 0 || D.n_used > 64 || D.n_used > D.n_expert)
+        return decline("router shape out of range (moe.zig:48-49)");
+    const size_t n_local = D.n_local ? D.n_local : D.n_expert;
+    if (D.expert0 + n_local > D.n_expert) return decline("expert range out of bounds");
+    Tensor *g = lookup(D.gate), *u = lookup(D.up), *dn = lookup(D.down);
+    const Tensor *sh[3] = {nullptr, nullptr, nullptr};
+    if (D.shexp_gate) {
+        sh[0] = lookup(D.shexp_gate);
+        sh[1] = lookup(D.shexp_up);
+        sh[2] = lookup(D.shexp_down);
+        if (!sh[0] || !sh[1] || !sh[2]) return decline("unknown shared-expert tensor");
+    }
+    RoutedLayerDev L{};
+    if (int rc = routed_layer(L, g, u, dn, D.dim, D.ffn, n_local, sh, D.shexp_ffn)) return rc;
+    L.n_expert = (int)D.n_expert;
+    L.n_used = (int)D.n_used;
+    L.gating = D.gating ? D.gating : 1;
+    L.weights_norm = D.weights_norm;
+    L.weights_scale = D.weights_scale;
+    L.expert0 = (int)D.expert0;
+    L.n_local = (int)n_local;
+    const float *bias = nullptr;
+    if (D.router_bias) {
+        Tensor *b = lookup(D.router_bias);
+        if (!b || b->type != T_F32 || b->nblk < D.n_expert) return decline("router bias must be f32 [n_expert]");
+        bias = reinterpret_cast<const float *>(b->base);
+    }
+    const size_t max_ffn = std::max<size_t>(D.ffn, sh[0] ? D.shexp_ffn : 0);
+    const size_t n_slots = T * D.n_used + (sh[0] ? T : 0);
+    if (int rc = ensure_moe_scratch(T, D.dim, max_ffn, D.n_expert, n_slots)) return rc;
+    const float *logits = d_logits;
+    if (!logits) {
+        Tensor *r = lookup(D.router);
+        if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
+        launch_mm_f32(reinterpret_cast<const float *>(r->base), (int)D.n_expert, (int)D.dim, d_x, (int)T,
+                      S.logits.as<float>(), st);
+        logits = S.logits.as<float>();
+    }
+    if (int rc = moe_routed_dev(L, T, d_x, logits, bias, d_out, d_residual, st)) return rc;
+    if (d_ids) CK(cudaMemcpyAsync(d_ids, S.ids.p, T * D.n_used * 4, cudaMemcpyDeviceToDevice, st));
+    CK(cudaGetLastError());
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_tensor_matmul(loom_tensor h, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
+                            void *stream) {
+    if (int rc = need_init()) return rc;
+    Tensor *t = lookup(h);
+    if (!t) return decline("unknown tensor");
+    const size_t be = block_elems(t->type);
+    if (cols == 0 || cols % be || t->nblk < rows * (cols / be)) return decline("shape does not fit the tensor");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    if (t->type == T_F32) {
+        launch_mm_f32(reinterpret_cast<const float *>(t->base), (int)rows, (int)cols, d_xs, (int)n, d_out, st);
+    } else {
+        if (int rc = ensure_xq(n, cols)) return rc;
+        quantize_into(d_xs, n, cols, act256(t->type), st);
+        launch_mm(t->w, 0, (int)rows, (int)cols, make_xq(act256(t->type), cols), (int)n, d_out, st);
+    }
+    CK(cudaGetLastError());
+    return LOOM_CUDA_OK;
+}
+
+}  // extern "C"

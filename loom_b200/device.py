@@ -1,0 +1,103 @@
+"""Device-resident API of the CUDA backend (include/loom_cuda.h, second half):
+tensors that live on the GPU in the backend's layout and whole MoE layers run
+on device buffers. Device buffers are torch CUDA tensors (plumbing only: the
+kernels are the backend's own)."""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+
+BLOCK_ELEMS = {0: 1, 2: 32, 8: 32, 12: 256, 14: 256}
+BLOCK_BYTES = {0: 4, 2: 18, 8: 34, 12: 144, 14: 210}
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class DeviceTensor:
+    def __init__(self, handle: int, ty: int, nblk: int):
+        self.handle, self.ty, self.nblk = handle, ty, nblk
+
+    @classmethod
+    def upload(cls, ty: int, data: np.ndarray) -> "DeviceTensor":
+        d = np.ascontiguousarray(data).view(np.uint8)
+        h = C.c_uint64(0)
+        _lib.must(_lib.lib().loom_cuda_tensor_upload(ty, d.ctypes.data_as(C.c_void_p), d.nbytes, C.byref(h)),
+                  "tensor_upload")
+        return cls(h.value, ty, d.nbytes // BLOCK_BYTES[ty])
+
+    @classmethod
+    def synth(cls, ty: int, nblk: int, seed: int, sigma: float = 1.0) -> "DeviceTensor":
+        h = C.c_uint64(0)
+        _lib.must(_lib.lib().loom_cuda_tensor_synth(ty, nblk, seed, sigma, C.byref(h)), "tensor_synth")
+        return cls(h.value, ty, nblk)
+
+    def download(self) -> np.ndarray:
+        out = np.empty(self.nblk * BLOCK_BYTES[self.ty], np.uint8)
+        _lib.must(_lib.lib().loom_cuda_tensor_download(self.handle, out.ctypes.data_as(C.c_void_p), out.nbytes),
+                  "tensor_download")
+        return out
+
+    @property
+    def device_bytes(self) -> int:
+        return int(_lib.lib().loom_cuda_tensor_device_bytes(self.handle))
+
+    def free(self) -> None:
+        if self.handle:
+            _lib.lib().loom_cuda_tensor_free(self.handle)
+            self.handle = 0
+
+
+@dataclass
+class MoeLayer:
+    dim: int
+    ffn: int
+    n_expert: int
+    n_used: int
+    gate: DeviceTensor
+    up: DeviceTensor
+    down: DeviceTensor
+    router: Optional[DeviceTensor] = None
+    router_bias: Optional[DeviceTensor] = None
+    gating: int = 1
+    weights_norm: bool = True
+    weights_scale: float = 1.0
+    shexp: Optional[tuple] = None
+    shexp_ffn: int = 0
+    expert0: int = 0
+    n_local: int = 0
+
+    def desc(self) -> _lib.MoeDesc:
+        h = lambda t: t.handle if t is not None else 0  # noqa: E731
+        sh = self.shexp or (None, None, None)
+        return _lib.MoeDesc(self.dim, self.ffn, self.n_expert, self.n_used, self.gating, int(self.weights_norm),
+                            self.weights_scale, h(self.router), h(self.router_bias), h(self.gate), h(self.up),
+                            h(self.down), h(sh[0]), h(sh[1]), h(sh[2]), self.shexp_ffn, self.expert0,
+                            self.n_local or self.n_expert)
+
+    def forward(self, x, out, residual=None, logits=None, ids=None, stream=None, desc=None) -> None:
+        """x, out: torch cuda float32 [T, dim]; ids: torch cuda int32 [T, n_used]."""
+        d = desc if desc is not None else self.desc()
+        T = x.shape[0]
+        rc = _lib.lib().loom_cuda_moe_forward(C.byref(d), _ptr(x), T, _ptr(out), _ptr(residual), _ptr(logits),
+                                              _ptr(ids), stream)
+        _lib.must(rc, "moe_forward")
+
+
+def reserve(T: int, dim: int, ffn: int, n_expert: int, n_used: int) -> None:
+    _lib.must(_lib.lib().loom_cuda_reserve(T, dim, ffn, n_expert, n_used), "reserve")
+
+
+def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -> None:
+    _lib.must(_lib.lib().loom_cuda_tensor_matmul(w.handle, rows, cols, _ptr(xs), xs.shape[0], _ptr(out), stream),
+              "tensor_matmul")
+
+
+def sync() -> None:
+    _lib.must(_lib.lib().loom_cuda_sync(), "sync")

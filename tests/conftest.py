@@ -17,3 +17,23 @@ def orc():
     from oracle import oracle
     oracle.lib()
     return oracle
+
+
+@pytest.fixture(scope="session")
+def be():
+    """The CUDA backend, initialised on cuda:0 (gpu tests only)."""
+    from loom_b200 import backend
+    backend.init(0)
+    return backend
+
+
+def bits(a):
+    import numpy as np
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def rel_l2(got, want):
+    import numpy as np
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))

@@ -1,0 +1,29 @@
+"""CPU checks of the C ABI library: it loads, exports every symbol the public
+header declares, and declines cleanly when no device is initialised."""
+import ctypes as C
+
+import numpy as np
+
+from loom_b200 import _lib
+
+
+def test_library_exports_every_header_symbol():
+    L = _lib.lib()
+    syms = _lib.header_symbols()
+    assert len(syms) >= 20
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, missing
+
+
+def test_seam_declines_before_init():
+    L = _lib.lib()
+    out = np.zeros(4, np.float32)
+    x = np.zeros(256, np.float32)
+    w = np.zeros(144 * 4, np.uint8)
+    rc = L.loom_cuda_matvec(12, out.ctypes.data_as(C.c_void_p), w.ctypes.data_as(C.c_void_p), w.nbytes,
+                            x.ctypes.data_as(C.c_void_p), 4, 256)
+    assert rc == _lib.DECLINED
+    assert "init" in _lib.last_error()
+    assert L.loom_cuda_register_arena(w.ctypes.data_as(C.c_void_p), w.nbytes) == _lib.DECLINED
+    assert L.loom_cuda_materialize_arenas() == 0
+    assert L.loom_cuda_take_cmdbuf_count() == 0

@@ -1,0 +1,155 @@
+"""GPU parity of the fused MoE entry points against the CPU oracle at the
+benchmark shapes: moeFfnBlock, moeFfnBlockRouted (Qwen3-30B-A3B layer,
+DeepSeek-V2-Lite layer with shared experts, sigmoid+bias routing), and the
+device-resident layer with its own router at T=1 and T=64.
+
+Tolerances (north star): top-k ids identical wherever the logit gap exceeds
+1e-4; FFN outputs within 2e-3 relative L2."""
+import numpy as np
+import pytest
+import torch
+
+from loom_b200 import backend as B
+from loom_b200.device import DeviceTensor, MoeLayer
+from tests.conftest import bits, rel_l2
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def synth_layer(orc, seed, ne, dim, ffn, gt=12, ut=12, dt=14):
+    rb = lambda t, n: orc.row_bytes(t, n)  # noqa: E731
+    bg, bu = ffn * dim // orc.BLOCK_ELEMS[gt], ffn * dim // orc.BLOCK_ELEMS[ut]
+    bd = dim * ffn // orc.BLOCK_ELEMS[dt]
+    g = orc.synth(gt, ne * bg, seed * 10 + 1)
+    u = orc.synth(ut, ne * bu, seed * 10 + 2)
+    d = orc.synth(dt, ne * bd, seed * 10 + 3)
+    assert g.size == ne * ffn * rb(gt, dim)
+    return g, u, d
+
+
+def test_moe_ffn_block_mixed_types(be, orc):
+    rng = np.random.default_rng(3)
+    dim, ffn = 1024, 512
+    from tests import npref
+    ex, oex = [], []
+    for k, (gt, ut, dt, w) in enumerate([(12, 8, 2, 0.5), (14, 12, 12, 0.3), (2, 2, 8, 0.2), (12, 12, 14, 1.0)]):
+        g = npref.random_blocks(rng, gt, ffn, dim)
+        u = npref.random_blocks(rng, ut, ffn, dim)
+        d = npref.random_blocks(rng, dt, dim, ffn)
+        ex.append(B.ExpertRef(B.WeightRef(gt, g), B.WeightRef(ut, u), B.WeightRef(dt, d), w, ffn))
+        oex.append(dict(gate_type=gt, up_type=ut, down_type=dt, gate=g, up=u, down=d, weight=w, ffn=ffn))
+    x = rng.standard_normal(dim).astype(np.float32)
+    out = np.full(dim, np.nan, np.float32)
+    B.takeCmdBufCount()
+    assert B.moeFfnBlock(x, ex, out)
+    assert B.takeCmdBufCount() == 1
+    want = orc.moe_ffn_block(x, oex, dim)
+    assert rel_l2(out, want) < TOL
+    assert np.mean(bits(out) == bits(want)) > 0.9  # identical except where an ulp of expf moved an int8
+
+
+def test_moe_ffn_routed_qwen3_layer(be, orc):
+    """BASELINE config 2 (Qwen3-30B-A3B MoE layer): 128 experts, top-8 softmax+renorm,
+    gate/up Q4_K [768x2048], down Q6_K [2048x768]."""
+    ne, k, dim, ffn = 128, 8, 2048, 768
+    g, u, d = synth_layer(orc, 1, ne, dim, ffn)
+    rng = np.random.default_rng(9)
+    cfg = B.RoutedCfg(ne, k, False, True, 1.0)
+    for trial in range(4):
+        x = rng.standard_normal(dim).astype(np.float32)
+        logits = (rng.standard_normal(ne) * 0.5).astype(np.float32)
+        out = np.full(dim, np.nan, np.float32)
+        assert B.moeFfnBlockRouted(x, logits, None, B.WeightRef(12, g), B.WeightRef(12, u), B.WeightRef(14, d), None,
+                                   ffn, 0, cfg, out)
+        want = orc.moe_ffn_routed(x, logits, (12, g), (12, u), (14, d), ffn, k)
+        assert rel_l2(out, want) < TOL, rel_l2(out, want)
+
+
+@pytest.mark.parametrize("sigmoid", [False, True])
+def test_moe_ffn_routed_deepseek_shared(be, orc, sigmoid):
+    """DeepSeek-V2-Lite-shaped layer: 64 experts top-6, moe_ffn 1408 (down Q8_0:
+    1408 is not a multiple of 256), 2 shared experts (2816), optional sigmoid
+    gating with selection bias and scale."""
+    ne, k, dim, ffn, sffn = 64, 6, 2048, 1408, 2816
+    g, u, d = synth_layer(orc, 2, ne, dim, ffn, 12, 12, 8)
+    sg, su, sd = synth_layer(orc, 3, 1, dim, sffn, 12, 12, 8)
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal(dim).astype(np.float32)
+    logits = rng.standard_normal(ne).astype(np.float32)
+    bias = (rng.standard_normal(ne) * 0.05).astype(np.float32) if sigmoid else None
+    scale = 2.5 if sigmoid else 1.0
+    cfg = B.RoutedCfg(ne, k, sigmoid, True, scale)
+    out = np.full(dim, np.nan, np.float32)
+    sh = [B.WeightRef(12, sg), B.WeightRef(12, su), B.WeightRef(8, sd)]
+    assert B.moeFfnBlockRouted(x, logits, bias, B.WeightRef(12, g), B.WeightRef(12, u), B.WeightRef(8, d), sh, ffn,
+                               sffn, cfg, out)
+    want = orc.moe_ffn_routed(x, logits, (12, g), (12, u), (8, d), ffn, k, gating_sigmoid=sigmoid,
+                              weights_scale=scale, bias=bias, shexp=[(12, sg), (12, su), (8, sd)], shexp_ffn=sffn)
+    assert rel_l2(out, want) < TOL
+
+
+@pytest.mark.parametrize("t", [0, 2, 8, 12, 14])
+def test_device_synth_matches_oracle(be, orc, t):
+    nblk = 1000
+    dt = DeviceTensor.synth(t, nblk, seed=77, sigma=0.02)
+    try:
+        got = dt.download()
+        want = orc.synth(t, nblk, seed=77, sigma=0.02).view(np.uint8)
+        assert np.array_equal(got, want)
+    finally:
+        dt.free()
+
+
+def test_arena_materialize_and_lookup(be, orc):
+    rng = np.random.default_rng(8)
+    from tests import npref
+    rows, cols = 96, 2048
+    arena = np.zeros(4096 + rows * orc.row_bytes(14, cols) + 1000, np.uint8)
+    w = npref.random_blocks(rng, 14, rows, cols)
+    arena[4096:4096 + w.size] = w
+    assert B.registerArena(arena)
+    assert B.materializeArenas() == arena.nbytes
+    assert B.arenaError() is None
+    x = rng.standard_normal(cols).astype(np.float32)
+    out = np.empty(rows, np.float32)
+    B.matvec(14, out, arena[4096:4096 + w.size], x, rows, cols)
+    assert np.array_equal(bits(out), bits(orc.matvec(14, w, x, rows, cols)))
+
+
+def _route_gaps_ok(logits_row, k):
+    s = np.sort(logits_row.astype(np.float64))[::-1]
+    return bool(np.all(s[:k] - s[1:k + 1] > 1e-4))
+
+
+@pytest.mark.parametrize("T", [1, 64])
+def test_device_layer_with_router(be, orc, T):
+    """The whole layer on the device (router GEMV -> route -> experts ->
+    combine) against the oracle's moeLayer at BASELINE config 2, T in {1, 64}."""
+    ne, k, dim, ffn = 128, 8, 2048, 768
+    g, u, d = synth_layer(orc, 4, ne, dim, ffn)
+    rw = orc.synth(0, ne * dim, seed=41, sigma=0.02)
+    x = orc.synth(0, T * dim, seed=42, sigma=1.0).reshape(T, dim)
+    L = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g), DeviceTensor.upload(12, u), DeviceTensor.upload(14, d),
+                 router=DeviceTensor.upload(0, rw))
+    xt = torch.from_numpy(x).cuda()
+    out = torch.full((T, dim), float("nan"), device="cuda")
+    ids = torch.zeros((T, k), dtype=torch.int32, device="cuda")
+    L.forward(xt, out, ids=ids)
+    torch.cuda.synchronize()
+    orc.parallel_begin(8)
+    try:
+        want, wids = orc.moe_layer(x, rw, (12, g), (12, u), (14, d), ffn, ne, k)
+        logits = orc.matmul(0, rw.view(np.uint8), x, ne, dim)
+    finally:
+        orc.parallel_end()
+    got, gids = out.cpu().numpy(), ids.cpu().numpy()
+    compared = 0
+    for t in range(T):
+        if _route_gaps_ok(logits[t], k):
+            assert list(gids[t]) == list(wids[t]), t
+            assert rel_l2(got[t], want[t]) < TOL, (t, rel_l2(got[t], want[t]))
+            compared += 1
+    assert compared >= max(1, T * 3 // 4)
+    for t in (L.gate, L.up, L.down, L.router):
+        t.free()
