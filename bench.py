@@ -220,19 +220,20 @@ def run_gpu(args):
     with torch.cuda.graph(g, stream=stream):
         step(torch.cuda.current_stream().cuda_stream)
     launches_per_step = B.kernelLaunches() - k0
-    for _ in range(args.warmup):
-        g.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as ck:
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
+    with torch.cuda.stream(stream):  # replay, events and timing all on the launching stream
+        for _ in range(args.warmup):
             g.replay()
-        e1.record(stream)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as ck:
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
         t = torch.tensor([ms], device="cuda")

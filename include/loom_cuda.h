@@ -176,6 +176,10 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);
+/* Test hook: 1 routes every MoE layer through the general slot kernels instead
+ * of the fused decode kernels (same numerics; used to cross-check the two).
+ * Returns the previous setting. */
+int loom_cuda_force_generic(int on);
 /* Synchronize the backend's stream. */
 int loom_cuda_sync(void);
 /* The backend's stream (cudaStream_t). */

@@ -88,6 +88,7 @@ def lib() -> C.CDLL:
         "loom_cuda_reserve": (i, [sz, sz, sz, sz, sz]),
         "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
         "loom_cuda_sync": (i, []),
+        "loom_cuda_force_generic": (i, [i]),
         "loom_cuda_stream": (vp, []),
     }
     for name, (res, args) in sig.items():

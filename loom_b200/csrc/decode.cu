@@ -1,0 +1,514 @@
+// decode.cu -- the fused MoE decode path: three kernels per layer chained
+// with programmatic dependent launch (PDL), each issuing its weight loads
+// before it waits for its producer.
+//
+//   k_router_route  router GEMV (dotF32 order) for 4 experts per CTA; the last
+//                   CTA of each token routes (moe.zig:106 route) and quantizes
+//                   the token's activation for the expert kernels. Router
+//                   weights are loaded BEFORE waiting for the previous layer.
+//   k_gateup_dec    gate and up rows of every (token, expert) slot + SwiGLU;
+//                   the last CTA of each slot quantizes the slot's activation
+//                   for the down projection.
+//   k_down_dec      per output row, the token's local experts' down rows
+//                   (weights loaded BEFORE waiting for k_gateup_dec), the
+//                   weighted combine in selection order, the shared expert and
+//                   the residual.
+//
+// Completion counters (one per token / per slot) live in scratch, start at
+// zero and are reset by the CTA that consumes them. Scratch written by an
+// earlier kernel is read through L2 (ld.global.cg).
+#include <cuda_runtime.h>
+
+#include "decode.cuh"
+#include "devutil.cuh"
+#include "warpdot.cuh"
+
+namespace loom {
+
+static inline unsigned cdivu(uint64_t a, uint64_t b) { return (unsigned)((a + b - 1) / b); }
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// ---- router + route + activation quantization ---------------------------------------
+
+constexpr int RR_WARPS = 4;
+constexpr int RR_CHUNK = 64;  // router weights per lane held in registers (2048 columns)
+
+__global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
+    extern __shared__ float smx[];  // x[dim] | scores[ne] | choice[ne]
+    __shared__ int last;
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int dim = A.dim, ne = A.n_expert;
+    const int row = blockIdx.x * RR_WARPS + warp;
+    const bool has_row = A.router && row < ne;
+    // 1. the first RR_CHUNK*32 weights of this warp's row, before the wait
+    float w[RR_CHUNK];
+    const int nfull = dim / 32;
+    if (has_row) {
+        const float *wr = A.router + (size_t)row * dim;
+#pragma unroll
+        for (int i = 0; i < RR_CHUNK; i++)
+            if (i < nfull) w[i] = __ldg(wr + i * 32 + lane);
+    }
+    pdl_wait();
+    pdl_trigger();
+    // 2. this token's activation into shared memory
+    const float *xt = A.x + (size_t)t * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = __ldcg(xt + i);
+    __syncthreads();
+    float *logits = A.logits + (size_t)t * ne;
+    if (A.router) {
+        if (has_row) {  // dotF32 (ggml.zig:198): lane j is accumulator lane j
+            const float *wr = A.router + (size_t)row * dim;
+            float a = 0.0f;
+#pragma unroll
+            for (int i = 0; i < RR_CHUNK; i++)
+                if (i < nfull) a = fadd(a, fmul(w[i], smx[i * 32 + lane]));
+            for (int i = RR_CHUNK; i < nfull; i++) a = fadd(a, fmul(__ldg(wr + i * 32 + lane), smx[i * 32 + lane]));
+            int i = nfull * 32;
+            for (; i + 8 <= dim; i += 8)
+                if (lane < 8) a = fadd(a, fmul(__ldg(wr + i + lane), smx[i + lane]));
+            const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
+            const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
+            const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
+            const float v = fadd(fadd(fadd(a, a8), a16), a24);
+            float r = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+            for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
+            for (; i < dim; i++) r = fadd(r, fmul(__ldg(wr + i), smx[i]));
+            if (lane == 0) logits[row] = r;
+        }
+        // 3. the last CTA of this token routes
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = atomicAdd(A.cnt_tok + t, 1) == (int)gridDim.x - 1;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+    }
+    float *scores = smx + dim, *choice = scores + ne;
+    if (warp == 0) {
+        const float *lg = A.router ? logits : A.logits_in + (size_t)t * ne;
+        // stage the logits in shared memory (through L2: other CTAs wrote them);
+        // each lane reads back only its own entries before overwriting them
+        for (int e = lane; e < ne; e += 32) choice[e] = __ldcg(lg + e);
+        __syncwarp();
+        route_warp(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice,
+                   A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
+        if (A.ids_out)
+            for (int k = lane; k < A.n_used; k += 32)
+                A.ids_out[(size_t)t * A.n_used + k] = A.ids[(size_t)t * A.n_used + k];
+    } else {
+        // quantize x in the format(s) the expert types read
+        const int nw = RR_WARPS - 1, wi = warp - 1;
+        if (A.need256)
+            for (int b = wi; b < dim / 256; b += nw)
+                quant_lane8(smx + b * 256 + lane * 8, true, 32, A.x256.q + (size_t)t * dim + b * 256 + lane * 8,
+                            A.x256.d + (size_t)t * (dim / 256) + b,
+                            A.x256.s + (size_t)t * (dim / 16) + b * 16 + lane / 2, nullptr, lane);
+        if (A.need32) {
+            const int nb = dim / 32, ng = (nb + 7) / 8;
+            for (int g = wi; g < ng; g += nw) {
+                const int b = g * 8 + lane / 4;
+                const int off = b * 32 + (lane & 3) * 8;
+                quant_lane8(smx + off, b < nb, 4, A.x32.q + (size_t)t * dim + off, A.x32.d + (size_t)t * (dim / 32) + b,
+                            nullptr, A.x32.s + (size_t)t * (dim / 32) + b, lane);
+            }
+        }
+    }
+    if (A.router && threadIdx.x == 0) A.cnt_tok[t] = 0;
+}
+
+// ---- slot description -------------------------------------------------------------
+
+struct SlotInfo {
+    int expert_local;  // -1 when not held here
+    int token;
+    int ffn;
+    bool shared;
+};
+
+__device__ __forceinline__ SlotInfo slot_info(const DecodeArgs &A, int slot) {
+    SlotInfo si;
+    const int nr = A.T * A.n_used;
+    if (slot < nr) {
+        si.token = slot / A.n_used;
+        const int le = __ldcg(A.ids + slot) - A.expert0;
+        si.expert_local = (le >= 0 && le < A.n_local) ? le : -1;
+        si.ffn = si.expert_local >= 0 ? A.ffn : 0;
+        si.shared = false;
+    } else {
+        si.token = slot - nr;
+        si.expert_local = 0;
+        si.ffn = A.shexp_ffn;
+        si.shared = true;
+    }
+    return si;
+}
+
+// stage `n` bytes (multiple of 16) from global (through L2) into shared memory
+__device__ __forceinline__ void stage16(void *dst, const void *src, int n) {
+    const int4 *s = reinterpret_cast<const int4 *>(src);
+    int4 *d = reinterpret_cast<int4 *>(dst);
+    for (int i = threadIdx.x; i < n / 16; i += blockDim.x) d[i] = __ldcg(s + i);
+}
+
+// ---- gate/up + SwiGLU ---------------------------------------------------------------
+
+constexpr int GU_WARPS = 4;
+constexpr int GU_NR = 2;  // rows per warp: streams = gate rows + up rows
+
+struct GateUpStreams {
+    WDev wg, wu;
+    uint64_t gb_g, gb_u;  // first block of the warp's first row
+    int nb;
+    XV x;
+    __device__ __forceinline__ void at(int s, WDev &w, uint64_t &gb, XV &xv) const {
+        const bool up = s >= GU_NR;
+        const int r = up ? s - GU_NR : s;
+        w = up ? wu : wg;
+        gb = (up ? gb_u : gb_g) + (uint64_t)r * nb;
+        xv = x;
+    }
+};
+
+template <int TY, int MAXU>
+__global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ int last;
+    pdl_wait();
+    pdl_trigger();
+    const int slot = blockIdx.y;
+    const SlotInfo si = slot_info(A, slot);
+    const int rows_cta = GU_WARPS * GU_NR;
+    const int nctas = (si.ffn + rows_cta - 1) / rows_cta;
+    if ((int)blockIdx.x >= nctas) return;
+    const int dim = A.dim;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // stage the token's quantized activation (gate and up share the K format)
+    int8_t *xq = reinterpret_cast<int8_t *>(sm);
+    float *xd = reinterpret_cast<float *>(sm + dim);
+    int32_t *xs = reinterpret_cast<int32_t *>(sm + dim + dim / 256 * 4);
+    stage16(xq, A.x256.q + (size_t)si.token * dim, dim);
+    for (int i = threadIdx.x; i < dim / 256; i += blockDim.x) xd[i] = __ldcg(A.x256.d + (size_t)si.token * (dim / 256) + i);
+    for (int i = threadIdx.x; i < dim / 16; i += blockDim.x) xs[i] = __ldcg(A.x256.s + (size_t)si.token * (dim / 16) + i);
+    __syncthreads();
+    const WDev wg = si.shared ? A.sg : A.g, wu = si.shared ? A.su : A.u;
+    const int nb = dim / 256;
+    const uint64_t plane = si.shared ? 0 : (uint64_t)si.expert_local * si.ffn * nb;
+    const int r0 = blockIdx.x * rows_cta + warp * GU_NR;
+    const int rmax = si.ffn - GU_NR;
+    const int rl = r0 <= rmax ? r0 : rmax;  // clamp the last (partial) group; its extra rows are not stored
+    GateUpStreams st{wg, wu, plane + (uint64_t)rl * nb, plane + (uint64_t)rl * nb, nb, XV{xq, xd, xs}};
+    WFrags<TY, MAXU> fr;
+    wd_load<TY, 2 * GU_NR, MAXU>(st, nb, 2 * GU_NR, fr, lane);
+    float acc[2 * GU_NR];
+    wd_finish<TY, 2 * GU_NR, MAXU>(st, nb, 2 * GU_NR, fr, acc, lane);
+    float *act = A.act + (size_t)slot * A.act_stride;
+    if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < GU_NR; i++) {
+            const int r = rl + i;
+            if (r >= r0 && r < si.ffn) {
+                const float g = acc[i], u = acc[GU_NR + i];
+                act[r] = fmul(fdiv(g, fadd(1.0f, expf(-g))), u);  // silu(g) * u (tensor.zig:30,53)
+            }
+        }
+    }
+    // the last CTA of this slot quantizes its activation for the down projection
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(A.cnt_slot + slot, 1) == nctas - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    float *xa = reinterpret_cast<float *>(sm);  // reuse: ffn floats
+    for (int i = threadIdx.x; i < si.ffn; i += blockDim.x) xa[i] = __ldcg(act + i);
+    __syncthreads();
+    const int dty = si.shared ? A.sdn.type : A.dn.type;
+    int8_t *q = A.aq + (size_t)slot * A.act_stride;
+    float *d = A.ad + (size_t)slot * (A.act_stride / 32);
+    int32_t *s = A.as + (size_t)slot * (A.act_stride / 16);
+    if (act256(dty)) {
+        for (int b = warp; b < si.ffn / 256; b += GU_WARPS)
+            quant_lane8(xa + b * 256 + lane * 8, true, 32, q + b * 256 + lane * 8, d + b, s + b * 16 + lane / 2, nullptr,
+                        lane);
+    } else {
+        const int nb32 = si.ffn / 32, ng = (nb32 + 7) / 8;
+        for (int g = warp; g < ng; g += GU_WARPS) {
+            const int b = g * 8 + lane / 4;
+            const int off = b * 32 + (lane & 3) * 8;
+            quant_lane8(xa + off, b < nb32, 4, q + off, d + b, nullptr, s + b, lane);
+        }
+    }
+    if (threadIdx.x == 0) A.cnt_slot[slot] = 0;
+}
+
+// ---- down + combine ------------------------------------------------------------------
+
+constexpr int DN_WARPS = 4;
+
+struct DownStreams {
+    WDev w;
+    const uint64_t *gb;  // per stream: first block of this output row (shared memory)
+    const int *sl;       // per stream: staged activation index (shared memory)
+    const int8_t *aq;    // staged activations: index j at aq + j*stride
+    const float *ad;
+    const int32_t *as;
+    int stride;
+    __device__ __forceinline__ void at(int s, WDev &wo, uint64_t &g, XV &xv) const {
+        wo = w;
+        g = gb[s];
+        const int j = sl[s];
+        xv = XV{aq + (size_t)j * stride, ad + (size_t)j * (stride / 32), as + (size_t)j * (stride / 16)};
+    }
+};
+
+template <int TY, int SC, int MAXU>
+__global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ int s_slot[64];  // local routed slots of this token, selection order
+    __shared__ float s_gate[64];
+    __shared__ int s_nloc;
+    __shared__ int s_shidx;
+    __shared__ uint64_t s_gb[DN_WARPS][SC];
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r = blockIdx.x * DN_WARPS + warp;
+    const int rr = r < A.dim ? r : A.dim - 1;
+    const int nk = A.n_used, ffn = A.ffn;
+    const int nb = ffn / QT<TY>::BE;
+    // Routing is final before this kernel may start: k_gateup_dec triggers its
+    // dependents only after its own wait on the router, so ids/gates are read now.
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int k = 0; k < nk; k++) {
+            const int le = __ldcg(A.ids + (size_t)t * nk + k) - A.expert0;
+            if (le >= 0 && le < A.n_local) {
+                s_slot[n] = k;
+                s_gate[n] = __ldcg(A.gates + (size_t)t * nk + k);
+                n++;
+            }
+        }
+        s_nloc = n;
+        s_shidx = nk;
+    }
+    __syncthreads();
+    const int nloc = s_nloc;
+    if (lane < SC && lane < nloc) {
+        const int le = __ldcg(A.ids + (size_t)t * nk + s_slot[lane]) - A.expert0;
+        s_gb[warp][lane] = ((uint64_t)le * A.dim + rr) * nb;
+    }
+    __syncwarp();
+    int8_t *aq = reinterpret_cast<int8_t *>(sm);
+    const int stride = A.act_stride;
+    const int nk1 = nk + (A.has_shared ? 1 : 0);  // staged: the token's routed slots, then its shared one
+    float *ad = reinterpret_cast<float *>(sm + (size_t)nk1 * stride);
+    int32_t *as = reinterpret_cast<int32_t *>(sm + (size_t)nk1 * stride + (size_t)nk1 * (stride / 32) * 4);
+    DownStreams st{A.dn, s_gb[warp], s_slot, aq, ad, as, stride};
+    WFrags<TY, MAXU> fr;
+    const int n0 = nloc < SC ? nloc : SC;
+    if (n0 > 0) wd_load<TY, SC, MAXU>(st, nb, n0, fr, lane);  // the first chunk's weights, before the wait
+    pdl_wait();
+    pdl_trigger();
+    const size_t slot0 = (size_t)t * nk;
+    stage16(aq, A.aq + slot0 * stride, nk * stride);
+    for (int i = threadIdx.x; i < nk * (stride / 32); i += blockDim.x) ad[i] = __ldcg(A.ad + slot0 * (stride / 32) + i);
+    for (int i = threadIdx.x; i < nk * (stride / 16); i += blockDim.x) as[i] = __ldcg(A.as + slot0 * (stride / 16) + i);
+    if (A.has_shared) {
+        const size_t ss = (size_t)A.T * nk + t;
+        stage16(aq + (size_t)nk * stride, A.aq + ss * stride, stride);
+        for (int i = threadIdx.x; i < stride / 32; i += blockDim.x)
+            ad[nk * (stride / 32) + i] = __ldcg(A.ad + ss * (stride / 32) + i);
+        for (int i = threadIdx.x; i < stride / 16; i += blockDim.x)
+            as[nk * (stride / 16) + i] = __ldcg(A.as + ss * (stride / 16) + i);
+    }
+    __syncthreads();
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < nloc; c0 += SC) {
+        const int n = nloc - c0 < SC ? nloc - c0 : SC;
+        if (c0 > 0) {
+            __syncwarp();
+            if (lane < n) {
+                const int le = __ldcg(A.ids + (size_t)t * nk + s_slot[c0 + lane]) - A.expert0;
+                s_gb[warp][lane] = ((uint64_t)le * A.dim + rr) * nb;
+            }
+            __syncwarp();
+            st.sl = s_slot + c0;
+            wd_load<TY, SC, MAXU>(st, nb, n, fr, lane);
+        }
+        float y[SC];
+        wd_finish<TY, SC, MAXU>(st, nb, n, fr, y, lane);
+#pragma unroll
+        for (int k = 0; k < SC; k++)
+            if (k < n) acc = fadd(acc, fmul(s_gate[c0 + k], y[k]));  // moeRun: acc += gate * out (llama.zig:1397)
+    }
+    if (A.has_shared) {  // shared expert added plainly after the routed sum (deepseek.zig:1498-1508)
+        const int nbs = A.shexp_ffn / QT<TY>::BE;
+        __syncwarp();
+        if (lane == 0) s_gb[warp][0] = (uint64_t)rr * nbs;
+        __syncwarp();
+        DownStreams sh{A.sdn, s_gb[warp], &s_shidx, aq, ad, as, stride};
+        wd_load<TY, SC, MAXU>(sh, nbs, 1, fr, lane);
+        float y[SC];
+        wd_finish<TY, SC, MAXU>(sh, nbs, 1, fr, y, lane);
+        acc = fadd(acc, y[0]);
+    }
+    if (lane == 0 && r < A.dim) {
+        const size_t o = (size_t)t * A.dim + r;
+        A.out[o] = A.residual ? fadd(__ldcg(A.residual + o), acc) : acc;
+    }
+}
+
+// ---- dispatch ---------------------------------------------------------------------
+
+// register budget: fragments per lane (Q6_K fragments are 17 registers, Q4_K 8, Q8_0 5)
+static constexpr int max_maxu(int ty) { return ty == T_Q6_K ? 8 : 16; }
+static constexpr int lanes_per_block(int ty) { return ty == T_Q4_K ? 8 : ty == T_Q6_K ? 4 : ty == T_Q8_0 ? 2 : 1; }
+
+static int pick_maxu(int units, int G, int ty) {
+    const int need = (units + G - 1) / G;
+    const int buckets[] = {2, 3, 4, 6, 8, 12, 16};
+    for (int b : buckets)
+        if (need <= b && b <= max_maxu(ty)) return b;
+    return 0;
+}
+
+template <int TY>
+static cudaError_t launch_gateup_t(const DecodeArgs &A, int maxu, dim3 grid, size_t smem, cudaStream_t st) {
+    const dim3 blk(GU_WARPS * 32);
+    switch (maxu) {
+        case 2: return launch_pdl(k_gateup_dec<TY, 2>, grid, blk, smem, st, A);
+        case 3: return launch_pdl(k_gateup_dec<TY, 3>, grid, blk, smem, st, A);
+        case 4: return launch_pdl(k_gateup_dec<TY, 4>, grid, blk, smem, st, A);
+        case 6: return launch_pdl(k_gateup_dec<TY, 6>, grid, blk, smem, st, A);
+        case 8: return launch_pdl(k_gateup_dec<TY, 8>, grid, blk, smem, st, A);
+        case 12:
+            if constexpr (max_maxu(TY) >= 12) return launch_pdl(k_gateup_dec<TY, 12>, grid, blk, smem, st, A);
+            break;
+        case 16:
+            if constexpr (max_maxu(TY) >= 16) return launch_pdl(k_gateup_dec<TY, 16>, grid, blk, smem, st, A);
+            break;
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int TY, int SC>
+static cudaError_t launch_down_t(const DecodeArgs &A, int maxu, dim3 grid, size_t smem, cudaStream_t st) {
+    const dim3 blk(DN_WARPS * 32);
+    switch (maxu) {
+        case 2: return launch_pdl(k_down_dec<TY, SC, 2>, grid, blk, smem, st, A);
+        case 3: return launch_pdl(k_down_dec<TY, SC, 3>, grid, blk, smem, st, A);
+        case 4: return launch_pdl(k_down_dec<TY, SC, 4>, grid, blk, smem, st, A);
+        case 6: return launch_pdl(k_down_dec<TY, SC, 6>, grid, blk, smem, st, A);
+        case 8: return launch_pdl(k_down_dec<TY, SC, 8>, grid, blk, smem, st, A);
+        case 12:
+            if constexpr (max_maxu(TY) >= 12) return launch_pdl(k_down_dec<TY, SC, 12>, grid, blk, smem, st, A);
+            break;
+        case 16:
+            if constexpr (max_maxu(TY) >= 16) return launch_pdl(k_down_dec<TY, SC, 16>, grid, blk, smem, st, A);
+            break;
+    }
+    return cudaErrorInvalidValue;
+}
+
+// streams per chunk of the down kernel, and its fragment bucket
+static int down_sc(int dty, int nb, int &maxu) {
+    const int G = 32 / lanes_per_block(dty);
+    const int want = dty == T_Q4_K ? 4 : 8;
+    if ((maxu = pick_maxu(want * nb, G, dty))) return want;
+    if ((maxu = pick_maxu(2 * nb, G, dty))) return 2;
+    return 0;
+}
+
+static size_t down_smem(const DecodeArgs &A) {
+    const size_t nk1 = A.n_used + (A.has_shared ? 1 : 0);
+    return nk1 * A.act_stride + nk1 * (A.act_stride / 32) * 4 + nk1 * (A.act_stride / 16) * 4;
+}
+
+bool decode_supported(const DecodeArgs &A) {
+    // gate and up: one K-quant type over whole super-blocks
+    if (A.g.type != A.u.type || (A.g.type != T_Q4_K && A.g.type != T_Q6_K)) return false;
+    if (A.dim % 256 || A.dim > 8192 || A.n_used > 64) return false;
+    if (!pick_maxu(2 * GU_NR * (A.dim / 256), 32 / lanes_per_block(A.g.type), A.g.type)) return false;
+    // down: Q4_K / Q6_K / Q8_0 over whole blocks
+    const int dty = A.dn.type;
+    if (dty != T_Q4_K && dty != T_Q6_K && dty != T_Q8_0) return false;
+    if (A.ffn % block_elems(dty)) return false;
+    int maxu = 0;
+    if (!down_sc(dty, A.ffn / block_elems(dty), maxu)) return false;
+    if (A.has_shared) {  // the shared expert must fit the same instantiation
+        if (A.sg.type != A.g.type || A.su.type != A.g.type || A.sdn.type != dty) return false;
+        if (A.shexp_ffn % block_elems(dty) || A.shexp_ffn > A.act_stride) return false;
+        if (A.shexp_ffn / block_elems(dty) > maxu * (32 / lanes_per_block(dty))) return false;
+    }
+    const size_t max_ffn = A.has_shared && A.shexp_ffn > A.ffn ? A.shexp_ffn : A.ffn;
+    return down_smem(A) <= 48 * 1024 && (size_t)(A.dim + 2 * A.n_expert) * 4 <= 48 * 1024 &&
+           max_ffn * 4 <= 48 * 1024;
+}
+
+cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
+    cudaError_t e;
+    // 1. router + route + activation quantization
+    {
+        const unsigned gx = A.router ? cdivu(A.n_expert, RR_WARPS) : 1;
+        const size_t smem = (size_t)(A.dim + 2 * A.n_expert) * 4;
+        e = launch_pdl(k_router_route, dim3(gx, A.T), dim3(RR_WARPS * 32), smem, st, A);
+        if (e != cudaSuccess) return e;
+    }
+    // 2. gate/up
+    {
+        const int n_slots = A.T * A.n_used + (A.has_shared ? A.T : 0);
+        const int max_ffn = A.has_shared && A.shexp_ffn > A.ffn ? A.shexp_ffn : A.ffn;
+        const dim3 grid(cdivu(max_ffn, GU_WARPS * GU_NR), n_slots);
+        const size_t smem_x = (size_t)A.dim + A.dim / 256 * 4 + A.dim / 16 * 4;
+        const size_t smem_q = (size_t)max_ffn * 4;
+        const size_t smem = smem_x > smem_q ? smem_x : smem_q;
+        const int units = 2 * GU_NR * (A.dim / 256);
+        if (A.g.type == T_Q4_K)
+            e = launch_gateup_t<T_Q4_K>(A, pick_maxu(units, 4, T_Q4_K), grid, smem, st);
+        else
+            e = launch_gateup_t<T_Q6_K>(A, pick_maxu(units, 8, T_Q6_K), grid, smem, st);
+        if (e != cudaSuccess) return e;
+    }
+    // 3. down + combine
+    {
+        const dim3 grid(cdivu(A.dim, DN_WARPS), A.T);
+        const int dty = A.dn.type;
+        int maxu = 0;
+        const int sc = down_sc(dty, A.ffn / block_elems(dty), maxu);
+        const size_t smem = down_smem(A);
+        if (dty == T_Q6_K)
+            e = sc == 8 ? launch_down_t<T_Q6_K, 8>(A, maxu, grid, smem, st)
+                        : launch_down_t<T_Q6_K, 2>(A, maxu, grid, smem, st);
+        else if (dty == T_Q4_K)
+            e = sc == 4 ? launch_down_t<T_Q4_K, 4>(A, maxu, grid, smem, st)
+                        : launch_down_t<T_Q4_K, 2>(A, maxu, grid, smem, st);
+        else
+            e = sc == 8 ? launch_down_t<T_Q8_0, 8>(A, maxu, grid, smem, st)
+                        : launch_down_t<T_Q8_0, 2>(A, maxu, grid, smem, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace loom

@@ -1,0 +1,50 @@
+// decode.cuh -- arguments of the fused MoE decode path (decode.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "kernels.cuh"
+
+namespace loom {
+
+struct XQW {  // writable quantized-activation buffers
+    int8_t *q;
+    float *d;
+    int32_t *s;
+};
+
+struct DecodeArgs {
+    int T, dim, ffn, n_expert, n_used;
+    int gating, weights_norm;
+    float weights_scale;
+    int expert0, n_local;
+    const float *router;     // f32 [n_expert][dim], or null when logits_in is given
+    const float *bias;       // selection bias [n_expert] or null
+    const float *logits_in;  // caller logits [T][n_expert] (router == null)
+    const float *x;          // [T][dim]
+    float *out;              // [T][dim]
+    const float *residual;   // [T][dim] or null
+    float *logits;           // scratch [T][n_expert]
+    int *ids;                // scratch [T][n_used]
+    float *gates;            // scratch [T][n_used]
+    uint32_t *ids_out;       // optional copy of ids for the caller
+    int *cnt_tok;            // zeroed counters [T]
+    int *cnt_slot;           // zeroed counters [n_slots]
+    XQW x256, x32;
+    int need256, need32;
+    WDev g, u, dn;
+    int has_shared;
+    WDev sg, su, sdn;
+    int shexp_ffn;
+    float *act;              // [n_slots][act_stride]
+    int8_t *aq;              // [n_slots][act_stride]
+    float *ad;               // [n_slots][act_stride/32]
+    int32_t *as;             // [n_slots][act_stride/16]
+    int act_stride;          // multiple of 256
+};
+
+// True when the fused decode kernels cover this layer's types and shapes.
+bool decode_supported(const DecodeArgs &A);
+// Enqueue the three PDL-chained kernels of one layer.
+cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st);
+
+}  // namespace loom

@@ -1,0 +1,123 @@
+// devutil.cuh -- device helpers shared by the kernel files: the activation
+// quantizer lane step and the warp router.
+#pragma once
+#include "common.cuh"
+
+namespace loom {
+
+// Activation quantization (ggml.zig:776 quantizeX256 / :1077 quantizeX): each
+// lane holds 8 consecutive values of a block that spans `group_lanes` lanes
+// (32 for a 256-wide block, 4 for a 32-wide one). d = amax/127 (IEEE divide),
+// q = round-half-away(v * (1/d)) saturated to +-127, non-finite -> 0.
+__device__ __forceinline__ void quant_lane8(const float *src, bool live, int group_lanes, int8_t *qdst, float *ddst,
+                                            int32_t *sdst_pairs, int32_t *sdst_group, int lane) {
+    float v[8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        v[i] = live ? src[i] : 0.0f;
+        if (isfinite(v[i])) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    for (int o = 1; o < group_lanes; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = fdiv(amax, 127.0f);
+    const float inv = (d != 0.0f && isfinite(d)) ? fdiv(1.0f, d) : 0.0f;
+    int sum = 0;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int q = to_i8_sat(fmul(v[i], inv));
+        sum += q;
+        if (i < 4) lo |= ((uint32_t)(q & 0xFF)) << (8 * i);
+        else hi |= ((uint32_t)(q & 0xFF)) << (8 * (i - 4));
+    }
+    if (live) *reinterpret_cast<uint2 *>(qdst) = make_uint2(lo, hi);
+    const int pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
+    if (sdst_pairs && live && (lane & 1) == 0) *sdst_pairs = pair;
+    if (sdst_group) {
+        int gs = sum;
+        for (int o = 1; o < group_lanes; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        if (live && (lane % group_lanes) == 0) *sdst_group = gs;
+    }
+    if (live && (lane % group_lanes) == 0) *ddst = isfinite(d) ? d : 0.0f;
+}
+
+
+// moe.zig:106-158 route, one warp per token. Scores and the biased choice live
+// in shared memory; top-k is k rounds of a warp arg-max that keeps the lowest
+// index on ties and never selects a value that is not > -inf (the serial
+// scan's strict '>').
+__device__ __forceinline__ void route_warp(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
+                           float weights_scale, float *scores, float *choice, int *ids, float *gates, int lane) {
+    if (gating == 2) {
+        for (int e = lane; e < ne; e += 32) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
+    } else if (gating == 1) {
+        float m = -INFINITY;
+        for (int e = lane; e < ne; e += 32) m = fmaxf(m, logits[e]);
+        m = warp_max(m);
+        float sum = 0.0f;
+        for (int e = lane; e < ne; e += 32) {
+            const float v = expf(fsub(logits[e], m));
+            scores[e] = v;
+            sum = fadd(sum, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum = fadd(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        const float inv = fdiv(1.0f, sum);
+        for (int e = lane; e < ne; e += 32) scores[e] = fmul(scores[e], inv);
+    } else {
+        for (int e = lane; e < ne; e += 32) scores[e] = logits[e];
+    }
+    for (int e = lane; e < ne; e += 32) choice[e] = bias ? fadd(scores[e], bias[e]) : scores[e];
+    __syncwarp();
+    for (int k = 0; k < nk; k++) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < ne; e += 32) {
+            const float c = choice[e];
+            if (c > bv) {  // strict: first maximum in this lane's (ascending) run
+                bv = c;
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
+        if (lane == 0) {
+            ids[k] = bi;
+            gates[k] = scores[bi];
+            choice[bi] = -INFINITY;  // used
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        if (gating == 3) {  // softmax over the selected k (tensor.zig:18 softmax)
+            float m = -INFINITY;
+            for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
+            float sum = 0.0f;
+            for (int k = 0; k < nk; k++) {
+                gates[k] = expf(fsub(gates[k], m));
+                sum = fadd(sum, gates[k]);
+            }
+            const float inv = fdiv(1.0f, sum);
+            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], inv);
+        }
+        if (weights_norm) {
+            float sum = 0.0f;
+            for (int k = 0; k < nk; k++) sum = fadd(sum, gates[k]);
+            const float denom = fmaxf(sum, 6.103515625e-5f);
+            for (int k = 0; k < nk; k++) gates[k] = fdiv(gates[k], denom);
+        }
+        if (weights_scale != 1.0f)
+            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], weights_scale);
+    }
+    __syncwarp();
+}
+
+}  // namespace loom

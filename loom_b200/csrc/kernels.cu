@@ -4,6 +4,7 @@
 
 #include "kernels.cuh"
 #include "rowdot.cuh"
+#include "devutil.cuh"
 
 namespace loom {
 
@@ -255,38 +256,6 @@ void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cuda
 // per-16 sums from lane pairs. 32-wide blocks: four lanes per block, eight
 // blocks per warp.
 
-__device__ __forceinline__ void quant_lane8(const float *src, bool live, int group_lanes, int8_t *qdst, float *ddst,
-                                            int32_t *sdst_pairs, int32_t *sdst_group, int lane) {
-    float v[8];
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        v[i] = live ? src[i] : 0.0f;
-        if (isfinite(v[i])) amax = fmaxf(amax, fabsf(v[i]));
-    }
-    for (int o = 1; o < group_lanes; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d = fdiv(amax, 127.0f);
-    const float inv = (d != 0.0f && isfinite(d)) ? fdiv(1.0f, d) : 0.0f;
-    int sum = 0;
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int q = to_i8_sat(fmul(v[i], inv));
-        sum += q;
-        if (i < 4) lo |= ((uint32_t)(q & 0xFF)) << (8 * i);
-        else hi |= ((uint32_t)(q & 0xFF)) << (8 * (i - 4));
-    }
-    if (live) *reinterpret_cast<uint2 *>(qdst) = make_uint2(lo, hi);
-    const int pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
-    if (sdst_pairs && live && (lane & 1) == 0) *sdst_pairs = pair;
-    if (sdst_group) {
-        int gs = sum;
-        for (int o = 1; o < group_lanes; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
-        if (live && (lane % group_lanes) == 0) *sdst_group = gs;
-    }
-    if (live && (lane % group_lanes) == 0) *ddst = isfinite(d) ? d : 0.0f;
-}
-
 __global__ void k_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d,
                             int32_t *s, int dstride, int sstride) {
     const int lane = threadIdx.x & 31;
@@ -371,80 +340,6 @@ void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok
 // top-k is k rounds of a warp arg-max that keeps the lowest index on ties and
 // never selects a value that is not > -inf (the serial scan's strict '>').
 
-__device__ void route_warp(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
-                           float weights_scale, float *scores, float *choice, int *ids, float *gates, int lane) {
-    if (gating == 2) {
-        for (int e = lane; e < ne; e += 32) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
-    } else if (gating == 1) {
-        float m = -INFINITY;
-        for (int e = lane; e < ne; e += 32) m = fmaxf(m, logits[e]);
-        m = warp_max(m);
-        float sum = 0.0f;
-        for (int e = lane; e < ne; e += 32) {
-            const float v = expf(fsub(logits[e], m));
-            scores[e] = v;
-            sum = fadd(sum, v);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum = fadd(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-        const float inv = fdiv(1.0f, sum);
-        for (int e = lane; e < ne; e += 32) scores[e] = fmul(scores[e], inv);
-    } else {
-        for (int e = lane; e < ne; e += 32) scores[e] = logits[e];
-    }
-    for (int e = lane; e < ne; e += 32) choice[e] = bias ? fadd(scores[e], bias[e]) : scores[e];
-    __syncwarp();
-    for (int k = 0; k < nk; k++) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int e = lane; e < ne; e += 32) {
-            const float c = choice[e];
-            if (c > bv) {  // strict: first maximum in this lane's (ascending) run
-                bv = c;
-                bi = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
-        if (lane == 0) {
-            ids[k] = bi;
-            gates[k] = scores[bi];
-            choice[bi] = -INFINITY;  // used
-        }
-        __syncwarp();
-    }
-    if (lane == 0) {
-        if (gating == 3) {  // softmax over the selected k (tensor.zig:18 softmax)
-            float m = -INFINITY;
-            for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
-            float sum = 0.0f;
-            for (int k = 0; k < nk; k++) {
-                gates[k] = expf(fsub(gates[k], m));
-                sum = fadd(sum, gates[k]);
-            }
-            const float inv = fdiv(1.0f, sum);
-            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], inv);
-        }
-        if (weights_norm) {
-            float sum = 0.0f;
-            for (int k = 0; k < nk; k++) sum = fadd(sum, gates[k]);
-            const float denom = fmaxf(sum, 6.103515625e-5f);
-            for (int k = 0; k < nk; k++) gates[k] = fdiv(gates[k], denom);
-        }
-        if (weights_scale != 1.0f)
-            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], weights_scale);
-    }
-    __syncwarp();
-}
-
 __global__ void k_route(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
                         float weights_scale, int *ids, float *gates) {
     extern __shared__ float sm[];
@@ -461,88 +356,78 @@ void launch_route(const float *logits, const float *bias, int T, int n_expert, i
     count_launch();
 }
 
-// Route, then expand the selection into per-(token, expert) slots. Slot
-// t*n_used + k is token t's k-th selected expert; the shared expert of token t
-// is slot T*n_used + t. Experts outside this rank's range get ffn = 0.
-__global__ void k_route_slots(const float *logits, const float *bias, int T, RoutedLayerDev L, int *ids, float *gates,
-                              Slot *slots, int act_stride) {
-    extern __shared__ float sm[];
-    const int t = blockIdx.x;
-    const int lane = threadIdx.x;
-    int *tid = ids + (size_t)t * L.n_used;
-    float *tg = gates + (size_t)t * L.n_used;
-    route_warp(logits + (size_t)t * L.n_expert, bias, L.n_expert, L.n_used, L.gating, L.weights_norm, L.weights_scale,
-               sm, sm + L.n_expert, tid, tg, lane);
-    for (int k = lane; k < L.n_used; k += 32) {
-        const int e = tid[k];
-        const int le = e - L.expert0;
-        const bool local = le >= 0 && le < L.n_local;
-        Slot s;
-        s.g = L.g;
-        s.u = L.u;
-        s.dn = L.dn;
-        s.gb_g = local ? (uint64_t)le * L.plane_blk_g : 0;
-        s.gb_u = local ? (uint64_t)le * L.plane_blk_u : 0;
-        s.gb_dn = local ? (uint64_t)le * L.plane_blk_dn : 0;
-        s.ffn = local ? L.ffn : 0;
-        s.token = t;
-        s.weight = tg[k];
-        s.act_off = (t * L.n_used + k) * act_stride;
-        slots[t * L.n_used + k] = s;
-    }
-    if (L.has_shared && lane == 0) {
-        Slot s;
-        s.g = L.sg;
-        s.u = L.su;
-        s.dn = L.sdn;
-        s.gb_g = s.gb_u = s.gb_dn = 0;
-        s.ffn = L.shexp_ffn;
-        s.token = t;
-        s.weight = 1.0f;
-        s.act_off = (T * L.n_used + t) * act_stride;
-        slots[T * L.n_used + t] = s;
-    }
-}
+// ---- slot sources -----------------------------------------------------------------
+// A slot is one (token, expert) pair. Host-listed experts (moeFfnBlock) come as
+// an array built on the host; routed layers derive each slot in registers from
+// the layer description and the router's ids/gates: slot t*n_used + k is token
+// t's k-th selected expert, slot T*n_used + t its shared expert. Experts outside
+// this rank's range get ffn = 0 (skipped).
 
-void launch_route_slots(const float *logits, const float *bias, int T, const RoutedLayerDev &L, int *ids, float *gates,
-                        Slot *slots, int act_stride, cudaStream_t st) {
-    if (T == 0) return;
-    k_route_slots<<<T, 32, 2 * L.n_expert * sizeof(float), st>>>(logits, bias, T, L, ids, gates, slots, act_stride);
-    count_launch();
-}
+struct HostSlots {
+    const Slot *p;
+    __device__ __forceinline__ Slot get(int i) const { return p[i]; }
+};
+
+struct RoutedSlots {
+    RoutedLayerDev L;
+    const int *ids;
+    const float *gates;
+    int T;
+    int act_stride;
+    __device__ __forceinline__ Slot get(int i) const {
+        Slot s;
+        const int nr = T * L.n_used;
+        if (i < nr) {
+            const int t = i / L.n_used;
+            const int le = __ldg(ids + i) - L.expert0;
+            const bool local = le >= 0 && le < L.n_local;
+            s.g = L.g;
+            s.u = L.u;
+            s.dn = L.dn;
+            s.gb_g = local ? (uint64_t)le * L.plane_blk_g : 0;
+            s.gb_u = local ? (uint64_t)le * L.plane_blk_u : 0;
+            s.gb_dn = local ? (uint64_t)le * L.plane_blk_dn : 0;
+            s.ffn = local ? L.ffn : 0;
+            s.token = t;
+            s.weight = __ldg(gates + i);
+        } else {
+            s.g = L.sg;
+            s.u = L.su;
+            s.dn = L.sdn;
+            s.gb_g = s.gb_u = s.gb_dn = 0;
+            s.ffn = L.shexp_ffn;
+            s.token = i - nr;
+            s.weight = 1.0f;
+        }
+        s.act_off = i * act_stride;
+        return s;
+    }
+};
 
 // ---- expert FFN ------------------------------------------------------------------
 // gate/up (+SwiGLU): warp per (slot, row). act = silu(g) * u, silu(g) = g/(1+e^-g)
 // (tensor.zig:30, :53).
 
-__global__ void __launch_bounds__(256) k_gateup(const Slot *__restrict__ slots, int dim, XQ x256, XQ x32, float *act) {
-    const Slot &s = slots[blockIdx.y];
+template <class Src>
+__global__ void __launch_bounds__(256) k_gateup(Src src, int dim, XQ x256, XQ x32, float *act) {
+    const Slot s = src.get(blockIdx.y);
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= s.ffn) return;
-    const XQ &xg = act256(s.g.type) ? x256 : x32;
-    const XQ &xu = act256(s.u.type) ? x256 : x32;
     const int nbg = dim / block_elems(s.g.type), nbu = dim / block_elems(s.u.type);
     float g[1] = {0.0f}, u[1] = {0.0f};
-    rowdot<1>(s.g, s.gb_g + (uint64_t)r * nbg, nbg, xg, s.token, 1, g, lane);
-    rowdot<1>(s.u, s.gb_u + (uint64_t)r * nbu, nbu, xu, s.token, 1, u, lane);
+    rowdot<1>(s.g, s.gb_g + (uint64_t)r * nbg, nbg, act256(s.g.type) ? x256 : x32, s.token, 1, g, lane);
+    rowdot<1>(s.u, s.gb_u + (uint64_t)r * nbu, nbu, act256(s.u.type) ? x256 : x32, s.token, 1, u, lane);
     if (lane == 0) {
         const float sl = fdiv(g[0], fadd(1.0f, expf(-g[0])));
         act[s.act_off + r] = fmul(sl, u[0]);
     }
 }
 
-void launch_gateup(const Slot *slots, int n_slots, int max_ffn, int dim, const XQ &x256, const XQ &x32, float *act,
-                   cudaStream_t st) {
-    if (n_slots == 0) return;
-    dim3 grid(cdiv(max_ffn, 8), n_slots);
-    k_gateup<<<grid, 256, 0, st>>>(slots, dim, x256, x32, act);
-    count_launch();
-}
-
 // Quantize each slot's activation in the format its down projection reads.
-__global__ void k_quant_slots(const Slot *__restrict__ slots, const float *act, int8_t *aq, float *ad, int32_t *as) {
-    const Slot &s = slots[blockIdx.y];
+template <class Src>
+__global__ void k_quant_slots(Src src, const float *act, int8_t *aq, float *ad, int32_t *as) {
+    const Slot s = src.get(blockIdx.y);
     if (s.ffn == 0) return;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -565,20 +450,12 @@ __global__ void k_quant_slots(const Slot *__restrict__ slots, const float *act, 
     }
 }
 
-void launch_quant_slots(const Slot *slots, int n_slots, int max_ffn, const float *act, int8_t *aq, float *ad, int32_t *as,
-                        cudaStream_t st) {
-    (void)max_ffn;
-    if (n_slots == 0) return;
-    k_quant_slots<<<dim3(1, n_slots), 256, 0, st>>>(slots, act, aq, ad, as);
-    count_launch();
-}
-
 // down + weighted combine: warp per (token, output row); the token's slots are
 // summed in selection order, then the shared expert is added (llama.zig:1397,
 // deepseek.zig:1498-1508).
-__global__ void __launch_bounds__(256) k_down(const Slot *__restrict__ slots, int T, int nk, int has_shared, int dim,
-                                              const int8_t *aq, const float *ad, const int32_t *as, float *out,
-                                              const float *residual) {
+template <class Src>
+__global__ void __launch_bounds__(256) k_down(Src src, int T, int nk, int has_shared, int dim, const int8_t *aq,
+                                              const float *ad, const int32_t *as, float *out, const float *residual) {
     const int t = blockIdx.y;
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -586,7 +463,7 @@ __global__ void __launch_bounds__(256) k_down(const Slot *__restrict__ slots, in
     float acc = 0.0f;
     const int n = nk + (has_shared ? 1 : 0);
     for (int k = 0; k < n; k++) {
-        const Slot &s = slots[k < nk ? t * nk + k : T * nk + t];
+        const Slot s = src.get(k < nk ? t * nk + k : T * nk + t);
         if (s.ffn == 0) continue;
         XQ xa;
         xa.q = aq + s.act_off;
@@ -604,12 +481,31 @@ __global__ void __launch_bounds__(256) k_down(const Slot *__restrict__ slots, in
     if (lane == 0) out[(size_t)t * dim + r] = residual ? fadd(residual[(size_t)t * dim + r], acc) : acc;
 }
 
-void launch_down(const Slot *slots, int T, int nk, int has_shared, int dim, const int8_t *aq, const float *ad,
-                 const int32_t *as, float *out, const float *residual, cudaStream_t st) {
-    if (T == 0) return;
-    dim3 grid(cdiv(dim, 8), T);
-    k_down<<<grid, 256, 0, st>>>(slots, T, nk, has_shared, dim, aq, ad, as, out, residual);
+template <class Src>
+static void run_expert_kernels(const Src &src, int T, int nk, int has_shared, int n_slots, int max_ffn, int dim,
+                               const XQ &x256, const XQ &x32, float *act, int8_t *aq, float *ad, int32_t *as,
+                               float *out, const float *residual, cudaStream_t st) {
+    if (n_slots == 0) return;
+    k_gateup<Src><<<dim3(cdiv(max_ffn, 8), n_slots), 256, 0, st>>>(src, dim, x256, x32, act);
     count_launch();
+    k_quant_slots<Src><<<dim3(1, n_slots), 256, 0, st>>>(src, act, aq, ad, as);
+    count_launch();
+    k_down<Src><<<dim3(cdiv(dim, 8), T), 256, 0, st>>>(src, T, nk, has_shared, dim, aq, ad, as, out, residual);
+    count_launch();
+}
+
+void launch_experts_host(const Slot *slots, int n, int max_ffn, int dim, const XQ &x256, const XQ &x32, float *act,
+                         int8_t *aq, float *ad, int32_t *as, float *out, cudaStream_t st) {
+    run_expert_kernels(HostSlots{slots}, 1, n, 0, n, max_ffn, dim, x256, x32, act, aq, ad, as, out, nullptr, st);
+}
+
+void launch_experts_routed(const RoutedLayerDev &L, const int *ids, const float *gates, int T, int act_stride,
+                           const XQ &x256, const XQ &x32, float *act, int8_t *aq, float *ad, int32_t *as, float *out,
+                           const float *residual, cudaStream_t st) {
+    const int n_slots = T * L.n_used + (L.has_shared ? T : 0);
+    const int max_ffn = L.has_shared ? max(L.ffn, L.shexp_ffn) : L.ffn;
+    run_expert_kernels(RoutedSlots{L, ids, gates, T, act_stride}, T, L.n_used, L.has_shared, n_slots, max_ffn, L.dim,
+                       x256, x32, act, aq, ad, as, out, residual, st);
 }
 
 }  // namespace loom

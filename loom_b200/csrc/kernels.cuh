@@ -48,14 +48,14 @@ void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x,
 void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out, cudaStream_t st);
 void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating,
                   int weights_norm, float weights_scale, int *ids, float *gates, cudaStream_t st);
-void launch_route_slots(const float *logits, const float *bias, int T, const RoutedLayerDev &L, int *ids,
-                        float *gates, Slot *slots, int act_stride, cudaStream_t st);
-void launch_gateup(const Slot *slots, int n_slots, int max_ffn, int dim, const XQ &x256, const XQ &x32,
-                   float *act, cudaStream_t st);
-void launch_quant_slots(const Slot *slots, int n_slots, int max_ffn, const float *act, int8_t *aq, float *ad,
-                        int32_t *as, cudaStream_t st);
-void launch_down(const Slot *slots, int T, int nk, int has_shared, int dim, const int8_t *aq, const float *ad,
-                 const int32_t *as, float *out, const float *residual, cudaStream_t st);
+// Expert phase (gate/up + SwiGLU, activation quantization, down + weighted
+// combine) for a host-built slot array (one token) or for a routed layer whose
+// router already wrote ids/gates [T][n_used].
+void launch_experts_host(const Slot *slots, int n, int max_ffn, int dim, const XQ &x256, const XQ &x32, float *act,
+                         int8_t *aq, float *ad, int32_t *as, float *out, cudaStream_t st);
+void launch_experts_routed(const RoutedLayerDev &L, const int *ids, const float *gates, int T, int act_stride,
+                           const XQ &x256, const XQ &x32, float *act, int8_t *aq, float *ad, int32_t *as, float *out,
+                           const float *residual, cudaStream_t st);
 
 // number of kernel launches issued by this library (host-side count)
 uint64_t launches();

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -13,6 +14,7 @@
 #include <vector>
 
 #include "../../include/loom_cuda.h"
+#include "decode.cuh"
 #include "kernels.cuh"
 
 using namespace loom;
@@ -71,7 +73,7 @@ std::vector<Arena> g_arenas;
 struct DBuf {
     void *p = nullptr;
     size_t cap = 0;
-    int ensure(size_t n) {
+    int ensure(size_t n, bool zero = false) {
         if (n <= cap) return 0;
         if (p) {
             cudaStreamSynchronize(g_stream);
@@ -82,6 +84,10 @@ struct DBuf {
         size_t want = std::max<size_t>(align256(n + n / 4), 256);
         cudaError_t e = cudaMalloc(&p, want);
         if (e != cudaSuccess) return fail("cudaMalloc(scratch)", e);
+        if (zero) {
+            e = cudaMemset(p, 0, want);
+            if (e != cudaSuccess) return fail("cudaMemset(scratch)", e);
+        }
         cap = want;
         return 0;
     }
@@ -109,7 +115,7 @@ struct HBuf {  // pinned host staging
 
 struct Scratch {
     DBuf xq256_q, xq256_d, xq256_s, xq32_q, xq32_d, xq32_s;
-    DBuf logits, ids, gates, slots, act, aq, ad, as;
+    DBuf logits, ids, gates, slots, act, aq, ad, as, counters;
     DBuf io_in, io_out, io_aux, raw;
     HBuf h_in, h_out;
 } S;
@@ -242,23 +248,13 @@ int ensure_moe_scratch(size_t T, size_t dim, size_t max_ffn, size_t n_expert, si
     if (int rc = S.aq.ensure(n_slots * act_stride)) return rc;
     if (int rc = S.ad.ensure(n_slots * act_stride / 32 * 4 + 64)) return rc;
     if (int rc = S.as.ensure(n_slots * act_stride / 16 * 4 + 64)) return rc;
+    if (int rc = S.counters.ensure((T + n_slots) * 4, true)) return rc;
     return 0;
 }
 
-// Run the expert phase for slots already on the device.
-int run_experts(size_t T, size_t dim, int nk, int has_shared, size_t n_slots, size_t max_ffn, bool need256,
-                bool need32, const float *d_x, float *d_out, const float *d_residual, cudaStream_t st) {
+void quantize_inputs(const float *d_x, size_t T, size_t dim, bool need256, bool need32, cudaStream_t st) {
     if (need256) quantize_into(d_x, T, dim, true, st);
     if (need32) quantize_into(d_x, T, dim, false, st);
-    const Slot *slots = S.slots.as<Slot>();
-    launch_gateup(slots, (int)n_slots, (int)max_ffn, (int)dim, make_xq(true, dim), make_xq(false, dim),
-                  S.act.as<float>(), st);
-    launch_quant_slots(slots, (int)n_slots, (int)max_ffn, S.act.as<float>(), S.aq.as<int8_t>(), S.ad.as<float>(),
-                       S.as.as<int32_t>(), st);
-    launch_down(slots, (int)T, nk, has_shared, (int)dim, S.aq.as<int8_t>(), S.ad.as<float>(), S.as.as<int32_t>(), d_out,
-                d_residual, st);
-    CK(cudaGetLastError());
-    return 0;
 }
 
 int check_moe_types(const Tensor *g, const Tensor *u, const Tensor *d) {
@@ -305,17 +301,86 @@ bool any_type(const RoutedLayerDev &L, bool k256) {
     return r;
 }
 
-// Device-side forward of a routed MoE layer (routing on the device).
-int moe_routed_dev(const RoutedLayerDev &L0, size_t T, const float *d_x, const float *d_logits, const float *d_bias,
-                   float *d_out, const float *d_residual, cudaStream_t st) {
-    RoutedLayerDev L = L0;
+// The fused decode kernels take up to this many tokens per layer; larger
+// batches use the slot kernels.
+constexpr size_t DECODE_MAX_T = 16;
+
+bool g_force_generic = false;  // test hook: route every layer through the slot kernels
+
+DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, const float *d_x,
+                       const float *d_logits_in, const float *d_bias, float *d_out, const float *d_residual,
+                       uint32_t *d_ids_out, size_t act_stride) {
+    DecodeArgs A{};
+    A.T = (int)T;
+    A.dim = L.dim;
+    A.ffn = L.ffn;
+    A.n_expert = L.n_expert;
+    A.n_used = L.n_used;
+    A.gating = L.gating;
+    A.weights_norm = L.weights_norm;
+    A.weights_scale = L.weights_scale;
+    A.expert0 = L.expert0;
+    A.n_local = L.n_local;
+    A.router = router;
+    A.bias = d_bias;
+    A.logits_in = d_logits_in;
+    A.x = d_x;
+    A.out = d_out;
+    A.residual = d_residual;
+    A.logits = S.logits.as<float>();
+    A.ids = S.ids.as<int>();
+    A.gates = S.gates.as<float>();
+    A.ids_out = d_ids_out;
+    A.cnt_tok = S.counters.as<int>();
+    A.cnt_slot = S.counters.as<int>() + T;
+    A.x256 = XQW{S.xq256_q.as<int8_t>(), S.xq256_d.as<float>(), S.xq256_s.as<int32_t>()};
+    A.x32 = XQW{S.xq32_q.as<int8_t>(), S.xq32_d.as<float>(), S.xq32_s.as<int32_t>()};
+    A.need256 = any_type(L, true);
+    A.need32 = any_type(L, false);
+    A.g = L.g;
+    A.u = L.u;
+    A.dn = L.dn;
+    A.has_shared = L.has_shared;
+    A.sg = L.sg;
+    A.su = L.su;
+    A.sdn = L.sdn;
+    A.shexp_ffn = L.shexp_ffn;
+    A.act = S.act.as<float>();
+    A.aq = S.aq.as<int8_t>();
+    A.ad = S.ad.as<float>();
+    A.as = S.as.as<int32_t>();
+    A.act_stride = (int)act_stride;
+    return A;
+}
+
+// Device-side forward of a routed MoE layer (routing on the device). `router`
+// (f32 [n_expert][dim]) computes the logits; otherwise d_logits holds them.
+int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const float *d_x, const float *d_logits,
+                   const float *d_bias, float *d_out, const float *d_residual, uint32_t *d_ids_out, cudaStream_t st) {
     const size_t max_ffn = std::max<size_t>(L.ffn, L.has_shared ? L.shexp_ffn : 0);
     const size_t n_slots = T * L.n_used + (L.has_shared ? T : 0);
     if (int rc = ensure_moe_scratch(T, L.dim, max_ffn, L.n_expert, n_slots)) return rc;
-    launch_route_slots(d_logits, d_bias, (int)T, L, S.ids.as<int>(), S.gates.as<float>(), S.slots.as<Slot>(),
-                       (int)align256(max_ffn), st);
-    return run_experts(T, L.dim, L.n_used, L.has_shared, n_slots, max_ffn, any_type(L, true), any_type(L, false), d_x,
-                       d_out, d_residual, st);
+    const size_t act_stride = align256(max_ffn);
+    if (!g_force_generic && T <= DECODE_MAX_T) {
+        DecodeArgs A = decode_args(L, T, router, d_x, d_logits, d_bias, d_out, d_residual, d_ids_out, act_stride);
+        if (decode_supported(A)) {
+            CK(launch_decode(A, st));
+            return 0;
+        }
+    }
+    if (router) {
+        launch_mm_f32(router, L.n_expert, L.dim, d_x, (int)T, S.logits.as<float>(), st);
+        d_logits = S.logits.as<float>();
+    }
+    launch_route(d_logits, d_bias, (int)T, L.n_expert, L.n_used, L.gating, L.weights_norm, L.weights_scale,
+                 S.ids.as<int>(), S.gates.as<float>(), st);
+    quantize_inputs(d_x, T, L.dim, any_type(L, true), any_type(L, false), st);
+    launch_experts_routed(L, S.ids.as<int>(), S.gates.as<float>(), (int)T, (int)act_stride, make_xq(true, L.dim),
+                          make_xq(false, L.dim), S.act.as<float>(), S.aq.as<int8_t>(), S.ad.as<float>(),
+                          S.as.as<int32_t>(), d_out, d_residual, st);
+    if (d_ids_out) CK(cudaMemcpyAsync(d_ids_out, S.ids.p, T * L.n_used * 4, cudaMemcpyDeviceToDevice, st));
+    CK(cudaGetLastError());
+    return 0;
 }
 
 }  // namespace
@@ -323,6 +388,7 @@ int moe_routed_dev(const RoutedLayerDev &L0, size_t T, const float *d_x, const f
 extern "C" {
 
 int loom_cuda_init(int device) {
+    if (const char *e = getenv("LOOM_CUDA_GENERIC")) g_force_generic = e[0] == '1';
     if (g_inited) return device == g_device ? LOOM_CUDA_OK : decline("already initialised on another device");
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return decline("no CUDA device");
@@ -360,7 +426,7 @@ void loom_cuda_shutdown(void) {
         if (a.dev) cudaFree(a.dev);
     g_arenas.clear();
     for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
-                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.io_in, &S.io_out, &S.io_aux, &S.raw}) {
+                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.io_in, &S.io_out, &S.io_aux, &S.raw}) {
         if (b->p) cudaFree(b->p);
         b->p = nullptr;
         b->cap = 0;
@@ -438,6 +504,12 @@ size_t loom_cuda_last_error(char *buf, size_t len) {
 }
 
 void *loom_cuda_stream(void) { return g_stream; }
+
+int loom_cuda_force_generic(int on) {
+    const int prev = g_force_generic;
+    g_force_generic = on != 0;
+    return prev;
+}
 
 int loom_cuda_sync(void) {
     if (int rc = need_init()) return rc;
@@ -575,9 +647,11 @@ int loom_cuda_moe_ffn_block(const float *normed, size_t dim, const loom_expert *
     memcpy(S.h_in.as<uint8_t>() + align256(slot_b), normed, dim * 4);
     CK(cudaMemcpyAsync(S.slots.p, S.h_in.p, slot_b, cudaMemcpyHostToDevice, g_stream));
     CK(cudaMemcpyAsync(S.io_in.p, S.h_in.as<uint8_t>() + align256(slot_b), dim * 4, cudaMemcpyHostToDevice, g_stream));
-    if (int rc = run_experts(1, dim, (int)n, 0, n, max_ffn, need256, need32, S.io_in.as<float>(), S.io_out.as<float>(),
-                             nullptr, g_stream))
-        return rc;
+    quantize_inputs(S.io_in.as<float>(), 1, dim, need256, need32, g_stream);
+    launch_experts_host(S.slots.as<Slot>(), (int)n, (int)max_ffn, (int)dim, make_xq(true, dim), make_xq(false, dim),
+                        S.act.as<float>(), S.aq.as<int8_t>(), S.ad.as<float>(), S.as.as<int32_t>(), S.io_out.as<float>(),
+                        g_stream);
+    CK(cudaGetLastError());
     CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
     CK(cudaStreamSynchronize(g_stream));
     memcpy(out, S.h_out.p, dim * 4);
@@ -624,8 +698,8 @@ int loom_cuda_moe_ffn_routed(const float *normed, size_t dim, const float *logit
     if (bias) memcpy(hin + dim + cfg.n_expert, bias, cfg.n_expert * 4);
     CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
     const float *dx = S.io_in.as<float>();
-    if (int rc = moe_routed_dev(L, 1, dx, dx + dim, bias ? dx + dim + cfg.n_expert : nullptr, S.io_out.as<float>(),
-                                nullptr, g_stream))
+    if (int rc = moe_routed_dev(L, 1, nullptr, dx, dx + dim, bias ? dx + dim + cfg.n_expert : nullptr,
+                                S.io_out.as<float>(), nullptr, nullptr, g_stream))
         return rc;
     CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
     CK(cudaStreamSynchronize(g_stream));
@@ -759,16 +833,13 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
     const size_t max_ffn = std::max<size_t>(D.ffn, sh[0] ? D.shexp_ffn : 0);
     const size_t n_slots = T * D.n_used + (sh[0] ? T : 0);
     if (int rc = ensure_moe_scratch(T, D.dim, max_ffn, D.n_expert, n_slots)) return rc;
-    const float *logits = d_logits;
-    if (!logits) {
+    const float *router = nullptr;
+    if (!d_logits) {
         Tensor *r = lookup(D.router);
         if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
-        launch_mm_f32(reinterpret_cast<const float *>(r->base), (int)D.n_expert, (int)D.dim, d_x, (int)T,
-                      S.logits.as<float>(), st);
-        logits = S.logits.as<float>();
+        router = reinterpret_cast<const float *>(r->base);
     }
-    if (int rc = moe_routed_dev(L, T, d_x, logits, bias, d_out, d_residual, st)) return rc;
-    if (d_ids) CK(cudaMemcpyAsync(d_ids, S.ids.p, T * D.n_used * 4, cudaMemcpyDeviceToDevice, st));
+    if (int rc = moe_routed_dev(L, T, router, d_x, d_logits, bias, d_out, d_residual, d_ids, st)) return rc;
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;
 }

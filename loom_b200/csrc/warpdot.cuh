@@ -1,0 +1,269 @@
+// warpdot.cuh -- the warp-level dot engine of the decode kernels.
+//
+// One warp computes up to S "streams" (a stream = one weight row against one
+// int8 activation vector) of NB blocks each. Work is cut into units
+// (stream, block); a unit is served by LPB lanes (Q4_K 8, Q6_K 4, Q8_0 2,
+// Q4_0 1), so a warp serves G = 32/LPB units per step. ALL weight loads of the
+// warp are issued before any is consumed (the fragments live in registers),
+// which is what keeps enough bytes in flight to stream HBM.
+//
+// Numerics are those of rowdot.cuh (ggml.zig kBlockDot :1002, matvecQ40Int
+// :1196, matvecQ80Int :1277): exact integer partials, one IEEE rounding per
+// float operation, and each stream's block terms added in block order, so the
+// results are bit-identical to the CPU reference.
+#pragma once
+#include "common.cuh"
+
+namespace loom {
+
+// Activation view for one stream: block b's int8 values at q + b*BE, its scale
+// at d[b], its sums at s + b*(BE == 256 ? 16 : 1). Plain (generic) loads: the
+// view may point at shared or global memory.
+struct XV {
+    const int8_t *q;
+    const float *d;
+    const int32_t *s;
+};
+
+template <int TY> struct QT;
+
+template <> struct QT<T_Q4_K> {
+    static constexpr int LPB = 8, BE = 256, SPB = 16;
+    struct Frag {
+        uint4 h, q;
+    };
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int sub) {
+        const uint8_t *blk = w.q + gb * 144;
+        return Frag{ld_stream_v4(blk), ld_stream_v4(blk + 16 + 16 * sub)};
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int sub, const int8_t *xq, const int32_t *xs, int &I,
+                                                int &M) {
+        const int j = sub >> 1, h = sub & 1;
+        const int4 xl = *reinterpret_cast<const int4 *>(xq + 64 * j + 16 * h);
+        const int4 xh = *reinterpret_cast<const int4 *>(xq + 64 * j + 32 + 16 * h);
+        int dl = 0, dh = 0;
+        dl = dp4a((int)(f.q.x & 0x0F0F0F0Fu), xl.x, dl);
+        dl = dp4a((int)(f.q.y & 0x0F0F0F0Fu), xl.y, dl);
+        dl = dp4a((int)(f.q.z & 0x0F0F0F0Fu), xl.z, dl);
+        dl = dp4a((int)(f.q.w & 0x0F0F0F0Fu), xl.w, dl);
+        dh = dp4a((int)((f.q.x >> 4) & 0x0F0F0F0Fu), xh.x, dh);
+        dh = dp4a((int)((f.q.y >> 4) & 0x0F0F0F0Fu), xh.y, dh);
+        dh = dp4a((int)((f.q.z >> 4) & 0x0F0F0F0Fu), xh.z, dh);
+        dh = dp4a((int)((f.q.w >> 4) & 0x0F0F0F0Fu), xh.w, dh);
+        // scaleMinK4 (ggml.zig:1332) for sub-blocks 2j and 2j+1 from the 12
+        // scale bytes held in h.y (bytes 0-3), h.z (4-7), h.w (8-11)
+        int sc0, mn0, sc1, mn1;
+        if (j < 2) {
+            const uint32_t a = f.h.y >> (16 * j), b = f.h.z >> (16 * j);
+            sc0 = a & 63;
+            sc1 = (a >> 8) & 63;
+            mn0 = b & 63;
+            mn1 = (b >> 8) & 63;
+        } else {
+            const int jj = j - 2;                    // sub-blocks 4+2jj, 5+2jj
+            const uint32_t lo = f.h.w >> (16 * jj);  // scales[8+2jj], scales[9+2jj]
+            const uint32_t hs = f.h.y >> (16 * jj);  // scales[2jj], scales[2jj+1]  (top 2 bits -> sc)
+            const uint32_t hm = f.h.z >> (16 * jj);  // scales[4+2jj], scales[5+2jj] (top 2 bits -> mn)
+            sc0 = (lo & 0xF) | (((hs >> 6) & 3) << 4);
+            mn0 = ((lo >> 4) & 0xF) | (((hm >> 6) & 3) << 4);
+            sc1 = ((lo >> 8) & 0xF) | (((hs >> 14) & 3) << 4);
+            mn1 = ((lo >> 12) & 0xF) | (((hm >> 14) & 3) << 4);
+        }
+        I = sc0 * dl + sc1 * dh;
+        M = mn0 * xs[4 * j + h] + mn1 * xs[4 * j + 2 + h];
+    }
+    __device__ __forceinline__ static float term(const Frag &f, int I, int M, float xd) {
+        const float d = f16_to_f32((uint16_t)(f.h.x & 0xFFFF));
+        const float dmin = f16_to_f32((uint16_t)(f.h.x >> 16));
+        return fmul(xd, fsub(fmul(d, (float)I), fmul(dmin, (float)M)));
+    }
+};
+
+template <> struct QT<T_Q6_K> {
+    static constexpr int LPB = 4, BE = 256, SPB = 16;
+    struct Frag {
+        uint4 a, b, h, s;
+        uint32_t d;
+    };
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int sub) {
+        const int n = sub >> 1, hh = sub & 1;
+        const uint8_t *qb = w.q + gb * 192;
+        Frag f;
+        f.a = ld_stream_v4(qb + 64 * n + 16 * hh);
+        f.b = ld_stream_v4(qb + 64 * n + 32 + 16 * hh);
+        f.h = ld_stream_v4(qb + 128 + 32 * n + 16 * hh);
+        f.s = ld_stream_v4(w.sc + gb * 16);
+        f.d = __ldg(w.d + gb);
+        return f;
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int sub, const int8_t *xq, const int32_t *xs, int &I,
+                                                int &M) {
+        const int n = sub >> 1, hh = sub & 1;
+        const int8_t *xb = xq + 128 * n + 16 * hh;
+        const int4 x0 = *reinterpret_cast<const int4 *>(xb), x1 = *reinterpret_cast<const int4 *>(xb + 32);
+        const int4 x2 = *reinterpret_cast<const int4 *>(xb + 64), x3 = *reinterpret_cast<const int4 *>(xb + 96);
+        const uint32_t A[4] = {f.a.x, f.a.y, f.a.z, f.a.w}, B[4] = {f.b.x, f.b.y, f.b.z, f.b.w};
+        const uint32_t H[4] = {f.h.x, f.h.y, f.h.z, f.h.w};
+        const int X0[4] = {x0.x, x0.y, x0.z, x0.w}, X1[4] = {x1.x, x1.y, x1.z, x1.w};
+        const int X2[4] = {x2.x, x2.y, x2.z, x2.w}, X3[4] = {x3.x, x3.y, x3.z, x3.w};
+        int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t a = A[k], b = B[k], h = H[k];
+            d0 = dp4a((int)((a & 0x0F0F0F0Fu) | ((h & 0x03030303u) << 4)), X0[k], d0);
+            d1 = dp4a((int)((b & 0x0F0F0F0Fu) | (((h >> 2) & 0x03030303u) << 4)), X1[k], d1);
+            d2 = dp4a((int)(((a >> 4) & 0x0F0F0F0Fu) | (((h >> 4) & 0x03030303u) << 4)), X2[k], d2);
+            d3 = dp4a((int)(((b >> 4) & 0x0F0F0F0Fu) | (((h >> 6) & 0x03030303u) << 4)), X3[k], d3);
+        }
+        // int8 scales sc[8n + 2g + hh], g = 0..3: byte (8n + hh + 2g) of f.s
+        const uint32_t sw0 = n ? f.s.z : f.s.x, sw1 = n ? f.s.w : f.s.y;
+        const int s0 = (int)(int8_t)(sw0 >> (8 * hh)), s1 = (int)(int8_t)(sw0 >> (8 * (hh + 2)));
+        const int s2 = (int)(int8_t)(sw1 >> (8 * hh)), s3 = (int)(int8_t)(sw1 >> (8 * (hh + 2)));
+        const int32_t *bs = xs + 8 * n + hh;
+        // (q - 32) . x = q . x - 32 * sum(x)
+        I = s0 * (d0 - 32 * bs[0]) + s1 * (d1 - 32 * bs[2]) + s2 * (d2 - 32 * bs[4]) + s3 * (d3 - 32 * bs[6]);
+        M = 0;
+    }
+    __device__ __forceinline__ static float term(const Frag &f, int I, int, float xd) {
+        return fmul(fmul(xd, f16_to_f32((uint16_t)f.d)), (float)I);
+    }
+};
+
+template <> struct QT<T_Q8_0> {
+    static constexpr int LPB = 2, BE = 32, SPB = 1;
+    struct Frag {
+        uint4 q;
+        uint32_t d;
+    };
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int sub) {
+        return Frag{ld_stream_v4(w.q + gb * 32 + 16 * sub), (uint32_t)__ldg(w.d + gb)};
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int sub, const int8_t *xq, const int32_t *, int &I,
+                                                int &M) {
+        const int4 x = *reinterpret_cast<const int4 *>(xq + 16 * sub);
+        int dot = 0;
+        dot = dp4a((int)f.q.x, x.x, dot);
+        dot = dp4a((int)f.q.y, x.y, dot);
+        dot = dp4a((int)f.q.z, x.z, dot);
+        dot = dp4a((int)f.q.w, x.w, dot);
+        I = dot;
+        M = 0;
+    }
+    __device__ __forceinline__ static float term(const Frag &f, int I, int, float xd) {
+        return fmul(fmul(f16_to_f32((uint16_t)f.d), xd), (float)I);
+    }
+};
+
+template <> struct QT<T_Q4_0> {
+    static constexpr int LPB = 1, BE = 32, SPB = 1;
+    struct Frag {
+        uint4 q;
+        uint32_t d;
+    };
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int) {
+        return Frag{ld_stream_v4(w.q + gb * 16), (uint32_t)__ldg(w.d + gb)};
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int, const int8_t *xq, const int32_t *xs, int &I, int &M) {
+        const int4 xl = *reinterpret_cast<const int4 *>(xq), xh = *reinterpret_cast<const int4 *>(xq + 16);
+        int dot = 0;
+        dot = dp4a((int)(f.q.x & 0x0F0F0F0Fu), xl.x, dot);
+        dot = dp4a((int)(f.q.y & 0x0F0F0F0Fu), xl.y, dot);
+        dot = dp4a((int)(f.q.z & 0x0F0F0F0Fu), xl.z, dot);
+        dot = dp4a((int)(f.q.w & 0x0F0F0F0Fu), xl.w, dot);
+        dot = dp4a((int)((f.q.x >> 4) & 0x0F0F0F0Fu), xh.x, dot);
+        dot = dp4a((int)((f.q.y >> 4) & 0x0F0F0F0Fu), xh.y, dot);
+        dot = dp4a((int)((f.q.z >> 4) & 0x0F0F0F0Fu), xh.z, dot);
+        dot = dp4a((int)((f.q.w >> 4) & 0x0F0F0F0Fu), xh.w, dot);
+        I = dot - 8 * xs[0];
+        M = 0;
+    }
+    __device__ __forceinline__ static float term(const Frag &f, int I, int, float xd) {
+        return fmul(fmul(f16_to_f32((uint16_t)f.d), xd), (float)I);
+    }
+};
+
+// Streams: a functor `at(s, w, gb, xv)` giving stream s's weight tensor, first
+// block, and activation view (s < nS <= S always).
+//
+// The engine is split so a kernel can issue its weight loads, then wait for
+// the producer of its activations (programmatic dependent launch), then
+// finish: wd_load issues every load of the warp; wd_finish forms the terms and
+// adds each stream's terms in block order into acc[0..nS). NB (blocks per
+// stream) and nS (streams in use, <= S) are runtime values with
+// nS*NB <= MAXU*G.
+template <int TY, int MAXU> struct WFrags {
+    typename QT<TY>::Frag f[MAXU];
+};
+
+template <int TY, int S, int MAXU, class Streams>
+__device__ __forceinline__ void wd_load(const Streams &st, int NB, int nS, WFrags<TY, MAXU> &fr, int lane) {
+    using Q = QT<TY>;
+    constexpr int G = 32 / Q::LPB;
+    const int U = nS * NB;
+    const int grp = lane / Q::LPB, sub = lane % Q::LPB;
+#pragma unroll
+    for (int j = 0; j < MAXU; j++) {
+        const int u = j * G + grp;
+        if (u < U) {
+            const int s = u / NB, b = u - s * NB;
+            WDev w;
+            uint64_t gb;
+            XV xv;
+            st.at(s, w, gb, xv);
+            fr.f[j] = Q::load(w, gb + b, sub);
+        }
+    }
+}
+
+template <int TY, int S, int MAXU, class Streams>
+__device__ __forceinline__ void wd_finish(const Streams &st, int NB, int nS, const WFrags<TY, MAXU> &fr,
+                                          float (&acc)[S], int lane) {
+    using Q = QT<TY>;
+    constexpr int G = 32 / Q::LPB;
+    const int U = nS * NB;
+    const int grp = lane / Q::LPB, sub = lane % Q::LPB;
+    float term[MAXU];
+#pragma unroll
+    for (int j = 0; j < MAXU; j++) {
+        const int u = j * G + grp;
+        int I = 0, M = 0;
+        float xd = 0.0f;
+        if (u < U) {
+            const int s = u / NB, b = u - s * NB;
+            WDev w;
+            uint64_t gb;
+            XV xv;
+            st.at(s, w, gb, xv);
+            Q::part(fr.f[j], sub, xv.q + b * Q::BE, xv.s + b * Q::SPB, I, M);
+            xd = xv.d[b];
+        }
+#pragma unroll
+        for (int o = 1; o < Q::LPB; o <<= 1) {
+            I += __shfl_xor_sync(0xffffffffu, I, o);
+            M += __shfl_xor_sync(0xffffffffu, M, o);
+        }
+        term[j] = u < U ? Q::term(fr.f[j], I, M, xd) : 0.0f;
+    }
+    // units are numbered stream-major, so walking them in order visits every
+    // stream's blocks in block order
+    float a = 0.0f;
+#pragma unroll
+    for (int j = 0; j < MAXU; j++) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const int u = j * G + g;
+            const float t = __shfl_sync(0xffffffffu, term[j], g * Q::LPB);
+            if (u < U) {
+                const int s = u / NB, b = u - s * NB;
+                a = fadd(b == 0 ? 0.0f : a, t);  // the CPU accumulator starts at +0
+                if (b == NB - 1) {
+#pragma unroll
+                    for (int ss = 0; ss < S; ss++)
+                        if (ss == s) acc[ss] = a;
+                }
+            }
+        }
+    }
+}
+
+}  // namespace loom

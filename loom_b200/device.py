@@ -99,5 +99,10 @@ def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -
               "tensor_matmul")
 
 
+def force_generic(on: bool) -> bool:
+    """Route MoE layers through the general slot kernels (test cross-check)."""
+    return bool(_lib.lib().loom_cuda_force_generic(int(on)))
+
+
 def sync() -> None:
     _lib.must(_lib.lib().loom_cuda_sync(), "sync")

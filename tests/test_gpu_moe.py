@@ -122,7 +122,7 @@ def _route_gaps_ok(logits_row, k):
     return bool(np.all(s[:k] - s[1:k + 1] > 1e-4))
 
 
-@pytest.mark.parametrize("T", [1, 64])
+@pytest.mark.parametrize("T", [1, 4, 64])
 def test_device_layer_with_router(be, orc, T):
     """The whole layer on the device (router GEMV -> route -> experts ->
     combine) against the oracle's moeLayer at BASELINE config 2, T in {1, 64}."""
@@ -153,3 +153,75 @@ def test_device_layer_with_router(be, orc, T):
     assert compared >= max(1, T * 3 // 4)
     for t in (L.gate, L.up, L.down, L.router):
         t.free()
+
+
+def _layer_case(orc, seed, ne, k, dim, ffn, gt, dt, shared=0, gating=1, scale=1.0, bias=False):
+    g, u, d = synth_layer(orc, seed, ne, dim, ffn, gt, gt, dt)
+    rw = orc.synth(0, ne * dim, seed=seed * 7 + 1, sigma=0.02)
+    L = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(gt, g), DeviceTensor.upload(gt, u), DeviceTensor.upload(dt, d),
+                 router=DeviceTensor.upload(0, rw), gating=gating, weights_scale=scale)
+    if bias:
+        L.router_bias = DeviceTensor.upload(0, (np.random.default_rng(seed).standard_normal(ne) * 0.05).astype(np.float32))
+    if shared:
+        sg, su, sd = synth_layer(orc, seed + 50, 1, dim, shared, gt, gt, dt)
+        L.shexp = (DeviceTensor.upload(gt, sg), DeviceTensor.upload(gt, su), DeviceTensor.upload(dt, sd))
+        L.shexp_ffn = shared
+    return L
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(ne=128, k=8, dim=2048, ffn=768, gt=12, dt=14),                     # Qwen3-30B-A3B
+    dict(ne=64, k=6, dim=2048, ffn=1408, gt=12, dt=8, shared=2816),          # DeepSeek-V2-Lite
+    dict(ne=256, k=8, dim=1024, ffn=512, gt=12, dt=12, shared=512, gating=2, scale=2.5, bias=True),  # V3-like
+    dict(ne=16, k=4, dim=512, ffn=256, gt=14, dt=14),                        # Q6_K gate/up
+], ids=["qwen3", "v2lite", "v3like", "q6k"])
+@pytest.mark.parametrize("T", [1, 3])
+def test_decode_kernels_bitexact_with_slot_kernels(be, orc, cfg, T):
+    """The fused decode kernels and the general slot kernels implement the
+    same arithmetic: their outputs must agree bit for bit."""
+    from loom_b200 import device as D
+    L = _layer_case(orc, 5, **cfg)
+    x = torch.from_numpy(orc.synth(0, T * cfg["dim"], seed=9).reshape(T, cfg["dim"])).cuda()
+    res = torch.randn(T, cfg["dim"], device="cuda")
+    outs, idss = [], []
+    for generic in (False, True):
+        prev = D.force_generic(generic)
+        try:
+            out = torch.full((T, cfg["dim"]), float("nan"), device="cuda")
+            ids = torch.zeros((T, cfg["k"]), dtype=torch.int32, device="cuda")
+            L.forward(x, out, residual=res, ids=ids)
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
+            idss.append(ids.cpu().numpy())
+        finally:
+            D.force_generic(prev)
+    assert np.array_equal(idss[0], idss[1])
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+
+
+def test_expert_parallel_partition_sums_to_full(be, orc):
+    """Expert-parallel shards: each rank runs only its expert range; the sum of
+    the partial outputs equals the unsharded layer (to rounding: the combine
+    order changes)."""
+    ne, k, dim, ffn = 64, 6, 1024, 512
+    g, u, d = synth_layer(orc, 6, ne, dim, ffn)
+    rw = orc.synth(0, ne * dim, seed=61, sigma=0.02)
+    x = torch.from_numpy(orc.synth(0, 2 * dim, seed=62).reshape(2, dim)).cuda()
+    pg, pd = ffn * orc.row_bytes(12, dim), dim * orc.row_bytes(14, ffn)
+    full = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g), DeviceTensor.upload(12, u),
+                    DeviceTensor.upload(14, d), router=DeviceTensor.upload(0, rw))
+    want = torch.empty((2, dim), device="cuda")
+    full.forward(x, want)
+    parts = []
+    R = 4
+    for rank in range(R):
+        e0, n = rank * ne // R, ne // R
+        L = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g[e0 * pg:(e0 + n) * pg]),
+                     DeviceTensor.upload(12, u[e0 * pg:(e0 + n) * pg]), DeviceTensor.upload(14, d[e0 * pd:(e0 + n) * pd]),
+                     router=full.router, expert0=e0, n_local=n)
+        o = torch.empty((2, dim), device="cuda")
+        L.forward(x, o)
+        parts.append(o)
+    got = sum(parts)
+    torch.cuda.synchronize()
+    assert rel_l2(got.cpu().numpy(), want.cpu().numpy()) < 1e-5
