@@ -334,7 +334,10 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers in the stack (default 48; smaller only for profiling captures)")
     args = ap.parse_args()
+    globals()["LAYERS"] = args.layers
     if args.impl == "reference":
         run_reference(args)
     else:

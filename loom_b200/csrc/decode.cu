@@ -181,18 +181,18 @@ struct GateUpStreams {
     WDev wg, wu;
     uint64_t gb_g, gb_u;  // first block of the warp's first row
     int nb;
-    XV x;
-    __device__ __forceinline__ void at(int s, WDev &w, uint64_t &gb, XV &xv) const {
-        const bool up = s >= GU_NR;
-        const int r = up ? s - GU_NR : s;
-        w = up ? wu : wg;
-        gb = (up ? gb_u : gb_g) + (uint64_t)r * nb;
-        xv = x;
+    XV xv;
+    __device__ __forceinline__ WDev w(int s) const { return s < GU_NR ? wg : wu; }
+    __device__ __forceinline__ uint64_t gb(int s) const {
+        return s < GU_NR ? gb_g + (uint64_t)s * nb : gb_u + (uint64_t)(s - GU_NR) * nb;
     }
+    __device__ __forceinline__ XV x(int) const { return xv; }
 };
 
-template <int TY, int MAXU>
+template <int TY, int NB>
 __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
+    using E = CEng<TY, 2 * GU_NR, NB>;
+    static_assert(E::OK, "unit mapping");
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ int last;
     pdl_wait();
@@ -202,27 +202,26 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
     const int rows_cta = GU_WARPS * GU_NR;
     const int nctas = (si.ffn + rows_cta - 1) / rows_cta;
     if ((int)blockIdx.x >= nctas) return;
-    const int dim = A.dim;
+    constexpr int dim = NB * 256;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // stage the token's quantized activation (gate and up share the K format)
     int8_t *xq = reinterpret_cast<int8_t *>(sm);
     float *xd = reinterpret_cast<float *>(sm + dim);
-    int32_t *xs = reinterpret_cast<int32_t *>(sm + dim + dim / 256 * 4);
+    int32_t *xs = reinterpret_cast<int32_t *>(sm + dim + NB * 4);
     stage16(xq, A.x256.q + (size_t)si.token * dim, dim);
-    for (int i = threadIdx.x; i < dim / 256; i += blockDim.x) xd[i] = __ldcg(A.x256.d + (size_t)si.token * (dim / 256) + i);
-    for (int i = threadIdx.x; i < dim / 16; i += blockDim.x) xs[i] = __ldcg(A.x256.s + (size_t)si.token * (dim / 16) + i);
-    __syncthreads();
+    for (int i = threadIdx.x; i < NB; i += blockDim.x) xd[i] = __ldcg(A.x256.d + (size_t)si.token * NB + i);
+    for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) xs[i] = __ldcg(A.x256.s + (size_t)si.token * NB * 16 + i);
     const WDev wg = si.shared ? A.sg : A.g, wu = si.shared ? A.su : A.u;
-    const int nb = dim / 256;
-    const uint64_t plane = si.shared ? 0 : (uint64_t)si.expert_local * si.ffn * nb;
+    const uint64_t plane = si.shared ? 0 : (uint64_t)si.expert_local * si.ffn * NB;
     const int r0 = blockIdx.x * rows_cta + warp * GU_NR;
     const int rmax = si.ffn - GU_NR;
     const int rl = r0 <= rmax ? r0 : rmax;  // clamp the last (partial) group; its extra rows are not stored
-    GateUpStreams st{wg, wu, plane + (uint64_t)rl * nb, plane + (uint64_t)rl * nb, nb, XV{xq, xd, xs}};
-    WFrags<TY, MAXU> fr;
-    wd_load<TY, 2 * GU_NR, MAXU>(st, nb, 2 * GU_NR, fr, lane);
+    GateUpStreams st{wg, wu, plane + (uint64_t)rl * NB, plane + (uint64_t)rl * NB, NB, XV{xq, xd, xs}};
+    typename E::Frags fr;
+    E::load(st, fr, lane);  // weight loads are in flight while the activation lands in shared memory
+    __syncthreads();
     float acc[2 * GU_NR];
-    wd_finish<TY, 2 * GU_NR, MAXU>(st, nb, 2 * GU_NR, fr, acc, lane);
+    E::finish(st, fr, acc, lane);
     float *act = A.act + (size_t)slot * A.act_stride;
     if (lane == 0) {
 #pragma unroll
@@ -268,23 +267,34 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
 constexpr int DN_WARPS = 4;
 
 struct DownStreams {
-    WDev w;
-    const uint64_t *gb;  // per stream: first block of this output row (shared memory)
+    WDev wd;
+    const uint64_t *g;   // per stream: first block of this output row (shared memory)
     const int *sl;       // per stream: staged activation index (shared memory)
     const int8_t *aq;    // staged activations: index j at aq + j*stride
     const float *ad;
     const int32_t *as;
     int stride;
-    __device__ __forceinline__ void at(int s, WDev &wo, uint64_t &g, XV &xv) const {
-        wo = w;
-        g = gb[s];
-        const int j = sl[s];
-        xv = XV{aq + (size_t)j * stride, ad + (size_t)j * (stride / 32), as + (size_t)j * (stride / 16)};
+    int nvalid;          // streams beyond this repeat stream 0 (their result is unused)
+    __device__ __forceinline__ WDev w(int) const { return wd; }
+    __device__ __forceinline__ uint64_t gb(int s) const { return g[s < nvalid ? s : 0]; }
+    __device__ __forceinline__ XV x(int s) const {
+        const int j = sl[s < nvalid ? s : 0];
+        return XV{aq + (size_t)j * stride, ad + (size_t)j * (stride / 32), as + (size_t)j * (stride / 16)};
+    }
+    // run-time engine interface
+    __device__ __forceinline__ void at(int s, WDev &wo, uint64_t &gg, XV &xv) const {
+        wo = wd;
+        gg = gb(s);
+        xv = x(s);
     }
 };
 
-template <int TY, int SC, int MAXU>
+// SC streams (experts) per chunk of NB blocks; NBSH = shared expert blocks (0: none)
+template <int TY, int SC, int NB, int NBSH>
 __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
+    using E = CEng<TY, SC, NB>;
+    using ES = CEng<TY, 1, (NBSH > 0 ? NBSH : QT<TY>::LPB == 8 ? 4 : 32 / QT<TY>::LPB)>;
+    static_assert(E::OK, "unit mapping");
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ int s_slot[64];  // local routed slots of this token, selection order
     __shared__ float s_gate[64];
@@ -295,8 +305,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.x * DN_WARPS + warp;
     const int rr = r < A.dim ? r : A.dim - 1;
-    const int nk = A.n_used, ffn = A.ffn;
-    const int nb = ffn / QT<TY>::BE;
+    const int nk = A.n_used;
     // Routing is final before this kernel may start: k_gateup_dec triggers its
     // dependents only after its own wait on the router, so ids/gates are read now.
     if (threadIdx.x == 0) {
@@ -314,27 +323,34 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     }
     __syncthreads();
     const int nloc = s_nloc;
-    if (lane < SC && lane < nloc) {
-        const int le = __ldcg(A.ids + (size_t)t * nk + s_slot[lane]) - A.expert0;
-        s_gb[warp][lane] = ((uint64_t)le * A.dim + rr) * nb;
-    }
-    __syncwarp();
+    auto set_gb = [&](int c0, int n) {
+        __syncwarp();
+        if (lane < n) {
+            const int le = __ldcg(A.ids + (size_t)t * nk + s_slot[c0 + lane]) - A.expert0;
+            s_gb[warp][lane] = ((uint64_t)le * A.dim + rr) * NB;
+        }
+        __syncwarp();
+    };
     int8_t *aq = reinterpret_cast<int8_t *>(sm);
     const int stride = A.act_stride;
-    const int nk1 = nk + (A.has_shared ? 1 : 0);  // staged: the token's routed slots, then its shared one
+    const int nk1 = nk + (NBSH > 0 ? 1 : 0);  // staged: the token's routed slots, then its shared one
     float *ad = reinterpret_cast<float *>(sm + (size_t)nk1 * stride);
     int32_t *as = reinterpret_cast<int32_t *>(sm + (size_t)nk1 * stride + (size_t)nk1 * (stride / 32) * 4);
-    DownStreams st{A.dn, s_gb[warp], s_slot, aq, ad, as, stride};
-    WFrags<TY, MAXU> fr;
+    typename E::Frags fr;
     const int n0 = nloc < SC ? nloc : SC;
-    if (n0 > 0) wd_load<TY, SC, MAXU>(st, nb, n0, fr, lane);  // the first chunk's weights, before the wait
+    DownStreams st{A.dn, s_gb[warp], s_slot, aq, ad, as, stride, n0};
+    if (n0 > 0) {  // the first chunk's weights, before the wait
+        set_gb(0, n0);
+        if (n0 == SC) E::load(st, fr, lane);
+        else wd_load<TY, SC, E::MAXU>(st, NB, n0, fr, lane);
+    }
     pdl_wait();
     pdl_trigger();
     const size_t slot0 = (size_t)t * nk;
     stage16(aq, A.aq + slot0 * stride, nk * stride);
     for (int i = threadIdx.x; i < nk * (stride / 32); i += blockDim.x) ad[i] = __ldcg(A.ad + slot0 * (stride / 32) + i);
     for (int i = threadIdx.x; i < nk * (stride / 16); i += blockDim.x) as[i] = __ldcg(A.as + slot0 * (stride / 16) + i);
-    if (A.has_shared) {
+    if (NBSH > 0) {
         const size_t ss = (size_t)A.T * nk + t;
         stage16(aq + (size_t)nk * stride, A.aq + ss * stride, stride);
         for (int i = threadIdx.x; i < stride / 32; i += blockDim.x)
@@ -346,31 +362,29 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     float acc = 0.0f;
     for (int c0 = 0; c0 < nloc; c0 += SC) {
         const int n = nloc - c0 < SC ? nloc - c0 : SC;
+        st.sl = s_slot + c0;
+        st.nvalid = n;
         if (c0 > 0) {
-            __syncwarp();
-            if (lane < n) {
-                const int le = __ldcg(A.ids + (size_t)t * nk + s_slot[c0 + lane]) - A.expert0;
-                s_gb[warp][lane] = ((uint64_t)le * A.dim + rr) * nb;
-            }
-            __syncwarp();
-            st.sl = s_slot + c0;
-            wd_load<TY, SC, MAXU>(st, nb, n, fr, lane);
+            set_gb(c0, n);
+            if (n == SC) E::load(st, fr, lane);
+            else wd_load<TY, SC, E::MAXU>(st, NB, n, fr, lane);
         }
         float y[SC];
-        wd_finish<TY, SC, MAXU>(st, nb, n, fr, y, lane);
+        if (n == SC) E::finish(st, fr, y, lane);
+        else wd_finish<TY, SC, E::MAXU>(st, NB, n, fr, y, lane);
 #pragma unroll
         for (int k = 0; k < SC; k++)
             if (k < n) acc = fadd(acc, fmul(s_gate[c0 + k], y[k]));  // moeRun: acc += gate * out (llama.zig:1397)
     }
-    if (A.has_shared) {  // shared expert added plainly after the routed sum (deepseek.zig:1498-1508)
-        const int nbs = A.shexp_ffn / QT<TY>::BE;
+    if constexpr (NBSH > 0) {  // shared expert added plainly after the routed sum (deepseek.zig:1498-1508)
         __syncwarp();
-        if (lane == 0) s_gb[warp][0] = (uint64_t)rr * nbs;
+        if (lane == 0) s_gb[warp][0] = (uint64_t)rr * NBSH;
         __syncwarp();
-        DownStreams sh{A.sdn, s_gb[warp], &s_shidx, aq, ad, as, stride};
-        wd_load<TY, SC, MAXU>(sh, nbs, 1, fr, lane);
-        float y[SC];
-        wd_finish<TY, SC, MAXU>(sh, nbs, 1, fr, y, lane);
+        DownStreams sh{A.sdn, s_gb[warp], &s_shidx, aq, ad, as, stride, 1};
+        typename ES::Frags fs;
+        ES::load(sh, fs, lane);
+        float y[1];
+        ES::finish(sh, fs, y, lane);
         acc = fadd(acc, y[0]);
     }
     if (lane == 0 && r < A.dim) {
@@ -380,64 +394,37 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
 }
 
 // ---- dispatch ---------------------------------------------------------------------
+// The instantiated shapes: gate/up blocks per row (dim/256) and, for the down
+// projection, (type, experts per chunk, blocks per row, shared-expert blocks).
+// Other shapes run on the general slot kernels (same arithmetic).
 
-// register budget: fragments per lane (Q6_K fragments are 17 registers, Q4_K 8, Q8_0 5)
-static constexpr int max_maxu(int ty) { return ty == T_Q6_K ? 8 : 16; }
-static constexpr int lanes_per_block(int ty) { return ty == T_Q4_K ? 8 : ty == T_Q6_K ? 4 : ty == T_Q8_0 ? 2 : 1; }
-
-static int pick_maxu(int units, int G, int ty) {
-    const int need = (units + G - 1) / G;
-    const int buckets[] = {2, 3, 4, 6, 8, 12, 16};
-    for (int b : buckets)
-        if (need <= b && b <= max_maxu(ty)) return b;
-    return 0;
+using GUFn = void (*)(DecodeArgs);
+static GUFn gateup_fn(int ty, int nb) {
+    if (ty == T_Q4_K) switch (nb) {
+            case 4: return k_gateup_dec<T_Q4_K, 4>;
+            case 8: return k_gateup_dec<T_Q4_K, 8>;
+            case 16: return k_gateup_dec<T_Q4_K, 16>;
+            case 28: return k_gateup_dec<T_Q4_K, 28>;
+        }
+    if (ty == T_Q6_K && nb == 8) return k_gateup_dec<T_Q6_K, 8>;
+    return nullptr;
 }
 
-template <int TY>
-static cudaError_t launch_gateup_t(const DecodeArgs &A, int maxu, dim3 grid, size_t smem, cudaStream_t st) {
-    const dim3 blk(GU_WARPS * 32);
-    switch (maxu) {
-        case 2: return launch_pdl(k_gateup_dec<TY, 2>, grid, blk, smem, st, A);
-        case 3: return launch_pdl(k_gateup_dec<TY, 3>, grid, blk, smem, st, A);
-        case 4: return launch_pdl(k_gateup_dec<TY, 4>, grid, blk, smem, st, A);
-        case 6: return launch_pdl(k_gateup_dec<TY, 6>, grid, blk, smem, st, A);
-        case 8: return launch_pdl(k_gateup_dec<TY, 8>, grid, blk, smem, st, A);
-        case 12:
-            if constexpr (max_maxu(TY) >= 12) return launch_pdl(k_gateup_dec<TY, 12>, grid, blk, smem, st, A);
-            break;
-        case 16:
-            if constexpr (max_maxu(TY) >= 16) return launch_pdl(k_gateup_dec<TY, 16>, grid, blk, smem, st, A);
-            break;
+static GUFn down_fn(int ty, int nb, int nbsh) {
+    if (ty == T_Q6_K && nbsh == 0) switch (nb) {  // 8 experts per chunk, block-major units
+            case 1: return k_down_dec<T_Q6_K, 8, 1, 0>;
+            case 2: return k_down_dec<T_Q6_K, 8, 2, 0>;
+            case 3: return k_down_dec<T_Q6_K, 8, 3, 0>;
+            case 4: return k_down_dec<T_Q6_K, 8, 4, 0>;
+            case 8: return k_down_dec<T_Q6_K, 8, 8, 0>;
+        }
+    if (ty == T_Q4_K) {  // 4 experts per chunk, stream-major units
+        if (nb == 4 && nbsh == 0) return k_down_dec<T_Q4_K, 4, 4, 0>;
+        if (nb == 4 && nbsh == 4) return k_down_dec<T_Q4_K, 4, 4, 4>;
+        if (nb == 8 && nbsh == 0) return k_down_dec<T_Q4_K, 4, 8, 0>;
+        if (nb == 8 && nbsh == 8) return k_down_dec<T_Q4_K, 4, 8, 8>;
     }
-    return cudaErrorInvalidValue;
-}
-
-template <int TY, int SC>
-static cudaError_t launch_down_t(const DecodeArgs &A, int maxu, dim3 grid, size_t smem, cudaStream_t st) {
-    const dim3 blk(DN_WARPS * 32);
-    switch (maxu) {
-        case 2: return launch_pdl(k_down_dec<TY, SC, 2>, grid, blk, smem, st, A);
-        case 3: return launch_pdl(k_down_dec<TY, SC, 3>, grid, blk, smem, st, A);
-        case 4: return launch_pdl(k_down_dec<TY, SC, 4>, grid, blk, smem, st, A);
-        case 6: return launch_pdl(k_down_dec<TY, SC, 6>, grid, blk, smem, st, A);
-        case 8: return launch_pdl(k_down_dec<TY, SC, 8>, grid, blk, smem, st, A);
-        case 12:
-            if constexpr (max_maxu(TY) >= 12) return launch_pdl(k_down_dec<TY, SC, 12>, grid, blk, smem, st, A);
-            break;
-        case 16:
-            if constexpr (max_maxu(TY) >= 16) return launch_pdl(k_down_dec<TY, SC, 16>, grid, blk, smem, st, A);
-            break;
-    }
-    return cudaErrorInvalidValue;
-}
-
-// streams per chunk of the down kernel, and its fragment bucket
-static int down_sc(int dty, int nb, int &maxu) {
-    const int G = 32 / lanes_per_block(dty);
-    const int want = dty == T_Q4_K ? 4 : 8;
-    if ((maxu = pick_maxu(want * nb, G, dty))) return want;
-    if ((maxu = pick_maxu(2 * nb, G, dty))) return 2;
-    return 0;
+    return nullptr;
 }
 
 static size_t down_smem(const DecodeArgs &A) {
@@ -445,22 +432,18 @@ static size_t down_smem(const DecodeArgs &A) {
     return nk1 * A.act_stride + nk1 * (A.act_stride / 32) * 4 + nk1 * (A.act_stride / 16) * 4;
 }
 
+static int shared_nb(const DecodeArgs &A) { return A.has_shared ? A.shexp_ffn / block_elems(A.sdn.type) : 0; }
+
 bool decode_supported(const DecodeArgs &A) {
-    // gate and up: one K-quant type over whole super-blocks
-    if (A.g.type != A.u.type || (A.g.type != T_Q4_K && A.g.type != T_Q6_K)) return false;
-    if (A.dim % 256 || A.dim > 8192 || A.n_used > 64) return false;
-    if (!pick_maxu(2 * GU_NR * (A.dim / 256), 32 / lanes_per_block(A.g.type), A.g.type)) return false;
-    // down: Q4_K / Q6_K / Q8_0 over whole blocks
+    if (A.g.type != A.u.type || A.dim % 256 || A.n_used > 64) return false;
+    if (!gateup_fn(A.g.type, A.dim / 256)) return false;
     const int dty = A.dn.type;
-    if (dty != T_Q4_K && dty != T_Q6_K && dty != T_Q8_0) return false;
-    if (A.ffn % block_elems(dty)) return false;
-    int maxu = 0;
-    if (!down_sc(dty, A.ffn / block_elems(dty), maxu)) return false;
-    if (A.has_shared) {  // the shared expert must fit the same instantiation
+    if (block_elems(dty) == 0 || A.ffn % block_elems(dty)) return false;
+    if (A.has_shared) {
         if (A.sg.type != A.g.type || A.su.type != A.g.type || A.sdn.type != dty) return false;
         if (A.shexp_ffn % block_elems(dty) || A.shexp_ffn > A.act_stride) return false;
-        if (A.shexp_ffn / block_elems(dty) > maxu * (32 / lanes_per_block(dty))) return false;
     }
+    if (!down_fn(dty, A.ffn / block_elems(dty), shared_nb(A))) return false;
     const size_t max_ffn = A.has_shared && A.shexp_ffn > A.ffn ? A.shexp_ffn : A.ffn;
     return down_smem(A) <= 48 * 1024 && (size_t)(A.dim + 2 * A.n_expert) * 4 <= 48 * 1024 &&
            max_ffn * 4 <= 48 * 1024;
@@ -482,30 +465,15 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
         const dim3 grid(cdivu(max_ffn, GU_WARPS * GU_NR), n_slots);
         const size_t smem_x = (size_t)A.dim + A.dim / 256 * 4 + A.dim / 16 * 4;
         const size_t smem_q = (size_t)max_ffn * 4;
-        const size_t smem = smem_x > smem_q ? smem_x : smem_q;
-        const int units = 2 * GU_NR * (A.dim / 256);
-        if (A.g.type == T_Q4_K)
-            e = launch_gateup_t<T_Q4_K>(A, pick_maxu(units, 4, T_Q4_K), grid, smem, st);
-        else
-            e = launch_gateup_t<T_Q6_K>(A, pick_maxu(units, 8, T_Q6_K), grid, smem, st);
+        e = launch_pdl(gateup_fn(A.g.type, A.dim / 256), grid, dim3(GU_WARPS * 32), smem_x > smem_q ? smem_x : smem_q,
+                       st, A);
         if (e != cudaSuccess) return e;
     }
     // 3. down + combine
     {
         const dim3 grid(cdivu(A.dim, DN_WARPS), A.T);
-        const int dty = A.dn.type;
-        int maxu = 0;
-        const int sc = down_sc(dty, A.ffn / block_elems(dty), maxu);
-        const size_t smem = down_smem(A);
-        if (dty == T_Q6_K)
-            e = sc == 8 ? launch_down_t<T_Q6_K, 8>(A, maxu, grid, smem, st)
-                        : launch_down_t<T_Q6_K, 2>(A, maxu, grid, smem, st);
-        else if (dty == T_Q4_K)
-            e = sc == 4 ? launch_down_t<T_Q4_K, 4>(A, maxu, grid, smem, st)
-                        : launch_down_t<T_Q4_K, 2>(A, maxu, grid, smem, st);
-        else
-            e = sc == 8 ? launch_down_t<T_Q8_0, 8>(A, maxu, grid, smem, st)
-                        : launch_down_t<T_Q8_0, 2>(A, maxu, grid, smem, st);
+        e = launch_pdl(down_fn(A.dn.type, A.ffn / block_elems(A.dn.type), shared_nb(A)), grid, dim3(DN_WARPS * 32),
+                       down_smem(A), st, A);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

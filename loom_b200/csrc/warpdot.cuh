@@ -267,3 +267,72 @@ __device__ __forceinline__ void wd_finish(const Streams &st, int NB, int nS, con
 }
 
 }  // namespace loom
+
+namespace loom {
+
+// ---- compile-time engine ------------------------------------------------------------
+// Same arithmetic as wd_load/wd_finish, with S streams of NB blocks fixed at
+// compile time and a unit order that makes every stream/block index a
+// constant or a lane offset (no division at run time):
+//   stream-major  (NB % G == 0): unit j*G + grp is stream (j*G)/NB, block (j*G)%NB + grp
+//   block-major   (S  % G == 0): unit j*G + grp is block (j*G)/S,  stream (j*G)%S + grp
+// The Streams functor takes the (possibly lane-dependent) stream index.
+template <int TY, int S, int NB> struct CEng {
+    using Q = QT<TY>;
+    static constexpr int G = 32 / Q::LPB;
+    static constexpr bool SM = NB % G == 0;
+    static constexpr bool BM = !SM && S % G == 0;
+    static constexpr bool OK = SM || BM;
+    static constexpr int MAXU = (S * NB) / G;
+    using Frags = WFrags<TY, MAXU>;  // shared with the run-time engine for partial chunks
+    __device__ __forceinline__ static void unit(int j, int grp, int &s, int &b) {
+        if constexpr (SM) {
+            s = (j * G) / NB;
+            b = (j * G) % NB + grp;
+        } else {
+            b = (j * G) / S;
+            s = (j * G) % S + grp;
+        }
+    }
+    template <class Streams>
+    __device__ __forceinline__ static void load(const Streams &st, Frags &fr, int lane) {
+        const int grp = lane / Q::LPB, sub = lane % Q::LPB;
+#pragma unroll
+        for (int j = 0; j < MAXU; j++) {
+            int s, b;
+            unit(j, grp, s, b);
+            fr.f[j] = Q::load(st.w(s), st.gb(s) + b, sub);
+        }
+    }
+    template <class Streams>
+    __device__ __forceinline__ static void finish(const Streams &st, const Frags &fr, float (&acc)[S], int lane) {
+        const int grp = lane / Q::LPB, sub = lane % Q::LPB;
+        float term[MAXU];
+#pragma unroll
+        for (int j = 0; j < MAXU; j++) {
+            int s, b;
+            unit(j, grp, s, b);
+            const XV xv = st.x(s);
+            int I, M;
+            Q::part(fr.f[j], sub, xv.q + b * Q::BE, xv.s + b * Q::SPB, I, M);
+#pragma unroll
+            for (int o = 1; o < Q::LPB; o <<= 1) {
+                I += __shfl_xor_sync(0xffffffffu, I, o);
+                if constexpr (TY == T_Q4_K) M += __shfl_xor_sync(0xffffffffu, M, o);
+            }
+            term[j] = Q::term(fr.f[j], I, M, xv.d[b]);
+        }
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            float a = 0.0f;
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const int u = SM ? s * NB + b : b * S + s;
+                a = fadd(a, __shfl_sync(0xffffffffu, term[u / G], (u % G) * Q::LPB));
+            }
+            acc[s] = a;
+        }
+    }
+};
+
+}  // namespace loom

@@ -172,7 +172,7 @@ def _layer_case(orc, seed, ne, k, dim, ffn, gt, dt, shared=0, gating=1, scale=1.
 @pytest.mark.parametrize("cfg", [
     dict(ne=128, k=8, dim=2048, ffn=768, gt=12, dt=14),                     # Qwen3-30B-A3B
     dict(ne=64, k=6, dim=2048, ffn=1408, gt=12, dt=8, shared=2816),          # DeepSeek-V2-Lite
-    dict(ne=256, k=8, dim=1024, ffn=512, gt=12, dt=12, shared=512, gating=2, scale=2.5, bias=True),  # V3-like
+    dict(ne=256, k=8, dim=1024, ffn=1024, gt=12, dt=12, shared=1024, gating=2, scale=2.5, bias=True),  # V3-like
     dict(ne=16, k=4, dim=512, ffn=256, gt=14, dt=14),                        # Q6_K gate/up
 ], ids=["qwen3", "v2lite", "v3like", "q6k"])
 @pytest.mark.parametrize("T", [1, 3])
