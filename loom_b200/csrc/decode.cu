@@ -2,21 +2,20 @@
 // with programmatic dependent launch (PDL), each issuing its weight loads
 // before it waits for its producer.
 //
-//   k_router_route  router GEMV (dotF32 order) for 4 experts per CTA; the last
-//                   CTA of each token routes (moe.zig:106 route) and quantizes
-//                   the token's activation for the expert kernels. Router
-//                   weights are loaded BEFORE waiting for the previous layer.
-//   k_gateup_dec    gate and up rows of every (token, expert) slot + SwiGLU;
-//                   the last CTA of each slot quantizes the slot's activation
-//                   for the down projection.
-//   k_down_dec      per output row, the token's local experts' down rows
-//                   (weights loaded BEFORE waiting for k_gateup_dec), the
-//                   weighted combine in selection order, the shared expert and
-//                   the residual.
+//   k_router_route  one 8-CTA cluster per token: router GEMV (dotF32 order),
+//                   logits gathered in CTA 0 through distributed shared
+//                   memory, then route (moe.zig:106) and the token's
+//                   activation quantization. Router weights are loaded BEFORE
+//                   waiting for the previous layer.
+//   k_gateup_dec    gate and up rows of every (token, expert) slot + SwiGLU.
+//   k_down_dec      per output row: the token's expert activations quantized
+//                   into shared memory, the local experts' down rows (weights
+//                   loaded BEFORE waiting for k_gateup_dec), the weighted
+//                   combine in selection order, the shared expert, the
+//                   residual.
 //
-// Completion counters (one per token / per slot) live in scratch, start at
-// zero and are reset by the CTA that consumes them. Scratch written by an
-// earlier kernel is read through L2 (ld.global.cg).
+// Scratch that an earlier kernel wrote before this one's producer ran is read
+// through L2 (ld.global.cg).
 #include <cuda_runtime.h>
 
 #include "decode.cuh"
@@ -48,70 +47,98 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 }
 
 // ---- router + route + activation quantization ---------------------------------------
+// One thread-block cluster of RR_CLUSTER CTAs per token: warp w of the cluster
+// computes router rows w, w + RR_WARPS_ALL, ... and writes each logit straight
+// into CTA 0's shared memory (distributed shared memory); after one cluster
+// barrier CTA 0 routes (warp 0) and quantizes the token's activation (the
+// other warps). No global atomics or fences sit on this path.
 
-constexpr int RR_WARPS = 4;
+constexpr int RR_CLUSTER = 8;
+constexpr int RR_WARPS = 16;
+constexpr int RR_WARPS_ALL = RR_CLUSTER * RR_WARPS;
 constexpr int RR_CHUNK = 64;  // router weights per lane held in registers (2048 columns)
+
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// store a float into CTA `rank`'s shared memory at the address of `local` in this CTA
+__device__ __forceinline__ void st_cluster_f32(float *local, unsigned rank, float v) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(local), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+// dotF32 (ggml.zig:198) of router row `wr` with x in shared memory; lane j is
+// accumulator lane j. `w` holds the row's first RR_CHUNK*32 weights.
+__device__ __forceinline__ float router_dot(const float (&w)[RR_CHUNK], const float *wr, const float *smx, int dim,
+                                            int lane) {
+    const int nfull = dim / 32;
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < RR_CHUNK; i++)
+        if (i < nfull) a = fadd(a, fmul(w[i], smx[i * 32 + lane]));
+    for (int i = RR_CHUNK; i < nfull; i++) a = fadd(a, fmul(__ldg(wr + i * 32 + lane), smx[i * 32 + lane]));
+    int i = nfull * 32;
+    for (; i + 8 <= dim; i += 8)
+        if (lane < 8) a = fadd(a, fmul(__ldg(wr + i + lane), smx[i + lane]));
+    const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
+    const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
+    const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
+    const float v = fadd(fadd(fadd(a, a8), a16), a24);
+    float r = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+    for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
+    for (; i < dim; i++) r = fadd(r, fmul(__ldg(wr + i), smx[i]));
+    return r;
+}
+
+__device__ __forceinline__ void load_row_chunk(float (&w)[RR_CHUNK], const float *wr, int dim, int lane) {
+    const int nfull = dim / 32;
+#pragma unroll
+    for (int i = 0; i < RR_CHUNK; i++)
+        if (i < nfull) w[i] = __ldg(wr + i * 32 + lane);
+}
 
 __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
     extern __shared__ float smx[];  // x[dim] | scores[ne] | choice[ne]
-    __shared__ int last;
     const int t = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int dim = A.dim, ne = A.n_expert;
-    const int row = blockIdx.x * RR_WARPS + warp;
-    const bool has_row = A.router && row < ne;
-    // 1. the first RR_CHUNK*32 weights of this warp's row, before the wait
+    const unsigned rank = A.router ? cluster_rank() : 0;
+    const int gw = (int)rank * RR_WARPS + warp;  // warp index within the cluster
+    float *scores = smx + dim, *choice = scores + ne;
+    // 1. the first row's leading weights, before the wait
     float w[RR_CHUNK];
-    const int nfull = dim / 32;
-    if (has_row) {
-        const float *wr = A.router + (size_t)row * dim;
-#pragma unroll
-        for (int i = 0; i < RR_CHUNK; i++)
-            if (i < nfull) w[i] = __ldg(wr + i * 32 + lane);
-    }
+    if (A.router && gw < ne) load_row_chunk(w, A.router + (size_t)gw * dim, dim, lane);
     pdl_wait();
     pdl_trigger();
     // 2. this token's activation into shared memory
     const float *xt = A.x + (size_t)t * dim;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = __ldcg(xt + i);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = xt[i];
     __syncthreads();
-    float *logits = A.logits + (size_t)t * ne;
     if (A.router) {
-        if (has_row) {  // dotF32 (ggml.zig:198): lane j is accumulator lane j
+        for (int row = gw; row < ne; row += RR_WARPS_ALL) {
             const float *wr = A.router + (size_t)row * dim;
-            float a = 0.0f;
-#pragma unroll
-            for (int i = 0; i < RR_CHUNK; i++)
-                if (i < nfull) a = fadd(a, fmul(w[i], smx[i * 32 + lane]));
-            for (int i = RR_CHUNK; i < nfull; i++) a = fadd(a, fmul(__ldg(wr + i * 32 + lane), smx[i * 32 + lane]));
-            int i = nfull * 32;
-            for (; i + 8 <= dim; i += 8)
-                if (lane < 8) a = fadd(a, fmul(__ldg(wr + i + lane), smx[i + lane]));
-            const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
-            const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
-            const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
-            const float v = fadd(fadd(fadd(a, a8), a16), a24);
-            float r = __shfl_sync(0xffffffffu, v, 0);
-#pragma unroll
-            for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
-            for (; i < dim; i++) r = fadd(r, fmul(__ldg(wr + i), smx[i]));
-            if (lane == 0) logits[row] = r;
+            if (row != gw) load_row_chunk(w, wr, dim, lane);
+            const float r = router_dot(w, wr, smx, dim, lane);
+            if (lane == 0) {
+                st_cluster_f32(choice + row, 0, r);
+                A.logits[(size_t)t * ne + row] = r;
+            }
         }
-        // 3. the last CTA of this token routes
-        __threadfence();
+        cluster_sync_all();  // every logit is in CTA 0's `choice`
+        if (rank != 0) return;
+    } else {
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = A.logits_in[(size_t)t * ne + e];
         __syncthreads();
-        if (threadIdx.x == 0) last = atomicAdd(A.cnt_tok + t, 1) == (int)gridDim.x - 1;
-        __syncthreads();
-        if (!last) return;
-        __threadfence();
     }
-    float *scores = smx + dim, *choice = scores + ne;
     if (warp == 0) {
-        const float *lg = A.router ? logits : A.logits_in + (size_t)t * ne;
-        // stage the logits in shared memory (through L2: other CTAs wrote them);
-        // each lane reads back only its own entries before overwriting them
-        for (int e = lane; e < ne; e += 32) choice[e] = __ldcg(lg + e);
-        __syncwarp();
+        // route_warp reads each logit before overwriting the same entry with its choice value
         route_warp(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice,
                    A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
         if (A.ids_out)
@@ -135,7 +162,6 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
             }
         }
     }
-    if (A.router && threadIdx.x == 0) A.cnt_tok[t] = 0;
 }
 
 // ---- slot description -------------------------------------------------------------
@@ -194,7 +220,6 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
     using E = CEng<TY, 2 * GU_NR, NB>;
     static_assert(E::OK, "unit mapping");
     extern __shared__ __align__(16) uint8_t sm[];
-    __shared__ int last;
     pdl_wait();
     pdl_trigger();
     const int slot = blockIdx.y;
@@ -233,33 +258,6 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
             }
         }
     }
-    // the last CTA of this slot quantizes its activation for the down projection
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(A.cnt_slot + slot, 1) == nctas - 1;
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    float *xa = reinterpret_cast<float *>(sm);  // reuse: ffn floats
-    for (int i = threadIdx.x; i < si.ffn; i += blockDim.x) xa[i] = __ldcg(act + i);
-    __syncthreads();
-    const int dty = si.shared ? A.sdn.type : A.dn.type;
-    int8_t *q = A.aq + (size_t)slot * A.act_stride;
-    float *d = A.ad + (size_t)slot * (A.act_stride / 32);
-    int32_t *s = A.as + (size_t)slot * (A.act_stride / 16);
-    if (act256(dty)) {
-        for (int b = warp; b < si.ffn / 256; b += GU_WARPS)
-            quant_lane8(xa + b * 256 + lane * 8, true, 32, q + b * 256 + lane * 8, d + b, s + b * 16 + lane / 2, nullptr,
-                        lane);
-    } else {
-        const int nb32 = si.ffn / 32, ng = (nb32 + 7) / 8;
-        for (int g = warp; g < ng; g += GU_WARPS) {
-            const int b = g * 8 + lane / 4;
-            const int off = b * 32 + (lane & 3) * 8;
-            quant_lane8(xa + off, b < nb32, 4, q + off, d + b, nullptr, s + b, lane);
-        }
-    }
-    if (threadIdx.x == 0) A.cnt_slot[slot] = 0;
 }
 
 // ---- down + combine ------------------------------------------------------------------
@@ -346,17 +344,28 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     }
     pdl_wait();
     pdl_trigger();
-    const size_t slot0 = (size_t)t * nk;
-    stage16(aq, A.aq + slot0 * stride, nk * stride);
-    for (int i = threadIdx.x; i < nk * (stride / 32); i += blockDim.x) ad[i] = __ldcg(A.ad + slot0 * (stride / 32) + i);
-    for (int i = threadIdx.x; i < nk * (stride / 16); i += blockDim.x) as[i] = __ldcg(A.as + slot0 * (stride / 16) + i);
-    if (NBSH > 0) {
-        const size_t ss = (size_t)A.T * nk + t;
-        stage16(aq + (size_t)nk * stride, A.aq + ss * stride, stride);
-        for (int i = threadIdx.x; i < stride / 32; i += blockDim.x)
-            ad[nk * (stride / 32) + i] = __ldcg(A.ad + ss * (stride / 32) + i);
-        for (int i = threadIdx.x; i < stride / 16; i += blockDim.x)
-            as[nk * (stride / 16) + i] = __ldcg(A.as + ss * (stride / 16) + i);
+    // quantize the token's expert activations into shared memory, in the down
+    // type's format (quantizeX256 / quantizeX): routed slot k at k*stride, the
+    // shared expert's at nk*stride
+    for (int k = warp; k < nk1; k += DN_WARPS) {
+        const size_t slot = k < nk ? (size_t)t * nk + k : (size_t)A.T * nk + t;
+        const int f = k < nk ? A.ffn : A.shexp_ffn;
+        const float *xa = A.act + slot * stride;
+        int8_t *q = aq + (size_t)k * stride;
+        float *dd = ad + (size_t)k * (stride / 32);
+        int32_t *ss = as + (size_t)k * (stride / 16);
+        if (act256(TY)) {
+            for (int b = 0; b < f / 256; b++)
+                quant_lane8(xa + b * 256 + lane * 8, true, 32, q + b * 256 + lane * 8, dd + b, ss + b * 16 + lane / 2,
+                            nullptr, lane);
+        } else {
+            const int nb32 = f / 32, ng = (nb32 + 7) / 8;
+            for (int g = 0; g < ng; g++) {
+                const int b = g * 8 + lane / 4;
+                const int off = b * 32 + (lane & 3) * 8;
+                quant_lane8(xa + off, b < nb32, 4, q + off, dd + b, nullptr, ss + b, lane);
+            }
+        }
     }
     __syncthreads();
     float acc = 0.0f;
@@ -453,9 +462,23 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
     cudaError_t e;
     // 1. router + route + activation quantization
     {
-        const unsigned gx = A.router ? cdivu(A.n_expert, RR_WARPS) : 1;
         const size_t smem = (size_t)(A.dim + 2 * A.n_expert) * 4;
-        e = launch_pdl(k_router_route, dim3(gx, A.T), dim3(RR_WARPS * 32), smem, st, A);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(A.router ? RR_CLUSTER : 1, A.T);
+        cfg.blockDim = dim3(RR_WARPS * 32);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = A.router ? RR_CLUSTER : 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        count_launch();
+        e = cudaLaunchKernelEx(&cfg, k_router_route, A);
         if (e != cudaSuccess) return e;
     }
     // 2. gate/up
