@@ -198,6 +198,8 @@ def run_gpu(args):
     B.init(local)
     T = args.tokens
     layers = build_model(T)
+    for l in range(LAYERS - 1):
+        layers[l].next_router = layers[l + 1].router  # prefetch hint
     D.reserve(T, DIM, FFN, NE, NK)
     descs = [L.desc() for L in layers]
     stream = torch.cuda.Stream()
@@ -235,6 +237,7 @@ def run_gpu(args):
             e1.record(stream)
             torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    phases = trace_phases(D, step, stream, torch) if args.trace else None
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -274,11 +277,46 @@ def run_gpu(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": ck.summary(),
     }
+    if phases:
+        line["phase_us"] = phases
     if e2e:
         line["e2e"] = e2e
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def trace_phases(D, step, stream, torch):
+    """One extra replay of a separately captured, traced graph: per decode
+    kernel the mean span (first CTA start to last CTA end) and the mean gap
+    between consecutive kernels, in microseconds (not part of the timed
+    region)."""
+    n = 8 * LAYERS
+    D.trace_enable(n)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step(torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            D.trace_reset()
+            g.replay()
+            torch.cuda.synchronize()
+    tr = D.trace_read(n).astype(np.float64).reshape(LAYERS, 8, 2)
+    D.trace_enable(0)
+    if tr.shape[0] < LAYERS:
+        return None
+    # per layer, relative to the previous layer's down end (layer 0 skipped)
+    prev_end = tr[:-1, 2, 1]
+    L = tr[1:]
+    rel = lambda v: round(float(np.mean(v - prev_end)) / 1e3, 2)  # noqa: E731
+    return {
+        "router_first_start": rel(L[:, 0, 0]), "router_x_staged": rel(L[:, 3, 0]),
+        "router_cluster_synced": rel(L[:, 3, 1]), "router_routed": rel(L[:, 6, 0]),
+        "router_quantized": rel(L[:, 6, 1]), "router_end": rel(L[:, 0, 1]),
+        "gateup_first_start": rel(L[:, 1, 0]), "gateup_post_wait": rel(L[:, 4, 0]), "gateup_end": rel(L[:, 1, 1]),
+        "down_first_start": rel(L[:, 2, 0]), "down_post_wait": rel(L[:, 5, 0]), "down_end": rel(L[:, 2, 1]),
+        "unit": "us after the previous layer's down end",
+    }
 
 
 def run_e2e(args, B):
@@ -334,6 +372,7 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="add per-kernel phase times (one extra traced replay)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers in the stack (default 48; smaller only for profiling captures)")
     args = ap.parse_args()

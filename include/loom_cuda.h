@@ -160,6 +160,9 @@ typedef struct {
     loom_tensor shexp_gate, shexp_up, shexp_down;
     size_t shexp_ffn;
     size_t expert0, n_local;
+    /* optional hint: the next layer's router (f32 [n_expert][dim]); its weights
+     * are prefetched into L2 while this layer's experts stream */
+    loom_tensor next_router;
 } loom_moe_desc;
 
 /* d_x: device f32 [T][dim]; d_out: device f32 [T][dim] (d_out = d_residual +
@@ -180,6 +183,20 @@ int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float
  * of the fused decode kernels (same numerics; used to cross-check the two).
  * Returns the previous setting. */
 int loom_cuda_force_generic(int on);
+/* Phase tracing of the fused decode kernels (the counterpart of the
+ * reference's LOOM_PROFILE phase timers, deepseek.zig:705-850): with room for
+ * n_kernels traced launches, each decode kernel records its first CTA start
+ * and last CTA end (GPU globaltimer, ns). Kernels are assigned trace entries
+ * in launch order, eight per layer: router, gate/up, down (first CTA start,
+ * last CTA end), the router's post-wait span up to its cluster barrier, the
+ * first post-wait instants of gate/up and down, (route done, activation
+ * quantized) in the router, and one spare. n_kernels = 0
+ * turns tracing off. */
+int loom_cuda_trace_enable(size_t n_kernels);
+/* Clear the recorded times (keeps the entry assignment of captured graphs). */
+int loom_cuda_trace_reset(void);
+/* Copy (start, end) pairs of the first n entries; returns entries copied. */
+size_t loom_cuda_trace_read(uint64_t *out, size_t n_kernels);
 /* Synchronize the backend's stream. */
 int loom_cuda_sync(void);
 /* The backend's stream (cudaStream_t). */

@@ -40,7 +40,8 @@ class MoeDesc(C.Structure):  # loom_moe_desc
                 ("router", C.c_uint64), ("router_bias", C.c_uint64),
                 ("gate", C.c_uint64), ("up", C.c_uint64), ("down", C.c_uint64),
                 ("shexp_gate", C.c_uint64), ("shexp_up", C.c_uint64), ("shexp_down", C.c_uint64),
-                ("shexp_ffn", C.c_size_t), ("expert0", C.c_size_t), ("n_local", C.c_size_t)]
+                ("shexp_ffn", C.c_size_t), ("expert0", C.c_size_t), ("n_local", C.c_size_t),
+                ("next_router", C.c_uint64)]
 
 
 def header_symbols() -> list[str]:
@@ -89,6 +90,9 @@ def lib() -> C.CDLL:
         "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
         "loom_cuda_sync": (i, []),
         "loom_cuda_force_generic": (i, [i]),
+        "loom_cuda_trace_enable": (i, [sz]),
+        "loom_cuda_trace_reset": (i, []),
+        "loom_cuda_trace_read": (sz, [vp, sz]),
         "loom_cuda_stream": (vp, []),
     }
     for name, (res, args) in sig.items():

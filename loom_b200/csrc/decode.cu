@@ -26,6 +26,32 @@ namespace loom {
 
 static inline unsigned cdivu(uint64_t a, uint64_t b) { return (unsigned)((a + b - 1) / b); }
 
+// Phase tracing (off unless the caller passes a trace buffer): the first CTA
+// start and the last CTA end of each kernel, in globaltimer nanoseconds.
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void trace_begin(const DecodeArgs &A, int k) {
+    if (A.trace && threadIdx.x == 0) atomicMin(A.trace + 2 * (A.trace_slot + k), gtimer());
+}
+__device__ __forceinline__ void trace_end(const DecodeArgs &A, int k) {
+    if (A.trace && threadIdx.x == 0) atomicMax(A.trace + 2 * (A.trace_slot + k) + 1, gtimer());
+}
+
+// Bulk prefetch of [p, p+bytes) into L2 (no data returned to the SM). p is
+// rounded down and the end up to 16 bytes.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
+    uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes + 15) & ~uintptr_t(15);
+    while (a < e) {
+        const uint32_t n = (uint32_t)((e - a) < 32768 ? (e - a) : 32768);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+        a += n;
+    }
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -105,13 +131,14 @@ __device__ __forceinline__ void load_row_chunk(float (&w)[RR_CHUNK], const float
 }
 
 __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
-    extern __shared__ float smx[];  // x[dim] | scores[ne] | choice[ne]
+    extern __shared__ float smx[];  // x[dim] | scores[ne] | choice[ne] | ids[64] | gates[64]
     const int t = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int dim = A.dim, ne = A.n_expert;
     const unsigned rank = A.router ? cluster_rank() : 0;
     const int gw = (int)rank * RR_WARPS + warp;  // warp index within the cluster
     float *scores = smx + dim, *choice = scores + ne;
+    trace_begin(A, 0);
     // 1. the first row's leading weights, before the wait
     float w[RR_CHUNK];
     if (A.router && gw < ne) load_row_chunk(w, A.router + (size_t)gw * dim, dim, lane);
@@ -119,6 +146,7 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
     pdl_trigger();
     // 2. this token's activation into shared memory
     const float *xt = A.x + (size_t)t * dim;
+    trace_begin(A, 3);
     for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = xt[i];
     __syncthreads();
     if (A.router) {
@@ -132,18 +160,30 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
             }
         }
         cluster_sync_all();  // every logit is in CTA 0's `choice`
+        trace_end(A, 3);
         if (rank != 0) return;
     } else {
         for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = A.logits_in[(size_t)t * ne + e];
         __syncthreads();
     }
+    __shared__ int s_ranked;
+    int *sid = reinterpret_cast<int *>(choice + ne);
+    float *sg = choice + ne + 64;
     if (warp == 0) {
-        // route_warp reads each logit before overwriting the same entry with its choice value
-        route_warp(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice,
-                   A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
+        // route_scores reads each logit before overwriting the same entry with its choice value
+        const bool r = route_scores(choice, A.bias, ne, A.gating, scores, choice, lane);
+        if (lane == 0) s_ranked = r;
+    }
+    __syncthreads();
+    const bool ranked = s_ranked;
+    if (ranked) route_rank(scores, choice, ne, A.n_used, sid, sg, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (warp == 0) {
+        route_finish(ranked, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
+                     A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
         if (A.ids_out)
-            for (int k = lane; k < A.n_used; k += 32)
-                A.ids_out[(size_t)t * A.n_used + k] = A.ids[(size_t)t * A.n_used + k];
+            for (int k = lane; k < A.n_used; k += 32) A.ids_out[(size_t)t * A.n_used + k] = sid[k];
+        if (A.trace && lane == 0) atomicMin(A.trace + 2 * (A.trace_slot + 6), gtimer());
     } else {
         // quantize x in the format(s) the expert types read
         const int nw = RR_WARPS - 1, wi = warp - 1;
@@ -161,7 +201,10 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
                             nullptr, A.x32.s + (size_t)t * (dim / 32) + b, lane);
             }
         }
+        if (A.trace && lane == 0) atomicMax(A.trace + 2 * (A.trace_slot + 6) + 1, gtimer());
     }
+    __syncthreads();
+    trace_end(A, 0);
 }
 
 // ---- slot description -------------------------------------------------------------
@@ -201,9 +244,11 @@ __device__ __forceinline__ void stage16(void *dst, const void *src, int n) {
 // ---- gate/up + SwiGLU ---------------------------------------------------------------
 
 constexpr int GU_WARPS = 4;
-constexpr int GU_NR = 2;  // rows per warp: streams = gate rows + up rows
+// rows per warp (streams = NR gate rows + NR up rows): 3 for rows of up to 8
+// super-blocks (one wave of CTAs at the Qwen shape), 1 for wider rows
+template <int NB> constexpr int gu_nr() { return NB <= 8 ? 3 : 1; }
 
-struct GateUpStreams {
+template <int GU_NR> struct GateUpStreams {
     WDev wg, wu;
     uint64_t gb_g, gb_u;  // first block of the warp's first row
     int nb;
@@ -217,11 +262,14 @@ struct GateUpStreams {
 
 template <int TY, int NB>
 __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
+    constexpr int GU_NR = gu_nr<NB>();
     using E = CEng<TY, 2 * GU_NR, NB>;
     static_assert(E::OK, "unit mapping");
     extern __shared__ __align__(16) uint8_t sm[];
+    trace_begin(A, 1);
     pdl_wait();
     pdl_trigger();
+    trace_begin(A, 4);
     const int slot = blockIdx.y;
     const SlotInfo si = slot_info(A, slot);
     const int rows_cta = GU_WARPS * GU_NR;
@@ -241,9 +289,25 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
     const int r0 = blockIdx.x * rows_cta + warp * GU_NR;
     const int rmax = si.ffn - GU_NR;
     const int rl = r0 <= rmax ? r0 : rmax;  // clamp the last (partial) group; its extra rows are not stored
-    GateUpStreams st{wg, wu, plane + (uint64_t)rl * NB, plane + (uint64_t)rl * NB, NB, XV{xq, xd, xs}};
+    GateUpStreams<GU_NR> st{wg, wu, plane + (uint64_t)rl * NB, plane + (uint64_t)rl * NB, NB, XV{xq, xd, xs}};
     typename E::Frags fr;
     E::load(st, fr, lane);  // weight loads are in flight while the activation lands in shared memory
+    if (threadIdx.x == 0) {
+        // warm L2 with this CTA's share of the slot's down plane for k_down_dec
+        // (and, from the first CTA, the next layer's router weights)
+        const WDev wd = si.shared ? A.sdn : A.dn;
+        const int f = si.shared ? A.shexp_ffn : A.ffn;
+        const uint64_t pb = (uint64_t)A.dim * (f / block_elems(wd.type));  // blocks per down plane
+        const uint64_t e0 = si.shared ? 0 : (uint64_t)si.expert_local * pb;
+        const uint64_t qb = pb * layout_qbytes(wd.type), chunk = (qb / nctas + 15) & ~uint64_t(15);
+        const uint64_t off = chunk * blockIdx.x;
+        if (off < qb) prefetch_l2(wd.q + e0 * layout_qbytes(wd.type) + off, off + chunk <= qb ? chunk : qb - off);
+        if (blockIdx.x == 0) {
+            if (wd.sc) prefetch_l2(wd.sc + e0 * 16, pb * 16);
+            if (wd.d) prefetch_l2(wd.d + e0, pb * 2);
+            if (A.next_router && blockIdx.y == 0) prefetch_l2(A.next_router, A.next_router_bytes);
+        }
+    }
     __syncthreads();
     float acc[2 * GU_NR];
     E::finish(st, fr, acc, lane);
@@ -258,6 +322,8 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
             }
         }
     }
+    __syncthreads();
+    trace_end(A, 1);
 }
 
 // ---- down + combine ------------------------------------------------------------------
@@ -300,6 +366,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     __shared__ int s_shidx;
     __shared__ uint64_t s_gb[DN_WARPS][SC];
     const int t = blockIdx.y;
+    trace_begin(A, 2);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = blockIdx.x * DN_WARPS + warp;
     const int rr = r < A.dim ? r : A.dim - 1;
@@ -344,26 +411,45 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     }
     pdl_wait();
     pdl_trigger();
+    trace_begin(A, 5);
     // quantize the token's expert activations into shared memory, in the down
     // type's format (quantizeX256 / quantizeX): routed slot k at k*stride, the
     // shared expert's at nk*stride
-    for (int k = warp; k < nk1; k += DN_WARPS) {
-        const size_t slot = k < nk ? (size_t)t * nk + k : (size_t)A.T * nk + t;
-        const int f = k < nk ? A.ffn : A.shexp_ffn;
-        const float *xa = A.act + slot * stride;
-        int8_t *q = aq + (size_t)k * stride;
-        float *dd = ad + (size_t)k * (stride / 32);
-        int32_t *ss = as + (size_t)k * (stride / 16);
-        if (act256(TY)) {
-            for (int b = 0; b < f / 256; b++)
-                quant_lane8(xa + b * 256 + lane * 8, true, 32, q + b * 256 + lane * 8, dd + b, ss + b * 16 + lane / 2,
-                            nullptr, lane);
-        } else {
-            const int nb32 = f / 32, ng = (nb32 + 7) / 8;
-            for (int g = 0; g < ng; g++) {
-                const int b = g * 8 + lane / 4;
-                const int off = b * 32 + (lane & 3) * 8;
-                quant_lane8(xa + off, b < nb32, 4, q + off, dd + b, nullptr, ss + b, lane);
+    {
+        // every (slot, block) pair of this token; each warp loads QB blocks' values
+        // before quantizing any, so the L2 reads overlap
+        constexpr int QB = 4;
+        constexpr int BEQ = act256(TY) ? 256 : 32;  // quantization block
+        constexpr int LPQ = BEQ / 8;                // lanes per quantization block
+        constexpr int BPW = 32 / LPQ;               // blocks per warp step
+        const int nbr = A.ffn / BEQ, nbs = NBSH > 0 ? A.shexp_ffn / BEQ : 0;
+        const int nunits = nk * nbr + nbs;  // warp units of BPW blocks
+        const int nsteps = (nunits + BPW - 1) / BPW;
+        for (int s0 = warp; s0 < nsteps; s0 += DN_WARPS * QB) {
+            float v[QB][8];
+            int kk[QB], bb[QB];
+            bool live[QB];
+#pragma unroll
+            for (int i = 0; i < QB; i++) {
+                const int st_ = s0 + i * DN_WARPS;
+                const int u = st_ * BPW + lane / LPQ;
+                live[i] = st_ < nsteps && u < nunits;
+                kk[i] = u < nk * nbr ? u / nbr : nk;
+                bb[i] = u < nk * nbr ? u % nbr : u - nk * nbr;
+                const size_t slot = kk[i] < nk ? (size_t)t * nk + kk[i] : (size_t)A.T * nk + t;
+                const float *src = A.act + slot * stride + bb[i] * BEQ + (lane % LPQ) * 8;
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[i][e] = live[i] ? src[e] : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < QB; i++) {
+                if (s0 + i * DN_WARPS >= nsteps) break;  // warp-uniform
+                const int k = kk[i], b = bb[i];
+                int8_t *q = aq + (size_t)k * stride + b * BEQ + (lane % LPQ) * 8;
+                float *dd = ad + (size_t)k * (stride / 32) + b;
+                int32_t *ss = as + (size_t)k * (stride / 16);
+                if (BEQ == 256) quant_vals8(v[i], live[i], 32, q, dd, ss + b * 16 + lane / 2, nullptr, lane);
+                else quant_vals8(v[i], live[i], 4, q, dd, nullptr, ss + b, lane);
             }
         }
     }
@@ -400,6 +486,8 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
         const size_t o = (size_t)t * A.dim + r;
         A.out[o] = A.residual ? fadd(__ldcg(A.residual + o), acc) : acc;
     }
+    __syncthreads();
+    trace_end(A, 2);
 }
 
 // ---- dispatch ---------------------------------------------------------------------
@@ -454,7 +542,7 @@ bool decode_supported(const DecodeArgs &A) {
     }
     if (!down_fn(dty, A.ffn / block_elems(dty), shared_nb(A))) return false;
     const size_t max_ffn = A.has_shared && A.shexp_ffn > A.ffn ? A.shexp_ffn : A.ffn;
-    return down_smem(A) <= 48 * 1024 && (size_t)(A.dim + 2 * A.n_expert) * 4 <= 48 * 1024 &&
+    return down_smem(A) <= 48 * 1024 && (size_t)(A.dim + 2 * A.n_expert + 128) * 4 <= 48 * 1024 &&
            max_ffn * 4 <= 48 * 1024;
 }
 
@@ -462,7 +550,7 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
     cudaError_t e;
     // 1. router + route + activation quantization
     {
-        const size_t smem = (size_t)(A.dim + 2 * A.n_expert) * 4;
+        const size_t smem = (size_t)(A.dim + 2 * A.n_expert + 128) * 4;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(A.router ? RR_CLUSTER : 1, A.T);
         cfg.blockDim = dim3(RR_WARPS * 32);
@@ -485,7 +573,7 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
     {
         const int n_slots = A.T * A.n_used + (A.has_shared ? A.T : 0);
         const int max_ffn = A.has_shared && A.shexp_ffn > A.ffn ? A.shexp_ffn : A.ffn;
-        const dim3 grid(cdivu(max_ffn, GU_WARPS * GU_NR), n_slots);
+        const dim3 grid(cdivu(max_ffn, GU_WARPS * (A.dim / 256 <= 8 ? 3 : 1)), n_slots);
         const size_t smem_x = (size_t)A.dim + A.dim / 256 * 4 + A.dim / 16 * 4;
         const size_t smem_q = (size_t)max_ffn * 4;
         e = launch_pdl(gateup_fn(A.g.type, A.dim / 256), grid, dim3(GU_WARPS * 32), smem_x > smem_q ? smem_x : smem_q,

@@ -40,6 +40,10 @@ struct DecodeArgs {
     float *ad;               // [n_slots][act_stride/32]
     int32_t *as;             // [n_slots][act_stride/16]
     int act_stride;          // multiple of 256
+    const uint8_t *next_router;   // optional: the next layer's router weights, prefetched into L2
+    size_t next_router_bytes;
+    unsigned long long *trace;  // optional [2*k] (first start, last end) globaltimer ns per kernel, or null
+    int trace_slot;             // this layer's first kernel index in `trace`
 };
 
 // True when the fused decode kernels cover this layer's types and shapes.

@@ -9,15 +9,12 @@ namespace loom {
 // lane holds 8 consecutive values of a block that spans `group_lanes` lanes
 // (32 for a 256-wide block, 4 for a 32-wide one). d = amax/127 (IEEE divide),
 // q = round-half-away(v * (1/d)) saturated to +-127, non-finite -> 0.
-__device__ __forceinline__ void quant_lane8(const float *src, bool live, int group_lanes, int8_t *qdst, float *ddst,
-                                            int32_t *sdst_pairs, int32_t *sdst_group, int lane) {
-    float v[8];
+__device__ __forceinline__ void quant_vals8(const float (&v)[8], bool live, int group_lanes, int8_t *qdst,
+                                            float *ddst, int32_t *sdst_pairs, int32_t *sdst_group, int lane) {
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        v[i] = live ? src[i] : 0.0f;
-        if (isfinite(v[i])) amax = fmaxf(amax, fabsf(v[i]));
-    }
+    for (int i = 0; i < 8; i++)
+        if (live && isfinite(v[i])) amax = fmaxf(amax, fabsf(v[i]));
     for (int o = 1; o < group_lanes; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float d = fdiv(amax, 127.0f);
     const float inv = (d != 0.0f && isfinite(d)) ? fdiv(1.0f, d) : 0.0f;
@@ -41,13 +38,29 @@ __device__ __forceinline__ void quant_lane8(const float *src, bool live, int gro
     if (live && (lane % group_lanes) == 0) *ddst = isfinite(d) ? d : 0.0f;
 }
 
+__device__ __forceinline__ void quant_lane8(const float *src, bool live, int group_lanes, int8_t *qdst, float *ddst,
+                                            int32_t *sdst_pairs, int32_t *sdst_group, int lane) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = live ? src[i] : 0.0f;
+    quant_vals8(v, live, group_lanes, qdst, ddst, sdst_pairs, sdst_group, lane);
+}
 
-// moe.zig:106-158 route, one warp per token. Scores and the biased choice live
-// in shared memory; top-k is k rounds of a warp arg-max that keeps the lowest
-// index on ties and never selects a value that is not > -inf (the serial
-// scan's strict '>').
-__device__ __forceinline__ void route_warp(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
-                           float weights_scale, float *scores, float *choice, int *ids, float *gates, int lane) {
+
+// moe.zig:106-158 route. Scores and the biased choice live in shared memory.
+// The route in three phases so a whole CTA can share the ranking:
+//   route_scores  (one warp)  scores = softmax / sigmoid / raw logits, choice =
+//                 scores + bias; returns whether every choice is > -inf
+//   route_rank    (any threads) the rank of e is the number of experts the
+//                 serial scan takes before it (greater value, or equal value
+//                 and lower index); with every value > -inf this is exactly the
+//                 serial first-max order, so rank < k selects slot `rank`
+//   route_finish  (one warp)  the serial k-round scan when some value is NaN or
+//                 -inf, then softmax_topk / renormalisation / scale, and the
+//                 copy to ids_out/gates_out
+// scores/choice: ne floats of shared memory; ids/gates: nk words of shared memory.
+__device__ __forceinline__ bool route_scores(const float *logits, const float *bias, int ne, int gating,
+                                             float *scores, float *choice, int lane) {
     if (gating == 2) {
         for (int e = lane; e < ne; e += 32) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
     } else if (gating == 1) {
@@ -67,57 +80,102 @@ __device__ __forceinline__ void route_warp(const float *logits, const float *bia
     } else {
         for (int e = lane; e < ne; e += 32) scores[e] = logits[e];
     }
-    for (int e = lane; e < ne; e += 32) choice[e] = bias ? fadd(scores[e], bias[e]) : scores[e];
-    __syncwarp();
-    for (int k = 0; k < nk; k++) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int e = lane; e < ne; e += 32) {
-            const float c = choice[e];
-            if (c > bv) {  // strict: first maximum in this lane's (ascending) run
-                bv = c;
-                bi = e;
-            }
+    bool all_finite = true;
+    for (int e = lane; e < ne; e += 32) {
+        const float c = bias ? fadd(scores[e], bias[e]) : scores[e];
+        choice[e] = c;
+        all_finite &= c > -INFINITY;
+    }
+    return __all_sync(0xffffffffu, all_finite);
+}
+
+__device__ __forceinline__ void route_rank(const float *scores, const float *choice, int ne, int nk, int *ids,
+                                           float *gates, int tid, int nthreads) {
+    for (int e = tid; e < ne; e += nthreads) {
+        const float c = choice[e];
+        int rank = 0;
+        for (int j = 0; j < ne; j++) {
+            const float cj = choice[j];
+            rank += (cj > c) | ((cj == c) & (j < e));
         }
+        if (rank < nk) {
+            ids[rank] = e;
+            gates[rank] = scores[e];
+        }
+    }
+}
+
+__device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int gating, int weights_norm,
+                                             float weights_scale, const float *scores, float *choice, int *ids,
+                                             float *gates, int *ids_out, float *gates_out, int lane) {
+    if (!ranked) {
+        for (int k = 0; k < nk; k++) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int e = lane; e < ne; e += 32) {
+                const float c = choice[e];
+                if (c > bv) {  // strict: first maximum in this lane's (ascending) run
+                    bv = c;
+                    bi = e;
+                }
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
             }
+            if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
+            if (lane == 0) {
+                ids[k] = bi;
+                gates[k] = scores[bi];
+                choice[bi] = -INFINITY;  // used
+            }
+            __syncwarp();
         }
-        if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
-        if (lane == 0) {
-            ids[k] = bi;
-            gates[k] = scores[bi];
-            choice[bi] = -INFINITY;  // used
-        }
-        __syncwarp();
     }
-    if (lane == 0) {
-        if (gating == 3) {  // softmax over the selected k (tensor.zig:18 softmax)
-            float m = -INFINITY;
-            for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
-            float sum = 0.0f;
-            for (int k = 0; k < nk; k++) {
-                gates[k] = expf(fsub(gates[k], m));
-                sum = fadd(sum, gates[k]);
-            }
-            const float inv = fdiv(1.0f, sum);
-            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], inv);
+    if (gating == 3 && lane == 0) {  // softmax over the selected k (tensor.zig:18 softmax)
+        float m = -INFINITY;
+        for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
+        float sum = 0.0f;
+        for (int k = 0; k < nk; k++) {
+            gates[k] = expf(fsub(gates[k], m));
+            sum = fadd(sum, gates[k]);
         }
-        if (weights_norm) {
-            float sum = 0.0f;
-            for (int k = 0; k < nk; k++) sum = fadd(sum, gates[k]);
-            const float denom = fmaxf(sum, 6.103515625e-5f);
-            for (int k = 0; k < nk; k++) gates[k] = fdiv(gates[k], denom);
-        }
-        if (weights_scale != 1.0f)
-            for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], weights_scale);
+        const float inv = fdiv(1.0f, sum);
+        for (int k = 0; k < nk; k++) gates[k] = fmul(gates[k], inv);
     }
     __syncwarp();
+    float denom = 1.0f;
+    if (weights_norm) {  // the sum runs in selection order, as the serial loop does
+        float sum = 0.0f;
+        for (int k = 0; k < nk; k++) sum = fadd(sum, gates[k]);
+        denom = fmaxf(sum, 6.103515625e-5f);
+    }
+    for (int k = lane; k < nk; k += 32) {
+        float g = gates[k];
+        if (weights_norm) g = fdiv(g, denom);
+        if (weights_scale != 1.0f) g = fmul(g, weights_scale);
+        ids_out[k] = ids[k];
+        gates_out[k] = g;
+        gates[k] = g;
+    }
+    __syncwarp();
+}
+
+// moe.zig:106-158 route by one warp.
+__device__ __forceinline__ void route_warp(const float *logits, const float *bias, int ne, int nk, int gating,
+                                           int weights_norm, float weights_scale, float *scores, float *choice,
+                                           int *ids_out, float *gates_out, int *ids, float *gates, int lane) {
+    const bool ranked = route_scores(logits, bias, ne, gating, scores, choice, lane) && ne <= 1024;
+    __syncwarp();
+    if (ranked) route_rank(scores, choice, ne, nk, ids, gates, lane, 32);
+    __syncwarp();
+    route_finish(ranked, ne, nk, gating, weights_norm, weights_scale, scores, choice, ids, gates, ids_out, gates_out,
+                 lane);
 }
 
 }  // namespace loom

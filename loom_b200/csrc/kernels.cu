@@ -345,13 +345,14 @@ __global__ void k_route(const float *logits, const float *bias, int ne, int nk, 
     extern __shared__ float sm[];
     const int t = blockIdx.x;
     route_warp(logits + (size_t)t * ne, bias, ne, nk, gating, weights_norm, weights_scale, sm, sm + ne,
-               ids + (size_t)t * nk, gates + (size_t)t * nk, threadIdx.x);
+               ids + (size_t)t * nk, gates + (size_t)t * nk, reinterpret_cast<int *>(sm + 2 * ne), sm + 2 * ne + 64,
+               threadIdx.x);
 }
 
 void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating, int weights_norm,
                   float weights_scale, int *ids, float *gates, cudaStream_t st) {
     if (T == 0) return;
-    k_route<<<T, 32, 2 * n_expert * sizeof(float), st>>>(logits, bias, n_expert, n_used, gating, weights_norm,
+    k_route<<<T, 32, (2 * n_expert + 128) * sizeof(float), st>>>(logits, bias, n_expert, n_used, gating, weights_norm,
                                                          weights_scale, ids, gates);
     count_launch();
 }

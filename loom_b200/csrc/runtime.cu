@@ -305,7 +305,12 @@ bool any_type(const RoutedLayerDev &L, bool k256) {
 // batches use the slot kernels.
 constexpr size_t DECODE_MAX_T = 16;
 
-bool g_force_generic = false;  // test hook: route every layer through the slot kernels
+bool g_force_generic = false;
+const uint8_t *g_next_router = nullptr;  // L2-prefetch hint for the layer being launched
+size_t g_next_router_bytes = 0;
+// phase trace: [2*n] (first start, last end) per traced kernel, see loom_cuda_trace_*
+unsigned long long *g_trace = nullptr;
+size_t g_trace_cap = 0, g_trace_next = 0;  // test hook: route every layer through the slot kernels
 
 DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, const float *d_x,
                        const float *d_logits_in, const float *d_bias, float *d_out, const float *d_residual,
@@ -350,6 +355,13 @@ DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, c
     A.ad = S.ad.as<float>();
     A.as = S.as.as<int32_t>();
     A.act_stride = (int)act_stride;
+    A.next_router = g_next_router;
+    A.next_router_bytes = g_next_router_bytes;
+    if (g_trace && g_trace_next + 8 <= g_trace_cap) {
+        A.trace = g_trace;
+        A.trace_slot = (int)g_trace_next;
+        g_trace_next += 8;
+    }
     return A;
 }
 
@@ -504,6 +516,38 @@ size_t loom_cuda_last_error(char *buf, size_t len) {
 }
 
 void *loom_cuda_stream(void) { return g_stream; }
+
+int loom_cuda_trace_enable(size_t n_kernels) {
+    if (int rc = need_init()) return rc;
+    CK(cudaStreamSynchronize(g_stream));
+    if (g_trace) cudaFree(g_trace);
+    g_trace = nullptr;
+    g_trace_cap = g_trace_next = 0;
+    if (n_kernels == 0) return LOOM_CUDA_OK;
+    CK(cudaMalloc(&g_trace, n_kernels * 16));
+    g_trace_cap = n_kernels;
+    return loom_cuda_trace_reset();
+}
+
+int loom_cuda_trace_reset(void) {
+    if (int rc = need_init()) return rc;
+    if (!g_trace) return decline("tracing is off");
+    std::vector<unsigned long long> init(2 * g_trace_cap);
+    for (size_t i = 0; i < g_trace_cap; i++) {
+        init[2 * i] = ~0ull;
+        init[2 * i + 1] = 0;
+    }
+    CK(cudaMemcpy(g_trace, init.data(), init.size() * 8, cudaMemcpyHostToDevice));
+    return LOOM_CUDA_OK;
+}
+
+size_t loom_cuda_trace_read(uint64_t *out, size_t n_kernels) {
+    if (!g_inited || !g_trace) return 0;
+    const size_t n = std::min(n_kernels, g_trace_next);
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
+    if (cudaMemcpy(out, g_trace, n * 16, cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+    return n;
+}
 
 int loom_cuda_force_generic(int on) {
     const int prev = g_force_generic;
@@ -839,7 +883,18 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
         if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
         router = reinterpret_cast<const float *>(r->base);
     }
-    if (int rc = moe_routed_dev(L, T, router, d_x, d_logits, bias, d_out, d_residual, d_ids, st)) return rc;
+    g_next_router = nullptr;
+    g_next_router_bytes = 0;
+    if (D.next_router) {
+        Tensor *nr = lookup(D.next_router);
+        if (nr && nr->type == T_F32) {
+            g_next_router = nr->base;
+            g_next_router_bytes = nr->nblk * 4;
+        }
+    }
+    const int rc = moe_routed_dev(L, T, router, d_x, d_logits, bias, d_out, d_residual, d_ids, st);
+    g_next_router = nullptr;
+    if (rc) return rc;
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;
 }

@@ -72,6 +72,7 @@ class MoeLayer:
     shexp_ffn: int = 0
     expert0: int = 0
     n_local: int = 0
+    next_router: Optional[DeviceTensor] = None  # L2-prefetch hint: the following layer's router
 
     def desc(self) -> _lib.MoeDesc:
         h = lambda t: t.handle if t is not None else 0  # noqa: E731
@@ -79,7 +80,7 @@ class MoeLayer:
         return _lib.MoeDesc(self.dim, self.ffn, self.n_expert, self.n_used, self.gating, int(self.weights_norm),
                             self.weights_scale, h(self.router), h(self.router_bias), h(self.gate), h(self.up),
                             h(self.down), h(sh[0]), h(sh[1]), h(sh[2]), self.shexp_ffn, self.expert0,
-                            self.n_local or self.n_expert)
+                            self.n_local or self.n_expert, h(self.next_router))
 
     def forward(self, x, out, residual=None, logits=None, ids=None, stream=None, desc=None) -> None:
         """x, out: torch cuda float32 [T, dim]; ids: torch cuda int32 [T, n_used]."""
@@ -102,6 +103,22 @@ def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -
 def force_generic(on: bool) -> bool:
     """Route MoE layers through the general slot kernels (test cross-check)."""
     return bool(_lib.lib().loom_cuda_force_generic(int(on)))
+
+
+def trace_enable(n_kernels: int) -> None:
+    """Record (first start, last end) of the next n_kernels decode kernels."""
+    _lib.must(_lib.lib().loom_cuda_trace_enable(n_kernels), "trace_enable")
+
+
+def trace_reset() -> None:
+    _lib.must(_lib.lib().loom_cuda_trace_reset(), "trace_reset")
+
+
+def trace_read(n_kernels: int) -> np.ndarray:
+    """[n, 2] globaltimer ns (start, end) per traced kernel."""
+    out = np.zeros((n_kernels, 2), np.uint64)
+    n = _lib.lib().loom_cuda_trace_read(out.ctypes.data_as(C.c_void_p), n_kernels)
+    return out[:n]
 
 
 def sync() -> None:
