@@ -176,6 +176,22 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
 /* Size the scratch for layers up to (dim, ffn, n_expert, n_used) at T tokens so
  * later forwards never allocate (required before CUDA-graph capture). */
 int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t n_used);
+/* Allocation-free variant of loom_cuda_moe_forward. No counterpart in the
+ * reference: it exists for callers that must not allocate device memory while
+ * they run (code inside someone else's CUDA stream capture, engines with a
+ * fixed memory budget, processes sharing a GPU under a fixed allocation).
+ * The layer's scratch is a fixed 1 MiB array (LOOM_CUDA_NOALLOC_SCRATCH_BYTES)
+ * that every GPU loading this library holds until the process exits; no
+ * cudaMalloc/cudaFree is ever called. Covers the fused decode shapes (T <= 16,
+ * the layer's scratch <= 1 MiB, router on the device); anything larger is
+ * declined with a message. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture. All calls share the one array and it keeps the last call's
+ * contents (nothing in it needs to start at zero): calls that overlap on the
+ * GPU (different streams, no ordering) race and must not be issued. */
+#define LOOM_CUDA_NOALLOC_SCRATCH_BYTES (1u << 20)
+int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
+                                  const float *d_residual, void *stream);
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);

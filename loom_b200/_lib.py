@@ -86,6 +86,7 @@ def lib() -> C.CDLL:
         "loom_cuda_tensor_free": (i, [u64]),
         "loom_cuda_tensor_device_bytes": (sz, [u64]),
         "loom_cuda_moe_forward": (i, [C.POINTER(MoeDesc), vp, sz, vp, vp, vp, vp, vp]),
+        "loom_cuda_moe_forward_noalloc": (i, [C.POINTER(MoeDesc), vp, sz, vp, vp, vp]),
         "loom_cuda_reserve": (i, [sz, sz, sz, sz, sz]),
         "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
         "loom_cuda_sync": (i, []),

@@ -919,3 +919,124 @@ int loom_cuda_tensor_matmul(loom_tensor h, size_t rows, size_t cols, const float
 }
 
 }  // extern "C"
+
+// ---- allocation-free MoE layer ----------------------------------------------------
+// For callers that must not allocate device memory while they run: code that
+// executes inside a CUDA stream capture owned by someone else, a host engine
+// whose memory is budgeted up front, or a process sharing the GPU under a
+// fixed allocation. The layer's scratch lives in one fixed array that the
+// library image carries on every device it is loaded on, so this entry point
+// never calls cudaMalloc/cudaFree and never grows the backend's own scratch.
+
+namespace {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(1) << 20;  // LOOM_CUDA_NOALLOC_SCRATCH_BYTES
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+uint8_t *g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};  // device address of g_noalloc_scratch, per device
+
+// Carve the decode-path scratch out of [base, base + NOALLOC_SCRATCH_BYTES);
+// returns the bytes used (0 when it does not fit).
+size_t noalloc_layout(uint8_t *base, size_t T, size_t dim, size_t n_expert, size_t n_used, size_t n_slots,
+                      size_t act_stride, DecodeArgs &A) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t *p = base + off;
+        off += align256(bytes);
+        return p;
+    };
+    A.x256 = XQW{reinterpret_cast<int8_t *>(take(T * dim)), reinterpret_cast<float *>(take(T * (dim / 256 + 1) * 4)),
+                 reinterpret_cast<int32_t *>(take(T * (dim / 16 + 1) * 4))};
+    A.x32 = XQW{reinterpret_cast<int8_t *>(take(T * dim)), reinterpret_cast<float *>(take(T * (dim / 32 + 1) * 4)),
+                reinterpret_cast<int32_t *>(take(T * (dim / 32 + 1) * 4))};
+    A.logits = reinterpret_cast<float *>(take(T * n_expert * 4));
+    A.ids = reinterpret_cast<int *>(take(T * n_used * 4));
+    A.gates = reinterpret_cast<float *>(take(T * n_used * 4));
+    A.act = reinterpret_cast<float *>(take(n_slots * act_stride * 4));
+    A.aq = reinterpret_cast<int8_t *>(take(n_slots * act_stride));
+    A.ad = reinterpret_cast<float *>(take(n_slots * (act_stride / 32) * 4));
+    A.as = reinterpret_cast<int32_t *>(take(n_slots * (act_stride / 16) * 4));
+    return off <= NOALLOC_SCRATCH_BYTES ? off : 0;
+}
+
+}  // namespace
+
+extern "C" int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
+                                             const float *d_residual, void *stream) {
+    if (int rc = need_init()) return rc;
+    if (!desc || T == 0) return decline("empty forward");
+    if (g_device < 0 || g_device >= NOALLOC_MAX_DEVICES) return decline("device index out of range for the fixed scratch");
+    // once per device, with that device current: the device address of the
+    // fixed array (host code only has a stand-in symbol for it)
+    if (!g_noalloc_ptr[g_device]) {
+        void *p = nullptr;
+        CK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_ptr[g_device] = static_cast<uint8_t *>(p);
+    }
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    const loom_moe_desc &D = *desc;
+    if (D.n_expert == 0 || D.n_expert > 1024 || D.n_used == 0 || D.n_used > 64 || D.n_used > D.n_expert)
+        return decline("router shape out of range (moe.zig:48-49)");
+    const size_t n_local = D.n_local ? D.n_local : D.n_expert;
+    if (D.expert0 + n_local > D.n_expert) return decline("expert range out of bounds");
+    Tensor *g = lookup(D.gate), *u = lookup(D.up), *dn = lookup(D.down), *r = lookup(D.router);
+    const Tensor *sh[3] = {nullptr, nullptr, nullptr};
+    if (D.shexp_gate) {
+        sh[0] = lookup(D.shexp_gate);
+        sh[1] = lookup(D.shexp_up);
+        sh[2] = lookup(D.shexp_down);
+        if (!sh[0] || !sh[1] || !sh[2]) return decline("unknown shared-expert tensor");
+    }
+    if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
+    RoutedLayerDev L{};
+    if (int rc = routed_layer(L, g, u, dn, D.dim, D.ffn, n_local, sh, D.shexp_ffn)) return rc;
+    L.n_expert = (int)D.n_expert;
+    L.n_used = (int)D.n_used;
+    L.gating = D.gating ? D.gating : 1;
+    L.weights_norm = D.weights_norm;
+    L.weights_scale = D.weights_scale;
+    L.expert0 = (int)D.expert0;
+    L.n_local = (int)n_local;
+    const float *bias = nullptr;
+    if (D.router_bias) {
+        Tensor *b = lookup(D.router_bias);
+        if (!b || b->type != T_F32 || b->nblk < D.n_expert) return decline("router bias must be f32 [n_expert]");
+        bias = reinterpret_cast<const float *>(b->base);
+    }
+    const size_t max_ffn = std::max<size_t>(D.ffn, sh[0] ? D.shexp_ffn : 0);
+    const size_t n_slots = T * D.n_used + (sh[0] ? T : 0);
+    const size_t act_stride = align256(max_ffn);
+    if (T > DECODE_MAX_T) return decline("the allocation-free layer takes at most 16 tokens");
+    DecodeArgs A{};
+    if (!noalloc_layout(g_noalloc_ptr[g_device], T, D.dim, D.n_expert, D.n_used, n_slots, act_stride, A))
+        return decline("layer scratch exceeds the 1 MiB fixed array of the allocation-free entry point");
+    A.T = (int)T;
+    A.dim = L.dim;
+    A.ffn = L.ffn;
+    A.n_expert = L.n_expert;
+    A.n_used = L.n_used;
+    A.gating = L.gating;
+    A.weights_norm = L.weights_norm;
+    A.weights_scale = L.weights_scale;
+    A.expert0 = L.expert0;
+    A.n_local = L.n_local;
+    A.router = reinterpret_cast<const float *>(r->base);
+    A.bias = bias;
+    A.x = d_x;
+    A.out = d_out;
+    A.residual = d_residual;
+    A.need256 = any_type(L, true);
+    A.need32 = any_type(L, false);
+    A.g = L.g;
+    A.u = L.u;
+    A.dn = L.dn;
+    A.has_shared = L.has_shared;
+    A.sg = L.sg;
+    A.su = L.su;
+    A.sdn = L.sdn;
+    A.shexp_ffn = L.shexp_ffn;
+    A.act_stride = (int)act_stride;
+    if (!decode_supported(A)) return decline("layer shape not covered by the fused decode kernels");
+    CK(launch_decode(A, st));
+    return LOOM_CUDA_OK;
+}
