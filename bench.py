@@ -311,7 +311,8 @@ def trace_phases(D, step, stream, torch):
     rel = lambda v: round(float(np.mean(v - prev_end)) / 1e3, 2)  # noqa: E731
     return {
         "router_first_start": rel(L[:, 0, 0]), "router_x_staged": rel(L[:, 3, 0]),
-        "router_cluster_synced": rel(L[:, 3, 1]), "router_routed": rel(L[:, 6, 0]),
+        "router_cluster_synced": rel(L[:, 3, 1]), "router_scored": rel(L[:, 7, 0]), "router_ranked": rel(L[:, 7, 1]),
+        "router_routed": rel(L[:, 6, 0]),
         "router_quantized": rel(L[:, 6, 1]), "router_end": rel(L[:, 0, 1]),
         "gateup_first_start": rel(L[:, 1, 0]), "gateup_post_wait": rel(L[:, 4, 0]), "gateup_end": rel(L[:, 1, 1]),
         "down_first_start": rel(L[:, 2, 0]), "down_post_wait": rel(L[:, 5, 0]), "down_end": rel(L[:, 2, 1]),

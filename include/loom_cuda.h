@@ -195,9 +195,10 @@ int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const float *d_x, s
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);
-/* Test hook: 1 routes every MoE layer through the general slot kernels instead
- * of the fused decode kernels (same numerics; used to cross-check the two).
- * Returns the previous setting. */
+/* Test hook selecting the MoE kernel family (all compute the same numbers):
+ * 0 automatic (fused decode kernels for T <= 16, expert-major batch kernels
+ * above), 1 the general slot kernels, 2 the expert-major batch kernels at any
+ * T. Returns the previous setting. */
 int loom_cuda_force_generic(int on);
 /* Phase tracing of the fused decode kernels (the counterpart of the
  * reference's LOOM_PROFILE phase timers, deepseek.zig:705-850): with room for

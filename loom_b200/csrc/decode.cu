@@ -173,11 +173,13 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
         // route_scores reads each logit before overwriting the same entry with its choice value
         const bool r = route_scores(choice, A.bias, ne, A.gating, scores, choice, lane);
         if (lane == 0) s_ranked = r;
+        if (A.trace && lane == 0) atomicMin(A.trace + 2 * (A.trace_slot + 7), gtimer());
     }
     __syncthreads();
     const bool ranked = s_ranked;
     if (ranked) route_rank(scores, choice, ne, A.n_used, sid, sg, threadIdx.x, blockDim.x);
     __syncthreads();
+    if (A.trace && threadIdx.x == 0) atomicMax(A.trace + 2 * (A.trace_slot + 7) + 1, gtimer());
     if (warp == 0) {
         route_finish(ranked, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
                      A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
@@ -546,29 +548,31 @@ bool decode_supported(const DecodeArgs &A) {
            max_ffn * 4 <= 48 * 1024;
 }
 
+static cudaError_t launch_router(const DecodeArgs &A, cudaStream_t st) {
+    const size_t smem = (size_t)(A.dim + 2 * A.n_expert + 128) * 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(A.router ? RR_CLUSTER : 1, A.T);
+    cfg.blockDim = dim3(RR_WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = A.router ? RR_CLUSTER : 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, k_router_route, A);
+}
+
 cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
     cudaError_t e;
     // 1. router + route + activation quantization
-    {
-        const size_t smem = (size_t)(A.dim + 2 * A.n_expert + 128) * 4;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(A.router ? RR_CLUSTER : 1, A.T);
-        cfg.blockDim = dim3(RR_WARPS * 32);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[2];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        attr[1].id = cudaLaunchAttributeClusterDimension;
-        attr[1].val.clusterDim.x = A.router ? RR_CLUSTER : 1;
-        attr[1].val.clusterDim.y = 1;
-        attr[1].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 2;
-        count_launch();
-        e = cudaLaunchKernelEx(&cfg, k_router_route, A);
-        if (e != cudaSuccess) return e;
-    }
+    e = launch_router(A, st);
+    if (e != cudaSuccess) return e;
     // 2. gate/up
     {
         const int n_slots = A.T * A.n_used + (A.has_shared ? A.T : 0);
@@ -588,6 +592,257 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+
+// ==== expert-major batch path ===========================================================
+// For T tokens the routed (token, expert) slots are grouped by expert, and
+// every kernel reads an expert's rows once for all the tokens that chose it
+// (the reference's moeBatchUnion, llama.zig:1828-1925, and matmulK256's
+// "decode once, dot n lanes", ggml.zig:1044). Per slot the arithmetic is the
+// decode path's, so results are bit-identical to it and to the CPU.
+
+// Group the local routed slots by expert (stable: slot order within a group).
+__global__ void __launch_bounds__(512) k_group(DecodeArgs A) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int cnt[1024];
+    const int ns = A.T * A.n_used;
+    for (int e = threadIdx.x; e < A.n_local; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int s = threadIdx.x; s < ns; s += blockDim.x) {
+        const int le = A.ids[s] - A.expert0;
+        if (le >= 0 && le < A.n_local) atomicAdd(&cnt[le], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // exclusive prefix over n_local (<= 1024) counts
+        int o = 0;
+        for (int e = 0; e < A.n_local; e++) {
+            A.grp_off[e] = o;
+            A.grp_cnt[e] = cnt[e];
+            o += cnt[e];
+        }
+    }
+    __syncthreads();
+    for (int s = threadIdx.x; s < ns; s += blockDim.x) {
+        const int id = A.ids[s];
+        const int le = id - A.expert0;
+        if (le < 0 || le >= A.n_local) continue;
+        int before = 0;  // earlier slots of the same expert
+        for (int j = 0; j < s; j++) before += A.ids[j] == id;
+        A.grp_list[A.grp_off[le] + before] = s;
+    }
+}
+
+// gate/up for expert blockIdx.y (n_local = the shared expert): the CTA's rows
+// are loaded once, then dotted with each token of the expert.
+template <int TY, int NB>
+__global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_grp(DecodeArgs A) {
+    constexpr int GU_NR = gu_nr<NB>();
+    using E = CEng<TY, 2 * GU_NR, NB>;
+    pdl_wait();
+    pdl_trigger();
+    const int e = blockIdx.y;
+    const bool shared = e == A.n_local;
+    const int n = shared ? A.T : A.grp_cnt[e];
+    const int ffn = shared ? A.shexp_ffn : A.ffn;
+    const int rows_cta = GU_WARPS * GU_NR;
+    if (n == 0 || (int)blockIdx.x * rows_cta >= ffn) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int dim = NB * 256;
+    const WDev wg = shared ? A.sg : A.g, wu = shared ? A.su : A.u;
+    const uint64_t plane = shared ? 0 : (uint64_t)e * ffn * NB;
+    const int r0 = blockIdx.x * rows_cta + warp * GU_NR;
+    const int rl = r0 <= ffn - GU_NR ? r0 : ffn - GU_NR;
+    GateUpStreams<GU_NR> st{wg, wu, plane + (uint64_t)rl * NB, plane + (uint64_t)rl * NB, NB, XV{nullptr, nullptr, nullptr}};
+    typename E::Frags fr;
+    E::load(st, fr, lane);
+    const int *list = shared ? nullptr : A.grp_list + A.grp_off[e];
+    for (int i = 0; i < n; i++) {
+        const int slot = shared ? A.T * A.n_used + i : list[i];
+        const int t = shared ? i : slot / A.n_used;
+        st.xv = XV{A.x256.q + (size_t)t * dim, A.x256.d + (size_t)t * NB, A.x256.s + (size_t)t * NB * 16};
+        float acc[2 * GU_NR];
+        E::finish(st, fr, acc, lane);
+        if (lane == 0) {
+            float *act = A.act + (size_t)slot * A.act_stride;
+#pragma unroll
+            for (int k = 0; k < GU_NR; k++) {
+                const int r = rl + k;
+                if (r >= r0 && r < ffn) act[r] = fmul(fdiv(acc[k], fadd(1.0f, expf(-acc[k]))), acc[GU_NR + k]);
+            }
+        }
+    }
+}
+
+// quantize every live slot's activation in the down type's format
+__global__ void __launch_bounds__(128) k_quant_grp(DecodeArgs A) {
+    pdl_wait();
+    pdl_trigger();
+    const int slot = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nr = A.T * A.n_used;
+    int f;
+    int dty;
+    if (slot < nr) {
+        const int le = A.ids[slot] - A.expert0;
+        if (le < 0 || le >= A.n_local) return;
+        f = A.ffn;
+        dty = A.dn.type;
+    } else {
+        f = A.shexp_ffn;
+        dty = A.sdn.type;
+    }
+    const float *x = A.act + (size_t)slot * A.act_stride;
+    int8_t *q = A.aq + (size_t)slot * A.act_stride;
+    float *d = A.ad + (size_t)slot * (A.act_stride / 32);
+    int32_t *s = A.as + (size_t)slot * (A.act_stride / 16);
+    if (act256(dty)) {
+        for (int b = warp; b < f / 256; b += 4)
+            quant_lane8(x + b * 256 + lane * 8, true, 32, q + b * 256 + lane * 8, d + b, s + b * 16 + lane / 2, nullptr,
+                        lane);
+    } else {
+        const int nb = f / 32, ng = (nb + 7) / 8;
+        for (int g = warp; g < ng; g += 4) {
+            const int b = g * 8 + lane / 4;
+            const int off = b * 32 + (lane & 3) * 8;
+            quant_lane8(x + off, b < nb, 4, q + off, d + b, nullptr, s + b, lane);
+        }
+    }
+}
+
+// down rows of expert blockIdx.y for each of its tokens: y[slot][row]
+template <int RS> struct RowStreams {  // RS consecutive rows of one expert plane
+    WDev wd;
+    uint64_t gb0;
+    int nb;
+    XV xv;
+    __device__ __forceinline__ WDev w(int) const { return wd; }
+    __device__ __forceinline__ uint64_t gb(int s) const { return gb0 + (uint64_t)s * nb; }
+    __device__ __forceinline__ XV x(int) const { return xv; }
+};
+
+template <int TY, int RS, int NB>
+__global__ void __launch_bounds__(DN_WARPS * 32) k_down_grp(DecodeArgs A) {
+    using E = CEng<TY, RS, NB>;
+    pdl_wait();
+    pdl_trigger();
+    const int e = blockIdx.y;
+    const bool shared = e == A.n_local;
+    const int n = shared ? A.T : A.grp_cnt[e];
+    if (n == 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = (blockIdx.x * DN_WARPS + warp) * RS;
+    if (r0 >= A.dim) return;
+    const int rl = r0 <= A.dim - RS ? r0 : A.dim - RS;
+    const WDev wd = shared ? A.sdn : A.dn;
+    const uint64_t plane = shared ? 0 : (uint64_t)e * A.dim * NB;
+    RowStreams<RS> st{wd, plane + (uint64_t)rl * NB, NB, XV{nullptr, nullptr, nullptr}};
+    typename E::Frags fr;
+    E::load(st, fr, lane);
+    const int *list = shared ? nullptr : A.grp_list + A.grp_off[e];
+    const int stride = A.act_stride;
+    for (int i = 0; i < n; i++) {
+        const int slot = shared ? A.T * A.n_used + i : list[i];
+        st.xv = XV{A.aq + (size_t)slot * stride, A.ad + (size_t)slot * (stride / 32), A.as + (size_t)slot * (stride / 16)};
+        float y[RS];
+        E::finish(st, fr, y, lane);
+        if (lane < RS) {
+            float v = y[0];
+#pragma unroll
+            for (int k = 1; k < RS; k++)
+                if (lane == k) v = y[k];
+            const int r = rl + lane;
+            if (r >= r0) A.y[(size_t)slot * A.dim + r] = v;
+        }
+    }
+}
+
+// out[t][r] = residual + sum over the token's local slots, in selection order,
+// of gate * y, then + the shared expert's y (llama.zig:1397, deepseek.zig:1498)
+__global__ void __launch_bounds__(256) k_combine(DecodeArgs A) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.y;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= A.dim) return;
+    float acc = 0.0f;
+    for (int k = 0; k < A.n_used; k++) {
+        const int slot = t * A.n_used + k;
+        const int le = A.ids[slot] - A.expert0;
+        if (le < 0 || le >= A.n_local) continue;
+        acc = fadd(acc, fmul(A.gates[slot], A.y[(size_t)slot * A.dim + r]));
+    }
+    if (A.has_shared) acc = fadd(acc, A.y[((size_t)A.T * A.n_used + t) * A.dim + r]);
+    const size_t o = (size_t)t * A.dim + r;
+    A.out[o] = A.residual ? fadd(A.residual[o], acc) : acc;
+}
+
+static GUFn gateup_grp_fn(int ty, int nb) {
+    if (ty == T_Q4_K) switch (nb) {
+            case 4: return k_gateup_grp<T_Q4_K, 4>;
+            case 8: return k_gateup_grp<T_Q4_K, 8>;
+            case 16: return k_gateup_grp<T_Q4_K, 16>;
+            case 28: return k_gateup_grp<T_Q4_K, 28>;
+        }
+    if (ty == T_Q6_K && nb == 8) return k_gateup_grp<T_Q6_K, 8>;
+    return nullptr;
+}
+
+// rows per warp of the grouped down kernel: 8 (Q6_K, block-major units) or 4
+// (Q4_K, stream-major units)
+static GUFn down_grp_fn(int ty, int nb, int &rs) {
+    if (ty == T_Q6_K) {
+        rs = 8;
+        switch (nb) {
+            case 1: return k_down_grp<T_Q6_K, 8, 1>;
+            case 2: return k_down_grp<T_Q6_K, 8, 2>;
+            case 3: return k_down_grp<T_Q6_K, 8, 3>;
+            case 4: return k_down_grp<T_Q6_K, 8, 4>;
+            case 8: return k_down_grp<T_Q6_K, 8, 8>;
+        }
+    }
+    if (ty == T_Q4_K) {
+        rs = 4;
+        switch (nb) {
+            case 4: return k_down_grp<T_Q4_K, 4, 4>;
+            case 8: return k_down_grp<T_Q4_K, 4, 8>;
+        }
+    }
+    return nullptr;
+}
+
+bool batch_supported(const DecodeArgs &A) {
+    if (A.g.type != A.u.type || A.dim % 256 || A.n_local > 1024) return false;
+    if (!gateup_grp_fn(A.g.type, A.dim / 256)) return false;
+    const int dty = A.dn.type;
+    if (block_elems(dty) == 0 || A.ffn % block_elems(dty)) return false;
+    int rs;
+    if (!down_grp_fn(dty, A.ffn / block_elems(dty), rs) || A.dim % rs) return false;
+    if (A.has_shared) {
+        if (A.sg.type != A.g.type || A.su.type != A.g.type || A.sdn.type != dty) return false;
+        if (A.shexp_ffn != A.ffn) return false;  // the shared expert reuses the routed instantiation
+    }
+    return (size_t)(A.dim + 2 * A.n_expert + 128) * 4 <= 48 * 1024;
+}
+
+cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st) {
+    cudaError_t e = launch_router(A, st);
+    if (e != cudaSuccess) return e;
+    if ((e = launch_pdl(k_group, dim3(1), dim3(512), 0, st, A)) != cudaSuccess) return e;
+    const int nexp = A.n_local + (A.has_shared ? 1 : 0);
+    const int nb = A.dim / 256;
+    const int rows_cta = GU_WARPS * (nb <= 8 ? 3 : 1);
+    if ((e = launch_pdl(gateup_grp_fn(A.g.type, nb), dim3(cdivu(A.ffn, rows_cta), nexp), dim3(GU_WARPS * 32), 0, st,
+                        A)) != cudaSuccess)
+        return e;
+    const int n_slots = A.T * A.n_used + (A.has_shared ? A.T : 0);
+    if ((e = launch_pdl(k_quant_grp, dim3(n_slots), dim3(128), 0, st, A)) != cudaSuccess) return e;
+    int rs = 0;
+    GUFn dfn = down_grp_fn(A.dn.type, A.ffn / block_elems(A.dn.type), rs);
+    if ((e = launch_pdl(dfn, dim3(cdivu(A.dim, DN_WARPS * rs), nexp), dim3(DN_WARPS * 32), 0, st, A)) != cudaSuccess)
+        return e;
+    return launch_pdl(k_combine, dim3(cdivu(A.dim, 256), A.T), dim3(256), 0, st, A);
 }
 
 }  // namespace loom

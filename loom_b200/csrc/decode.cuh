@@ -40,6 +40,11 @@ struct DecodeArgs {
     float *ad;               // [n_slots][act_stride/32]
     int32_t *as;             // [n_slots][act_stride/16]
     int act_stride;          // multiple of 256
+    // expert-major batch path (launch_batch): tokens grouped per local expert
+    int *grp_cnt;            // [n_local] slots per local expert
+    int *grp_off;            // [n_local] first position in grp_list
+    int *grp_list;           // [T*n_used] routed slots, grouped by expert, slot order within a group
+    float *y;                // [n_slots][dim] per-slot down outputs
     const uint8_t *next_router;   // optional: the next layer's router weights, prefetched into L2
     size_t next_router_bytes;
     unsigned long long *trace;  // optional [2*k] (first start, last end) globaltimer ns per kernel, or null
@@ -50,5 +55,10 @@ struct DecodeArgs {
 bool decode_supported(const DecodeArgs &A);
 // Enqueue the three PDL-chained kernels of one layer.
 cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st);
+// Expert-major batch path (any T): router, grouping, gate/up per expert with
+// every token of the expert against one read of its rows, activation
+// quantization, down per expert, ordered combine.
+bool batch_supported(const DecodeArgs &A);
+cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st);
 
 }  // namespace loom

@@ -115,7 +115,7 @@ struct HBuf {  // pinned host staging
 
 struct Scratch {
     DBuf xq256_q, xq256_d, xq256_s, xq32_q, xq32_d, xq32_s;
-    DBuf logits, ids, gates, slots, act, aq, ad, as, counters;
+    DBuf logits, ids, gates, slots, act, aq, ad, as, counters, grp, ybuf;
     DBuf io_in, io_out, io_aux, raw;
     HBuf h_in, h_out;
 } S;
@@ -373,10 +373,20 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
     const size_t n_slots = T * L.n_used + (L.has_shared ? T : 0);
     if (int rc = ensure_moe_scratch(T, L.dim, max_ffn, L.n_expert, n_slots)) return rc;
     const size_t act_stride = align256(max_ffn);
-    if (!g_force_generic && T <= DECODE_MAX_T) {
+    if (g_force_generic != 1) {
         DecodeArgs A = decode_args(L, T, router, d_x, d_logits, d_bias, d_out, d_residual, d_ids_out, act_stride);
-        if (decode_supported(A)) {
+        if (g_force_generic == 0 && T <= DECODE_MAX_T && decode_supported(A)) {
             CK(launch_decode(A, st));
+            return 0;
+        }
+        if (router && batch_supported(A)) {
+            if (int rc = S.grp.ensure((2 * (size_t)L.n_local + T * L.n_used) * 4)) return rc;
+            if (int rc = S.ybuf.ensure(n_slots * (size_t)L.dim * 4)) return rc;
+            A.grp_cnt = S.grp.as<int>();
+            A.grp_off = A.grp_cnt + L.n_local;
+            A.grp_list = A.grp_off + L.n_local;
+            A.y = S.ybuf.as<float>();
+            CK(launch_batch(A, st));
             return 0;
         }
     }
@@ -400,7 +410,7 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
 extern "C" {
 
 int loom_cuda_init(int device) {
-    if (const char *e = getenv("LOOM_CUDA_GENERIC")) g_force_generic = e[0] == '1';
+    if (const char *e = getenv("LOOM_CUDA_GENERIC")) g_force_generic = e[0] - '0';
     if (g_inited) return device == g_device ? LOOM_CUDA_OK : decline("already initialised on another device");
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return decline("no CUDA device");
@@ -438,7 +448,7 @@ void loom_cuda_shutdown(void) {
         if (a.dev) cudaFree(a.dev);
     g_arenas.clear();
     for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
-                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.io_in, &S.io_out, &S.io_aux, &S.raw}) {
+                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.grp, &S.ybuf, &S.io_in, &S.io_out, &S.io_aux, &S.raw}) {
         if (b->p) cudaFree(b->p);
         b->p = nullptr;
         b->cap = 0;
@@ -551,7 +561,7 @@ size_t loom_cuda_trace_read(uint64_t *out, size_t n_kernels) {
 
 int loom_cuda_force_generic(int on) {
     const int prev = g_force_generic;
-    g_force_generic = on != 0;
+    g_force_generic = on;
     return prev;
 }
 
@@ -837,6 +847,8 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
     if (int rc = need_init()) return rc;
     const size_t n_slots = T * (n_used + 1);
     if (int rc = ensure_moe_scratch(T, dim, ffn, n_expert, n_slots)) return rc;
+    if (int rc = S.grp.ensure((2 * n_expert + T * n_used) * 4)) return rc;
+    if (int rc = S.ybuf.ensure(n_slots * dim * 4)) return rc;
     CK(cudaStreamSynchronize(g_stream));
     return LOOM_CUDA_OK;
 }

@@ -100,9 +100,9 @@ def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -
               "tensor_matmul")
 
 
-def force_generic(on: bool) -> bool:
-    """Route MoE layers through the general slot kernels (test cross-check)."""
-    return bool(_lib.lib().loom_cuda_force_generic(int(on)))
+def force_generic(mode) -> int:
+    """Kernel family for MoE layers: 0 automatic, 1 (True) slot kernels, 2 expert-major batch kernels."""
+    return int(_lib.lib().loom_cuda_force_generic(int(mode)))
 
 
 def trace_enable(n_kernels: int) -> None:

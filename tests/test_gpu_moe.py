@@ -175,16 +175,17 @@ def _layer_case(orc, seed, ne, k, dim, ffn, gt, dt, shared=0, gating=1, scale=1.
     dict(ne=256, k=8, dim=1024, ffn=1024, gt=12, dt=12, shared=1024, gating=2, scale=2.5, bias=True),  # V3-like
     dict(ne=16, k=4, dim=512, ffn=256, gt=14, dt=14),                        # Q6_K gate/up
 ], ids=["qwen3", "v2lite", "v3like", "q6k"])
-@pytest.mark.parametrize("T", [1, 3])
+@pytest.mark.parametrize("T", [1, 3, 40])
 def test_decode_kernels_bitexact_with_slot_kernels(be, orc, cfg, T):
-    """The fused decode kernels and the general slot kernels implement the
-    same arithmetic: their outputs must agree bit for bit."""
+    """The fused decode kernels, the expert-major batch kernels and the general
+    slot kernels implement the same arithmetic: their outputs must agree bit for
+    bit."""
     from loom_b200 import device as D
     L = _layer_case(orc, 5, **cfg)
     x = torch.from_numpy(orc.synth(0, T * cfg["dim"], seed=9).reshape(T, cfg["dim"])).cuda()
     res = torch.randn(T, cfg["dim"], device="cuda")
     outs, idss = [], []
-    for generic in (False, True):
+    for generic in (0, 2, 1):
         prev = D.force_generic(generic)
         try:
             out = torch.full((T, cfg["dim"]), float("nan"), device="cuda")
@@ -195,8 +196,9 @@ def test_decode_kernels_bitexact_with_slot_kernels(be, orc, cfg, T):
             idss.append(ids.cpu().numpy())
         finally:
             D.force_generic(prev)
-    assert np.array_equal(idss[0], idss[1])
-    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    for i in (1, 2):
+        assert np.array_equal(idss[0], idss[i])
+        assert np.array_equal(bits(outs[0]), bits(outs[i])), i
 
 
 def test_expert_parallel_partition_sums_to_full(be, orc):
