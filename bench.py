@@ -291,7 +291,7 @@ def trace_phases(D, step, stream, torch):
     kernel the mean span (first CTA start to last CTA end) and the mean gap
     between consecutive kernels, in microseconds (not part of the timed
     region)."""
-    n = 8 * LAYERS
+    n = 12 * LAYERS
     D.trace_enable(n)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
@@ -301,7 +301,7 @@ def trace_phases(D, step, stream, torch):
             D.trace_reset()
             g.replay()
             torch.cuda.synchronize()
-    tr = D.trace_read(n).astype(np.float64).reshape(LAYERS, 8, 2)
+    tr = D.trace_read(n).astype(np.float64).reshape(LAYERS, 12, 2)
     D.trace_enable(0)
     if tr.shape[0] < LAYERS:
         return None
@@ -311,11 +311,14 @@ def trace_phases(D, step, stream, torch):
     rel = lambda v: round(float(np.mean(v - prev_end)) / 1e3, 2)  # noqa: E731
     return {
         "router_first_start": rel(L[:, 0, 0]), "router_x_staged": rel(L[:, 3, 0]),
-        "router_cluster_synced": rel(L[:, 3, 1]), "router_scored": rel(L[:, 7, 0]), "router_ranked": rel(L[:, 7, 1]),
-        "router_routed": rel(L[:, 6, 0]),
+        "router_cluster_synced": rel(L[:, 3, 1]), "router_routed": rel(L[:, 6, 0]),
         "router_quantized": rel(L[:, 6, 1]), "router_end": rel(L[:, 0, 1]),
         "gateup_first_start": rel(L[:, 1, 0]), "gateup_post_wait": rel(L[:, 4, 0]), "gateup_end": rel(L[:, 1, 1]),
         "down_first_start": rel(L[:, 2, 0]), "down_post_wait": rel(L[:, 5, 0]), "down_end": rel(L[:, 2, 1]),
+        "cycles": {"router_copy_wait": float(np.median(L[:, 7, 0])), "router_dots": float(np.median(L[:, 7, 1])),
+                   "router_tail": float(np.median(L[:, 8, 1])), "gateup_stage": float(np.median(L[:, 9, 0])),
+                   "gateup_dots": float(np.median(L[:, 9, 1])), "down_quant": float(np.median(L[:, 10, 0])),
+                   "down_dots": float(np.median(L[:, 10, 1]))},
         "unit": "us after the previous layer's down end",
     }
 

@@ -204,16 +204,22 @@ int loom_cuda_force_generic(int on);
  * reference's LOOM_PROFILE phase timers, deepseek.zig:705-850): with room for
  * n_kernels traced launches, each decode kernel records its first CTA start
  * and last CTA end (GPU globaltimer, ns). Kernels are assigned trace entries
- * in launch order, eight per layer: router, gate/up, down (first CTA start,
+ * in launch order, twelve per layer: router, gate/up, down (first CTA start,
  * last CTA end), the router's post-wait span up to its cluster barrier, the
  * first post-wait instants of gate/up and down, (route done, activation
- * quantized) in the router, and one spare. n_kernels = 0
+ * quantized) in the router, then SM-cycle counts (max over CTAs) of the
+ * router's copy wait and dots, its route tail, gate/up's staging and dots,
+ * and down's quantization and dots. n_kernels = 0
  * turns tracing off. */
 int loom_cuda_trace_enable(size_t n_kernels);
 /* Clear the recorded times (keeps the entry assignment of captured graphs). */
 int loom_cuda_trace_reset(void);
 /* Copy (start, end) pairs of the first n entries; returns entries copied. */
 size_t loom_cuda_trace_read(uint64_t *out, size_t n_kernels);
+/* Bitwise OR of the device error words the kernels raise instead of trapping
+ * (1 = a bounded wait on an asynchronous copy gave up); 0 when none, -1 when
+ * the stream itself is in error. Synchronizes the backend's stream. */
+int loom_cuda_device_error(void);
 /* Synchronize the backend's stream. */
 int loom_cuda_sync(void);
 /* The backend's stream (cudaStream_t). */

@@ -91,6 +91,7 @@ def lib() -> C.CDLL:
         "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
         "loom_cuda_sync": (i, []),
         "loom_cuda_force_generic": (i, [i]),
+        "loom_cuda_device_error": (i, []),
         "loom_cuda_trace_enable": (i, [sz]),
         "loom_cuda_trace_reset": (i, []),
         "loom_cuda_trace_read": (sz, [vp, sz]),

@@ -40,7 +40,7 @@ __host__ __device__ constexpr int layout_qbytes(int t) {
     return t == T_F32 ? 4 : t == T_Q4_0 ? 16 : t == T_Q8_0 ? 32 : t == T_Q4_K ? 144 : t == T_Q6_K ? 192 : 0;
 }
 // true when a type's activation is quantized per 256 (Q8_K style) rather than per 32
-__host__ __device__ constexpr bool act256(int t) { return t == T_Q4_K || t == T_Q6_K; }
+__host__ __device__ constexpr bool act256(int t) { return t == T_Q4_K || t == T_Q6_K || t == 112; }
 
 // A device-resident weight tensor in its device layout.
 struct WDev {

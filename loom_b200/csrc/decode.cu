@@ -20,6 +20,7 @@
 
 #include "decode.cuh"
 #include "devutil.cuh"
+#include "tma.cuh"
 #include "warpdot.cuh"
 
 namespace loom {
@@ -130,6 +131,44 @@ __device__ __forceinline__ void load_row_chunk(float (&w)[RR_CHUNK], const float
         if (i < nfull) w[i] = __ldg(wr + i * 32 + lane);
 }
 
+// CTA 0 of a token's router cluster, once every logit is in `choice`:
+// route (moe.zig:106) and quantize the token's activation (smx) for the expert
+// kernels. nw = warps in the CTA.
+__device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const float *smx, float *scores, float *choice,
+                                            int nw) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int dim = A.dim, ne = A.n_expert;
+    int *sid = reinterpret_cast<int *>(choice + ne);
+    float *sg = choice + ne + 64;
+    float *red = choice + ne + 128;
+    if (threadIdx.x < ROUTE_THREADS) {
+        route_block(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
+                    red, A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used);
+        if (A.ids_out)
+            for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS)
+                A.ids_out[(size_t)t * A.n_used + k] = sid[k];
+        if (A.trace && threadIdx.x == 0) atomicMin(A.trace + 2 * (A.trace_slot + 6), gtimer());
+    } else {
+        // quantize x in the format(s) the expert types read
+        const int nwq = nw - ROUTE_THREADS / 32, wi = warp - ROUTE_THREADS / 32;
+        if (A.need256)
+            for (int b = wi; b < dim / 256; b += nwq)
+                quant_lane8(smx + b * 256 + lane * 8, true, 32, A.x256.q + (size_t)t * dim + b * 256 + lane * 8,
+                            A.x256.d + (size_t)t * (dim / 256) + b,
+                            A.x256.s + (size_t)t * (dim / 16) + b * 16 + lane / 2, nullptr, lane);
+        if (A.need32) {
+            const int nb = dim / 32, ng = (nb + 7) / 8;
+            for (int g = wi; g < ng; g += nwq) {
+                const int b = g * 8 + lane / 4;
+                const int off = b * 32 + (lane & 3) * 8;
+                quant_lane8(smx + off, b < nb, 4, A.x32.q + (size_t)t * dim + off, A.x32.d + (size_t)t * (dim / 32) + b,
+                            nullptr, A.x32.s + (size_t)t * (dim / 32) + b, lane);
+            }
+        }
+        if (A.trace && lane == 0) atomicMax(A.trace + 2 * (A.trace_slot + 6) + 1, gtimer());
+    }
+}
+
 __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
     extern __shared__ float smx[];  // x[dim] | scores[ne] | choice[ne] | ids[64] | gates[64]
     const int t = blockIdx.y;
@@ -166,46 +205,84 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
         for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = A.logits_in[(size_t)t * ne + e];
         __syncthreads();
     }
-    __shared__ int s_ranked;
-    int *sid = reinterpret_cast<int *>(choice + ne);
-    float *sg = choice + ne + 64;
-    if (warp == 0) {
-        // route_scores reads each logit before overwriting the same entry with its choice value
-        const bool r = route_scores(choice, A.bias, ne, A.gating, scores, choice, lane);
-        if (lane == 0) s_ranked = r;
-        if (A.trace && lane == 0) atomicMin(A.trace + 2 * (A.trace_slot + 7), gtimer());
+    router_tail(A, t, smx, scores, choice, RR_WARPS);
+    __syncthreads();
+    trace_end(A, 0);
+}
+
+// TMA variant: one cluster of RR2_CLUSTER CTAs per token; each CTA copies its
+// slice of router rows into shared memory with bulk asynchronous copies issued
+// BEFORE the wait, so the 1 MiB of router weights streams while the previous
+// layer finishes; after the wait the dots read shared memory only.
+constexpr int RR2_WARPS = 8;
+constexpr uint32_t WAIT_POLLS = 1u << 22;  // bounded mbarrier wait (far beyond any legitimate latency)
+
+__global__ void __launch_bounds__(RR2_WARPS * 32) k_router_tma(DecodeArgs A) {
+    extern __shared__ __align__(16) float smw[];  // W rows [rpc][dim] | x[dim] | scores | choice | ids | gates
+    __shared__ __align__(8) uint64_t bar;
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int dim = A.dim, ne = A.n_expert;
+    const unsigned rank = cluster_rank();
+    const int ncl = (int)gridDim.x;
+    const int rpc = (ne + ncl - 1) / ncl;  // rows per CTA
+    const int row0 = (int)rank * rpc;
+    const int nrows = row0 >= ne ? 0 : (ne - row0 < rpc ? ne - row0 : rpc);
+    float *smx = smw + (size_t)rpc * dim;
+    float *scores = smx + dim, *choice = scores + ne;
+    trace_begin(A, 0);
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    if (threadIdx.x == 0 && nrows > 0) {
+        mbar_expect_tx(&bar, (uint32_t)(nrows * dim * 4));
+        for (int r = 0; r < nrows; r++)
+            bulk_g2s(smw + (size_t)r * dim, A.router + (size_t)(row0 + r) * dim, (uint32_t)(dim * 4), &bar);
     }
+    pdl_wait();
+    
+    const float *xt = A.x + (size_t)t * dim;
+    trace_begin(A, 3);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = xt[i];
     __syncthreads();
-    const bool ranked = s_ranked;
-    if (ranked) route_rank(scores, choice, ne, A.n_used, sid, sg, threadIdx.x, blockDim.x);
-    __syncthreads();
-    if (A.trace && threadIdx.x == 0) atomicMax(A.trace + 2 * (A.trace_slot + 7) + 1, gtimer());
-    if (warp == 0) {
-        route_finish(ranked, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
-                     A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
-        if (A.ids_out)
-            for (int k = lane; k < A.n_used; k += 32) A.ids_out[(size_t)t * A.n_used + k] = sid[k];
-        if (A.trace && lane == 0) atomicMin(A.trace + 2 * (A.trace_slot + 6), gtimer());
-    } else {
-        // quantize x in the format(s) the expert types read
-        const int nw = RR_WARPS - 1, wi = warp - 1;
-        if (A.need256)
-            for (int b = wi; b < dim / 256; b += nw)
-                quant_lane8(smx + b * 256 + lane * 8, true, 32, A.x256.q + (size_t)t * dim + b * 256 + lane * 8,
-                            A.x256.d + (size_t)t * (dim / 256) + b,
-                            A.x256.s + (size_t)t * (dim / 16) + b * 16 + lane / 2, nullptr, lane);
-        if (A.need32) {
-            const int nb = dim / 32, ng = (nb + 7) / 8;
-            for (int g = wi; g < ng; g += nw) {
-                const int b = g * 8 + lane / 4;
-                const int off = b * 32 + (lane & 3) * 8;
-                quant_lane8(smx + off, b < nb, 4, A.x32.q + (size_t)t * dim + off, A.x32.d + (size_t)t * (dim / 32) + b,
-                            nullptr, A.x32.s + (size_t)t * (dim / 32) + b, lane);
-            }
+    const long long c0 = clock64();
+    if (nrows > 0 && !mbar_wait(&bar, 0, WAIT_POLLS)) {
+        if (threadIdx.x == 0 && A.err) atomicOr(A.err, 1);
+    }
+    const long long c1 = clock64();
+    for (int r = warp; r < nrows; r += RR2_WARPS) {  // dotF32 (ggml.zig:198), lane j = accumulator lane j
+        const float *wr = smw + (size_t)r * dim;
+        const int nfull = dim / 32;
+        float a = 0.0f;
+        for (int i = 0; i < nfull; i++) a = fadd(a, fmul(wr[i * 32 + lane], smx[i * 32 + lane]));
+        int i = nfull * 32;
+        for (; i + 8 <= dim; i += 8)
+            if (lane < 8) a = fadd(a, fmul(wr[i + lane], smx[i + lane]));
+        const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
+        const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
+        const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
+        const float v = fadd(fadd(fadd(a, a8), a16), a24);
+        float res = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+        for (int jj = 1; jj < 8; jj++) res = fadd(res, __shfl_sync(0xffffffffu, v, jj));
+        for (; i < dim; i++) res = fadd(res, fmul(wr[i], smx[i]));
+        if (lane == 0) {
+            st_cluster_f32(choice + row0 + r, 0, res);
+            A.logits[(size_t)t * ne + row0 + r] = res;
         }
-        if (A.trace && lane == 0) atomicMax(A.trace + 2 * (A.trace_slot + 6) + 1, gtimer());
     }
+    const long long c2 = clock64();
+    cluster_sync_all();  // every logit is in CTA 0's `choice`
+    trace_end(A, 3);
+    if (A.trace && threadIdx.x == 0) {  // cycles: TMA wait, dots (max over the cluster)
+        atomicMax(A.trace + 2 * (A.trace_slot + 7), (unsigned long long)(c1 - c0));
+        atomicMax(A.trace + 2 * (A.trace_slot + 7) + 1, (unsigned long long)(c2 - c1));
+    }
+    if (rank != 0) return;
+    const long long c3 = clock64();
+    router_tail(A, t, smx, scores, choice, RR2_WARPS);
+    if (A.trace && threadIdx.x == 0) atomicMax(A.trace + 2 * (A.trace_slot + 8) + 1, (unsigned long long)(clock64() - c3));
     __syncthreads();
+    pdl_trigger();  // late: the expert kernel's CTAs would only wait on this SM's issue slots
     trace_end(A, 0);
 }
 
@@ -272,6 +349,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
     pdl_wait();
     pdl_trigger();
     trace_begin(A, 4);
+    const long long gc0 = clock64();
     const int slot = blockIdx.y;
     const SlotInfo si = slot_info(A, slot);
     const int rows_cta = GU_WARPS * GU_NR;
@@ -293,6 +371,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
     const int rl = r0 <= rmax ? r0 : rmax;  // clamp the last (partial) group; its extra rows are not stored
     GateUpStreams<GU_NR> st{wg, wu, plane + (uint64_t)rl * NB, plane + (uint64_t)rl * NB, NB, XV{xq, xd, xs}};
     typename E::Frags fr;
+    const long long gc1 = clock64();
     E::load(st, fr, lane);  // weight loads are in flight while the activation lands in shared memory
     if (threadIdx.x == 0) {
         // warm L2 with this CTA's share of the slot's down plane for k_down_dec
@@ -324,13 +403,19 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
             }
         }
     }
+    if (A.trace && lane == 0) {  // cycles: ids + activation staging, weights in + dots
+        atomicMax(A.trace + 2 * (A.trace_slot + 9), (unsigned long long)(gc1 - gc0));
+        atomicMax(A.trace + 2 * (A.trace_slot + 9) + 1, (unsigned long long)(clock64() - gc1));
+    }
     __syncthreads();
     trace_end(A, 1);
 }
 
 // ---- down + combine ------------------------------------------------------------------
 
-constexpr int DN_WARPS = 4;
+constexpr int DN_WARPS = 4;    // grouped down kernel
+constexpr int DND_WARPS = 16;  // decode down kernel: one 512-thread CTA per SM, so each CTA
+                               // quantizes the token's activations once for 16 rows
 
 struct DownStreams {
     WDev wd;
@@ -357,7 +442,7 @@ struct DownStreams {
 
 // SC streams (experts) per chunk of NB blocks; NBSH = shared expert blocks (0: none)
 template <int TY, int SC, int NB, int NBSH>
-__global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
+__global__ void __launch_bounds__(DND_WARPS * 32) k_down_dec(DecodeArgs A) {
     using E = CEng<TY, SC, NB>;
     using ES = CEng<TY, 1, (NBSH > 0 ? NBSH : QT<TY>::LPB == 8 ? 4 : 32 / QT<TY>::LPB)>;
     static_assert(E::OK, "unit mapping");
@@ -366,11 +451,11 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     __shared__ float s_gate[64];
     __shared__ int s_nloc;
     __shared__ int s_shidx;
-    __shared__ uint64_t s_gb[DN_WARPS][SC];
+    __shared__ uint64_t s_gb[DND_WARPS][SC];
     const int t = blockIdx.y;
     trace_begin(A, 2);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int r = blockIdx.x * DN_WARPS + warp;
+    const int r = blockIdx.x * DND_WARPS + warp;
     const int rr = r < A.dim ? r : A.dim - 1;
     const int nk = A.n_used;
     // Routing is final before this kernel may start: k_gateup_dec triggers its
@@ -414,6 +499,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
     pdl_wait();
     pdl_trigger();
     trace_begin(A, 5);
+    const long long dc0 = clock64();
     // quantize the token's expert activations into shared memory, in the down
     // type's format (quantizeX256 / quantizeX): routed slot k at k*stride, the
     // shared expert's at nk*stride
@@ -427,25 +513,30 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
         const int nbr = A.ffn / BEQ, nbs = NBSH > 0 ? A.shexp_ffn / BEQ : 0;
         const int nunits = nk * nbr + nbs;  // warp units of BPW blocks
         const int nsteps = (nunits + BPW - 1) / BPW;
-        for (int s0 = warp; s0 < nsteps; s0 += DN_WARPS * QB) {
+        for (int s0 = warp; s0 < nsteps; s0 += DND_WARPS * QB) {
             float v[QB][8];
             int kk[QB], bb[QB];
             bool live[QB];
 #pragma unroll
             for (int i = 0; i < QB; i++) {
-                const int st_ = s0 + i * DN_WARPS;
+                const int st_ = s0 + i * DND_WARPS;
                 const int u = st_ * BPW + lane / LPQ;
                 live[i] = st_ < nsteps && u < nunits;
                 kk[i] = u < nk * nbr ? u / nbr : nk;
                 bb[i] = u < nk * nbr ? u % nbr : u - nk * nbr;
                 const size_t slot = kk[i] < nk ? (size_t)t * nk + kk[i] : (size_t)A.T * nk + t;
                 const float *src = A.act + slot * stride + bb[i] * BEQ + (lane % LPQ) * 8;
-#pragma unroll
-                for (int e = 0; e < 8; e++) v[i][e] = live[i] ? src[e] : 0.0f;
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b4 = a;
+                if (live[i]) {
+                    a = reinterpret_cast<const float4 *>(src)[0];
+                    b4 = reinterpret_cast<const float4 *>(src)[1];
+                }
+                v[i][0] = a.x, v[i][1] = a.y, v[i][2] = a.z, v[i][3] = a.w;
+                v[i][4] = b4.x, v[i][5] = b4.y, v[i][6] = b4.z, v[i][7] = b4.w;
             }
 #pragma unroll
             for (int i = 0; i < QB; i++) {
-                if (s0 + i * DN_WARPS >= nsteps) break;  // warp-uniform
+                if (s0 + i * DND_WARPS >= nsteps) break;  // warp-uniform
                 const int k = kk[i], b = bb[i];
                 int8_t *q = aq + (size_t)k * stride + b * BEQ + (lane % LPQ) * 8;
                 float *dd = ad + (size_t)k * (stride / 32) + b;
@@ -456,6 +547,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
         }
     }
     __syncthreads();
+    const long long dc1 = clock64();
     float acc = 0.0f;
     for (int c0 = 0; c0 < nloc; c0 += SC) {
         const int n = nloc - c0 < SC ? nloc - c0 : SC;
@@ -488,6 +580,10 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_down_dec(DecodeArgs A) {
         const size_t o = (size_t)t * A.dim + r;
         A.out[o] = A.residual ? fadd(__ldcg(A.residual + o), acc) : acc;
     }
+    if (A.trace && lane == 0) {  // cycles: activation quantization, dots + combine
+        atomicMax(A.trace + 2 * (A.trace_slot + 10), (unsigned long long)(dc1 - dc0));
+        atomicMax(A.trace + 2 * (A.trace_slot + 10) + 1, (unsigned long long)(clock64() - dc1));
+    }
     __syncthreads();
     trace_end(A, 2);
 }
@@ -501,8 +597,8 @@ using GUFn = void (*)(DecodeArgs);
 static GUFn gateup_fn(int ty, int nb) {
     if (ty == T_Q4_K) switch (nb) {
             case 4: return k_gateup_dec<T_Q4_K, 4>;
-            case 8: return k_gateup_dec<T_Q4_K, 8>;
-            case 16: return k_gateup_dec<T_Q4_K, 16>;
+            case 8: return k_gateup_dec<T_Q4_KW, 8>;
+            case 16: return k_gateup_dec<T_Q4_KW, 16>;
             case 28: return k_gateup_dec<T_Q4_K, 28>;
         }
     if (ty == T_Q6_K && nb == 8) return k_gateup_dec<T_Q6_K, 8>;
@@ -515,13 +611,12 @@ static GUFn down_fn(int ty, int nb, int nbsh) {
             case 2: return k_down_dec<T_Q6_K, 8, 2, 0>;
             case 3: return k_down_dec<T_Q6_K, 8, 3, 0>;
             case 4: return k_down_dec<T_Q6_K, 8, 4, 0>;
-            case 8: return k_down_dec<T_Q6_K, 8, 8, 0>;
         }
     if (ty == T_Q4_K) {  // 4 experts per chunk, stream-major units
         if (nb == 4 && nbsh == 0) return k_down_dec<T_Q4_K, 4, 4, 0>;
         if (nb == 4 && nbsh == 4) return k_down_dec<T_Q4_K, 4, 4, 4>;
-        if (nb == 8 && nbsh == 0) return k_down_dec<T_Q4_K, 4, 8, 0>;
-        if (nb == 8 && nbsh == 8) return k_down_dec<T_Q4_K, 4, 8, 8>;
+        if (nb == 8 && nbsh == 0) return k_down_dec<T_Q4_KW, 4, 8, 0>;
+        if (nb == 8 && nbsh == 8) return k_down_dec<T_Q4_KW, 4, 8, 8>;
     }
     return nullptr;
 }
@@ -544,28 +639,64 @@ bool decode_supported(const DecodeArgs &A) {
     }
     if (!down_fn(dty, A.ffn / block_elems(dty), shared_nb(A))) return false;
     const size_t max_ffn = A.has_shared && A.shexp_ffn > A.ffn ? A.shexp_ffn : A.ffn;
-    return down_smem(A) <= 48 * 1024 && (size_t)(A.dim + 2 * A.n_expert + 128) * 4 <= 48 * 1024 &&
+    return down_smem(A) <= 48 * 1024 && (size_t)(A.dim + 2 * A.n_expert + 136) * 4 <= 48 * 1024 &&
            max_ffn * 4 <= 48 * 1024;
 }
 
+// Router cluster shape for the TMA variant: 16 CTAs when the device can place
+// a 16-CTA cluster (non-portable size), else 8; 0 when the rows do not fit.
+static int tma_cluster(const DecodeArgs &A, size_t &smem) {
+    static int c16 = -1, ok = 0;
+    if (c16 < 0) {
+        c16 = 0;
+        ok = cudaFuncSetAttribute(k_router_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess;
+        if (ok && cudaFuncSetAttribute(k_router_tma, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(16);
+            cfg.blockDim = dim3(RR2_WARPS * 32);
+            cfg.dynamicSmemBytes = 96 * 1024;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 16;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, k_router_tma, &cfg) == cudaSuccess && n > 0) c16 = 1;
+        }
+        cudaGetLastError();
+    }
+    if (!ok) return 0;
+    for (int c : {c16 ? 16 : 8, 8}) {
+        const int rpc = (A.n_expert + c - 1) / c;
+        smem = ((size_t)rpc * A.dim + A.dim + 2 * A.n_expert + 136) * 4;
+        if (A.dim % 4 == 0 && smem <= 200 * 1024) return c;
+    }
+    return 0;
+}
+
 static cudaError_t launch_router(const DecodeArgs &A, cudaStream_t st) {
-    const size_t smem = (size_t)(A.dim + 2 * A.n_expert + 128) * 4;
+    size_t smem = 0;
+    const int tc = (A.router && !A.trace_reg) ? tma_cluster(A, smem) : 0;
+    if (!tc) smem = (size_t)(A.dim + 2 * A.n_expert + 136) * 4;
+    const int cl = tc ? tc : (A.router ? RR_CLUSTER : 1);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(A.router ? RR_CLUSTER : 1, A.T);
-    cfg.blockDim = dim3(RR_WARPS * 32);
+    cfg.gridDim = dim3(cl, A.T);
+    cfg.blockDim = dim3((tc ? RR2_WARPS : RR_WARPS) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = A.router ? RR_CLUSTER : 1;
+    attr[1].val.clusterDim.x = cl;
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     count_launch();
-    return cudaLaunchKernelEx(&cfg, k_router_route, A);
+    return cudaLaunchKernelEx(&cfg, tc ? k_router_tma : k_router_route, A);
 }
 
 cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
@@ -586,8 +717,8 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st) {
     }
     // 3. down + combine
     {
-        const dim3 grid(cdivu(A.dim, DN_WARPS), A.T);
-        e = launch_pdl(down_fn(A.dn.type, A.ffn / block_elems(A.dn.type), shared_nb(A)), grid, dim3(DN_WARPS * 32),
+        const dim3 grid(cdivu(A.dim, DND_WARPS), A.T);
+        e = launch_pdl(down_fn(A.dn.type, A.ffn / block_elems(A.dn.type), shared_nb(A)), grid, dim3(DND_WARPS * 32),
                        down_smem(A), st, A);
         if (e != cudaSuccess) return e;
     }
@@ -781,8 +912,8 @@ __global__ void __launch_bounds__(256) k_combine(DecodeArgs A) {
 static GUFn gateup_grp_fn(int ty, int nb) {
     if (ty == T_Q4_K) switch (nb) {
             case 4: return k_gateup_grp<T_Q4_K, 4>;
-            case 8: return k_gateup_grp<T_Q4_K, 8>;
-            case 16: return k_gateup_grp<T_Q4_K, 16>;
+            case 8: return k_gateup_grp<T_Q4_KW, 8>;
+            case 16: return k_gateup_grp<T_Q4_KW, 16>;
             case 28: return k_gateup_grp<T_Q4_K, 28>;
         }
     if (ty == T_Q6_K && nb == 8) return k_gateup_grp<T_Q6_K, 8>;
@@ -806,7 +937,7 @@ static GUFn down_grp_fn(int ty, int nb, int &rs) {
         rs = 4;
         switch (nb) {
             case 4: return k_down_grp<T_Q4_K, 4, 4>;
-            case 8: return k_down_grp<T_Q4_K, 4, 8>;
+            case 8: return k_down_grp<T_Q4_KW, 4, 8>;
         }
     }
     return nullptr;
@@ -823,7 +954,7 @@ bool batch_supported(const DecodeArgs &A) {
         if (A.sg.type != A.g.type || A.su.type != A.g.type || A.sdn.type != dty) return false;
         if (A.shexp_ffn != A.ffn) return false;  // the shared expert reuses the routed instantiation
     }
-    return (size_t)(A.dim + 2 * A.n_expert + 128) * 4 <= 48 * 1024;
+    return (size_t)(A.dim + 2 * A.n_expert + 136) * 4 <= 48 * 1024;
 }
 
 cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st) {

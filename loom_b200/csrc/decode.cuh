@@ -45,6 +45,8 @@ struct DecodeArgs {
     int *grp_off;            // [n_local] first position in grp_list
     int *grp_list;           // [T*n_used] routed slots, grouped by expert, slot order within a group
     float *y;                // [n_slots][dim] per-slot down outputs
+    int trace_reg;           // test hook: use the register-staged router instead of the TMA one
+    int *err;                // device error word (bounded waits that timed out), or null
     const uint8_t *next_router;   // optional: the next layer's router weights, prefetched into L2
     size_t next_router_bytes;
     unsigned long long *trace;  // optional [2*k] (first start, last end) globaltimer ns per kernel, or null

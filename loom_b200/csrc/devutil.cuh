@@ -166,16 +166,90 @@ __device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int ga
     __syncwarp();
 }
 
-// moe.zig:106-158 route by one warp.
-__device__ __forceinline__ void route_warp(const float *logits, const float *bias, int ne, int nk, int gating,
-                                           int weights_norm, float weights_scale, float *scores, float *choice,
-                                           int *ids_out, float *gates_out, int *ids, float *gates, int lane) {
-    const bool ranked = route_scores(logits, bias, ne, gating, scores, choice, lane) && ne <= 1024;
-    __syncwarp();
-    if (ranked) route_rank(scores, choice, ne, nk, ids, gates, lane, 32);
-    __syncwarp();
-    route_finish(ranked, ne, nk, gating, weights_norm, weights_scale, scores, choice, ids, gates, ids_out, gates_out,
-                 lane);
+// moe.zig:106-158 route by the first ROUTE_THREADS threads of a CTA (the
+// other warps may run other work meanwhile: this code synchronizes with named
+// barrier 1 over these threads only). logits may alias choice. red: 8 floats
+// of shared memory.
+constexpr int ROUTE_THREADS = 128;
+
+__device__ __forceinline__ void route_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void route_block(const float *logits, const float *bias, int ne, int nk, int gating,
+                                            int weights_norm, float weights_scale, float *scores, float *choice,
+                                            int *ids, float *gates, float *red, int *ids_out, float *gates_out) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = ROUTE_THREADS / 32;
+    if (gating == 2) {
+        for (int e = tid; e < ne; e += ROUTE_THREADS) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
+    } else if (gating == 1) {
+        float m = -INFINITY;
+        for (int e = tid; e < ne; e += ROUTE_THREADS) m = fmaxf(m, logits[e]);
+        m = warp_max(m);
+        if (lane == 0) red[warp] = m;
+        route_bar();
+        m = red[0];
+#pragma unroll
+        for (int w = 1; w < NW; w++) m = fmaxf(m, red[w]);
+        float sum = 0.0f;
+        for (int e = tid; e < ne; e += ROUTE_THREADS) {
+            const float v = expf(fsub(logits[e], m));
+            scores[e] = v;
+            sum = fadd(sum, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum = fadd(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        route_bar();  // everyone has read red[] as the max
+        if (lane == 0) red[warp] = sum;
+        route_bar();
+        float tot = red[0];
+#pragma unroll
+        for (int w = 1; w < NW; w++) tot = fadd(tot, red[w]);
+        const float inv = fdiv(1.0f, tot);
+        for (int e = tid; e < ne; e += ROUTE_THREADS) scores[e] = fmul(scores[e], inv);
+    } else {
+        for (int e = tid; e < ne; e += ROUTE_THREADS) scores[e] = logits[e];
+    }
+    bool fin = true;
+    for (int e = tid; e < ne; e += ROUTE_THREADS) {
+        const float c = bias ? fadd(scores[e], bias[e]) : scores[e];
+        choice[e] = c;
+        fin &= c > -INFINITY;
+    }
+    fin = __all_sync(0xffffffffu, fin);
+    route_bar();  // red[] free again, choice complete
+    if (lane == 0) red[warp] = fin ? 1.0f : 0.0f;
+    route_bar();
+    bool ranked = ne % 4 == 0;
+#pragma unroll
+    for (int w = 0; w < NW; w++) ranked &= red[w] != 0.0f;
+    if (ranked) {
+        // the rank of e is the number of experts the serial scan takes before
+        // it (greater value, or equal value and lower index); with every value
+        // > -inf this is exactly the serial first-max order
+        const float4 *c4 = reinterpret_cast<const float4 *>(choice);
+        for (int e = tid; e < ne; e += ROUTE_THREADS) {
+            const float c = choice[e];
+            int rank = 0;
+#pragma unroll 8
+            for (int j4 = 0; j4 < ne / 4; j4++) {
+                const float4 v = c4[j4];
+                const int j = 4 * j4;
+                rank += (v.x > c) | ((v.x == c) & (j < e));
+                rank += (v.y > c) | ((v.y == c) & (j + 1 < e));
+                rank += (v.z > c) | ((v.z == c) & (j + 2 < e));
+                rank += (v.w > c) | ((v.w == c) & (j + 3 < e));
+            }
+            if (rank < nk) {
+                ids[rank] = e;
+                gates[rank] = scores[e];
+            }
+        }
+    }
+    route_bar();
+    if (warp == 0)
+        route_finish(ranked, ne, nk, gating, weights_norm, weights_scale, scores, choice, ids, gates, ids_out,
+                     gates_out, lane);
+    route_bar();
 }
 
 }  // namespace loom

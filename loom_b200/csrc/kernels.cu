@@ -340,20 +340,24 @@ void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok
 // top-k is k rounds of a warp arg-max that keeps the lowest index on ties and
 // never selects a value that is not > -inf (the serial scan's strict '>').
 
-__global__ void k_route(const float *logits, const float *bias, int ne, int nk, int gating, int weights_norm,
-                        float weights_scale, int *ids, float *gates) {
-    extern __shared__ float sm[];
+__global__ void __launch_bounds__(ROUTE_THREADS) k_route(const float *logits, const float *bias, int ne, int nk,
+                                                         int gating, int weights_norm, float weights_scale, int *ids,
+                                                         float *gates) {
+    extern __shared__ float sm[];  // scores[ne] | choice[ne] | ids[64] | gates[64] | red[8]
     const int t = blockIdx.x;
-    route_warp(logits + (size_t)t * ne, bias, ne, nk, gating, weights_norm, weights_scale, sm, sm + ne,
-               ids + (size_t)t * nk, gates + (size_t)t * nk, reinterpret_cast<int *>(sm + 2 * ne), sm + 2 * ne + 64,
-               threadIdx.x);
+    float *choice = sm + ne;
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = logits[(size_t)t * ne + e];
+    __syncthreads();
+    route_block(choice, bias, ne, nk, gating, weights_norm, weights_scale, sm, choice,
+                reinterpret_cast<int *>(sm + 2 * ne), sm + 2 * ne + 64, sm + 2 * ne + 128, ids + (size_t)t * nk,
+                gates + (size_t)t * nk);
 }
 
 void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating, int weights_norm,
                   float weights_scale, int *ids, float *gates, cudaStream_t st) {
     if (T == 0) return;
-    k_route<<<T, 32, (2 * n_expert + 128) * sizeof(float), st>>>(logits, bias, n_expert, n_used, gating, weights_norm,
-                                                         weights_scale, ids, gates);
+    k_route<<<T, ROUTE_THREADS, (2 * n_expert + 136) * sizeof(float), st>>>(logits, bias, n_expert, n_used, gating,
+                                                                            weights_norm, weights_scale, ids, gates);
     count_launch();
 }
 

@@ -248,7 +248,7 @@ int ensure_moe_scratch(size_t T, size_t dim, size_t max_ffn, size_t n_expert, si
     if (int rc = S.aq.ensure(n_slots * act_stride)) return rc;
     if (int rc = S.ad.ensure(n_slots * act_stride / 32 * 4 + 64)) return rc;
     if (int rc = S.as.ensure(n_slots * act_stride / 16 * 4 + 64)) return rc;
-    if (int rc = S.counters.ensure((T + n_slots) * 4, true)) return rc;
+    if (int rc = S.counters.ensure((T + n_slots + 1) * 4, true)) return rc;
     return 0;
 }
 
@@ -338,6 +338,7 @@ DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, c
     A.ids_out = d_ids_out;
     A.cnt_tok = S.counters.as<int>();
     A.cnt_slot = S.counters.as<int>() + T;
+    A.err = S.counters.as<int>() + T + (T * L.n_used + (L.has_shared ? T : 0));
     A.x256 = XQW{S.xq256_q.as<int8_t>(), S.xq256_d.as<float>(), S.xq256_s.as<int32_t>()};
     A.x32 = XQW{S.xq32_q.as<int8_t>(), S.xq32_d.as<float>(), S.xq32_s.as<int32_t>()};
     A.need256 = any_type(L, true);
@@ -357,10 +358,10 @@ DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, c
     A.act_stride = (int)act_stride;
     A.next_router = g_next_router;
     A.next_router_bytes = g_next_router_bytes;
-    if (g_trace && g_trace_next + 8 <= g_trace_cap) {
+    if (g_trace && g_trace_next + 12 <= g_trace_cap) {
         A.trace = g_trace;
         A.trace_slot = (int)g_trace_next;
-        g_trace_next += 8;
+        g_trace_next += 12;
     }
     return A;
 }
@@ -543,8 +544,8 @@ int loom_cuda_trace_reset(void) {
     if (int rc = need_init()) return rc;
     if (!g_trace) return decline("tracing is off");
     std::vector<unsigned long long> init(2 * g_trace_cap);
-    for (size_t i = 0; i < g_trace_cap; i++) {
-        init[2 * i] = ~0ull;
+    for (size_t i = 0; i < g_trace_cap; i++) {  // per layer: 7 (start, end) spans, then 5 cycle-count pairs
+        init[2 * i] = i % 12 < 7 ? ~0ull : 0;
         init[2 * i + 1] = 0;
     }
     CK(cudaMemcpy(g_trace, init.data(), init.size() * 8, cudaMemcpyHostToDevice));
@@ -557,6 +558,17 @@ size_t loom_cuda_trace_read(uint64_t *out, size_t n_kernels) {
     if (cudaStreamSynchronize(g_stream) != cudaSuccess) return 0;
     if (cudaMemcpy(out, g_trace, n * 16, cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
     return n;
+}
+
+int loom_cuda_device_error(void) {
+    if (!g_inited || !S.counters.p) return 0;
+    int v = 0;
+    // the error word sits after the counters of the last layer shape reserved
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) return -1;
+    std::vector<int> all(S.counters.cap / 4);
+    if (cudaMemcpy(all.data(), S.counters.p, all.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    for (int x : all) v |= x;
+    return v;
 }
 
 int loom_cuda_force_generic(int on) {

@@ -79,6 +79,60 @@ template <> struct QT<T_Q4_K> {
     }
 };
 
+// Q4_K with 32 bytes of nibbles per lane (4 lanes per super-block): half the
+// reduction and bookkeeping instructions per weight byte of the 8-lane form.
+// Used where the unit mapping allows G = 8.
+constexpr int T_Q4_KW = 112;
+
+template <> struct QT<T_Q4_KW> {
+    static constexpr int LPB = 4, BE = 256, SPB = 16;
+    struct Frag {
+        uint4 h, q0, q1;
+    };
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int sub) {
+        const uint8_t *blk = w.q + gb * 144;
+        return Frag{ld_stream_v4(blk), ld_stream_v4(blk + 16 + 32 * sub), ld_stream_v4(blk + 32 + 32 * sub)};
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int j, const int8_t *xq, const int32_t *xs, int &I,
+                                                int &M) {
+        const int4 *x4 = reinterpret_cast<const int4 *>(xq + 64 * j);
+        const int4 l0 = x4[0], l1 = x4[1], h0 = x4[2], h1 = x4[3];
+        int dl = 0, dh = 0;
+        dl = dp4a((int)(f.q0.x & 0x0F0F0F0Fu), l0.x, dl);
+        dl = dp4a((int)(f.q0.y & 0x0F0F0F0Fu), l0.y, dl);
+        dl = dp4a((int)(f.q0.z & 0x0F0F0F0Fu), l0.z, dl);
+        dl = dp4a((int)(f.q0.w & 0x0F0F0F0Fu), l0.w, dl);
+        dl = dp4a((int)(f.q1.x & 0x0F0F0F0Fu), l1.x, dl);
+        dl = dp4a((int)(f.q1.y & 0x0F0F0F0Fu), l1.y, dl);
+        dl = dp4a((int)(f.q1.z & 0x0F0F0F0Fu), l1.z, dl);
+        dl = dp4a((int)(f.q1.w & 0x0F0F0F0Fu), l1.w, dl);
+        dh = dp4a((int)((f.q0.x >> 4) & 0x0F0F0F0Fu), h0.x, dh);
+        dh = dp4a((int)((f.q0.y >> 4) & 0x0F0F0F0Fu), h0.y, dh);
+        dh = dp4a((int)((f.q0.z >> 4) & 0x0F0F0F0Fu), h0.z, dh);
+        dh = dp4a((int)((f.q0.w >> 4) & 0x0F0F0F0Fu), h0.w, dh);
+        dh = dp4a((int)((f.q1.x >> 4) & 0x0F0F0F0Fu), h1.x, dh);
+        dh = dp4a((int)((f.q1.y >> 4) & 0x0F0F0F0Fu), h1.y, dh);
+        dh = dp4a((int)((f.q1.z >> 4) & 0x0F0F0F0Fu), h1.z, dh);
+        dh = dp4a((int)((f.q1.w >> 4) & 0x0F0F0F0Fu), h1.w, dh);
+        // scaleMinK4 (ggml.zig:1332) for sub-blocks 2j, 2j+1, without divergence
+        const int sh = 16 * (j & 1);
+        const uint32_t a = f.h.y >> sh, b = f.h.z >> sh, lo = f.h.w >> sh;
+        const bool low = j < 2;
+        const int sc0 = low ? (a & 63) : ((lo & 0xF) | (((a >> 6) & 3) << 4));
+        const int mn0 = low ? (b & 63) : (((lo >> 4) & 0xF) | (((b >> 6) & 3) << 4));
+        const int sc1 = low ? ((a >> 8) & 63) : (((lo >> 8) & 0xF) | (((a >> 14) & 3) << 4));
+        const int mn1 = low ? ((b >> 8) & 63) : (((lo >> 12) & 0xF) | (((b >> 14) & 3) << 4));
+        const int4 bs = *reinterpret_cast<const int4 *>(xs + 4 * j);
+        I = sc0 * dl + sc1 * dh;
+        M = mn0 * (bs.x + bs.y) + mn1 * (bs.z + bs.w);
+    }
+    __device__ __forceinline__ static float term(const Frag &f, int I, int M, float xd) {
+        const float d = f16_to_f32((uint16_t)(f.h.x & 0xFFFF));
+        const float dmin = f16_to_f32((uint16_t)(f.h.x >> 16));
+        return fmul(xd, fsub(fmul(d, (float)I), fmul(dmin, (float)M)));
+    }
+};
+
 template <> struct QT<T_Q6_K> {
     static constexpr int LPB = 4, BE = 256, SPB = 16;
     struct Frag {
@@ -318,7 +372,7 @@ template <int TY, int S, int NB> struct CEng {
 #pragma unroll
             for (int o = 1; o < Q::LPB; o <<= 1) {
                 I += __shfl_xor_sync(0xffffffffu, I, o);
-                if constexpr (TY == T_Q4_K) M += __shfl_xor_sync(0xffffffffu, M, o);
+                if constexpr (TY == T_Q4_K || TY == T_Q4_KW) M += __shfl_xor_sync(0xffffffffu, M, o);
             }
             term[j] = Q::term(fr.f[j], I, M, xv.d[b]);
         }

@@ -196,6 +196,8 @@ def test_decode_kernels_bitexact_with_slot_kernels(be, orc, cfg, T):
             idss.append(ids.cpu().numpy())
         finally:
             D.force_generic(prev)
+    from loom_b200 import _lib
+    assert _lib.lib().loom_cuda_device_error() == 0  # no bounded wait gave up
     for i in (1, 2):
         assert np.array_equal(idss[0], idss[i])
         assert np.array_equal(bits(outs[0]), bits(outs[i])), i
