@@ -47,11 +47,12 @@ Q4K, Q6K, F32 = 12, 14, 0
 METRIC = "decode tok/s (Qwen3-30B-A3B MoE stack, Q4_K/Q6_K, T=1)"
 
 
-def layer_bytes_model(T_ids: np.ndarray) -> int:
+def layer_bytes_model(T_ids: np.ndarray, e0: int = 0, nl: int = NE) -> int:
     """Algorithmic HBM bytes of one layer: router + every distinct selected
-    expert's gate/up/down plane once + activations in/out."""
+    expert's gate/up/down plane once (those held in [e0, e0+nl)) + activations."""
     plane = 2 * FFN * (DIM // 256) * 144 + DIM * (FFN // 256) * 210
-    n_distinct = len(np.unique(T_ids))
+    u = np.unique(T_ids)
+    n_distinct = int(np.sum((u >= e0) & (u < e0 + nl)))
     T = T_ids.shape[0]
     return NE * DIM * 4 + n_distinct * plane + T * DIM * 4 * 3
 
@@ -65,45 +66,43 @@ def peaks():
 
 
 class Clocks:
-    """Samples nvidia-smi during the timed region."""
+    """Samples the SM clock and the throttle reasons during the timed region
+    (NVML every 2 ms; nvidia-smi every 100 ms when NVML is unavailable)."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, gpu: int):
-        self.gpu, self.samples, self.proc = gpu, [], None
+        self.gpu, self.samples, self.stop = gpu, [], threading.Event()
 
     def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop.is_set():
+                    self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                         pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    time.sleep(0.002)
+            self.t = threading.Thread(target=poll, daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception:  # noqa: BLE001 -- clocks are reported, never required
+            self.max = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.samples.append([s.strip() for s in line.split(",")])
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if hasattr(self, "t"):
+            self.t.join(timeout=1)
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > i + 2 and s[i + 2] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max, "reasons": ["unsampled"]}
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max, "reasons": reasons,
+                "samples": len(self.samples)}
 
 
 def dist_env():
@@ -171,17 +170,21 @@ def run_reference(args):
 
 # ---- GPU path ----------------------------------------------------------------------
 
-def build_model(T: int, seed_base: int = 1000):
+def build_model(T: int, seed_base: int = 1000, e0: int = 0, nl: int = NE):
+    """The 48 layers; with expert parallelism only experts [e0, e0+nl) of each
+    layer are generated (the same bytes the full model holds there)."""
     from loom_b200.device import DeviceTensor, MoeLayer
+    pg, pd = FFN * DIM // 256, DIM * FFN // 256  # blocks per expert plane
     layers = []
     for l in range(LAYERS):
         s = seed_base + l
         layers.append(MoeLayer(
             DIM, FFN, NE, NK,
-            gate=DeviceTensor.synth(Q4K, NE * FFN * DIM // 256, s * 10 + 1),
-            up=DeviceTensor.synth(Q4K, NE * FFN * DIM // 256, s * 10 + 2),
-            down=DeviceTensor.synth(Q6K, NE * DIM * FFN // 256, s * 10 + 3),
-            router=DeviceTensor.synth(F32, NE * DIM, s * 10 + 4, sigma=0.02)))
+            gate=DeviceTensor.synth_range(Q4K, e0 * pg, nl * pg, s * 10 + 1),
+            up=DeviceTensor.synth_range(Q4K, e0 * pg, nl * pg, s * 10 + 2),
+            down=DeviceTensor.synth_range(Q6K, e0 * pd, nl * pd, s * 10 + 3),
+            router=DeviceTensor.synth(F32, NE * DIM, s * 10 + 4, sigma=0.02),
+            expert0=e0, n_local=nl))
     return layers
 
 
@@ -197,13 +200,18 @@ def run_gpu(args):
     torch.cuda.set_device(local)
     B.init(local)
     T = args.tokens
-    layers = build_model(T)
+    ep = args.ep and world > 1
+    e0, nl = D.expert_range(NE, rank, world) if ep else (0, NE)
+    if ep:
+        D.ep_init(rank, world, dist)
+    layers = build_model(T, e0=e0, nl=nl)
     for l in range(LAYERS - 1):
         layers[l].next_router = layers[l + 1].router  # prefetch hint
     D.reserve(T, DIM, FFN, NE, NK)
     descs = [L.desc() for L in layers]
     stream = torch.cuda.Stream()
-    x0 = torch.from_numpy(np.random.default_rng(rank).standard_normal((T, DIM)).astype(np.float32)).cuda()
+    # replicas decode independent streams; expert-parallel ranks share one stream
+    x0 = torch.from_numpy(np.random.default_rng(0 if ep else rank).standard_normal((T, DIM)).astype(np.float32)).cuda()
     bufs = [torch.empty((T, DIM), device="cuda") for _ in range(2)]
     ids = torch.zeros((LAYERS, T, NK), dtype=torch.int32, device="cuda")
 
@@ -244,15 +252,20 @@ def run_gpu(args):
         ms = float(t.item())
         dist.barrier()
     ids_np = ids.cpu().numpy()
-    bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1)) for l in range(LAYERS))
+    if ep:  # this rank's bytes: router + its own selected experts + activations
+        bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1), e0, nl) for l in range(LAYERS))
+    else:
+        bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1)) for l in range(LAYERS))
     achieved = bytes_step / (ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
-    value = world * T / (ms * 1e-3)
+    value = (T if ep else world * T) / (ms * 1e-3)
 
     # e2e through the seam with host buffers
     e2e = None
-    if args.e2e_layers > 0:
+    if args.e2e_layers > 0 and not ep:
         e2e = run_e2e(args, B)
+    elif ep:
+        e2e = run_e2e_device(args, g, stream, x0, bufs[(LAYERS - 1) % 2], torch, dist, world)
 
     if rank != 0:
         return
@@ -264,11 +277,13 @@ def run_gpu(args):
                "sample": f"1 token x 2 sampled layers x 3 reps, extrapolated to {LAYERS} layers"}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong" if ep else "weak",
         "vs_baseline": None, "dtype": "int8xq4/q6 (f32 accum)", "data": "synthetic (seeded generator), random-init weights",
         "config": {"workload": f"qwen3-30b-a3b moe stack decode, T={T}, {LAYERS} layers", "tokens": T,
                    "layers": LAYERS, "n_expert": NE, "n_used": NK, "dim": DIM, "ffn": FFN,
-                   "parallelism": f"replicas x{world}" if world > 1 else "1 gpu",
+                   "parallelism": (f"ep{world} (experts sharded, NCCL all-reduce combine)" if ep else
+                                   f"replicas x{world}" if world > 1 else "1 gpu"),
                    "l2": "inputs > L2 (48 distinct layers, ~1.2 GB touched per token)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
@@ -321,6 +336,39 @@ def trace_phases(D, step, stream, torch):
                    "down_dots": float(np.median(L[:, 10, 1]))},
         "unit": "us after the previous layer's down end",
     }
+
+
+def run_e2e_device(args, g, stream, x0, out, torch, dist, world):
+    """End to end through the device-resident API: every step copies the
+    token's activation in from pinned host memory, replays the step and reads
+    the final output back."""
+    hx = torch.empty(x0.shape, dtype=torch.float32, pin_memory=True)
+    hx.copy_(x0.cpu())
+    ho = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            x0.copy_(hx, non_blocking=True)
+            g.replay()
+            ho.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            x0.copy_(hx, non_blocking=True)
+            g.replay()
+            ho.copy_(out, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    T = x0.shape[0]
+    return {"value": round(T / (ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": int(hx.numel() * 4),
+            "d2h_bytes_per_step": int(ho.numel() * 4), "path": "device API with pinned host input/output per step"}
 
 
 def run_e2e(args, B):
@@ -377,6 +425,9 @@ def main():
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--trace", action="store_true", help="add per-kernel phase times (one extra traced replay)")
+    ap.add_argument("--ep", action="store_true",
+                    help="with torchrun: shard each layer's experts over the ranks (expert parallel) instead of "
+                         "running independent replicas")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers in the stack (default 48; smaller only for profiling captures)")
     args = ap.parse_args()

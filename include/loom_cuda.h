@@ -140,6 +140,10 @@ int loom_cuda_tensor_upload(int ggml_type, const void *data, size_t bytes, loom_
  * (the synthetic-weight generator the benchmarks use; sigma is the f32
  * standard deviation). */
 int loom_cuda_tensor_synth(int ggml_type, uint64_t nblocks, uint64_t seed, float sigma, loom_tensor *out);
+/* The same generator for blocks [blk0, blk0 + nblocks) of a larger tensor
+ * (an expert-parallel rank's slice of a 3D expert tensor). */
+int loom_cuda_tensor_synth_range(int ggml_type, uint64_t blk0, uint64_t nblocks, uint64_t seed, float sigma,
+                                 loom_tensor *out);
 /* Read a tensor back as GGUF bytes (bytes = nblocks * block bytes). */
 int loom_cuda_tensor_download(loom_tensor t, void *dst, size_t bytes);
 int loom_cuda_tensor_free(loom_tensor t);
@@ -192,6 +196,20 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
 #define LOOM_CUDA_NOALLOC_SCRATCH_BYTES (1u << 20)
 int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
                                   const float *d_residual, void *stream);
+/* ---- expert parallelism (no counterpart in the reference: its experts never
+ * leave one node's CPU/GPU; this is the north star's expert-parallel mode over
+ * NVLink) -------------------------------------------------------------------
+ * One process per GPU. Rank 0 creates an id, every rank passes it to
+ * loom_cuda_ep_init. After that, loom_cuda_moe_forward on a descriptor whose
+ * expert range [expert0, expert0+n_local) is a strict subset of the experts
+ * computes this rank's partial output and sums the ranks' partials with an
+ * NCCL all-reduce on the same stream (the residual is added on rank 0 only),
+ * so every rank ends with the full layer output. */
+int loom_cuda_ep_unique_id(void *out, size_t bytes);
+int loom_cuda_ep_init(int nranks, int rank, const void *id, size_t bytes);
+void loom_cuda_ep_shutdown(void);
+int loom_cuda_ep_rank(void);
+int loom_cuda_ep_size(void);
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);

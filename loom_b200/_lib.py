@@ -82,6 +82,7 @@ def lib() -> C.CDLL:
         "loom_cuda_moe_ffn_routed": (i, [vp, sz, vp, vp, Weight, Weight, Weight, vp, sz, sz, RoutedCfg, vp]),
         "loom_cuda_tensor_upload": (i, [i, vp, sz, C.POINTER(u64)]),
         "loom_cuda_tensor_synth": (i, [i, u64, u64, f, C.POINTER(u64)]),
+        "loom_cuda_tensor_synth_range": (i, [i, u64, u64, u64, f, C.POINTER(u64)]),
         "loom_cuda_tensor_download": (i, [u64, vp, sz]),
         "loom_cuda_tensor_free": (i, [u64]),
         "loom_cuda_tensor_device_bytes": (sz, [u64]),
@@ -92,6 +93,11 @@ def lib() -> C.CDLL:
         "loom_cuda_sync": (i, []),
         "loom_cuda_force_generic": (i, [i]),
         "loom_cuda_device_error": (i, []),
+        "loom_cuda_ep_unique_id": (i, [vp, sz]),
+        "loom_cuda_ep_init": (i, [i, i, vp, sz]),
+        "loom_cuda_ep_shutdown": (None, []),
+        "loom_cuda_ep_rank": (i, []),
+        "loom_cuda_ep_size": (i, []),
         "loom_cuda_trace_enable": (i, [sz]),
         "loom_cuda_trace_reset": (i, []),
         "loom_cuda_trace_read": (sz, [vp, sz]),

@@ -15,6 +15,7 @@
 
 #include "../../include/loom_cuda.h"
 #include "decode.cuh"
+#include "ep.cuh"
 #include "kernels.cuh"
 
 using namespace loom;
@@ -785,13 +786,17 @@ int loom_cuda_tensor_upload(int type, const void *data, size_t bytes, loom_tenso
 }
 
 int loom_cuda_tensor_synth(int type, uint64_t nblk, uint64_t seed, float sigma, loom_tensor *out) {
+    return loom_cuda_tensor_synth_range(type, 0, nblk, seed, sigma, out);
+}
+
+int loom_cuda_tensor_synth_range(int type, uint64_t blk0, uint64_t nblk, uint64_t seed, float sigma, loom_tensor *out) {
     if (int rc = need_init()) return rc;
     if (!type_ok(type)) return decline("unsupported ggml type");
     Tensor t;
     if (int rc = alloc_tensor(type, nblk, t)) return rc;
     const size_t bb = block_bytes(type);
     if (type == T_F32 || type == T_Q4_K) {
-        launch_synth(type, t.base, 0, nblk, seed, sigma, g_stream);
+        launch_synth(type, t.base, blk0, nblk, seed, sigma, g_stream);
     } else {
         // generate GGUF bytes in bounded chunks, then repack each into the layout
         const uint64_t chunk = std::max<uint64_t>(1, (256ull << 20) / bb);
@@ -801,7 +806,7 @@ int loom_cuda_tensor_synth(int type, uint64_t nblk, uint64_t seed, float sigma, 
         }
         for (uint64_t b0 = 0; b0 < nblk; b0 += chunk) {
             const uint64_t nb = std::min(chunk, nblk - b0);
-            launch_synth(type, S.raw.as<uint8_t>(), b0, nb, seed, sigma, g_stream);
+            launch_synth(type, S.raw.as<uint8_t>(), blk0 + b0, nb, seed, sigma, g_stream);
             uint8_t *q = t.base + b0 * layout_qbytes(type);
             uint8_t *sc = t.w.sc ? const_cast<uint8_t *>(t.w.sc) + b0 * 16 : nullptr;
             uint16_t *d = t.w.d ? const_cast<uint16_t *>(t.w.d) + b0 : nullptr;
@@ -916,9 +921,15 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
             g_next_router_bytes = nr->nblk * 4;
         }
     }
-    const int rc = moe_routed_dev(L, T, router, d_x, d_logits, bias, d_out, d_residual, d_ids, st);
+    // expert parallel: this rank's partial, then the sum over ranks (residual once)
+    const bool sharded = ep_active() && n_local < D.n_expert;
+    const float *res = sharded && ep_rank() != 0 ? nullptr : d_residual;
+    const int rc = moe_routed_dev(L, T, router, d_x, d_logits, bias, d_out, res, d_ids, st);
     g_next_router = nullptr;
     if (rc) return rc;
+    if (sharded) {
+        if (int e = ep_allreduce_sum(d_out, T * D.dim, st, g_err)) return e;
+    }
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;
 }

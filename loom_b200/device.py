@@ -38,6 +38,13 @@ class DeviceTensor:
         _lib.must(_lib.lib().loom_cuda_tensor_synth(ty, nblk, seed, sigma, C.byref(h)), "tensor_synth")
         return cls(h.value, ty, nblk)
 
+    @classmethod
+    def synth_range(cls, ty: int, blk0: int, nblk: int, seed: int, sigma: float = 1.0) -> "DeviceTensor":
+        """Blocks [blk0, blk0+nblk) of the seeded tensor (an expert-parallel slice)."""
+        h = C.c_uint64(0)
+        _lib.must(_lib.lib().loom_cuda_tensor_synth_range(ty, blk0, nblk, seed, sigma, C.byref(h)), "tensor_synth_range")
+        return cls(h.value, ty, nblk)
+
     def download(self) -> np.ndarray:
         out = np.empty(self.nblk * BLOCK_BYTES[self.ty], np.uint8)
         _lib.must(_lib.lib().loom_cuda_tensor_download(self.handle, out.ctypes.data_as(C.c_void_p), out.nbytes),
@@ -89,6 +96,26 @@ class MoeLayer:
         rc = _lib.lib().loom_cuda_moe_forward(C.byref(d), _ptr(x), T, _ptr(out), _ptr(residual), _ptr(logits),
                                               _ptr(ids), stream)
         _lib.must(rc, "moe_forward")
+
+
+def ep_init(rank: int, world: int, dist=None) -> None:
+    """Create the backend's NCCL communicator (one process per GPU). The id is
+    made on rank 0 and broadcast with torch.distributed (any backend)."""
+    ident = np.zeros(128, np.uint8)
+    if rank == 0:
+        _lib.must(_lib.lib().loom_cuda_ep_unique_id(ident.ctypes.data_as(C.c_void_p), ident.nbytes), "ep_unique_id")
+    if world > 1:
+        box = [ident.tobytes()]
+        dist.broadcast_object_list(box, src=0)
+        ident = np.frombuffer(box[0], np.uint8).copy()
+    _lib.must(_lib.lib().loom_cuda_ep_init(world, rank, ident.ctypes.data_as(C.c_void_p), ident.nbytes), "ep_init")
+
+
+def expert_range(n_expert: int, rank: int, world: int):
+    """Contiguous expert shard of a rank: (expert0, n_local)."""
+    e0 = rank * n_expert // world
+    e1 = (rank + 1) * n_expert // world
+    return e0, e1 - e0
 
 
 def reserve(T: int, dim: int, ffn: int, n_expert: int, n_used: int) -> None:
