@@ -201,10 +201,10 @@ def run_gpu(args):
     B.init(local)
     T = args.tokens
     ep = args.ep and world > 1
-    e0, nl = D.expert_range(NE, rank, world) if ep else (0, NE)
+    ex0, nloc = D.expert_range(NE, rank, world) if ep else (0, NE)
     if ep:
         D.ep_init(rank, world, dist)
-    layers = build_model(T, e0=e0, nl=nl)
+    layers = build_model(T, e0=ex0, nl=nloc)
     for l in range(LAYERS - 1):
         layers[l].next_router = layers[l + 1].router  # prefetch hint
     D.reserve(T, DIM, FFN, NE, NK)
@@ -253,7 +253,7 @@ def run_gpu(args):
         dist.barrier()
     ids_np = ids.cpu().numpy()
     if ep:  # this rank's bytes: router + its own selected experts + activations
-        bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1), e0, nl) for l in range(LAYERS))
+        bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1), ex0, nloc) for l in range(LAYERS))
     else:
         bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1)) for l in range(LAYERS))
     achieved = bytes_step / (ms * 1e-3) / 1e9
