@@ -215,7 +215,16 @@ def run_gpu(args):
     bufs = [torch.empty((T, DIM), device="cuda") for _ in range(2)]
     ids = torch.zeros((LAYERS, T, NK), dtype=torch.int32, device="cuda")
 
+    stack = None
+    if args.engine == "stack":
+        if T != 1 or ep:
+            raise SystemExit("--engine stack runs the T=1 decode of unsharded layers")
+        stack = D.Stack(layers)
+
     def step(sh):
+        if stack is not None:
+            stack.forward(x0, bufs[(LAYERS - 1) % 2], ids, stream=sh)
+            return
         cur = x0
         for l, L in enumerate(layers):
             nxt = bufs[l % 2]
@@ -245,7 +254,9 @@ def run_gpu(args):
             e1.record(stream)
             torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    phases = trace_phases(D, step, stream, torch) if args.trace else None
+    if stack is not None:
+        assert stack.error() == 0, "stack kernel grid barrier timed out"
+    phases = trace_phases(D, step, stream, torch) if args.trace and stack is None else None
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -284,6 +295,7 @@ def run_gpu(args):
                    "layers": LAYERS, "n_expert": NE, "n_used": NK, "dim": DIM, "ffn": FFN,
                    "parallelism": (f"ep{world} (experts sharded, NCCL all-reduce combine)" if ep else
                                    f"replicas x{world}" if world > 1 else "1 gpu"),
+                   "engine": args.engine,
                    "l2": "inputs > L2 (48 distinct layers, ~1.2 GB touched per token)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
@@ -424,6 +436,8 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--engine", default="layers", choices=["layers", "stack"],
+                    help="layers: per-layer kernels in a CUDA graph; stack: one persistent kernel for all layers (T=1)")
     ap.add_argument("--trace", action="store_true", help="add per-kernel phase times (one extra traced replay)")
     ap.add_argument("--ep", action="store_true",
                     help="with torchrun: shard each layer's experts over the ranks (expert parallel) instead of "

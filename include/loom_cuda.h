@@ -196,6 +196,23 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
 #define LOOM_CUDA_NOALLOC_SCRATCH_BYTES (1u << 20)
 int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
                                   const float *d_residual, void *stream);
+/* A decode step (one token) through a whole stack of MoE layers as ONE
+ * persistent cooperative kernel: x_{l+1} = x_l + MoE_l(x_l) for every layer,
+ * the phases of each layer separated by grid barriers instead of kernel
+ * launches. The layers share one shape and routing configuration (plain
+ * routed layers: no bias, shared expert or expert sharding). prepare uploads
+ * the layer table (outside any stream capture); forward only launches, so it
+ * can be captured in a CUDA graph. Output is bit-identical to running
+ * loom_cuda_moe_forward layer by layer with the residual. d_ids (optional)
+ * receives [n_layers][n_used] expert ids. Engine-level API: no counterpart
+ * in the reference's seam. */
+int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_layers, uint64_t *handle);
+int loom_cuda_stack_forward(uint64_t handle, const float *d_x, float *d_out, uint32_t *d_ids, void *stream);
+/* The stack kernel's device error word (2 = a grid barrier gave up waiting);
+ * synchronizes, and re-arms the barrier after an error. -1 on an unknown handle or a failed stream. */
+int loom_cuda_stack_error(uint64_t handle);
+int loom_cuda_stack_free(uint64_t handle);
+
 /* ---- expert parallelism (no counterpart in the reference: its experts never
  * leave one node's CPU/GPU; this is the north star's expert-parallel mode over
  * NVLink) -------------------------------------------------------------------

@@ -93,6 +93,10 @@ def lib() -> C.CDLL:
         "loom_cuda_sync": (i, []),
         "loom_cuda_force_generic": (i, [i]),
         "loom_cuda_device_error": (i, []),
+        "loom_cuda_stack_prepare": (i, [vp, sz, C.POINTER(u64)]),
+        "loom_cuda_stack_forward": (i, [u64, vp, vp, vp, vp]),
+        "loom_cuda_stack_error": (i, [u64]),
+        "loom_cuda_stack_free": (i, [u64]),
         "loom_cuda_ep_unique_id": (i, [vp, sz]),
         "loom_cuda_ep_init": (i, [i, i, vp, sz]),
         "loom_cuda_ep_shutdown": (None, []),

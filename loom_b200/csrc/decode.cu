@@ -976,4 +976,244 @@ cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st) {
     return launch_pdl(k_combine, dim3(cdivu(A.dim, 256), A.T), dim3(256), 0, st, A);
 }
 
+
+// ==== persistent decode stack ===========================================================
+// One cooperative kernel runs every layer of a T = 1 decode step. Per layer:
+//   P1  router rows spread one per warp over the grid (dotF32 order)     | barrier
+//   P2  every CTA routes (replicated, bit-identical) and quantizes x;
+//       gate/up rows of the selected experts spread over the grid;
+//       each CTA warms L2 with the down rows it will read               | barrier
+//   P3  every CTA quantizes the experts' activations into shared memory;
+//       down rows + ordered combine + residual spread over the grid;
+//       each CTA warms L2 with its router rows of the next layer         | barrier
+// Data written by other CTAs inside the kernel is read through L2 (ld.cg).
+// The arithmetic per element is the decode kernels', so the stack output is
+// bit-identical to running the layers one by one.
+
+constexpr int PS_WARPS = 16;
+constexpr uint32_t BAR_POLLS = 1u << 21;  // bounded grid-barrier wait (~1 s of polling)
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid-wide barrier over gridDim.x co-resident CTAs. Gives up after BAR_POLLS
+// polls, or as soon as another CTA has given up, raising bit 2 of *err; returns
+// false then (the caller leaves the kernel: it never traps or spins forever).
+__device__ __forceinline__ bool grid_barrier(unsigned *bar, int *err) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned gen = ld_acquire_u32(bar + 1);
+        __threadfence();
+        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+            bar[0] = 0;
+            __threadfence();
+            st_release_u32(bar + 1, gen + 1);
+        } else {
+            uint32_t i = 0;
+            for (; i < BAR_POLLS; i++) {
+                if (ld_acquire_u32(bar + 1) != gen) break;
+                if ((i & 1023) == 1023 && ld_acquire_u32(reinterpret_cast<unsigned *>(err)) & 2) i = BAR_POLLS - 1;
+            }
+            if (i >= BAR_POLLS) {
+                atomicOr(err, 2);
+                ok = 0;
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+struct StackDownStreams {  // the token's experts for one output row; activations staged in shared memory
+    WDev wd;
+    const uint64_t *g;
+    const int8_t *aq;
+    const float *ad;
+    const int32_t *as;
+    int stride, k0, nvalid;
+    __device__ __forceinline__ WDev w(int) const { return wd; }
+    __device__ __forceinline__ uint64_t gb(int s) const { return g[s < nvalid ? s : 0]; }
+    __device__ __forceinline__ XV x(int s) const {
+        const int j = k0 + (s < nvalid ? s : 0);
+        return XV{aq + (size_t)j * stride, ad + (size_t)j * (stride / 32), as + (size_t)j * (stride / 16)};
+    }
+    __device__ __forceinline__ void at(int s, WDev &wo, uint64_t &gg, XV &xv) const {
+        wo = wd;
+        gg = gb(s);
+        xv = x(s);
+    }
+};
+
+template <int TYG, int NBG, int TYD, int SC, int NBD>
+__global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
+    constexpr int NR = gu_nr<NBG>();
+    using EG = CEng<TYG, 2 * NR, NBG>;
+    using ED = CEng<TYD, SC, NBD>;
+    constexpr int dim = NBG * 256;
+    extern __shared__ __align__(16) uint8_t smraw[];
+    float *xs = reinterpret_cast<float *>(smraw);                       // x [dim]
+    int8_t *xq = reinterpret_cast<int8_t *>(xs + dim);                  // [dim]
+    float *xqd = reinterpret_cast<float *>(xq + dim);                   // [NBG]
+    int32_t *xqs = reinterpret_cast<int32_t *>(xqd + NBG);              // [NBG*16]
+    float *scores = reinterpret_cast<float *>(xqs + NBG * 16);          // [ne]
+    float *choice = scores + A.n_expert;                                // [ne]
+    int *sid = reinterpret_cast<int *>(choice + A.n_expert);            // [64]
+    float *sg = reinterpret_cast<float *>(sid + 64);                    // [64]
+    float *red = sg + 64;                                               // [8]
+    int8_t *aq = reinterpret_cast<int8_t *>(red + 8);                   // [nk][stride]
+    const int stride = A.act_stride, nk = A.n_used, ne = A.n_expert;
+    float *ad = reinterpret_cast<float *>(aq + (size_t)nk * stride);    // [nk][stride/32]
+    int32_t *as = reinterpret_cast<int32_t *>(ad + (size_t)nk * (stride / 32));  // [nk][stride/16]
+    __shared__ uint64_t s_gb[PS_WARPS][SC];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int ffn = A.ffn;
+    // warm L2 with this CTA's router rows of layer 0
+    for (int row = warp * G + c; warp == 0 && row < ne; row += PS_WARPS * G)
+        if (lane == 0) prefetch_l2(A.layers[0].router + (size_t)row * dim, dim * 4);
+    for (int l = 0; l < A.n_layers; l++) {
+        const StackLayer &Ly = A.layers[l];
+        const float *x = l == 0 ? A.x_in : (l & 1 ? A.xbuf0 : A.xbuf1);
+        float *xn = l == A.n_layers - 1 ? A.out : (l & 1 ? A.xbuf1 : A.xbuf0);
+        // ---- P1: router rows
+        for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
+            reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(x) + i);
+        __syncthreads();
+        for (int row = warp * G + c; row < ne; row += PS_WARPS * G) {
+            float w[RR_CHUNK];
+            const float *wr = Ly.router + (size_t)row * dim;
+            load_row_chunk(w, wr, dim, lane);
+            const float r = router_dot(w, wr, xs, dim, lane);
+            if (lane == 0) A.logits[row] = r;
+        }
+        if (!grid_barrier(A.bar, A.err)) return;
+        // ---- P2: route (replicated) + quantize x, then gate/up
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = __ldcg(A.logits + e);
+        __syncthreads();
+        if (threadIdx.x < ROUTE_THREADS) {
+            route_block(choice, nullptr, ne, nk, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
+                        red, sid, sg);
+        } else {
+            const int wi = warp - ROUTE_THREADS / 32, nwq = PS_WARPS - ROUTE_THREADS / 32;
+            for (int b = wi; b < NBG; b += nwq)
+                quant_lane8(xs + b * 256 + lane * 8, true, 32, xq + b * 256 + lane * 8, xqd + b,
+                            xqs + b * 16 + lane / 2, nullptr, lane);
+        }
+        __syncthreads();
+        if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = sid[threadIdx.x];
+        const int r0 = c * dim / G, r1 = (c + 1) * dim / G;  // this CTA's down rows (P3)
+        if (threadIdx.x < nk && r1 > r0) {
+            const uint64_t b0 = ((uint64_t)sid[threadIdx.x] * dim + r0) * NBD, nb = (uint64_t)(r1 - r0) * NBD;
+            prefetch_l2(Ly.dn.q + b0 * layout_qbytes(TYD), nb * layout_qbytes(TYD));
+            if (Ly.dn.sc) prefetch_l2(Ly.dn.sc + b0 * 16, nb * 16);
+            if (Ly.dn.d) prefetch_l2(Ly.dn.d + b0, nb * 2);
+        }
+        {
+            const int per_e = ffn / NR, total = nk * per_e;
+            for (int grp = c * total / G + warp; grp < (c + 1) * total / G; grp += PS_WARPS) {
+                const int k = grp / per_e, rl = (grp % per_e) * NR;
+                const uint64_t plane = (uint64_t)sid[k] * ffn * NBG;
+                GateUpStreams<NR> st{Ly.g, Ly.u, plane + (uint64_t)rl * NBG, plane + (uint64_t)rl * NBG, NBG,
+                                     XV{xq, xqd, xqs}};
+                typename EG::Frags fr;
+                EG::load(st, fr, lane);
+                float acc[2 * NR];
+                EG::finish(st, fr, acc, lane);
+                if (lane == 0)
+                    for (int i = 0; i < NR; i++)
+                        A.act[(size_t)k * stride + rl + i] = fmul(fdiv(acc[i], fadd(1.0f, expf(-acc[i]))), acc[NR + i]);
+            }
+        }
+        if (!grid_barrier(A.bar, A.err)) return;
+        // ---- P3: quantize the experts' activations, down rows + combine + residual
+        for (int u = warp; u < nk * (ffn / 256); u += PS_WARPS) {
+            const int k = u / (ffn / 256), b = u % (ffn / 256);
+            const float *src = A.act + (size_t)k * stride + b * 256 + lane * 8;
+            float v[8];
+            const float4 p = __ldcg(reinterpret_cast<const float4 *>(src)), q = __ldcg(reinterpret_cast<const float4 *>(src) + 1);
+            v[0] = p.x, v[1] = p.y, v[2] = p.z, v[3] = p.w, v[4] = q.x, v[5] = q.y, v[6] = q.z, v[7] = q.w;
+            quant_vals8(v, true, 32, aq + (size_t)k * stride + b * 256 + lane * 8, ad + (size_t)k * (stride / 32) + b,
+                        as + (size_t)k * (stride / 16) + b * 16 + lane / 2, nullptr, lane);
+        }
+        __syncthreads();
+        for (int r = r0 + warp; r < r1; r += PS_WARPS) {
+            float acc = 0.0f;
+            for (int k0 = 0; k0 < nk; k0 += SC) {
+                const int n = nk - k0 < SC ? nk - k0 : SC;
+                __syncwarp();
+                if (lane < n) s_gb[warp][lane] = ((uint64_t)sid[k0 + lane] * dim + r) * NBD;
+                __syncwarp();
+                StackDownStreams st{Ly.dn, s_gb[warp], aq, ad, as, stride, k0, n};
+                typename ED::Frags fr;
+                float y[SC];
+                if (n == SC) {
+                    ED::load(st, fr, lane);
+                    ED::finish(st, fr, y, lane);
+                } else {
+                    wd_load<TYD, SC, ED::MAXU>(st, NBD, n, fr, lane);
+                    wd_finish<TYD, SC, ED::MAXU>(st, NBD, n, fr, y, lane);
+                }
+#pragma unroll
+                for (int k = 0; k < SC; k++)
+                    if (k < n) acc = fadd(acc, fmul(sg[k0 + k], y[k]));
+            }
+            if (lane == 0) xn[r] = fadd(__ldcg(x + r), acc);
+        }
+        if (l + 1 < A.n_layers)  // warm L2 with this CTA's router rows of the next layer
+            for (int row = warp * G + c; row < ne; row += PS_WARPS * G)
+                if (lane == 0) prefetch_l2(A.layers[l + 1].router + (size_t)row * dim, dim * 4);
+        if (!grid_barrier(A.bar, A.err)) return;
+    }
+}
+
+using StackFn = void (*)(StackArgs);
+static StackFn stack_fn(int gty, int nbg, int dty, int nbd) {
+    if (gty == T_Q4_K && nbg == 8 && dty == T_Q6_K && nbd == 3) return k_stack<T_Q4_KW, 8, T_Q6_K, 8, 3>;
+    return nullptr;
+}
+
+static size_t stack_smem(const StackArgs &S) {
+    const size_t nbg = S.dim / 256;
+    return (size_t)S.dim * 4 + S.dim + nbg * 4 + nbg * 64 + (size_t)2 * S.n_expert * 4 + 64 * 8 + 32 +
+           (size_t)S.n_used * S.act_stride * (1 + 4.0 / 32 + 4.0 / 16) + 64;
+}
+
+bool stack_supported(const StackArgs &S, int g_type, int dn_type) {
+    if (S.dim % 256 || S.ffn % 256 || S.n_used > 64 || S.n_expert > 1024 || S.n_expert % 4) return false;
+    if (!stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type))) return false;
+    return stack_smem(S) <= 48 * 1024;
+}
+
+cudaError_t launch_stack(const StackArgs &S, int g_type, int dn_type, cudaStream_t st) {
+    StackFn fn = stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type));
+    int dev = 0, nsm = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const size_t smem = stack_smem(S);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, PS_WARPS * 32, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nsm);
+    cfg.blockDim = dim3(PS_WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, fn, S);
+}
+
 }  // namespace loom

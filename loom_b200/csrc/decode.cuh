@@ -64,3 +64,35 @@ bool batch_supported(const DecodeArgs &A);
 cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st);
 
 }  // namespace loom
+
+namespace loom {
+
+// One decode step (T = 1) through a stack of MoE layers in ONE persistent
+// cooperative kernel: x_{l+1} = x_l + MoE_l(x_l), phases separated by grid
+// barriers instead of kernel boundaries.
+struct StackLayer {
+    const float *router;  // f32 [n_expert][dim]
+    WDev g, u, dn;        // [n_expert][ffn][dim], [n_expert][dim][ffn]
+};
+
+struct StackArgs {
+    const StackLayer *layers;  // device array [n_layers]
+    int n_layers;
+    int dim, ffn, n_expert, n_used;
+    int gating, weights_norm;
+    float weights_scale;
+    const float *x_in;
+    float *xbuf0, *xbuf1;      // [dim] ping-pong between layers
+    float *out;                // [dim] output of the last layer
+    float *logits;             // [n_expert]
+    float *act;                // [n_used][act_stride]
+    uint32_t *ids_out;         // optional [n_layers][n_used]
+    unsigned *bar;             // [2] zeroed: arrival count, generation
+    int *err;                  // device error word
+    int act_stride;
+};
+
+bool stack_supported(const StackArgs &S, int g_type, int dn_type);
+cudaError_t launch_stack(const StackArgs &S, int g_type, int dn_type, cudaStream_t st);
+
+}  // namespace loom

@@ -1075,3 +1075,108 @@ extern "C" int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const fl
     CK(launch_decode(A, st));
     return LOOM_CUDA_OK;
 }
+
+// ---- persistent decode stack --------------------------------------------------------
+
+namespace {
+struct StackRec {
+    StackArgs args{};
+    int gty = 0, dty = 0;
+    void *mem = nullptr;  // layers + buffers, one allocation
+};
+std::unordered_map<uint64_t, StackRec> g_stacks;
+uint64_t g_next_stack = 1;
+}  // namespace
+
+extern "C" int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_layers, uint64_t *handle) {
+    if (int rc = need_init()) return rc;
+    if (!descs || n_layers == 0) return decline("empty stack");
+    const loom_moe_desc &D0 = descs[0];
+    std::vector<StackLayer> host(n_layers);
+    int gty = -1, dty = -1;
+    for (size_t l = 0; l < n_layers; l++) {
+        const loom_moe_desc &D = descs[l];
+        if (D.dim != D0.dim || D.ffn != D0.ffn || D.n_expert != D0.n_expert || D.n_used != D0.n_used ||
+            D.gating != D0.gating || D.weights_norm != D0.weights_norm || D.weights_scale != D0.weights_scale)
+            return decline("stack layers must share one shape and routing configuration");
+        if (D.router_bias || D.shexp_gate || (D.n_local && D.n_local != D.n_expert) || D.expert0)
+            return decline("the stack kernel takes plain routed layers (no bias, shared expert or sharding)");
+        Tensor *r = lookup(D.router), *g = lookup(D.gate), *u = lookup(D.up), *dn = lookup(D.down);
+        const Tensor *sh[3] = {nullptr, nullptr, nullptr};
+        RoutedLayerDev L{};
+        if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
+        if (int rc = routed_layer(L, g, u, dn, D.dim, D.ffn, D.n_expert, sh, 0)) return rc;
+        if (g->type != u->type) return decline("gate and up types differ");
+        if (l == 0) {
+            gty = g->type;
+            dty = dn->type;
+        } else if (g->type != gty || dn->type != dty) {
+            return decline("stack layers must share block types");
+        }
+        host[l] = StackLayer{reinterpret_cast<const float *>(r->base), g->w, u->w, dn->w};
+    }
+    StackRec S;
+    StackArgs &A = S.args;
+    A.n_layers = (int)n_layers;
+    A.dim = (int)D0.dim;
+    A.ffn = (int)D0.ffn;
+    A.n_expert = (int)D0.n_expert;
+    A.n_used = (int)D0.n_used;
+    A.gating = D0.gating ? D0.gating : 1;
+    A.weights_norm = D0.weights_norm;
+    A.weights_scale = D0.weights_scale;
+    A.act_stride = (int)align256(D0.ffn);
+    if (!stack_supported(A, gty, dty)) return decline("layer shape not covered by the stack kernel");
+    const size_t lay_b = align256(n_layers * sizeof(StackLayer)), x_b = align256(D0.dim * 4);
+    const size_t lg_b = align256(D0.n_expert * 4), act_b = align256(D0.n_used * (size_t)A.act_stride * 4);
+    const size_t total = lay_b + 2 * x_b + lg_b + act_b + 256;
+    CK(cudaMalloc(&S.mem, total));
+    uint8_t *p = static_cast<uint8_t *>(S.mem);
+    A.layers = reinterpret_cast<const StackLayer *>(p);
+    A.xbuf0 = reinterpret_cast<float *>(p + lay_b);
+    A.xbuf1 = reinterpret_cast<float *>(p + lay_b + x_b);
+    A.logits = reinterpret_cast<float *>(p + lay_b + 2 * x_b);
+    A.act = reinterpret_cast<float *>(p + lay_b + 2 * x_b + lg_b);
+    A.bar = reinterpret_cast<unsigned *>(p + lay_b + 2 * x_b + lg_b + act_b);
+    A.err = reinterpret_cast<int *>(A.bar + 2);
+    CK(cudaMemcpy(p, host.data(), n_layers * sizeof(StackLayer), cudaMemcpyHostToDevice));
+    CK(cudaMemset(A.bar, 0, 256));
+    S.gty = gty;
+    S.dty = dty;
+    const uint64_t h = g_next_stack++;
+    g_stacks[h] = S;
+    *handle = h;
+    return LOOM_CUDA_OK;
+}
+
+extern "C" int loom_cuda_stack_forward(uint64_t handle, const float *d_x, float *d_out, uint32_t *d_ids, void *stream) {
+    if (int rc = need_init()) return rc;
+    auto it = g_stacks.find(handle);
+    if (it == g_stacks.end()) return decline("unknown stack");
+    StackArgs A = it->second.args;
+    A.x_in = d_x;
+    A.out = d_out;
+    A.ids_out = d_ids;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    CK(launch_stack(A, it->second.gty, it->second.dty, st));
+    return LOOM_CUDA_OK;
+}
+
+extern "C" int loom_cuda_stack_error(uint64_t handle) {
+    auto it = g_stacks.find(handle);
+    if (it == g_stacks.end()) return -1;
+    int v = 0;
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) return -1;
+    if (cudaMemcpy(&v, it->second.args.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v && cudaMemset(it->second.args.bar, 0, 256) != cudaSuccess) return -1;  // re-arm the barrier words
+    return v;
+}
+
+extern "C" int loom_cuda_stack_free(uint64_t handle) {
+    auto it = g_stacks.find(handle);
+    if (it == g_stacks.end()) return decline("unknown stack");
+    cudaDeviceSynchronize();
+    cudaFree(it->second.mem);
+    g_stacks.erase(it);
+    return LOOM_CUDA_OK;
+}

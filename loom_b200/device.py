@@ -98,6 +98,28 @@ class MoeLayer:
         _lib.must(rc, "moe_forward")
 
 
+class Stack:
+    """A decode step through several MoE layers as one persistent kernel."""
+
+    def __init__(self, layers):
+        descs = (_lib.MoeDesc * len(layers))(*[L.desc() for L in layers])
+        h = C.c_uint64(0)
+        _lib.must(_lib.lib().loom_cuda_stack_prepare(C.cast(descs, C.c_void_p), len(layers), C.byref(h)), "stack_prepare")
+        self.handle = h.value
+        self.n_layers = len(layers)
+
+    def forward(self, x, out, ids=None, stream=None) -> None:
+        _lib.must(_lib.lib().loom_cuda_stack_forward(self.handle, _ptr(x), _ptr(out), _ptr(ids), stream), "stack_forward")
+
+    def error(self) -> int:
+        return int(_lib.lib().loom_cuda_stack_error(self.handle))
+
+    def free(self) -> None:
+        if self.handle:
+            _lib.lib().loom_cuda_stack_free(self.handle)
+            self.handle = 0
+
+
 def ep_init(rank: int, world: int, dist=None) -> None:
     """Create the backend's NCCL communicator (one process per GPU). The id is
     made on rank 0 and broadcast with torch.distributed (any backend)."""

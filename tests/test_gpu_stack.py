@@ -1,0 +1,65 @@
+"""The persistent decode stack (one cooperative kernel for a whole stack of
+MoE layers at T = 1) must reproduce, bit for bit, running the same layers one
+by one through loom_cuda_moe_forward with the residual add: same expert ids,
+same output bits, on every layer."""
+import numpy as np
+import pytest
+import torch
+
+from loom_b200 import _lib
+from loom_b200.device import DeviceTensor, MoeLayer, Stack
+from tests.conftest import bits
+from tests.test_gpu_moe import synth_layer
+
+pytestmark = pytest.mark.gpu
+
+
+def _qwen_layers(orc, n, ne=128, k=8, dim=2048, ffn=768):
+    layers = []
+    for i in range(n):
+        g, u, d = synth_layer(orc, 100 + i, ne, dim, ffn)
+        rw = orc.synth(0, ne * dim, seed=300 + i, sigma=0.02)
+        layers.append(MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g), DeviceTensor.upload(12, u),
+                               DeviceTensor.upload(14, d), router=DeviceTensor.upload(0, rw)))
+    return layers
+
+
+@pytest.mark.parametrize("n_layers", [1, 2, 5])
+def test_stack_bitexact_with_layer_loop(be, orc, n_layers):
+    layers = _qwen_layers(orc, n_layers)
+    dim, k = layers[0].dim, layers[0].n_used
+    x0 = torch.from_numpy(orc.synth(0, dim, seed=501, sigma=1.0).reshape(1, dim)).cuda()
+    # layer loop: x_{l+1} = x_l + MoE_l(x_l)
+    want_ids = []
+    x = x0.clone()
+    for L in layers:
+        out = torch.empty_like(x)
+        ids = torch.zeros((1, k), dtype=torch.int32, device="cuda")
+        L.forward(x, out, residual=x, ids=ids)
+        want_ids.append(ids)
+        x = out
+    torch.cuda.synchronize()
+    want = x.cpu().numpy()
+    S = Stack(layers)
+    try:
+        for rep in range(2):  # a second launch reuses the barrier words
+            out = torch.full((1, dim), float("nan"), device="cuda")
+            ids = torch.zeros((n_layers, k), dtype=torch.int32, device="cuda")
+            S.forward(x0, out, ids)
+            torch.cuda.synchronize()
+            assert S.error() == 0
+            assert np.array_equal(ids.cpu().numpy(), torch.cat(want_ids).cpu().numpy()), rep
+            assert np.array_equal(bits(out.cpu().numpy()), bits(want)), rep
+    finally:
+        S.free()
+    assert _lib.lib().loom_cuda_device_error() == 0
+    for L in layers:
+        for t in (L.gate, L.up, L.down, L.router):
+            t.free()
+
+
+def test_stack_declines_shared_expert(be, orc):
+    from tests.test_gpu_moe import _layer_case
+    L = _layer_case(orc, 5, ne=64, k=6, dim=2048, ffn=1408, gt=12, dt=8, shared=2816)
+    with pytest.raises(RuntimeError):
+        Stack([L])
