@@ -256,7 +256,9 @@ def run_gpu(args):
     ms = e0.elapsed_time(e1) / args.steps
     if stack is not None:
         assert stack.error() == 0, "stack kernel grid barrier timed out"
-    phases = trace_phases(D, step, stream, torch) if args.trace and stack is None else None
+    phases = None
+    if args.trace:
+        phases = trace_phases(D, step, stream, torch) if stack is None else trace_stack(stack, step, stream, torch)
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -311,6 +313,28 @@ def run_gpu(args):
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def trace_stack(stack, step, stream, torch):
+    """One extra traced launch of the stack kernel: per layer, the mean time
+    from the layer's start to each phase point, in microseconds."""
+    stack.trace_enable()
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)
+    tr = stack.trace_read().astype(np.float64)
+    rel = tr[1:] - tr[1:, :1]
+    names = ["start", "router_rows_done", "route_barrier_exit", "route_done", "gateup_done",
+             "gateup_barrier_exit", "act_quantized", "down_done", "unused", "gateup_tiles_landed",
+             "down_tiles_landed"]
+    out = {n: round(float(np.mean(rel[:, i])) / 1e3, 2) for i, n in enumerate(names) if i and n != "unused"}
+    out["worst_layer_total"] = round(float(np.max(np.diff(tr[:, 0]))) / 1e3, 2)
+    out["layer_total"] = round(float(np.mean(np.diff(tr[:, 0]))) / 1e3, 2)
+    sec = ["p1_load", "router_dot", "bar1_wait", "route", "stage_issue", "gateup_tiles_wait", "gateup_compute",
+           "bar2_wait", "act_load", "act_quant", "down_tiles_wait", "down_compute", "bar3_wait", "gateup_dots_w0", "act_store_w0", "spare"]
+    cyc = tr[1:, 12:].reshape(-1, 16, 2)
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    out["cycles_max_mean"] = {n: [int(np.mean(cyc[:, i, 0])), int(np.mean(cyc[:, i, 1]) / G)] for i, n in enumerate(sec)}
+    return out
 
 
 def trace_phases(D, step, stream, torch):

@@ -212,6 +212,18 @@ int loom_cuda_stack_forward(uint64_t handle, const float *d_x, float *d_out, uin
  * synchronizes, and re-arms the barrier after an error. -1 on an unknown handle or a failed stream. */
 int loom_cuda_stack_error(uint64_t handle);
 int loom_cuda_stack_free(uint64_t handle);
+/* Phase trace of the stack kernel: enable=1 arms it for the following
+ * launches (outside stream capture); enable=0 synchronizes, copies up to n
+ * words into out and disarms it. Per layer 44 words: 12 %globaltimer ns
+ * points (layer start, router rows done, route barrier exit, route done,
+ * gate/up done, gate/up barrier exit, activations quantized, down rows done,
+ * unused, gate/up tiles landed, down tiles landed, unused), then for 13
+ * sections of thread 0's work (x load, router dot, barrier, route, tile
+ * requests, gate/up tile wait, gate/up compute, barrier, activation load,
+ * activation quantization, down tile wait, down compute, barrier, then
+ * within the gate/up compute: the dots, the activation stores, unused) the
+ * max and the sum over CTAs of its clock64 cycles. */
+int loom_cuda_stack_trace(uint64_t handle, int enable, uint64_t *out, size_t n);
 
 /* ---- expert parallelism (no counterpart in the reference: its experts never
  * leave one node's CPU/GPU; this is the north star's expert-parallel mode over

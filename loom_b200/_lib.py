@@ -97,6 +97,7 @@ def lib() -> C.CDLL:
         "loom_cuda_stack_forward": (i, [u64, vp, vp, vp, vp]),
         "loom_cuda_stack_error": (i, [u64]),
         "loom_cuda_stack_free": (i, [u64]),
+        "loom_cuda_stack_trace": (i, [u64, i, vp, sz]),
         "loom_cuda_ep_unique_id": (i, [vp, sz]),
         "loom_cuda_ep_init": (i, [i, i, vp, sz]),
         "loom_cuda_ep_shutdown": (None, []),

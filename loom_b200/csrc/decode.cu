@@ -992,214 +992,512 @@ cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st) {
 
 constexpr int PS_WARPS = 16;
 constexpr uint32_t BAR_POLLS = 1u << 21;  // bounded grid-barrier wait (~1 s of polling)
+constexpr uint32_t STAGE_POLLS = 1u << 22; // bounded wait on a bulk copy into shared memory
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_add_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Grid-wide barrier over gridDim.x co-resident CTAs. Gives up after BAR_POLLS
-// polls, or as soon as another CTA has given up, raising bit 2 of *err; returns
-// false then (the caller leaves the kernel: it never traps or spins forever).
-__device__ __forceinline__ bool grid_barrier(unsigned *bar, int *err) {
+// Trace slots of the stack kernel: the latest CTA to reach a point (max over
+// CTAs), or CTA 0's time at a barrier exit.
+__device__ __forceinline__ void trace_max(unsigned long long *slot) {
+    if (slot && threadIdx.x == 0) atomicMax(slot, gtimer());
+}
+
+// Grid-wide barrier over gridDim.x co-resident CTAs on a monotonic 64-bit
+// arrival counter: each CTA adds 1 with release semantics (no round trip) and
+// polls with acquire loads until the counter reaches its target, which thread 0
+// of each CTA advances by gridDim.x per barrier. Gives up after BAR_POLLS
+// polls, or as soon as *err is set by another CTA, raising bit 2 of *err, and
+// returns false (the caller leaves the kernel: it never traps or spins forever).
+// Thread 0's section cycle counter of the stack kernel (no-op without a trace).
+struct CycTrace {
+    unsigned long long *base;  // this layer's cycle pairs, or null
+    long long t;
+    __device__ __forceinline__ void mark(int i) {
+        if (threadIdx.x == 0) {
+            const long long n = clock64();
+            if (base) {
+                atomicMax(base + 2 * i, (unsigned long long)(n - t));
+                atomicAdd(base + 2 * i + 1, (unsigned long long)(n - t));
+            }
+            t = n;
+        }
+    }
+};
+
+__device__ __forceinline__ bool grid_barrier(unsigned long long *ctr, unsigned long long &target, int *err,
+                                             unsigned long long *t_in = nullptr, unsigned long long *t_out = nullptr,
+                                             CycTrace *cy = nullptr, int ci = 0) {
     __shared__ int s_ok;
     __syncthreads();
+    trace_max(t_in);
+    if (cy) cy->mark(ci);
     if (threadIdx.x == 0) {
         int ok = 1;
-        const unsigned gen = ld_acquire_u32(bar + 1);
-        __threadfence();
-        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-            bar[0] = 0;
-            __threadfence();
-            st_release_u32(bar + 1, gen + 1);
-        } else {
-            uint32_t i = 0;
-            for (; i < BAR_POLLS; i++) {
-                if (ld_acquire_u32(bar + 1) != gen) break;
-                if ((i & 1023) == 1023 && ld_acquire_u32(reinterpret_cast<unsigned *>(err)) & 2) i = BAR_POLLS - 1;
-            }
-            if (i >= BAR_POLLS) {
-                atomicOr(err, 2);
-                ok = 0;
-            }
+        target += gridDim.x;
+        red_release_add_u64(ctr, 1ull);
+        uint32_t i = 0;
+        for (; i < BAR_POLLS; i++) {
+            if (ld_acquire_u64(ctr) >= target) break;
+            if ((i & 1023) == 1023 && *reinterpret_cast<volatile int *>(err)) i = BAR_POLLS;  // another CTA failed
+        }
+        if (i >= BAR_POLLS) {
+            atomicOr(err, 2);
+            ok = 0;
         }
         s_ok = ok;
+        if (t_out && blockIdx.x == 0) *t_out = gtimer();
     }
+    if (cy) cy->mark(ci + 1);
     __syncthreads();
     return s_ok != 0;
 }
 
-struct StackDownStreams {  // the token's experts for one output row; activations staged in shared memory
-    WDev wd;
-    const uint64_t *g;
-    const int8_t *aq;
-    const float *ad;
-    const int32_t *as;
-    int stride, k0, nvalid;
-    __device__ __forceinline__ WDev w(int) const { return wd; }
-    __device__ __forceinline__ uint64_t gb(int s) const { return g[s < nvalid ? s : 0]; }
-    __device__ __forceinline__ XV x(int s) const {
-        const int j = k0 + (s < nvalid ? s : 0);
-        return XV{aq + (size_t)j * stride, ad + (size_t)j * (stride / 32), as + (size_t)j * (stride / 16)};
-    }
-    __device__ __forceinline__ void at(int s, WDev &wo, uint64_t &gg, XV &xv) const {
-        wo = wd;
-        gg = gb(s);
-        xv = x(s);
+// Down streams of the stack kernel: SC consecutive output rows of ONE expert
+// (this CTA's expert), weights staged in shared memory as a row-major tile
+// [rows][NBD blocks], the expert's int8 activations (xpad_q6k layout) shared
+// by every stream.
+template <int NBD> struct StackDownRows {
+    WDev w_;         // the tile (quants, scales, f16 scales from doff)
+    uint64_t row0;   // tile row of stream 0
+    int nvalid;      // streams that are real rows
+    XV xv;
+    __device__ __forceinline__ WDev w(int) const { return w_; }
+    __device__ __forceinline__ uint64_t gb(int s) const { return (row0 + (s < nvalid ? s : 0)) * NBD; }
+    __device__ __forceinline__ XV x(int) const { return xv; }
+};
+
+__host__ __device__ constexpr size_t round_to_mod128(size_t n, size_t r) {  // smallest m >= n, m % 128 == r
+    return (n + (128 - r) + 127) / 128 * 128 - (128 - r);
+}
+
+// Work split of the stack kernel over G CTAs (c = blockIdx.x):
+//   gate/up  groups of NR rows of gate and up, n_used * ffn / NR of them, in
+//            order (expert slot, row); CTA c takes groups [c*total/G, (c+1)*total/G)
+//   down     CTA c serves expert slot kd = c*n_used/G; the CTAs of one slot
+//            split the dim output rows evenly
+struct StackSplit {
+    int g0, g1;  // gate/up groups
+    int kd;      // down: expert slot
+    int ra, rb;  // down: output rows
+    __device__ __forceinline__ StackSplit(int c, int G, int total, int nk, int dim) {
+        g0 = (int)((long long)c * total / G);
+        g1 = (int)((long long)(c + 1) * total / G);
+        kd = c * nk / G;
+        const int first = (kd * G + nk - 1) / nk, last = ((kd + 1) * G + nk - 1) / nk, n = last - first;
+        ra = (c - first) * dim / n;
+        rb = (c - first + 1) * dim / n;
     }
 };
 
-template <int TYG, int NBG, int TYD, int SC, int NBD>
-__global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
-    constexpr int NR = gu_nr<NBG>();
-    using EG = CEng<TYG, 2 * NR, NBG>;
-    using ED = CEng<TYD, SC, NBD>;
+// Shared-memory map of the stack kernel (recomputed per phase so that no
+// pointer stays live in registers across phases). Sizes depend on the grid:
+// ngmax gate/up groups and nrmax down rows per CTA.
+template <int NBG, int NR, int NBD> struct StackSmem {
+    static constexpr int dim = NBG * 256;
+    static constexpr int GU_HALF = NR * NBG * 144;  // one group's NR rows of gate (or of up), Q4_K
+    float *xs;        // x [dim] of the current layer
+    int8_t *xq;       // [NBG * XPAD_BLOCK] (xpad_q4kw layout)
+    float *xqd;       // [NBG]
+    int32_t *xqs;     // [NBG*16]
+    float *scores;    // [ne]
+    float *choice;    // [ne]
+    int *sid;         // [64]
+    float *sg;        // [64]
+    int *doff;        // [8]
+    float *red;       // [8]
+    uint64_t *mbar;   // [4]: router rows, gate/up tiles, down tiles
+    float *rbuf;      // [rpc][dim] this CTA's router rows of the current layer
+    uint8_t *gub;     // gate tiles [ngmax][GU_HALF], then up tiles [ngmax][GU_HALF]
+    uint8_t *dq;      // [nrmax*NBD][192] down tile quants
+    uint8_t *dsc;     // [nrmax*NBD][16]
+    uint16_t *dd;     // [dslot/2]
+    float *af;        // [ffn] this CTA's expert's activations
+    int8_t *aq;       // [ffn/256 * XPAD_BLOCK]
+    float *ad;        // [ffn/256]
+    int32_t *as;      // [ffn/16]
+    static __host__ __device__ size_t dslot(int nrmax) { return ((size_t)nrmax * NBD * 2 + 15) / 16 * 16 + 16; }
+    __device__ __forceinline__ StackSmem(uint8_t *base, int ne, int ffn, int rpc, int ngmax, int nrmax) {
+        xs = reinterpret_cast<float *>(base);
+        xq = reinterpret_cast<int8_t *>(xs + dim);
+        xqd = reinterpret_cast<float *>(xq + NBG * XPAD_BLOCK);
+        xqs = reinterpret_cast<int32_t *>(xqd + NBG);
+        scores = reinterpret_cast<float *>(xqs + NBG * 16);
+        choice = scores + ne;
+        sid = reinterpret_cast<int *>(choice + ne);
+        sg = reinterpret_cast<float *>(sid + 64);
+        doff = reinterpret_cast<int *>(sg + 64);
+        red = reinterpret_cast<float *>(doff + 8);
+        mbar = reinterpret_cast<uint64_t *>(red + 8);  // 16-byte aligned: ne % 4 == 0
+        rbuf = reinterpret_cast<float *>(mbar + 4);
+        gub = reinterpret_cast<uint8_t *>(rbuf + (size_t)rpc * dim);
+        dq = gub + (size_t)2 * ngmax * GU_HALF;
+        dsc = dq + (size_t)nrmax * NBD * 192;
+        dd = reinterpret_cast<uint16_t *>(dsc + (size_t)nrmax * NBD * 16);
+        af = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(dd) + dslot(nrmax));
+        aq = reinterpret_cast<int8_t *>(af + ffn);
+        ad = reinterpret_cast<float *>(aq + (size_t)(ffn / 256) * XPAD_BLOCK);
+        as = reinterpret_cast<int32_t *>(ad + ffn / 256);
+    }
+    static size_t bytes(int ne, int ffn, int rpc, int ngmax, int nrmax) {
+        return (size_t)dim * 4 + NBG * XPAD_BLOCK + NBG * 4 + NBG * 64 + (size_t)2 * ne * 4 + 64 * 8 + 32 + 32 + 32 +
+               (size_t)rpc * dim * 4 + (size_t)2 * ngmax * GU_HALF + (size_t)nrmax * NBD * (192 + 16) + dslot(nrmax) +
+               (size_t)ffn * 4 + (size_t)(ffn / 256) * XPAD_BLOCK + (size_t)(ffn / 256) * 4 + (size_t)(ffn / 16) * 4;
+    }
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Thread 0: stage this CTA's router rows of layer `l` (rows c, c+G, ...) into
+// shared memory with bulk copies completing on *mbar.
+__device__ __noinline__ void stage_router_rows(const StackArgs &A, int l, float *rbuf, uint64_t *mbar) {
+    const int G = gridDim.x, c = blockIdx.x, dim = A.dim;
+    int n = 0;
+    for (int row = c; row < A.n_expert; row += G) n++;
+    if (n == 0) return;
+    fence_proxy_async_smem();
+    mbar_expect_tx(mbar, (uint32_t)(n * dim * 4));
+    int j = 0;
+#pragma unroll 1
+    for (int row = c; row < A.n_expert; row += G, j++)
+        bulk_g2s(rbuf + (size_t)j * dim, A.layers[l].router + (size_t)row * dim, (uint32_t)(dim * 4), mbar);
+}
+
+// Warp 0: stage this CTA's gate/up tiles (groups g0..g1: NR rows of gate and
+// of up each, contiguous within one expert, so one copy per expert and
+// matrix) and its down tile (rows ra..rb of expert slot kd: quants, scales,
+// and the f16 scales through a 16-byte-aligned window whose offset goes to
+// *doff).
+template <int NBG, int NR, int NBD>
+__device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const StackLayer &Ly, const int *sid, int *doff,
+                                                   uint8_t *gub, uint8_t *dq, uint8_t *dsc, uint16_t *dd,
+                                                   uint64_t *mb_gu, uint64_t *mb_dn, const StackSplit &P, int ngmax) {
+    using SM = StackSmem<NBG, NR, NBD>;
     constexpr int dim = NBG * 256;
-    extern __shared__ __align__(16) uint8_t smraw[];
-    float *xs = reinterpret_cast<float *>(smraw);                       // x [dim]
-    int8_t *xq = reinterpret_cast<int8_t *>(xs + dim);                  // [dim]
-    float *xqd = reinterpret_cast<float *>(xq + dim);                   // [NBG]
-    int32_t *xqs = reinterpret_cast<int32_t *>(xqd + NBG);              // [NBG*16]
-    float *scores = reinterpret_cast<float *>(xqs + NBG * 16);          // [ne]
-    float *choice = scores + A.n_expert;                                // [ne]
-    int *sid = reinterpret_cast<int *>(choice + A.n_expert);            // [64]
-    float *sg = reinterpret_cast<float *>(sid + 64);                    // [64]
-    float *red = sg + 64;                                               // [8]
-    int8_t *aq = reinterpret_cast<int8_t *>(red + 8);                   // [nk][stride]
-    const int stride = A.act_stride, nk = A.n_used, ne = A.n_expert;
-    float *ad = reinterpret_cast<float *>(aq + (size_t)nk * stride);    // [nk][stride/32]
-    int32_t *as = reinterpret_cast<int32_t *>(ad + (size_t)nk * (stride / 32));  // [nk][stride/16]
-    __shared__ uint64_t s_gb[PS_WARPS][SC];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int G = gridDim.x, c = blockIdx.x;
-    const int ffn = A.ffn;
-    // warm L2 with this CTA's router rows of layer 0
-    for (int row = warp * G + c; warp == 0 && row < ne; row += PS_WARPS * G)
-        if (lane == 0) prefetch_l2(A.layers[0].router + (size_t)row * dim, dim * 4);
-    for (int l = 0; l < A.n_layers; l++) {
-        const StackLayer &Ly = A.layers[l];
-        const float *x = l == 0 ? A.x_in : (l & 1 ? A.xbuf0 : A.xbuf1);
-        float *xn = l == A.n_layers - 1 ? A.out : (l & 1 ? A.xbuf1 : A.xbuf0);
-        // ---- P1: router rows
-        for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
-            reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(x) + i);
-        __syncthreads();
-        for (int row = warp * G + c; row < ne; row += PS_WARPS * G) {
-            float w[RR_CHUNK];
-            const float *wr = Ly.router + (size_t)row * dim;
-            load_row_chunk(w, wr, dim, lane);
-            const float r = router_dot(w, wr, xs, dim, lane);
-            if (lane == 0) A.logits[row] = r;
+    const int lane = threadIdx.x & 31, ffn = A.ffn, per_e = ffn / NR;
+    const int ng = P.g1 - P.g0, nr = P.rb - P.ra;
+    const uint64_t b0 = ((uint64_t)sid[P.kd] * dim + P.ra) * NBD, nb = (uint64_t)nr * NBD;
+    const uintptr_t d0 = reinterpret_cast<uintptr_t>(Ly.dn.d + b0);
+    const uintptr_t da = d0 & ~uintptr_t(15), de = (d0 + nb * 2 + 15) & ~uintptr_t(15);
+    if (lane == 0) {
+        fence_proxy_async_smem();
+        if (ng) mbar_expect_tx(mb_gu, (uint32_t)(2 * ng * SM::GU_HALF));
+        if (nr) {
+            *doff = (int)((d0 - da) / 2);
+            mbar_expect_tx(mb_dn, (uint32_t)(nb * (192 + 16) + (de - da)));
         }
-        if (!grid_barrier(A.bar, A.err)) return;
-        // ---- P2: route (replicated) + quantize x, then gate/up
-        for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = __ldcg(A.logits + e);
-        __syncthreads();
-        if (threadIdx.x < ROUTE_THREADS) {
-            route_block(choice, nullptr, ne, nk, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
-                        red, sid, sg);
-        } else {
-            const int wi = warp - ROUTE_THREADS / 32, nwq = PS_WARPS - ROUTE_THREADS / 32;
-            for (int b = wi; b < NBG; b += nwq)
-                quant_lane8(xs + b * 256 + lane * 8, true, 32, xq + b * 256 + lane * 8, xqd + b,
-                            xqs + b * 16 + lane / 2, nullptr, lane);
+    }
+    __syncwarp();
+    fence_proxy_async_smem();
+    // gate/up: the CTA's groups form a few runs inside one expert each,
+    // contiguous in global memory and in the tile: lane 2i copies run i's gate
+    // rows, lane 2i+1 its up rows
+    if (ng) {
+        const int ka = P.g0 / per_e, kb = (P.g1 - 1) / per_e;
+        for (int q = lane; q < 2 * (kb - ka + 1); q += 32) {
+            const int k = ka + q / 2, up = q & 1;
+            const int ga = max(P.g0, k * per_e), gz = min(P.g1, (k + 1) * per_e);
+            const uint64_t blk = ((uint64_t)sid[k] * ffn + (uint64_t)(ga - k * per_e) * NR) * NBG;
+            bulk_g2s(gub + (size_t)(up ? ngmax : 0) * SM::GU_HALF + (size_t)(ga - P.g0) * SM::GU_HALF,
+                     (up ? Ly.u : Ly.g).q + blk * 144, (uint32_t)(gz - ga) * SM::GU_HALF, mb_gu);
         }
-        __syncthreads();
-        if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = sid[threadIdx.x];
-        const int r0 = c * dim / G, r1 = (c + 1) * dim / G;  // this CTA's down rows (P3)
-        if (threadIdx.x < nk && r1 > r0) {
-            const uint64_t b0 = ((uint64_t)sid[threadIdx.x] * dim + r0) * NBD, nb = (uint64_t)(r1 - r0) * NBD;
-            prefetch_l2(Ly.dn.q + b0 * layout_qbytes(TYD), nb * layout_qbytes(TYD));
-            if (Ly.dn.sc) prefetch_l2(Ly.dn.sc + b0 * 16, nb * 16);
-            if (Ly.dn.d) prefetch_l2(Ly.dn.d + b0, nb * 2);
-        }
-        {
-            const int per_e = ffn / NR, total = nk * per_e;
-            for (int grp = c * total / G + warp; grp < (c + 1) * total / G; grp += PS_WARPS) {
-                const int k = grp / per_e, rl = (grp % per_e) * NR;
-                const uint64_t plane = (uint64_t)sid[k] * ffn * NBG;
-                GateUpStreams<NR> st{Ly.g, Ly.u, plane + (uint64_t)rl * NBG, plane + (uint64_t)rl * NBG, NBG,
-                                     XV{xq, xqd, xqs}};
-                typename EG::Frags fr;
-                EG::load(st, fr, lane);
-                float acc[2 * NR];
-                EG::finish(st, fr, acc, lane);
-                if (lane == 0)
-                    for (int i = 0; i < NR; i++)
-                        A.act[(size_t)k * stride + rl + i] = fmul(fdiv(acc[i], fadd(1.0f, expf(-acc[i]))), acc[NR + i]);
-            }
-        }
-        if (!grid_barrier(A.bar, A.err)) return;
-        // ---- P3: quantize the experts' activations, down rows + combine + residual
-        for (int u = warp; u < nk * (ffn / 256); u += PS_WARPS) {
-            const int k = u / (ffn / 256), b = u % (ffn / 256);
-            const float *src = A.act + (size_t)k * stride + b * 256 + lane * 8;
-            float v[8];
-            const float4 p = __ldcg(reinterpret_cast<const float4 *>(src)), q = __ldcg(reinterpret_cast<const float4 *>(src) + 1);
-            v[0] = p.x, v[1] = p.y, v[2] = p.z, v[3] = p.w, v[4] = q.x, v[5] = q.y, v[6] = q.z, v[7] = q.w;
-            quant_vals8(v, true, 32, aq + (size_t)k * stride + b * 256 + lane * 8, ad + (size_t)k * (stride / 32) + b,
-                        as + (size_t)k * (stride / 16) + b * 16 + lane / 2, nullptr, lane);
-        }
-        __syncthreads();
-        for (int r = r0 + warp; r < r1; r += PS_WARPS) {
-            float acc = 0.0f;
-            for (int k0 = 0; k0 < nk; k0 += SC) {
-                const int n = nk - k0 < SC ? nk - k0 : SC;
-                __syncwarp();
-                if (lane < n) s_gb[warp][lane] = ((uint64_t)sid[k0 + lane] * dim + r) * NBD;
-                __syncwarp();
-                StackDownStreams st{Ly.dn, s_gb[warp], aq, ad, as, stride, k0, n};
-                typename ED::Frags fr;
-                float y[SC];
-                if (n == SC) {
-                    ED::load(st, fr, lane);
-                    ED::finish(st, fr, y, lane);
-                } else {
-                    wd_load<TYD, SC, ED::MAXU>(st, NBD, n, fr, lane);
-                    wd_finish<TYD, SC, ED::MAXU>(st, NBD, n, fr, y, lane);
-                }
-#pragma unroll
-                for (int k = 0; k < SC; k++)
-                    if (k < n) acc = fadd(acc, fmul(sg[k0 + k], y[k]));
-            }
-            if (lane == 0) xn[r] = fadd(__ldcg(x + r), acc);
-        }
-        if (l + 1 < A.n_layers)  // warm L2 with this CTA's router rows of the next layer
-            for (int row = warp * G + c; row < ne; row += PS_WARPS * G)
-                if (lane == 0) prefetch_l2(A.layers[l + 1].router + (size_t)row * dim, dim * 4);
-        if (!grid_barrier(A.bar, A.err)) return;
+    }
+    if (nr) {
+        if (lane == 29) bulk_g2s(dq, Ly.dn.q + b0 * 192, (uint32_t)(nb * 192), mb_dn);
+        if (lane == 30) bulk_g2s(dsc, Ly.dn.sc + b0 * 16, (uint32_t)(nb * 16), mb_dn);
+        if (lane == 31) bulk_g2s(dd, reinterpret_cast<const void *>(da), (uint32_t)(de - da), mb_dn);
     }
 }
 
+// dotF32 (ggml.zig:198) of a router row in shared memory with x in shared
+// memory, dim a multiple of 32: lane j accumulates elements j, j+32, ... in
+// order, then the eight-lane / four-way reduction of the CPU's 4x8 accumulators.
+__device__ __forceinline__ float router_dot_smem(const float *wr, const float *x, int dim, int lane) {
+    float a = 0.0f;
+#pragma unroll 8
+    for (int i = lane; i < dim; i += 32) a = fadd(a, fmul(wr[i], x[i]));
+    const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
+    const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
+    const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
+    const float v = fadd(fadd(fadd(a, a8), a16), a24);
+    float r = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+    for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
+    return r;
+}
+
+// Bounded wait on a staging barrier; on time-out raise bit 4 of *err (the
+// other CTAs' grid barriers then give up early), wait once more so that no
+// copy is left in flight, and tell the caller to leave.
+__device__ __noinline__ bool stage_wait(uint64_t *mbar, int parity, int *err) {
+    if (mbar_wait(mbar, parity, STAGE_POLLS)) return true;
+    if (threadIdx.x == 0) atomicOr(err, 4);
+    mbar_wait(mbar, parity, STAGE_POLLS);
+    return false;
+}
+
+// One activation block of 256 values (8 per lane) quantized as quantizeX256
+// (one scale per block, sums per 16) into a padded int8 layout: xpad_q6k for
+// the down operand (Q6K = true), xpad_q4kw for the gate/up operand.
+template <bool Q6K>
+__device__ __noinline__ void quant_block256_padded(const float *src, int8_t *qbase, float *d256, int32_t *s16,
+                                                   int lane) {
+    float v[8];
+    const float4 p = *reinterpret_cast<const float4 *>(src + lane * 8);
+    const float4 q = *reinterpret_cast<const float4 *>(src + lane * 8 + 4);
+    v[0] = p.x, v[1] = p.y, v[2] = p.z, v[3] = p.w, v[4] = q.x, v[5] = q.y, v[6] = q.z, v[7] = q.w;
+    quant_vals8(v, true, 32, qbase + (Q6K ? xpad_q6k(lane * 8) : xpad_q4kw(lane * 8)), d256, s16 + lane / 2, nullptr,
+                lane);
+}
+
+// x of the next layer: x += sum over expert slots k (in order, from +0) of the
+// gate-weighted partial outputs part[k][r] (moe.zig combine order), each
+// thread on its own elements of the shared-memory x.
+__device__ __forceinline__ void combine_parts(const float *part, int nk, int dim, float *xs) {
+#pragma unroll 1
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+        for (int k = 0; k < nk; k++) {
+            const float4 p = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)k * dim) + i);
+            acc.x = fadd(acc.x, p.x);
+            acc.y = fadd(acc.y, p.y);
+            acc.z = fadd(acc.z, p.z);
+            acc.w = fadd(acc.w, p.w);
+        }
+        float4 &x = reinterpret_cast<float4 *>(xs)[i];
+        x.x = fadd(x.x, acc.x);
+        x.y = fadd(x.y, acc.y);
+        x.z = fadd(x.z, acc.z);
+        x.w = fadd(x.w, acc.w);
+    }
+}
+
+template <int TYG, int NBG, int TYD, int SC, int NBD, int RW, bool TRACE>
+__global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
+    constexpr int NR = gu_nr<NBG>();
+    static_assert(TYG == T_Q4_KW && TYD == T_Q6_K, "staged tiles are laid out for Q4_K gate/up and Q6_K down");
+    using EG = CEng<T_Q4_KW_S, 2 * NR, NBG>;
+    using ED = CEng<T_Q6_K_S, SC, NBD>;
+    using SM = StackSmem<NBG, NR, NBD>;
+    constexpr int dim = NBG * 256;
+    extern __shared__ __align__(16) uint8_t smraw[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int nk = A.n_used, ffn = A.ffn;
+    const int rpc = (A.n_expert + G - 1) / G;
+    const int per_e = ffn / NR, total = nk * per_e, ngmax = (total + G - 1) / G;
+    const int nrmax = (dim + G / nk - 1) / (G / nk);
+    const int lg_stride = A.n_expert + 32;  // one logit replica
+    const StackSplit P(c, G, total, nk, dim);
+#define STACK_SMEM SM S(smraw, A.n_expert, ffn, rpc, ngmax, nrmax)
+    unsigned long long *ctr = reinterpret_cast<unsigned long long *>(A.bar);
+    unsigned long long target = 0;  // thread 0: this launch's barrier targets
+    if (threadIdx.x == 0) {
+        // Every earlier launch completed all 3 * n_layers barriers, so the
+        // counter stood at a multiple of that many rounds when this launch
+        // began; fewer than G arrivals of this launch can precede this read.
+        const unsigned long long per = 3ull * A.n_layers * G, v = ld_acquire_u64(ctr);
+        target = v - v % per;
+        STACK_SMEM;
+        mbar_init(S.mbar + 0, 1);
+        mbar_init(S.mbar + 1, 1);
+        mbar_init(S.mbar + 2, 1);
+        stage_router_rows(A, 0, S.rbuf, S.mbar);
+    }
+    __syncthreads();
+    CycTrace cy{nullptr, TRACE ? clock64() : 0};
+#pragma unroll 1
+    for (int l = 0; l < A.n_layers; l++) {
+        unsigned long long *tr = TRACE ? A.trace + (size_t)l * STACK_TRACE_WORDS : nullptr;
+        if (TRACE) cy.base = tr + STACK_TRACE_SLOTS;
+        if (TRACE && c == 0 && threadIdx.x == 0) tr[0] = gtimer();  // the previous barrier's exit
+        {   // ---- P1: x of this layer (x_in, or the previous layer's x plus its combined experts), router rows . x
+            STACK_SMEM;
+            if (l == 0) {
+#pragma unroll 1
+                for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
+                    reinterpret_cast<float4 *>(S.xs)[i] = __ldcg(reinterpret_cast<const float4 *>(A.x_in) + i);
+            } else {
+                combine_parts(A.part, nk, dim, S.xs);
+            }
+            if (c < A.n_expert && !stage_wait(S.mbar, l & 1, A.err)) return;
+            __syncthreads();
+            if (TRACE) cy.mark(0);  // x ready, router rows landed
+            // warps with a router row take it; the rest quantize x for gate/up meanwhile
+            const int nrw = (A.n_expert - c + G - 1) / G;  // this CTA's router rows
+            if (warp < nrw) {
+#pragma unroll 1
+                for (int row = c + warp * G, j = warp; row < A.n_expert; row += PS_WARPS * G, j += PS_WARPS) {
+                    const float r = router_dot_smem(S.rbuf + (size_t)j * dim, S.xs, dim, lane);
+                    if (lane < LOGIT_REPLICAS) A.logits[(size_t)lane * lg_stride + row] = r;
+                }
+            } else {
+                const int nq = PS_WARPS - (nrw < PS_WARPS ? nrw : PS_WARPS - 1);
+#pragma unroll 1
+                for (int b = warp - (PS_WARPS - nq); b < NBG; b += nq)
+                    quant_block256_padded<false>(S.xs + b * 256, S.xq + b * XPAD_BLOCK, S.xqd + b, S.xqs + b * 16, lane);
+            }
+        }
+        if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 1 : nullptr, TRACE ? tr + 2 : nullptr,
+                          TRACE ? &cy : nullptr, 1))
+            return;
+        {   // ---- P2: route (replicated in every CTA); stage gate/up and down tiles; gate/up
+            STACK_SMEM;
+            const int ne = A.n_expert;
+            if (warp == 0)
+                route_warp_regs<true, RW>(A.logits + (size_t)(c % LOGIT_REPLICAS) * lg_stride, nullptr, ne, nk,
+                                          A.gating, A.weights_norm, A.weights_scale, S.scores, S.choice, S.sid, S.sg,
+                                          S.sid, S.sg, lane);
+            if (TRACE) cy.mark(3);  // route (thread 0's warp)
+            __syncthreads();
+            if (TRACE) trace_max(tr + 3);
+            const StackLayer &Ly = A.layers[l];
+            if (warp == 0)
+                stage_expert_tiles<NBG, NR, NBD>(A, Ly, S.sid, S.doff, S.gub, S.dq, S.dsc, S.dd, S.mbar + 1, S.mbar + 2,
+                                                 P, ngmax);
+            if (TRACE) cy.mark(4);  // tiles requested
+            if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = S.sid[threadIdx.x];
+            if (P.g1 > P.g0) {
+                if (!stage_wait(S.mbar + 1, l & 1, A.err)) {
+                    if (P.rb > P.ra) mbar_wait(S.mbar + 2, l & 1, STAGE_POLLS);
+                    return;
+                }
+                if (TRACE) {
+                    trace_max(tr + 9);
+                    cy.mark(5);  // gate/up tiles landed
+                }
+                const WDev wt{S.gub, nullptr, nullptr, T_Q4_K, 0};
+#pragma unroll 1
+                for (int g = warp; g < P.g1 - P.g0; g += PS_WARPS) {
+                    const int grp = P.g0 + g, k = grp / per_e, rl = (grp % per_e) * NR;
+                    GateUpStreams<NR> st{wt, wt, (uint64_t)g * NR * NBG, (uint64_t)(ngmax + g) * NR * NBG, NBG,
+                                         XV{S.xq, S.xqd, S.xqs}};
+                    float acc[2 * NR];
+                    EG::run(st, acc, lane);
+                    if (TRACE && g == 0) cy.mark(13);  // warp 0's gate/up dots
+                    if (lane < NR)
+#pragma unroll
+                        for (int i = 0; i < NR; i++)
+                            if (i == lane)
+                                A.act[(size_t)k * A.act_stride + rl + i] =
+                                    fmul(fdiv(acc[i], fadd(1.0f, expf(-acc[i]))), acc[NR + i]);
+                    if (TRACE && g == 0) cy.mark(14);  // warp 0's activations stored
+                }
+            }
+        }
+        if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 4 : nullptr, TRACE ? tr + 5 : nullptr,
+                          TRACE ? &cy : nullptr, 6)) {
+            STACK_SMEM;
+            if (P.rb > P.ra) mbar_wait(S.mbar + 2, l & 1, STAGE_POLLS);
+            return;
+        }
+        {   // ---- P3: this CTA's expert: its activations quantized, rows ra..rb of its down matrix
+            STACK_SMEM;
+            const int nbf = ffn / 256;
+#pragma unroll 1
+            for (int i = threadIdx.x; i < ffn / 4; i += blockDim.x)
+                reinterpret_cast<float4 *>(S.af)[i] =
+                    __ldcg(reinterpret_cast<const float4 *>(A.act + (size_t)P.kd * A.act_stride) + i);
+            __syncthreads();
+            if (TRACE) cy.mark(8);  // activations loaded
+            if (warp < nbf)
+                quant_block256_padded<true>(S.af + warp * 256, S.aq + warp * XPAD_BLOCK, S.ad + warp, S.as + warp * 16,
+                                            lane);
+            __syncthreads();
+            if (TRACE) {
+                cy.mark(9);  // activations quantized
+                trace_max(tr + 6);
+            }
+            if (P.rb > P.ra && !stage_wait(S.mbar + 2, l & 1, A.err)) return;
+            if (TRACE) {
+                trace_max(tr + 10);
+                cy.mark(10);  // down tile landed
+            }
+            const float gk = S.sg[P.kd];
+            float *pout = A.part + (size_t)P.kd * dim;
+            const WDev wt{S.dq, S.dsc, S.dd + *S.doff, T_Q6_K, 0};
+#pragma unroll 1
+            for (int r = P.ra + warp * SC; r < P.rb; r += PS_WARPS * SC) {
+                const int n = P.rb - r < SC ? P.rb - r : SC;
+                StackDownRows<NBD> st{wt, (uint64_t)(r - P.ra), n, XV{S.aq, S.ad, S.as}};
+                float y[SC];
+                ED::run(st, y, lane);
+#pragma unroll
+                for (int s = 0; s < SC; s++)
+                    if (s == lane && s < n) pout[r + s] = fmul(gk, y[s]);
+            }
+            __syncthreads();  // rbuf is free: stage the next layer's router rows
+            if (l + 1 < A.n_layers && threadIdx.x == 0) stage_router_rows(A, l + 1, S.rbuf, S.mbar);
+        }
+        if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 7 : nullptr, nullptr, TRACE ? &cy : nullptr, 11)) {
+            STACK_SMEM;
+            if (l + 1 < A.n_layers && c < A.n_expert) mbar_wait(S.mbar, (l + 1) & 1, STAGE_POLLS);
+            return;
+        }
+    }
+    {   // the last layer's output: x plus its combined experts, this CTA's slice of rows
+        STACK_SMEM;
+        const int r0 = c * dim / G, r1 = (c + 1) * dim / G;
+        for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+            float acc = 0.0f;
+            for (int k = 0; k < nk; k++) acc = fadd(acc, __ldcg(A.part + (size_t)k * dim + r));
+            A.out[r] = fadd(S.xs[r], acc);
+        }
+    }
+#undef STACK_SMEM
+}
+
 using StackFn = void (*)(StackArgs);
-static StackFn stack_fn(int gty, int nbg, int dty, int nbd) {
-    if (gty == T_Q4_K && nbg == 8 && dty == T_Q6_K && nbd == 3) return k_stack<T_Q4_KW, 8, T_Q6_K, 8, 3>;
+static StackFn stack_fn(int gty, int nbg, int dty, int nbd, int ne, bool trace) {
+    if (gty == T_Q4_K && nbg == 8 && dty == T_Q6_K && nbd == 3) {
+        if (ne <= 128)
+            return trace ? k_stack<T_Q4_KW, 8, T_Q6_K, 8, 3, 4, true> : k_stack<T_Q4_KW, 8, T_Q6_K, 8, 3, 4, false>;
+        if (ne <= 256)
+            return trace ? k_stack<T_Q4_KW, 8, T_Q6_K, 8, 3, 8, true> : k_stack<T_Q4_KW, 8, T_Q6_K, 8, 3, 8, false>;
+    }
     return nullptr;
 }
 
-static size_t stack_smem(const StackArgs &S) {
-    const size_t nbg = S.dim / 256;
-    return (size_t)S.dim * 4 + S.dim + nbg * 4 + nbg * 64 + (size_t)2 * S.n_expert * 4 + 64 * 8 + 32 +
-           (size_t)S.n_used * S.act_stride * (1 + 4.0 / 32 + 4.0 / 16) + 64;
+static size_t stack_smem(const StackArgs &S, int n_sm) {
+    const int rpc = (S.n_expert + n_sm - 1) / n_sm;
+    const int total = S.n_used * (S.ffn / gu_nr<8>());
+    const int per_slot = n_sm / S.n_used;  // fewest CTAs serving one expert slot's down rows
+    return StackSmem<8, gu_nr<8>(), 3>::bytes(S.n_expert, S.ffn, rpc, (total + n_sm - 1) / n_sm,
+                                              (S.dim + per_slot - 1) / per_slot);
+}
+
+static int sm_count() {
+    int dev = 0, nsm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    return nsm;
 }
 
 bool stack_supported(const StackArgs &S, int g_type, int dn_type) {
     if (S.dim % 256 || S.ffn % 256 || S.n_used > 64 || S.n_expert > 1024 || S.n_expert % 4) return false;
-    if (!stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type))) return false;
-    return stack_smem(S) <= 48 * 1024;
+    if (!stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type), S.n_expert, false)) return false;
+    if (S.dim / 256 != 8) return false;  // the shared-memory map is instantiated for dim 2048
+    if (S.n_used > 8 * PS_WARPS || S.ffn / 256 > PS_WARPS || sm_count() < S.n_used) return false;
+    return stack_smem(S, sm_count()) <= 227 * 1024;
 }
 
 cudaError_t launch_stack(const StackArgs &S, int g_type, int dn_type, cudaStream_t st) {
-    StackFn fn = stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type));
-    int dev = 0, nsm = 0, per_sm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const size_t smem = stack_smem(S);
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, PS_WARPS * 32, smem);
+    StackFn fn = stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type), S.n_expert, S.trace != nullptr);
+    const int nsm = sm_count();
+    int per_sm = 0;
+    const size_t smem = stack_smem(S, nsm);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, PS_WARPS * 32, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
     cudaLaunchConfig_t cfg = {};

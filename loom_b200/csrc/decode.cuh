@@ -82,15 +82,22 @@ struct StackArgs {
     int gating, weights_norm;
     float weights_scale;
     const float *x_in;
-    float *xbuf0, *xbuf1;      // [dim] ping-pong between layers
+    float *part;               // [n_used][dim] gate-weighted expert outputs of the current layer
     float *out;                // [dim] output of the last layer
-    float *logits;             // [n_expert]
+    float *logits;             // [LOGIT_REPLICAS][n_expert + 32]
     float *act;                // [n_used][act_stride]
     uint32_t *ids_out;         // optional [n_layers][n_used]
-    unsigned *bar;             // [2] zeroed: arrival count, generation
-    int *err;                  // device error word
+    unsigned *bar;             // zeroed, 8-byte aligned: 64-bit grid-barrier arrival counter
+    int *err;                  // device error word (2: a grid barrier gave up, 4: router staging timed out)
     int act_stride;
+    unsigned long long *trace; // optional [n_layers][STACK_TRACE_SLOTS] %globaltimer ns (zeroed; max-reduced)
 };
+constexpr int LOGIT_REPLICAS = 16;  // copies of the router logits (stride n_expert + 32): every CTA reads them
+constexpr int STACK_TRACE_SLOTS = 12;
+// After the 12 timer slots of a layer: STACK_CYC_SECTIONS pairs (max over
+// CTAs, sum over CTAs) of thread 0's clock64 cycles spent in each section.
+constexpr int STACK_CYC_SECTIONS = 16;
+constexpr int STACK_TRACE_WORDS = STACK_TRACE_SLOTS + 2 * STACK_CYC_SECTIONS;
 
 bool stack_supported(const StackArgs &S, int g_type, int dn_type);
 cudaError_t launch_stack(const StackArgs &S, int g_type, int dn_type, cudaStream_t st);

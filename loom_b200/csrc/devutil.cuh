@@ -15,7 +15,10 @@ __device__ __forceinline__ void quant_vals8(const float (&v)[8], bool live, int 
 #pragma unroll
     for (int i = 0; i < 8; i++)
         if (live && isfinite(v[i])) amax = fmaxf(amax, fabsf(v[i]));
-    for (int o = 1; o < group_lanes; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (group_lanes == 32)  // amax >= 0: its bits order as unsigned integers
+        amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+    else
+        for (int o = 1; o < group_lanes; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float d = fdiv(amax, 127.0f);
     const float inv = (d != 0.0f && isfinite(d)) ? fdiv(1.0f, d) : 0.0f;
     int sum = 0;
@@ -32,7 +35,10 @@ __device__ __forceinline__ void quant_vals8(const float (&v)[8], bool live, int 
     if (sdst_pairs && live && (lane & 1) == 0) *sdst_pairs = pair;
     if (sdst_group) {
         int gs = sum;
-        for (int o = 1; o < group_lanes; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        if (group_lanes == 32)
+            gs = __reduce_add_sync(0xffffffffu, gs);
+        else
+            for (int o = 1; o < group_lanes; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
         if (live && (lane % group_lanes) == 0) *sdst_group = gs;
     }
     if (live && (lane % group_lanes) == 0) *ddst = isfinite(d) ? d : 0.0f;
@@ -105,38 +111,44 @@ __device__ __forceinline__ void route_rank(const float *scores, const float *cho
     }
 }
 
+// The serial k-round first-max scan (the cold path of route_finish: some
+// value is NaN or -inf). Out of line to keep the kernels that inline the
+// route small.
+static __device__ __noinline__ void route_scan_serial(int ne, int nk, const float *scores, float *choice, int *ids,
+                                                      float *gates, int lane) {
+    for (int k = 0; k < nk; k++) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < ne; e += 32) {
+            const float c = choice[e];
+            if (c > bv) {  // strict: first maximum in this lane's (ascending) run
+                bv = c;
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
+        if (lane == 0) {
+            ids[k] = bi;
+            gates[k] = scores[bi];
+            choice[bi] = -INFINITY;  // used
+        }
+        __syncwarp();
+    }
+}
+
 __device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int gating, int weights_norm,
                                              float weights_scale, const float *scores, float *choice, int *ids,
                                              float *gates, int *ids_out, float *gates_out, int lane) {
-    if (!ranked) {
-        for (int k = 0; k < nk; k++) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int e = lane; e < ne; e += 32) {
-                const float c = choice[e];
-                if (c > bv) {  // strict: first maximum in this lane's (ascending) run
-                    bv = c;
-                    bi = e;
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (bi == 0x7fffffff) bi = 0;  // nothing beats -inf: the serial scan keeps index 0
-            if (lane == 0) {
-                ids[k] = bi;
-                gates[k] = scores[bi];
-                choice[bi] = -INFINITY;  // used
-            }
-            __syncwarp();
-        }
-    }
+    if (!ranked) route_scan_serial(ne, nk, scores, choice, ids, gates, lane);
     if (gating == 3 && lane == 0) {  // softmax over the selected k (tensor.zig:18 softmax)
         float m = -INFINITY;
         for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
@@ -164,6 +176,128 @@ __device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int ga
         gates[k] = g;
     }
     __syncwarp();
+}
+
+// Order-preserving 32-bit key of a float (+0 and -0 map to the same key):
+// a > b  <=>  key(a) > key(b) for non-NaN a, b.
+__device__ __forceinline__ uint32_t f32_order_key(float x) {
+    const uint32_t u = x == 0.0f ? 0u : __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// moe.zig:106-158 route by ONE warp with the expert values in registers
+// (lane l holds experts l, l+32, ..., ne <= 32*RW_MAX), bit-identical to
+// route_block: the softmax sum runs in route_block's order (per 128-thread
+// stride, then per warp, then the four warp partials in order), and top-k
+// takes k rounds of a warp arg-max on (value, lowest index) keys, which is the
+// serial first-max order when every value is > -inf; otherwise the serial scan
+// of route_finish runs on scores/choice in shared memory. ids/gates: shared
+// memory (nk words); logits may be global memory written by other CTAs of the
+// grid (read with ld.global.cg) or shared memory.
+constexpr int RW_MAX = 8;
+
+template <bool GLOBAL_CG, int RW = RW_MAX>
+__device__ __forceinline__ void route_warp_regs(const float *logits, const float *bias, int ne, int nk, int gating,
+                                                int weights_norm, float weights_scale, float *scores, float *choice,
+                                                int *ids, float *gates, int *ids_out, float *gates_out, int lane) {
+    float v[RW], sc[RW];
+#pragma unroll
+    for (int t = 0; t < RW; t++) {
+        const int e = lane + 32 * t;
+        v[t] = e < ne ? (GLOBAL_CG ? __ldcg(logits + e) : logits[e]) : -INFINITY;
+    }
+    if (gating == 2) {
+#pragma unroll
+        for (int t = 0; t < RW; t++) sc[t] = fdiv(1.0f, fadd(1.0f, expf(-v[t])));
+    } else if (gating == 1) {
+        float m = -INFINITY;  // fmaxf skips NaN, so the lane maximum is never NaN
+#pragma unroll
+        for (int t = 0; t < RW; t++)
+            if (lane + 32 * t < ne) m = fmaxf(m, v[t]);
+        {
+            const uint32_t km = __reduce_max_sync(0xffffffffu, f32_order_key(m));
+            m = __uint_as_float((km & 0x80000000u) ? (km & 0x7fffffffu) : ~km);
+        }
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // route_block's warp w sums experts 32w + l + 128j
+#pragma unroll
+        for (int t = 0; t < RW; t++) {
+            sc[t] = expf(fsub(v[t], m));
+            if (lane + 32 * t < ne) part[t & 3] = fadd(part[t & 3], sc[t]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int w = 0; w < 4; w++) part[w] = fadd(part[w], __shfl_xor_sync(0xffffffffu, part[w], o));
+        const float tot = fadd(fadd(fadd(part[0], part[1]), part[2]), part[3]);
+        const float inv = fdiv(1.0f, tot);
+#pragma unroll
+        for (int t = 0; t < RW; t++) sc[t] = fmul(sc[t], inv);
+    } else {
+#pragma unroll
+        for (int t = 0; t < RW; t++) sc[t] = v[t];
+    }
+    bool fin = true;
+    uint32_t key[RW];
+    int ei[RW];
+#pragma unroll
+    for (int t = 0; t < RW; t++) {
+        const int e = lane + 32 * t;
+        const float c = bias && e < ne ? fadd(sc[t], bias[e]) : sc[t];
+        if (e < ne) fin &= c > -INFINITY;
+        key[t] = e < ne ? f32_order_key(c) : 0u;  // 0: below every real key (exhausted / absent)
+        ei[t] = e;
+        v[t] = c;
+    }
+    fin = __all_sync(0xffffffffu, fin);
+    if (fin) {
+        // sort the lane's candidates by (value desc, index asc), then take k
+        // rounds of the warp maximum of the lanes' current heads
+        float sv[RW];
+#pragma unroll
+        for (int t = 0; t < RW; t++) sv[t] = sc[t];
+#pragma unroll
+        for (int i = 0; i < RW; i++)
+#pragma unroll
+            for (int j = RW - 1; j > i; j--) {
+                const bool sw = key[j] > key[j - 1] || (key[j] == key[j - 1] && ei[j] < ei[j - 1]);
+                if (sw) {
+                    const uint32_t tk = key[j]; key[j] = key[j - 1]; key[j - 1] = tk;
+                    const int te = ei[j]; ei[j] = ei[j - 1]; ei[j - 1] = te;
+                    const float ts = sv[j]; sv[j] = sv[j - 1]; sv[j - 1] = ts;
+                }
+            }
+        for (int k = 0; k < nk; k++) {
+            const uint32_t kmax = __reduce_max_sync(0xffffffffu, key[0]);
+            const bool mine = key[0] == kmax;
+            const uint32_t ball = __ballot_sync(0xffffffffu, mine);
+            bool win = mine;
+            if (__popc(ball) > 1)  // equal values: the lowest index wins
+                win = mine && (uint32_t)ei[0] == __reduce_min_sync(0xffffffffu, mine ? (uint32_t)ei[0] : 0xffffffffu);
+            if (win) {
+                ids[k] = ei[0];
+                gates[k] = sv[0];
+#pragma unroll
+                for (int t = 0; t + 1 < RW; t++) {
+                    key[t] = key[t + 1];
+                    ei[t] = ei[t + 1];
+                    sv[t] = sv[t + 1];
+                }
+                key[RW - 1] = 0u;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < RW; t++) {
+            const int e = lane + 32 * t;
+            if (e < ne) {
+                scores[e] = sc[t];
+                choice[e] = v[t];
+            }
+        }
+    }
+    __syncwarp();
+    route_finish(fin, ne, nk, gating, weights_norm, weights_scale, scores, choice, ids, gates, ids_out, gates_out,
+                 lane);
 }
 
 // moe.zig:106-158 route by the first ROUTE_THREADS threads of a CTA (the

@@ -1127,17 +1127,16 @@ extern "C" int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_laye
     A.weights_scale = D0.weights_scale;
     A.act_stride = (int)align256(D0.ffn);
     if (!stack_supported(A, gty, dty)) return decline("layer shape not covered by the stack kernel");
-    const size_t lay_b = align256(n_layers * sizeof(StackLayer)), x_b = align256(D0.dim * 4);
-    const size_t lg_b = align256(D0.n_expert * 4), act_b = align256(D0.n_used * (size_t)A.act_stride * 4);
-    const size_t total = lay_b + 2 * x_b + lg_b + act_b + 256;
+    const size_t lay_b = align256(n_layers * sizeof(StackLayer)), part_b = align256(D0.n_used * D0.dim * 4);
+    const size_t lg_b = align256((D0.n_expert + 32) * 4 * LOGIT_REPLICAS), act_b = align256(D0.n_used * (size_t)A.act_stride * 4);
+    const size_t total = lay_b + part_b + lg_b + act_b + 256;
     CK(cudaMalloc(&S.mem, total));
     uint8_t *p = static_cast<uint8_t *>(S.mem);
     A.layers = reinterpret_cast<const StackLayer *>(p);
-    A.xbuf0 = reinterpret_cast<float *>(p + lay_b);
-    A.xbuf1 = reinterpret_cast<float *>(p + lay_b + x_b);
-    A.logits = reinterpret_cast<float *>(p + lay_b + 2 * x_b);
-    A.act = reinterpret_cast<float *>(p + lay_b + 2 * x_b + lg_b);
-    A.bar = reinterpret_cast<unsigned *>(p + lay_b + 2 * x_b + lg_b + act_b);
+    A.part = reinterpret_cast<float *>(p + lay_b);
+    A.logits = reinterpret_cast<float *>(p + lay_b + part_b);
+    A.act = reinterpret_cast<float *>(p + lay_b + part_b + lg_b);
+    A.bar = reinterpret_cast<unsigned *>(p + lay_b + part_b + lg_b + act_b);
     A.err = reinterpret_cast<int *>(A.bar + 2);
     CK(cudaMemcpy(p, host.data(), n_layers * sizeof(StackLayer), cudaMemcpyHostToDevice));
     CK(cudaMemset(A.bar, 0, 256));
@@ -1172,11 +1171,30 @@ extern "C" int loom_cuda_stack_error(uint64_t handle) {
     return v;
 }
 
+extern "C" int loom_cuda_stack_trace(uint64_t handle, int enable, uint64_t *out, size_t n) {
+    auto it = g_stacks.find(handle);
+    if (it == g_stacks.end()) return decline("unknown stack");
+    StackArgs &A = it->second.args;
+    const size_t slots = (size_t)A.n_layers * STACK_TRACE_WORDS;
+    if (enable && !A.trace) CK(cudaMalloc(&A.trace, slots * 8));
+    if (enable) {
+        CK(cudaMemset(A.trace, 0, slots * 8));
+        return LOOM_CUDA_OK;
+    }
+    if (!A.trace) return decline("stack trace not enabled");
+    CK(cudaDeviceSynchronize());
+    if (out) CK(cudaMemcpy(out, A.trace, (n < slots ? n : slots) * 8, cudaMemcpyDeviceToHost));
+    cudaFree(A.trace);
+    A.trace = nullptr;
+    return LOOM_CUDA_OK;
+}
+
 extern "C" int loom_cuda_stack_free(uint64_t handle) {
     auto it = g_stacks.find(handle);
     if (it == g_stacks.end()) return decline("unknown stack");
     cudaDeviceSynchronize();
     cudaFree(it->second.mem);
+    if (it->second.args.trace) cudaFree(it->second.args.trace);
     g_stacks.erase(it);
     return LOOM_CUDA_OK;
 }

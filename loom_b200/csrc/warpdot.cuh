@@ -183,6 +183,51 @@ template <> struct QT<T_Q6_K> {
     }
 };
 
+// Q4_KW and Q6_K read from shared memory (tiles staged there by bulk copies):
+// same fragments and arithmetic, plain loads instead of streaming global
+// loads, and the int8 activations in a padded shared-memory layout that keeps
+// a quarter-warp's 16-byte loads on distinct banks:
+//   Q4_KW_S  block stride 320 bytes, 64-value chunk j at 80*j
+//   Q6_K_S   block stride 320 bytes, 128-value half n at 160*n
+constexpr int T_Q4_KW_S = 113;
+constexpr int T_Q6_K_S = 114;
+constexpr int XPAD_BLOCK = 320;
+
+__device__ __forceinline__ int xpad_q4kw(int i) { return (i >> 8) * XPAD_BLOCK + ((i & 255) >> 6) * 80 + (i & 63); }
+__device__ __forceinline__ int xpad_q6k(int i) { return (i >> 8) * XPAD_BLOCK + ((i & 255) >> 7) * 160 + (i & 127); }
+
+template <> struct QT<T_Q4_KW_S> : QT<T_Q4_KW> {
+    static constexpr int BE = XPAD_BLOCK;  // activation block stride (bytes)
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int sub) {
+        const uint8_t *blk = w.q + gb * 144;
+        return Frag{*reinterpret_cast<const uint4 *>(blk), *reinterpret_cast<const uint4 *>(blk + 16 + 32 * sub),
+                    *reinterpret_cast<const uint4 *>(blk + 32 + 32 * sub)};
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int j, const int8_t *xq, const int32_t *xs, int &I,
+                                                int &M) {
+        QT<T_Q4_KW>::part(f, j, xq + 16 * j, xs, I, M);  // chunk j at 80*j
+    }
+};
+
+template <> struct QT<T_Q6_K_S> : QT<T_Q6_K> {
+    static constexpr int BE = XPAD_BLOCK;
+    __device__ __forceinline__ static Frag load(const WDev &w, uint64_t gb, int sub) {
+        const int n = sub >> 1, hh = sub & 1;
+        const uint8_t *qb = w.q + gb * 192;
+        Frag f;
+        f.a = *reinterpret_cast<const uint4 *>(qb + 64 * n + 16 * hh);
+        f.b = *reinterpret_cast<const uint4 *>(qb + 64 * n + 32 + 16 * hh);
+        f.h = *reinterpret_cast<const uint4 *>(qb + 128 + 32 * n + 16 * hh);
+        f.s = *reinterpret_cast<const uint4 *>(w.sc + gb * 16);
+        f.d = w.d[gb];
+        return f;
+    }
+    __device__ __forceinline__ static void part(const Frag &f, int sub, const int8_t *xq, const int32_t *xs, int &I,
+                                                int &M) {
+        QT<T_Q6_K>::part(f, sub, xq + 32 * (sub >> 1), xs, I, M);  // half n at 160*n
+    }
+};
+
 template <> struct QT<T_Q8_0> {
     static constexpr int LPB = 2, BE = 32, SPB = 1;
     struct Frag {
@@ -372,10 +417,37 @@ template <int TY, int S, int NB> struct CEng {
 #pragma unroll
             for (int o = 1; o < Q::LPB; o <<= 1) {
                 I += __shfl_xor_sync(0xffffffffu, I, o);
-                if constexpr (TY == T_Q4_K || TY == T_Q4_KW) M += __shfl_xor_sync(0xffffffffu, M, o);
+                if constexpr (TY == T_Q4_K || TY == T_Q4_KW || TY == T_Q4_KW_S) M += __shfl_xor_sync(0xffffffffu, M, o);
             }
             term[j] = Q::term(fr.f[j], I, M, xv.d[b]);
         }
+        sum_terms(term, acc);
+    }
+    // load + finish in one pass for operands in shared memory (no fragment
+    // array held across the loads)
+    template <class Streams>
+    __device__ __forceinline__ static void run(const Streams &st, float (&acc)[S], int lane) {
+        const int grp = lane / Q::LPB, sub = lane % Q::LPB;
+        float term[MAXU];
+#pragma unroll
+        for (int j = 0; j < MAXU; j++) {
+            int s, b;
+            unit(j, grp, s, b);
+            const typename Q::Frag f = Q::load(st.w(s), st.gb(s) + b, sub);
+            const XV xv = st.x(s);
+            int I, M;
+            Q::part(f, sub, xv.q + b * Q::BE, xv.s + b * Q::SPB, I, M);
+#pragma unroll
+            for (int o = 1; o < Q::LPB; o <<= 1) {
+                I += __shfl_xor_sync(0xffffffffu, I, o);
+                if constexpr (TY == T_Q4_K || TY == T_Q4_KW || TY == T_Q4_KW_S) M += __shfl_xor_sync(0xffffffffu, M, o);
+            }
+            term[j] = Q::term(f, I, M, xv.d[b]);
+        }
+        sum_terms(term, acc);
+    }
+    // each stream's block terms added in block order from +0
+    __device__ __forceinline__ static void sum_terms(const float (&term)[MAXU], float (&acc)[S]) {
 #pragma unroll
         for (int s = 0; s < S; s++) {
             float a = 0.0f;

@@ -114,6 +114,17 @@ class Stack:
     def error(self) -> int:
         return int(_lib.lib().loom_cuda_stack_error(self.handle))
 
+    def trace_enable(self) -> None:
+        _lib.must(_lib.lib().loom_cuda_stack_trace(self.handle, 1, None, 0), "stack_trace")
+
+    def trace_read(self):
+        """[n_layers][12 + 26]: 12 globaltimer ns points, then (max, sum) over
+        CTAs of 16 sections' cycles (see loom_cuda_stack_trace)."""
+        import numpy as np
+        out = np.zeros((self.n_layers, 12 + 2 * 16), np.uint64)
+        _lib.must(_lib.lib().loom_cuda_stack_trace(self.handle, 0, out.ctypes.data, out.size), "stack_trace")
+        return out
+
     def free(self) -> None:
         if self.handle:
             _lib.lib().loom_cuda_stack_free(self.handle)
