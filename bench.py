@@ -323,14 +323,14 @@ def trace_stack(stack, step, stream, torch):
         step(stream.cuda_stream)
     tr = stack.trace_read().astype(np.float64)
     rel = tr[1:] - tr[1:, :1]
-    names = ["start", "router_rows_done", "route_barrier_exit", "route_done", "gateup_done",
-             "gateup_barrier_exit", "act_quantized", "down_done", "unused", "gateup_tiles_landed",
+    names = ["start", "router_rows_done", "unused", "route_done", "gateup_done",
+             "unused", "act_quantized", "down_done", "unused", "gateup_tiles_landed",
              "down_tiles_landed"]
     out = {n: round(float(np.mean(rel[:, i])) / 1e3, 2) for i, n in enumerate(names) if i and n != "unused"}
     out["worst_layer_total"] = round(float(np.max(np.diff(tr[:, 0]))) / 1e3, 2)
     out["layer_total"] = round(float(np.mean(np.diff(tr[:, 0]))) / 1e3, 2)
-    sec = ["p1_load", "router_dot", "bar1_wait", "route", "stage_issue", "gateup_tiles_wait", "gateup_compute",
-           "bar2_wait", "act_load", "act_quant", "down_tiles_wait", "down_compute", "bar3_wait", "gateup_dots_w0", "act_store_w0", "spare"]
+    sec = ["p1_load", "router_dot", "logits_wait", "route", "stage_issue", "gateup_tiles_wait", "gateup_compute",
+           "unused", "act_wait", "act_quant", "down_tiles_wait", "down_compute", "bar3_wait", "gateup_dots_w0", "act_store_w0", "spare"]
     cyc = tr[1:, 12:].reshape(-1, 16, 2)
     G = torch.cuda.get_device_properties(0).multi_processor_count
     out["cycles_max_mean"] = {n: [int(np.mean(cyc[:, i, 0])), int(np.mean(cyc[:, i, 1]) / G)] for i, n in enumerate(sec)}

@@ -1059,6 +1059,20 @@ __device__ __forceinline__ bool grid_barrier(unsigned long long *ctr, unsigned l
     return s_ok != 0;
 }
 
+// Tagged words: a float and the tag of the layer (and launch) that wrote it,
+// in one 8-byte store, so a reader that sees the tag sees the value (one
+// single-copy-atomic access) and needs no barrier of its own.
+constexpr uint32_t TAG_POLLS = 1u << 20;  // bounded poll on tagged data (~1 s)
+
+__device__ __forceinline__ unsigned long long tagged(float v, uint32_t tag) {
+    return ((unsigned long long)tag << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Down streams of the stack kernel: SC consecutive output rows of ONE expert
 // (this CTA's expert), weights staged in shared memory as a row-major tile
 // [rows][NBD blocks], the expert's int8 activations (xpad_q6k layout) shared
@@ -1099,6 +1113,9 @@ struct StackSplit {
 // Shared-memory map of the stack kernel (recomputed per phase so that no
 // pointer stays live in registers across phases). Sizes depend on the grid:
 // ngmax gate/up groups and nrmax down rows per CTA.
+constexpr int MB_ROUTER = 0, MB_DOWN = 1, MB_GATEUP = 2, MB_COUNT = 4;
+constexpr int STACK_MAX_LAYERS = 64;
+
 template <int NBG, int NR, int NBD> struct StackSmem {
     static constexpr int dim = NBG * 256;
     static constexpr int GU_HALF = NR * NBG * 144;  // one group's NR rows of gate (or of up), Q4_K
@@ -1112,7 +1129,7 @@ template <int NBG, int NR, int NBD> struct StackSmem {
     float *sg;        // [64]
     int *doff;        // [8]
     float *red;       // [8]
-    uint64_t *mbar;   // [4]: router rows, gate/up tiles, down tiles
+    uint64_t *mbar;   // [MB_COUNT]: router rows, down tile, gate/up tiles
     float *rbuf;      // [rpc][dim] this CTA's router rows of the current layer
     uint8_t *gub;     // gate tiles [ngmax][GU_HALF], then up tiles [ngmax][GU_HALF]
     uint8_t *dq;      // [nrmax*NBD][192] down tile quants
@@ -1122,6 +1139,7 @@ template <int NBG, int NR, int NBD> struct StackSmem {
     int8_t *aq;       // [ffn/256 * XPAD_BLOCK]
     float *ad;        // [ffn/256]
     int32_t *as;      // [ffn/16]
+    StackLayer *lys;  // [n_layers] the layer descriptors
     static __host__ __device__ size_t dslot(int nrmax) { return ((size_t)nrmax * NBD * 2 + 15) / 16 * 16 + 16; }
     __device__ __forceinline__ StackSmem(uint8_t *base, int ne, int ffn, int rpc, int ngmax, int nrmax) {
         xs = reinterpret_cast<float *>(base);
@@ -1135,7 +1153,7 @@ template <int NBG, int NR, int NBD> struct StackSmem {
         doff = reinterpret_cast<int *>(sg + 64);
         red = reinterpret_cast<float *>(doff + 8);
         mbar = reinterpret_cast<uint64_t *>(red + 8);  // 16-byte aligned: ne % 4 == 0
-        rbuf = reinterpret_cast<float *>(mbar + 4);
+        rbuf = reinterpret_cast<float *>(mbar + MB_COUNT);
         gub = reinterpret_cast<uint8_t *>(rbuf + (size_t)rpc * dim);
         dq = gub + (size_t)2 * ngmax * GU_HALF;
         dsc = dq + (size_t)nrmax * NBD * 192;
@@ -1144,9 +1162,11 @@ template <int NBG, int NR, int NBD> struct StackSmem {
         aq = reinterpret_cast<int8_t *>(af + ffn);
         ad = reinterpret_cast<float *>(aq + (size_t)(ffn / 256) * XPAD_BLOCK);
         as = reinterpret_cast<int32_t *>(ad + ffn / 256);
+        lys = reinterpret_cast<StackLayer *>(base + ((reinterpret_cast<uintptr_t>(as + ffn / 16) - reinterpret_cast<uintptr_t>(base) + 15) & ~uintptr_t(15)));
     }
-    static size_t bytes(int ne, int ffn, int rpc, int ngmax, int nrmax) {
-        return (size_t)dim * 4 + NBG * XPAD_BLOCK + NBG * 4 + NBG * 64 + (size_t)2 * ne * 4 + 64 * 8 + 32 + 32 + 32 +
+    static size_t bytes(int ne, int ffn, int rpc, int ngmax, int nrmax, int n_layers) {
+        return (size_t)dim * 4 + NBG * XPAD_BLOCK + NBG * 4 + NBG * 64 + (size_t)2 * ne * 4 + 64 * 8 + 32 + 32 + 8 * MB_COUNT +
+               16 + (size_t)n_layers * sizeof(StackLayer) +
                (size_t)rpc * dim * 4 + (size_t)2 * ngmax * GU_HALF + (size_t)nrmax * NBD * (192 + 16) + dslot(nrmax) +
                (size_t)ffn * 4 + (size_t)(ffn / 256) * XPAD_BLOCK + (size_t)(ffn / 256) * 4 + (size_t)(ffn / 16) * 4;
     }
@@ -1188,7 +1208,6 @@ __device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const Sta
     const uintptr_t d0 = reinterpret_cast<uintptr_t>(Ly.dn.d + b0);
     const uintptr_t da = d0 & ~uintptr_t(15), de = (d0 + nb * 2 + 15) & ~uintptr_t(15);
     if (lane == 0) {
-        fence_proxy_async_smem();
         if (ng) mbar_expect_tx(mb_gu, (uint32_t)(2 * ng * SM::GU_HALF));
         if (nr) {
             *doff = (int)((d0 - da) / 2);
@@ -1199,7 +1218,7 @@ __device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const Sta
     fence_proxy_async_smem();
     // gate/up: the CTA's groups form a few runs inside one expert each,
     // contiguous in global memory and in the tile: lane 2i copies run i's gate
-    // rows, lane 2i+1 its up rows
+    // rows, lane 2i+1 its up rows, all on one barrier
     if (ng) {
         const int ka = P.g0 / per_e, kb = (P.g1 - 1) / per_e;
         for (int q = lane; q < 2 * (kb - ka + 1); q += 32) {
@@ -1234,14 +1253,18 @@ __device__ __forceinline__ float router_dot_smem(const float *wr, const float *x
     return r;
 }
 
-// Bounded wait on a staging barrier; on time-out raise bit 4 of *err (the
-// other CTAs' grid barriers then give up early), wait once more so that no
-// copy is left in flight, and tell the caller to leave.
-__device__ __noinline__ bool stage_wait(uint64_t *mbar, int parity, int *err) {
-    if (mbar_wait(mbar, parity, STAGE_POLLS)) return true;
-    if (threadIdx.x == 0) atomicOr(err, 4);
-    mbar_wait(mbar, parity, STAGE_POLLS);
-    return false;
+// Bounded wait on a staging barrier. Only thread 0 polls; the verdict is
+// shared, so every thread of the CTA takes the same path. On a
+// time-out bit 4 of *err is raised: the caller skips its work and the next
+// grid barrier, seeing *err, lets the whole grid leave (after draining).
+__device__ __noinline__ bool cta_stage_wait(uint64_t *mbar, int parity, int *err) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        s_ok = mbar_wait(mbar, parity, STAGE_POLLS);
+        if (!s_ok) atomicOr(err, 4);
+    }
+    __syncthreads();
+    return s_ok != 0;
 }
 
 // One activation block of 256 values (8 per lane) quantized as quantizeX256
@@ -1256,6 +1279,29 @@ __device__ __noinline__ void quant_block256_padded(const float *src, int8_t *qba
     v[0] = p.x, v[1] = p.y, v[2] = p.z, v[3] = p.w, v[4] = q.x, v[5] = q.y, v[6] = q.z, v[7] = q.w;
     quant_vals8(v, true, 32, qbase + (Q6K ? xpad_q6k(lane * 8) : xpad_q4kw(lane * 8)), d256, s16 + lane / 2, nullptr,
                 lane);
+}
+
+// Every CTA, on every way out: count the exit; the last one to leave advances
+// the launch epoch (the next launch's tags), so stale tagged words of this
+// launch never match a later one.
+__device__ __noinline__ void stack_exit(const StackArgs &A) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        unsigned *ex = A.bar + 6;
+        if (atomicAdd(ex, 1u) == gridDim.x - 1) {
+            *ex = 0;
+            atomicAdd(A.bar + 4, 1u);
+        }
+    }
+}
+
+// Leaving early (an error): let every copy of layer l this CTA requested land
+// first (bounded waits), so that no bulk copy into shared memory outlives it.
+__device__ __noinline__ void stack_drain(uint64_t *mbar, const StackSplit &P, int l) {
+    if (threadIdx.x != 0) return;
+    if (P.g1 > P.g0) mbar_wait(mbar + MB_GATEUP, l & 1, STAGE_POLLS);
+    if (P.rb > P.ra) mbar_wait(mbar + MB_DOWN, l & 1, STAGE_POLLS);
 }
 
 // x of the next layer: x += sum over expert slots k (in order, from +0) of the
@@ -1301,17 +1347,21 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
 #define STACK_SMEM SM S(smraw, A.n_expert, ffn, rpc, ngmax, nrmax)
     unsigned long long *ctr = reinterpret_cast<unsigned long long *>(A.bar);
     unsigned long long target = 0;  // thread 0: this launch's barrier targets
+    // tags of this launch: the epoch advances once per completed launch
+    const uint32_t tag0 = *reinterpret_cast<volatile unsigned *>(A.bar + 4) * 64u;
     if (threadIdx.x == 0) {
-        // Every earlier launch completed all 3 * n_layers barriers, so the
+        // Every earlier launch completed all n_layers barriers, so the
         // counter stood at a multiple of that many rounds when this launch
         // began; fewer than G arrivals of this launch can precede this read.
-        const unsigned long long per = 3ull * A.n_layers * G, v = ld_acquire_u64(ctr);
+        const unsigned long long per = (unsigned long long)A.n_layers * G, v = ld_acquire_u64(ctr);
         target = v - v % per;
         STACK_SMEM;
-        mbar_init(S.mbar + 0, 1);
-        mbar_init(S.mbar + 1, 1);
-        mbar_init(S.mbar + 2, 1);
-        stage_router_rows(A, 0, S.rbuf, S.mbar);
+        for (int i = 0; i < MB_COUNT; i++) mbar_init(S.mbar + i, 1);
+        stage_router_rows(A, 0, S.rbuf, S.mbar + MB_ROUTER);
+    }
+    {
+        STACK_SMEM;
+        for (int i = threadIdx.x; i < A.n_layers; i += blockDim.x) S.lys[i] = A.layers[i];
     }
     __syncthreads();
     CycTrace cy{nullptr, TRACE ? clock64() : 0};
@@ -1320,6 +1370,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
         unsigned long long *tr = TRACE ? A.trace + (size_t)l * STACK_TRACE_WORDS : nullptr;
         if (TRACE) cy.base = tr + STACK_TRACE_SLOTS;
         if (TRACE && c == 0 && threadIdx.x == 0) tr[0] = gtimer();  // the previous barrier's exit
+        const uint32_t tag = tag0 + (uint32_t)l + 1u;
         {   // ---- P1: x of this layer (x_in, or the previous layer's x plus its combined experts), router rows . x
             STACK_SMEM;
             if (l == 0) {
@@ -1329,16 +1380,17 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
             } else {
                 combine_parts(A.part, nk, dim, S.xs);
             }
-            if (c < A.n_expert && !stage_wait(S.mbar, l & 1, A.err)) return;
             __syncthreads();
+            const bool ok = c >= A.n_expert || cta_stage_wait(S.mbar + MB_ROUTER, l & 1, A.err);
             if (TRACE) cy.mark(0);  // x ready, router rows landed
             // warps with a router row take it; the rest quantize x for gate/up meanwhile
             const int nrw = (A.n_expert - c + G - 1) / G;  // this CTA's router rows
-            if (warp < nrw) {
+            if (!ok) {
+            } else if (warp < nrw) {
 #pragma unroll 1
                 for (int row = c + warp * G, j = warp; row < A.n_expert; row += PS_WARPS * G, j += PS_WARPS) {
                     const float r = router_dot_smem(S.rbuf + (size_t)j * dim, S.xs, dim, lane);
-                    if (lane < LOGIT_REPLICAS) A.logits[(size_t)lane * lg_stride + row] = r;
+                    if (lane < LOGIT_REPLICAS) A.logits[(size_t)lane * lg_stride + row] = tagged(r, tag);
                 }
             } else {
                 const int nq = PS_WARPS - (nrw < PS_WARPS ? nrw : PS_WARPS - 1);
@@ -1347,68 +1399,104 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                     quant_block256_padded<false>(S.xs + b * 256, S.xq + b * XPAD_BLOCK, S.xqd + b, S.xqs + b * 16, lane);
             }
         }
-        if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 1 : nullptr, TRACE ? tr + 2 : nullptr,
-                          TRACE ? &cy : nullptr, 1))
-            return;
+        if (TRACE) {
+            __syncthreads();
+            trace_max(tr + 1);
+            cy.mark(1);  // router rows and x quantization done
+        }
         {   // ---- P2: route (replicated in every CTA); stage gate/up and down tiles; gate/up
             STACK_SMEM;
             const int ne = A.n_expert;
-            if (warp == 0)
-                route_warp_regs<true, RW>(A.logits + (size_t)(c % LOGIT_REPLICAS) * lg_stride, nullptr, ne, nk,
-                                          A.gating, A.weights_norm, A.weights_scale, S.scores, S.choice, S.sid, S.sg,
-                                          S.sid, S.sg, lane);
+            if (warp == 0) {
+                // the logits of this layer, as they arrive (tagged words of replica c % R)
+                const unsigned long long *lg = A.logits + (size_t)(c % LOGIT_REPLICAS) * lg_stride;
+                float v[RW];
+                uint32_t it = 0;
+                for (; it < TAG_POLLS; it++) {
+                    bool have = true;
+#pragma unroll
+                    for (int t = 0; t < RW; t++) {
+                        const int e = lane + 32 * t;
+                        v[t] = -INFINITY;
+                        if (e < ne) {
+                            const unsigned long long w = ld_relaxed_u64(lg + e);
+                            v[t] = __uint_as_float((uint32_t)w);
+                            have &= (uint32_t)(w >> 32) == tag;
+                        }
+                    }
+                    if (__all_sync(0xffffffffu, have)) break;
+                }
+                if (it == TAG_POLLS && lane == 0) atomicOr(A.err, 8);
+                if (TRACE) cy.mark(2);  // logits arrived
+                route_warp_vals<RW>(v, nullptr, ne, nk, A.gating, A.weights_norm, A.weights_scale, S.scores, S.choice,
+                                    S.sid, S.sg, S.sid, S.sg, lane);
+            }
             if (TRACE) cy.mark(3);  // route (thread 0's warp)
             __syncthreads();
             if (TRACE) trace_max(tr + 3);
-            const StackLayer &Ly = A.layers[l];
             if (warp == 0)
-                stage_expert_tiles<NBG, NR, NBD>(A, Ly, S.sid, S.doff, S.gub, S.dq, S.dsc, S.dd, S.mbar + 1, S.mbar + 2,
-                                                 P, ngmax);
+                stage_expert_tiles<NBG, NR, NBD>(A, S.lys[l], S.sid, S.doff, S.gub, S.dq, S.dsc, S.dd,
+                                                 S.mbar + MB_GATEUP, S.mbar + MB_DOWN, P, ngmax);
             if (TRACE) cy.mark(4);  // tiles requested
             if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = S.sid[threadIdx.x];
-            if (P.g1 > P.g0) {
-                if (!stage_wait(S.mbar + 1, l & 1, A.err)) {
-                    if (P.rb > P.ra) mbar_wait(S.mbar + 2, l & 1, STAGE_POLLS);
-                    return;
-                }
-                if (TRACE) {
-                    trace_max(tr + 9);
-                    cy.mark(5);  // gate/up tiles landed
-                }
-                const WDev wt{S.gub, nullptr, nullptr, T_Q4_K, 0};
+            const bool ok = P.g1 <= P.g0 || cta_stage_wait(S.mbar + MB_GATEUP, l & 1, A.err);
+            if (TRACE) {
+                trace_max(tr + 9);
+                cy.mark(5);  // gate/up tiles landed
+            }
+            const WDev wt{S.gub, nullptr, nullptr, T_Q4_K, 0};
 #pragma unroll 1
-                for (int g = warp; g < P.g1 - P.g0; g += PS_WARPS) {
-                    const int grp = P.g0 + g, k = grp / per_e, rl = (grp % per_e) * NR;
-                    GateUpStreams<NR> st{wt, wt, (uint64_t)g * NR * NBG, (uint64_t)(ngmax + g) * NR * NBG, NBG,
-                                         XV{S.xq, S.xqd, S.xqs}};
-                    float acc[2 * NR];
-                    EG::run(st, acc, lane);
-                    if (TRACE && g == 0) cy.mark(13);  // warp 0's gate/up dots
-                    if (lane < NR)
+            for (int g = warp; ok && g < P.g1 - P.g0; g += PS_WARPS) {
+                const int grp = P.g0 + g, k = grp / per_e, rl = (grp % per_e) * NR;
+                GateUpStreams<NR> st{wt, wt, (uint64_t)g * NR * NBG, (uint64_t)(ngmax + g) * NR * NBG, NBG,
+                                     XV{S.xq, S.xqd, S.xqs}};
+                float acc[2 * NR];
+                EG::run(st, acc, lane);
+                if (TRACE && g == 0) cy.mark(13);  // warp 0's gate/up dots
+                if (lane < NR) {  // lane i: silu(gate row i) * up row i
+                    float a = acc[0], u = acc[NR];
 #pragma unroll
-                        for (int i = 0; i < NR; i++)
-                            if (i == lane)
-                                A.act[(size_t)k * A.act_stride + rl + i] =
-                                    fmul(fdiv(acc[i], fadd(1.0f, expf(-acc[i]))), acc[NR + i]);
-                    if (TRACE && g == 0) cy.mark(14);  // warp 0's activations stored
+                    for (int i = 1; i < NR; i++)
+                        if (lane == i) a = acc[i], u = acc[NR + i];
+                    A.act[(size_t)k * A.act_stride + rl + lane] = tagged(fmul(fdiv(a, fadd(1.0f, expf(-a))), u), tag);
                 }
+                if (TRACE && g == 0) cy.mark(14);  // warp 0's activations stored
             }
         }
-        if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 4 : nullptr, TRACE ? tr + 5 : nullptr,
-                          TRACE ? &cy : nullptr, 6)) {
-            STACK_SMEM;
-            if (P.rb > P.ra) mbar_wait(S.mbar + 2, l & 1, STAGE_POLLS);
-            return;
+        if (TRACE) {
+            __syncthreads();
+            trace_max(tr + 4);
+            cy.mark(6);  // gate/up done
         }
         {   // ---- P3: this CTA's expert: its activations quantized, rows ra..rb of its down matrix
             STACK_SMEM;
             const int nbf = ffn / 256;
-#pragma unroll 1
-            for (int i = threadIdx.x; i < ffn / 4; i += blockDim.x)
-                reinterpret_cast<float4 *>(S.af)[i] =
-                    __ldcg(reinterpret_cast<const float4 *>(A.act + (size_t)P.kd * A.act_stride) + i);
+            {   // this expert's activations as they arrive (tagged words)
+                const unsigned long long *src = A.act + (size_t)P.kd * A.act_stride;
+                constexpr int PER = 2;  // entries per thread polled together (ffn <= PER * blockDim.x)
+                unsigned long long w[PER];
+                bool have = false;
+                uint32_t it = 0;
+                for (; it < TAG_POLLS && !have; it++) {
+                    have = true;
+#pragma unroll
+                    for (int j = 0; j < PER; j++) {
+                        const int i = threadIdx.x + j * blockDim.x;
+                        if (i < ffn) {
+                            w[j] = ld_relaxed_u64(src + i);
+                            have &= (uint32_t)(w[j] >> 32) == tag;
+                        }
+                    }
+                }
+                if (!have) atomicOr(A.err, 8);
+#pragma unroll
+                for (int j = 0; j < PER; j++) {
+                    const int i = threadIdx.x + j * blockDim.x;
+                    if (i < ffn) S.af[i] = __uint_as_float((uint32_t)w[j]);
+                }
+            }
             __syncthreads();
-            if (TRACE) cy.mark(8);  // activations loaded
+            if (TRACE) cy.mark(8);  // activations arrived
             if (warp < nbf)
                 quant_block256_padded<true>(S.af + warp * 256, S.aq + warp * XPAD_BLOCK, S.ad + warp, S.as + warp * 16,
                                             lane);
@@ -1417,7 +1505,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 cy.mark(9);  // activations quantized
                 trace_max(tr + 6);
             }
-            if (P.rb > P.ra && !stage_wait(S.mbar + 2, l & 1, A.err)) return;
+            const bool ok = P.rb <= P.ra || cta_stage_wait(S.mbar + MB_DOWN, l & 1, A.err);
             if (TRACE) {
                 trace_max(tr + 10);
                 cy.mark(10);  // down tile landed
@@ -1426,7 +1514,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
             float *pout = A.part + (size_t)P.kd * dim;
             const WDev wt{S.dq, S.dsc, S.dd + *S.doff, T_Q6_K, 0};
 #pragma unroll 1
-            for (int r = P.ra + warp * SC; r < P.rb; r += PS_WARPS * SC) {
+            for (int r = P.ra + warp * SC; ok && r < P.rb; r += PS_WARPS * SC) {
                 const int n = P.rb - r < SC ? P.rb - r : SC;
                 StackDownRows<NBD> st{wt, (uint64_t)(r - P.ra), n, XV{S.aq, S.ad, S.as}};
                 float y[SC];
@@ -1436,12 +1524,15 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                     if (s == lane && s < n) pout[r + s] = fmul(gk, y[s]);
             }
             __syncthreads();  // rbuf is free: stage the next layer's router rows
-            if (l + 1 < A.n_layers && threadIdx.x == 0) stage_router_rows(A, l + 1, S.rbuf, S.mbar);
+            if (l + 1 < A.n_layers && threadIdx.x == 0) stage_router_rows(A, l + 1, S.rbuf, S.mbar + MB_ROUTER);
         }
         if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 7 : nullptr, nullptr, TRACE ? &cy : nullptr, 11)) {
             STACK_SMEM;
-            if (l + 1 < A.n_layers && c < A.n_expert) mbar_wait(S.mbar, (l + 1) & 1, STAGE_POLLS);
-            return;
+            if (threadIdx.x == 0) {
+                if (l + 1 < A.n_layers && c < A.n_expert) mbar_wait(S.mbar + MB_ROUTER, (l + 1) & 1, STAGE_POLLS);
+                if (P.rb > P.ra) mbar_wait(S.mbar + MB_DOWN, l & 1, STAGE_POLLS);
+            }
+            { stack_exit(A); return; }
         }
     }
     {   // the last layer's output: x plus its combined experts, this CTA's slice of rows
@@ -1453,6 +1544,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
             A.out[r] = fadd(S.xs[r], acc);
         }
     }
+    stack_exit(A);
 #undef STACK_SMEM
 }
 
@@ -1472,7 +1564,7 @@ static size_t stack_smem(const StackArgs &S, int n_sm) {
     const int total = S.n_used * (S.ffn / gu_nr<8>());
     const int per_slot = n_sm / S.n_used;  // fewest CTAs serving one expert slot's down rows
     return StackSmem<8, gu_nr<8>(), 3>::bytes(S.n_expert, S.ffn, rpc, (total + n_sm - 1) / n_sm,
-                                              (S.dim + per_slot - 1) / per_slot);
+                                              (S.dim + per_slot - 1) / per_slot, S.n_layers);
 }
 
 static int sm_count() {
@@ -1486,7 +1578,9 @@ bool stack_supported(const StackArgs &S, int g_type, int dn_type) {
     if (S.dim % 256 || S.ffn % 256 || S.n_used > 64 || S.n_expert > 1024 || S.n_expert % 4) return false;
     if (!stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type), S.n_expert, false)) return false;
     if (S.dim / 256 != 8) return false;  // the shared-memory map is instantiated for dim 2048
-    if (S.n_used > 8 * PS_WARPS || S.ffn / 256 > PS_WARPS || sm_count() < S.n_used) return false;
+    const int nsm = sm_count(), total = S.n_used * (S.ffn / gu_nr<8>());
+    if (S.n_used > 64 || S.ffn / 256 > PS_WARPS || nsm < S.n_used || S.n_layers > STACK_MAX_LAYERS) return false;
+    (void)total;
     return stack_smem(S, sm_count()) <= 227 * 1024;
 }
 

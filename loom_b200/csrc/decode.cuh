@@ -84,10 +84,11 @@ struct StackArgs {
     const float *x_in;
     float *part;               // [n_used][dim] gate-weighted expert outputs of the current layer
     float *out;                // [dim] output of the last layer
-    float *logits;             // [LOGIT_REPLICAS][n_expert + 32]
-    float *act;                // [n_used][act_stride]
+    unsigned long long *logits; // [LOGIT_REPLICAS][n_expert + 32] tagged words (float bits | layer tag << 32)
+    unsigned long long *act;   // [n_used][act_stride] tagged words
     uint32_t *ids_out;         // optional [n_layers][n_used]
-    unsigned *bar;             // zeroed, 8-byte aligned: 64-bit grid-barrier arrival counter
+    unsigned *bar;             // zeroed 256 bytes: [0,8) grid-barrier arrivals (u64), [8,12) err, [16,20) launch
+                               // epoch, [24,28) exit count
     int *err;                  // device error word (2: a grid barrier gave up, 4: router staging timed out)
     int act_stride;
     unsigned long long *trace; // optional [n_layers][STACK_TRACE_SLOTS] %globaltimer ns (zeroed; max-reduced)

@@ -196,16 +196,13 @@ __device__ __forceinline__ uint32_t f32_order_key(float x) {
 // grid (read with ld.global.cg) or shared memory.
 constexpr int RW_MAX = 8;
 
-template <bool GLOBAL_CG, int RW = RW_MAX>
-__device__ __forceinline__ void route_warp_regs(const float *logits, const float *bias, int ne, int nk, int gating,
+// The route on logits already in registers: v[t] = logit of expert lane + 32t
+// (-inf past ne).
+template <int RW>
+__device__ __forceinline__ void route_warp_vals(float (&v)[RW], const float *bias, int ne, int nk, int gating,
                                                 int weights_norm, float weights_scale, float *scores, float *choice,
                                                 int *ids, float *gates, int *ids_out, float *gates_out, int lane) {
-    float v[RW], sc[RW];
-#pragma unroll
-    for (int t = 0; t < RW; t++) {
-        const int e = lane + 32 * t;
-        v[t] = e < ne ? (GLOBAL_CG ? __ldcg(logits + e) : logits[e]) : -INFINITY;
-    }
+    float sc[RW];
     if (gating == 2) {
 #pragma unroll
         for (int t = 0; t < RW; t++) sc[t] = fdiv(1.0f, fadd(1.0f, expf(-v[t])));
@@ -298,6 +295,20 @@ __device__ __forceinline__ void route_warp_regs(const float *logits, const float
     __syncwarp();
     route_finish(fin, ne, nk, gating, weights_norm, weights_scale, scores, choice, ids, gates, ids_out, gates_out,
                  lane);
+}
+
+template <bool GLOBAL_CG, int RW = RW_MAX>
+__device__ __forceinline__ void route_warp_regs(const float *logits, const float *bias, int ne, int nk, int gating,
+                                                int weights_norm, float weights_scale, float *scores, float *choice,
+                                                int *ids, float *gates, int *ids_out, float *gates_out, int lane) {
+    float v[RW];
+#pragma unroll
+    for (int t = 0; t < RW; t++) {
+        const int e = lane + 32 * t;
+        v[t] = e < ne ? (GLOBAL_CG ? __ldcg(logits + e) : logits[e]) : -INFINITY;
+    }
+    route_warp_vals<RW>(v, bias, ne, nk, gating, weights_norm, weights_scale, scores, choice, ids, gates, ids_out,
+                        gates_out, lane);
 }
 
 // moe.zig:106-158 route by the first ROUTE_THREADS threads of a CTA (the

@@ -1081,6 +1081,7 @@ extern "C" int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const fl
 namespace {
 struct StackRec {
     StackArgs args{};
+    size_t tagged_bytes = 0;  // logits + act, contiguous from args.logits
     int gty = 0, dty = 0;
     void *mem = nullptr;  // layers + buffers, one allocation
 };
@@ -1128,18 +1129,19 @@ extern "C" int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_laye
     A.act_stride = (int)align256(D0.ffn);
     if (!stack_supported(A, gty, dty)) return decline("layer shape not covered by the stack kernel");
     const size_t lay_b = align256(n_layers * sizeof(StackLayer)), part_b = align256(D0.n_used * D0.dim * 4);
-    const size_t lg_b = align256((D0.n_expert + 32) * 4 * LOGIT_REPLICAS), act_b = align256(D0.n_used * (size_t)A.act_stride * 4);
+    const size_t lg_b = align256((D0.n_expert + 32) * 8 * LOGIT_REPLICAS), act_b = align256(D0.n_used * (size_t)A.act_stride * 8);
     const size_t total = lay_b + part_b + lg_b + act_b + 256;
     CK(cudaMalloc(&S.mem, total));
     uint8_t *p = static_cast<uint8_t *>(S.mem);
     A.layers = reinterpret_cast<const StackLayer *>(p);
     A.part = reinterpret_cast<float *>(p + lay_b);
-    A.logits = reinterpret_cast<float *>(p + lay_b + part_b);
-    A.act = reinterpret_cast<float *>(p + lay_b + part_b + lg_b);
+    A.logits = reinterpret_cast<unsigned long long *>(p + lay_b + part_b);
+    A.act = reinterpret_cast<unsigned long long *>(p + lay_b + part_b + lg_b);
     A.bar = reinterpret_cast<unsigned *>(p + lay_b + part_b + lg_b + act_b);
     A.err = reinterpret_cast<int *>(A.bar + 2);
     CK(cudaMemcpy(p, host.data(), n_layers * sizeof(StackLayer), cudaMemcpyHostToDevice));
-    CK(cudaMemset(A.bar, 0, 256));
+    CK(cudaMemset(p + lay_b, 0, total - lay_b));  // tagged words, barrier words, epoch
+    S.tagged_bytes = lg_b + act_b;
     S.gty = gty;
     S.dty = dty;
     const uint64_t h = g_next_stack++;
@@ -1167,7 +1169,10 @@ extern "C" int loom_cuda_stack_error(uint64_t handle) {
     int v = 0;
     if (cudaStreamSynchronize(g_stream) != cudaSuccess) return -1;
     if (cudaMemcpy(&v, it->second.args.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
-    if (v && cudaMemset(it->second.args.bar, 0, 256) != cudaSuccess) return -1;  // re-arm the barrier words
+    if (v) {  // re-arm: barrier words, epoch, and every tagged word (so no stale tag can match)
+        if (cudaMemset(it->second.args.bar, 0, 256) != cudaSuccess) return -1;
+        if (cudaMemset(it->second.args.logits, 0, it->second.tagged_bytes) != cudaSuccess) return -1;
+    }
     return v;
 }
 
