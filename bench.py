@@ -330,7 +330,7 @@ def trace_stack(stack, step, stream, torch):
     out["worst_layer_total"] = round(float(np.max(np.diff(tr[:, 0]))) / 1e3, 2)
     out["layer_total"] = round(float(np.mean(np.diff(tr[:, 0]))) / 1e3, 2)
     sec = ["p1_load", "router_dot", "logits_wait", "route", "stage_issue", "gateup_tiles_wait", "gateup_compute",
-           "unused", "act_wait", "act_quant", "down_tiles_wait", "down_compute", "bar3_wait", "gateup_dots_w0", "act_store_w0", "spare"]
+           "unused", "act_wait", "act_quant", "down_tiles_wait", "down_compute", "unused2", "gateup_dots_w0", "act_store_w0", "spare"]
     cyc = tr[1:, 12:].reshape(-1, 16, 2)
     G = torch.cuda.get_device_properties(0).multi_processor_count
     out["cycles_max_mean"] = {n: [int(np.mean(cyc[:, i, 0])), int(np.mean(cyc[:, i, 1]) / G)] for i, n in enumerate(sec)}

@@ -1304,21 +1304,46 @@ __device__ __noinline__ void stack_drain(uint64_t *mbar, const StackSplit &P, in
     if (P.rb > P.ra) mbar_wait(mbar + MB_DOWN, l & 1, STAGE_POLLS);
 }
 
+__device__ __forceinline__ ulonglong2 ld_relaxed_v2u64(const unsigned long long *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+constexpr int STACK_MAX_USED = 8;
+
+// Wait (thread 0, bounded) until the parts counter of a layer has seen every
+// CTA's arrival; the CTA-wide barrier after it orders every thread's reads of
+// the parts after the acquire.
+__device__ __forceinline__ void wait_parts(const unsigned long long *cnt, unsigned long long target, int *err) {
+    if (threadIdx.x == 0) {
+        uint32_t it = 0;
+        for (; it < TAG_POLLS; it++)
+            if (ld_acquire_u64(cnt) >= target) break;
+        if (it == TAG_POLLS) atomicOr(err, 16);
+    }
+    __syncthreads();
+}
+
 // x of the next layer: x += sum over expert slots k (in order, from +0) of the
 // gate-weighted partial outputs part[k][r] (moe.zig combine order), each
 // thread on its own elements of the shared-memory x.
 __device__ __forceinline__ void combine_parts(const float *part, int nk, int dim, float *xs) {
 #pragma unroll 1
     for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) {
+        float4 p[STACK_MAX_USED];
+#pragma unroll
+        for (int k = 0; k < STACK_MAX_USED; k++)
+            if (k < nk) p[k] = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)k * dim) + i);
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 4
-        for (int k = 0; k < nk; k++) {
-            const float4 p = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)k * dim) + i);
-            acc.x = fadd(acc.x, p.x);
-            acc.y = fadd(acc.y, p.y);
-            acc.z = fadd(acc.z, p.z);
-            acc.w = fadd(acc.w, p.w);
-        }
+#pragma unroll
+        for (int k = 0; k < STACK_MAX_USED; k++)
+            if (k < nk) {
+                acc.x = fadd(acc.x, p[k].x);
+                acc.y = fadd(acc.y, p[k].y);
+                acc.z = fadd(acc.z, p[k].z);
+                acc.w = fadd(acc.w, p[k].w);
+            }
         float4 &x = reinterpret_cast<float4 *>(xs)[i];
         x.x = fadd(x.x, acc.x);
         x.y = fadd(x.y, acc.y);
@@ -1345,16 +1370,16 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
     const int lg_stride = A.n_expert + 32;  // one logit replica
     const StackSplit P(c, G, total, nk, dim);
 #define STACK_SMEM SM S(smraw, A.n_expert, ffn, rpc, ngmax, nrmax)
-    unsigned long long *ctr = reinterpret_cast<unsigned long long *>(A.bar);
-    unsigned long long target = 0;  // thread 0: this launch's barrier targets
     // tags of this launch: the epoch advances once per completed launch
-    const uint32_t tag0 = *reinterpret_cast<volatile unsigned *>(A.bar + 4) * 64u;
+    const uint32_t epoch = *reinterpret_cast<volatile unsigned *>(A.bar + 4);
+    const uint32_t tag0 = epoch * 64u;
+    // parts counters, one per layer parity: G arrivals per layer of that parity
+    unsigned long long *pcnt = reinterpret_cast<unsigned long long *>(A.bar + 8);
+    const unsigned long long n_par[2] = {(unsigned long long)(A.n_layers + 1) / 2, (unsigned long long)A.n_layers / 2};
+    auto parts_target = [&](int l) {
+        return (unsigned long long)G * ((unsigned long long)epoch * n_par[l & 1] + (unsigned long long)(l >> 1) + 1ull);
+    };
     if (threadIdx.x == 0) {
-        // Every earlier launch completed all n_layers barriers, so the
-        // counter stood at a multiple of that many rounds when this launch
-        // began; fewer than G arrivals of this launch can precede this read.
-        const unsigned long long per = (unsigned long long)A.n_layers * G, v = ld_acquire_u64(ctr);
-        target = v - v % per;
         STACK_SMEM;
         for (int i = 0; i < MB_COUNT; i++) mbar_init(S.mbar + i, 1);
         stage_router_rows(A, 0, S.rbuf, S.mbar + MB_ROUTER);
@@ -1378,7 +1403,8 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
                     reinterpret_cast<float4 *>(S.xs)[i] = __ldcg(reinterpret_cast<const float4 *>(A.x_in) + i);
             } else {
-                combine_parts(A.part, nk, dim, S.xs);
+                wait_parts(pcnt + ((l - 1) & 1), parts_target(l - 1), A.err);
+                combine_parts(A.part + (size_t)((l - 1) & 1) * nk * dim, nk, dim, S.xs);
             }
             __syncthreads();
             const bool ok = c >= A.n_expert || cta_stage_wait(S.mbar + MB_ROUTER, l & 1, A.err);
@@ -1397,6 +1423,10 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
 #pragma unroll 1
                 for (int b = warp - (PS_WARPS - nq); b < NBG; b += nq)
                     quant_block256_padded<false>(S.xs + b * 256, S.xq + b * XPAD_BLOCK, S.xqd + b, S.xqs + b * 16, lane);
+            }
+            if (nrw > 0) {  // rbuf is free once the dots are done: stage the next layer's router rows
+                __syncthreads();
+                if (l + 1 < A.n_layers && threadIdx.x == 0) stage_router_rows(A, l + 1, S.rbuf, S.mbar + MB_ROUTER);
             }
         }
         if (TRACE) {
@@ -1511,7 +1541,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 cy.mark(10);  // down tile landed
             }
             const float gk = S.sg[P.kd];
-            float *pout = A.part + (size_t)P.kd * dim;
+            float *pout = A.part + ((size_t)(l & 1) * nk + P.kd) * dim;
             const WDev wt{S.dq, S.dsc, S.dd + *S.doff, T_Q6_K, 0};
 #pragma unroll 1
             for (int r = P.ra + warp * SC; ok && r < P.rb; r += PS_WARPS * SC) {
@@ -1523,24 +1553,22 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 for (int s = 0; s < SC; s++)
                     if (s == lane && s < n) pout[r + s] = fmul(gk, y[s]);
             }
-            __syncthreads();  // rbuf is free: stage the next layer's router rows
-            if (l + 1 < A.n_layers && threadIdx.x == 0) stage_router_rows(A, l + 1, S.rbuf, S.mbar + MB_ROUTER);
-        }
-        if (!grid_barrier(ctr, target, A.err, TRACE ? tr + 7 : nullptr, nullptr, TRACE ? &cy : nullptr, 11)) {
-            STACK_SMEM;
-            if (threadIdx.x == 0) {
-                if (l + 1 < A.n_layers && c < A.n_expert) mbar_wait(S.mbar + MB_ROUTER, (l + 1) & 1, STAGE_POLLS);
-                if (P.rb > P.ra) mbar_wait(S.mbar + MB_DOWN, l & 1, STAGE_POLLS);
+            __syncthreads();  // every row of this CTA stored: arrive on the layer's parts counter
+            if (threadIdx.x == 0) red_release_add_u64(pcnt + (l & 1), 1ull);
+            if (TRACE) {
+                trace_max(tr + 7);
+                cy.mark(11);  // down rows done
             }
-            { stack_exit(A); return; }
         }
     }
     {   // the last layer's output: x plus its combined experts, this CTA's slice of rows
         STACK_SMEM;
-        const int r0 = c * dim / G, r1 = (c + 1) * dim / G;
+        const int r0 = c * dim / G, r1 = (c + 1) * dim / G, L = A.n_layers;
+        const float *pl = A.part + (size_t)((L - 1) & 1) * nk * dim;
+        wait_parts(pcnt + ((L - 1) & 1), parts_target(L - 1), A.err);
         for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
             float acc = 0.0f;
-            for (int k = 0; k < nk; k++) acc = fadd(acc, __ldcg(A.part + (size_t)k * dim + r));
+            for (int k = 0; k < nk; k++) acc = fadd(acc, __ldcg(pl + (size_t)k * dim + r));
             A.out[r] = fadd(S.xs[r], acc);
         }
     }
@@ -1579,7 +1607,7 @@ bool stack_supported(const StackArgs &S, int g_type, int dn_type) {
     if (!stack_fn(g_type, S.dim / 256, dn_type, S.ffn / block_elems(dn_type), S.n_expert, false)) return false;
     if (S.dim / 256 != 8) return false;  // the shared-memory map is instantiated for dim 2048
     const int nsm = sm_count(), total = S.n_used * (S.ffn / gu_nr<8>());
-    if (S.n_used > 64 || S.ffn / 256 > PS_WARPS || nsm < S.n_used || S.n_layers > STACK_MAX_LAYERS) return false;
+    if (S.n_used > STACK_MAX_USED || S.ffn > 2 * PS_WARPS * 32 || S.ffn / 256 > PS_WARPS || nsm < S.n_used || S.n_layers > STACK_MAX_LAYERS) return false;
     (void)total;
     return stack_smem(S, sm_count()) <= 227 * 1024;
 }

@@ -82,13 +82,13 @@ struct StackArgs {
     int gating, weights_norm;
     float weights_scale;
     const float *x_in;
-    float *part;               // [n_used][dim] gate-weighted expert outputs of the current layer
+    float *part;               // [2][n_used][dim] gate-weighted expert outputs (by layer parity)
     float *out;                // [dim] output of the last layer
     unsigned long long *logits; // [LOGIT_REPLICAS][n_expert + 32] tagged words (float bits | layer tag << 32)
     unsigned long long *act;   // [n_used][act_stride] tagged words
     uint32_t *ids_out;         // optional [n_layers][n_used]
-    unsigned *bar;             // zeroed 256 bytes: [0,8) grid-barrier arrivals (u64), [8,12) err, [16,20) launch
-                               // epoch, [24,28) exit count
+    unsigned *bar;             // zeroed 256 bytes: [8,12) err, [16,20) launch epoch, [24,28) exit count,
+                               // [32,48) parts arrival counters (u64) by layer parity
     int *err;                  // device error word (2: a grid barrier gave up, 4: router staging timed out)
     int act_stride;
     unsigned long long *trace; // optional [n_layers][STACK_TRACE_SLOTS] %globaltimer ns (zeroed; max-reduced)

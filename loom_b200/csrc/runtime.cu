@@ -1082,6 +1082,7 @@ namespace {
 struct StackRec {
     StackArgs args{};
     size_t tagged_bytes = 0;  // logits + act, contiguous from args.logits
+    size_t part_bytes = 0;    // tagged partial outputs at args.part
     int gty = 0, dty = 0;
     void *mem = nullptr;  // layers + buffers, one allocation
 };
@@ -1128,7 +1129,7 @@ extern "C" int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_laye
     A.weights_scale = D0.weights_scale;
     A.act_stride = (int)align256(D0.ffn);
     if (!stack_supported(A, gty, dty)) return decline("layer shape not covered by the stack kernel");
-    const size_t lay_b = align256(n_layers * sizeof(StackLayer)), part_b = align256(D0.n_used * D0.dim * 4);
+    const size_t lay_b = align256(n_layers * sizeof(StackLayer)), part_b = align256(2 * D0.n_used * D0.dim * 4);
     const size_t lg_b = align256((D0.n_expert + 32) * 8 * LOGIT_REPLICAS), act_b = align256(D0.n_used * (size_t)A.act_stride * 8);
     const size_t total = lay_b + part_b + lg_b + act_b + 256;
     CK(cudaMalloc(&S.mem, total));
@@ -1142,6 +1143,7 @@ extern "C" int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_laye
     CK(cudaMemcpy(p, host.data(), n_layers * sizeof(StackLayer), cudaMemcpyHostToDevice));
     CK(cudaMemset(p + lay_b, 0, total - lay_b));  // tagged words, barrier words, epoch
     S.tagged_bytes = lg_b + act_b;
+    S.part_bytes = part_b;
     S.gty = gty;
     S.dty = dty;
     const uint64_t h = g_next_stack++;
@@ -1172,6 +1174,7 @@ extern "C" int loom_cuda_stack_error(uint64_t handle) {
     if (v) {  // re-arm: barrier words, epoch, and every tagged word (so no stale tag can match)
         if (cudaMemset(it->second.args.bar, 0, 256) != cudaSuccess) return -1;
         if (cudaMemset(it->second.args.logits, 0, it->second.tagged_bytes) != cudaSuccess) return -1;
+        if (cudaMemset(it->second.args.part, 0, it->second.part_bytes) != cudaSuccess) return -1;
     }
     return v;
 }
