@@ -324,7 +324,7 @@ def trace_stack(stack, step, stream, torch):
     tr = stack.trace_read().astype(np.float64)
     rel = tr[1:] - tr[1:, :1]
     names = ["start", "router_rows_done", "unused", "route_done", "gateup_done",
-             "unused", "act_quantized", "down_done", "unused", "gateup_tiles_landed",
+             "unused", "act_quantized", "down_done", "gateup_half2_landed", "gateup_tiles_landed",
              "down_tiles_landed"]
     out = {n: round(float(np.mean(rel[:, i])) / 1e3, 2) for i, n in enumerate(names) if i and n != "unused"}
     out["worst_layer_total"] = round(float(np.max(np.diff(tr[:, 0]))) / 1e3, 2)

@@ -1113,7 +1113,7 @@ struct StackSplit {
 // Shared-memory map of the stack kernel (recomputed per phase so that no
 // pointer stays live in registers across phases). Sizes depend on the grid:
 // ngmax gate/up groups and nrmax down rows per CTA.
-constexpr int MB_ROUTER = 0, MB_DOWN = 1, MB_GATEUP = 2, MB_COUNT = 4;
+constexpr int MB_ROUTER = 0, MB_DOWN = 1, MB_GATEUP = 2, MB_COUNT = 4;  // MB_GATEUP, MB_GATEUP + 1: the halves
 constexpr int STACK_MAX_LAYERS = 64;
 
 template <int NBG, int NR, int NBD> struct StackSmem {
@@ -1207,8 +1207,13 @@ __device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const Sta
     const uint64_t b0 = ((uint64_t)sid[P.kd] * dim + P.ra) * NBD, nb = (uint64_t)nr * NBD;
     const uintptr_t d0 = reinterpret_cast<uintptr_t>(Ly.dn.d + b0);
     const uintptr_t da = d0 & ~uintptr_t(15), de = (d0 + nb * 2 + 15) & ~uintptr_t(15);
+    // gate/up in two halves (groups [g0, gm) and [gm, g1)), each on its own
+    // barrier, the first half requested first: its warps start while the
+    // second half is still streaming in
+    const int gm = P.g0 + (ng + 1) / 2;
     if (lane == 0) {
-        if (ng) mbar_expect_tx(mb_gu, (uint32_t)(2 * ng * SM::GU_HALF));
+        if (ng) mbar_expect_tx(mb_gu, (uint32_t)(2 * (gm - P.g0) * SM::GU_HALF));
+        if (gm < P.g1) mbar_expect_tx(mb_gu + 1, (uint32_t)(2 * (P.g1 - gm) * SM::GU_HALF));
         if (nr) {
             *doff = (int)((d0 - da) / 2);
             mbar_expect_tx(mb_dn, (uint32_t)(nb * (192 + 16) + (de - da)));
@@ -1216,18 +1221,21 @@ __device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const Sta
     }
     __syncwarp();
     fence_proxy_async_smem();
-    // gate/up: the CTA's groups form a few runs inside one expert each,
-    // contiguous in global memory and in the tile: lane 2i copies run i's gate
-    // rows, lane 2i+1 its up rows, all on one barrier
-    if (ng) {
-        const int ka = P.g0 / per_e, kb = (P.g1 - 1) / per_e;
+    // each half: a run of groups inside one expert is contiguous in global
+    // memory and in the tile; lane q of the half copies (run q/2, gate or up)
+#pragma unroll 1
+    for (int h = 0; h < 2; h++) {
+        const int ha = h ? gm : P.g0, hz = h ? P.g1 : gm;
+        if (ha >= hz) continue;
+        const int ka = ha / per_e, kb = (hz - 1) / per_e;
         for (int q = lane; q < 2 * (kb - ka + 1); q += 32) {
             const int k = ka + q / 2, up = q & 1;
-            const int ga = max(P.g0, k * per_e), gz = min(P.g1, (k + 1) * per_e);
+            const int ga = max(ha, k * per_e), gz = min(hz, (k + 1) * per_e);
             const uint64_t blk = ((uint64_t)sid[k] * ffn + (uint64_t)(ga - k * per_e) * NR) * NBG;
             bulk_g2s(gub + (size_t)(up ? ngmax : 0) * SM::GU_HALF + (size_t)(ga - P.g0) * SM::GU_HALF,
-                     (up ? Ly.u : Ly.g).q + blk * 144, (uint32_t)(gz - ga) * SM::GU_HALF, mb_gu);
+                     (up ? Ly.u : Ly.g).q + blk * 144, (uint32_t)(gz - ga) * SM::GU_HALF, mb_gu + h);
         }
+        __syncwarp();
     }
     if (nr) {
         if (lane == 29) bulk_g2s(dq, Ly.dn.q + b0 * 192, (uint32_t)(nb * 192), mb_dn);
@@ -1301,6 +1309,7 @@ __device__ __noinline__ void stack_exit(const StackArgs &A) {
 __device__ __noinline__ void stack_drain(uint64_t *mbar, const StackSplit &P, int l) {
     if (threadIdx.x != 0) return;
     if (P.g1 > P.g0) mbar_wait(mbar + MB_GATEUP, l & 1, STAGE_POLLS);
+    if (P.g1 - P.g0 > 1) mbar_wait(mbar + MB_GATEUP + 1, l & 1, STAGE_POLLS);
     if (P.rb > P.ra) mbar_wait(mbar + MB_DOWN, l & 1, STAGE_POLLS);
 }
 
@@ -1469,14 +1478,27 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                                                  S.mbar + MB_GATEUP, S.mbar + MB_DOWN, P, ngmax);
             if (TRACE) cy.mark(4);  // tiles requested
             if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = S.sid[threadIdx.x];
-            const bool ok = P.g1 <= P.g0 || cta_stage_wait(S.mbar + MB_GATEUP, l & 1, A.err);
-            if (TRACE) {
-                trace_max(tr + 9);
-                cy.mark(5);  // gate/up tiles landed
-            }
             const WDev wt{S.gub, nullptr, nullptr, T_Q4_K, 0};
+            const int ng = P.g1 - P.g0, nga = (ng + 1) / 2;  // groups, and groups in the first half
+            __shared__ int s_half_ok[2];
 #pragma unroll 1
-            for (int g = warp; ok && g < P.g1 - P.g0; g += PS_WARPS) {
+            for (int g = warp; g < ng; g += PS_WARPS) {
+                {   // this group's half of the tiles: ONE thread per half waits on its
+                    // barrier (bounded), the half's other warps park on a named barrier
+                    const int h = g >= nga, first = h ? nga : 0, nw = h ? ng - nga : nga;
+                    if (lane == 0 && g == first) {
+                        const int ok = mbar_wait(S.mbar + MB_GATEUP + h, l & 1, STAGE_POLLS);
+                        if (!ok) atomicOr(A.err, 4);
+                        s_half_ok[h] = ok;
+                    }
+                    asm volatile("bar.sync %0, %1;" ::"r"(2 + h), "r"(nw * 32) : "memory");
+                    if (!s_half_ok[h]) break;
+                }
+                if (TRACE && g == 0) {
+                    trace_max(tr + 9);
+                    cy.mark(5);  // warp 0's gate/up tiles landed
+                }
+                if (TRACE && g == nga && lane == 0) atomicMax(tr + 8, gtimer());  // second half landed
                 const int grp = P.g0 + g, k = grp / per_e, rl = (grp % per_e) * NR;
                 GateUpStreams<NR> st{wt, wt, (uint64_t)g * NR * NBG, (uint64_t)(ngmax + g) * NR * NBG, NBG,
                                      XV{S.xq, S.xqd, S.xqs}};

@@ -40,4 +40,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     return false;
 }
 
+// Wait for phase `parity` with non-blocking tests (mbarrier.test_wait) and a
+// short sleep between them: for barriers several warps wait on at once, where
+// a suspended try_wait may not be woken promptly. Gives up after `max_polls`.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, uint32_t max_polls) {
+    for (uint32_t i = 0; i < max_polls; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        __nanosleep(20);
+    }
+    return false;
+}
+
 }  // namespace loom
