@@ -10,12 +10,17 @@ path and not timed. Weights come from the seeded generator (synthetic: no
 checkpoint or dataset is available offline); 48 distinct layers touch
 ~1.2 GB per token, far more than the 126 MB L2, so no flush is needed.
 
-  value      tok/s of the device-resident path (CUDA graph of 48 layers,
-             inputs already in HBM), max over ranks
+  value      tok/s of the device-resident path, inputs already in HBM, max
+             over ranks. T=1 unsharded (the default): the persistent stack
+             kernel, one launch per token for all 48 layers
+             (loom_cuda_stack_forward); otherwise the per-layer kernels
+             (loom_cuda_moe_forward) replayed from a CUDA graph
   e2e        the same token through the reference-facing seam calls with
              HOST buffers (loom_cuda_matvec for the router +
              loom_cuda_moe_ffn_routed per layer, as deepseek.zig:1334-1380
              drives its backend)
+  e2e_device the device-resident path with the token copied in from pinned
+             host memory and the output read back every step
   roofline   HBM bytes the layer must move (router + the distinct selected
              experts' planes + activations) / measured layer time
   cpu_baseline  the CPU restatement of the reference kernels (oracle/) on
@@ -216,7 +221,10 @@ def run_gpu(args):
     ids = torch.zeros((LAYERS, T, NK), dtype=torch.int32, device="cuda")
 
     stack = None
-    if args.engine == "stack":
+    engine = args.engine
+    if engine == "auto":
+        engine = "stack" if T == 1 and not ep else "layers"
+    if engine == "stack":
         if T != 1 or ep:
             raise SystemExit("--engine stack runs the T=1 decode of unsharded layers")
         stack = D.Stack(layers)
@@ -270,15 +278,22 @@ def run_gpu(args):
     else:
         bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1)) for l in range(LAYERS))
     achieved = bytes_step / (ms * 1e-3) / 1e9
+    # DRAM bytes (read + write) per layer of k_stack from one ncu capture of a
+    # 4-layer launch (dram__bytes_read.sum 102,891,776 + dram__bytes_write.sum
+    # 9,694,464), scaled by layers: traffic grows in proportion to the layers
+    traffic = (102891776 + 9694464) * LAYERS // 4 if stack is not None else None
     peak, peak_kind = peaks()
     value = (T if ep else world * T) / (ms * 1e-3)
 
     # e2e through the seam with host buffers
     e2e = None
+    e2e_device = None
     if args.e2e_layers > 0 and not ep:
         e2e = run_e2e(args, B)
-    elif ep:
-        e2e = run_e2e_device(args, g, stream, x0, bufs[(LAYERS - 1) % 2], torch, dist, world)
+    if ep or stack is not None:
+        e2e_device = run_e2e_device(args, g, stream, x0, bufs[(LAYERS - 1) % 2], torch, dist, world)
+        if ep:
+            e2e = e2e_device
 
     if rank != 0:
         return
@@ -297,11 +312,13 @@ def run_gpu(args):
                    "layers": LAYERS, "n_expert": NE, "n_used": NK, "dim": DIM, "ffn": FFN,
                    "parallelism": (f"ep{world} (experts sharded, NCCL all-reduce combine)" if ep else
                                    f"replicas x{world}" if world > 1 else "1 gpu"),
-                   "engine": args.engine,
+                   "engine": engine,
                    "l2": "inputs > L2 (48 distinct layers, ~1.2 GB touched per token)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
-                     "kernel": "moe layer (router gemv + route + gate/up + down/combine)",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": ("k_stack: every layer's router GEMV, route, gate/up, down and combine in one "
+                                "persistent launch" if stack is not None else
+                                "moe layer (router gemv + route + gate/up + down/combine)"),
                      "peak_kind": peak_kind, "bytes_per_step": bytes_step},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": ck.summary(),
@@ -310,6 +327,8 @@ def run_gpu(args):
         line["phase_us"] = phases
     if e2e:
         line["e2e"] = e2e
+    if e2e_device and e2e_device is not e2e:
+        line["e2e_device"] = e2e_device
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -460,8 +479,9 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--engine", default="layers", choices=["layers", "stack"],
-                    help="layers: per-layer kernels in a CUDA graph; stack: one persistent kernel for all layers (T=1)")
+    ap.add_argument("--engine", default="auto", choices=["auto", "layers", "stack"],
+                    help="layers: per-layer kernels in a CUDA graph; stack: one persistent kernel for all layers "
+                         "(T=1); auto: stack for unsharded T=1, else layers")
     ap.add_argument("--trace", action="store_true", help="add per-kernel phase times (one extra traced replay)")
     ap.add_argument("--ep", action="store_true",
                     help="with torchrun: shard each layer's experts over the ranks (expert parallel) instead of "
