@@ -348,7 +348,7 @@ def trace_stack(stack, step, stream, torch):
     out = {n: round(float(np.mean(rel[:, i])) / 1e3, 2) for i, n in enumerate(names) if i and n != "unused"}
     out["worst_layer_total"] = round(float(np.max(np.diff(tr[:, 0]))) / 1e3, 2)
     out["layer_total"] = round(float(np.mean(np.diff(tr[:, 0]))) / 1e3, 2)
-    sec = ["p1_load", "router_dot", "logits_wait", "route", "stage_issue", "gateup_tiles_wait", "gateup_compute",
+    sec = ["p1_load", "router_dot", "logits_wait", "route", "stage_issue_w0", "gateup_tiles_wait", "gateup_compute",
            "unused", "act_wait", "act_quant", "down_tiles_wait", "down_compute", "unused2", "gateup_dots_w0", "act_store_w0", "spare"]
     cyc = tr[1:, 12:].reshape(-1, 16, 2)
     G = torch.cuda.get_device_properties(0).multi_processor_count

@@ -1191,42 +1191,31 @@ __device__ __noinline__ void stage_router_rows(const StackArgs &A, int l, float 
         bulk_g2s(rbuf + (size_t)j * dim, A.layers[l].router + (size_t)row * dim, (uint32_t)(dim * 4), mbar);
 }
 
-// Warp 0: stage this CTA's gate/up tiles (groups g0..g1: NR rows of gate and
-// of up each, contiguous within one expert, so one copy per expert and
-// matrix) and its down tile (rows ra..rb of expert slot kd: quants, scales,
-// and the f16 scales through a 16-byte-aligned window whose offset goes to
-// *doff).
+// Stage this CTA's tiles with bulk copies, three warps issuing in parallel
+// (a bulk copy takes a few hundred cycles to issue):
+//   warp 0  gate/up tiles of the first half of its groups  -> mb_gu
+//   warp 1  gate/up tiles of the second half               -> mb_gu + 1
+//   last warp  the down tile, once the gate/up tiles have landed: rows
+//           ra..rb of expert slot kd (quants, scales, and the f16 scales
+//           through a 16-byte-aligned window whose offset goes to *doff)
+//                                                          -> mb_dn
+// Within a half, a run of groups inside one expert is contiguous in global
+// memory and in the tile: lane q copies (run q/2, gate or up).
 template <int NBG, int NR, int NBD>
 __device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const StackLayer &Ly, const int *sid, int *doff,
                                                    uint8_t *gub, uint8_t *dq, uint8_t *dsc, uint16_t *dd,
-                                                   uint64_t *mb_gu, uint64_t *mb_dn, const StackSplit &P, int ngmax) {
+                                                   uint64_t *mb_gu, uint64_t *mb_dn, const StackSplit &P, int ngmax,
+                                                   uint32_t parity) {
     using SM = StackSmem<NBG, NR, NBD>;
     constexpr int dim = NBG * 256;
-    const int lane = threadIdx.x & 31, ffn = A.ffn, per_e = ffn / NR;
-    const int ng = P.g1 - P.g0, nr = P.rb - P.ra;
-    const uint64_t b0 = ((uint64_t)sid[P.kd] * dim + P.ra) * NBD, nb = (uint64_t)nr * NBD;
-    const uintptr_t d0 = reinterpret_cast<uintptr_t>(Ly.dn.d + b0);
-    const uintptr_t da = d0 & ~uintptr_t(15), de = (d0 + nb * 2 + 15) & ~uintptr_t(15);
-    // gate/up in two halves (groups [g0, gm) and [gm, g1)), each on its own
-    // barrier, the first half requested first: its warps start while the
-    // second half is still streaming in
-    const int gm = P.g0 + (ng + 1) / 2;
-    if (lane == 0) {
-        if (ng) mbar_expect_tx(mb_gu, (uint32_t)(2 * (gm - P.g0) * SM::GU_HALF));
-        if (gm < P.g1) mbar_expect_tx(mb_gu + 1, (uint32_t)(2 * (P.g1 - gm) * SM::GU_HALF));
-        if (nr) {
-            *doff = (int)((d0 - da) / 2);
-            mbar_expect_tx(mb_dn, (uint32_t)(nb * (192 + 16) + (de - da)));
-        }
-    }
-    __syncwarp();
-    fence_proxy_async_smem();
-    // each half: a run of groups inside one expert is contiguous in global
-    // memory and in the tile; lane q of the half copies (run q/2, gate or up)
-#pragma unroll 1
-    for (int h = 0; h < 2; h++) {
-        const int ha = h ? gm : P.g0, hz = h ? P.g1 : gm;
-        if (ha >= hz) continue;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, ffn = A.ffn, per_e = ffn / NR;
+    const int ng = P.g1 - P.g0, nr = P.rb - P.ra, gm = P.g0 + (ng + 1) / 2;
+    if (warp < 2) {
+        const int h = warp, ha = h ? gm : P.g0, hz = h ? P.g1 : gm;
+        if (ha >= hz) return;
+        if (lane == 0) mbar_expect_tx(mb_gu + h, (uint32_t)(2 * (hz - ha) * SM::GU_HALF));
+        __syncwarp();
+        fence_proxy_async_smem();
         const int ka = ha / per_e, kb = (hz - 1) / per_e;
         for (int q = lane; q < 2 * (kb - ka + 1); q += 32) {
             const int k = ka + q / 2, up = q & 1;
@@ -1235,12 +1224,25 @@ __device__ __forceinline__ void stage_expert_tiles(const StackArgs &A, const Sta
             bulk_g2s(gub + (size_t)(up ? ngmax : 0) * SM::GU_HALF + (size_t)(ga - P.g0) * SM::GU_HALF,
                      (up ? Ly.u : Ly.g).q + blk * 144, (uint32_t)(gz - ga) * SM::GU_HALF, mb_gu + h);
         }
+    } else if (warp == PS_WARPS - 1 && nr) {
+        // the down tile is needed only after the gate/up phase: request it once
+        // the first gate/up tiles have landed, so the two do not share DRAM
+        // bandwidth
+        // the first half's leader (warp 0) arrives on named barrier 4 once its
+        // tiles have landed; this warp waits there in hardware (no mbarrier poll)
+        if (ng > 0 && ng < PS_WARPS) asm volatile("bar.sync 4, 64;" ::: "memory");
+        const uint64_t b0 = ((uint64_t)sid[P.kd] * dim + P.ra) * NBD, nb = (uint64_t)nr * NBD;
+        const uintptr_t d0 = reinterpret_cast<uintptr_t>(Ly.dn.d + b0);
+        const uintptr_t da = d0 & ~uintptr_t(15), de = (d0 + nb * 2 + 15) & ~uintptr_t(15);
+        if (lane == 0) {
+            *doff = (int)((d0 - da) / 2);
+            mbar_expect_tx(mb_dn, (uint32_t)(nb * (192 + 16) + (de - da)));
+        }
         __syncwarp();
-    }
-    if (nr) {
-        if (lane == 29) bulk_g2s(dq, Ly.dn.q + b0 * 192, (uint32_t)(nb * 192), mb_dn);
-        if (lane == 30) bulk_g2s(dsc, Ly.dn.sc + b0 * 16, (uint32_t)(nb * 16), mb_dn);
-        if (lane == 31) bulk_g2s(dd, reinterpret_cast<const void *>(da), (uint32_t)(de - da), mb_dn);
+        fence_proxy_async_smem();
+        if (lane == 0) bulk_g2s(dq, Ly.dn.q + b0 * 192, (uint32_t)(nb * 192), mb_dn);
+        if (lane == 1) bulk_g2s(dsc, Ly.dn.sc + b0 * 16, (uint32_t)(nb * 16), mb_dn);
+        if (lane == 2) bulk_g2s(dd, reinterpret_cast<const void *>(da), (uint32_t)(de - da), mb_dn);
     }
 }
 
@@ -1473,9 +1475,9 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
             if (TRACE) cy.mark(3);  // route (thread 0's warp)
             __syncthreads();
             if (TRACE) trace_max(tr + 3);
-            if (warp == 0)
+            if (warp < 2 || warp == PS_WARPS - 1)
                 stage_expert_tiles<NBG, NR, NBD>(A, S.lys[l], S.sid, S.doff, S.gub, S.dq, S.dsc, S.dd,
-                                                 S.mbar + MB_GATEUP, S.mbar + MB_DOWN, P, ngmax);
+                                                 S.mbar + MB_GATEUP, S.mbar + MB_DOWN, P, ngmax, l & 1);
             if (TRACE) cy.mark(4);  // tiles requested
             if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = S.sid[threadIdx.x];
             const WDev wt{S.gub, nullptr, nullptr, T_Q4_K, 0};
@@ -1491,6 +1493,8 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                         if (!ok) atomicOr(A.err, 4);
                         s_half_ok[h] = ok;
                     }
+                    if (g == 0 && ng < PS_WARPS && P.rb > P.ra)  // release the down-tile warp
+                        asm volatile("bar.arrive 4, 64;" ::: "memory");
                     asm volatile("bar.sync %0, %1;" ::"r"(2 + h), "r"(nw * 32) : "memory");
                     if (!s_half_ok[h]) break;
                 }
