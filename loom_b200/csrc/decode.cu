@@ -1067,6 +1067,11 @@ constexpr uint32_t TAG_POLLS = 1u << 20;  // bounded poll on tagged data (~1 s)
 __device__ __forceinline__ unsigned long long tagged(float v, uint32_t tag) {
     return ((unsigned long long)tag << 32) | __float_as_uint(v);
 }
+__device__ __forceinline__ ulonglong2 ld_relaxed_v2u64(const unsigned long long *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
     unsigned long long v;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -1140,6 +1145,7 @@ template <int NBG, int NR, int NBD> struct StackSmem {
     float *ad;        // [ffn/256]
     int32_t *as;      // [ffn/16]
     StackLayer *lys;  // [n_layers] the layer descriptors
+    float *tt;        // [PS_WARPS][2*NR*NBG] per-warp transpose of the gate/up block terms
     static __host__ __device__ size_t dslot(int nrmax) { return ((size_t)nrmax * NBD * 2 + 15) / 16 * 16 + 16; }
     __device__ __forceinline__ StackSmem(uint8_t *base, int ne, int ffn, int rpc, int ngmax, int nrmax) {
         xs = reinterpret_cast<float *>(base);
@@ -1163,10 +1169,11 @@ template <int NBG, int NR, int NBD> struct StackSmem {
         ad = reinterpret_cast<float *>(aq + (size_t)(ffn / 256) * XPAD_BLOCK);
         as = reinterpret_cast<int32_t *>(ad + ffn / 256);
         lys = reinterpret_cast<StackLayer *>(base + ((reinterpret_cast<uintptr_t>(as + ffn / 16) - reinterpret_cast<uintptr_t>(base) + 15) & ~uintptr_t(15)));
+        tt = reinterpret_cast<float *>(lys + STACK_MAX_LAYERS);
     }
     static size_t bytes(int ne, int ffn, int rpc, int ngmax, int nrmax, int n_layers) {
         return (size_t)dim * 4 + NBG * XPAD_BLOCK + NBG * 4 + NBG * 64 + (size_t)2 * ne * 4 + 64 * 8 + 32 + 32 + 8 * MB_COUNT +
-               16 + (size_t)n_layers * sizeof(StackLayer) +
+               16 + (size_t)STACK_MAX_LAYERS * sizeof(StackLayer) + (size_t)PS_WARPS * 2 * NR * NBG * 4 +
                (size_t)rpc * dim * 4 + (size_t)2 * ngmax * GU_HALF + (size_t)nrmax * NBD * (192 + 16) + dslot(nrmax) +
                (size_t)ffn * 4 + (size_t)(ffn / 256) * XPAD_BLOCK + (size_t)(ffn / 256) * 4 + (size_t)(ffn / 16) * 4;
     }
@@ -1315,11 +1322,6 @@ __device__ __noinline__ void stack_drain(uint64_t *mbar, const StackSplit &P, in
     if (P.rb > P.ra) mbar_wait(mbar + MB_DOWN, l & 1, STAGE_POLLS);
 }
 
-__device__ __forceinline__ ulonglong2 ld_relaxed_v2u64(const unsigned long long *p) {
-    ulonglong2 v;
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
-    return v;
-}
 
 constexpr int STACK_MAX_USED = 8;
 
@@ -1367,8 +1369,6 @@ template <int TYG, int NBG, int TYD, int SC, int NBD, int RW, bool TRACE>
 __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
     constexpr int NR = gu_nr<NBG>();
     static_assert(TYG == T_Q4_KW && TYD == T_Q6_K, "staged tiles are laid out for Q4_K gate/up and Q6_K down");
-    using EG = CEng<T_Q4_KW_S, 2 * NR, NBG>;
-    using ED = CEng<T_Q6_K_S, SC, NBD>;
     using SM = StackSmem<NBG, NR, NBD>;
     constexpr int dim = NBG * 256;
     extern __shared__ __align__(16) uint8_t smraw[];
@@ -1480,7 +1480,6 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                                                  S.mbar + MB_GATEUP, S.mbar + MB_DOWN, P, ngmax, l & 1);
             if (TRACE) cy.mark(4);  // tiles requested
             if (c == 0 && A.ids_out && threadIdx.x < nk) A.ids_out[(size_t)l * nk + threadIdx.x] = S.sid[threadIdx.x];
-            const WDev wt{S.gub, nullptr, nullptr, T_Q4_K, 0};
             const int ng = P.g1 - P.g0, nga = (ng + 1) / 2;  // groups, and groups in the first half
             __shared__ int s_half_ok[2];
 #pragma unroll 1
@@ -1504,18 +1503,14 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 }
                 if (TRACE && g == nga && lane == 0) atomicMax(tr + 8, gtimer());  // second half landed
                 const int grp = P.g0 + g, k = grp / per_e, rl = (grp % per_e) * NR;
-                GateUpStreams<NR> st{wt, wt, (uint64_t)g * NR * NBG, (uint64_t)(ngmax + g) * NR * NBG, NBG,
-                                     XV{S.xq, S.xqd, S.xqs}};
-                float acc[2 * NR];
-                EG::run(st, acc, lane);
+                const float dotv = q4k_group_dot_smem<NR, NBG>(S.gub + (size_t)g * SM::GU_HALF,
+                                                              S.gub + (size_t)(ngmax + g) * SM::GU_HALF, S.xq, S.xqd,
+                                                              S.xqs, S.tt + warp * 2 * NR * NBG, lane);
                 if (TRACE && g == 0) cy.mark(13);  // warp 0's gate/up dots
-                if (lane < NR) {  // lane i: silu(gate row i) * up row i
-                    float a = acc[0], u = acc[NR];
-#pragma unroll
-                    for (int i = 1; i < NR; i++)
-                        if (lane == i) a = acc[i], u = acc[NR + i];
-                    A.act[(size_t)k * A.act_stride + rl + lane] = tagged(fmul(fdiv(a, fadd(1.0f, expf(-a))), u), tag);
-                }
+                const float u = __shfl_down_sync(0xffffffffu, dotv, NR);  // lane i < NR: up row i
+                if (lane < NR)  // lane i: silu(gate row i) * up row i
+                    A.act[(size_t)k * A.act_stride + rl + lane] =
+                        tagged(fmul(fdiv(dotv, fadd(1.0f, expf(-dotv))), u), tag);
                 if (TRACE && g == 0) cy.mark(14);  // warp 0's activations stored
             }
         }
@@ -1527,7 +1522,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
         {   // ---- P3: this CTA's expert: its activations quantized, rows ra..rb of its down matrix
             STACK_SMEM;
             const int nbf = ffn / 256;
-            {   // this expert's activations as they arrive (tagged words)
+            {   // this expert's activations as they arrive (tagged words), every thread polling its share
                 const unsigned long long *src = A.act + (size_t)P.kd * A.act_stride;
                 constexpr int PER = 2;  // entries per thread polled together (ffn <= PER * blockDim.x)
                 unsigned long long w[PER];
@@ -1572,12 +1567,8 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
 #pragma unroll 1
             for (int r = P.ra + warp * SC; ok && r < P.rb; r += PS_WARPS * SC) {
                 const int n = P.rb - r < SC ? P.rb - r : SC;
-                StackDownRows<NBD> st{wt, (uint64_t)(r - P.ra), n, XV{S.aq, S.ad, S.as}};
-                float y[SC];
-                ED::run(st, y, lane);
-#pragma unroll
-                for (int s = 0; s < SC; s++)
-                    if (s == lane && s < n) pout[r + s] = fmul(gk, y[s]);
+                const float yv = q6k_rows_dot_smem<SC, NBD>(wt, r - P.ra, n, S.aq, S.ad, S.as, lane);
+                if ((lane & 3) == 0 && (lane >> 2) < n) pout[r + (lane >> 2)] = fmul(gk, yv);
             }
             __syncthreads();  // every row of this CTA stored: arrive on the layer's parts counter
             if (threadIdx.x == 0) red_release_add_u64(pcnt + (l & 1), 1ull);

@@ -228,6 +228,132 @@ template <> struct QT<T_Q6_K_S> : QT<T_Q6_K> {
     }
 };
 
+// dp4a with unsigned bytes in a and signed bytes in b (dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One group of the T = 1 gate/up phase from shared memory: NR rows of gate
+// and NR rows of up (2*NR "streams", NB Q4_K blocks each, the NR rows of a
+// matrix consecutive in the tile) against one int8 activation vector in the
+// xpad_q4kw layout. Lane (b = lane/4, j = lane%4) takes block b and sub-block
+// pair j of every stream, so its activation fragment is loaded once; the two
+// nibble halves go through dp4a directly (the high half unshifted, as 16x the
+// nibble through the unsigned form, divided back exactly). Each stream's block
+// terms are then added in block order from +0 through a per-warp shared
+// transpose `tt` (2*NR*NB floats), leaving stream s's dot in lane s.
+// Numerics are QT<T_Q4_KW>'s exactly (integer partials, same float tail).
+template <int NR, int NB>
+__device__ __forceinline__ float q4k_group_dot_smem(const uint8_t *tile_g, const uint8_t *tile_u, const int8_t *xq,
+                                                    const float *xd, const int32_t *xs, float *tt, int lane) {
+    static_assert(NB == 8, "one lane group per block");
+    constexpr int S = 2 * NR;
+    const int b = lane >> 2, j = lane & 3;
+    const int4 *x4 = reinterpret_cast<const int4 *>(xq + b * XPAD_BLOCK + 80 * j);
+    const int4 l0 = x4[0], l1 = x4[1], h0 = x4[2], h1 = x4[3];
+    const int4 bs = *reinterpret_cast<const int4 *>(xs + b * 16 + 4 * j);
+    const float xdb = xd[b];
+    const int ms0 = bs.x + bs.y, ms1 = bs.z + bs.w;
+    const int sh = 16 * (j & 1);
+    const bool low = j < 2;
+    // straight-line per stream (no branch, no shuffle): the streams' chains interleave
+    int I[S], M[S];
+    uint32_t hx[S];
+#pragma unroll
+    for (int s = 0; s < S; s++) {
+        const uint8_t *blk = (s < NR ? tile_g + (size_t)s * NB * 144 : tile_u + (size_t)(s - NR) * NB * 144) + b * 144;
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * j);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * j);
+        int dla = dp4a((int)(q0.x & 0x0F0F0F0Fu), l0.x, 0), dlb = dp4a((int)(q0.y & 0x0F0F0F0Fu), l0.y, 0);
+        dla = dp4a((int)(q0.z & 0x0F0F0F0Fu), l0.z, dla);
+        dlb = dp4a((int)(q0.w & 0x0F0F0F0Fu), l0.w, dlb);
+        dla = dp4a((int)(q1.x & 0x0F0F0F0Fu), l1.x, dla);
+        dlb = dp4a((int)(q1.y & 0x0F0F0F0Fu), l1.y, dlb);
+        dla = dp4a((int)(q1.z & 0x0F0F0F0Fu), l1.z, dla);
+        dlb = dp4a((int)(q1.w & 0x0F0F0F0Fu), l1.w, dlb);
+        int dha = dp4a_us(q0.x & 0xF0F0F0F0u, h0.x, 0), dhb = dp4a_us(q0.y & 0xF0F0F0F0u, h0.y, 0);
+        dha = dp4a_us(q0.z & 0xF0F0F0F0u, h0.z, dha);
+        dhb = dp4a_us(q0.w & 0xF0F0F0F0u, h0.w, dhb);
+        dha = dp4a_us(q1.x & 0xF0F0F0F0u, h1.x, dha);
+        dhb = dp4a_us(q1.y & 0xF0F0F0F0u, h1.y, dhb);
+        dha = dp4a_us(q1.z & 0xF0F0F0F0u, h1.z, dha);
+        dhb = dp4a_us(q1.w & 0xF0F0F0F0u, h1.w, dhb);
+        const int dl = dla + dlb, dh = (dha + dhb) >> 4;  // exact: a multiple of 16
+        // scaleMinK4 (ggml.zig:1332) for sub-blocks 2j, 2j+1
+        const uint32_t a = h.y >> sh, bb = h.z >> sh, lo = h.w >> sh;
+        const int sc0 = low ? (a & 63) : ((lo & 0xF) | (((a >> 6) & 3) << 4));
+        const int mn0 = low ? (bb & 63) : (((lo >> 4) & 0xF) | (((bb >> 6) & 3) << 4));
+        const int sc1 = low ? ((a >> 8) & 63) : (((lo >> 8) & 0xF) | (((a >> 14) & 3) << 4));
+        const int mn1 = low ? ((bb >> 8) & 63) : (((lo >> 12) & 0xF) | (((bb >> 14) & 3) << 4));
+        I[s] = sc0 * dl + sc1 * dh;
+        M[s] = mn0 * ms0 + mn1 * ms1;
+        hx[s] = h.x;
+    }
+    // the block's four lanes: integer sums (exact, any order)
+#pragma unroll
+    for (int s = 0; s < S; s++) {
+        I[s] += __shfl_xor_sync(0xffffffffu, I[s], 1);
+        M[s] += __shfl_xor_sync(0xffffffffu, M[s], 1);
+    }
+#pragma unroll
+    for (int s = 0; s < S; s++) {
+        I[s] += __shfl_xor_sync(0xffffffffu, I[s], 2);
+        M[s] += __shfl_xor_sync(0xffffffffu, M[s], 2);
+    }
+    if (j == 0) {
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            const float d = f16_to_f32((uint16_t)(hx[s] & 0xFFFF)), dmin = f16_to_f32((uint16_t)(hx[s] >> 16));
+            tt[s * NB + b] = fmul(xdb, fsub(fmul(d, (float)I[s]), fmul(dmin, (float)M[s])));
+        }
+    }
+    __syncwarp();
+    float acc = 0.0f;
+    if (lane < S) {
+#pragma unroll
+        for (int bb = 0; bb < NB; bb++) acc = fadd(acc, tt[lane * NB + bb]);
+    }
+    __syncwarp();
+    return acc;
+}
+
+// SC consecutive rows of a staged Q6_K tile (row r's NB blocks at block index
+// (row0 + r) * NB; rows past nvalid repeat row0) against one int8 activation
+// vector in the xpad_q6k layout (one scale per 256-block, sums per 16). Lane
+// group g = lane/4 takes row g and, lane sub = lane%4, a quarter of every
+// block; each row's block terms are then added in block order from +0 inside
+// the group's own lanes (no transpose). Returns row (lane/4)'s dot on every
+// lane of its group. Numerics are QT<T_Q6_K>'s exactly.
+template <int SC, int NB>
+__device__ __forceinline__ float q6k_rows_dot_smem(const WDev &w, int row0, int nvalid, const int8_t *aq,
+                                                   const float *ad, const int32_t *as, int lane) {
+    static_assert(SC == 8, "one lane group per row");
+    const int g = lane >> 2, sub = lane & 3;
+    const uint64_t gb0 = (uint64_t)(row0 + (g < nvalid ? g : 0)) * NB;
+    int I[NB];
+    uint32_t dw[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const typename QT<T_Q6_K_S>::Frag f = QT<T_Q6_K_S>::load(w, gb0 + b, sub);
+        int Ib, Mb;
+        QT<T_Q6_K_S>::part(f, sub, aq + b * XPAD_BLOCK, as + b * 16, Ib, Mb);
+        I[b] = Ib;
+        dw[b] = f.d;
+    }
+#pragma unroll
+    for (int b = 0; b < NB; b++) I[b] += __shfl_xor_sync(0xffffffffu, I[b], 1);
+#pragma unroll
+    for (int b = 0; b < NB; b++) I[b] += __shfl_xor_sync(0xffffffffu, I[b], 2);
+    float acc = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+        acc = fadd(acc, fmul(fmul(ad[b], f16_to_f32((uint16_t)dw[b])), (float)I[b]));
+    return acc;
+}
+
 template <> struct QT<T_Q8_0> {
     static constexpr int LPB = 2, BE = 32, SPB = 1;
     struct Frag {
