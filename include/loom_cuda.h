@@ -242,10 +242,14 @@ int loom_cuda_ep_size(void);
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);
-/* Test hook selecting the MoE kernel family (all compute the same numbers):
- * 0 automatic (fused decode kernels for T <= 16, expert-major batch kernels
- * above), 1 the general slot kernels, 2 the expert-major batch kernels at any
- * T. Returns the previous setting. */
+/* Test hook selecting the MoE kernel family: 0 automatic (fused decode
+ * kernels for T <= 16, expert-major batch kernels above, on the tensor cores
+ * once the experts average >= 16 tokens), 1 the general slot kernels, 2 the
+ * expert-major batch kernels at any T, 3 the expert-major batch kernels on
+ * the tensor cores at any T (Q4_K gate/up with Q6_K down; other types fall
+ * back to 2). 0-2 compute the same numbers bit for bit; 3 rounds the weights
+ * and activations to bf16 (within 2e-3 relative L2). Returns the previous
+ * setting. */
 int loom_cuda_force_generic(int on);
 /* Phase tracing of the fused decode kernels (the counterpart of the
  * reference's LOOM_PROFILE phase timers, deepseek.zig:705-850): with room for

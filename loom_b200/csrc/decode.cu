@@ -755,13 +755,14 @@ __global__ void __launch_bounds__(512) k_group(DecodeArgs A) {
         }
     }
     __syncthreads();
+    for (int e = threadIdx.x; e < A.n_local; e += blockDim.x) cnt[e] = 0;  // now: fill positions
+    __syncthreads();
+    // the order of slots inside a group does not matter: every slot's output is
+    // computed on its own and the combine adds slots in selection order
     for (int s = threadIdx.x; s < ns; s += blockDim.x) {
-        const int id = A.ids[s];
-        const int le = id - A.expert0;
+        const int le = A.ids[s] - A.expert0;
         if (le < 0 || le >= A.n_local) continue;
-        int before = 0;  // earlier slots of the same expert
-        for (int j = 0; j < s; j++) before += A.ids[j] == id;
-        A.grp_list[A.grp_off[le] + before] = s;
+        A.grp_list[A.grp_off[le] + atomicAdd(&cnt[le], 1)] = s;
     }
 }
 
@@ -957,10 +958,19 @@ bool batch_supported(const DecodeArgs &A) {
     return (size_t)(A.dim + 2 * A.n_expert + 136) * 4 <= 48 * 1024;
 }
 
-cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st) {
+static cudaError_t launch_quant_grp(const DecodeArgs &A, cudaStream_t st) {
+    const int n_slots = A.T * A.n_used + (A.has_shared ? A.T : 0);
+    return launch_pdl(k_quant_grp, dim3(n_slots), dim3(128), 0, st, A);
+}
+
+cudaError_t launch_batch(const DecodeArgs &A, bool mma, cudaStream_t st) {
     cudaError_t e = launch_router(A, st);
     if (e != cudaSuccess) return e;
     if ((e = launch_pdl(k_group, dim3(1), dim3(512), 0, st, A)) != cudaSuccess) return e;
+    if (mma) {
+        if ((e = launch_moe_mma(A, st, launch_quant_grp)) != cudaSuccess) return e;
+        return launch_pdl(k_combine, dim3(cdivu(A.dim, 256), A.T), dim3(256), 0, st, A);
+    }
     const int nexp = A.n_local + (A.has_shared ? 1 : 0);
     const int nb = A.dim / 256;
     const int rows_cta = GU_WARPS * (nb <= 8 ? 3 : 1);

@@ -61,7 +61,12 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st);
 // every token of the expert against one read of its rows, activation
 // quantization, down per expert, ordered combine.
 bool batch_supported(const DecodeArgs &A);
-cudaError_t launch_batch(const DecodeArgs &A, cudaStream_t st);
+// mma: gate/up and down as tcgen05 bf16 GEMMs (moe_mma_supported) instead of
+// the int8 dot kernels
+cudaError_t launch_batch(const DecodeArgs &A, bool mma, cudaStream_t st);
+bool moe_mma_supported(const DecodeArgs &A);
+cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st,
+                           cudaError_t (*quant)(const DecodeArgs &, cudaStream_t));
 
 }  // namespace loom
 

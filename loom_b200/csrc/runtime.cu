@@ -306,7 +306,7 @@ bool any_type(const RoutedLayerDev &L, bool k256) {
 // batches use the slot kernels.
 constexpr size_t DECODE_MAX_T = 16;
 
-bool g_force_generic = false;
+int g_force_generic = 0;  // test hook: 0 auto, 1 slot kernels, 2 batch kernels, 3 batch on the tensor cores
 const uint8_t *g_next_router = nullptr;  // L2-prefetch hint for the layer being launched
 size_t g_next_router_bytes = 0;
 // phase trace: [2*n] (first start, last end) per traced kernel, see loom_cuda_trace_*
@@ -382,13 +382,16 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
             return 0;
         }
         if (router && batch_supported(A)) {
+            // tensor cores once the experts average 16 or more tokens each (prefill)
+            const bool mma = moe_mma_supported(A) &&
+                             (g_force_generic == 3 || (g_force_generic == 0 && T * L.n_used >= 16 * (size_t)L.n_local));
             if (int rc = S.grp.ensure((2 * (size_t)L.n_local + T * L.n_used) * 4)) return rc;
             if (int rc = S.ybuf.ensure(n_slots * (size_t)L.dim * 4)) return rc;
             A.grp_cnt = S.grp.as<int>();
             A.grp_off = A.grp_cnt + L.n_local;
             A.grp_list = A.grp_off + L.n_local;
             A.y = S.ybuf.as<float>();
-            CK(launch_batch(A, st));
+            CK(launch_batch(A, mma, st));
             return 0;
         }
     }

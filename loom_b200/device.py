@@ -161,7 +161,8 @@ def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -
 
 
 def force_generic(mode) -> int:
-    """Kernel family for MoE layers: 0 automatic, 1 (True) slot kernels, 2 expert-major batch kernels."""
+    """Kernel family for MoE layers: 0 automatic, 1 (True) slot kernels, 2 expert-major batch kernels
+    (int8 dots), 3 expert-major batch kernels on the tensor cores (bf16 tcgen05 GEMMs)."""
     return int(_lib.lib().loom_cuda_force_generic(int(mode)))
 
 

@@ -1,0 +1,86 @@
+"""The tensor-core batch path (tcgen05 kind::f16 MMAs carrying the
+reference's integer sub-block products: sc*q weights and int8 activations,
+exact in fp16 and in the f32 accumulator) against the CPU oracle and against
+the int8 batch kernels: bit-identical outputs, ids the router's."""
+from tests.conftest import bits
+import numpy as np
+import pytest
+import torch
+
+from loom_b200 import _lib
+from loom_b200 import device as D
+from tests.conftest import rel_l2
+from tests.test_gpu_moe import _layer_case, _route_gaps_ok, synth_layer
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def _run(L, x, mode, k):
+    prev = D.force_generic(mode)
+    try:
+        out = torch.full(x.shape, float("nan"), device="cuda")
+        ids = torch.zeros((x.shape[0], k), dtype=torch.int32, device="cuda")
+        L.forward(x, out, ids=ids)
+        torch.cuda.synchronize()
+    finally:
+        D.force_generic(prev)
+    assert _lib.lib().loom_cuda_device_error() == 0
+    return out.cpu().numpy(), ids.cpu().numpy()
+
+
+@pytest.mark.parametrize("T", [64, 256])
+def test_mma_layer_vs_oracle(be, orc, T):
+    """Qwen3-30B-A3B layer (config 2) forced onto the tensor cores, against
+    the oracle's moeLayer token by token."""
+    ne, k, dim, ffn = 128, 8, 2048, 768
+    g, u, d = synth_layer(orc, 11, ne, dim, ffn)
+    rw = orc.synth(0, ne * dim, seed=111, sigma=0.02)
+    x = orc.synth(0, T * dim, seed=112, sigma=1.0).reshape(T, dim)
+    L = D.MoeLayer(dim, ffn, ne, k, D.DeviceTensor.upload(12, g), D.DeviceTensor.upload(12, u),
+                   D.DeviceTensor.upload(14, d), router=D.DeviceTensor.upload(0, rw))
+    got, gids = _run(L, torch.from_numpy(x).cuda(), 3, k)
+    orc.parallel_begin(16)
+    try:
+        want, wids = orc.moe_layer(x, rw, (12, g), (12, u), (14, d), ffn, ne, k)
+        logits = orc.matmul(0, rw.view(np.uint8), x, ne, dim)
+    finally:
+        orc.parallel_end()
+    compared = 0
+    for t in range(T):
+        if _route_gaps_ok(logits[t], k):
+            assert list(gids[t]) == list(wids[t]), t
+            assert rel_l2(got[t], want[t]) < TOL, (t, rel_l2(got[t], want[t]))
+            compared += 1
+    assert compared >= T * 3 // 4
+    for t in (L.gate, L.up, L.down, L.router):
+        t.free()
+
+
+def test_mma_auto_prefill_matches_int8_batch(be, orc):
+    """T = 512 (32 tokens per expert): the automatic choice is the tensor-core
+    path; it agrees with the int8 expert-major kernels within tolerance."""
+    ne, k, dim, ffn, T = 128, 8, 2048, 768, 512
+    L = _layer_case(orc, 21, ne=ne, k=k, dim=dim, ffn=ffn, gt=12, dt=14)
+    x = torch.from_numpy(orc.synth(0, T * dim, seed=212, sigma=1.0).reshape(T, dim)).cuda()
+    auto, ids_a = _run(L, x, 0, k)
+    ref, ids_r = _run(L, x, 2, k)
+    assert np.array_equal(ids_a, ids_r)
+    assert np.array_equal(bits(auto), bits(ref))
+    k0 = _lib.lib().loom_cuda_kernel_launches()
+    _run(L, x, 0, k)
+    assert _lib.lib().loom_cuda_kernel_launches() > k0
+
+
+def test_mma_shared_expert_and_ragged_groups(be, orc):
+    """A layer with a shared expert (DeepSeek-style, sigmoid + bias routing),
+    dim 1024 / ffn 512, 40 experts so groups are ragged: tensor cores vs the
+    int8 batch kernels."""
+    cfg = dict(ne=40, k=4, dim=1024, ffn=512, gt=12, dt=14, shared=512, gating=2, scale=2.5, bias=True)
+    L = _layer_case(orc, 31, **cfg)
+    T = 200
+    x = torch.from_numpy(orc.synth(0, T * cfg["dim"], seed=312, sigma=1.0).reshape(T, cfg["dim"])).cuda()
+    mma, ids_m = _run(L, x, 3, cfg["k"])
+    ref, ids_r = _run(L, x, 2, cfg["k"])
+    assert np.array_equal(ids_m, ids_r)
+    assert np.array_equal(bits(mma), bits(ref)), rel_l2(mma, ref)
