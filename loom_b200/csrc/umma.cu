@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(128) k_umma_selftest(const uint16_t *A, const 
 using namespace loom;
 
 extern "C" int loom_cuda_umma_selftest(const uint16_t *A, const uint16_t *B, float *D, int M, int N, int K);
+extern "C" int loom_cuda_mma_profile(unsigned long long *out16);
 
 // Diagnostic entry (no counterpart in the reference): runs the bf16 tcgen05
 // GEMM on host arrays; returns 0, 1 on bad arguments, 2 on a CUDA error, 3 if
@@ -165,6 +166,35 @@ __device__ __forceinline__ uint4 h8_from_i8(uint32_t lo, uint32_t hi) {
                       h2i(sb(hi, 2), sb(hi, 3)));
 }
 
+// Exact small-integer -> fp16 conversions through the fp16 "magic" 1024:
+// 0x6400 | v is 1024 + v for 0 <= v < 1024, and one fused HFMA2 / HSUB2 of
+// exactly representable operands with an exactly representable result is
+// exact.
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Q4_K: 4 bytes of nibbles -> low nibbles (4 values, scale sl) and high
+// nibbles (4 values, scale sh) as fp16 pairs: sc * q, exact (<= 945)
+__device__ __forceinline__ void q4_word_to_h(uint32_t w, __half2 sl2, __half2 offl, __half2 sh16, __half2 offh,
+                                             uint32_t &lo01, uint32_t &lo23, uint32_t &hi01, uint32_t &hi23) {
+    const uint32_t p01 = __byte_perm(w, 0, 0x4140), p23 = __byte_perm(w, 0, 0x4342);
+    lo01 = h2u(__hfma2(u2h((p01 & 0x000F000Fu) | 0x64006400u), sl2, offl));  // (1024 + q) * sc - 1024 sc
+    lo23 = h2u(__hfma2(u2h((p23 & 0x000F000Fu) | 0x64006400u), sl2, offl));
+    hi01 = h2u(__hfma2(u2h((p01 & 0x00F000F0u) | 0x64006400u), sh16, offh));  // (1024 + 16q) * sc/16 - 64 sc
+    hi23 = h2u(__hfma2(u2h((p23 & 0x00F000F0u) | 0x64006400u), sh16, offh));
+}
+
+// 8 int8 (two words) -> 8 fp16, exact: (1024 + (v + 128)) - 1152
+__device__ __forceinline__ uint4 h8_from_i8_fast(uint32_t lo, uint32_t hi) {
+    const __half2 k = u2h(0x64806480u);  // 1152, 1152
+    lo ^= 0x80808080u;
+    hi ^= 0x80808080u;
+    return make_uint4(h2u(__hsub2(u2h(__byte_perm(lo, 0x64646464u, 0x7170) ), k)),
+                      h2u(__hsub2(u2h(__byte_perm(lo, 0x64646464u, 0x7372)), k)),
+                      h2u(__hsub2(u2h(__byte_perm(hi, 0x64646464u, 0x7170)), k)),
+                      h2u(__hsub2(u2h(__byte_perm(hi, 0x64646464u, 0x7372)), k)));
+}
+
 // Instruction descriptor of kind::f16 with fp16 A and B, f32 accumulator
 // (formats 0 = F16 in bits [7,10) and [10,13)).
 __host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N) {
@@ -173,6 +203,23 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N) {
 
 constexpr int MMA_THREADS = 512;  // 16 warps: TMEM row quarter = warp % 4, token group = warp / 4
 constexpr int MMA_NP = 64;        // tokens per pass (the MMA's N)
+
+// Diagnostic: cycles spent by thread 0 of every CTA in the sections of the
+// MMA kernels, summed over CTAs ([kernel 0 = gate/up, 1 = down][section]);
+// read and cleared by loom_cuda_mma_profile.
+__device__ unsigned long long g_mma_cyc[2][8];
+
+struct MmaProf {
+    long long t;
+    int k;
+    __device__ __forceinline__ void mark(int sec) {
+        if (threadIdx.x == 0) {
+            const long long n = clock64();
+            atomicAdd(&g_mma_cyc[k][sec], (unsigned long long)(n - t));
+            t = n;
+        }
+    }
+};
 
 struct MmaCtl {
     uint64_t mbar[2];
@@ -200,6 +247,21 @@ __device__ __forceinline__ void tmem_ints16(uint32_t tmem, int q, uint32_t col, 
     for (int i = 0; i < 16; i++) v[i] = __float2int_rn(__uint_as_float(r[i]));
 }
 
+// raw Q4_K words thread t needs at gate/up step ks: the super-block header and
+// the 32 nibble bytes of its sub-block pair
+template <int NBG>
+__device__ __forceinline__ void gu_fetch_t(uint4 (&pw)[3], const WDev &wg, const WDev &wu, uint64_t plane, int row0,
+                                           int ffn, int ks, int t) {
+    const int mat = t >> 8, jj = (t >> 7) & 1, r = t & 127, row = row0 + r;
+    if (row >= ffn) return;
+    const uint8_t *bp = (mat ? wu : wg).q + (plane + (uint64_t)row * NBG + (ks >> 1)) * 144;
+    const int j = 2 * (ks & 1) + jj;
+    pw[0] = ld_stream_v4(bp);
+    pw[1] = ld_stream_v4(bp + 16 + 32 * j);
+    pw[2] = ld_stream_v4(bp + 32 + 32 * j);
+}
+#define gu_fetch gu_fetch_t<NBG>
+
 // ---- gate/up (Q4_K): act[slot][row] = silu(gate . x) * (up . x) ----------------------------
 // Expert blockIdx.y (n_local = the shared expert), rows [128*blockIdx.x, +128).
 template <int NBG>
@@ -214,6 +276,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
     __shared__ uint32_t s_mn[2][2][128][2];
     __shared__ float s_xd[2][MMA_NP];
     __shared__ int s_bs[2][MMA_NP][8];
+    __shared__ const int8_t *s_tok[MMA_NP];
     umma_pdl_wait();
     const int e = blockIdx.y;
     const bool shared = e == A.n_local;
@@ -246,45 +309,53 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
 #pragma unroll
         for (int i = 0; i < 16; i++) ag[i] = au[i] = 0.0f;
         const uint32_t step0 = gstep;
+        for (int i = t; i < nc; i += MMA_THREADS) {  // this pass's tokens' int8 rows
+            const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
+            s_tok[i] = A.x256.q + (size_t)(shared ? c0 + i : slot / A.n_used) * dim;
+        }
+        __syncthreads();
+        uint4 pw[3];  // this thread's raw weight words of the next step (header, two nibble quarters)
+        gu_fetch(pw, wg, wu, plane, row0, ffn, 0, t);
+        uint2 px[2];  // this thread's token words of the next step
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int it = t + u * MMA_THREADS;
+            if (it < N * 16 && (it >> 4) < nc) px[u] = *reinterpret_cast<const uint2 *>(s_tok[it >> 4] + (it & 15) * 8);
+        }
+        MmaProf pf{clock64(), 0};
         for (int ks = 0; ks <= KSTEPS; ks++) {
             if (ks < KSTEPS) {  // ---- stage step ks into buffer gstep & 1 (its previous MMAs were awaited below)
                 const int b = gstep & 1, blk = ks >> 1, h = ks & 1, pb = blk & 1;
                 uint8_t *tA = sm + (size_t)b * (A_BYTES + B_BYTES), *tB = tA + A_BYTES;
-                {   // weights: thread -> (matrix, row, sub-block pair jj of this half)
-                    const int mat = t >> 8, r = (t >> 1) & 127, jj = t & 1, row = row0 + r;
+                {   // weights (prefetched one step ahead): thread -> (matrix, sub-block pair jj of this half, row);
+                    // a warp stores 32 consecutive rows of one chunk (no bank conflicts)
+                    const int mat = t >> 8, jj = (t >> 7) & 1, r = t & 127, row = row0 + r;
                     uint8_t *tile = tA + (size_t)mat * 16 * 128 * 16;
+                    const uint4 hd = pw[0], q0 = pw[1], q1 = pw[2];
+                    if (ks + 1 < KSTEPS) gu_fetch(pw, wg, wu, plane, row0, ffn, ks + 1, t);
                     if (row < ffn) {
-                        const uint8_t *bp = (mat ? wu : wg).q + (plane + (uint64_t)row * NBG + blk) * 144;
-                        const uint4 hd = *reinterpret_cast<const uint4 *>(bp);
-                        const int j = 2 * h + jj;
-                        const uint4 q0 = *reinterpret_cast<const uint4 *>(bp + 16 + 32 * j);
-                        const uint4 q1 = *reinterpret_cast<const uint4 *>(bp + 32 + 32 * j);
+                        const int j = 2 * h + jj;  // warp-uniform
                         int sl, ml, sh, mh;
                         scale_min_k4w(2 * j, hd.y, hd.z, hd.w, sl, ml);
                         scale_min_k4w(2 * j + 1, hd.y, hd.z, hd.w, sh, mh);
+                        const __half2 sl2 = __half2half2(__int2half_rn(sl)), offl = __half2half2(__int2half_rn(-1024 * sl));
+                        const __half2 sh16 = __half2half2(__float2half_rn((float)sh * 0.0625f)),
+                                      offh = __half2half2(__int2half_rn(-64 * sh));
                         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {  // chunk 8jj + c: low nibbles, 8jj + 4 + c: high
-                            const uint32_t a = w[2 * c], bb = w[2 * c + 1];
-                            auto nb = [](uint32_t x, int i, int sh4) { return (int)((x >> (8 * i + sh4)) & 0xF); };
-                            *reinterpret_cast<uint4 *>(tile + ((size_t)(8 * jj + c) * 128 + r) * 16) =
-                                make_uint4(h2i(sl * nb(a, 0, 0), sl * nb(a, 1, 0)), h2i(sl * nb(a, 2, 0), sl * nb(a, 3, 0)),
-                                           h2i(sl * nb(bb, 0, 0), sl * nb(bb, 1, 0)), h2i(sl * nb(bb, 2, 0), sl * nb(bb, 3, 0)));
-                            *reinterpret_cast<uint4 *>(tile + ((size_t)(8 * jj + 4 + c) * 128 + r) * 16) =
-                                make_uint4(h2i(sh * nb(a, 0, 4), sh * nb(a, 1, 4)), h2i(sh * nb(a, 2, 4), sh * nb(a, 3, 4)),
-                                           h2i(sh * nb(bb, 0, 4), sh * nb(bb, 1, 4)), h2i(sh * nb(bb, 2, 4), sh * nb(bb, 3, 4)));
+                        for (int c = 0; c < 4; c++) {  // chunk 8jj + c: low nibbles of bytes 8c..8c+7, 8jj + 4 + c: high
+                            uint32_t a0, a1, b0, b1, c0_, c1_, d0, d1;
+                            q4_word_to_h(w[2 * c], sl2, offl, sh16, offh, a0, a1, b0, b1);
+                            q4_word_to_h(w[2 * c + 1], sl2, offl, sh16, offh, c0_, c1_, d0, d1);
+                            *reinterpret_cast<uint4 *>(tile + ((size_t)(8 * jj + c) * 128 + r) * 16) = make_uint4(a0, a1, c0_, c1_);
+                            *reinterpret_cast<uint4 *>(tile + ((size_t)(8 * jj + 4 + c) * 128 + r) * 16) = make_uint4(b0, b1, d0, d1);
                         }
                         if (h == 0 && jj == 0) {  // the super-block's float scales and its 8 mins
                             s_d[pb][mat][r] = f16_to_f32((uint16_t)(hd.x & 0xFFFF));
                             s_dmin[pb][mat][r] = f16_to_f32((uint16_t)(hd.x >> 16));
-                            uint32_t m0 = 0, m1 = 0;
-#pragma unroll
-                            for (int sbk = 0; sbk < 8; sbk++) {
-                                int sc_, mn_;
-                                scale_min_k4w(sbk, hd.y, hd.z, hd.w, sc_, mn_);
-                                if (sbk < 4) m0 |= (uint32_t)mn_ << (8 * sbk);
-                                else m1 |= (uint32_t)mn_ << (8 * (sbk - 4));
-                            }
+                            // mins: bytes 4..7 & 63 (sub-blocks 0-3); sub-blocks 4-7: (byte 8+i >> 4) | (byte 4+i >> 6) << 4
+                            const uint32_t m0 = hd.z & 0x3F3F3F3Fu;
+                            const uint32_t m1 = ((hd.w >> 4) & 0x0F0F0F0Fu) | (((hd.z >> 6) & 0x03030303u) << 4);
                             s_mn[pb][mat][r][0] = m0;
                             s_mn[pb][mat][r][1] = m1;
                         }
@@ -293,17 +364,17 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                             *reinterpret_cast<uint4 *>(tile + ((size_t)kc * 128 + r) * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                for (int it = t; it < N * 16; it += MMA_THREADS) {  // tokens: int8 activations -> fp16
-                    const int i = it >> 4, kc = it & 15;
-                    uint4 v4 = make_uint4(0, 0, 0, 0);
-                    if (i < nc) {
-                        const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
-                        const int tok = shared ? c0 + i : slot / A.n_used;
-                        const uint2 x8 = *reinterpret_cast<const uint2 *>(A.x256.q + (size_t)tok * dim + blk * 256 +
-                                                                          h * 128 + kc * 8);
-                        v4 = h8_from_i8(x8.x, x8.y);
+                pf.mark(0);  // weights
+#pragma unroll
+                for (int u = 0; u < 2; u++) {  // tokens (prefetched one step ahead): int8 activations -> fp16
+                    const int it = t + u * MMA_THREADS;
+                    if (it < N * 16) {
+                        const int i = it >> 4, kc = it & 15;
+                        *reinterpret_cast<uint4 *>(tB + ((size_t)kc * N + i) * 16) =
+                            i < nc ? h8_from_i8_fast(px[u].x, px[u].y) : make_uint4(0, 0, 0, 0);
+                        if (ks + 1 < KSTEPS && i < nc)
+                            px[u] = *reinterpret_cast<const uint2 *>(s_tok[i] + ((ks + 1) >> 1) * 256 + ((ks + 1) & 1) * 128 + kc * 8);
                     }
-                    *reinterpret_cast<uint4 *>(tB + ((size_t)kc * N + i) * 16) = v4;
                 }
                 if (h == 0)
                     for (int it = t; it < nc * 9; it += MMA_THREADS) {  // tokens' xd and per-32 sums of block blk
@@ -316,26 +387,32 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                             s_bs[pb][i][k] = ss[0] + ss[1];
                         }
                     }
+                pf.mark(1);  // tokens
                 fence_async_smem();
                 __syncthreads();
+                pf.mark(2);  // barrier
                 if (t == 0) {
                     tc_fence_after();
                     const uint32_t dcol = (uint32_t)b * 2 * MMA_NP;
+                    // K step s: the start address field (16-byte units) advances by 2 chunks
+                    const uint64_t ag = umma_desc_kmajor(tA, 128), au = umma_desc_kmajor(tA + 16 * 128 * 16, 128);
+                    const uint64_t bd = umma_desc_kmajor(tB, (uint32_t)N);
 #pragma unroll
                     for (int s = 0; s < 8; s++) {
-                        const uint64_t bd = umma_desc_kmajor(tB + (size_t)2 * s * N * 16, (uint32_t)N);
-                        umma_bf16(tmem + dcol, umma_desc_kmajor(tA + 2 * s * 128 * 16, 128), bd, idesc, s > 0);
-                        umma_bf16(tmem + dcol + MMA_NP, umma_desc_kmajor(tA + 16 * 128 * 16 + 2 * s * 128 * 16, 128),
-                                  bd, idesc, s > 0);
+                        const uint64_t bs = bd + (uint64_t)(2 * s * N);
+                        umma_bf16(tmem + dcol, ag + (uint64_t)(256 * s), bs, idesc, s > 0);
+                        umma_bf16(tmem + dcol + MMA_NP, au + (uint64_t)(256 * s), bs, idesc, s > 0);
                     }
                     umma_commit(&S.mbar[b]);
                 }
+                pf.mark(3);  // issue
                 gstep++;
             }
             if (ks >= 1) {  // ---- epilogue of step ks - 1 (its MMAs done), overlapping step ks's MMAs
                 const uint32_t ps = gstep - (ks < KSTEPS ? 2 : 1);  // the step to finish
                 const int pbuf = ps & 1;
                 if (!mma_wait(S, pbuf, (ps >> 1) & 1, A.err)) break;
+                pf.mark(4);  // MMA wait
                 tc_fence_after();
                 const int pks = (int)(ps - step0), pblk = pks >> 1, ph = pks & 1, pb = pblk & 1;
                 if (tok0 < N) {
@@ -373,6 +450,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                     }
                 }
                 tc_fence_before();
+                pf.mark(5);  // epilogue
             }
         }
         if (!S.ok) break;
@@ -394,6 +472,25 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
     if (warp == 0) tmem_free(tmem, ncols);
 }
 
+// raw Q6_K words thread t needs at down step ks: its group's 32 ql bytes, the
+// half's 32 qh bytes, its two scales, and the block's d
+template <int NBD>
+__device__ __forceinline__ void dn_fetch_t(uint4 (&pq)[4], uint32_t &scw, float &d, const WDev &wd, uint64_t plane,
+                                           int row0, int dim, int ks, int t) {
+    const int g = t >> 7, r = t & 127, row = row0 + r, h = ks & 1;
+    if (row >= dim) return;
+    const uint64_t gb = plane + (uint64_t)row * NBD + (ks >> 1);
+    const uint8_t *qb = wd.q + gb * 192;
+    pq[0] = ld_stream_v4(qb + 64 * h + 32 * (g & 1));
+    pq[1] = ld_stream_v4(qb + 64 * h + 32 * (g & 1) + 16);
+    pq[2] = ld_stream_v4(qb + 128 + 32 * h);
+    pq[3] = ld_stream_v4(qb + 128 + 32 * h + 16);
+    const uint16_t s2 = *reinterpret_cast<const uint16_t *>(wd.sc + gb * 16 + 8 * h + 2 * g);
+    scw = s2;
+    d = f16_to_f32(wd.d[gb]);
+}
+#define dn_fetch dn_fetch_t<NBD>
+
 // ---- down (Q6_K): y[slot][row] = W_down[row] . act[slot] ------------------------------------
 // act quantized per slot by quantizeX256 (aq / ad); expert blockIdx.y, output
 // rows [128*blockIdx.x, +128).
@@ -404,6 +501,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_dn_mma(DecodeArgs A) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ MmaCtl S;
     __shared__ float s_d[2][128], s_xd[2][MMA_NP];
+    __shared__ const int8_t *s_act[MMA_NP];
     umma_pdl_wait();
     const int e = blockIdx.y;
     const bool shared = e == A.n_local;
@@ -436,49 +534,67 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_dn_mma(DecodeArgs A) {
 #pragma unroll
         for (int i = 0; i < 16; i++) acc[i] = 0.0f;
         const uint32_t step0 = gstep;
+        for (int i = t; i < nc; i += MMA_THREADS) {  // this pass's slots' int8 activations
+            const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
+            s_act[i] = A.aq + (size_t)slot * stride;
+        }
+        __syncthreads();
+        uint4 pq[4];  // next step's raw words: ql (32 B) and qh (32 B) of this thread's group
+        uint32_t pscw = 0;
+        float pd = 0.0f;
+        dn_fetch(pq, pscw, pd, wd, plane, row0, A.dim, 0, t);
+        uint2 px[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int it = t + u * MMA_THREADS;
+            if (it < N * 16 && (it >> 4) < nc) px[u] = *reinterpret_cast<const uint2 *>(s_act[it >> 4] + (it & 15) * 8);
+        }
         for (int ks = 0; ks <= KSTEPS; ks++) {
             if (ks < KSTEPS) {
                 const int b = gstep & 1, blk = ks >> 1, h = ks & 1, pb = blk & 1;
                 uint8_t *tA = sm + (size_t)b * (A_BYTES + B_BYTES), *tB = tA + A_BYTES;
-                {   // weights: thread -> (row, group g of the half): values 32g + l, l < 32 -> chunks 4g .. 4g+3
-                    const int r = t >> 2, g = t & 3, row = row0 + r;
+                {   // weights (prefetched one step ahead): thread -> (row, group g of the half):
+                    // values 32g + l, l < 32 -> chunks 4g .. 4g+3
+                    const int g = t >> 7, r = t & 127, row = row0 + r;
+                    const uint4 ql0 = pq[0], ql1 = pq[1], qh0 = pq[2], qh1 = pq[3];
+                    const uint32_t scw = pscw;
+                    const float dcur = pd;
+                    if (ks + 1 < KSTEPS) dn_fetch(pq, pscw, pd, wd, plane, row0, A.dim, ks + 1, t);
                     if (row < A.dim) {
-                        const uint64_t gb = plane + (uint64_t)row * NBD + blk;
-                        const uint8_t *qb = wd.q + gb * 192;
-                        const int8_t *scb = reinterpret_cast<const int8_t *>(wd.sc + gb * 16) + 8 * h;
-                        const int s0 = scb[2 * g], s1 = scb[2 * g + 1];  // l < 16, l >= 16
+                        const int s0 = (int)(int8_t)(scw & 0xFF), s1 = (int)(int8_t)((scw >> 8) & 0xFF);
+                        const __half2 k1056 = u2h(0x64206420u);  // 1056 = 1024 + 32
+                        const uint32_t qlw[8] = {ql0.x, ql0.y, ql0.z, ql0.w, ql1.x, ql1.y, ql1.z, ql1.w};
+                        const uint32_t qhw[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
 #pragma unroll
                         for (int c = 0; c < 4; c++) {
-                            const uint2 qlw = *reinterpret_cast<const uint2 *>(qb + 64 * h + 32 * (g & 1) + 8 * c);
-                            const uint2 qhw = *reinterpret_cast<const uint2 *>(qb + 128 + 32 * h + 8 * c);
-                            const int sc = c < 2 ? s0 : s1;
-                            int v[8];
+                            const __half2 sc2 = __half2half2(__int2half_rn(c < 2 ? s0 : s1));
+                            uint32_t o[4];
 #pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                const uint32_t lw = i < 4 ? qlw.x : qlw.y, hw = i < 4 ? qhw.x : qhw.y;
-                                const uint32_t lb = (lw >> (8 * (i & 3))) & 0xFF, hb = (hw >> (8 * (i & 3))) & 0xFF;
-                                const int qv = (int)((g >= 2 ? lb >> 4 : lb & 0xF) | (((hb >> (2 * g)) & 3) << 4));
-                                v[i] = sc * (qv - 32);
+                            for (int wi = 0; wi < 2; wi++) {  // 4 values per word: q = low/high nibble | 2 qh bits << 4
+                                const uint32_t lw = qlw[2 * c + wi], hw = qhw[2 * c + wi];
+                                const uint32_t lo4 = (g >= 2 ? lw >> 4 : lw) & 0x0F0F0F0Fu;
+                                const uint32_t qb = lo4 | (((hw >> (2 * g)) & 0x03030303u) << 4);
+                                o[2 * wi] = h2u(__hmul2(__hsub2(u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), sc2));
+                                o[2 * wi + 1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), sc2));
                             }
-                            *reinterpret_cast<uint4 *>(tA + ((size_t)(4 * g + c) * 128 + r) * 16) =
-                                make_uint4(h2i(v[0], v[1]), h2i(v[2], v[3]), h2i(v[4], v[5]), h2i(v[6], v[7]));
+                            *reinterpret_cast<uint4 *>(tA + ((size_t)(4 * g + c) * 128 + r) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
                         }
-                        if (h == 0 && g == 0) s_d[pb][r] = f16_to_f32(wd.d[gb]);
+                        if (h == 0 && g == 0) s_d[pb][r] = dcur;
                     } else {
                         for (int kc = 4 * g; kc < 4 * g + 4; kc++)
                             *reinterpret_cast<uint4 *>(tA + ((size_t)kc * 128 + r) * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                for (int it = t; it < N * 16; it += MMA_THREADS) {  // int8 activations -> fp16
-                    const int i = it >> 4, kc = it & 15;
-                    uint4 v4 = make_uint4(0, 0, 0, 0);
-                    if (i < nc) {
-                        const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
-                        const uint2 x8 =
-                            *reinterpret_cast<const uint2 *>(A.aq + (size_t)slot * stride + blk * 256 + h * 128 + kc * 8);
-                        v4 = h8_from_i8(x8.x, x8.y);
+#pragma unroll
+                for (int u = 0; u < 2; u++) {  // activations (prefetched one step ahead): int8 -> fp16
+                    const int it = t + u * MMA_THREADS;
+                    if (it < N * 16) {
+                        const int i = it >> 4, kc = it & 15;
+                        *reinterpret_cast<uint4 *>(tB + ((size_t)kc * N + i) * 16) =
+                            i < nc ? h8_from_i8_fast(px[u].x, px[u].y) : make_uint4(0, 0, 0, 0);
+                        if (ks + 1 < KSTEPS && i < nc)
+                            px[u] = *reinterpret_cast<const uint2 *>(s_act[i] + ((ks + 1) >> 1) * 256 + ((ks + 1) & 1) * 128 + kc * 8);
                     }
-                    *reinterpret_cast<uint4 *>(tB + ((size_t)kc * N + i) * 16) = v4;
                 }
                 if (h == 0)
                     for (int i = t; i < nc; i += MMA_THREADS) {
@@ -490,10 +606,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_dn_mma(DecodeArgs A) {
                 if (t == 0) {
                     tc_fence_after();
                     const uint32_t dcol = (uint32_t)b * MMA_NP;
+                    const uint64_t ad = umma_desc_kmajor(tA, 128), bd = umma_desc_kmajor(tB, (uint32_t)N);
 #pragma unroll
                     for (int s = 0; s < 8; s++)
-                        umma_bf16(tmem + dcol, umma_desc_kmajor(tA + 2 * s * 128 * 16, 128),
-                                  umma_desc_kmajor(tB + (size_t)2 * s * N * 16, (uint32_t)N), idesc, s > 0);
+                        umma_bf16(tmem + dcol, ad + (uint64_t)(256 * s), bd + (uint64_t)(2 * s * N), idesc, s > 0);
                     umma_commit(&S.mbar[b]);
                 }
                 gstep++;
@@ -590,3 +706,14 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
 }
 
 }  // namespace loom
+
+// Diagnostic entry (no counterpart in the reference): copies the MMA kernels'
+// section cycle sums (2 x 8: gate/up then down; sections weights, tokens,
+// barrier, issue, MMA wait, epilogue) into out16 and clears them.
+int loom_cuda_mma_profile(unsigned long long *out16) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return 2;
+    if (cudaMemcpyFromSymbol(out16, loom::g_mma_cyc, sizeof(unsigned long long) * 16) != cudaSuccess) return 2;
+    unsigned long long z[16] = {};
+    if (cudaMemcpyToSymbol(loom::g_mma_cyc, z, sizeof z) != cudaSuccess) return 2;
+    return 0;
+}
