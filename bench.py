@@ -212,7 +212,8 @@ def run_gpu(args):
     layers = build_model(T, e0=ex0, nl=nloc)
     for l in range(LAYERS - 1):
         layers[l].next_router = layers[l + 1].router  # prefetch hint
-    D.reserve(T, DIM, FFN, NE, NK)
+    # size the scratch once for decode and prefill: graphs keep the pointers they captured
+    D.reserve(max(T, args.prefill_tokens if not ep else 0), DIM, FFN, NE, NK)
     descs = [L.desc() for L in layers]
     stream = torch.cuda.Stream()
     # replicas decode independent streams; expert-parallel ranks share one stream
@@ -287,6 +288,9 @@ def run_gpu(args):
 
     # e2e through the seam with host buffers
     e2e = None
+    prefill = None
+    if args.prefill_tokens > 0 and not ep:
+        prefill = run_prefill(args, layers, stream, torch, D)
     e2e_device = None
     if args.e2e_layers > 0 and not ep:
         e2e = run_e2e(args, B)
@@ -329,6 +333,8 @@ def run_gpu(args):
         line["e2e"] = e2e
     if e2e_device and e2e_device is not e2e:
         line["e2e_device"] = e2e_device
+    if prefill:
+        line["prefill"] = prefill
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -391,6 +397,59 @@ def trace_phases(D, step, stream, torch):
                    "down_dots": float(np.median(L[:, 10, 1]))},
         "unit": "us after the previous layer's down end",
     }
+
+
+def run_prefill(args, layers, stream, torch, D):
+    """Prefill: args.prefill_tokens tokens through the same layers on the
+    expert-major batch path (the experts average >= 16 tokens, so gate/up
+    and down run as tcgen05 MMAs), captured in one CUDA graph."""
+    T = args.prefill_tokens
+    D.reserve(T, DIM, FFN, NE, NK)
+    x0 = torch.from_numpy(np.random.default_rng(7).standard_normal((T, DIM)).astype(np.float32)).cuda()
+    bufs = [torch.empty((T, DIM), device="cuda") for _ in range(2)]
+    ids = torch.zeros((LAYERS, T, NK), dtype=torch.int32, device="cuda")
+    descs = [L.desc() for L in layers]
+
+    def step(sh):
+        cur = x0
+        for l, L in enumerate(layers):
+            nxt = bufs[l % 2]
+            L.forward(cur, nxt, residual=cur, ids=ids[l], stream=sh, desc=descs[l])
+            cur = nxt
+
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step(torch.cuda.current_stream().cuda_stream)
+    steps = max(2, min(args.steps, 5))
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    ids_np = ids.cpu().numpy()
+    bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1)) for l in range(LAYERS))
+    flops = 2.0 * T * NK * 3 * DIM * FFN * LAYERS  # gate, up, down per routed token
+    peak, peak_kind = peaks()
+    tpeak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"]) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    gbs = bytes_step / (ms * 1e-3) / 1e9
+    tfs = flops / (ms * 1e-3) / 1e12
+    return {"tokens": T, "layers": LAYERS, "value": round(T / (ms * 1e-3), 1), "unit": "tok/s",
+            "ms_per_step": round(ms, 3), "steps": steps,
+            "engine": "expert-major batch: tiled router GEMV, tcgen05 kind::f16 gate/up and down (integer-exact)",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "bytes_per_step": bytes_step,
+                         "tensor_tflops": round(tfs, 2), "tensor_peak": tpeak,
+                         "tensor_frac": round(tfs / tpeak, 5)}}
 
 
 def run_e2e_device(args, g, stream, x0, out, torch, dist, world):
@@ -479,6 +538,8 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=512,
+                    help="also time a prefill of this many tokens through the same layers (0: skip)")
     ap.add_argument("--engine", default="auto", choices=["auto", "layers", "stack"],
                     help="layers: per-layer kernels in a CUDA graph; stack: one persistent kernel for all layers "
                          "(T=1); auto: stack for unsharded T=1, else layers")

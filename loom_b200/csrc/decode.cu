@@ -645,6 +645,84 @@ bool decode_supported(const DecodeArgs &A) {
 
 // Router cluster shape for the TMA variant: 16 CTAs when the device can place
 // a 16-CTA cluster (non-portable size), else 8; 0 when the rows do not fit.
+// dotF32 (ggml.zig:198) of a router row and x, both in shared memory, dim a
+// multiple of 32 (the stack kernel's router_dot_smem, same order)
+__device__ __forceinline__ float router_dot_smem_(const float *wr, const float *x, int dim, int lane) {
+    float a = 0.0f;
+#pragma unroll 8
+    for (int i = lane; i < dim; i += 32) a = fadd(a, fmul(wr[i], x[i]));
+    const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
+    const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
+    const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
+    const float v = fadd(fadd(fadd(a, a8), a16), a24);
+    float r = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+    for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
+    return r;
+}
+
+// ---- batch router (T > 16 tokens): router GEMV tiled over experts x tokens,
+// then one block per token for route + activation quantization. The logits
+// are dotF32 (ggml.zig:198) in the same order as the decode router, and the
+// route is router_tail's, so every path routes identically.
+constexpr int RB_WARPS = 16, RB_TOK = 16;
+
+static int rb_experts(int dim) {  // router rows a CTA keeps in shared memory (<= RB_WARPS, ~190 KB)
+    int et = (int)((190 * 1024 - 2 * (size_t)dim * 4) / ((size_t)dim * 4));
+    return et < 1 ? 1 : et > RB_WARPS ? RB_WARPS : et;
+}
+
+__global__ void __launch_bounds__(RB_WARPS * 32) k_router_batch(DecodeArgs A, int et) {
+    extern __shared__ __align__(16) float rbs[];  // rows [et][dim] | x [2][dim]
+    pdl_wait();
+    pdl_trigger();
+    const int dim = A.dim, ne = A.n_expert;
+    const int e0 = blockIdx.x * et, t0 = blockIdx.y * RB_TOK;
+    const int ne_here = ne - e0 < et ? ne - e0 : et;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *rows = rbs, *xb = rbs + (size_t)et * dim;
+    for (int i = threadIdx.x; i < ne_here * dim / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(rows)[i] = __ldg(reinterpret_cast<const float4 *>(A.router + (size_t)e0 * dim) + i);
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(xb)[i] = __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)t0 * dim) + i);
+    __syncthreads();
+    for (int tt = 0; tt < RB_TOK && t0 + tt < A.T; tt++) {
+        const int t = t0 + tt;
+        float4 nx[4];  // the next token's x, in flight while this one is dotted
+        const bool more = tt + 1 < RB_TOK && t + 1 < A.T;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (more && i < dim / 4) nx[j] = __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)(t + 1) * dim) + i);
+        }
+        const float *xs = xb + (size_t)(tt & 1) * dim;
+        if (warp < ne_here) {
+            const float r = router_dot_smem_(rows + (size_t)warp * dim, xs, dim, lane);
+            if (lane == 0) A.logits[(size_t)t * ne + e0 + warp] = r;
+        }
+        if (more)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int i = threadIdx.x + j * blockDim.x;
+                if (i < dim / 4) reinterpret_cast<float4 *>(xb + (size_t)((tt + 1) & 1) * dim)[i] = nx[j];
+            }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(256) k_route_batch(DecodeArgs A) {
+    extern __shared__ float smx[];  // x[dim] | scores[ne] | choice[ne] | ids[64] | gates[64] | red
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x, dim = A.dim, ne = A.n_expert;
+    float *scores = smx + dim, *choice = scores + ne;
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(smx)[i] = __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)t * dim) + i);
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = __ldcg(A.logits + (size_t)t * ne + e);
+    __syncthreads();
+    router_tail(A, t, smx, scores, choice, 8);
+}
+
 static int tma_cluster(const DecodeArgs &A, size_t &smem) {
     static int c16 = -1, ok = 0;
     if (c16 < 0) {
@@ -677,6 +755,20 @@ static int tma_cluster(const DecodeArgs &A, size_t &smem) {
 }
 
 static cudaError_t launch_router(const DecodeArgs &A, cudaStream_t st) {
+    if (A.router && A.T > 16 && A.dim % 32 == 0 && A.dim <= 8192 && !A.trace_reg) {  // batch router
+        const int et = rb_experts(A.dim);
+        const size_t smem = ((size_t)et + 2) * A.dim * 4;
+        cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        if ((e = launch_pdl(k_router_batch, dim3(cdivu(A.n_expert, et), cdivu(A.T, RB_TOK)), dim3(RB_WARPS * 32), smem,
+                            st, A, et)) != cudaSuccess)
+            return e;
+        const size_t rs = (size_t)(A.dim + 2 * A.n_expert + 136) * 4;
+        if (rs > 48 * 1024 &&
+            (e = cudaFuncSetAttribute(k_route_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rs)) != cudaSuccess)
+            return e;
+        return launch_pdl(k_route_batch, dim3(A.T), dim3(256), rs, st, A);
+    }
     size_t smem = 0;
     const int tc = (A.router && !A.trace_reg) ? tma_cluster(A, smem) : 0;
     if (!tc) smem = (size_t)(A.dim + 2 * A.n_expert + 136) * 4;
