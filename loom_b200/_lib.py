@@ -99,7 +99,6 @@ def lib() -> C.CDLL:
         "loom_cuda_stack_free": (i, [u64]),
         "loom_cuda_stack_trace": (i, [u64, i, vp, sz]),
         "loom_cuda_umma_selftest": (i, [vp, vp, vp, i, i, i]),
-        "loom_cuda_mma_profile": (i, [vp]),
         "loom_cuda_ep_unique_id": (i, [vp, sz]),
         "loom_cuda_ep_init": (i, [i, i, vp, sz]),
         "loom_cuda_ep_shutdown": (None, []),

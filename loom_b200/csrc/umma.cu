@@ -6,6 +6,7 @@
 #include <string>
 
 #include "umma.cuh"
+#include "warpdot.cuh"
 
 namespace loom {
 
@@ -85,7 +86,6 @@ __global__ void __launch_bounds__(128) k_umma_selftest(const uint16_t *A, const 
 using namespace loom;
 
 extern "C" int loom_cuda_umma_selftest(const uint16_t *A, const uint16_t *B, float *D, int M, int N, int K);
-extern "C" int loom_cuda_mma_profile(unsigned long long *out16);
 
 // Diagnostic entry (no counterpart in the reference): runs the bf16 tcgen05
 // GEMM on host arrays; returns 0, 1 on bad arguments, 2 on a CUDA error, 3 if
@@ -204,23 +204,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N) {
 constexpr int MMA_THREADS = 512;  // 16 warps: TMEM row quarter = warp % 4, token group = warp / 4
 constexpr int MMA_NP = 64;        // tokens per pass (the MMA's N)
 
-// Diagnostic: cycles spent by thread 0 of every CTA in the sections of the
-// MMA kernels, summed over CTAs ([kernel 0 = gate/up, 1 = down][section]);
-// read and cleared by loom_cuda_mma_profile.
-__device__ unsigned long long g_mma_cyc[2][8];
-
-struct MmaProf {
-    long long t;
-    int k;
-    __device__ __forceinline__ void mark(int sec) {
-        if (threadIdx.x == 0) {
-            const long long n = clock64();
-            atomicAdd(&g_mma_cyc[k][sec], (unsigned long long)(n - t));
-            t = n;
-        }
-    }
-};
-
 struct MmaCtl {
     uint64_t mbar[2];
     uint32_t tmem;
@@ -275,7 +258,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
     __shared__ float s_d[2][2][128], s_dmin[2][2][128];
     __shared__ uint32_t s_mn[2][2][128][2];
     __shared__ float s_xd[2][MMA_NP];
-    __shared__ int s_bs[2][MMA_NP][8];
+    __shared__ uint4 s_bsp[2][MMA_NP];  // per token: per-32 sums of the block as low bytes | signed high bytes
     __shared__ const int8_t *s_tok[MMA_NP];
     umma_pdl_wait();
     const int e = blockIdx.y;
@@ -322,7 +305,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
             const int it = t + u * MMA_THREADS;
             if (it < N * 16 && (it >> 4) < nc) px[u] = *reinterpret_cast<const uint2 *>(s_tok[it >> 4] + (it & 15) * 8);
         }
-        MmaProf pf{clock64(), 0};
         for (int ks = 0; ks <= KSTEPS; ks++) {
             if (ks < KSTEPS) {  // ---- stage step ks into buffer gstep & 1 (its previous MMAs were awaited below)
                 const int b = gstep & 1, blk = ks >> 1, h = ks & 1, pb = blk & 1;
@@ -364,7 +346,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                             *reinterpret_cast<uint4 *>(tile + ((size_t)kc * 128 + r) * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                pf.mark(0);  // weights
 #pragma unroll
                 for (int u = 0; u < 2; u++) {  // tokens (prefetched one step ahead): int8 activations -> fp16
                     const int it = t + u * MMA_THREADS;
@@ -377,20 +358,24 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                     }
                 }
                 if (h == 0)
-                    for (int it = t; it < nc * 9; it += MMA_THREADS) {  // tokens' xd and per-32 sums of block blk
-                        const int i = it / 9, k = it % 9;
-                        const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
-                        const int tok = shared ? c0 + i : slot / A.n_used;
-                        if (k == 8) s_xd[pb][i] = A.x256.d[(size_t)tok * NBG + blk];
-                        else {
-                            const int32_t *ss = A.x256.s + ((size_t)tok * NBG + blk) * 16 + 2 * k;
-                            s_bs[pb][i][k] = ss[0] + ss[1];
+                    for (int i = t; i < nc; i += MMA_THREADS) {  // tokens' xd and per-32 sums of block blk
+                        const int tok = (int)((s_tok[i] - A.x256.q) / dim);
+                        s_xd[pb][i] = A.x256.d[(size_t)tok * NBG + blk];
+                        const int4 *ss = reinterpret_cast<const int4 *>(A.x256.s + ((size_t)tok * NBG + blk) * 16);
+                        uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; k4++) {  // per-32 sum bs = 256*hi + lo (lo unsigned byte, hi signed)
+                            const int4 v = ss[k4];
+                            const int b0 = v.x + v.y, b1 = v.z + v.w, k = 2 * k4;
+                            lo[k >> 2] |= (uint32_t)(b0 & 0xFF) << (8 * (k & 3));
+                            hi[k >> 2] |= (uint32_t)((b0 >> 8) & 0xFF) << (8 * (k & 3));
+                            lo[(k + 1) >> 2] |= (uint32_t)(b1 & 0xFF) << (8 * ((k + 1) & 3));
+                            hi[(k + 1) >> 2] |= (uint32_t)((b1 >> 8) & 0xFF) << (8 * ((k + 1) & 3));
                         }
+                        s_bsp[pb][i] = make_uint4(lo[0], lo[1], hi[0], hi[1]);
                     }
-                pf.mark(1);  // tokens
                 fence_async_smem();
                 __syncthreads();
-                pf.mark(2);  // barrier
                 if (t == 0) {
                     tc_fence_after();
                     const uint32_t dcol = (uint32_t)b * 2 * MMA_NP;
@@ -405,14 +390,12 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                     }
                     umma_commit(&S.mbar[b]);
                 }
-                pf.mark(3);  // issue
                 gstep++;
             }
             if (ks >= 1) {  // ---- epilogue of step ks - 1 (its MMAs done), overlapping step ks's MMAs
                 const uint32_t ps = gstep - (ks < KSTEPS ? 2 : 1);  // the step to finish
                 const int pbuf = ps & 1;
                 if (!mma_wait(S, pbuf, (ps >> 1) & 1, A.err)) break;
-                pf.mark(4);  // MMA wait
                 tc_fence_after();
                 const int pks = (int)(ps - step0), pblk = pks >> 1, ph = pks & 1, pb = pblk & 1;
                 if (tok0 < N) {
@@ -435,13 +418,12 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                         for (int i = 0; i < 16; i++) {
                             const int ti = tok0 + i;
                             if (ti < nc) {
-                                int Mg = 0, Mu = 0;
-#pragma unroll
-                                for (int sb = 0; sb < 8; sb++) {
-                                    const int bs = s_bs[pb][ti][sb];
-                                    Mg += (int)(((sb < 4 ? mg0 : mg1) >> (8 * (sb & 3))) & 0xFF) * bs;
-                                    Mu += (int)(((sb < 4 ? mu0 : mu1) >> (8 * (sb & 3))) & 0xFF) * bs;
-                                }
+                                // mins term M = sum_sub mn * bs through dp4a on bs = 256*hi + lo (exact)
+                                const uint4 bp = s_bsp[pb][ti];
+                                const int Mg = (int)__dp4a(mg0, bp.x, __dp4a(mg1, bp.y, 0u)) +
+                                               256 * dp4a_us(mg0, (int)bp.z, dp4a_us(mg1, (int)bp.w, 0));
+                                const int Mu = (int)__dp4a(mu0, bp.x, __dp4a(mu1, bp.y, 0u)) +
+                                               256 * dp4a_us(mu0, (int)bp.z, dp4a_us(mu1, (int)bp.w, 0));
                                 const float xd = s_xd[pb][ti];
                                 ag[i] = fadd(ag[i], fmul(xd, fsub(fmul(dg, (float)Ig[i]), fmul(dmg, (float)Mg))));
                                 au[i] = fadd(au[i], fmul(xd, fsub(fmul(du, (float)Iu[i]), fmul(dmu, (float)Mu))));
@@ -450,7 +432,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
                     }
                 }
                 tc_fence_before();
-                pf.mark(5);  // epilogue
             }
         }
         if (!S.ok) break;
@@ -472,122 +453,142 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_gu_mma(DecodeArgs A) {
     if (warp == 0) tmem_free(tmem, ncols);
 }
 
-// raw Q6_K words thread t needs at down step ks: its group's 32 ql bytes, the
-// half's 32 qh bytes, its two scales, and the block's d
-template <int NBD>
-__device__ __forceinline__ void dn_fetch_t(uint4 (&pq)[4], uint32_t &scw, float &d, const WDev &wd, uint64_t plane,
-                                           int row0, int dim, int ks, int t) {
-    const int g = t >> 7, r = t & 127, row = row0 + r, h = ks & 1;
-    if (row >= dim) return;
-    const uint64_t gb = plane + (uint64_t)row * NBD + (ks >> 1);
-    const uint8_t *qb = wd.q + gb * 192;
-    pq[0] = ld_stream_v4(qb + 64 * h + 32 * (g & 1));
-    pq[1] = ld_stream_v4(qb + 64 * h + 32 * (g & 1) + 16);
-    pq[2] = ld_stream_v4(qb + 128 + 32 * h);
-    pq[3] = ld_stream_v4(qb + 128 + 32 * h + 16);
-    const uint16_t s2 = *reinterpret_cast<const uint16_t *>(wd.sc + gb * 16 + 8 * h + 2 * g);
-    scw = s2;
-    d = f16_to_f32(wd.d[gb]);
+constexpr int GU_NP = 32;  // tokens per pass of the pipelined down kernel
+
+__device__ __forceinline__ bool mbar_wait_err(uint64_t *bar, uint32_t parity, int *ok, int *err) {
+    if (!*reinterpret_cast<volatile int *>(ok)) return false;
+    if (mbar_wait(bar, parity, UMMA_POLLS)) return true;
+    if (err) atomicOr(err, 32);
+    *reinterpret_cast<volatile int *>(ok) = 0;
+    return false;
 }
-#define dn_fetch dn_fetch_t<NBD>
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 // ---- down (Q6_K): y[slot][row] = W_down[row] . act[slot] ------------------------------------
 // act quantized per slot by quantizeX256 (aq / ad); expert blockIdx.y, output
-// rows [128*blockIdx.x, +128).
+// rows [128*blockIdx.x, +128). The same two-group pipeline as k_gu_mma. A
+// fill thread takes row tf & 127 and the value groups gp and gp + 2 of the
+// half super-block (gp = tf >> 7), which share their ql bytes (low and high
+// nibbles): A = sc * (q - 32).
+template <int NBD>
+__device__ __forceinline__ void dn_fetch_w(uint4 (&pq)[4], uint32_t &scw, float &d, const WDev &wd, uint64_t plane,
+                                           int row0, int dim, int ks, int tf) {
+    const int r = tf & 127, gp = tf >> 7, row = row0 + r, h = ks & 1;
+    if (row >= dim) return;
+    const uint64_t gb = plane + (uint64_t)row * NBD + (ks >> 1);
+    const uint8_t *qb = wd.q + gb * 192;
+    pq[0] = ld_stream_v4(qb + 64 * h + 32 * gp);
+    pq[1] = ld_stream_v4(qb + 64 * h + 32 * gp + 16);
+    pq[2] = ld_stream_v4(qb + 128 + 32 * h);
+    pq[3] = ld_stream_v4(qb + 128 + 32 * h + 16);
+    const uint8_t *scb = wd.sc + gb * 16 + 8 * h;  // groups g: scales scb[2g] (l < 16), scb[2g + 1]
+    scw = (uint32_t)scb[2 * gp] | ((uint32_t)scb[2 * gp + 1] << 8) | ((uint32_t)scb[2 * gp + 4] << 16) |
+          ((uint32_t)scb[2 * gp + 5] << 24);
+    d = f16_to_f32(wd.d[gb]);
+}
+
 template <int NBD>
 __global__ void __launch_bounds__(MMA_THREADS, 1) k_dn_mma(DecodeArgs A) {
     constexpr int KSTEPS = NBD * 2;
-    constexpr size_t A_BYTES = (size_t)16 * 128 * 16, B_BYTES = (size_t)16 * MMA_NP * 16;
+    constexpr size_t A_BYTES = (size_t)16 * 128 * 16, B_BYTES = (size_t)16 * GU_NP * 16;
     extern __shared__ __align__(128) uint8_t sm[];
-    __shared__ MmaCtl S;
-    __shared__ float s_d[2][128], s_xd[2][MMA_NP];
-    __shared__ const int8_t *s_act[MMA_NP];
+    __shared__ __align__(8) uint64_t full[2], done[2], sfree[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_ok;
+    __shared__ float s_d[2][128], s_xd[2][GU_NP];
+    __shared__ const int8_t *s_act[GU_NP];
     umma_pdl_wait();
     const int e = blockIdx.y;
     const bool shared = e == A.n_local;
     const int n = shared ? A.T : A.grp_cnt[e];
     const int row0 = blockIdx.x * 128;
     if (n == 0 || row0 >= A.dim) return;
-    const int t = threadIdx.x, warp = t >> 5, lane = t & 31, q = warp & 3, tg = warp >> 2;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const bool fillg = warp < 8;
     const int *list = shared ? nullptr : A.grp_list + A.grp_off[e];
     const WDev wd = shared ? A.sdn : A.dn;
     const uint64_t plane = shared ? 0 : (uint64_t)e * A.dim * NBD;
     const int stride = A.act_stride;
-    const uint32_t ncols = 2 * MMA_NP;
-    if (warp == 0) tmem_alloc(&S.tmem, ncols);
+    const uint32_t ncols = 2 * GU_NP;
+    if (warp == 0) tmem_alloc(&s_tmem, ncols);
     if (t == 0) {
-        mbar_init(&S.mbar[0], 1);
-        mbar_init(&S.mbar[1], 1);
-        S.ok = 1;
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&done[i], 1);
+            mbar_init(&sfree[i], 1);
+        }
+        s_ok = 1;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = S.tmem;
-    uint32_t gstep = 0;
-    for (int c0 = 0; c0 < n && S.ok; c0 += MMA_NP) {
-        const int nc = n - c0 < MMA_NP ? n - c0 : MMA_NP, N = (nc + 15) / 16 * 16;
+    const uint32_t tmem = s_tmem;
+    uint32_t g0 = 0;
+    for (int c0 = 0; c0 < n; c0 += GU_NP) {
+        const int nc = n - c0 < GU_NP ? n - c0 : GU_NP, N = (nc + 15) / 16 * 16;
         const uint32_t idesc = umma_idesc_f16_f32(128, N);
-        const int tok0 = 16 * tg;
-        int I[16];
-        float acc[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) acc[i] = 0.0f;
-        const uint32_t step0 = gstep;
-        for (int i = t; i < nc; i += MMA_THREADS) {  // this pass's slots' int8 activations
+        for (int i = t; i < nc; i += MMA_THREADS) {
             const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
             s_act[i] = A.aq + (size_t)slot * stride;
         }
         __syncthreads();
-        uint4 pq[4];  // next step's raw words: ql (32 B) and qh (32 B) of this thread's group
-        uint32_t pscw = 0;
-        float pd = 0.0f;
-        dn_fetch(pq, pscw, pd, wd, plane, row0, A.dim, 0, t);
-        uint2 px[2];
+        if (fillg) {
+            const int tf = t, r = tf & 127, gp = tf >> 7, row = row0 + r;
+            uint4 pq[4];
+            uint32_t pscw = 0;
+            float pd = 0.0f;
+            dn_fetch_w<NBD>(pq, pscw, pd, wd, plane, row0, A.dim, 0, tf);
+            uint2 px[2];
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int it = t + u * MMA_THREADS;
-            if (it < N * 16 && (it >> 4) < nc) px[u] = *reinterpret_cast<const uint2 *>(s_act[it >> 4] + (it & 15) * 8);
-        }
-        for (int ks = 0; ks <= KSTEPS; ks++) {
-            if (ks < KSTEPS) {
-                const int b = gstep & 1, blk = ks >> 1, h = ks & 1, pb = blk & 1;
+            for (int u = 0; u < 2; u++) {
+                const int it = tf + u * 256;
+                if (it < N * 16 && (it >> 4) < nc) px[u] = *reinterpret_cast<const uint2 *>(s_act[it >> 4] + (it & 15) * 8);
+            }
+            const __half2 k1056 = u2h(0x64206420u);  // 1056 = 1024 + 32
+            for (int ks = 0; ks < KSTEPS; ks++) {
+                const uint32_t g = g0 + ks;
+                const int b = g & 1, blk = ks >> 1, h = ks & 1, pb = blk & 1;
+                if (g >= 2 && tf == 0) mbar_wait_err(&sfree[b], ((g >> 1) - 1) & 1, &s_ok, A.err);
+                named_sync(1, 256);
                 uint8_t *tA = sm + (size_t)b * (A_BYTES + B_BYTES), *tB = tA + A_BYTES;
-                {   // weights (prefetched one step ahead): thread -> (row, group g of the half):
-                    // values 32g + l, l < 32 -> chunks 4g .. 4g+3
-                    const int g = t >> 7, r = t & 127, row = row0 + r;
-                    const uint4 ql0 = pq[0], ql1 = pq[1], qh0 = pq[2], qh1 = pq[3];
-                    const uint32_t scw = pscw;
-                    const float dcur = pd;
-                    if (ks + 1 < KSTEPS) dn_fetch(pq, pscw, pd, wd, plane, row0, A.dim, ks + 1, t);
-                    if (row < A.dim) {
-                        const int s0 = (int)(int8_t)(scw & 0xFF), s1 = (int)(int8_t)((scw >> 8) & 0xFF);
-                        const __half2 k1056 = u2h(0x64206420u);  // 1056 = 1024 + 32
-                        const uint32_t qlw[8] = {ql0.x, ql0.y, ql0.z, ql0.w, ql1.x, ql1.y, ql1.z, ql1.w};
-                        const uint32_t qhw[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+                const uint4 ql0 = pq[0], ql1 = pq[1], qh0 = pq[2], qh1 = pq[3];
+                const uint32_t scw = pscw;
+                const float dcur = pd;
+                if (ks + 1 < KSTEPS) dn_fetch_w<NBD>(pq, pscw, pd, wd, plane, row0, A.dim, ks + 1, tf);
+                if (row < A.dim) {
+                    const uint32_t qlw[8] = {ql0.x, ql0.y, ql0.z, ql0.w, ql1.x, ql1.y, ql1.z, ql1.w};
+                    const uint32_t qhw[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+#pragma unroll
+                    for (int gi = 0; gi < 2; gi++) {  // group g = gp + 2 gi: low (gi 0) or high (gi 1) nibbles
+                        const int gg = gp + 2 * gi;
 #pragma unroll
                         for (int c = 0; c < 4; c++) {
-                            const __half2 sc2 = __half2half2(__int2half_rn(c < 2 ? s0 : s1));
+                            const int sc = (int)(int8_t)((scw >> (16 * gi + 8 * (c >> 1))) & 0xFF);
+                            const __half2 sc2 = __half2half2(__int2half_rn(sc));
                             uint32_t o[4];
 #pragma unroll
-                            for (int wi = 0; wi < 2; wi++) {  // 4 values per word: q = low/high nibble | 2 qh bits << 4
+                            for (int wi = 0; wi < 2; wi++) {
                                 const uint32_t lw = qlw[2 * c + wi], hw = qhw[2 * c + wi];
-                                const uint32_t lo4 = (g >= 2 ? lw >> 4 : lw) & 0x0F0F0F0Fu;
-                                const uint32_t qb = lo4 | (((hw >> (2 * g)) & 0x03030303u) << 4);
+                                const uint32_t lo4 = (gi ? lw >> 4 : lw) & 0x0F0F0F0Fu;
+                                const uint32_t qb = lo4 | (((hw >> (2 * gg)) & 0x03030303u) << 4);
                                 o[2 * wi] = h2u(__hmul2(__hsub2(u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), sc2));
                                 o[2 * wi + 1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), sc2));
                             }
-                            *reinterpret_cast<uint4 *>(tA + ((size_t)(4 * g + c) * 128 + r) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<uint4 *>(tA + ((size_t)(4 * gg + c) * 128 + r) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
                         }
-                        if (h == 0 && g == 0) s_d[pb][r] = dcur;
-                    } else {
-                        for (int kc = 4 * g; kc < 4 * g + 4; kc++)
-                            *reinterpret_cast<uint4 *>(tA + ((size_t)kc * 128 + r) * 16) = make_uint4(0, 0, 0, 0);
                     }
+                    if (h == 0 && gp == 0) s_d[pb][r] = dcur;
+                } else {
+                    for (int gi = 0; gi < 2; gi++)
+                        for (int c = 0; c < 4; c++)
+                            *reinterpret_cast<uint4 *>(tA + ((size_t)(4 * (gp + 2 * gi) + c) * 128 + r) * 16) = make_uint4(0, 0, 0, 0);
                 }
 #pragma unroll
                 for (int u = 0; u < 2; u++) {  // activations (prefetched one step ahead): int8 -> fp16
-                    const int it = t + u * MMA_THREADS;
+                    const int it = tf + u * 256;
                     if (it < N * 16) {
                         const int i = it >> 4, kc = it & 15;
                         *reinterpret_cast<uint4 *>(tB + ((size_t)kc * N + i) * 16) =
@@ -597,56 +598,72 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_dn_mma(DecodeArgs A) {
                     }
                 }
                 if (h == 0)
-                    for (int i = t; i < nc; i += MMA_THREADS) {
-                        const int slot = shared ? A.T * A.n_used + c0 + i : list[c0 + i];
-                        s_xd[pb][i] = A.ad[(size_t)slot * (stride / 32) + blk];
+                    for (int i = tf; i < nc; i += 256) {
+                        const size_t slot = (size_t)(s_act[i] - A.aq) / stride;
+                        s_xd[pb][i] = A.ad[slot * (stride / 32) + blk];
                     }
                 fence_async_smem();
-                __syncthreads();
-                if (t == 0) {
-                    tc_fence_after();
-                    const uint32_t dcol = (uint32_t)b * MMA_NP;
-                    const uint64_t ad = umma_desc_kmajor(tA, 128), bd = umma_desc_kmajor(tB, (uint32_t)N);
-#pragma unroll
-                    for (int s = 0; s < 8; s++)
-                        umma_bf16(tmem + dcol, ad + (uint64_t)(256 * s), bd + (uint64_t)(2 * s * N), idesc, s > 0);
-                    umma_commit(&S.mbar[b]);
-                }
-                gstep++;
+                named_sync(1, 256);
+                if (tf == 0) mbar_arrive(&full[b]);
             }
-            if (ks >= 1) {
-                const uint32_t ps = gstep - (ks < KSTEPS ? 2 : 1);
-                const int pbuf = ps & 1;
-                if (!mma_wait(S, pbuf, (ps >> 1) & 1, A.err)) break;
+        } else {
+            const int we = warp - 8, q = we & 3, tok0 = 16 * (we >> 2);
+            const bool lead = t == 256;
+            int I[16];
+            float acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+            auto issue = [&](uint32_t g) {
+                const int b = g & 1;
+                if (!mbar_wait_err(&full[b], (g >> 1) & 1, &s_ok, A.err)) return;
                 tc_fence_after();
-                const int pks = (int)(ps - step0), pblk = pks >> 1, ph = pks & 1, pb = pblk & 1;
+                uint8_t *tA = sm + (size_t)b * (A_BYTES + B_BYTES), *tB = tA + A_BYTES;
+                const uint64_t ad = umma_desc_kmajor(tA, 128), bd = umma_desc_kmajor(tB, (uint32_t)N);
+#pragma unroll
+                for (int s2 = 0; s2 < 8; s2++)
+                    umma_bf16(tmem + (uint32_t)b * GU_NP, ad + (uint64_t)(256 * s2), bd + (uint64_t)(2 * s2 * N), idesc,
+                              s2 > 0);
+                umma_commit(&done[b]);
+            };
+            if (lead) issue(g0);
+            for (int ks = 0; ks < KSTEPS; ks++) {
+                const uint32_t g = g0 + ks;
+                const int b = g & 1, blk = ks >> 1, h = ks & 1, pb = blk & 1;
+                if (lead) {
+                    if (ks + 1 < KSTEPS) issue(g + 1);
+                    if (mbar_wait_err(&done[b], (g >> 1) & 1, &s_ok, A.err)) mbar_arrive(&sfree[b]);
+                }
+                named_sync(2, 256);
+                tc_fence_after();
                 if (tok0 < N) {
                     int v[16];
-                    tmem_ints16(tmem, q, (uint32_t)pbuf * MMA_NP + (uint32_t)tok0, v);
+                    tmem_ints16(tmem, q, (uint32_t)b * GU_NP + (uint32_t)tok0, v);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) I[i] = ph ? I[i] + v[i] : v[i];
-                    if (ph == 1) {
-                        const float d = s_d[pb][32 * q + lane];
-#pragma unroll
-                        for (int i = 0; i < 16; i++)
-                            if (tok0 + i < nc) acc[i] = fadd(acc[i], fmul(fmul(s_xd[pb][tok0 + i], d), (float)I[i]));
-                    }
+                    for (int i = 0; i < 16; i++) I[i] = h ? I[i] + v[i] : v[i];
                 }
                 tc_fence_before();
+                named_sync(2, 256);
+                if (h == 1 && tok0 < N) {
+                    const float d = s_d[pb][32 * q + lane];
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        if (tok0 + i < nc) acc[i] = fadd(acc[i], fmul(fmul(s_xd[pb][tok0 + i], d), (float)I[i]));
+                }
+            }
+            if (s_ok && tok0 < nc) {
+                const int row = row0 + 32 * q + lane;
+                if (row < A.dim)
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        if (tok0 + i >= nc) break;
+                        const int slot = shared ? A.T * A.n_used + c0 + tok0 + i : list[c0 + tok0 + i];
+                        A.y[(size_t)slot * A.dim + row] = acc[i];
+                    }
             }
         }
-        if (!S.ok) break;
-        if (tok0 < nc) {
-            const int row = row0 + 32 * q + lane;
-            if (row < A.dim)
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    if (tok0 + i >= nc) break;
-                    const int slot = shared ? A.T * A.n_used + c0 + tok0 + i : list[c0 + tok0 + i];
-                    A.y[(size_t)slot * A.dim + row] = acc[i];
-                }
-        }
+        g0 += KSTEPS;
         __syncthreads();
+        if (!s_ok) break;
     }
     tc_fence_before();
     __syncthreads();
@@ -676,7 +693,7 @@ static MmaFn dn_mma_fn(int nbd) {
 }
 
 static constexpr size_t GU_MMA_SMEM = (size_t)2 * ((size_t)2 * 16 * 128 * 16 + (size_t)16 * MMA_NP * 16);
-static constexpr size_t DN_MMA_SMEM = (size_t)2 * ((size_t)16 * 128 * 16 + (size_t)16 * MMA_NP * 16);
+static constexpr size_t DN_MMA_SMEM = (size_t)2 * ((size_t)16 * 128 * 16 + (size_t)16 * GU_NP * 16);
 
 bool moe_mma_supported(const DecodeArgs &A) {
     if (A.g.type != T_Q4_K || A.u.type != T_Q4_K || A.dn.type != T_Q6_K) return false;
@@ -706,14 +723,3 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
 }
 
 }  // namespace loom
-
-// Diagnostic entry (no counterpart in the reference): copies the MMA kernels'
-// section cycle sums (2 x 8: gate/up then down; sections weights, tokens,
-// barrier, issue, MMA wait, epilogue) into out16 and clears them.
-int loom_cuda_mma_profile(unsigned long long *out16) {
-    if (cudaDeviceSynchronize() != cudaSuccess) return 2;
-    if (cudaMemcpyFromSymbol(out16, loom::g_mma_cyc, sizeof(unsigned long long) * 16) != cudaSuccess) return 2;
-    unsigned long long z[16] = {};
-    if (cudaMemcpyToSymbol(loom::g_mma_cyc, z, sizeof z) != cudaSuccess) return 2;
-    return 0;
-}
