@@ -167,6 +167,12 @@ typedef struct {
     /* optional hint: the next layer's router (f32 [n_expert][dim]); its weights
      * are prefetched into L2 while this layer's experts stream */
     loom_tensor next_router;
+    /* DeepSeek-V3 group-limited routing (no counterpart in the reference):
+     * the experts form n_group groups of n_expert / n_group consecutive ids,
+     * only the topk_group groups with the largest sum of their two best
+     * biased scores are eligible for the top-n_used. n_group 0 or 1 = plain
+     * moe.zig:106 route. */
+    size_t n_group, topk_group;
 } loom_moe_desc;
 
 /* d_x: device f32 [T][dim]; d_out: device f32 [T][dim] (d_out = d_residual +

@@ -41,7 +41,7 @@ class MoeDesc(C.Structure):  # loom_moe_desc
                 ("gate", C.c_uint64), ("up", C.c_uint64), ("down", C.c_uint64),
                 ("shexp_gate", C.c_uint64), ("shexp_up", C.c_uint64), ("shexp_down", C.c_uint64),
                 ("shexp_ffn", C.c_size_t), ("expert0", C.c_size_t), ("n_local", C.c_size_t),
-                ("next_router", C.c_uint64)]
+                ("next_router", C.c_uint64), ("n_group", C.c_size_t), ("topk_group", C.c_size_t)]
 
 
 def header_symbols() -> list[str]:

@@ -143,7 +143,7 @@ __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const fl
     float *red = choice + ne + 128;
     if (threadIdx.x < ROUTE_THREADS) {
         route_block(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
-                    red, A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used);
+                    red, A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, A.n_group, A.topk_group);
         if (A.ids_out)
             for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS)
                 A.ids_out[(size_t)t * A.n_used + k] = sid[k];

@@ -16,6 +16,7 @@ struct DecodeArgs {
     int T, dim, ffn, n_expert, n_used;
     int gating, weights_norm;
     float weights_scale;
+    int n_group, topk_group; // group-limited selection (1, 1: plain top-k)
     int expert0, n_local;
     const float *router;     // f32 [n_expert][dim], or null when logits_in is given
     const float *bias;       // selection bias [n_expert] or null

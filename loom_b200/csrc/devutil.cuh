@@ -145,6 +145,48 @@ static __device__ __noinline__ void route_scan_serial(int ne, int nk, const floa
     }
 }
 
+// DeepSeek-V3's group-limited selection by one warp (no counterpart in the
+// reference; restated from the published routing): ne experts in n_group
+// (<= 32) groups of ne / n_group consecutive ids; lane g scores group g as the
+// sum of its two largest choices (its one choice when a group holds one
+// expert); the topk_group best groups are kept by a serial first-max scan
+// (lowest group index on ties), every lane running the same scan over the
+// shuffled scores; choices outside the kept groups become -inf.
+static __device__ __noinline__ void route_group_mask(float *choice, int ne, int n_group, int topk_group, int lane) {
+    const int gs = ne / n_group;
+    float gsc = -INFINITY;
+    if (lane < n_group) {
+        float top1 = -INFINITY, top2 = -INFINITY;
+        for (int e = lane * gs; e < (lane + 1) * gs; e++) {
+            const float c = choice[e];
+            if (c > top1) {
+                top2 = top1;
+                top1 = c;
+            } else if (c > top2) {
+                top2 = c;
+            }
+        }
+        gsc = gs == 1 ? top1 : fadd(top1, top2);
+    }
+    uint32_t keep = 0;
+    for (int k = 0; k < topk_group; k++) {
+        int best = -1;
+        float bv = -INFINITY;
+        for (int g = 0; g < n_group; g++) {
+            const float v = __shfl_sync(0xffffffffu, gsc, g);
+            if (!(keep >> g & 1u) && (best < 0 || v > bv)) {
+                best = g;
+                bv = v;
+            }
+        }
+        keep |= 1u << best;
+    }
+    __syncwarp();
+    for (int e = lane; e < ne; e += 32)
+        if (!(keep >> (e / gs) & 1u)) choice[e] = -INFINITY;
+    __syncwarp();
+}
+
 __device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int gating, int weights_norm,
                                              float weights_scale, const float *scores, float *choice, int *ids,
                                              float *gates, int *ids_out, float *gates_out, int lane) {
@@ -321,7 +363,8 @@ __device__ __forceinline__ void route_bar() { asm volatile("bar.sync 1, 128;" ::
 
 __device__ __forceinline__ void route_block(const float *logits, const float *bias, int ne, int nk, int gating,
                                             int weights_norm, float weights_scale, float *scores, float *choice,
-                                            int *ids, float *gates, float *red, int *ids_out, float *gates_out) {
+                                            int *ids, float *gates, float *red, int *ids_out, float *gates_out,
+                                            int n_group = 1, int topk_group = 1) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = ROUTE_THREADS / 32;
     if (gating == 2) {
@@ -359,6 +402,11 @@ __device__ __forceinline__ void route_block(const float *logits, const float *bi
         const float c = bias ? fadd(scores[e], bias[e]) : scores[e];
         choice[e] = c;
         fin &= c > -INFINITY;
+    }
+    if (n_group > 1 && topk_group < n_group) {  // masked experts are -inf: the serial scan picks
+        route_bar();
+        if (warp == 0) route_group_mask(choice, ne, n_group, topk_group, lane);
+        fin = false;
     }
     fin = __all_sync(0xffffffffu, fin);
     route_bar();  // red[] free again, choice complete

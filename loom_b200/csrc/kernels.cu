@@ -342,7 +342,7 @@ void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok
 
 __global__ void __launch_bounds__(ROUTE_THREADS) k_route(const float *logits, const float *bias, int ne, int nk,
                                                          int gating, int weights_norm, float weights_scale, int *ids,
-                                                         float *gates) {
+                                                         float *gates, int n_group, int topk_group) {
     extern __shared__ float sm[];  // scores[ne] | choice[ne] | ids[64] | gates[64] | red[8]
     const int t = blockIdx.x;
     float *choice = sm + ne;
@@ -350,14 +350,14 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(const float *logits, co
     __syncthreads();
     route_block(choice, bias, ne, nk, gating, weights_norm, weights_scale, sm, choice,
                 reinterpret_cast<int *>(sm + 2 * ne), sm + 2 * ne + 64, sm + 2 * ne + 128, ids + (size_t)t * nk,
-                gates + (size_t)t * nk);
+                gates + (size_t)t * nk, n_group, topk_group);
 }
 
 void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating, int weights_norm,
-                  float weights_scale, int *ids, float *gates, cudaStream_t st) {
+                  float weights_scale, int *ids, float *gates, cudaStream_t st, int n_group, int topk_group) {
     if (T == 0) return;
-    k_route<<<T, ROUTE_THREADS, (2 * n_expert + 136) * sizeof(float), st>>>(logits, bias, n_expert, n_used, gating,
-                                                                            weights_norm, weights_scale, ids, gates);
+    k_route<<<T, ROUTE_THREADS, (2 * n_expert + 136) * sizeof(float), st>>>(
+        logits, bias, n_expert, n_used, gating, weights_norm, weights_scale, ids, gates, n_group, topk_group);
     count_launch();
 }
 

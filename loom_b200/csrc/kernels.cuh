@@ -29,6 +29,7 @@ struct RoutedLayerDev {
     int gating;           // 1 softmax, 2 sigmoid, 3 softmax_topk
     int weights_norm;
     float weights_scale;
+    int n_group, topk_group;  // group-limited selection (1, 1: plain top-k)
     int has_shared;
     WDev sg, su, sdn;     // shared expert (gb offsets 0)
     int shexp_ffn;
@@ -47,7 +48,8 @@ void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x,
                cudaStream_t st);
 void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out, cudaStream_t st);
 void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating,
-                  int weights_norm, float weights_scale, int *ids, float *gates, cudaStream_t st);
+                  int weights_norm, float weights_scale, int *ids, float *gates, cudaStream_t st,
+                  int n_group = 1, int topk_group = 1);
 // Expert phase (gate/up + SwiGLU, activation quantization, down + weighted
 // combine) for a host-built slot array (one token) or for a routed layer whose
 // router already wrote ids/gates [T][n_used].

@@ -313,6 +313,18 @@ size_t g_next_router_bytes = 0;
 unsigned long long *g_trace = nullptr;
 size_t g_trace_cap = 0, g_trace_next = 0;  // test hook: route every layer through the slot kernels
 
+// Group-limited selection of a layer (DeepSeek-V3 routing): n_group 0 or 1 is
+// plain top-k; otherwise n_group <= 32 groups dividing n_expert, 1 <=
+// topk_group <= n_group, and n_used no more than the kept experts.
+int group_cfg(const loom_moe_desc &D, RoutedLayerDev &L) {
+    const size_t ng = D.n_group ? D.n_group : 1, tg = D.n_group > 1 ? D.topk_group : 1;
+    if (ng > 32 || D.n_expert % ng || tg == 0 || tg > ng || D.n_used > tg * (D.n_expert / ng))
+        return decline("expert groups out of range (n_group <= 32 dividing n_expert, 1 <= topk_group <= n_group)");
+    L.n_group = (int)ng;
+    L.topk_group = (int)tg;
+    return 0;
+}
+
 DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, const float *d_x,
                        const float *d_logits_in, const float *d_bias, float *d_out, const float *d_residual,
                        uint32_t *d_ids_out, size_t act_stride) {
@@ -325,6 +337,8 @@ DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, c
     A.gating = L.gating;
     A.weights_norm = L.weights_norm;
     A.weights_scale = L.weights_scale;
+    A.n_group = L.n_group;
+    A.topk_group = L.topk_group;
     A.expert0 = L.expert0;
     A.n_local = L.n_local;
     A.router = router;
@@ -400,7 +414,7 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
         d_logits = S.logits.as<float>();
     }
     launch_route(d_logits, d_bias, (int)T, L.n_expert, L.n_used, L.gating, L.weights_norm, L.weights_scale,
-                 S.ids.as<int>(), S.gates.as<float>(), st);
+                 S.ids.as<int>(), S.gates.as<float>(), st, L.n_group, L.topk_group);
     quantize_inputs(d_x, T, L.dim, any_type(L, true), any_type(L, false), st);
     launch_experts_routed(L, S.ids.as<int>(), S.gates.as<float>(), (int)T, (int)act_stride, make_xq(true, L.dim),
                           make_xq(false, L.dim), S.act.as<float>(), S.aq.as<int8_t>(), S.ad.as<float>(),
@@ -755,6 +769,7 @@ int loom_cuda_moe_ffn_routed(const float *normed, size_t dim, const float *logit
     L.gating = cfg.gating_sigmoid ? 2 : 1;
     L.weights_norm = cfg.weights_norm;
     L.weights_scale = cfg.weights_scale;
+    L.n_group = L.topk_group = 1;
     L.expert0 = 0;
     L.n_local = (int)cfg.n_expert;
     const size_t in_b = (dim + 2 * cfg.n_expert) * 4;
@@ -898,6 +913,7 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
     L.gating = D.gating ? D.gating : 1;
     L.weights_norm = D.weights_norm;
     L.weights_scale = D.weights_scale;
+    if (int rc = group_cfg(D, L)) return rc;
     L.expert0 = (int)D.expert0;
     L.n_local = (int)n_local;
     const float *bias = nullptr;
@@ -1033,6 +1049,7 @@ extern "C" int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const fl
     L.gating = D.gating ? D.gating : 1;
     L.weights_norm = D.weights_norm;
     L.weights_scale = D.weights_scale;
+    if (int rc = group_cfg(D, L)) return rc;
     L.expert0 = (int)D.expert0;
     L.n_local = (int)n_local;
     const float *bias = nullptr;
@@ -1056,6 +1073,8 @@ extern "C" int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const fl
     A.gating = L.gating;
     A.weights_norm = L.weights_norm;
     A.weights_scale = L.weights_scale;
+    A.n_group = L.n_group;
+    A.topk_group = L.topk_group;
     A.expert0 = L.expert0;
     A.n_local = L.n_local;
     A.router = reinterpret_cast<const float *>(r->base);
@@ -1104,8 +1123,9 @@ extern "C" int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_laye
         if (D.dim != D0.dim || D.ffn != D0.ffn || D.n_expert != D0.n_expert || D.n_used != D0.n_used ||
             D.gating != D0.gating || D.weights_norm != D0.weights_norm || D.weights_scale != D0.weights_scale)
             return decline("stack layers must share one shape and routing configuration");
-        if (D.router_bias || D.shexp_gate || (D.n_local && D.n_local != D.n_expert) || D.expert0)
-            return decline("the stack kernel takes plain routed layers (no bias, shared expert or sharding)");
+        if (D.router_bias || D.shexp_gate || (D.n_local && D.n_local != D.n_expert) || D.expert0 ||
+            (D.n_group > 1 && D.topk_group < D.n_group))
+            return decline("the stack kernel takes plain routed layers (no bias, shared expert, sharding or groups)");
         Tensor *r = lookup(D.router), *g = lookup(D.gate), *u = lookup(D.up), *dn = lookup(D.down);
         const Tensor *sh[3] = {nullptr, nullptr, nullptr};
         RoutedLayerDev L{};

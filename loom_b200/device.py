@@ -80,6 +80,8 @@ class MoeLayer:
     expert0: int = 0
     n_local: int = 0
     next_router: Optional[DeviceTensor] = None  # L2-prefetch hint: the following layer's router
+    n_group: int = 1      # DeepSeek-V3 group-limited routing: expert groups ...
+    topk_group: int = 1   # ... and how many of them stay eligible
 
     def desc(self) -> _lib.MoeDesc:
         h = lambda t: t.handle if t is not None else 0  # noqa: E731
@@ -87,7 +89,7 @@ class MoeLayer:
         return _lib.MoeDesc(self.dim, self.ffn, self.n_expert, self.n_used, self.gating, int(self.weights_norm),
                             self.weights_scale, h(self.router), h(self.router_bias), h(self.gate), h(self.up),
                             h(self.down), h(sh[0]), h(sh[1]), h(sh[2]), self.shexp_ffn, self.expert0,
-                            self.n_local or self.n_expert, h(self.next_router))
+                            self.n_local or self.n_expert, h(self.next_router), self.n_group, self.topk_group)
 
     def forward(self, x, out, residual=None, logits=None, ids=None, stream=None, desc=None) -> None:
         """x, out: torch cuda float32 [T, dim]; ids: torch cuda int32 [T, n_used]."""

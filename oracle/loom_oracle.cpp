@@ -547,7 +547,59 @@ void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps)
 // moe.zig:106-158 route
 int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
              int weights_norm, float weights_scale, uint32_t *ids, float *gates) {
+    return or_route_grouped(logits, bias, n_expert, n_used, gating, weights_norm, weights_scale, 1, 1, ids, gates);
+}
+
+// Group-limited selection (DeepSeek-V3's published routing; the reference has
+// no implementation): the n_expert experts form n_group equal groups of
+// consecutive ids; a group's score is the sum of its two largest biased
+// choices (its one choice when a group holds one expert); the topk_group
+// groups with the highest scores are kept (serial first-max scan, lowest
+// group index on ties) and every expert outside them is masked to -inf before
+// moe.zig's k-round top-k. n_group = 1 (or topk_group = n_group) masks
+// nothing, which is exactly moe.zig:106-158 route.
+static int or_group_mask(float *choice, size_t n_expert, size_t n_group, size_t topk_group) {
+    if (n_group <= 1 || topk_group >= n_group) return 0;
+    const size_t gs = n_expert / n_group;
+    float gsc[32];
+    for (size_t g = 0; g < n_group; g++) {
+        float top1 = -INFINITY, top2 = -INFINITY;
+        for (size_t e = g * gs; e < (g + 1) * gs; e++) {
+            const float c = choice[e];
+            if (c > top1) {
+                top2 = top1;
+                top1 = c;
+            } else if (c > top2) {
+                top2 = c;
+            }
+        }
+        gsc[g] = gs == 1 ? top1 : top1 + top2;
+    }
+    uint32_t keep = 0;
+    for (size_t k = 0; k < topk_group; k++) {
+        int best = -1;
+        float bv = -INFINITY;
+        for (size_t g = 0; g < n_group; g++) {
+            if (keep >> g & 1u) continue;
+            if (best < 0 || gsc[g] > bv) {
+                best = (int)g;
+                bv = gsc[g];
+            }
+        }
+        keep |= 1u << best;
+    }
+    for (size_t e = 0; e < n_expert; e++)
+        if (!(keep >> (e / gs) & 1u)) choice[e] = -INFINITY;
+    return 0;
+}
+
+int or_route_grouped(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
+                     int weights_norm, float weights_scale, size_t n_group, size_t topk_group, uint32_t *ids,
+                     float *gates) {
     if (n_expert > 1024 || n_used > 64 || n_used > n_expert) return -1;  // MAX_EXPERTS/MAX_SELECTED, moe.zig:48-49
+    if (n_group == 0 || n_group > 32 || n_expert % n_group || topk_group == 0 || topk_group > n_group ||
+        n_used > topk_group * (n_expert / n_group))
+        return -1;
     float scores[1024], choice[1024];
     bool used[1024] = {};
     if (gating == 2) {
@@ -559,6 +611,7 @@ int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_u
     std::memcpy(choice, scores, n_expert * 4);
     if (bias)
         for (size_t i = 0; i < n_expert; i++) choice[i] += bias[i];
+    or_group_mask(choice, n_expert, n_group, topk_group);
     for (size_t k = 0; k < n_used; k++) {
         size_t best = 0;
         float best_v = -INFINITY;

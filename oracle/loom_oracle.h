@@ -55,6 +55,13 @@ void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps)
 /* router, src/gguf/moe.zig:106-158. gating: 1 softmax, 2 sigmoid, 3 softmax_topk */
 int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
              int weights_norm, float weights_scale, uint32_t *ids, float *gates);
+/* or_route with DeepSeek-V3's group-limited selection (n_group groups of
+ * n_expert / n_group consecutive experts, the topk_group best by the sum of
+ * their two largest biased choices kept); n_group = 1 is or_route. No
+ * counterpart in the reference: restated from the published routing. */
+int or_route_grouped(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
+                     int weights_norm, float weights_scale, size_t n_group, size_t topk_group, uint32_t *ids,
+                     float *gates);
 
 /* One expert as the seam's ExpertRef (src/compute/cpu.zig:23). */
 typedef struct {

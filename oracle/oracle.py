@@ -51,6 +51,7 @@ def lib() -> C.CDLL:
         L.or_sigmoid.restype = fp
         L.or_sigmoid.argtypes = [fp]
         L.or_route.argtypes = [vp, vp, sz, sz, C.c_int, C.c_int, fp, vp, vp]
+        L.or_route_grouped.argtypes = [vp, vp, sz, sz, C.c_int, C.c_int, fp, sz, sz, vp, vp]
         L.or_moe_ffn_block.argtypes = [vp, sz, vp, sz, vp]
         L.or_moe_ffn_routed.argtypes = [vp, sz, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, sz,
                                         vp, vp, sz, sz, sz, C.c_int, C.c_int, fp, vp]
@@ -152,11 +153,19 @@ def sigmoid(v):
     return float(lib().or_sigmoid(v))
 
 
-def route(logits, n_used, gating=1, weights_norm=True, weights_scale=1.0, bias=None):
+def route(logits, n_used, gating=1, weights_norm=True, weights_scale=1.0, bias=None, n_group=1,
+          topk_group=1):
+    """moe.zig:106-158 route; n_group > 1 adds DeepSeek-V3's group-limited
+    selection (or_route_grouped)."""
     logits = np.ascontiguousarray(logits, np.float32)
     bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
     ids = np.empty(n_used, np.uint32)
     gates = np.empty(n_used, np.float32)
+    if n_group > 1:
+        rc = lib().or_route_grouped(_p(logits), _p(bias), logits.size, n_used, gating, int(weights_norm),
+                                    weights_scale, n_group, topk_group, _p(ids), _p(gates))
+        assert rc == 0
+        return ids, gates
     rc = lib().or_route(_p(logits), _p(bias), logits.size, n_used, gating, int(weights_norm),
                         weights_scale, _p(ids), _p(gates))
     assert rc == 0

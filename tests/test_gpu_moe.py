@@ -155,11 +155,12 @@ def test_device_layer_with_router(be, orc, T):
         t.free()
 
 
-def _layer_case(orc, seed, ne, k, dim, ffn, gt, dt, shared=0, gating=1, scale=1.0, bias=False):
+def _layer_case(orc, seed, ne, k, dim, ffn, gt, dt, shared=0, gating=1, scale=1.0, bias=False, groups=(1, 1)):
     g, u, d = synth_layer(orc, seed, ne, dim, ffn, gt, gt, dt)
     rw = orc.synth(0, ne * dim, seed=seed * 7 + 1, sigma=0.02)
     L = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(gt, g), DeviceTensor.upload(gt, u), DeviceTensor.upload(dt, d),
-                 router=DeviceTensor.upload(0, rw), gating=gating, weights_scale=scale)
+                 router=DeviceTensor.upload(0, rw), gating=gating, weights_scale=scale, n_group=groups[0],
+                 topk_group=groups[1])
     if bias:
         L.router_bias = DeviceTensor.upload(0, (np.random.default_rng(seed).standard_normal(ne) * 0.05).astype(np.float32))
     if shared:
@@ -174,7 +175,9 @@ def _layer_case(orc, seed, ne, k, dim, ffn, gt, dt, shared=0, gating=1, scale=1.
     dict(ne=64, k=6, dim=2048, ffn=1408, gt=12, dt=8, shared=2816),          # DeepSeek-V2-Lite
     dict(ne=256, k=8, dim=1024, ffn=1024, gt=12, dt=12, shared=1024, gating=2, scale=2.5, bias=True),  # V3-like
     dict(ne=16, k=4, dim=512, ffn=256, gt=14, dt=14),                        # Q6_K gate/up
-], ids=["qwen3", "v2lite", "v3like", "q6k"])
+    dict(ne=256, k=8, dim=1024, ffn=512, gt=12, dt=12, shared=512, gating=2, scale=2.5, bias=True,
+         groups=(8, 4)),                                                     # V3 group-limited routing
+], ids=["qwen3", "v2lite", "v3like", "q6k", "v3grouped"])
 @pytest.mark.parametrize("T", [1, 3, 40])
 def test_decode_kernels_bitexact_with_slot_kernels(be, orc, cfg, T):
     """The fused decode kernels, the expert-major batch kernels and the general
@@ -229,3 +232,73 @@ def test_expert_parallel_partition_sums_to_full(be, orc):
     got = sum(parts)
     torch.cuda.synchronize()
     assert rel_l2(got.cpu().numpy(), want.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_grouped_routing_layer_vs_oracle(be, orc, T):
+    """DeepSeek-V3 group-limited routing (256 experts in 8 groups, the best 4
+    groups by the sum of their two best biased sigmoid scores stay eligible,
+    top-8, renormalised, scaled) through the device layer: ids equal to the
+    oracle's grouped route on the oracle's logits wherever the selection is
+    decided by more than 1e-4 (no near-tie between the k-th and (k+1)-th
+    eligible choice or between the kept and dropped groups), outputs within
+    the FFN tolerance of the oracle's moeFfnBlock over those experts."""
+    ne, k, dim, ffn, ng, tg, scale = 256, 8, 1024, 512, 8, 4, 2.5
+    g, u, d = synth_layer(orc, 11, ne, dim, ffn)
+    rw = orc.synth(0, ne * dim, seed=111, sigma=0.05)
+    bias = (np.random.default_rng(12).standard_normal(ne) * 0.05).astype(np.float32)
+    x = orc.synth(0, T * dim, seed=112, sigma=1.0).reshape(T, dim)
+    L = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g), DeviceTensor.upload(12, u), DeviceTensor.upload(14, d),
+                 router=DeviceTensor.upload(0, rw), router_bias=DeviceTensor.upload(0, bias), gating=2,
+                 weights_scale=scale, n_group=ng, topk_group=tg)
+    xt = torch.from_numpy(x).cuda()
+    out = torch.full((T, dim), float("nan"), device="cuda")
+    ids = torch.zeros((T, k), dtype=torch.int32, device="cuda")
+    L.forward(xt, out, ids=ids)
+    torch.cuda.synchronize()
+    got, gids = out.cpu().numpy(), ids.cpu().numpy()
+    orc.parallel_begin(8)
+    try:
+        logits = orc.matmul(0, rw.view(np.uint8), x, ne, dim)
+        gp, dp = ffn * orc.row_bytes(12, dim), dim * orc.row_bytes(14, ffn)
+        compared = 0
+        for t in range(T):
+            c = 1.0 / (1.0 + np.exp(-logits[t].astype(np.float64))) + bias
+            grp = np.sort(c.reshape(ng, -1), axis=1)[:, ::-1]
+            gsc = np.sort(grp[:, 0] + grp[:, 1])[::-1]
+            kept = np.sort(c.reshape(ng, -1)[np.argsort(-(grp[:, 0] + grp[:, 1]))[:tg]].ravel())[::-1]
+            if gsc[tg - 1] - gsc[tg] <= 1e-4 or kept[k - 1] - kept[k] <= 1e-4:
+                continue
+            wids, wg = orc.route(logits[t], k, 2, True, scale, bias, n_group=ng, topk_group=tg)
+            assert list(gids[t]) == list(wids), t
+            assert len(set(int(i) // (ne // ng) for i in wids)) <= tg
+            ex = [dict(gate_type=12, up_type=12, down_type=14, gate=g[i * gp:(i + 1) * gp],
+                       up=u[i * gp:(i + 1) * gp], down=d[i * dp:(i + 1) * dp], weight=float(w), ffn=ffn)
+                  for i, w in zip(wids, wg)]
+            want = orc.moe_ffn_block(x[t], ex, dim)
+            assert rel_l2(got[t], want) < TOL, (t, rel_l2(got[t], want))
+            compared += 1
+    finally:
+        orc.parallel_end()
+    assert compared >= max(1, T * 3 // 4)
+    for t_ in (L.gate, L.up, L.down, L.router, L.router_bias):
+        t_.free()
+
+
+def test_grouped_routing_declines_bad_groups(be, orc):
+    ne, k, dim, ffn = 64, 6, 512, 256
+    g, u, d = synth_layer(orc, 13, ne, dim, ffn)
+    L = MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g), DeviceTensor.upload(12, u), DeviceTensor.upload(14, d),
+                 router=DeviceTensor.upload(0, orc.synth(0, ne * dim, seed=5, sigma=0.02)), n_group=3, topk_group=1)
+    x = torch.zeros((1, dim), device="cuda")
+    out = torch.empty((1, dim), device="cuda")
+    with pytest.raises(Exception):
+        L.forward(x, out)  # 64 experts do not split into 3 groups
+    L.n_group, L.topk_group = 8, 0
+    with pytest.raises(Exception):
+        L.forward(x, out)  # no group kept
+    L.n_group, L.topk_group = 16, 1
+    with pytest.raises(Exception):
+        L.forward(x, out)  # one group of 4 experts cannot supply 6
+    for t_ in (L.gate, L.up, L.down, L.router):
+        t_.free()

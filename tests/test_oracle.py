@@ -197,3 +197,62 @@ def test_synth_matches_spec(orc):
     assert abs(f.std() - 0.02) < 0.002 and abs(f.mean()) < 0.001
     again = orc.synth(12, 8, seed=11, blk0=10)
     assert np.array_equal(again, b[10:18].ravel())
+
+
+def _np_grouped_route(logits, bias, k, n_group, topk_group):
+    """Independent restatement of DeepSeek-V3's group-limited top-k (sigmoid
+    gating, bias for selection only, renormalised gates): group score = sum of
+    the group's two largest biased scores; the topk_group best groups are
+    kept; top-k over the kept experts; ties take the lowest index."""
+    s = (1.0 / (1.0 + np.exp(-logits.astype(np.float64)))).astype(np.float32)
+    c = s + bias
+    gs = logits.size // n_group
+    grp = np.sort(c.reshape(n_group, gs), axis=1)[:, ::-1]
+    gsc = grp[:, 0] + grp[:, 1]
+    keep = np.argsort(-gsc, kind="stable")[:topk_group]
+    mask = np.full(logits.size, -np.inf, np.float32)
+    for g in keep:
+        mask[g * gs:(g + 1) * gs] = 0.0
+    ids = np.argsort(-(c + mask), kind="stable")[:k]
+    g = s[ids]
+    return ids, g / g.sum()
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_grouped_route_matches_restatement(orc, seed):
+    """DeepSeek-V3 shape: 256 experts, 8 groups, keep 4, top-8."""
+    rng = np.random.default_rng(100 + seed)
+    logits = rng.standard_normal(256).astype(np.float32) * 2
+    bias = rng.standard_normal(256).astype(np.float32) * 0.1
+    ids, gates = orc.route(logits, 8, 2, True, 1.0, bias, n_group=8, topk_group=4)
+    rids, rg = _np_grouped_route(logits, bias, 8, 8, 4)
+    assert list(ids) == list(rids)
+    np.testing.assert_allclose(gates, rg, rtol=1e-5, atol=0)
+    kept = set(int(i) // 32 for i in ids)
+    assert len(kept) <= 4
+
+
+@pytest.mark.parametrize("gating", [1, 2, 3])
+def test_grouped_route_one_group_is_route(orc, gating):
+    """n_group = 1 (or topk_group = n_group) reduces exactly to moe.route."""
+    rng = np.random.default_rng(5)
+    logits = rng.standard_normal(64).astype(np.float32)
+    bias = rng.standard_normal(64).astype(np.float32) * 0.1
+    a = orc.route(logits, 6, gating, True, 1.0, bias)
+    for ng, tg in [(1, 1), (8, 8)]:
+        ids = np.empty(6, np.uint32)
+        g = np.empty(6, np.float32)
+        assert orc.lib().or_route_grouped(orc._p(logits), orc._p(bias), 64, 6, gating, 1, 1.0, ng, tg,
+                                          orc._p(ids), orc._p(g)) == 0
+        assert list(ids) == list(a[0])
+        assert g.tobytes() == a[1].tobytes()
+
+
+def test_grouped_route_rejects_bad_groups(orc):
+    logits = np.zeros(64, np.float32)
+    ids = np.empty(8, np.uint32)
+    g = np.empty(8, np.float32)
+    L = orc.lib()
+    assert L.or_route_grouped(orc._p(logits), None, 64, 8, 2, 1, 1.0, 3, 1, orc._p(ids), orc._p(g)) != 0  # 64 % 3
+    assert L.or_route_grouped(orc._p(logits), None, 64, 8, 2, 1, 1.0, 8, 0, orc._p(ids), orc._p(g)) != 0
+    assert L.or_route_grouped(orc._p(logits), None, 64, 9, 2, 1, 1.0, 8, 1, orc._p(ids), orc._p(g)) != 0  # k > 8
