@@ -206,6 +206,7 @@ def run_gpu(args):
     B.init(local)
     T = args.tokens
     ep = args.ep and world > 1
+    a2a = ep and args.ep_mode == "a2a"
     ex0, nloc = D.expert_range(NE, rank, world) if ep else (0, NE)
     if ep:
         D.ep_init(rank, world, dist)
@@ -217,7 +218,9 @@ def run_gpu(args):
     descs = [L.desc() for L in layers]
     stream = torch.cuda.Stream()
     # replicas decode independent streams; expert-parallel ranks share one stream
-    x0 = torch.from_numpy(np.random.default_rng(0 if ep else rank).standard_normal((T, DIM)).astype(np.float32)).cuda()
+    # all-to-all ranks own different tokens (token-sharded attention)
+    x0 = torch.from_numpy(np.random.default_rng(0 if ep and not a2a else rank).standard_normal((T, DIM))
+                          .astype(np.float32)).cuda()
     bufs = [torch.empty((T, DIM), device="cuda") for _ in range(2)]
     ids = torch.zeros((LAYERS, T, NK), dtype=torch.int32, device="cuda")
 
@@ -237,16 +240,28 @@ def run_gpu(args):
         cur = x0
         for l, L in enumerate(layers):
             nxt = bufs[l % 2]
-            L.forward(cur, nxt, residual=cur, ids=ids[l], stream=sh, desc=descs[l])
+            if a2a:
+                L.forward_a2a(cur, nxt, residual=cur, ids=ids[l], stream=sh)
+            else:
+                L.forward(cur, nxt, residual=cur, ids=ids[l], stream=sh, desc=descs[l])
             cur = nxt
 
     with torch.cuda.stream(stream):
         step(stream.cuda_stream)  # sizes all scratch before capture
     torch.cuda.synchronize()
     k0 = B.kernelLaunches()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        step(torch.cuda.current_stream().cuda_stream)
+    if a2a:  # the receive counts go to the host every layer: no graph, eager launches
+        class _Eager:
+            def replay(self):
+                step(stream.cuda_stream)
+        g = _Eager()
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+    else:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(torch.cuda.current_stream().cuda_stream)
     launches_per_step = B.kernelLaunches() - k0
     with torch.cuda.stream(stream):  # replay, events and timing all on the launching stream
         for _ in range(args.warmup):
@@ -284,7 +299,7 @@ def run_gpu(args):
     # 9,694,464), scaled by layers: traffic grows in proportion to the layers
     traffic = (102891776 + 9694464) * LAYERS // 4 if stack is not None else None
     peak, peak_kind = peaks()
-    value = (T if ep else world * T) / (ms * 1e-3)
+    value = (T if ep and not a2a else world * T) / (ms * 1e-3)
 
     # e2e through the seam with host buffers
     e2e = None
@@ -295,7 +310,8 @@ def run_gpu(args):
     if args.e2e_layers > 0 and not ep:
         e2e = run_e2e(args, B)
     if ep or stack is not None:
-        e2e_device = run_e2e_device(args, g, stream, x0, bufs[(LAYERS - 1) % 2], torch, dist, world)
+        e2e_device = run_e2e_device(args, g, stream, x0, bufs[(LAYERS - 1) % 2], torch, dist, world,
+                                    job_tokens=T if ep and not a2a else world * T)
         if ep:
             e2e = e2e_device
 
@@ -310,11 +326,13 @@ def run_gpu(args):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "strong" if ep else "weak",
+        "scaling": "strong" if ep and not a2a else "weak",
         "vs_baseline": None, "dtype": "int8xq4/q6 (f32 accum)", "data": "synthetic (seeded generator), random-init weights",
         "config": {"workload": f"qwen3-30b-a3b moe stack decode, T={T}, {LAYERS} layers", "tokens": T,
                    "layers": LAYERS, "n_expert": NE, "n_used": NK, "dim": DIM, "ffn": FFN,
-                   "parallelism": (f"ep{world} (experts sharded, NCCL all-reduce combine)" if ep else
+                   "parallelism": (f"ep{world} (experts sharded, tokens sharded, NCCL all-to-all dispatch and "
+                                   f"combine)" if a2a else
+                                   f"ep{world} (experts sharded, NCCL all-reduce combine)" if ep else
                                    f"replicas x{world}" if world > 1 else "1 gpu"),
                    "engine": engine,
                    "l2": "inputs > L2 (48 distinct layers, ~1.2 GB touched per token)"},
@@ -452,7 +470,7 @@ def run_prefill(args, layers, stream, torch, D):
                          "tensor_frac": round(tfs / tpeak, 5)}}
 
 
-def run_e2e_device(args, g, stream, x0, out, torch, dist, world):
+def run_e2e_device(args, g, stream, x0, out, torch, dist, world, job_tokens=None):
     """End to end through the device-resident API: every step copies the
     token's activation in from pinned host memory, replays the step and reads
     the final output back."""
@@ -480,7 +498,7 @@ def run_e2e_device(args, g, stream, x0, out, torch, dist, world):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    T = x0.shape[0]
+    T = x0.shape[0] if job_tokens is None else job_tokens  # whole job: every rank's own tokens
     return {"value": round(T / (ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": int(hx.numel() * 4),
             "d2h_bytes_per_step": int(ho.numel() * 4), "path": "device API with pinned host input/output per step"}
 
@@ -547,6 +565,9 @@ def main():
     ap.add_argument("--ep", action="store_true",
                     help="with torchrun: shard each layer's experts over the ranks (expert parallel) instead of "
                          "running independent replicas")
+    ap.add_argument("--ep-mode", default="allreduce", choices=["allreduce", "a2a"],
+                    help="allreduce: every rank runs the same tokens, partial outputs summed; a2a: every rank owns "
+                         "its own T tokens, routed rows travel to the experts' ranks and back (NCCL send/recv)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers in the stack (default 48; smaller only for profiling captures)")
     args = ap.parse_args()

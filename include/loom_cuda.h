@@ -245,6 +245,17 @@ int loom_cuda_ep_init(int nranks, int rank, const void *id, size_t bytes);
 void loom_cuda_ep_shutdown(void);
 int loom_cuda_ep_rank(void);
 int loom_cuda_ep_size(void);
+/* All-to-all form (token-sharded attention): each rank passes ITS OWN T
+ * tokens (T may differ between ranks, and may be 0) and a descriptor of its
+ * contiguous shard [r*E/R, (r+1)*E/R). The rank routes its tokens, sends each
+ * routed row to the expert's owner (grouped ncclSend/ncclRecv), runs the rows
+ * that arrive through its experts, receives the outputs back and combines
+ * them in selection order with its tokens' shared expert: d_out is
+ * bit-identical to the unsharded layer on those tokens. Collective: every
+ * rank calls it for every layer. Synchronises the stream once (the receive
+ * counts go to the host). Without loom_cuda_ep_init it runs as one rank. */
+int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
+                             const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream);
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);

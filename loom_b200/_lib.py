@@ -104,6 +104,7 @@ def lib() -> C.CDLL:
         "loom_cuda_ep_shutdown": (None, []),
         "loom_cuda_ep_rank": (i, []),
         "loom_cuda_ep_size": (i, []),
+        "loom_cuda_ep_a2a_forward": (i, [C.POINTER(MoeDesc), vp, sz, vp, vp, vp, vp, vp]),
         "loom_cuda_trace_enable": (i, [sz]),
         "loom_cuda_trace_reset": (i, []),
         "loom_cuda_trace_read": (sz, [vp, sz]),

@@ -141,7 +141,14 @@ __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const fl
     int *sid = reinterpret_cast<int *>(choice + ne);
     float *sg = choice + ne + 64;
     float *red = choice + ne + 128;
-    if (threadIdx.x < ROUTE_THREADS) {
+    if (threadIdx.x < ROUTE_THREADS && A.ids_in) {  // rows routed elsewhere: take their experts and gates
+        for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS) {
+            const size_t i = (size_t)t * A.n_used + k;
+            A.ids[i] = A.ids_in[i];
+            A.gates[i] = A.gates_in ? A.gates_in[i] : 1.0f;
+            if (A.ids_out) A.ids_out[i] = A.ids_in[i];
+        }
+    } else if (threadIdx.x < ROUTE_THREADS) {
         route_block(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
                     red, A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, A.n_group, A.topk_group);
         if (A.ids_out)
@@ -718,7 +725,8 @@ __global__ void __launch_bounds__(256) k_route_batch(DecodeArgs A) {
     float *scores = smx + dim, *choice = scores + ne;
     for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
         reinterpret_cast<float4 *>(smx)[i] = __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)t * dim) + i);
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = __ldcg(A.logits + (size_t)t * ne + e);
+    if (!A.ids_in)
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) choice[e] = __ldcg(A.logits + (size_t)t * ne + e);
     __syncthreads();
     router_tail(A, t, smx, scores, choice, 8);
 }
@@ -755,6 +763,14 @@ static int tma_cluster(const DecodeArgs &A, size_t &smem) {
 }
 
 static cudaError_t launch_router(const DecodeArgs &A, cudaStream_t st) {
+    if (A.ids_in) {  // pre-routed rows: copy the routing, quantize the rows
+        const size_t rs = (size_t)(A.dim + 2 * A.n_expert + 136) * 4;
+        cudaError_t e = cudaSuccess;
+        if (rs > 48 * 1024 &&
+            (e = cudaFuncSetAttribute(k_route_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rs)) != cudaSuccess)
+            return e;
+        return launch_pdl(k_route_batch, dim3(A.T), dim3(256), rs, st, A);
+    }
     if (A.router && A.T > 16 && A.dim % 32 == 0 && A.dim <= 8192 && !A.trace_reg) {  // batch router
         const int et = rb_experts(A.dim);
         const size_t smem = ((size_t)et + 2) * A.dim * 4;

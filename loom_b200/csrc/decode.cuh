@@ -21,6 +21,8 @@ struct DecodeArgs {
     const float *router;     // f32 [n_expert][dim], or null when logits_in is given
     const float *bias;       // selection bias [n_expert] or null
     const float *logits_in;  // caller logits [T][n_expert] (router == null)
+    const int *ids_in;       // optional routing decided elsewhere [T][n_used] (then no router, no route) ...
+    const float *gates_in;   // ... with these gates (null: 1.0)
     const float *x;          // [T][dim]
     float *out;              // [T][dim]
     const float *residual;   // [T][dim] or null

@@ -24,6 +24,10 @@ struct Nccl {
     ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*groupStart)() = nullptr;
+    ncclResult_t (*groupEnd)() = nullptr;
     const char *(*getErrorString)(ncclResult_t) = nullptr;
 } N;
 
@@ -44,7 +48,12 @@ bool load_nccl(std::string &err) {
     N.allReduce = reinterpret_cast<decltype(N.allReduce)>(dlsym(h, "ncclAllReduce"));
     N.commDestroy = reinterpret_cast<decltype(N.commDestroy)>(dlsym(h, "ncclCommDestroy"));
     N.getErrorString = reinterpret_cast<decltype(N.getErrorString)>(dlsym(h, "ncclGetErrorString"));
-    if (!N.getUniqueId || !N.commInitRank || !N.allReduce || !N.commDestroy || !N.getErrorString) {
+    N.send = reinterpret_cast<decltype(N.send)>(dlsym(h, "ncclSend"));
+    N.recv = reinterpret_cast<decltype(N.recv)>(dlsym(h, "ncclRecv"));
+    N.groupStart = reinterpret_cast<decltype(N.groupStart)>(dlsym(h, "ncclGroupStart"));
+    N.groupEnd = reinterpret_cast<decltype(N.groupEnd)>(dlsym(h, "ncclGroupEnd"));
+    if (!N.getUniqueId || !N.commInitRank || !N.allReduce || !N.commDestroy || !N.getErrorString || !N.send ||
+        !N.recv || !N.groupStart || !N.groupEnd) {
         err = "NCCL library lacks an expected symbol";
         return false;
     }
@@ -63,6 +72,39 @@ int ep_allreduce_sum(float *buf, size_t n, cudaStream_t st, std::string &err) {
     ncclResult_t r = N.allReduce(buf, buf, n, ncclFloat32, ncclSum, g_comm, st);
     if (r != ncclSuccess) {
         err = std::string("ncclAllReduce: ") + N.getErrorString(r);
+        return LOOM_CUDA_ERROR;
+    }
+    return LOOM_CUDA_OK;
+}
+
+int ep_alltoallv(const void *send, const size_t *soff, const size_t *scnt, void *recv, const size_t *roff,
+                 const size_t *rcnt, size_t unit_bytes, cudaStream_t st, std::string &err) {
+    const int world = ep_active() ? g_size : 1, me = ep_active() ? g_rank : 0;
+    const uint8_t *s = static_cast<const uint8_t *>(send);
+    uint8_t *d = static_cast<uint8_t *>(recv);
+    if (scnt[me] != rcnt[me]) {
+        err = "all-to-all: the run to this rank and the run from it differ in size";
+        return LOOM_CUDA_ERROR;
+    }
+    if (scnt[me]) {
+        cudaError_t e = cudaMemcpyAsync(d + roff[me] * unit_bytes, s + soff[me] * unit_bytes, scnt[me] * unit_bytes,
+                                        cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) {
+            err = std::string("all-to-all self copy: ") + cudaGetErrorString(e);
+            return LOOM_CUDA_ERROR;
+        }
+    }
+    if (world == 1) return LOOM_CUDA_OK;
+    ncclResult_t r = N.groupStart();
+    for (int p = 0; p < world && r == ncclSuccess; p++) {
+        if (p == me) continue;
+        if (scnt[p]) r = N.send(s + soff[p] * unit_bytes, scnt[p] * unit_bytes, ncclUint8, p, g_comm, st);
+        if (r == ncclSuccess && rcnt[p]) r = N.recv(d + roff[p] * unit_bytes, rcnt[p] * unit_bytes, ncclUint8, p, g_comm, st);
+    }
+    const ncclResult_t r2 = N.groupEnd();
+    if (r == ncclSuccess) r = r2;
+    if (r != ncclSuccess) {
+        err = std::string("ncclSend/ncclRecv: ") + N.getErrorString(r);
         return LOOM_CUDA_ERROR;
     }
     return LOOM_CUDA_OK;

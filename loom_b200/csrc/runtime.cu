@@ -118,7 +118,9 @@ struct Scratch {
     DBuf xq256_q, xq256_d, xq256_s, xq32_q, xq32_d, xq32_s;
     DBuf logits, ids, gates, slots, act, aq, ad, as, counters, grp, ybuf;
     DBuf io_in, io_out, io_aux, raw;
-    HBuf h_in, h_out;
+    // all-to-all expert parallelism: home-side lists and rows, receive-side rows
+    DBuf a2a_i, a2a_sx, a2a_yb, a2a_ysh, a2a_rx, a2a_re, a2a_yr, a2a_g1;
+    HBuf h_in, h_out, h_cnt;
 } S;
 
 int alloc_tensor(int type, uint64_t nblk, Tensor &t) {
@@ -467,7 +469,8 @@ void loom_cuda_shutdown(void) {
         if (a.dev) cudaFree(a.dev);
     g_arenas.clear();
     for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
-                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.grp, &S.ybuf, &S.io_in, &S.io_out, &S.io_aux, &S.raw}) {
+                    &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.grp, &S.ybuf, &S.io_in, &S.io_out, &S.io_aux, &S.raw, &S.a2a_i, &S.a2a_sx,
+                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1}) {
         if (b->p) cudaFree(b->p);
         b->p = nullptr;
         b->cap = 0;
@@ -949,6 +952,160 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
     if (sharded) {
         if (int e = ep_allreduce_sum(d_out, T * D.dim, st, g_err)) return e;
     }
+    CK(cudaGetLastError());
+    return LOOM_CUDA_OK;
+}
+
+// All-to-all expert parallelism (a2a.cu): route this rank's own tokens, send
+// each routed row to the expert's owner, run the rows that arrive through
+// this rank's experts, send the outputs back, combine in selection order.
+int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
+                             const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream) {
+    if (int rc = need_init()) return rc;
+    if (!desc) return decline("no layer description");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    const loom_moe_desc &D = *desc;
+    if (D.n_expert == 0 || D.n_expert > 1024 || D.n_used == 0 || D.n_used > 64 || D.n_used > D.n_expert)
+        return decline("router shape out of range (moe.zig:48-49)");
+    const int world = ep_active() ? ep_size() : 1, me = ep_active() ? ep_rank() : 0;
+    if (world > A2A_MAX_RANKS) return decline("too many ranks for the all-to-all layer");
+    const size_t e0 = (size_t)me * D.n_expert / world, e1 = (size_t)(me + 1) * D.n_expert / world;
+    const size_t n_local = D.n_local ? D.n_local : D.n_expert;
+    if (D.expert0 != e0 || n_local != e1 - e0)
+        return decline("the all-to-all layer needs this rank's contiguous shard [r*E/R, (r+1)*E/R)");
+    if (D.dim % 4) return decline("dim must be a multiple of 4");
+    Tensor *g = lookup(D.gate), *u = lookup(D.up), *dn = lookup(D.down);
+    const Tensor *sh[3] = {nullptr, nullptr, nullptr};
+    if (D.shexp_gate) {
+        sh[0] = lookup(D.shexp_gate);
+        sh[1] = lookup(D.shexp_up);
+        sh[2] = lookup(D.shexp_down);
+        if (!sh[0] || !sh[1] || !sh[2]) return decline("unknown shared-expert tensor");
+    }
+    RoutedLayerDev L{};
+    if (int rc = routed_layer(L, g, u, dn, D.dim, D.ffn, n_local, sh, D.shexp_ffn)) return rc;
+    L.n_expert = (int)D.n_expert;
+    L.n_used = (int)D.n_used;
+    L.gating = D.gating ? D.gating : 1;
+    L.weights_norm = D.weights_norm;
+    L.weights_scale = D.weights_scale;
+    if (int rc = group_cfg(D, L)) return rc;
+    L.expert0 = (int)e0;
+    L.n_local = (int)n_local;
+    const float *bias = nullptr;
+    if (D.router_bias) {
+        Tensor *b = lookup(D.router_bias);
+        if (!b || b->type != T_F32 || b->nblk < D.n_expert) return decline("router bias must be f32 [n_expert]");
+        bias = reinterpret_cast<const float *>(b->base);
+    }
+    const float *router = nullptr;
+    if (!d_logits) {
+        Tensor *r = lookup(D.router);
+        if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
+        router = reinterpret_cast<const float *>(r->base);
+    }
+    const size_t dim = D.dim, k = D.n_used, ns = T * k;
+    const size_t max_ffn = std::max<size_t>(D.ffn, sh[0] ? D.shexp_ffn : 0), act_stride = align256(max_ffn);
+    // home side: route, then the destination-ordered send lists
+    if (int rc = ensure_moe_scratch(std::max<size_t>(T, 1), dim, max_ffn, D.n_expert, std::max<size_t>(T, 1) * (k + 1)))
+        return rc;
+    const size_t ni = align256(ns + 1);
+    if (int rc = S.a2a_i.ensure((4 * ni + 2 * A2A_MAX_RANKS) * 4)) return rc;
+    if (int rc = S.a2a_sx.ensure(std::max<size_t>(ns, 1) * dim * 4)) return rc;
+    if (int rc = S.a2a_yb.ensure(std::max<size_t>(ns, 1) * dim * 4)) return rc;
+    if (int rc = S.a2a_ysh.ensure(std::max<size_t>(T, 1) * dim * 4)) return rc;
+    if (int rc = S.h_cnt.ensure(2 * A2A_MAX_RANKS * 4)) return rc;
+    int *send_eid = S.a2a_i.as<int>(), *send_tok = send_eid + ni, *slot_pos = send_tok + ni;
+    float *home_gates = reinterpret_cast<float *>(slot_pos + ni);
+    int *cnt = slot_pos + 2 * ni;  // [A2A_MAX_RANKS] sent, then [A2A_MAX_RANKS] received
+    if (T) {
+        if (router) {
+            launch_mm_f32(router, L.n_expert, L.dim, d_x, (int)T, S.logits.as<float>(), st);
+            d_logits = S.logits.as<float>();
+        }
+        launch_route(d_logits, bias, (int)T, L.n_expert, L.n_used, L.gating, L.weights_norm, L.weights_scale,
+                     S.ids.as<int>(), S.gates.as<float>(), st, L.n_group, L.topk_group);
+        CK(cudaMemcpyAsync(home_gates, S.gates.p, ns * 4, cudaMemcpyDeviceToDevice, st));
+        if (d_ids) CK(cudaMemcpyAsync(d_ids, S.ids.p, ns * 4, cudaMemcpyDeviceToDevice, st));
+    }
+    launch_a2a_pack(S.ids.as<int>(), (int)T, (int)k, (int)D.n_expert, world, d_x, (int)dim, send_eid, send_tok,
+                    slot_pos, cnt, S.a2a_sx.as<float>(), st);
+    // counts: one int to and from every rank, then to the host
+    std::vector<size_t> one(world, 1), idx(world), scnt(world), soff(world), rcnt(world), roff(world);
+    for (int r = 0; r < world; r++) idx[r] = r;
+    if (int e = ep_alltoallv(cnt, idx.data(), one.data(), cnt + A2A_MAX_RANKS, idx.data(), one.data(), 4, st, g_err))
+        return e;
+    CK(cudaMemcpyAsync(S.h_cnt.p, cnt, 2 * A2A_MAX_RANKS * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    const int *hc = S.h_cnt.as<int>();
+    size_t so = 0, ro = 0;
+    for (int r = 0; r < world; r++) {
+        scnt[r] = (size_t)hc[r];
+        rcnt[r] = (size_t)hc[A2A_MAX_RANKS + r];
+        soff[r] = so;
+        roff[r] = ro;
+        so += scnt[r];
+        ro += rcnt[r];
+    }
+    if (so != ns) return fail("all-to-all pack", cudaErrorUnknown);
+    const size_t nr = ro;
+    // receive side buffers (sized now that the counts are known)
+    if (int rc = S.a2a_rx.ensure(std::max<size_t>(nr, 1) * dim * 4)) return rc;
+    if (int rc = S.a2a_re.ensure(std::max<size_t>(nr, 1) * 4)) return rc;
+    if (int rc = S.a2a_yr.ensure(std::max<size_t>(nr, 1) * dim * 4)) return rc;
+    if (int rc = S.a2a_g1.ensure(std::max<size_t>(nr, 1) * 4)) return rc;
+    const size_t nmax = std::max<size_t>(std::max(T, nr), 1);
+    if (int rc = ensure_moe_scratch(nmax, dim, max_ffn, D.n_expert, nmax * (k + 1))) return rc;
+    if (int e = ep_alltoallv(S.a2a_sx.p, soff.data(), scnt.data(), S.a2a_rx.p, roff.data(), rcnt.data(), dim * 4, st,
+                             g_err))
+        return e;
+    if (int e = ep_alltoallv(send_eid, soff.data(), scnt.data(), S.a2a_re.p, roff.data(), rcnt.data(), 4, st, g_err))
+        return e;
+    // the shared expert of this rank's own tokens (replicated weights)
+    const float *y_sh = nullptr;
+    if (sh[0] && T) {
+        RoutedLayerDev Ls = L;
+        Ls.n_used = 0;
+        quantize_inputs(d_x, T, dim, any_type(Ls, true), any_type(Ls, false), st);
+        launch_experts_routed(Ls, nullptr, nullptr, (int)T, (int)act_stride, make_xq(true, dim), make_xq(false, dim),
+                              S.act.as<float>(), S.aq.as<int8_t>(), S.ad.as<float>(), S.as.as<int32_t>(),
+                              S.a2a_ysh.as<float>(), nullptr, st);
+        y_sh = S.a2a_ysh.as<float>();
+    }
+    // the rows that arrived, each through its one local expert with weight 1
+    if (nr) {
+        RoutedLayerDev Lr = L;
+        Lr.n_used = 1;
+        Lr.has_shared = 0;
+        DecodeArgs A = decode_args(Lr, nr, nullptr, S.a2a_rx.as<float>(), nullptr, nullptr, S.a2a_yr.as<float>(),
+                                   nullptr, nullptr, act_stride);
+        A.ids_in = S.a2a_re.as<int>();
+        A.trace = nullptr;
+        if (g_force_generic != 1 && batch_supported(A)) {
+            // expert-major: each local expert's rows against one read of its weights
+            const bool mma = moe_mma_supported(A) &&
+                             (g_force_generic == 3 || (g_force_generic == 0 && nr >= 16 * (size_t)Lr.n_local));
+            if (int rc = S.grp.ensure((2 * (size_t)Lr.n_local + nr) * 4)) return rc;
+            if (int rc = S.ybuf.ensure(nr * dim * 4)) return rc;
+            A.grp_cnt = S.grp.as<int>();
+            A.grp_off = A.grp_cnt + Lr.n_local;
+            A.grp_list = A.grp_off + Lr.n_local;
+            A.y = S.ybuf.as<float>();
+            CK(launch_batch(A, mma, st));
+        } else {  // per-row slot kernels
+            launch_a2a_fill(S.a2a_g1.as<float>(), (int)nr, 1.0f, st);
+            quantize_inputs(S.a2a_rx.as<float>(), nr, dim, any_type(Lr, true), any_type(Lr, false), st);
+            launch_experts_routed(Lr, S.a2a_re.as<int>(), S.a2a_g1.as<float>(), (int)nr, (int)act_stride,
+                                  make_xq(true, dim), make_xq(false, dim), S.act.as<float>(), S.aq.as<int8_t>(),
+                                  S.ad.as<float>(), S.as.as<int32_t>(), S.a2a_yr.as<float>(), nullptr, st);
+        }
+    }
+    // outputs back to the rows' home ranks (the reverse of the dispatch)
+    if (int e = ep_alltoallv(S.a2a_yr.p, roff.data(), rcnt.data(), S.a2a_yb.p, soff.data(), scnt.data(), dim * 4, st,
+                             g_err))
+        return e;
+    launch_a2a_combine(S.a2a_yb.as<float>(), slot_pos, home_gates, y_sh, d_residual, d_out, (int)T, (int)k, (int)dim,
+                       st);
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;
 }

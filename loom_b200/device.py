@@ -91,6 +91,15 @@ class MoeLayer:
                             h(self.down), h(sh[0]), h(sh[1]), h(sh[2]), self.shexp_ffn, self.expert0,
                             self.n_local or self.n_expert, h(self.next_router), self.n_group, self.topk_group)
 
+    def forward_a2a(self, x, out, residual=None, logits=None, ids=None, stream=None) -> None:
+        """All-to-all expert parallelism: x/out are THIS rank's tokens [T, dim]
+        (T may be 0); collective over the ranks of ep_init."""
+        d = self.desc()
+        T = x.shape[0]
+        rc = _lib.lib().loom_cuda_ep_a2a_forward(C.byref(d), _ptr(x), T, _ptr(out), _ptr(residual), _ptr(logits),
+                                                 _ptr(ids), stream)
+        _lib.must(rc, "ep_a2a_forward")
+
     def forward(self, x, out, residual=None, logits=None, ids=None, stream=None, desc=None) -> None:
         """x, out: torch cuda float32 [T, dim]; ids: torch cuda int32 [T, n_used]."""
         d = desc if desc is not None else self.desc()
