@@ -260,14 +260,16 @@ int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);
 /* Test hook selecting the MoE kernel family: 0 automatic (fused decode
- * kernels for T <= 16, expert-major batch kernels above, on the tensor cores
+ * kernels for T <= 2, expert-major batch kernels above, on the tensor cores
  * once the experts average >= 16 tokens), 1 the general slot kernels, 2 the
  * expert-major batch kernels at any T, 3 the expert-major batch kernels on
- * the tensor cores at any T (Q4_K gate/up with Q6_K down; other types fall
- * back to 2). 0-2 compute the same numbers bit for bit; 3 rounds the weights
- * and activations to bf16 (within 2e-3 relative L2). Returns the previous
- * setting. */
+ * the tensor cores at any T (Q4_K gate/up with Q6_K down whose scales are
+ * within +-64; other layers fall back to 2). Every family computes the same
+ * numbers bit for bit. Returns the previous setting. */
 int loom_cuda_force_generic(int on);
+/* Kernel family the last routed layer ran: 0 fused decode, 1 slot kernels,
+ * 2 expert-major int8 batch kernels, 3 tensor cores; -1 before the first. */
+int loom_cuda_last_path(void);
 /* Phase tracing of the fused decode kernels (the counterpart of the
  * reference's LOOM_PROFILE phase timers, deepseek.zig:705-850): with room for
  * n_kernels traced launches, each decode kernel records its first CTA start

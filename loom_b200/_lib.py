@@ -92,6 +92,7 @@ def lib() -> C.CDLL:
         "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
         "loom_cuda_sync": (i, []),
         "loom_cuda_force_generic": (i, [i]),
+        "loom_cuda_last_path": (i, []),
         "loom_cuda_device_error": (i, []),
         "loom_cuda_stack_prepare": (i, [vp, sz, C.POINTER(u64)]),
         "loom_cuda_stack_forward": (i, [u64, vp, vp, vp, vp]),
@@ -99,6 +100,7 @@ def lib() -> C.CDLL:
         "loom_cuda_stack_free": (i, [u64]),
         "loom_cuda_stack_trace": (i, [u64, i, vp, sz]),
         "loom_cuda_umma_selftest": (i, [vp, vp, vp, i, i, i]),
+        "loom_cuda_tc_profile": (i, [i, vp, sz]),
         "loom_cuda_ep_unique_id": (i, [vp, sz]),
         "loom_cuda_ep_init": (i, [i, i, vp, sz]),
         "loom_cuda_ep_shutdown": (None, []),

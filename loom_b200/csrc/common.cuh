@@ -48,8 +48,11 @@ struct WDev {
     const uint8_t *sc;  // Q6_K scales region, else null
     const uint16_t *d;  // f16 scales region (Q6_K/Q8_0/Q4_0), else null
     int type;
-    int pad_;
+    int pad_;           // flags (WDEV_*)
 };
+// Q6_K tensor whose int8 sub-block scales all satisfy |sc| <= 64, so that
+// sc * (q - 32) is an integer fp16 holds exactly (the tensor-core path)
+constexpr int WDEV_Q6K_SMALL_SCALES = 1;
 
 // Quantized activations for a batch of vectors, each `cols` wide:
 //   q[t*cols + i]        int8

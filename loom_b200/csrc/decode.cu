@@ -855,11 +855,22 @@ __global__ void __launch_bounds__(512) k_group(DecodeArgs A) {
     }
     __syncthreads();
     if (threadIdx.x == 0) {  // exclusive prefix over n_local (<= 1024) counts
-        int o = 0;
+        int o = 0, c = 0;
         for (int e = 0; e < A.n_local; e++) {
             A.grp_off[e] = o;
             A.grp_cnt[e] = cnt[e];
             o += cnt[e];
+            if (A.tc_pre) {
+                A.tc_pre[e] = c;
+                c += (cnt[e] + MOE_TC_N - 1) / MOE_TC_N;
+            }
+        }
+        if (A.tc_pre) {
+            if (A.has_shared) {
+                A.tc_pre[A.n_local] = c;
+                c += (A.T + MOE_TC_N - 1) / MOE_TC_N;
+            }
+            A.tc_pre[A.n_local + (A.has_shared ? 1 : 0)] = c;
         }
     }
     __syncthreads();

@@ -47,6 +47,7 @@ struct DecodeArgs {
     int *grp_cnt;            // [n_local] slots per local expert
     int *grp_off;            // [n_local] first position in grp_list
     int *grp_list;           // [T*n_used] routed slots, grouped by expert, slot order within a group
+    int *tc_pre;             // [n_local + 2] tensor-core path: chunks of MOE_TC_N slots before each expert
     float *y;                // [n_slots][dim] per-slot down outputs
     int trace_reg;           // test hook: use the register-staged router instead of the TMA one
     int *err;                // device error word (bounded waits that timed out), or null
@@ -68,6 +69,9 @@ bool batch_supported(const DecodeArgs &A);
 // the int8 dot kernels
 cudaError_t launch_batch(const DecodeArgs &A, bool mma, cudaStream_t st);
 bool moe_mma_supported(const DecodeArgs &A);
+constexpr int MOE_TC_N = 64;  // slots per tensor-core tile
+// Largest |scale| of a Q6_K scales region (nblk x 16 int8); synchronises st. -1 on error.
+int q6k_max_scale(const uint8_t *sc, uint64_t nblk, int *d_tmp, cudaStream_t st);
 cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st,
                            cudaError_t (*quant)(const DecodeArgs &, cudaStream_t));
 

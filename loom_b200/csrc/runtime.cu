@@ -119,6 +119,7 @@ struct Scratch {
     DBuf logits, ids, gates, slots, act, aq, ad, as, counters, grp, ybuf;
     DBuf io_in, io_out, io_aux, raw;
     // all-to-all expert parallelism: home-side lists and rows, receive-side rows
+    DBuf tmp;  // small synchronous scratch (tensor scans)
     DBuf a2a_i, a2a_sx, a2a_yb, a2a_ysh, a2a_rx, a2a_re, a2a_yr, a2a_g1;
     HBuf h_in, h_out, h_cnt;
 } S;
@@ -151,6 +152,17 @@ int fill_from_raw_dev(Tensor &t, const uint8_t *raw_dev) {
     return 0;
 }
 
+// Q6_K: record whether every sub-block scale is within +-64 (the tensor-core
+// path folds sc * (q - 32) into fp16, exact only then). Synchronises g_stream.
+int mark_q6k(Tensor &t) {
+    if (t.type != T_Q6_K) return 0;
+    if (int rc = S.tmp.ensure(64)) return rc;
+    const int m = q6k_max_scale(t.w.sc, t.nblk, S.tmp.as<int>(), g_stream);
+    if (m < 0) return fail("q6k scale scan", cudaGetLastError());
+    if (m <= 64) t.w.pad_ |= WDEV_Q6K_SMALL_SCALES;
+    return 0;
+}
+
 const uint8_t *arena_lookup(const void *p, size_t bytes) {
     const uint8_t *hp = static_cast<const uint8_t *>(p);
     for (auto &a : g_arenas)
@@ -176,6 +188,7 @@ int upload_tensor(int type, const void *data, size_t bytes, uint64_t &handle) {
         if (int rc = fill_from_raw_dev(t, raw_dev)) return rc;
     }
     CK(cudaStreamSynchronize(g_stream));  // the host bytes are only borrowed
+    if (int rc = mark_q6k(t)) return rc;
     handle = g_next_handle++;
     g_tensors[handle] = t;
     return 0;
@@ -304,11 +317,16 @@ bool any_type(const RoutedLayerDev &L, bool k256) {
     return r;
 }
 
-// The fused decode kernels take up to this many tokens per layer; larger
-// batches use the slot kernels.
+// The fused decode kernels take up to this many tokens per layer (the
+// allocation-free entry point runs them up to this size).
 constexpr size_t DECODE_MAX_T = 16;
+// Above this many tokens the expert-major batch kernels win (one read of each
+// selected expert for all its tokens; measured on B200 at the Qwen3 layer:
+// T = 2 decode 1.86 ms vs batch 2.15 ms per 48 layers, T = 4 3.13 vs 2.51).
+constexpr size_t DECODE_AUTO_T = 2;
 
 int g_force_generic = 0;  // test hook: 0 auto, 1 slot kernels, 2 batch kernels, 3 batch on the tensor cores
+int g_last_path = -1;      // kernel family of the last routed layer (loom_cuda_last_path)
 const uint8_t *g_next_router = nullptr;  // L2-prefetch hint for the layer being launched
 size_t g_next_router_bytes = 0;
 // phase trace: [2*n] (first start, last end) per traced kernel, see loom_cuda_trace_*
@@ -393,20 +411,24 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
     const size_t act_stride = align256(max_ffn);
     if (g_force_generic != 1) {
         DecodeArgs A = decode_args(L, T, router, d_x, d_logits, d_bias, d_out, d_residual, d_ids_out, act_stride);
-        if (g_force_generic == 0 && T <= DECODE_MAX_T && decode_supported(A)) {
+        const bool batch_ok = router && batch_supported(A);
+        if (g_force_generic == 0 && (T <= DECODE_AUTO_T || (!batch_ok && T <= DECODE_MAX_T)) && decode_supported(A)) {
+            g_last_path = 0;
             CK(launch_decode(A, st));
             return 0;
         }
-        if (router && batch_supported(A)) {
+        if (batch_ok) {
             // tensor cores once the experts average 16 or more tokens each (prefill)
             const bool mma = moe_mma_supported(A) &&
                              (g_force_generic == 3 || (g_force_generic == 0 && T * L.n_used >= 16 * (size_t)L.n_local));
-            if (int rc = S.grp.ensure((2 * (size_t)L.n_local + T * L.n_used) * 4)) return rc;
+            if (int rc = S.grp.ensure((3 * (size_t)L.n_local + T * L.n_used + 4) * 4)) return rc;
             if (int rc = S.ybuf.ensure(n_slots * (size_t)L.dim * 4)) return rc;
             A.grp_cnt = S.grp.as<int>();
             A.grp_off = A.grp_cnt + L.n_local;
             A.grp_list = A.grp_off + L.n_local;
+            A.tc_pre = A.grp_list + T * L.n_used;
             A.y = S.ybuf.as<float>();
+            g_last_path = mma ? 3 : 2;
             CK(launch_batch(A, mma, st));
             return 0;
         }
@@ -415,6 +437,7 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
         launch_mm_f32(router, L.n_expert, L.dim, d_x, (int)T, S.logits.as<float>(), st);
         d_logits = S.logits.as<float>();
     }
+    g_last_path = 1;
     launch_route(d_logits, d_bias, (int)T, L.n_expert, L.n_used, L.gating, L.weights_norm, L.weights_scale,
                  S.ids.as<int>(), S.gates.as<float>(), st, L.n_group, L.topk_group);
     quantize_inputs(d_x, T, L.dim, any_type(L, true), any_type(L, false), st);
@@ -470,7 +493,7 @@ void loom_cuda_shutdown(void) {
     g_arenas.clear();
     for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
                     &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.grp, &S.ybuf, &S.io_in, &S.io_out, &S.io_aux, &S.raw, &S.a2a_i, &S.a2a_sx,
-                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1}) {
+                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1, &S.tmp}) {
         if (b->p) cudaFree(b->p);
         b->p = nullptr;
         b->cap = 0;
@@ -591,6 +614,8 @@ int loom_cuda_device_error(void) {
     for (int x : all) v |= x;
     return v;
 }
+
+int loom_cuda_last_path(void) { return g_last_path; }
 
 int loom_cuda_force_generic(int on) {
     const int prev = g_force_generic;
@@ -840,6 +865,10 @@ int loom_cuda_tensor_synth_range(int type, uint64_t blk0, uint64_t nblk, uint64_
         cudaFree(t.base);
         return fail("tensor_synth", e);
     }
+    if (int rc = mark_q6k(t)) {
+        cudaFree(t.base);
+        return rc;
+    }
     uint64_t h = g_next_handle++;
     g_tensors[h] = t;
     *out = h;
@@ -885,7 +914,7 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
     if (int rc = need_init()) return rc;
     const size_t n_slots = T * (n_used + 1);
     if (int rc = ensure_moe_scratch(T, dim, ffn, n_expert, n_slots)) return rc;
-    if (int rc = S.grp.ensure((2 * n_expert + T * n_used) * 4)) return rc;
+    if (int rc = S.grp.ensure((3 * n_expert + T * n_used + 4) * 4)) return rc;
     if (int rc = S.ybuf.ensure(n_slots * dim * 4)) return rc;
     CK(cudaStreamSynchronize(g_stream));
     return LOOM_CUDA_OK;
@@ -1085,11 +1114,13 @@ int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t
             // expert-major: each local expert's rows against one read of its weights
             const bool mma = moe_mma_supported(A) &&
                              (g_force_generic == 3 || (g_force_generic == 0 && nr >= 16 * (size_t)Lr.n_local));
-            if (int rc = S.grp.ensure((2 * (size_t)Lr.n_local + nr) * 4)) return rc;
+            if (int rc = S.grp.ensure((3 * (size_t)Lr.n_local + nr + 4) * 4)) return rc;
             if (int rc = S.ybuf.ensure(nr * dim * 4)) return rc;
             A.grp_cnt = S.grp.as<int>();
             A.grp_off = A.grp_cnt + Lr.n_local;
             A.grp_list = A.grp_off + Lr.n_local;
+            A.tc_pre = A.grp_list + nr;
+            g_last_path = mma ? 3 : 2;
             A.y = S.ybuf.as<float>();
             CK(launch_batch(A, mma, st));
         } else {  // per-row slot kernels

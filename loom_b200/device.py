@@ -173,8 +173,13 @@ def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -
 
 def force_generic(mode) -> int:
     """Kernel family for MoE layers: 0 automatic, 1 (True) slot kernels, 2 expert-major batch kernels
-    (int8 dots), 3 expert-major batch kernels on the tensor cores (bf16 tcgen05 GEMMs)."""
+    (int8 dots), 3 expert-major batch kernels on the tensor cores (integer-exact tcgen05 MMAs)."""
     return int(_lib.lib().loom_cuda_force_generic(int(mode)))
+
+
+def last_path() -> int:
+    """Kernel family of the last routed layer: 0 decode, 1 slot, 2 int8 batch, 3 tensor cores."""
+    return int(_lib.lib().loom_cuda_last_path())
 
 
 def trace_enable(n_kernels: int) -> None:

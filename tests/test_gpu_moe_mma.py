@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-3
 
 
-def _run(L, x, mode, k):
+def _run(L, x, mode, k, path=None):
     prev = D.force_generic(mode)
     try:
         out = torch.full(x.shape, float("nan"), device="cuda")
@@ -26,6 +26,8 @@ def _run(L, x, mode, k):
     finally:
         D.force_generic(prev)
     assert _lib.lib().loom_cuda_device_error() == 0
+    if path is not None:
+        assert D.last_path() == path
     return out.cpu().numpy(), ids.cpu().numpy()
 
 
@@ -39,7 +41,7 @@ def test_mma_layer_vs_oracle(be, orc, T):
     x = orc.synth(0, T * dim, seed=112, sigma=1.0).reshape(T, dim)
     L = D.MoeLayer(dim, ffn, ne, k, D.DeviceTensor.upload(12, g), D.DeviceTensor.upload(12, u),
                    D.DeviceTensor.upload(14, d), router=D.DeviceTensor.upload(0, rw))
-    got, gids = _run(L, torch.from_numpy(x).cuda(), 3, k)
+    got, gids = _run(L, torch.from_numpy(x).cuda(), 3, k, path=3)
     orc.parallel_begin(16)
     try:
         want, wids = orc.moe_layer(x, rw, (12, g), (12, u), (14, d), ffn, ne, k)
@@ -63,8 +65,8 @@ def test_mma_auto_prefill_matches_int8_batch(be, orc):
     ne, k, dim, ffn, T = 128, 8, 2048, 768, 512
     L = _layer_case(orc, 21, ne=ne, k=k, dim=dim, ffn=ffn, gt=12, dt=14)
     x = torch.from_numpy(orc.synth(0, T * dim, seed=212, sigma=1.0).reshape(T, dim)).cuda()
-    auto, ids_a = _run(L, x, 0, k)
-    ref, ids_r = _run(L, x, 2, k)
+    auto, ids_a = _run(L, x, 0, k, path=3)
+    ref, ids_r = _run(L, x, 2, k, path=2)
     assert np.array_equal(ids_a, ids_r)
     assert np.array_equal(bits(auto), bits(ref))
     k0 = _lib.lib().loom_cuda_kernel_launches()
@@ -80,7 +82,38 @@ def test_mma_shared_expert_and_ragged_groups(be, orc):
     L = _layer_case(orc, 31, **cfg)
     T = 200
     x = torch.from_numpy(orc.synth(0, T * cfg["dim"], seed=312, sigma=1.0).reshape(T, cfg["dim"])).cuda()
-    mma, ids_m = _run(L, x, 3, cfg["k"])
-    ref, ids_r = _run(L, x, 2, cfg["k"])
+    mma, ids_m = _run(L, x, 3, cfg["k"], path=3)
+    ref, ids_r = _run(L, x, 2, cfg["k"], path=2)
     assert np.array_equal(ids_m, ids_r)
     assert np.array_equal(bits(mma), bits(ref)), rel_l2(mma, ref)
+
+
+@pytest.mark.parametrize("T", [1, 8, 40, 1100])
+def test_mma_token_counts(be, orc, T):
+    """Few tokens per expert (MMA N = 16 with padding), and more than one
+    64-token chunk per expert (T = 1100 over 40 experts, ~110 each): the
+    tensor-core path equals the int8 batch kernels bit for bit."""
+    cfg = dict(ne=40, k=4, dim=1024, ffn=512, gt=12, dt=14)
+    L = _layer_case(orc, 41, **cfg)
+    x = torch.from_numpy(orc.synth(0, T * cfg["dim"], seed=412, sigma=1.0).reshape(T, cfg["dim"])).cuda()
+    mma, ids_m = _run(L, x, 3, cfg["k"], path=3)
+    ref, ids_r = _run(L, x, 2, cfg["k"], path=2)
+    assert np.array_equal(ids_m, ids_r)
+    assert np.array_equal(bits(mma), bits(ref)), rel_l2(mma, ref)
+
+
+def test_mma_declines_large_q6k_scales(be, orc):
+    """Q6_K down weights with a sub-block scale beyond +-64 (sc * (q - 32)
+    would round in fp16): the layer stays on the int8 kernels and still
+    matches them."""
+    ne, k, dim, ffn, T = 16, 4, 1024, 512, 128
+    g, u, d = synth_layer(orc, 51, ne, dim, ffn, 12, 12, 14)
+    d = d.copy()
+    d[192 + 3] = 100  # block 0, scale 3 (int8 100)
+    rw = orc.synth(0, ne * dim, seed=52, sigma=0.02)
+    L = D.MoeLayer(dim, ffn, ne, k, D.DeviceTensor.upload(12, g), D.DeviceTensor.upload(12, u),
+                   D.DeviceTensor.upload(14, d), router=D.DeviceTensor.upload(0, rw))
+    x = torch.from_numpy(orc.synth(0, T * dim, seed=53, sigma=1.0).reshape(T, dim)).cuda()
+    a, ia = _run(L, x, 3, k, path=2)
+    b, ib = _run(L, x, 2, k, path=2)
+    assert np.array_equal(ia, ib) and np.array_equal(bits(a), bits(b))
