@@ -470,38 +470,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
                             for (int c = 0; c < 8; c++)
                                 *reinterpret_cast<uint4 *>(tA + tc_sw(r, c)) = make_uint4(0, 0, 0, 0);
                         }
-                    } else {  // thread = (value group gp of the quarter, row): 32 values
-                        const int gp = ct >> 7, r = ct & 127, h = q >> 1, p = q & 1, gg = 2 * p + gp;
+                    } else {  // thread = (row, 16-byte quarter j of the half's 64 ql bytes), two rows:
+                              // 8 consecutive lanes read 2 rows x 4 chunks (row pitch 192 B): conflict-free
+                        const int h = q >> 1, p = q & 1, j = ct & 3;
+                        const int gp = j >> 1, hl = j & 1, gg = 2 * p + gp;  // values l = 16 hl .. 16 hl + 15 of group gg
                         uint8_t *tA = O;
-                        if (r < rows) {
-                            const uint8_t *wr = W + (size_t)r * 192;
-                            const uint4 l0 = *reinterpret_cast<const uint4 *>(wr + 64 * h + 32 * gp);
-                            const uint4 l1 = *reinterpret_cast<const uint4 *>(wr + 64 * h + 32 * gp + 16);
-                            const uint4 h0 = *reinterpret_cast<const uint4 *>(wr + 128 + 32 * h);
-                            const uint4 h1 = *reinterpret_cast<const uint4 *>(wr + 128 + 32 * h + 16);
-                            const int8_t *scb =
-                                reinterpret_cast<const int8_t *>(W + 128 * 192 + (size_t)r * 16 + 8 * h + 2 * gg);
-                            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-                            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-                            const __half2 k1056 = tc_u2h(0x64206420u);  // 1024 + 32
+                        const __half2 k1056 = tc_u2h(0x64206420u);  // 1024 + 32
 #pragma unroll
-                            for (int c = 0; c < 4; c++) {  // values l = 8c .. 8c + 7 of group gg
-                                const __half2 sc2 = __half2half2(__int2half_rn((int)scb[c >> 1]));
-                                uint32_t o[4];
+                        for (int u = 0; u < 2; u++) {
+                            const int r = (ct >> 2) + 64 * u;
+                            const int c0 = 4 * gp + 2 * hl;  // output chunks c0, c0 + 1
+                            if (r < rows) {
+                                const uint8_t *wr = W + (size_t)r * 192;
+                                const uint4 l4 = *reinterpret_cast<const uint4 *>(wr + 64 * h + 16 * j);
+                                const uint4 h4 = *reinterpret_cast<const uint4 *>(wr + 128 + 32 * h + 16 * hl);
+                                const int sc = (int)*reinterpret_cast<const int8_t *>(W + 128 * 192 + (size_t)r * 16 + 8 * h +
+                                                                                      2 * gg + hl);
+                                const __half2 sc2 = __half2half2(__int2half_rn(sc));
+                                const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+                                uint32_t o[8];
 #pragma unroll
-                                for (int wi = 0; wi < 2; wi++) {
-                                    const uint32_t lo4 = (p ? lw[2 * c + wi] >> 4 : lw[2 * c + wi]) & 0x0F0F0F0Fu;
-                                    const uint32_t qb = lo4 | (((hw[2 * c + wi] >> (2 * gg)) & 0x03030303u) << 4);
-                                    o[2 * wi] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), sc2));
-                                    o[2 * wi + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), sc2));
+                                for (int w = 0; w < 4; w++) {
+                                    const uint32_t lo4 = (p ? lw[w] >> 4 : lw[w]) & 0x0F0F0F0Fu;
+                                    const uint32_t qb = lo4 | (((hw[w] >> (2 * gg)) & 0x03030303u) << 4);
+                                    o[2 * w] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), sc2));
+                                    o[2 * w + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), sc2));
                                 }
-                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, 4 * gp + c)) =
-                                    make_uint4(o[0], o[1], o[2], o[3]);
+                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0)) = make_uint4(o[0], o[1], o[2], o[3]);
+                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                            } else {
+                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0)) = make_uint4(0, 0, 0, 0);
+                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0 + 1)) = make_uint4(0, 0, 0, 0);
                             }
-                        } else {
-#pragma unroll
-                            for (int c = 0; c < 4; c++)
-                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, 4 * gp + c)) = make_uint4(0, 0, 0, 0);
                         }
                     }
                     const long long c_b = clock64();
