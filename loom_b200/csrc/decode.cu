@@ -654,29 +654,42 @@ bool decode_supported(const DecodeArgs &A) {
 // a 16-CTA cluster (non-portable size), else 8; 0 when the rows do not fit.
 // dotF32 (ggml.zig:198) of a router row and x, both in shared memory, dim a
 // multiple of 32 (the stack kernel's router_dot_smem, same order)
-__device__ __forceinline__ float router_dot_smem_(const float *wr, const float *x, int dim, int lane) {
-    float a = 0.0f;
-#pragma unroll 8
-    for (int i = lane; i < dim; i += 32) a = fadd(a, fmul(wr[i], x[i]));
-    const float a8 = __shfl_down_sync(0xffffffffu, a, 8);
-    const float a16 = __shfl_down_sync(0xffffffffu, a, 16);
-    const float a24 = __shfl_down_sync(0xffffffffu, a, 24);
-    const float v = fadd(fadd(fadd(a, a8), a16), a24);
-    float r = __shfl_sync(0xffffffffu, v, 0);
-#pragma unroll
-    for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
-    return r;
-}
-
 // ---- batch router (T > 16 tokens): router GEMV tiled over experts x tokens,
 // then one block per token for route + activation quantization. The logits
 // are dotF32 (ggml.zig:198) in the same order as the decode router, and the
 // route is router_tail's, so every path routes identically.
-constexpr int RB_WARPS = 16, RB_TOK = 16;
+constexpr int RB_WARPS = 16, RB_TOK = 4;
 
 static int rb_experts(int dim) {  // router rows a CTA keeps in shared memory (<= RB_WARPS, ~190 KB)
-    int et = (int)((190 * 1024 - 2 * (size_t)dim * 4) / ((size_t)dim * 4));
+    int et = (int)((190 * 1024 - RB_TOK * (size_t)dim * 4) / ((size_t)dim * 4));
     return et < 1 ? 1 : et > RB_WARPS ? RB_WARPS : et;
+}
+
+// dotF32 order (as router_dot_smem_) for RB_TOK tokens at once: the warp's
+// lanes read each weight once and carry one accumulator per token
+__device__ __forceinline__ void router_dot_smem_tok(const float *wr, const float *x, int dim, int lane, int nt,
+                                                    float (&out)[RB_TOK]) {
+    float a[RB_TOK];
+#pragma unroll
+    for (int t = 0; t < RB_TOK; t++) a[t] = 0.0f;
+#pragma unroll 4
+    for (int i = lane; i < dim; i += 32) {
+        const float w = wr[i];
+#pragma unroll
+        for (int t = 0; t < RB_TOK; t++) a[t] = fadd(a[t], fmul(w, x[(size_t)t * dim + i]));
+    }
+#pragma unroll
+    for (int t = 0; t < RB_TOK; t++) {
+        const float a8 = __shfl_down_sync(0xffffffffu, a[t], 8);
+        const float a16 = __shfl_down_sync(0xffffffffu, a[t], 16);
+        const float a24 = __shfl_down_sync(0xffffffffu, a[t], 24);
+        const float v = fadd(fadd(fadd(a[t], a8), a16), a24);
+        float r = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+        for (int jj = 1; jj < 8; jj++) r = fadd(r, __shfl_sync(0xffffffffu, v, jj));
+        out[t] = r;
+    }
+    (void)nt;
 }
 
 __global__ void __launch_bounds__(RB_WARPS * 32) k_router_batch(DecodeArgs A, int et) {
@@ -687,33 +700,21 @@ __global__ void __launch_bounds__(RB_WARPS * 32) k_router_batch(DecodeArgs A, in
     const int e0 = blockIdx.x * et, t0 = blockIdx.y * RB_TOK;
     const int ne_here = ne - e0 < et ? ne - e0 : et;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float *rows = rbs, *xb = rbs + (size_t)et * dim;
+    float *rows = rbs, *xb = rbs + (size_t)et * dim;  // x: [RB_TOK][dim], zero past the last token
+    const int nt = A.T - t0 < RB_TOK ? A.T - t0 : RB_TOK;
     for (int i = threadIdx.x; i < ne_here * dim / 4; i += blockDim.x)
         reinterpret_cast<float4 *>(rows)[i] = __ldg(reinterpret_cast<const float4 *>(A.router + (size_t)e0 * dim) + i);
-    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
-        reinterpret_cast<float4 *>(xb)[i] = __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)t0 * dim) + i);
+    for (int i = threadIdx.x; i < RB_TOK * dim / 4; i += blockDim.x)
+        reinterpret_cast<float4 *>(xb)[i] = i < nt * dim / 4
+            ? __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)t0 * dim) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
-    for (int tt = 0; tt < RB_TOK && t0 + tt < A.T; tt++) {
-        const int t = t0 + tt;
-        float4 nx[4];  // the next token's x, in flight while this one is dotted
-        const bool more = tt + 1 < RB_TOK && t + 1 < A.T;
+    if (warp < ne_here) {
+        float r[RB_TOK];
+        router_dot_smem_tok(rows + (size_t)warp * dim, xb, dim, lane, nt, r);
+        if (lane == 0)
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int i = threadIdx.x + j * blockDim.x;
-            if (more && i < dim / 4) nx[j] = __ldg(reinterpret_cast<const float4 *>(A.x + (size_t)(t + 1) * dim) + i);
-        }
-        const float *xs = xb + (size_t)(tt & 1) * dim;
-        if (warp < ne_here) {
-            const float r = router_dot_smem_(rows + (size_t)warp * dim, xs, dim, lane);
-            if (lane == 0) A.logits[(size_t)t * ne + e0 + warp] = r;
-        }
-        if (more)
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int i = threadIdx.x + j * blockDim.x;
-                if (i < dim / 4) reinterpret_cast<float4 *>(xb + (size_t)((tt + 1) & 1) * dim)[i] = nx[j];
-            }
-        __syncthreads();
+            for (int t = 0; t < RB_TOK; t++)
+                if (t < nt) A.logits[(size_t)(t0 + t) * ne + e0 + warp] = r[t];
     }
 }
 
@@ -773,7 +774,7 @@ static cudaError_t launch_router(const DecodeArgs &A, cudaStream_t st) {
     }
     if (A.router && A.T > 16 && A.dim % 32 == 0 && A.dim <= 8192 && !A.trace_reg) {  // batch router
         const int et = rb_experts(A.dim);
-        const size_t smem = ((size_t)et + 2) * A.dim * 4;
+        const size_t smem = ((size_t)et + RB_TOK) * A.dim * 4;
         cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         if ((e = launch_pdl(k_router_batch, dim3(cdivu(A.n_expert, et), cdivu(A.T, RB_TOK)), dim3(RB_WARPS * 32), smem,
@@ -860,15 +861,15 @@ __global__ void __launch_bounds__(512) k_group(DecodeArgs A) {
             A.grp_off[e] = o;
             A.grp_cnt[e] = cnt[e];
             o += cnt[e];
-            if (A.tc_pre) {
+            if (A.tc_pre && A.tc_chunk) {
                 A.tc_pre[e] = c;
-                c += (cnt[e] + MOE_TC_N - 1) / MOE_TC_N;
+                c += (cnt[e] + A.tc_chunk - 1) / A.tc_chunk;
             }
         }
-        if (A.tc_pre) {
+        if (A.tc_pre && A.tc_chunk) {
             if (A.has_shared) {
                 A.tc_pre[A.n_local] = c;
-                c += (A.T + MOE_TC_N - 1) / MOE_TC_N;
+                c += (A.T + A.tc_chunk - 1) / A.tc_chunk;
             }
             A.tc_pre[A.n_local + (A.has_shared ? 1 : 0)] = c;
         }
@@ -1082,12 +1083,15 @@ static cudaError_t launch_quant_grp(const DecodeArgs &A, cudaStream_t st) {
     return launch_pdl(k_quant_grp, dim3(n_slots), dim3(128), 0, st, A);
 }
 
-cudaError_t launch_batch(const DecodeArgs &A, bool mma, cudaStream_t st) {
+cudaError_t launch_batch(const DecodeArgs &A0, int path, cudaStream_t st) {
+    DecodeArgs A = A0;
+    A.tc_chunk = path == BATCH_MMA ? MOE_TC_N : path == BATCH_DP4A ? MOE_DP_CH : 0;
     cudaError_t e = launch_router(A, st);
     if (e != cudaSuccess) return e;
     if ((e = launch_pdl(k_group, dim3(1), dim3(512), 0, st, A)) != cudaSuccess) return e;
-    if (mma) {
-        if ((e = launch_moe_mma(A, st, launch_quant_grp)) != cudaSuccess) return e;
+    if (path == BATCH_MMA || path == BATCH_DP4A) {
+        if ((e = (path == BATCH_MMA ? launch_moe_mma : launch_moe_dp4a)(A, st, launch_quant_grp)) != cudaSuccess)
+            return e;
         return launch_pdl(k_combine, dim3(cdivu(A.dim, 256), A.T), dim3(256), 0, st, A);
     }
     const int nexp = A.n_local + (A.has_shared ? 1 : 0);

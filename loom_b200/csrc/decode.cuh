@@ -47,7 +47,8 @@ struct DecodeArgs {
     int *grp_cnt;            // [n_local] slots per local expert
     int *grp_off;            // [n_local] first position in grp_list
     int *grp_list;           // [T*n_used] routed slots, grouped by expert, slot order within a group
-    int *tc_pre;             // [n_local + 2] tensor-core path: chunks of MOE_TC_N slots before each expert
+    int *tc_pre;             // [n_local + 2] tiled expert kernels: chunks of tc_chunk slots before each expert
+    int tc_chunk;            // slots per tile of the tiled expert kernels (0: none)
     float *y;                // [n_slots][dim] per-slot down outputs
     int trace_reg;           // test hook: use the register-staged router instead of the TMA one
     int *err;                // device error word (bounded waits that timed out), or null
@@ -65,10 +66,16 @@ cudaError_t launch_decode(const DecodeArgs &A, cudaStream_t st);
 // every token of the expert against one read of its rows, activation
 // quantization, down per expert, ordered combine.
 bool batch_supported(const DecodeArgs &A);
-// mma: gate/up and down as tcgen05 bf16 GEMMs (moe_mma_supported) instead of
-// the int8 dot kernels
-cudaError_t launch_batch(const DecodeArgs &A, bool mma, cudaStream_t st);
+// path: BATCH_GRP the int8 dot kernels per expert, BATCH_MMA gate/up and down
+// on the tensor cores (moe_mma_supported), BATCH_DP4A the tiled dp4a kernels
+// (moe_dp4a_supported)
+enum { BATCH_GRP = 2, BATCH_MMA = 3, BATCH_DP4A = 4 };
+cudaError_t launch_batch(const DecodeArgs &A, int path, cudaStream_t st);
 bool moe_mma_supported(const DecodeArgs &A);
+bool moe_dp4a_supported(const DecodeArgs &A);
+constexpr int MOE_DP_CH = 16;  // slots per dp4a tile
+cudaError_t launch_moe_dp4a(const DecodeArgs &A, cudaStream_t st,
+                            cudaError_t (*quant)(const DecodeArgs &, cudaStream_t));
 constexpr int MOE_TC_N = 64;  // slots per tensor-core tile
 // Largest |scale| of a Q6_K scales region (nblk x 16 int8); synchronises st. -1 on error.
 int q6k_max_scale(const uint8_t *sc, uint64_t nblk, int *d_tmp, cudaStream_t st);

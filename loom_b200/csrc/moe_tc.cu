@@ -95,8 +95,9 @@ struct TcTile {
     bool shared;
 };
 
-// Tile t of this launch (RT row tiles per expert); false past the last tile.
-__device__ __forceinline__ bool tc_tile(const DecodeArgs &A, int RT, int t, TcTile &o) {
+// Tile t of this launch (RT row tiles per expert, CH slots per token chunk);
+// false past the last tile.
+__device__ __forceinline__ bool tc_tile(const DecodeArgs &A, int RT, int t, TcTile &o, int CH = TC_N) {
     const int nexp = A.n_local + (A.has_shared ? 1 : 0);
     const int *pre = A.tc_pre;
     if (t >= pre[nexp] * RT) return false;
@@ -110,9 +111,9 @@ __device__ __forceinline__ bool tc_tile(const DecodeArgs &A, int RT, int t, TcTi
     o.e = lo;
     o.shared = lo == A.n_local;
     o.rt = loc / nch;
-    o.c0 = (loc % nch) * TC_N;
+    o.c0 = (loc % nch) * CH;
     const int n = o.shared ? A.T : A.grp_cnt[lo];
-    o.nc = n - o.c0 < TC_N ? n - o.c0 : TC_N;
+    o.nc = n - o.c0 < CH ? n - o.c0 : CH;
     return true;
 }
 
@@ -835,3 +836,376 @@ int loom_cuda_tc_profile(int enable, unsigned long long *out, size_t n) {
     memcpy(out, h, std::min(n, (size_t)(2 * TC_PROF_SLOTS)) * 8);
     return 0;
 }
+
+namespace loom {
+
+// ==== expert FFN of small batches with dp4a (a few tokens per expert) ======================
+// The same tiles and staging as the tensor-core kernels (TMA 2D weight boxes
+// of 128 rows per super-block, bulk copies of the tile's token rows, a
+// 2-stage ring), but the dots run on the integer pipes: each compute thread
+// owns one weight row, unpacks each super-block once into int8 words and
+// dots it with every token of the tile by dp4a, exactly the reference's
+// integer arithmetic (ggml.zig kBlockDot :1002; Q4_K I = sum_j sc_j (q . x)_j
+// and M = sum_j mn_j bs_j, Q6_K I = sum_j sc_j ((q . x)_j - 32 s_j)), then its
+// float tail per block, accumulated in block order. Two CTAs per SM.
+//
+// Roles (288 threads): warps 0-7 compute (gate/up: thread = (matrix, row),
+// all tokens; down: thread = (token half, row)), warp 8 the producer.
+// Tiles hold up to DP_CH tokens of one expert.
+constexpr int DP_CH = MOE_DP_CH;        // tokens per tile
+constexpr int DP_CWARPS = 8, DP_THREADS = (DP_CWARPS + 1) * 32;
+constexpr int DP_RS = 2;
+
+template <int FMT> struct DpLayout {
+    static constexpr int MATS = FMT == 0 ? 2 : 1;
+    static constexpr size_t RAW_W = FMT == 0 ? (size_t)2 * 128 * 144 : (size_t)128 * 192 + 128 * 16;
+    static constexpr size_t RAW = RAW_W + (size_t)DP_CH * 256;        // + the tokens' int8 rows of the block
+    static constexpr size_t TOKW = FMT == 0 ? 12 : 20;               // words per token per block: xd, sums
+    static constexpr size_t TOK = (size_t)DP_CH * TOKW * 4;
+    static constexpr size_t XCHG = FMT == 0 ? (size_t)256 * DP_CH * 4 : 0;  // gate/up: the accumulators [token][thread]
+    static constexpr size_t SMEM = DP_RS * (RAW + TOK) + XCHG;
+};
+
+struct DpBars {
+    uint64_t full[DP_RS], empty[DP_RS];
+    int err;
+};
+
+template <int FMT, int NB>
+__global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const __grid_constant__ TcMaps M) {
+    using Ly = DpLayout<FMT>;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    extern __shared__ __align__(1024) uint8_t sm[];
+    __shared__ DpBars B;
+    uint8_t *raw = sm, *tokb = sm + DP_RS * Ly::RAW;
+    float *xchg = reinterpret_cast<float *>(tokb + DP_RS * Ly::TOK);
+    const int R = FMT == 0 ? A.ffn : A.dim, RT = (R + 127) / 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int dim = A.dim, stride = A.act_stride;
+    {
+        TcTile t0;
+        if (!tc_tile(A, RT, blockIdx.x, t0, DP_CH)) return;
+    }
+    if (tid == 0) {
+        for (int i = 0; i < DP_RS; i++) {
+            mbar_init(&B.full[i], 1);
+            mbar_init(&B.empty[i], DP_CWARPS);
+        }
+        B.err = 0;
+    }
+    __syncthreads();
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {  // one lane waits; the verdict is the warp's
+        int ok = 1;
+        if (lane == 0) {
+            ok = !*reinterpret_cast<volatile int *>(&B.err) && mbar_wait(bar, parity, TC_POLLS);
+            if (!ok) {
+                *reinterpret_cast<volatile int *>(&B.err) = 1;
+                if (A.err) atomicOr(A.err, 64);
+            }
+        }
+        return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    };
+
+    if (warp == DP_CWARPS) {
+        // ---- producer ----------------------------------------------------------------------
+        uint32_t gb = 0;
+        bool run = true;
+        TcTile tl;
+        for (int ti = blockIdx.x; run && tc_tile(A, RT, ti, tl, DP_CH); ti += gridDim.x) {
+            const int row0 = tl.rt * 128;
+            const int8_t *src = nullptr;  // this lane's token row (i = lane)
+            if (lane < tl.nc) {
+                const int slot = tc_slot(A, tl, lane);
+                src = FMT == 0 ? A.x256.q + (size_t)(tl.shared ? tl.c0 + lane : slot / A.n_used) * dim
+                               : A.aq + (size_t)slot * stride;
+            }
+            for (int blk = 0; blk < NB; blk++, gb++) {
+                const int s = gb % DP_RS;
+                if (gb >= DP_RS && !wait(&B.empty[s], ((gb / DP_RS) - 1) & 1)) {
+                    run = false;
+                    break;
+                }
+                uint8_t *W = raw + (size_t)s * Ly::RAW, *X = W + Ly::RAW_W;
+                if (lane == 0) {
+                    mbar_expect_tx(&B.full[s], (uint32_t)Ly::RAW_W + (uint32_t)tl.nc * 256);
+                    const int y = (tl.shared ? 0 : tl.e * R) + row0, m0 = tl.shared ? 2 : 0;
+                    if (FMT == 0) {
+                        tma_load_2d(W, &M.m[m0], blk * 144, y, &B.full[s]);
+                        tma_load_2d(W + 128 * 144, &M.m[m0 + 1], blk * 144, y, &B.full[s]);
+                    } else {
+                        tma_load_2d(W, &M.m[m0], blk * 192, y, &B.full[s]);
+                        tma_load_2d(W + 128 * 192, &M.m[m0 + 1], blk * 16, y, &B.full[s]);
+                    }
+                }
+                __syncwarp();
+                if (src) bulk_g2s(X + (size_t)lane * 256, src + blk * 256, 256, &B.full[s]);
+            }
+        }
+        if (lane == 0 && !run)  // the last stages' copies must land before the CTA can exit
+            for (uint32_t g = gb > DP_RS ? gb - DP_RS : 0; g < gb; g++)
+                mbar_wait(&B.full[g % DP_RS], (g / DP_RS) & 1, TC_POLLS);
+    } else {
+        // ---- compute ----------------------------------------------------------------------
+        const int r = tid & 127, hi = tid >> 7;  // FMT 0: hi = matrix; FMT 1: hi = token half
+        uint32_t gb = 0;
+        TcTile tl;
+        for (int ti = blockIdx.x; tc_tile(A, RT, ti, tl, DP_CH); ti += gridDim.x) {
+            const int row0 = tl.rt * 128, rows = R - row0 < 128 ? R - row0 : 128;
+            // this thread's token (tid < nc): its slot, for the per-block scalars and the stores
+            const int my_slot = tid < tl.nc ? tc_slot(A, tl, tid) : 0;
+            const size_t my_tok = tl.shared ? (size_t)(tl.c0 + tid) : (size_t)(my_slot / A.n_used);
+            float acc[FMT == 0 ? 1 : DP_CH / 2];  // down: in registers; gate/up: in shared memory (xchg)
+#pragma unroll
+            for (int i = 0; i < (FMT == 0 ? 1 : DP_CH / 2); i++) acc[i] = 0.0f;
+            if (FMT == 0)
+#pragma unroll
+                for (int i = 0; i < DP_CH; i++) xchg[i * 256 + tid] = 0.0f;
+            bool run = true;
+            for (int blk = 0; blk < NB; blk++, gb++) {
+                const int s = gb % DP_RS;
+                if (!wait(&B.full[s], (gb / DP_RS) & 1)) {
+                    run = false;
+                    break;
+                }
+                // the tokens' per-block scalars into the stage's token words
+                uint32_t *TK = reinterpret_cast<uint32_t *>(tokb + (size_t)s * Ly::TOK);
+                if (tid < tl.nc) {
+                    uint32_t *tw = TK + (size_t)tid * Ly::TOKW;
+                    if (FMT == 0) {
+                        tw[0] = __float_as_uint(A.x256.d[my_tok * NB + blk]);
+                        const int4 *ss = reinterpret_cast<const int4 *>(A.x256.s + (my_tok * NB + blk) * 16);
+                        uint32_t lo[2] = {0, 0}, hb[2] = {0, 0};
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; k4++) {  // per-32 sums bs = 256 hi + lo (lo unsigned, hi signed bytes)
+                            const int4 v = ss[k4];
+                            const int b0 = v.x + v.y, b1 = v.z + v.w, k = 2 * k4;
+                            lo[k >> 2] |= (uint32_t)(b0 & 0xFF) << (8 * (k & 3));
+                            hb[k >> 2] |= (uint32_t)((b0 >> 8) & 0xFF) << (8 * (k & 3));
+                            lo[(k + 1) >> 2] |= (uint32_t)(b1 & 0xFF) << (8 * ((k + 1) & 3));
+                            hb[(k + 1) >> 2] |= (uint32_t)((b1 >> 8) & 0xFF) << (8 * ((k + 1) & 3));
+                        }
+                        tw[4] = lo[0];
+                        tw[5] = lo[1];
+                        tw[6] = hb[0];
+                        tw[7] = hb[1];
+                    } else {
+                        tw[0] = __float_as_uint(A.ad[(size_t)my_slot * (stride / 32) + blk]);
+                        const int4 *ss = reinterpret_cast<const int4 *>(A.as + (size_t)my_slot * (stride / 16) + blk * 16);
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; k4++) *reinterpret_cast<int4 *>(tw + 4 + 4 * k4) = ss[k4];
+                    }
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(DP_CWARPS * 32) : "memory");
+                const uint8_t *W = raw + (size_t)s * Ly::RAW;
+                const int8_t *X = reinterpret_cast<const int8_t *>(W + Ly::RAW_W);
+                if (FMT == 0) {
+                    const uint8_t *wr = W + (size_t)(hi * 128 + r) * 144;
+                    const uint4 hd = *reinterpret_cast<const uint4 *>(wr);
+                    const float d = f16_to_f32((uint16_t)(hd.x & 0xFFFF)), dmin = f16_to_f32((uint16_t)(hd.x >> 16));
+                    // scaleMinK4 for all 8 sub-blocks at once, as bytes: scales s0 (0-3), s1 (4-7); mins m0, m1
+                    const uint32_t s0 = hd.y & 0x3F3F3F3Fu;
+                    const uint32_t s1 = (hd.w & 0x0F0F0F0Fu) | (((hd.y >> 6) & 0x03030303u) << 4);
+                    const uint32_t m0 = hd.z & 0x3F3F3F3Fu;
+                    const uint32_t m1 = ((hd.w >> 4) & 0x0F0F0F0Fu) | (((hd.z >> 6) & 0x03030303u) << 4);
+#pragma unroll
+                    for (int g = 0; g < DP_CH / 8; g++) {
+                        if (8 * g >= tl.nc) break;  // uniform
+                        int isum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {  // sub-blocks 2j (low nibbles), 2j + 1 (high)
+                            const uint4 q0 = *reinterpret_cast<const uint4 *>(wr + 16 + 32 * j);
+                            const uint4 q1 = *reinterpret_cast<const uint4 *>(wr + 32 + 32 * j);
+                            const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                            const uint32_t sw = j < 2 ? s0 : s1;
+                            const int sca = (int)((sw >> (16 * (j & 1))) & 0xFF), scb = (int)((sw >> (16 * (j & 1) + 8)) & 0xFF);
+                            int lo[8], hv[8];
+#pragma unroll
+                            for (int w = 0; w < 8; w++) {
+                                lo[w] = (int)(qw[w] & 0x0F0F0F0Fu);
+                                hv[w] = (int)((qw[w] >> 4) & 0x0F0F0F0Fu);
+                            }
+#pragma unroll
+                            for (int t = 0; t < 8; t++) {
+                                const int i = 8 * g + t;
+                                if (i < tl.nc) {
+                                    const int4 *xp = reinterpret_cast<const int4 *>(X + (size_t)i * 256 + 64 * j);
+                                    const int4 x0 = xp[0], x1 = xp[1], x2 = xp[2], x3 = xp[3];
+                                    int a = 0, b = 0;
+                                    a = __dp4a(lo[0], x0.x, a); a = __dp4a(lo[1], x0.y, a);
+                                    a = __dp4a(lo[2], x0.z, a); a = __dp4a(lo[3], x0.w, a);
+                                    a = __dp4a(lo[4], x1.x, a); a = __dp4a(lo[5], x1.y, a);
+                                    a = __dp4a(lo[6], x1.z, a); a = __dp4a(lo[7], x1.w, a);
+                                    b = __dp4a(hv[0], x2.x, b); b = __dp4a(hv[1], x2.y, b);
+                                    b = __dp4a(hv[2], x2.z, b); b = __dp4a(hv[3], x2.w, b);
+                                    b = __dp4a(hv[4], x3.x, b); b = __dp4a(hv[5], x3.y, b);
+                                    b = __dp4a(hv[6], x3.z, b); b = __dp4a(hv[7], x3.w, b);
+                                    isum[t] += sca * a + scb * b;
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int t = 0; t < 8; t++) {
+                            const int i = 8 * g + t;
+                            if (i < tl.nc) {
+                                const uint32_t *tw = TK + (size_t)i * Ly::TOKW;
+                                // mins term M = sum_j mn_j bs_j through dp4a on bs = 256 hi + lo (exact)
+                                const int Mi = (int)__dp4a(m0, tw[4], __dp4a(m1, tw[5], 0u)) +
+                                               256 * dp4a_us(m0, (int)tw[6], dp4a_us(m1, (int)tw[7], 0));
+                                const float xd = __uint_as_float(tw[0]);
+                                float &a = xchg[i * 256 + tid];
+                                a = fadd(a, fmul(xd, fsub(fmul(d, (float)isum[t]), fmul(dmin, (float)Mi))));
+                            }
+                        }
+                    }
+                } else {
+                    const uint8_t *wr = W + (size_t)r * 192;
+                    const int8_t *scb = reinterpret_cast<const int8_t *>(W + 128 * 192 + (size_t)r * 16);
+                    float d = 0.0f;
+                    if (r < rows) {
+                        const WDev w = tl.shared ? A.sdn : A.dn;
+                        const uint64_t pl = tl.shared ? 0 : (uint64_t)tl.e * R * NB;
+                        d = f16_to_f32(w.d[pl + (uint64_t)(row0 + r) * NB + blk]);
+                    }
+#pragma unroll
+                    for (int g = 0; g < DP_CH / 16; g++) {  // this thread's tokens: DP_CH / 2 * hi + 8 g + t
+                        const int i0 = DP_CH / 2 * hi + 8 * g;
+                        if (i0 >= tl.nc) break;  // uniform per warp
+                        int isum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+                        for (int n = 0; n < 2; n++) {  // halves of 128 values
+                            const uint4 h0 = *reinterpret_cast<const uint4 *>(wr + 128 + 32 * n);
+                            const uint4 h1 = *reinterpret_cast<const uint4 *>(wr + 128 + 32 * n + 16);
+                            const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+                            for (int gg = 0; gg < 4; gg++) {  // 32 values 128 n + 32 gg + l
+                                const uint4 l0 = *reinterpret_cast<const uint4 *>(wr + 64 * n + 32 * (gg & 1));
+                                const uint4 l1 = *reinterpret_cast<const uint4 *>(wr + 64 * n + 32 * (gg & 1) + 16);
+                                const uint32_t ql[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+                                int qv[8];
+#pragma unroll
+                                for (int w = 0; w < 8; w++)
+                                    qv[w] = (int)((((gg >> 1) ? ql[w] >> 4 : ql[w]) & 0x0F0F0F0Fu) |
+                                                  (((qh[w] >> (2 * gg)) & 0x03030303u) << 4));
+                                const int s0 = scb[8 * n + 2 * gg], s1 = scb[8 * n + 2 * gg + 1];
+#pragma unroll
+                                for (int t = 0; t < 8; t++) {
+                                    const int i = i0 + t;
+                                    if (i < tl.nc) {
+                                        const int4 *xp = reinterpret_cast<const int4 *>(X + (size_t)i * 256 + 128 * n + 32 * gg);
+                                        const int4 x0 = xp[0], x1 = xp[1];
+                                        int a = 0, b = 0;
+                                        a = __dp4a(qv[0], x0.x, a); a = __dp4a(qv[1], x0.y, a);
+                                        a = __dp4a(qv[2], x0.z, a); a = __dp4a(qv[3], x0.w, a);
+                                        b = __dp4a(qv[4], x1.x, b); b = __dp4a(qv[5], x1.y, b);
+                                        b = __dp4a(qv[6], x1.z, b); b = __dp4a(qv[7], x1.w, b);
+                                        const uint32_t *tw = TK + (size_t)i * Ly::TOKW + 4;  // per-16 sums
+                                        const int k = 8 * n + 2 * gg;
+                                        isum[t] += s0 * (a - 32 * (int)tw[k]) + s1 * (b - 32 * (int)tw[k + 1]);
+                                    }
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int t = 0; t < 8; t++) {
+                            const int i = i0 + t;
+                            if (i < tl.nc) {
+                                const float xd = __uint_as_float(TK[(size_t)i * Ly::TOKW]);
+                                acc[8 * g + t] = fadd(acc[8 * g + t], fmul(fmul(xd, d), (float)isum[t]));
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) tc_arrive(&B.empty[s]);
+            }
+            if (!run) break;
+            if (FMT == 0) {  // act = silu(gate) * up, the up row's sums from thread 128 + r
+                asm volatile("bar.sync 1, %0;" ::"r"(DP_CWARPS * 32) : "memory");
+                if (hi == 0 && r < rows)
+#pragma unroll
+                    for (int i = 0; i < DP_CH; i++) {
+                        if (i >= tl.nc) break;
+                        const int slot = tc_slot(A, tl, i);
+                        const float g = xchg[i * 256 + r], u = xchg[i * 256 + 128 + r];
+                        A.act[(size_t)slot * stride + row0 + r] = fmul(fdiv(g, fadd(1.0f, expf(-g))), u);
+                    }
+                asm volatile("bar.sync 1, %0;" ::"r"(DP_CWARPS * 32) : "memory");  // xchg zeroed by the next tile
+            } else if (r < rows) {
+#pragma unroll
+                for (int k = 0; k < DP_CH / 2; k++) {
+                    const int i = DP_CH / 2 * hi + k;
+                    if (i >= tl.nc) break;
+                    A.y[(size_t)tc_slot(A, tl, i) * dim + row0 + r] = acc[k];
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+using DpFn = void (*)(DecodeArgs, TcMaps);
+
+static DpFn dp_gu_fn(int nb) {
+    switch (nb) {
+        case 4: return k_moe_dp4a<0, 4>;
+        case 8: return k_moe_dp4a<0, 8>;
+        case 16: return k_moe_dp4a<0, 16>;
+        case 28: return k_moe_dp4a<0, 28>;
+    }
+    return nullptr;
+}
+static DpFn dp_dn_fn(int nb) {
+    switch (nb) {
+        case 2: return k_moe_dp4a<1, 2>;
+        case 3: return k_moe_dp4a<1, 3>;
+        case 4: return k_moe_dp4a<1, 4>;
+        case 8: return k_moe_dp4a<1, 8>;
+    }
+    return nullptr;
+}
+
+bool moe_dp4a_supported(const DecodeArgs &A) {
+    if (A.g.type != T_Q4_K || A.u.type != T_Q4_K || A.dn.type != T_Q6_K) return false;
+    if (A.dim % 256 || A.ffn % 256 || A.n_local + 1 > 1024) return false;
+    if (!dp_gu_fn(A.dim / 256) || !dp_dn_fn(A.ffn / 256) || !tc_encoder()) return false;
+    if (A.has_shared && (A.sg.type != T_Q4_K || A.su.type != T_Q4_K || A.sdn.type != T_Q6_K || A.shexp_ffn != A.ffn))
+        return false;
+    return true;
+}
+
+cudaError_t launch_moe_dp4a(const DecodeArgs &A, cudaStream_t st, cudaError_t (*quant)(const DecodeArgs &, cudaStream_t)) {
+    static int n_sm = 0;
+    if (!n_sm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (n_sm <= 0) n_sm = 148;
+    }
+    DpFn gf = dp_gu_fn(A.dim / 256), df = dp_dn_fn(A.ffn / 256);
+    const int nbg = A.dim / 256, nbd = A.ffn / 256;
+    TcMaps mg, md;
+    memset(&mg, 0, sizeof mg);
+    memset(&md, 0, sizeof md);
+    const uint64_t gr = (uint64_t)A.n_local * A.ffn, dr = (uint64_t)A.n_local * A.dim;
+    bool ok = tc_map(mg.m[0], A.g.q, nbg * 144ull, gr, 144) && tc_map(mg.m[1], A.u.q, nbg * 144ull, gr, 144) &&
+              tc_map(md.m[0], A.dn.q, nbd * 192ull, dr, 192) && tc_map(md.m[1], A.dn.sc, nbd * 16ull, dr, 16);
+    if (ok && A.has_shared)
+        ok = tc_map(mg.m[2], A.sg.q, nbg * 144ull, (uint64_t)A.shexp_ffn, 144) &&
+             tc_map(mg.m[3], A.su.q, nbg * 144ull, (uint64_t)A.shexp_ffn, 144) &&
+             tc_map(md.m[2], A.sdn.q, nbd * 192ull, (uint64_t)A.dim, 192) &&
+             tc_map(md.m[3], A.sdn.sc, nbd * 16ull, (uint64_t)A.dim, 16);
+    if (!ok) return cudaErrorInvalidValue;
+    constexpr size_t gs = DpLayout<0>::SMEM, ds = DpLayout<1>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(gf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(df, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ds);
+    if (e != cudaSuccess) return e;
+    count_launch();
+    gf<<<2 * n_sm, DP_THREADS, gs, st>>>(A, mg);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = quant(A, st)) != cudaSuccess) return e;
+    count_launch();
+    df<<<2 * n_sm, DP_THREADS, ds, st>>>(A, md);
+    return cudaGetLastError();
+}
+
+}  // namespace loom

@@ -325,13 +325,26 @@ constexpr size_t DECODE_MAX_T = 16;
 // T = 2 decode 1.86 ms vs batch 2.15 ms per 48 layers, T = 4 3.13 vs 2.51).
 constexpr size_t DECODE_AUTO_T = 2;
 
-int g_force_generic = 0;  // test hook: 0 auto, 1 slot kernels, 2 batch kernels, 3 batch on the tensor cores
+int g_force_generic = 0;  // test hook: 0 auto, 1 slot kernels, 2 int8 batch kernels, 3 tensor cores, 4 dp4a tiles
 int g_last_path = -1;      // kernel family of the last routed layer (loom_cuda_last_path)
 const uint8_t *g_next_router = nullptr;  // L2-prefetch hint for the layer being launched
 size_t g_next_router_bytes = 0;
 // phase trace: [2*n] (first start, last end) per traced kernel, see loom_cuda_trace_*
 unsigned long long *g_trace = nullptr;
 size_t g_trace_cap = 0, g_trace_next = 0;  // test hook: route every layer through the slot kernels
+
+// Kernel family of an expert-major batch layer with `slots` routed slots:
+// the tensor cores once the experts average 16 or more slots each (prefill),
+// else the tiled dp4a kernels, else the per-expert int8 kernels; the test
+// hook g_force_generic (2, 3, 4) selects one where the layer's types allow.
+int batch_path(const DecodeArgs &A, size_t slots, int n_local) {
+    if (g_force_generic == 2) return BATCH_GRP;
+    if (g_force_generic == 3) return moe_mma_supported(A) ? BATCH_MMA : BATCH_GRP;
+    if (g_force_generic == 4) return moe_dp4a_supported(A) ? BATCH_DP4A : BATCH_GRP;
+    if (moe_mma_supported(A) && slots >= 16 * (size_t)n_local) return BATCH_MMA;
+    if (moe_dp4a_supported(A)) return BATCH_DP4A;
+    return BATCH_GRP;
+}
 
 // Group-limited selection of a layer (DeepSeek-V3 routing): n_group 0 or 1 is
 // plain top-k; otherwise n_group <= 32 groups dividing n_expert, 1 <=
@@ -418,9 +431,7 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
             return 0;
         }
         if (batch_ok) {
-            // tensor cores once the experts average 16 or more tokens each (prefill)
-            const bool mma = moe_mma_supported(A) &&
-                             (g_force_generic == 3 || (g_force_generic == 0 && T * L.n_used >= 16 * (size_t)L.n_local));
+            const int path = batch_path(A, T * L.n_used, L.n_local);
             if (int rc = S.grp.ensure((3 * (size_t)L.n_local + T * L.n_used + 4) * 4)) return rc;
             if (int rc = S.ybuf.ensure(n_slots * (size_t)L.dim * 4)) return rc;
             A.grp_cnt = S.grp.as<int>();
@@ -428,8 +439,8 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
             A.grp_list = A.grp_off + L.n_local;
             A.tc_pre = A.grp_list + T * L.n_used;
             A.y = S.ybuf.as<float>();
-            g_last_path = mma ? 3 : 2;
-            CK(launch_batch(A, mma, st));
+            g_last_path = path;
+            CK(launch_batch(A, path, st));
             return 0;
         }
     }
@@ -1112,17 +1123,16 @@ int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t
         A.trace = nullptr;
         if (g_force_generic != 1 && batch_supported(A)) {
             // expert-major: each local expert's rows against one read of its weights
-            const bool mma = moe_mma_supported(A) &&
-                             (g_force_generic == 3 || (g_force_generic == 0 && nr >= 16 * (size_t)Lr.n_local));
+            const int path = batch_path(A, nr, Lr.n_local);
             if (int rc = S.grp.ensure((3 * (size_t)Lr.n_local + nr + 4) * 4)) return rc;
             if (int rc = S.ybuf.ensure(nr * dim * 4)) return rc;
             A.grp_cnt = S.grp.as<int>();
             A.grp_off = A.grp_cnt + Lr.n_local;
             A.grp_list = A.grp_off + Lr.n_local;
             A.tc_pre = A.grp_list + nr;
-            g_last_path = mma ? 3 : 2;
+            g_last_path = path;
             A.y = S.ybuf.as<float>();
-            CK(launch_batch(A, mma, st));
+            CK(launch_batch(A, path, st));
         } else {  // per-row slot kernels
             launch_a2a_fill(S.a2a_g1.as<float>(), (int)nr, 1.0f, st);
             quantize_inputs(S.a2a_rx.as<float>(), nr, dim, any_type(Lr, true), any_type(Lr, false), st);

@@ -117,3 +117,21 @@ def test_mma_declines_large_q6k_scales(be, orc):
     a, ia = _run(L, x, 3, k, path=2)
     b, ib = _run(L, x, 2, k, path=2)
     assert np.array_equal(ia, ib) and np.array_equal(bits(a), bits(b))
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(ne=40, k=4, dim=1024, ffn=512, gt=12, dt=14),
+    dict(ne=40, k=4, dim=1024, ffn=512, gt=12, dt=14, shared=512, gating=2, scale=2.5, bias=True),
+    dict(ne=128, k=8, dim=2048, ffn=768, gt=12, dt=14),
+], ids=["small", "shared", "qwen3"])
+@pytest.mark.parametrize("T", [1, 3, 16, 64, 200])
+def test_dp4a_tiles_match_int8_batch(be, orc, cfg, T):
+    """The tiled dp4a kernels (16-token tiles, one thread per weight row)
+    equal the per-expert int8 kernels bit for bit, including experts with more
+    than one tile of tokens and a shared expert."""
+    L = _layer_case(orc, 61, **cfg)
+    x = torch.from_numpy(orc.synth(0, T * cfg["dim"], seed=612, sigma=1.0).reshape(T, cfg["dim"])).cuda()
+    a, ia = _run(L, x, 4, cfg["k"], path=4)
+    b, ib = _run(L, x, 2, cfg["k"], path=2)
+    assert np.array_equal(ia, ib)
+    assert np.array_equal(bits(a), bits(b)), rel_l2(a, b)
