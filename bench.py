@@ -303,9 +303,12 @@ def run_gpu(args):
 
     # e2e through the seam with host buffers
     e2e = None
-    prefill = None
+    prefill = batch = None
     if args.prefill_tokens > 0 and not ep:
         prefill = run_prefill(args, layers, stream, torch, D)
+        if args.batch_tokens > 0:
+            batch = run_prefill(args, layers, stream, torch, D, T=args.batch_tokens,
+                                label=f"decode batch {args.batch_tokens} (one step of {args.batch_tokens} streams)")
     e2e_device = None
     if args.e2e_layers > 0 and not ep:
         e2e = run_e2e(args, B)
@@ -353,6 +356,8 @@ def run_gpu(args):
         line["e2e_device"] = e2e_device
     if prefill:
         line["prefill"] = prefill
+    if batch:
+        line["batch"] = batch
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
@@ -417,11 +422,12 @@ def trace_phases(D, step, stream, torch):
     }
 
 
-def run_prefill(args, layers, stream, torch, D):
-    """Prefill: args.prefill_tokens tokens through the same layers on the
-    expert-major batch path (the experts average >= 16 tokens, so gate/up
-    and down run as tcgen05 MMAs), captured in one CUDA graph."""
-    T = args.prefill_tokens
+def run_prefill(args, layers, stream, torch, D, T=None, label="prefill"):
+    """T tokens (default --prefill-tokens) through the same layers on the
+    expert-major batch path, captured in one CUDA graph: a prefill (the
+    experts average >= 16 tokens, so gate/up and down run as tcgen05 MMAs) or
+    a batched decode step (the tiled dp4a kernels)."""
+    T = args.prefill_tokens if T is None else T
     D.reserve(T, DIM, FFN, NE, NK)
     x0 = torch.from_numpy(np.random.default_rng(7).standard_normal((T, DIM)).astype(np.float32)).cuda()
     bufs = [torch.empty((T, DIM), device="cuda") for _ in range(2)]
@@ -461,9 +467,12 @@ def run_prefill(args, layers, stream, torch, D):
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
     gbs = bytes_step / (ms * 1e-3) / 1e9
     tfs = flops / (ms * 1e-3) / 1e12
-    return {"tokens": T, "layers": LAYERS, "value": round(T / (ms * 1e-3), 1), "unit": "tok/s",
+    path = {0: "fused decode kernels", 1: "slot kernels", 2: "per-expert int8 dot kernels",
+            3: "tcgen05 kind::f16 gate/up and down (integer-exact), warp-specialized",
+            4: "tiled dp4a gate/up and down (TMA-staged rows, integer-exact)"}.get(D.last_path(), "?")
+    return {"workload": label, "tokens": T, "layers": LAYERS, "value": round(T / (ms * 1e-3), 1), "unit": "tok/s",
             "ms_per_step": round(ms, 3), "steps": steps,
-            "engine": "expert-major batch: tiled router GEMV, tcgen05 kind::f16 gate/up and down (integer-exact)",
+            "engine": "expert-major batch: tiled router GEMV, " + path,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "bytes_per_step": bytes_step,
                          "tensor_tflops": round(tfs, 2), "tensor_peak": tpeak,
@@ -558,6 +567,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=512,
                     help="also time a prefill of this many tokens through the same layers (0: skip)")
+    ap.add_argument("--batch-tokens", type=int, default=32,
+                    help="also time one batched decode step of this many tokens (0: skip)")
     ap.add_argument("--engine", default="auto", choices=["auto", "layers", "stack"],
                     help="layers: per-layer kernels in a CUDA graph; stack: one persistent kernel for all layers "
                          "(T=1); auto: stack for unsharded T=1, else layers")
