@@ -50,8 +50,10 @@ struct WDev {
     int type;
     int pad_;           // flags (WDEV_*)
 };
-// Q6_K tensor whose int8 sub-block scales all satisfy |sc| <= 64, so that
-// sc * (q - 32) is an integer fp16 holds exactly (the tensor-core path)
+// Q6_K tensor whose int8 sub-block scales all satisfy |sc| <= 32: then
+// |sc * (q - 32)| <= 1024 is an integer fp16 holds exactly, and 128 of them
+// times int8 activations sum to less than 2^24 (exact in an f32 accumulator):
+// the tensor-core path's condition
 constexpr int WDEV_Q6K_SMALL_SCALES = 1;
 
 // Quantized activations for a batch of vectors, each `cols` wide:

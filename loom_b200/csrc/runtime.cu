@@ -152,14 +152,15 @@ int fill_from_raw_dev(Tensor &t, const uint8_t *raw_dev) {
     return 0;
 }
 
-// Q6_K: record whether every sub-block scale is within +-64 (the tensor-core
-// path folds sc * (q - 32) into fp16, exact only then). Synchronises g_stream.
+// Q6_K: record whether every sub-block scale is within +-32 (the tensor-core
+// path folds sc * (q - 32) into fp16 and sums 128 such products times int8
+// activations in f32: exact only then). Synchronises g_stream.
 int mark_q6k(Tensor &t) {
     if (t.type != T_Q6_K) return 0;
     if (int rc = S.tmp.ensure(64)) return rc;
     const int m = q6k_max_scale(t.w.sc, t.nblk, S.tmp.as<int>(), g_stream);
     if (m < 0) return fail("q6k scale scan", cudaGetLastError());
-    if (m <= 64) t.w.pad_ |= WDEV_Q6K_SMALL_SCALES;
+    if (m <= 32) t.w.pad_ |= WDEV_Q6K_SMALL_SCALES;
     return 0;
 }
 

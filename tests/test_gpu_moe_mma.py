@@ -103,9 +103,9 @@ def test_mma_token_counts(be, orc, T):
 
 
 def test_mma_declines_large_q6k_scales(be, orc):
-    """Q6_K down weights with a sub-block scale beyond +-64 (sc * (q - 32)
-    would round in fp16): the layer stays on the int8 kernels and still
-    matches them."""
+    """Q6_K down weights with a sub-block scale beyond +-32 (the fp16 fold and
+    its f32 sums would no longer be exact): the layer stays on the int8
+    kernels and still matches them."""
     ne, k, dim, ffn, T = 16, 4, 1024, 512, 128
     g, u, d = synth_layer(orc, 51, ne, dim, ffn, 12, 12, 14)
     d = d.copy()
