@@ -256,6 +256,17 @@ int loom_cuda_ep_size(void);
  * counts go to the host). Without loom_cuda_ep_init it runs as one rank. */
 int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
                              const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream);
+/* Greedy sampling (sampler.zig:7-15 argmax) of device logits into *d_index
+ * (device u32): the first maximum; NaN never taken; 0 when nothing is above
+ * -inf. Asynchronous on `stream`; calls on one device share a 16-byte scratch,
+ * so they must not run concurrently on different streams. */
+int loom_cuda_argmax(const float *d_logits, size_t n, uint32_t *d_index, void *stream);
+/* The output head of one token and its greedy sample (llama.zig:1225-1226,
+ * sampler.zig:7-15): logits[vocab] = W[vocab][dim] . x with the tensor's
+ * bit-exact matvec, then their argmax. d_logits may be NULL (library
+ * scratch). */
+int loom_cuda_lm_head_argmax(loom_tensor w, size_t vocab, size_t dim, const float *d_x, float *d_logits,
+                             uint32_t *d_index, void *stream);
 /* Device matvec/matmul on a device tensor: out[k*rows + r], device buffers. */
 int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,
                             void *stream);

@@ -514,3 +514,55 @@ void launch_experts_routed(const RoutedLayerDev &L, const int *ids, const float 
 }
 
 }  // namespace loom
+
+namespace loom {
+
+// ---- greedy sampling (sampler.zig:7-15 argmax) --------------------------------------
+// The reference scans with a strict '>' from -inf: the first maximum wins, NaN
+// is never taken, and nothing above -inf gives index 0. Here every value above
+// -inf becomes the 64-bit key (order key of the value, ~index): the largest
+// key is the largest value at its lowest index. Blocks fold their best key
+// into *slot with atomicMax; the last block to finish (counter) writes the
+// index and re-arms slot and counter for the next call.
+__global__ void __launch_bounds__(256) k_argmax(const float *v, int n, unsigned long long *slot, unsigned *count,
+                                                uint32_t *out) {
+    unsigned long long best = 0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float x = __ldg(v + i);
+        if (x > -INFINITY) {  // false for NaN and -inf
+            const unsigned long long k = ((unsigned long long)f32_order_key(x) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+            best = k > best ? k : best;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+        best = ob > best ? ob : best;
+    }
+    __shared__ unsigned long long wb[8];
+    __shared__ bool last;
+    if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = wb[w] > best ? wb[w] : best;
+        best = wb[0] > best ? wb[0] : best;
+        if (best) atomicMax(slot, best);
+        __threadfence();
+        last = atomicAdd(count, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        const unsigned long long k = atomicExch(slot, 0ull);
+        *out = k ? 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull) : 0u;
+        *count = 0;
+    }
+}
+
+void launch_argmax(const float *v, int n, unsigned long long *slot, unsigned *count, uint32_t *out, cudaStream_t st) {
+    const int grid = n <= 256 ? 1 : (n + 2047) / 2048 < 148 ? (n + 2047) / 2048 : 148;
+    k_argmax<<<grid, 256, 0, st>>>(v, n, slot, count, out);
+    count_launch();
+}
+
+}  // namespace loom

@@ -59,6 +59,10 @@ void launch_experts_routed(const RoutedLayerDev &L, const int *ids, const float 
                            const XQ &x256, const XQ &x32, float *act, int8_t *aq, float *ad, int32_t *as, float *out,
                            const float *residual, cudaStream_t st);
 
+// sampler.zig:7-15 argmax of v[0..n) into *out; slot / count: 16 zeroed bytes
+// of device scratch that the kernel leaves zeroed again
+void launch_argmax(const float *v, int n, unsigned long long *slot, unsigned *count, uint32_t *out, cudaStream_t st);
+
 // number of kernel launches issued by this library (host-side count)
 uint64_t launches();
 void count_launch();

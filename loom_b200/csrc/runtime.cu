@@ -120,6 +120,8 @@ struct Scratch {
     DBuf io_in, io_out, io_aux, raw;
     // all-to-all expert parallelism: home-side lists and rows, receive-side rows
     DBuf tmp;  // small synchronous scratch (tensor scans)
+    DBuf amax;  // argmax slot + counter (zeroed once, left zeroed by the kernel); lm_head logits
+    DBuf head_logits;
     DBuf a2a_i, a2a_sx, a2a_yb, a2a_ysh, a2a_rx, a2a_re, a2a_yr, a2a_g1;
     HBuf h_in, h_out, h_cnt;
 } S;
@@ -505,7 +507,7 @@ void loom_cuda_shutdown(void) {
     g_arenas.clear();
     for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
                     &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.grp, &S.ybuf, &S.io_in, &S.io_out, &S.io_aux, &S.raw, &S.a2a_i, &S.a2a_sx,
-                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1, &S.tmp}) {
+                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1, &S.tmp, &S.amax, &S.head_logits}) {
         if (b->p) cudaFree(b->p);
         b->p = nullptr;
         b->cap = 0;
@@ -1169,6 +1171,33 @@ int loom_cuda_tensor_matmul(loom_tensor h, size_t rows, size_t cols, const float
     }
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;
+}
+
+// sampler.zig:7-15 argmax on device logits.
+int loom_cuda_argmax(const float *d_logits, size_t n, uint32_t *d_index, void *stream) {
+    if (int rc = need_init()) return rc;
+    if (!d_logits || !d_index || n == 0 || n > 0x7FFFFFFFu) return decline("argmax needs 1 <= n < 2^31 logits");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    if (int rc = S.amax.ensure(16, true)) return rc;
+    launch_argmax(d_logits, (int)n, S.amax.as<unsigned long long>(), reinterpret_cast<unsigned *>(S.amax.as<uint8_t>() + 8),
+                  d_index, st);
+    CK(cudaGetLastError());
+    return LOOM_CUDA_OK;
+}
+
+// The output head and greedy sampling of one token (llama.zig:1225-1226 +
+// sampler.zig:7-15): logits = W x through the bit-exact matvec of the
+// tensor's type, then their argmax.
+int loom_cuda_lm_head_argmax(loom_tensor w, size_t vocab, size_t dim, const float *d_x, float *d_logits,
+                             uint32_t *d_index, void *stream) {
+    if (int rc = need_init()) return rc;
+    if (!d_index || vocab == 0 || vocab > 0x7FFFFFFFu) return decline("lm_head needs 1 <= vocab < 2^31");
+    if (!d_logits) {
+        if (int rc = S.head_logits.ensure(vocab * 4)) return rc;
+        d_logits = S.head_logits.as<float>();
+    }
+    if (int rc = loom_cuda_tensor_matmul(w, vocab, dim, d_x, 1, d_logits, stream)) return rc;
+    return loom_cuda_argmax(d_logits, vocab, d_index, stream);
 }
 
 }  // extern "C"

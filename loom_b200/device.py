@@ -162,6 +162,23 @@ def expert_range(n_expert: int, rank: int, world: int):
     return e0, e1 - e0
 
 
+def argmax(logits, out=None, stream=None):
+    """sampler.zig:7-15 argmax of a cuda float32 vector; returns a cuda int32 [1] (the index)."""
+    import torch
+    out = torch.zeros(1, dtype=torch.int32, device=logits.device) if out is None else out
+    _lib.must(_lib.lib().loom_cuda_argmax(_ptr(logits), logits.numel(), _ptr(out), stream), "argmax")
+    return out
+
+
+def lm_head_argmax(w: DeviceTensor, vocab: int, dim: int, x, logits=None, out=None, stream=None):
+    """Output head + greedy sample of one token: (logits W x, their argmax)."""
+    import torch
+    out = torch.zeros(1, dtype=torch.int32, device=x.device) if out is None else out
+    _lib.must(_lib.lib().loom_cuda_lm_head_argmax(w.handle, vocab, dim, _ptr(x), _ptr(logits), _ptr(out), stream),
+              "lm_head_argmax")
+    return out
+
+
 def reserve(T: int, dim: int, ffn: int, n_expert: int, n_used: int) -> None:
     _lib.must(_lib.lib().loom_cuda_reserve(T, dim, ffn, n_expert, n_used), "reserve")
 

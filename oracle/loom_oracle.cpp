@@ -545,6 +545,18 @@ void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps)
 }
 
 // moe.zig:106-158 route
+// sampler.zig:7-15
+size_t or_argmax(const float *logits, size_t n) {
+    size_t best = 0;
+    float best_v = -INFINITY;
+    for (size_t i = 0; i < n; i++)
+        if (logits[i] > best_v) {
+            best_v = logits[i];
+            best = i;
+        }
+    return best;
+}
+
 int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
              int weights_norm, float weights_scale, uint32_t *ids, float *gates) {
     return or_route_grouped(logits, bias, n_expert, n_used, gating, weights_norm, weights_scale, 1, 1, ids, gates);

@@ -55,6 +55,9 @@ void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps)
 /* router, src/gguf/moe.zig:106-158. gating: 1 softmax, 2 sigmoid, 3 softmax_topk */
 int or_route(const float *logits, const float *bias, size_t n_expert, size_t n_used, int gating,
              int weights_norm, float weights_scale, uint32_t *ids, float *gates);
+/* sampler.zig:7-15 argmax: strict '>' from -inf, so the first maximum wins,
+ * NaN is never taken, and an input with nothing above -inf gives 0. */
+size_t or_argmax(const float *logits, size_t n);
 /* or_route with DeepSeek-V3's group-limited selection (n_group groups of
  * n_expert / n_group consecutive experts, the topk_group best by the sum of
  * their two largest biased choices kept); n_group = 1 is or_route. No

@@ -51,6 +51,8 @@ def lib() -> C.CDLL:
         L.or_sigmoid.restype = fp
         L.or_sigmoid.argtypes = [fp]
         L.or_route.argtypes = [vp, vp, sz, sz, C.c_int, C.c_int, fp, vp, vp]
+        L.or_argmax.restype = sz
+        L.or_argmax.argtypes = [vp, sz]
         L.or_route_grouped.argtypes = [vp, vp, sz, sz, C.c_int, C.c_int, fp, sz, sz, vp, vp]
         L.or_moe_ffn_block.argtypes = [vp, sz, vp, sz, vp]
         L.or_moe_ffn_routed.argtypes = [vp, sz, vp, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, sz,
@@ -151,6 +153,12 @@ def silu(v):
 
 def sigmoid(v):
     return float(lib().or_sigmoid(v))
+
+
+def argmax(logits):
+    """sampler.zig:7-15 argmax."""
+    logits = np.ascontiguousarray(logits, np.float32)
+    return int(lib().or_argmax(_p(logits), logits.size))
 
 
 def route(logits, n_used, gating=1, weights_norm=True, weights_scale=1.0, bias=None, n_group=1,

@@ -9,6 +9,7 @@ Sources (ch4r10t33r/loom):
   src/gguf/moe.zig:241-254     "renormalization makes the top-k gates sum to one"
   src/gguf/moe.zig:256-262     "weights_scale multiplies after normalization"
   src/core/tensor.zig:86-91    "softmax sums to one"
+  src/engine/sampler.zig:33-36 "argmax finds the max index"
 
 Expected values are the ones the reference tests assert, with the reference
 tests' tolerances. Run: python tests/golden/make_golden.py
@@ -77,6 +78,8 @@ def main():
         ],
         "softmax": [{"name": "sums_to_one", "ref": "src/core/tensor.zig:86", "x": [1, 2, 3, 4],
                      "expect_sum": 1.0, "tol": 1e-6}],
+        "argmax": [{"name": "finds_max_index", "ref": "src/engine/sampler.zig:33", "logits": [-1, 3, 2, 3.5, 0],
+                    "expect": 3}],
     }
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "known_answers.json")
     with open(path, "w") as f:

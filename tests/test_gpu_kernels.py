@@ -169,3 +169,46 @@ def test_launch_counter_moves(be):
     be.matvec(12, out, data, np.ones(256, np.float32), 64, 256)
     assert be.takeCmdBufCount() == 1
     assert be.kernelLaunches() > k0
+
+
+@pytest.mark.parametrize("n", [1, 5, 300, 151936])
+def test_device_argmax_matches_sampler(be, orc, n):
+    """sampler.zig:7-15 on the device: first maximum, NaN never taken, 0 when
+    nothing is above -inf; bit-compatible with the oracle on random logits,
+    planted ties, NaN and infinities."""
+    import torch
+    from loom_b200 import device as D
+    rng = np.random.default_rng(n)
+    cases = [rng.standard_normal(n).astype(np.float32)]
+    v = rng.standard_normal(n).astype(np.float32)
+    if n >= 5:
+        v[[n // 3, n // 2, n - 1]] = 7.0  # ties: the first one wins
+        v[n // 4] = np.nan
+    cases.append(v)
+    cases.append(np.full(n, -np.inf, np.float32))
+    cases.append(np.full(n, np.nan, np.float32))
+    w = rng.standard_normal(n).astype(np.float32)
+    w[n - 1] = np.inf
+    cases.append(w)
+    for c in cases:
+        got = int(D.argmax(torch.from_numpy(c).cuda()).item())
+        assert got == orc.argmax(c)
+
+
+def test_lm_head_argmax_q6k(be, orc):
+    """The output head (Q6_K [151936 x 2048], Qwen3's vocab) and its greedy
+    sample: logits bit-identical to the oracle's matvec, the same token."""
+    import torch
+    from loom_b200 import device as D
+    vocab, dim = 151936, 2048
+    nblk = vocab * dim // 256
+    W = D.DeviceTensor.synth(14, nblk, seed=901, sigma=1.0)
+    try:
+        x = orc.synth(0, dim, seed=902, sigma=1.0)
+        logits = torch.empty(vocab, device="cuda")
+        tok = D.lm_head_argmax(W, vocab, dim, torch.from_numpy(x).cuda(), logits=logits)
+        want = orc.matvec(14, orc.synth(14, nblk, seed=901), x, vocab, dim)
+        assert np.array_equal(bits(logits.cpu().numpy()), bits(want))
+        assert int(tok.item()) == orc.argmax(want)
+    finally:
+        W.free()

@@ -256,3 +256,20 @@ def test_grouped_route_rejects_bad_groups(orc):
     assert L.or_route_grouped(orc._p(logits), None, 64, 8, 2, 1, 1.0, 3, 1, orc._p(ids), orc._p(g)) != 0  # 64 % 3
     assert L.or_route_grouped(orc._p(logits), None, 64, 8, 2, 1, 1.0, 8, 0, orc._p(ids), orc._p(g)) != 0
     assert L.or_route_grouped(orc._p(logits), None, 64, 9, 2, 1, 1.0, 8, 1, orc._p(ids), orc._p(g)) != 0  # k > 8
+
+
+def test_known_answer_argmax(orc):
+    """sampler.zig:33-36."""
+    for case in GOLDEN["argmax"]:
+        assert orc.argmax(np.array(case["logits"], np.float32)) == case["expect"]
+
+
+def test_argmax_ties_nan_and_inf(orc):
+    """Strict '>' from -inf: the first maximum wins, NaN is never taken, nothing above -inf gives 0."""
+    f = lambda v: orc.argmax(np.array(v, np.float32))  # noqa: E731
+    assert f([1.0, 5.0, 5.0, 2.0]) == 1
+    assert f([np.nan, 1.0, np.nan, 3.0]) == 3
+    assert f([-np.inf, -np.inf]) == 0
+    assert f([np.nan, np.nan]) == 0
+    assert f([-np.inf, -5.0, np.inf, np.inf]) == 2
+    assert f([0.0, -0.0]) == 0 and f([-0.0, 0.0]) == 0
