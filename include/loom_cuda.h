@@ -39,7 +39,10 @@ enum {
     LOOM_F32 = 0,
     LOOM_Q4_0 = 2,
     LOOM_Q8_0 = 8,
+    LOOM_Q2_K = 10,
+    LOOM_Q3_K = 11,
     LOOM_Q4_K = 12,
+    LOOM_Q5_K = 13,
     LOOM_Q6_K = 14
 };
 

@@ -24,23 +24,31 @@
 
 namespace loom {
 
-enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+enum GgmlType : int {
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14
+};
+__host__ __device__ constexpr bool is_kquant(int t) {
+    return t == T_Q2_K || t == T_Q3_K || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K;
+}
 
 constexpr int QK_0 = 32;
 constexpr int QK_K = 256;
 
 __host__ __device__ constexpr int block_elems(int t) {
-    return t == T_F32 ? 1 : (t == T_Q4_0 || t == T_Q8_0) ? QK_0 : (t == T_Q4_K || t == T_Q6_K) ? QK_K : 0;
+    return t == T_F32 ? 1 : (t == T_Q4_0 || t == T_Q8_0) ? QK_0 : is_kquant(t) ? QK_K : 0;
 }
 __host__ __device__ constexpr int block_bytes(int t) {
-    return t == T_F32 ? 4 : t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_Q6_K ? 210 : 0;
+    return t == T_F32 ? 4 : t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_Q6_K ? 210
+         : t == T_Q2_K ? 84 : t == T_Q3_K ? 110 : t == T_Q5_K ? 176 : 0;
 }
-// bytes of the quant region per block in the device layout
+// bytes of the quant region per block in the device layout (Q2_K: scales +
+// quants; Q3_K: high-bit mask + quants; Q4_K / Q5_K: the whole block)
 __host__ __device__ constexpr int layout_qbytes(int t) {
-    return t == T_F32 ? 4 : t == T_Q4_0 ? 16 : t == T_Q8_0 ? 32 : t == T_Q4_K ? 144 : t == T_Q6_K ? 192 : 0;
+    return t == T_F32 ? 4 : t == T_Q4_0 ? 16 : t == T_Q8_0 ? 32 : t == T_Q4_K ? 144 : t == T_Q6_K ? 192
+         : t == T_Q2_K ? 80 : t == T_Q3_K ? 96 : t == T_Q5_K ? 176 : 0;
 }
 // true when a type's activation is quantized per 256 (Q8_K style) rather than per 32
-__host__ __device__ constexpr bool act256(int t) { return t == T_Q4_K || t == T_Q6_K || t == 112; }
+__host__ __device__ constexpr bool act256(int t) { return is_kquant(t) || t == 112; }
 
 // A device-resident weight tensor in its device layout.
 struct WDev {
@@ -103,6 +111,14 @@ __device__ __forceinline__ int to_i8_sat(float v) {
 }
 
 // ggml.zig:1332-1340 scaleMinK4, on the 12 scale bytes held as three words
+// q3kScales (ggml.zig:1173-1191): six-bit scale j (0..15) of the 12 packed
+// bytes p (low four bits from bytes 0-7, high two bits from bytes 8-11)
+__host__ __device__ __forceinline__ int q3k_scale(const uint8_t *p, int j) {
+    const int lo = j < 8 ? (p[j] & 0x0F) : (p[j - 8] >> 4);
+    const int hi = (p[8 + (j & 3)] >> (2 * (j >> 2))) & 3;
+    return lo | (hi << 4);
+}
+
 __device__ __forceinline__ void scale_min_k4(int j, const uint8_t *s, int &sc, int &mn) {
     if (j < 4) {
         sc = s[j] & 63;

@@ -83,6 +83,29 @@ __global__ void k_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, ui
                 blk[208] = d & 0xFF; blk[209] = d >> 8;
                 break;
             }
+            case T_Q5_K: {
+                uint8_t *blk = raw + i * 176;
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                uint16_t dm = rand_scale(rword(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8; blk[2] = dm & 0xFF; blk[3] = dm >> 8;
+                put_bytes(blk + 4, 172, seed, w0 + 2);
+                break;
+            }
+            case T_Q2_K: {
+                uint8_t *blk = raw + i * 84;
+                put_bytes(blk, 80, seed, w0 + 2);
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                uint16_t dm = rand_scale(rword(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[80] = d & 0xFF; blk[81] = d >> 8; blk[82] = dm & 0xFF; blk[83] = dm >> 8;
+                break;
+            }
+            case T_Q3_K: {
+                uint8_t *blk = raw + i * 110;
+                put_bytes(blk, 108, seed, w0 + 2);
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                blk[108] = d & 0xFF; blk[109] = d >> 8;
+                break;
+            }
             case T_Q4_0: {
                 uint8_t *blk = raw + i * 18;
                 uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 1.9e-2f);
@@ -127,6 +150,20 @@ __global__ void k_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, 
                 for (int i = 0; i < 32; i++) q[b * 32 + i] = src[2 + i];
                 break;
             }
+            case T_Q2_K: {  // scales + quants | d, dmin
+                const uint8_t *src = raw + b * 84;
+                for (int i = 0; i < 80; i++) q[b * 80 + i] = src[i];
+                d[2 * b] = (uint16_t)(src[80] | (src[81] << 8));
+                d[2 * b + 1] = (uint16_t)(src[82] | (src[83] << 8));
+                break;
+            }
+            case T_Q3_K: {  // high-bit mask + quants | packed scales (12 of 16 bytes) | d
+                const uint8_t *src = raw + b * 110;
+                for (int i = 0; i < 96; i++) q[b * 96 + i] = src[i];
+                for (int i = 0; i < 16; i++) sc[b * 16 + i] = i < 12 ? src[96 + i] : 0;
+                d[b] = (uint16_t)(src[108] | (src[109] << 8));
+                break;
+            }
             case T_Q4_0: {
                 const uint8_t *src = raw + b * 18;
                 d[b] = (uint16_t)(src[0] | (src[1] << 8));
@@ -151,6 +188,26 @@ __global__ void k_unpack(WDev w, uint8_t *raw, uint64_t nblk) {
             case T_Q4_K:
                 for (int i = 0; i < 144; i++) raw[b * 144 + i] = w.q[b * 144 + i];
                 break;
+            case T_Q5_K:
+                for (int i = 0; i < 176; i++) raw[b * 176 + i] = w.q[b * 176 + i];
+                break;
+            case T_Q2_K: {
+                uint8_t *dst = raw + b * 84;
+                for (int i = 0; i < 80; i++) dst[i] = w.q[b * 80 + i];
+                dst[80] = w.d[2 * b] & 0xFF;
+                dst[81] = w.d[2 * b] >> 8;
+                dst[82] = w.d[2 * b + 1] & 0xFF;
+                dst[83] = w.d[2 * b + 1] >> 8;
+                break;
+            }
+            case T_Q3_K: {
+                uint8_t *dst = raw + b * 110;
+                for (int i = 0; i < 96; i++) dst[i] = w.q[b * 96 + i];
+                for (int i = 0; i < 12; i++) dst[96 + i] = w.sc[b * 16 + i];
+                dst[108] = w.d[b] & 0xFF;
+                dst[109] = w.d[b] >> 8;
+                break;
+            }
             case T_Q6_K: {
                 uint8_t *dst = raw + b * 210;
                 for (int i = 0; i < 192; i++) dst[i] = w.q[b * 192 + i];
@@ -226,6 +283,36 @@ __global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
                 }
                 const float s = fmul(d, (float)scs[8 * n + l / 16 + 2 * g]);
                 v = fmul(s, fsub((float)q, 32.0f));
+                break;
+            }
+            case T_Q5_K: {  // dequantBlockQ5K :1376: (d*sc)*(q + 16 h) - (dmin*m)
+                const uint8_t *blk = w.q + gb * 176;
+                const float d = f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+                const float dmin = f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+                const int j = i / 64, l = i % 64, sb = 2 * j + (l >= 32);
+                const uint8_t byte = blk[48 + 32 * j + (l & 31)];
+                const int q = l < 32 ? (byte & 0x0F) : (byte >> 4);
+                const bool hb = (blk[16 + (l & 31)] >> sb) & 1;
+                int sc, mn;
+                scale_min_k4(sb, blk + 4, sc, mn);
+                v = fsub(fmul(fmul(d, (float)sc), fadd((float)q, hb ? 16.0f : 0.0f)), fmul(dmin, (float)mn));
+                break;
+            }
+            case T_Q2_K: {  // dequantBlockQ2K :1476: (d*sc)*q - (dmin*m), sub-block j = i / 16
+                const uint8_t *qb = w.q + gb * 80;
+                const float d = f16_to_f32(w.d[2 * gb]), dmin = f16_to_f32(w.d[2 * gb + 1]);
+                const int g = i / 32, l = i % 32, j = i / 16;
+                const uint8_t sc = qb[j];
+                const int q = (qb[16 + 32 * (g / 4) + l] >> (2 * (g % 4))) & 3;
+                v = fsub(fmul(fmul(d, (float)(sc & 0xF)), (float)q), fmul(dmin, (float)(sc >> 4)));
+                break;
+            }
+            case T_Q3_K: {  // dequantBlockQ3K :1508: (d*(sc-32))*(q - 4 [high bit clear])
+                const uint8_t *qb = w.q + gb * 96;
+                const int g = i / 32, l = i % 32, j = i / 16;
+                const int q2 = (qb[32 + 32 * (g / 4) + l] >> (2 * (g % 4))) & 3;
+                const int off = (qb[l] >> g) & 1 ? 0 : 4;
+                v = fmul(fmul(f16_to_f32(w.d[gb]), (float)(q3k_scale(w.sc + gb * 16, j) - 32)), (float)(q2 - off));
                 break;
             }
             case T_Q4_0: {

@@ -259,6 +259,130 @@ __device__ __forceinline__ float rowdot_f32(const float *__restrict__ row, const
     return r;
 }
 
+// ---- Q2_K / Q3_K / Q5_K: the uniform K-quant decode (ggml.zig kDecode :882) --------
+// Eight lanes per super-block, lane g holding weight group g (values 32g ..
+// 32g+31, per-16 sub-blocks 2g and 2g+1), four super-blocks per pass:
+//   Q5_K  nibble of qs[32 (g/2) + l] (low for even g) | bit g of qh[l] << 4
+//   Q2_K  (qs[32 (g/4) + l] >> 2 (g%4)) & 3, per-16 scale / min nibbles
+//   Q3_K  ((qs[32 (g/4) + l] >> 2 (g%4)) & 3) | bit g of hmask[l] << 2, minus 4
+//         (as sum u x - 4 bsum, an integer identity), per-16 scales q3kScales - 32
+// then kBlockDot :1002: I = sum_j sc_j (w.x)_j, M = sum_j mn_j bsum_j,
+// term = xd*(d*I - dmin*M) (Q2_K, Q5_K) or (xd*d)*I (Q3_K), blocks in order.
+template <int TY, int NT>
+__device__ __forceinline__ void rowdot_kq(const WDev &w, uint64_t gb0, int nb, const XQ &x, int t0, int nt,
+                                          float (&acc)[NT], int lane) {
+    const int g = lane & 7, grp = lane >> 3;
+    for (int b0 = 0; b0 < nb; b0 += 4) {
+        const int b = b0 + grp;
+        const bool live = b < nb;
+        uint32_t wv[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // the group's 32 weights as int8 (Q3_K: u = q + 4)
+        int sc0 = 0, sc1 = 0, mn0 = 0, mn1 = 0;
+        float d = 0.0f, dmin = 0.0f;
+        if (live) {
+            const uint64_t gb = gb0 + b;
+            if (TY == T_Q5_K) {
+                const uint8_t *blk = w.q + gb * 176;
+                const uint4 hdr = ld_stream_v4(blk);
+                const uint4 h0 = ld_stream_v4(blk + 16), h1 = ld_stream_v4(blk + 32);
+                const uint4 q0 = ld_stream_v4(blk + 48 + 32 * (g >> 1)), q1 = ld_stream_v4(blk + 64 + 32 * (g >> 1));
+                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    wv[k] = ((g & 1) ? (qw[k] >> 4) & 0x0F0F0F0Fu : qw[k] & 0x0F0F0F0Fu) | (((hw[k] >> g) & 0x01010101u) << 4);
+                uint8_t s[12];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    s[i] = (hdr.y >> (8 * i)) & 0xFF;
+                    s[4 + i] = (hdr.z >> (8 * i)) & 0xFF;
+                    s[8 + i] = (hdr.w >> (8 * i)) & 0xFF;
+                }
+                scale_min_k4(g, s, sc0, mn0);
+                sc1 = sc0;
+                mn1 = mn0;
+                d = f16_to_f32((uint16_t)(hdr.x & 0xFFFF));
+                dmin = f16_to_f32((uint16_t)(hdr.x >> 16));
+            } else if (TY == T_Q2_K) {
+                const uint8_t *qb = w.q + gb * 80;
+                const uint4 sv = ld_stream_v4(qb);
+                const uint4 q0 = ld_stream_v4(qb + 16 + 32 * (g >> 2)), q1 = ld_stream_v4(qb + 32 + 32 * (g >> 2));
+                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) wv[k] = (qw[k] >> (2 * (g & 3))) & 0x03030303u;
+                const uint32_t s4[4] = {sv.x, sv.y, sv.z, sv.w};
+                const uint32_t sb0 = (s4[g >> 1] >> (16 * (g & 1))) & 0xFF, sb1 = (s4[g >> 1] >> (16 * (g & 1) + 8)) & 0xFF;
+                sc0 = (int)(sb0 & 0xF);
+                mn0 = (int)(sb0 >> 4);
+                sc1 = (int)(sb1 & 0xF);
+                mn1 = (int)(sb1 >> 4);
+                d = f16_to_f32(__ldg(w.d + 2 * gb));
+                dmin = f16_to_f32(__ldg(w.d + 2 * gb + 1));
+            } else {  // T_Q3_K
+                const uint8_t *qb = w.q + gb * 96;
+                const uint4 h0 = ld_stream_v4(qb), h1 = ld_stream_v4(qb + 16);
+                const uint4 q0 = ld_stream_v4(qb + 32 + 32 * (g >> 2)), q1 = ld_stream_v4(qb + 48 + 32 * (g >> 2));
+                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    wv[k] = ((qw[k] >> (2 * (g & 3))) & 0x03030303u) | (((hw[k] >> g) & 0x01010101u) << 2);
+                const uint4 sv = ld_stream_v4(w.sc + gb * 16);
+                uint8_t p[12];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    p[i] = (sv.x >> (8 * i)) & 0xFF;
+                    p[4 + i] = (sv.y >> (8 * i)) & 0xFF;
+                    p[8 + i] = (sv.z >> (8 * i)) & 0xFF;
+                }
+                sc0 = q3k_scale(p, 2 * g) - 32;
+                sc1 = q3k_scale(p, 2 * g + 1) - 32;
+                d = f16_to_f32(__ldg(w.d + gb));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < NT; k++) {
+            int I = 0, M = 0;
+            if (live && k < nt) {
+                const int t = t0 + k;
+                const int8_t *xb = x.q + (size_t)t * x.cols + b * 256 + 32 * g;
+                const int4 xl = ld_i4(xb), xh = ld_i4(xb + 16);
+                int dl = 0, dh = 0;
+                dl = dp4a((int)wv[0], xl.x, dl);
+                dl = dp4a((int)wv[1], xl.y, dl);
+                dl = dp4a((int)wv[2], xl.z, dl);
+                dl = dp4a((int)wv[3], xl.w, dl);
+                dh = dp4a((int)wv[4], xh.x, dh);
+                dh = dp4a((int)wv[5], xh.y, dh);
+                dh = dp4a((int)wv[6], xh.z, dh);
+                dh = dp4a((int)wv[7], xh.w, dh);
+                const int32_t *bs = x.s + (size_t)t * x.sstride + b * 16 + 2 * g;
+                if (TY == T_Q3_K) {
+                    dl -= 4 * __ldg(bs);
+                    dh -= 4 * __ldg(bs + 1);
+                } else {
+                    M = mn0 * __ldg(bs) + mn1 * __ldg(bs + 1);
+                }
+                I = sc0 * dl + sc1 * dh;
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                I += __shfl_xor_sync(0xffffffffu, I, o);
+                if (TY != T_Q3_K) M += __shfl_xor_sync(0xffffffffu, M, o);
+            }
+            float term = 0.0f;
+            if (live && k < nt) {
+                const float xd = __ldg(x.d + (size_t)(t0 + k) * x.dstride + b);
+                term = TY == T_Q3_K ? fmul(fmul(xd, d), (float)I) : fmul(xd, fsub(fmul(d, (float)I), fmul(dmin, (float)M)));
+            }
+#pragma unroll
+            for (int gg = 0; gg < 4; gg++) {
+                const float tg = __shfl_sync(0xffffffffu, term, 8 * gg);
+                if (b0 + gg < nb) acc[k] = fadd(acc[k], tg);
+            }
+        }
+    }
+}
+
 // Dispatch on the (warp-uniform) block type. acc must start at 0.
 template <int NT>
 __device__ __forceinline__ void rowdot(const WDev &w, uint64_t gb0, int nb, const XQ &x, int t0, int nt,
@@ -268,6 +392,9 @@ __device__ __forceinline__ void rowdot(const WDev &w, uint64_t gb0, int nb, cons
         case T_Q6_K: rowdot_q6k<NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         case T_Q8_0: rowdot_q80<NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         case T_Q4_0: rowdot_q40<NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
+        case T_Q5_K: rowdot_kq<T_Q5_K, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
+        case T_Q2_K: rowdot_kq<T_Q2_K, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
+        case T_Q3_K: rowdot_kq<T_Q3_K, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         default: break;
     }
 }

@@ -46,7 +46,9 @@ int decline(const char *why) {
     } while (0)
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
-bool type_ok(int t) { return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; }
+bool type_ok(int t) { return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || is_kquant(t); }
+// types stored as their GGUF blocks unchanged (16-byte multiples)
+bool raw_layout(int t) { return t == T_F32 || t == T_Q4_K || t == T_Q5_K; }
 
 // ---- device tensors ---------------------------------------------------------------
 
@@ -130,8 +132,9 @@ int alloc_tensor(int type, uint64_t nblk, Tensor &t) {
     t.type = type;
     t.nblk = nblk;
     const size_t qb = align256(nblk * (size_t)layout_qbytes(type));
-    const size_t scb = type == T_Q6_K ? align256(nblk * 16) : 0;
-    const size_t db = (type == T_Q6_K || type == T_Q8_0 || type == T_Q4_0) ? align256(nblk * 2) : 0;
+    const size_t scb = (type == T_Q6_K || type == T_Q3_K) ? align256(nblk * 16) : 0;
+    const size_t db = (type == T_Q6_K || type == T_Q8_0 || type == T_Q4_0 || type == T_Q3_K) ? align256(nblk * 2)
+                    : type == T_Q2_K ? align256(nblk * 4) : 0;  // Q2_K: d and dmin
     t.dev_bytes = qb + scb + db;
     cudaError_t e = cudaMalloc(&t.base, std::max<size_t>(t.dev_bytes, 256));
     if (e != cudaSuccess) return fail("cudaMalloc(tensor)", e);
@@ -144,7 +147,7 @@ int alloc_tensor(int type, uint64_t nblk, Tensor &t) {
 
 // Fill a tensor from GGUF bytes already on the device (`raw_dev`).
 int fill_from_raw_dev(Tensor &t, const uint8_t *raw_dev) {
-    if (t.type == T_F32 || t.type == T_Q4_K) {
+    if (raw_layout(t.type)) {
         CK(cudaMemcpyAsync(t.base, raw_dev, t.nblk * (size_t)block_bytes(t.type), cudaMemcpyDeviceToDevice, g_stream));
     } else {
         launch_repack(t.type, raw_dev, t.base, const_cast<uint8_t *>(t.w.sc), const_cast<uint16_t *>(t.w.d), t.nblk,
@@ -180,7 +183,7 @@ int upload_tensor(int type, const void *data, size_t bytes, uint64_t &handle) {
     Tensor t;
     if (int rc = alloc_tensor(type, bytes / bb, t)) return rc;
     const uint8_t *raw_dev = arena_lookup(data, bytes);
-    if (!raw_dev && (type == T_F32 || type == T_Q4_K)) {
+    if (!raw_dev && raw_layout(type)) {
         CK(cudaMemcpyAsync(t.base, data, bytes, cudaMemcpyHostToDevice, g_stream));
     } else {
         if (!raw_dev) {
@@ -855,7 +858,7 @@ int loom_cuda_tensor_synth_range(int type, uint64_t blk0, uint64_t nblk, uint64_
     Tensor t;
     if (int rc = alloc_tensor(type, nblk, t)) return rc;
     const size_t bb = block_bytes(type);
-    if (type == T_F32 || type == T_Q4_K) {
+    if (raw_layout(type)) {
         launch_synth(type, t.base, blk0, nblk, seed, sigma, g_stream);
     } else {
         // generate GGUF bytes in bounded chunks, then repack each into the layout
@@ -895,7 +898,7 @@ int loom_cuda_tensor_download(loom_tensor h, void *dst, size_t bytes) {
     if (!t) return decline("unknown tensor");
     const size_t raw_b = t->nblk * (size_t)block_bytes(t->type);
     if (bytes != raw_b) return decline("size mismatch");
-    if (t->type == T_F32 || t->type == T_Q4_K) {
+    if (raw_layout(t->type)) {
         CK(cudaMemcpyAsync(dst, t->base, raw_b, cudaMemcpyDeviceToHost, g_stream));
     } else {
         if (int rc = S.raw.ensure(raw_b)) return rc;

@@ -26,6 +26,9 @@ constexpr size_t QK_K = 256;
 constexpr size_t Q4_0_BLOCK = 18;
 constexpr size_t Q8_0_BLOCK = 34;
 constexpr size_t Q4_K_BLOCK = 144;
+constexpr size_t Q5_K_BLOCK = 176;  // ggml.zig:87-159: d, dmin, scales[12], qh[32], qs[128]
+constexpr size_t Q2_K_BLOCK = 84;   // scales[16], qs[64], d, dmin
+constexpr size_t Q3_K_BLOCK = 110;  // hmask[32], qs[64], scales[12], d
 constexpr size_t Q6_K_BLOCK = 210;
 
 // ggml.zig:260 f16FromBytes: exact widening of an IEEE half.
@@ -124,7 +127,7 @@ struct XQ {  // quantized activation vector
     std::vector<int32_t> s;  // bsum16 (K) or sum32 (Q4_0/Q8_0)
 };
 
-bool uses_q8k(int t) { return t == OR_Q4_K || t == OR_Q6_K; }
+bool uses_q8k(int t) { return t == OR_Q4_K || t == OR_Q6_K || t == OR_Q2_K || t == OR_Q3_K || t == OR_Q5_K; }
 
 void quantize(int t, const float *x, size_t cols, XQ &xq) {
     xq.q.resize(cols);
@@ -223,6 +226,107 @@ inline float q80_block_dot(const uint8_t *blk, const int8_t *xq, float xd) {
     return d * xd * (float)dot32((const int8_t *)(blk + 2), xq);
 }
 
+// ggml.zig:1173-1191 q3kScales: 12 packed bytes -> 16 six-bit scales
+inline void q3k_scales(const uint8_t *p, uint8_t out[16]) {
+    uint32_t aux[4];
+    std::memcpy(&aux[0], p, 4);
+    std::memcpy(&aux[1], p + 4, 4);
+    std::memcpy(&aux[2], p + 8, 4);
+    const uint32_t kmask1 = 0x03030303u, kmask2 = 0x0f0f0f0fu, tmp = aux[2];
+    aux[2] = ((aux[0] >> 4) & kmask2) | (((tmp >> 4) & kmask1) << 4);
+    aux[3] = ((aux[1] >> 4) & kmask2) | (((tmp >> 6) & kmask1) << 4);
+    aux[0] = (aux[0] & kmask2) | (((tmp >> 0) & kmask1) << 4);
+    aux[1] = (aux[1] & kmask2) | (((tmp >> 2) & kmask1) << 4);
+    std::memcpy(out, aux, 16);
+}
+
+// ggml.zig:844-997 kDecode for q2_k / q3_k / q5_k into the uniform shape:
+// eight 32-wide int8 weight groups (group g = values 32g..32g+31, per-16
+// sub-blocks 2g and 2g+1), sixteen per-16 scales and mins, d and dmin.
+struct KDec {
+    int8_t w[256];
+    int32_t sc[16], mn[16];
+    float d, dmin;
+    bool has_min;
+};
+
+inline void k_decode(int t, const uint8_t *blk, KDec &k) {
+    switch (t) {
+        case OR_Q5_K: {
+            k.d = f16at(blk);
+            k.dmin = f16at(blk + 2);
+            k.has_min = true;
+            const uint8_t *scales = blk + 4, *qh = blk + 16, *qs = blk + 48;
+            for (int j = 0; j < 8; j++) {
+                int sc, mn;
+                scale_min_k4(j, scales, sc, mn);
+                k.sc[2 * j] = k.sc[2 * j + 1] = sc;
+                k.mn[2 * j] = k.mn[2 * j + 1] = mn;
+                for (int l = 0; l < 32; l++) {
+                    const uint8_t b = qs[(j / 2) * 32 + l];
+                    const int nib = (j % 2) ? (b >> 4) : (b & 0x0F);
+                    const int hb = (qh[l] >> (j % 2 + 2 * (j / 2))) & 1;  // the fifth bit of sub-block j
+                    k.w[32 * j + l] = (int8_t)(nib | (hb << 4));
+                }
+            }
+            break;
+        }
+        case OR_Q2_K: {
+            const uint8_t *scales = blk, *qs = blk + 16;
+            k.d = f16at(blk + 80);
+            k.dmin = f16at(blk + 82);
+            k.has_min = true;
+            for (int j = 0; j < 16; j++) {
+                k.sc[j] = scales[j] & 0xF;
+                k.mn[j] = scales[j] >> 4;
+            }
+            for (int half = 0; half < 2; half++)
+                for (int shift = 0; shift < 4; shift++)
+                    for (int l = 0; l < 32; l++)
+                        k.w[32 * (half * 4 + shift) + l] = (int8_t)((qs[half * 32 + l] >> (2 * shift)) & 3);
+            break;
+        }
+        case OR_Q3_K: {
+            const uint8_t *hmask = blk, *qs = blk + 32;
+            uint8_t sc16[16];
+            q3k_scales(blk + 96, sc16);
+            k.d = f16at(blk + 108);
+            k.dmin = 0.0f;
+            k.has_min = false;
+            for (int j = 0; j < 16; j++) {
+                k.sc[j] = (int32_t)sc16[j] - 32;
+                k.mn[j] = 0;
+            }
+            for (int half = 0; half < 2; half++)
+                for (int shift = 0; shift < 4; shift++) {
+                    const int idx = half * 4 + shift;
+                    for (int l = 0; l < 32; l++) {
+                        const int q2 = (qs[half * 32 + l] >> (2 * shift)) & 3;
+                        const int off = (hmask[l] & (1 << idx)) ? 0 : 4;  // subtract 4 where the high bit is clear
+                        k.w[32 * idx + l] = (int8_t)(q2 - off);
+                    }
+                }
+            break;
+        }
+    }
+}
+
+// ggml.zig:1002-1021 kBlockDot on a uniform decode
+inline float k_block_dot(const KDec &k, const int8_t *xq, float xd, const int32_t *bsum) {
+    int32_t isum = 0;
+    for (int j = 0; j < 16; j++) {
+        int32_t s = 0;
+        for (int l = 0; l < 16; l++) s += (int32_t)k.w[16 * j + l] * (int32_t)xq[16 * j + l];
+        isum += s * k.sc[j];
+    }
+    if (k.has_min) {
+        int32_t msum = 0;
+        for (int j = 0; j < 16; j++) msum += k.mn[j] * bsum[j];
+        return xd * (k.d * (float)isum - k.dmin * (float)msum);
+    }
+    return xd * k.d * (float)isum;
+}
+
 // One row against a quantized activation.
 float row_dot(int t, const uint8_t *row, const XQ &xq, size_t cols) {
     float acc = 0.0f;
@@ -239,6 +343,17 @@ float row_dot(int t, const uint8_t *row, const XQ &xq, size_t cols) {
             for (size_t b = 0; b < cols / QK_0; b++)
                 acc += q40_block_dot(row + b * Q4_0_BLOCK, &xq.q[b * QK_0], xq.d[b]);
             break;
+        case OR_Q2_K:
+        case OR_Q3_K:
+        case OR_Q5_K: {  // matvecK256 :1024 over the uniform decode
+            const size_t bb = or_block_bytes(t);
+            KDec k;
+            for (size_t b = 0; b < cols / QK_K; b++) {
+                k_decode(t, row + b * bb, k);
+                acc += k_block_dot(k, &xq.q[b * QK_K], xq.d[b], &xq.s[b * 16]);
+            }
+            break;
+        }
         case OR_Q8_0:
             for (size_t b = 0; b < cols / QK_0; b++)
                 acc += q80_block_dot(row + b * Q8_0_BLOCK, &xq.q[b * QK_0], xq.d[b]);
@@ -334,7 +449,7 @@ size_t or_block_elems(int t) {
     switch (t) {
         case OR_F32: case OR_F16: return 1;
         case OR_Q4_0: case OR_Q8_0: return QK_0;
-        case OR_Q4_K: case OR_Q6_K: return QK_K;
+        case OR_Q2_K: case OR_Q3_K: case OR_Q4_K: case OR_Q5_K: case OR_Q6_K: return QK_K;
     }
     return 0;
 }
@@ -347,6 +462,9 @@ size_t or_block_bytes(int t) {
         case OR_Q8_0: return Q8_0_BLOCK;
         case OR_Q4_K: return Q4_K_BLOCK;
         case OR_Q6_K: return Q6_K_BLOCK;
+        case OR_Q2_K: return Q2_K_BLOCK;
+        case OR_Q3_K: return Q3_K_BLOCK;
+        case OR_Q5_K: return Q5_K_BLOCK;
     }
     return 0;
 }
@@ -458,6 +576,67 @@ int or_dequant_row(int t, float *out, const uint8_t *data, size_t r, size_t cols
                 }
             }
             return 0;
+        case OR_Q5_K:  // dequantBlockQ5K, ggml.zig:1376-1418
+            for (size_t b = 0; b < cols / QK_K; b++) {
+                const uint8_t *blk = row + b * Q5_K_BLOCK;
+                const float d = f16at(blk), dmin = f16at(blk + 2);
+                const uint8_t *scales = blk + 4, *qh = blk + 16, *qs = blk + 48;
+                float *v = out + b * QK_K;
+                for (int j = 0; j < 4; j++) {
+                    int sc, mn;
+                    scale_min_k4(2 * j, scales, sc, mn);
+                    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+                    scale_min_k4(2 * j + 1, scales, sc, mn);
+                    const float d2 = d * (float)sc, m2 = dmin * (float)mn;
+                    const uint8_t hb1 = (uint8_t)(1u << (2 * j)), hb2 = (uint8_t)(2u << (2 * j));
+                    for (int l = 0; l < 32; l++) {
+                        const uint8_t q = qs[32 * j + l];
+                        v[64 * j + l] = d1 * ((float)(q & 0x0F) + ((qh[l] & hb1) ? 16.0f : 0.0f)) - m1;
+                        v[64 * j + 32 + l] = d2 * ((float)(q >> 4) + ((qh[l] & hb2) ? 16.0f : 0.0f)) - m2;
+                    }
+                }
+            }
+            return 0;
+        case OR_Q2_K:  // dequantBlockQ2K, ggml.zig:1476-1505
+            for (size_t b = 0; b < cols / QK_K; b++) {
+                const uint8_t *blk = row + b * Q2_K_BLOCK;
+                const uint8_t *scales = blk, *qs = blk + 16;
+                const float d = f16at(blk + 80), dmin = f16at(blk + 82);
+                float *v = out + b * QK_K;
+                int y = 0, is = 0;
+                for (int n = 0; n < 2; n++)
+                    for (int j = 0; j < 4; j++)
+                        for (int half = 0; half < 2; half++) {
+                            const uint8_t sc = scales[is++];
+                            const float dl = d * (float)(sc & 0xF), ml = dmin * (float)(sc >> 4);
+                            for (int l = 0; l < 16; l++)
+                                v[y++] = dl * (float)((qs[32 * n + half * 16 + l] >> (2 * j)) & 3) - ml;
+                        }
+            }
+            return 0;
+        case OR_Q3_K:  // dequantBlockQ3K, ggml.zig:1508-1540
+            for (size_t b = 0; b < cols / QK_K; b++) {
+                const uint8_t *blk = row + b * Q3_K_BLOCK;
+                const uint8_t *hmask = blk, *qs = blk + 32;
+                uint8_t sc16[16];
+                q3k_scales(blk + 96, sc16);
+                const float d = f16at(blk + 108);
+                float *v = out + b * QK_K;
+                int y = 0, is = 0;
+                for (int n = 0; n < 2; n++)
+                    for (int j = 0; j < 4; j++) {
+                        const uint8_t m = (uint8_t)(1u << (4 * n + j));
+                        for (int half = 0; half < 2; half++) {
+                            const float dl = d * (float)((int)sc16[is++] - 32);
+                            for (int l = 0; l < 16; l++) {
+                                const int idx = half * 16 + l;
+                                const int q2 = (qs[32 * n + idx] >> (2 * j)) & 3;
+                                v[y++] = dl * (float)(q2 - ((hmask[idx] & m) ? 0 : 4));
+                            }
+                        }
+                    }
+            }
+            return 0;
         case OR_Q4_0:
             for (size_t b = 0; b < cols / QK_0; b++) {
                 const uint8_t *blk = row + b * Q4_0_BLOCK;
@@ -490,7 +669,7 @@ int or_matvec(int t, float *out, const uint8_t *data, const float *x, size_t row
         });
         return 0;
     }
-    if (t != OR_Q4_K && t != OR_Q6_K && t != OR_Q4_0 && t != OR_Q8_0) return -1;
+    if (or_block_elems(t) == 0 || t == OR_F16) return -1;
     if (cols % or_block_elems(t) != 0) return -1;
     XQ xq;
     quantize(t, x, cols, xq);
@@ -509,7 +688,7 @@ int or_matmul(int t, float *out, const uint8_t *data, const float *xs, size_t n,
         for (size_t k = 0; k < n; k++) or_matvec(t, out + k * rows, data, xs + k * cols, rows, cols);
         return 0;
     }
-    if (t != OR_Q4_K && t != OR_Q6_K && t != OR_Q4_0 && t != OR_Q8_0) return -1;
+    if (or_block_elems(t) == 0 || t == OR_F16) return -1;
     std::vector<XQ> xq(n);
     for (size_t k = 0; k < n; k++) quantize(t, xs + k * cols, cols, xq[k]);
     const size_t rb = or_row_bytes(t, cols);
@@ -798,6 +977,29 @@ void or_synth(int type, void *out, uint64_t blk0, uint64_t nblk, uint64_t seed, 
                 for (int k = 0; k < 16; k++) blk[192 + k] = (uint8_t)(int8_t)((int)(sc[k] % 64) - 32);
                 uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
                 blk[208] = d & 0xFF; blk[209] = d >> 8;
+                break;
+            }
+            case OR_Q5_K: {  // as Q4_K: f16 d, dmin ~U(1e-3, 1e-2), random scales, high bits and nibbles
+                uint8_t *blk = o + i * Q5_K_BLOCK;
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                uint16_t dm = rand_scale(word(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8; blk[2] = dm & 0xFF; blk[3] = dm >> 8;
+                put_bytes(blk + 4, 172, seed, w0 + 2);
+                break;
+            }
+            case OR_Q2_K: {  // random scale/min nibbles and quants, f16 d, dmin ~U(1e-3, 1e-2)
+                uint8_t *blk = o + i * Q2_K_BLOCK;
+                put_bytes(blk, 80, seed, w0 + 2);
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                uint16_t dm = rand_scale(word(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[80] = d & 0xFF; blk[81] = d >> 8; blk[82] = dm & 0xFF; blk[83] = dm >> 8;
+                break;
+            }
+            case OR_Q3_K: {  // random high-bit mask, quants and packed 6-bit scales, f16 d ~U(1e-3, 1e-2)
+                uint8_t *blk = o + i * Q3_K_BLOCK;
+                put_bytes(blk, 108, seed, w0 + 2);
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                blk[108] = d & 0xFF; blk[109] = d >> 8;
                 break;
             }
             case OR_Q4_0: {

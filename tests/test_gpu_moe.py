@@ -89,7 +89,7 @@ def test_moe_ffn_routed_deepseek_shared(be, orc, sigmoid):
     assert rel_l2(out, want) < TOL
 
 
-@pytest.mark.parametrize("t", [0, 2, 8, 12, 14])
+@pytest.mark.parametrize("t", [0, 2, 8, 10, 11, 12, 13, 14])
 def test_device_synth_matches_oracle(be, orc, t):
     nblk = 1000
     dt = DeviceTensor.synth(t, nblk, seed=77, sigma=0.02)
@@ -302,3 +302,23 @@ def test_grouped_routing_declines_bad_groups(be, orc):
         L.forward(x, out)  # one group of 4 experts cannot supply 6
     for t_ in (L.gate, L.up, L.down, L.router):
         t_.free()
+
+
+def test_moe_ffn_block_other_k_types(be, orc):
+    """Experts in Q5_K / Q2_K / Q3_K (the types real Q*_K_M / Q*_K_S checkpoints
+    mix in): moeFfnBlock through the general slot kernels against the oracle."""
+    rng = np.random.default_rng(33)
+    dim, ffn = 1024, 512
+    from tests import npref
+    ex, oex = [], []
+    for gt, ut, dt, w in [(13, 13, 13, 0.6), (10, 11, 10, 0.3), (11, 13, 12, 0.1)]:
+        g = npref.random_blocks(rng, gt, ffn, dim)
+        u = npref.random_blocks(rng, ut, ffn, dim)
+        d = npref.random_blocks(rng, dt, dim, ffn)
+        ex.append(B.ExpertRef(B.WeightRef(gt, g), B.WeightRef(ut, u), B.WeightRef(dt, d), w, ffn))
+        oex.append(dict(gate_type=gt, up_type=ut, down_type=dt, gate=g, up=u, down=d, weight=w, ffn=ffn))
+    x = rng.standard_normal(dim).astype(np.float32)
+    out = np.full(dim, np.nan, np.float32)
+    assert B.moeFfnBlock(x, ex, out)
+    want = orc.moe_ffn_block(x, oex, dim)
+    assert rel_l2(out, want) < TOL

@@ -273,3 +273,75 @@ def test_argmax_ties_nan_and_inf(orc):
     assert f([np.nan, np.nan]) == 0
     assert f([-np.inf, -5.0, np.inf, np.inf]) == 2
     assert f([0.0, -0.0]) == 0 and f([-0.0, 0.0]) == 0
+
+
+def test_q5k_high_bit_adds_16(orc):
+    """ggml.zig:1979-1990: d = 1, dmin = 0, sc(sub-block 0) = 1, qh bit 0 of byte 0 set, qs zero."""
+    blk = np.zeros(176, np.uint8)
+    blk[0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    blk[4] = 1
+    blk[16] = 1
+    v = orc.dequant_row(13, blk, 0, 256)
+    assert abs(v[0] - 16.0) < 1e-4 and abs(v[1]) < 1e-4
+
+
+@pytest.mark.parametrize("t", [10, 11, 13])
+def test_new_k_types_matvec_agrees_with_dequant(orc, t):
+    """ggml.zig:2021-2087 for q2_k / q3_k / q5_k: random bytes (one f16 exponent
+    bit cleared so no scale is NaN/Inf), int8-activation matvec within
+    mass * 0.01 of dequant-then-dot; matmul bit-identical to n matvecs."""
+    rng = np.random.default_rng(t)
+    cols, rows = 512, 3
+    data = rng.integers(0, 256, rows * (cols // 256) * orc.BLOCK_BYTES[t], dtype=np.uint8)
+    data[1::2] &= 0xFB
+    x = ((rng.random(cols) - 0.5) * 4.0).astype(np.float32)
+    got = orc.matvec(t, data, x, rows, cols)
+    for r in range(rows):
+        w = orc.dequant_row(t, data, r, cols).astype(np.float64)
+        want, mass = float(np.sum(w * x)), float(np.sum(np.abs(w * x)))
+        assert abs(got[r] - want) <= mass * 0.01, (t, r, got[r], want)
+    xs = ((rng.random((4, cols)) - 0.5) * 4.0).astype(np.float32)
+    mm = orc.matmul(t, data, xs, rows, cols)
+    for k in range(4):
+        assert np.array_equal(np.asarray(mm).reshape(4, rows)[k].view(np.uint32),
+                              orc.matvec(t, data, xs[k], rows, cols).view(np.uint32))
+
+
+def test_q2k_q3k_decode_matches_numpy_restatement(orc):
+    """Independent numpy restatement of dequantBlockQ2K (:1476) and
+    dequantBlockQ3K (:1508), including q3kScales (:1173)."""
+    rng = np.random.default_rng(3)
+    b2 = rng.integers(0, 256, 84, dtype=np.uint8)
+    b2[81] &= 0xFB
+    b2[83] &= 0xFB
+    d, dmin = np.frombuffer(b2[80:82].tobytes(), np.float16)[0], np.frombuffer(b2[82:84].tobytes(), np.float16)[0]
+    want = []
+    for n in range(2):
+        for j in range(4):
+            for half in range(2):
+                sc = b2[8 * n + 2 * j + half]
+                dl, ml = np.float32(d) * np.float32(sc & 15), np.float32(dmin) * np.float32(sc >> 4)
+                for l in range(16):
+                    q = (int(b2[16 + 32 * n + half * 16 + l]) >> (2 * j)) & 3
+                    want.append(np.float32(dl * np.float32(q)) - ml)
+    assert np.array_equal(np.array(want, np.float32).view(np.uint32), orc.dequant_row(10, b2, 0, 256).view(np.uint32))
+    b3 = rng.integers(0, 256, 110, dtype=np.uint8)
+    b3[109] &= 0xFB
+    aux = np.frombuffer(b3[96:108].tobytes(), np.uint32).copy()
+    a0, a1, tmp = int(aux[0]), int(aux[1]), int(aux[2])
+    m1, m2 = 0x03030303, 0x0f0f0f0f
+    words = [(a0 & m2) | (((tmp >> 0) & m1) << 4), (a1 & m2) | (((tmp >> 2) & m1) << 4),
+             ((a0 >> 4) & m2) | (((tmp >> 4) & m1) << 4), ((a1 >> 4) & m2) | (((tmp >> 6) & m1) << 4)]
+    sc16 = np.frombuffer(np.array(words, np.uint32).tobytes(), np.uint8).astype(np.int32) - 32
+    d3 = np.float32(np.frombuffer(b3[108:110].tobytes(), np.float16)[0])
+    want = []
+    for n in range(2):
+        for j in range(4):
+            m = 1 << (4 * n + j)
+            for half in range(2):
+                dl = d3 * np.float32(sc16[8 * n + 2 * j + half])
+                for l in range(16):
+                    idx = half * 16 + l
+                    q = (int(b3[32 + 32 * n + idx]) >> (2 * j)) & 3
+                    want.append(dl * np.float32(q - (0 if b3[idx] & m else 4)))
+    assert np.array_equal(np.array(want, np.float32).view(np.uint32), orc.dequant_row(11, b3, 0, 256).view(np.uint32))
