@@ -38,6 +38,8 @@ extern "C" {
 enum {
     LOOM_F32 = 0,
     LOOM_Q4_0 = 2,
+    LOOM_Q4_1 = 3,
+    LOOM_Q5_1 = 7,
     LOOM_Q8_0 = 8,
     LOOM_Q2_K = 10,
     LOOM_Q3_K = 11,

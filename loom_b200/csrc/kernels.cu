@@ -83,6 +83,15 @@ __global__ void k_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, ui
                 blk[208] = d & 0xFF; blk[209] = d >> 8;
                 break;
             }
+            case T_Q4_1:
+            case T_Q5_1: {
+                uint8_t *blk = raw + i * (type == T_Q4_1 ? 20 : 24);
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                uint16_t m = rand_scale(rword(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8; blk[2] = m & 0xFF; blk[3] = m >> 8;
+                put_bytes(blk + 4, type == T_Q4_1 ? 16 : 20, seed, w0 + 2);
+                break;
+            }
             case T_Q5_K: {
                 uint8_t *blk = raw + i * 176;
                 uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
@@ -150,6 +159,17 @@ __global__ void k_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, 
                 for (int i = 0; i < 32; i++) q[b * 32 + i] = src[2 + i];
                 break;
             }
+            case T_Q4_1:
+            case T_Q5_1: {  // quants | d, m | (Q5_1) the 32 high bits
+                const uint8_t *src = raw + b * (type == T_Q4_1 ? 20 : 24);
+                const int qo = type == T_Q4_1 ? 4 : 8;
+                for (int i = 0; i < 16; i++) q[b * 16 + i] = src[qo + i];
+                d[2 * b] = (uint16_t)(src[0] | (src[1] << 8));
+                d[2 * b + 1] = (uint16_t)(src[2] | (src[3] << 8));
+                if (type == T_Q5_1)
+                    for (int i = 0; i < 4; i++) sc[b * 4 + i] = src[4 + i];
+                break;
+            }
             case T_Q2_K: {  // scales + quants | d, dmin
                 const uint8_t *src = raw + b * 84;
                 for (int i = 0; i < 80; i++) q[b * 80 + i] = src[i];
@@ -191,6 +211,19 @@ __global__ void k_unpack(WDev w, uint8_t *raw, uint64_t nblk) {
             case T_Q5_K:
                 for (int i = 0; i < 176; i++) raw[b * 176 + i] = w.q[b * 176 + i];
                 break;
+            case T_Q4_1:
+            case T_Q5_1: {
+                const bool q5 = w.type == T_Q5_1;
+                uint8_t *dst = raw + b * (q5 ? 24 : 20);
+                dst[0] = w.d[2 * b] & 0xFF;
+                dst[1] = w.d[2 * b] >> 8;
+                dst[2] = w.d[2 * b + 1] & 0xFF;
+                dst[3] = w.d[2 * b + 1] >> 8;
+                if (q5)
+                    for (int i = 0; i < 4; i++) dst[4 + i] = w.sc[b * 4 + i];
+                for (int i = 0; i < 16; i++) dst[(q5 ? 8 : 4) + i] = w.q[b * 16 + i];
+                break;
+            }
             case T_Q2_K: {
                 uint8_t *dst = raw + b * 84;
                 for (int i = 0; i < 80; i++) dst[i] = w.q[b * 80 + i];
@@ -283,6 +316,18 @@ __global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
                 }
                 const float s = fmul(d, (float)scs[8 * n + l / 16 + 2 * g]);
                 v = fmul(s, fsub((float)q, 32.0f));
+                break;
+            }
+            case T_Q4_1:
+            case T_Q5_1: {  // dequantRow :1795: q*d + m
+                const uint8_t byte = w.q[gb * 16 + (i & 15)];
+                int q = i < 16 ? (byte & 0x0F) : (byte >> 4);
+                if (w.type == T_Q5_1) {
+                    const uint32_t qh = (uint32_t)w.sc[gb * 4] | ((uint32_t)w.sc[gb * 4 + 1] << 8) |
+                                        ((uint32_t)w.sc[gb * 4 + 2] << 16) | ((uint32_t)w.sc[gb * 4 + 3] << 24);
+                    q |= (int)((qh >> i) & 1) << 4;  // value i < 16: bit i; value 16 + j: bit 16 + j
+                }
+                v = fadd(fmul((float)q, f16_to_f32(w.d[2 * gb])), f16_to_f32(w.d[2 * gb + 1]));
                 break;
             }
             case T_Q5_K: {  // dequantBlockQ5K :1376: (d*sc)*(q + 16 h) - (dmin*m)

@@ -238,6 +238,62 @@ __device__ __forceinline__ void rowdot_q40(const WDev &w, uint64_t gb0, int nb, 
     }
 }
 
+// ---- Q4_1 / Q5_1 (matvecQ41Int :1242): one lane per block ------------------------------
+// dot over the unsigned (5-bit) quants, the min folded out as m * sum(xq):
+// term = xd * (d*dot + m*sum). Q5_1's fifth bits: value i < 16 takes bit i of
+// qh, value 16 + i bit 16 + i; spread4 moves four bits to bit 4 of four bytes.
+__device__ __forceinline__ uint32_t spread4(uint32_t b) {
+    return ((b & 1u) << 4) | ((b & 2u) << 11) | ((b & 4u) << 18) | ((b & 8u) << 25);
+}
+
+template <int TY, int NT>
+__device__ __forceinline__ void rowdot_q41(const WDev &w, uint64_t gb0, int nb, const XQ &x, int t0, int nt,
+                                           float (&acc)[NT], int lane) {
+    for (int b0 = 0; b0 < nb; b0 += 32) {
+        const int b = b0 + lane;
+        const bool live = b < nb;
+        uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+        float d = 0.0f, m = 0.0f;
+        if (live) {
+            const uint64_t gb = gb0 + b;
+            const uint4 qv = ld_stream_v4(w.q + gb * 16);
+            const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+            uint32_t qh = 0;
+            if (TY == T_Q5_1) qh = __ldg(reinterpret_cast<const uint32_t *>(w.sc) + gb);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                lo[k] = (qw[k] & 0x0F0F0F0Fu) | (TY == T_Q5_1 ? spread4((qh >> (4 * k)) & 0xF) : 0u);
+                hi[k] = ((qw[k] >> 4) & 0x0F0F0F0Fu) | (TY == T_Q5_1 ? spread4((qh >> (16 + 4 * k)) & 0xF) : 0u);
+            }
+            d = f16_to_f32(__ldg(w.d + 2 * gb));
+            m = f16_to_f32(__ldg(w.d + 2 * gb + 1));
+        }
+#pragma unroll
+        for (int k = 0; k < NT; k++) {
+            float term = 0.0f;
+            if (live && k < nt) {
+                const int t = t0 + k;
+                const int8_t *xb = x.q + (size_t)t * x.cols + b * 32;
+                const int4 xl = ld_i4(xb), xh = ld_i4(xb + 16);
+                int dot = 0;
+                dot = dp4a((int)lo[0], xl.x, dot);
+                dot = dp4a((int)lo[1], xl.y, dot);
+                dot = dp4a((int)lo[2], xl.z, dot);
+                dot = dp4a((int)lo[3], xl.w, dot);
+                dot = dp4a((int)hi[0], xh.x, dot);
+                dot = dp4a((int)hi[1], xh.y, dot);
+                dot = dp4a((int)hi[2], xh.z, dot);
+                dot = dp4a((int)hi[3], xh.w, dot);
+                const int sum = __ldg(x.s + (size_t)t * x.sstride + b);
+                const float xd = __ldg(x.d + (size_t)t * x.dstride + b);
+                term = fmul(xd, fadd(fmul(d, (float)dot), fmul(m, (float)sum)));
+            }
+            const int lim = min(32, nb - b0);
+            for (int g = 0; g < lim; g++) acc[k] = fadd(acc[k], __shfl_sync(0xffffffffu, term, g));
+        }
+    }
+}
+
 // ---- F32 (dotF32 order) ------------------------------------------------------------
 // Lane j is accumulator lane j of dotF32's four 8-wide vectors (acc(j/8)[j%8]).
 __device__ __forceinline__ float rowdot_f32(const float *__restrict__ row, const float *__restrict__ xv, int n,
@@ -393,6 +449,8 @@ __device__ __forceinline__ void rowdot(const WDev &w, uint64_t gb0, int nb, cons
         case T_Q8_0: rowdot_q80<NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         case T_Q4_0: rowdot_q40<NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         case T_Q5_K: rowdot_kq<T_Q5_K, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
+        case T_Q4_1: rowdot_q41<T_Q4_1, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
+        case T_Q5_1: rowdot_q41<T_Q5_1, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         case T_Q2_K: rowdot_kq<T_Q2_K, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         case T_Q3_K: rowdot_kq<T_Q3_K, NT>(w, gb0, nb, x, t0, nt, acc, lane); break;
         default: break;

@@ -46,7 +46,7 @@ int decline(const char *why) {
     } while (0)
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
-bool type_ok(int t) { return t == T_F32 || t == T_Q4_0 || t == T_Q8_0 || is_kquant(t); }
+bool type_ok(int t) { return t == T_F32 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_1 || t == T_Q8_0 || is_kquant(t); }
 // types stored as their GGUF blocks unchanged (16-byte multiples)
 bool raw_layout(int t) { return t == T_F32 || t == T_Q4_K || t == T_Q5_K; }
 
@@ -132,9 +132,10 @@ int alloc_tensor(int type, uint64_t nblk, Tensor &t) {
     t.type = type;
     t.nblk = nblk;
     const size_t qb = align256(nblk * (size_t)layout_qbytes(type));
-    const size_t scb = (type == T_Q6_K || type == T_Q3_K) ? align256(nblk * 16) : 0;
+    const size_t scb = (type == T_Q6_K || type == T_Q3_K) ? align256(nblk * 16)
+                     : type == T_Q5_1 ? align256(nblk * 4) : 0;  // Q5_1: the 32 high bits
     const size_t db = (type == T_Q6_K || type == T_Q8_0 || type == T_Q4_0 || type == T_Q3_K) ? align256(nblk * 2)
-                    : type == T_Q2_K ? align256(nblk * 4) : 0;  // Q2_K: d and dmin
+                    : (type == T_Q2_K || type == T_Q4_1 || type == T_Q5_1) ? align256(nblk * 4) : 0;  // d and dmin / m
     t.dev_bytes = qb + scb + db;
     cudaError_t e = cudaMalloc(&t.base, std::max<size_t>(t.dev_bytes, 256));
     if (e != cudaSuccess) return fail("cudaMalloc(tensor)", e);

@@ -26,6 +26,8 @@ constexpr size_t QK_K = 256;
 constexpr size_t Q4_0_BLOCK = 18;
 constexpr size_t Q8_0_BLOCK = 34;
 constexpr size_t Q4_K_BLOCK = 144;
+constexpr size_t Q4_1_BLOCK = 20;   // ggml.zig:89: d, m, qs[16]
+constexpr size_t Q5_1_BLOCK = 24;   // ggml.zig:91: d, m, qh (u32), qs[16]
 constexpr size_t Q5_K_BLOCK = 176;  // ggml.zig:87-159: d, dmin, scales[12], qh[32], qs[128]
 constexpr size_t Q2_K_BLOCK = 84;   // scales[16], qs[64], d, dmin
 constexpr size_t Q3_K_BLOCK = 110;  // hmask[32], qs[64], scales[12], d
@@ -220,6 +222,23 @@ inline float q40_block_dot(const uint8_t *blk, const int8_t *xq, float xd) {
     return d * xd * (float)(dot - 8 * sum);
 }
 
+// ggml.zig:1242-1275 matvecQ41Int (q4_1 / q5_1), one block: the min folds
+// out as m * sum(xq): xd * (d * dot + m * sum)
+inline float q41_block_dot(int t, const uint8_t *blk, const int8_t *xq, float xd) {
+    const float d = f16at(blk), m = f16at(blk + 2);
+    uint32_t qh = 0;
+    if (t == OR_Q5_1) std::memcpy(&qh, blk + 4, 4);
+    const uint8_t *qs = blk + (t == OR_Q5_1 ? 8 : 4);
+    int32_t dot = 0, sum = 0;
+    for (int i = 0; i < 16; i++) {
+        const int32_t lo = (qs[i] & 0x0F) | (t == OR_Q5_1 ? (int32_t)(((qh >> i) << 4) & 0x10) : 0);
+        const int32_t hi = (qs[i] >> 4) | (t == OR_Q5_1 ? (int32_t)((qh >> (i + 12)) & 0x10) : 0);
+        dot += lo * (int32_t)xq[i] + hi * (int32_t)xq[i + 16];
+        sum += (int32_t)xq[i] + (int32_t)xq[i + 16];
+    }
+    return xd * (d * (float)dot + m * (float)sum);
+}
+
 // ggml.zig:1277-1294 matvecQ80Int, one block
 inline float q80_block_dot(const uint8_t *blk, const int8_t *xq, float xd) {
     const float d = f16at(blk);
@@ -343,6 +362,12 @@ float row_dot(int t, const uint8_t *row, const XQ &xq, size_t cols) {
             for (size_t b = 0; b < cols / QK_0; b++)
                 acc += q40_block_dot(row + b * Q4_0_BLOCK, &xq.q[b * QK_0], xq.d[b]);
             break;
+        case OR_Q4_1:
+        case OR_Q5_1: {
+            const size_t bb = or_block_bytes(t);
+            for (size_t b = 0; b < cols / QK_0; b++) acc += q41_block_dot(t, row + b * bb, &xq.q[b * QK_0], xq.d[b]);
+            break;
+        }
         case OR_Q2_K:
         case OR_Q3_K:
         case OR_Q5_K: {  // matvecK256 :1024 over the uniform decode
@@ -448,7 +473,7 @@ extern "C" {
 size_t or_block_elems(int t) {
     switch (t) {
         case OR_F32: case OR_F16: return 1;
-        case OR_Q4_0: case OR_Q8_0: return QK_0;
+        case OR_Q4_0: case OR_Q4_1: case OR_Q5_1: case OR_Q8_0: return QK_0;
         case OR_Q2_K: case OR_Q3_K: case OR_Q4_K: case OR_Q5_K: case OR_Q6_K: return QK_K;
     }
     return 0;
@@ -465,6 +490,8 @@ size_t or_block_bytes(int t) {
         case OR_Q2_K: return Q2_K_BLOCK;
         case OR_Q3_K: return Q3_K_BLOCK;
         case OR_Q5_K: return Q5_K_BLOCK;
+        case OR_Q4_1: return Q4_1_BLOCK;
+        case OR_Q5_1: return Q5_1_BLOCK;
     }
     return 0;
 }
@@ -635,6 +662,22 @@ int or_dequant_row(int t, float *out, const uint8_t *data, size_t r, size_t cols
                             }
                         }
                     }
+            }
+            return 0;
+        case OR_Q4_1:
+        case OR_Q5_1:  // dequantRow :1795-1819: q * d + m
+            for (size_t b = 0; b < cols / QK_0; b++) {
+                const uint8_t *blk = row + b * or_block_bytes(t);
+                const float d = f16at(blk), m = f16at(blk + 2);
+                uint32_t qh = 0;
+                if (t == OR_Q5_1) std::memcpy(&qh, blk + 4, 4);
+                const uint8_t *qs = blk + (t == OR_Q5_1 ? 8 : 4);
+                for (int j = 0; j < 16; j++) {
+                    const int lo = (qs[j] & 0x0F) | (t == OR_Q5_1 ? (int)(((qh >> j) << 4) & 0x10) : 0);
+                    const int hi = (qs[j] >> 4) | (t == OR_Q5_1 ? (int)((qh >> (j + 12)) & 0x10) : 0);
+                    out[b * 32 + j] = (float)lo * d + m;
+                    out[b * 32 + j + 16] = (float)hi * d + m;
+                }
             }
             return 0;
         case OR_Q4_0:
@@ -977,6 +1020,15 @@ void or_synth(int type, void *out, uint64_t blk0, uint64_t nblk, uint64_t seed, 
                 for (int k = 0; k < 16; k++) blk[192 + k] = (uint8_t)(int8_t)((int)(sc[k] % 64) - 32);
                 uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
                 blk[208] = d & 0xFF; blk[209] = d >> 8;
+                break;
+            }
+            case OR_Q4_1:
+            case OR_Q5_1: {  // f16 d, m ~U(1e-3, 1e-2), random (high bits and) nibbles
+                uint8_t *blk = o + i * (type == OR_Q4_1 ? Q4_1_BLOCK : Q5_1_BLOCK);
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                uint16_t m = rand_scale(word(seed, w0 + 1), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8; blk[2] = m & 0xFF; blk[3] = m >> 8;
+                put_bytes(blk + 4, type == OR_Q4_1 ? 16 : 20, seed, w0 + 2);
                 break;
             }
             case OR_Q5_K: {  // as Q4_K: f16 d, dmin ~U(1e-3, 1e-2), random scales, high bits and nibbles

@@ -89,7 +89,7 @@ def test_moe_ffn_routed_deepseek_shared(be, orc, sigmoid):
     assert rel_l2(out, want) < TOL
 
 
-@pytest.mark.parametrize("t", [0, 2, 8, 10, 11, 12, 13, 14])
+@pytest.mark.parametrize("t", [0, 2, 3, 7, 8, 10, 11, 12, 13, 14])
 def test_device_synth_matches_oracle(be, orc, t):
     nblk = 1000
     dt = DeviceTensor.synth(t, nblk, seed=77, sigma=0.02)
@@ -305,13 +305,14 @@ def test_grouped_routing_declines_bad_groups(be, orc):
 
 
 def test_moe_ffn_block_other_k_types(be, orc):
-    """Experts in Q5_K / Q2_K / Q3_K (the types real Q*_K_M / Q*_K_S checkpoints
-    mix in): moeFfnBlock through the general slot kernels against the oracle."""
+    """Experts in Q5_K / Q2_K / Q3_K / Q4_1 / Q5_1 (the types real Q*_K_M / Q*_K_S
+    checkpoints mix in; DeepSeek-Coder-V2-Lite's ffn_down_exps are Q5_1):
+    moeFfnBlock through the general slot kernels against the oracle."""
     rng = np.random.default_rng(33)
     dim, ffn = 1024, 512
     from tests import npref
     ex, oex = [], []
-    for gt, ut, dt, w in [(13, 13, 13, 0.6), (10, 11, 10, 0.3), (11, 13, 12, 0.1)]:
+    for gt, ut, dt, w in [(13, 13, 13, 0.6), (10, 11, 10, 0.3), (11, 13, 12, 0.1), (12, 12, 7, 0.4), (3, 7, 3, 0.2)]:
         g = npref.random_blocks(rng, gt, ffn, dim)
         u = npref.random_blocks(rng, ut, ffn, dim)
         d = npref.random_blocks(rng, dt, dim, ffn)

@@ -285,14 +285,14 @@ def test_q5k_high_bit_adds_16(orc):
     assert abs(v[0] - 16.0) < 1e-4 and abs(v[1]) < 1e-4
 
 
-@pytest.mark.parametrize("t", [10, 11, 13])
+@pytest.mark.parametrize("t", [3, 7, 10, 11, 13])
 def test_new_k_types_matvec_agrees_with_dequant(orc, t):
-    """ggml.zig:2021-2087 for q2_k / q3_k / q5_k: random bytes (one f16 exponent
+    """ggml.zig:2021-2087 for q4_1 / q5_1 / q2_k / q3_k / q5_k: random bytes (one f16 exponent
     bit cleared so no scale is NaN/Inf), int8-activation matvec within
     mass * 0.01 of dequant-then-dot; matmul bit-identical to n matvecs."""
     rng = np.random.default_rng(t)
     cols, rows = 512, 3
-    data = rng.integers(0, 256, rows * (cols // 256) * orc.BLOCK_BYTES[t], dtype=np.uint8)
+    data = rng.integers(0, 256, rows * (cols // orc.BLOCK_ELEMS[t]) * orc.BLOCK_BYTES[t], dtype=np.uint8)
     data[1::2] &= 0xFB
     x = ((rng.random(cols) - 0.5) * 4.0).astype(np.float32)
     got = orc.matvec(t, data, x, rows, cols)
@@ -345,3 +345,20 @@ def test_q2k_q3k_decode_matches_numpy_restatement(orc):
                     q = (int(b3[32 + 32 * n + idx]) >> (2 * j)) & 3
                     want.append(dl * np.float32(q - (0 if b3[idx] & m else 4)))
     assert np.array_equal(np.array(want, np.float32).view(np.uint32), orc.dequant_row(11, b3, 0, 256).view(np.uint32))
+
+
+def test_q51_matches_numpy_restatement(orc):
+    """matvecQ41Int (:1242) and dequantRow (:1795) for q5_1, restated in numpy."""
+    rng = np.random.default_rng(71)
+    blk = rng.integers(0, 256, 24, dtype=np.uint8)
+    blk[1] &= 0xFB
+    blk[3] &= 0xFB
+    d, m = (np.float32(v) for v in np.frombuffer(blk[0:4].tobytes(), np.float16))
+    qh = int(np.frombuffer(blk[4:8].tobytes(), np.uint32)[0])
+    want = np.zeros(32, np.float32)
+    for j in range(16):
+        lo = (int(blk[8 + j]) & 15) | (((qh >> j) << 4) & 0x10)
+        hi = (int(blk[8 + j]) >> 4) | ((qh >> (j + 12)) & 0x10)
+        want[j] = np.float32(np.float32(lo) * d) + m
+        want[j + 16] = np.float32(np.float32(hi) * d) + m
+    assert np.array_equal(want.view(np.uint32), orc.dequant_row(7, blk, 0, 32).view(np.uint32))
