@@ -305,16 +305,23 @@ __device__ __forceinline__ void route_warp_vals(float (&v)[RW], const float *bia
                     const float ts = sv[j]; sv[j] = sv[j - 1]; sv[j - 1] = ts;
                 }
             }
+        // k rounds; the winner's value and index reach every lane by shuffle (off the
+        // rounds' dependency chain) and lane k keeps pick k in registers, while
+        // the renormalisation sum runs in selection order as the picks arrive
+        int my_id = 0;
+        float my_g = 0.0f, sum = 0.0f;
         for (int k = 0; k < nk; k++) {
             const uint32_t kmax = __reduce_max_sync(0xffffffffu, key[0]);
             const bool mine = key[0] == kmax;
             const uint32_t ball = __ballot_sync(0xffffffffu, mine);
-            bool win = mine;
-            if (__popc(ball) > 1)  // equal values: the lowest index wins
-                win = mine && (uint32_t)ei[0] == __reduce_min_sync(0xffffffffu, mine ? (uint32_t)ei[0] : 0xffffffffu);
-            if (win) {
-                ids[k] = ei[0];
-                gates[k] = sv[0];
+            int wl = __ffs(ball) - 1;
+            if (__popc(ball) > 1) {  // equal values: the lowest index wins
+                const uint32_t emin = __reduce_min_sync(0xffffffffu, mine ? (uint32_t)ei[0] : 0xffffffffu);
+                wl = __ffs(__ballot_sync(0xffffffffu, mine && (uint32_t)ei[0] == emin)) - 1;
+            }
+            const float gk = __shfl_sync(0xffffffffu, sv[0], wl);
+            const int ik = __shfl_sync(0xffffffffu, ei[0], wl);
+            if (lane == wl) {
 #pragma unroll
                 for (int t = 0; t + 1 < RW; t++) {
                     key[t] = key[t + 1];
@@ -323,6 +330,35 @@ __device__ __forceinline__ void route_warp_vals(float (&v)[RW], const float *bia
                 }
                 key[RW - 1] = 0u;
             }
+            if (k < 32 && lane == k) {
+                my_id = ik;
+                my_g = gk;
+            }
+            if (gating != 3) sum = fadd(sum, gk);
+            if (k >= 32 || gating == 3) {  // the general tail keeps the picks in shared memory
+                if (lane == 0) {
+                    ids[k] = ik;
+                    gates[k] = gk;
+                }
+            }
+        }
+        if (gating != 3 && nk <= 32) {  // the tail of route_finish (moe.zig:149-157), lane k for pick k
+            const float denom = fmaxf(sum, 6.103515625e-5f);
+            if (lane < nk) {
+                float g = my_g;
+                if (weights_norm) g = fdiv(g, denom);
+                if (weights_scale != 1.0f) g = fmul(g, weights_scale);
+                ids_out[lane] = my_id;
+                gates_out[lane] = g;
+                ids[lane] = my_id;
+                gates[lane] = g;
+            }
+            __syncwarp();
+            return;
+        }
+        if (lane < nk && lane < 32) {
+            ids[lane] = my_id;
+            gates[lane] = my_g;
         }
     } else {
 #pragma unroll
