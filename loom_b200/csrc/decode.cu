@@ -1568,8 +1568,10 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 for (int b = warp - (PS_WARPS - nq); b < NBG; b += nq)
                     quant_block256_padded<false>(S.xs + b * 256, S.xq + b * XPAD_BLOCK, S.xqd + b, S.xqs + b * 16, lane);
             }
-            if (nrw > 0) {  // rbuf is free once the dots are done: stage the next layer's router rows
-                __syncthreads();
+            if (warp < nrw) {  // rbuf is free once the router warps' dots are done: stage the next layer's rows
+                // (only the router warps meet: the route of P2 need not wait for x's quantization)
+                if (nrw == 1) __syncwarp();
+                else asm volatile("bar.sync 5, %0;" ::"r"((nrw < PS_WARPS ? nrw : PS_WARPS) * 32) : "memory");
                 if (l + 1 < A.n_layers && threadIdx.x == 0) stage_router_rows(A, l + 1, S.rbuf, S.mbar + MB_ROUTER);
             }
         }
