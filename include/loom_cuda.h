@@ -39,6 +39,7 @@ enum {
     LOOM_F32 = 0,
     LOOM_Q4_0 = 2,
     LOOM_Q4_1 = 3,
+    LOOM_Q5_0 = 6,
     LOOM_Q5_1 = 7,
     LOOM_Q8_0 = 8,
     LOOM_Q2_K = 10,

@@ -25,7 +25,7 @@
 namespace loom {
 
 enum GgmlType : int {
-    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12,
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12,
     T_Q5_K = 13, T_Q6_K = 14
 };
 __host__ __device__ constexpr bool is_kquant(int t) {
@@ -36,17 +36,18 @@ constexpr int QK_0 = 32;
 constexpr int QK_K = 256;
 
 __host__ __device__ constexpr int block_elems(int t) {
-    return t == T_F32 ? 1 : (t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_1 || t == T_Q8_0) ? QK_0 : is_kquant(t) ? QK_K : 0;
+    return t == T_F32 ? 1 : (t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_1 || t == T_Q8_0) ? QK_0
+         : is_kquant(t) ? QK_K : 0;
 }
 __host__ __device__ constexpr int block_bytes(int t) {
     return t == T_F32 ? 4 : t == T_Q4_0 ? 18 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_Q6_K ? 210
-         : t == T_Q2_K ? 84 : t == T_Q3_K ? 110 : t == T_Q5_K ? 176 : t == T_Q4_1 ? 20 : t == T_Q5_1 ? 24 : 0;
+         : t == T_Q2_K ? 84 : t == T_Q3_K ? 110 : t == T_Q5_K ? 176 : t == T_Q4_1 ? 20 : t == T_Q5_1 ? 24 : t == T_Q5_0 ? 22 : 0;
 }
 // bytes of the quant region per block in the device layout (Q2_K: scales +
 // quants; Q3_K: high-bit mask + quants; Q4_K / Q5_K: the whole block)
 __host__ __device__ constexpr int layout_qbytes(int t) {
     return t == T_F32 ? 4 : t == T_Q4_0 ? 16 : t == T_Q8_0 ? 32 : t == T_Q4_K ? 144 : t == T_Q6_K ? 192
-         : t == T_Q2_K ? 80 : t == T_Q3_K ? 96 : t == T_Q5_K ? 176 : (t == T_Q4_1 || t == T_Q5_1) ? 16 : 0;
+         : t == T_Q2_K ? 80 : t == T_Q3_K ? 96 : t == T_Q5_K ? 176 : (t == T_Q4_1 || t == T_Q5_1 || t == T_Q5_0) ? 16 : 0;
 }
 // true when a type's activation is quantized per 256 (Q8_K style) rather than per 32
 __host__ __device__ constexpr bool act256(int t) { return is_kquant(t) || t == 112; }

@@ -83,6 +83,13 @@ __global__ void k_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, ui
                 blk[208] = d & 0xFF; blk[209] = d >> 8;
                 break;
             }
+            case T_Q5_0: {
+                uint8_t *blk = raw + i * 22;
+                uint16_t d = rand_scale(rword(seed, w0), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8;
+                put_bytes(blk + 2, 20, seed, w0 + 2);
+                break;
+            }
             case T_Q4_1:
             case T_Q5_1: {
                 uint8_t *blk = raw + i * (type == T_Q4_1 ? 20 : 24);
@@ -159,6 +166,13 @@ __global__ void k_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, 
                 for (int i = 0; i < 32; i++) q[b * 32 + i] = src[2 + i];
                 break;
             }
+            case T_Q5_0: {  // quants | d | the 32 high bits
+                const uint8_t *src = raw + b * 22;
+                d[b] = (uint16_t)(src[0] | (src[1] << 8));
+                for (int i = 0; i < 4; i++) sc[b * 4 + i] = src[2 + i];
+                for (int i = 0; i < 16; i++) q[b * 16 + i] = src[6 + i];
+                break;
+            }
             case T_Q4_1:
             case T_Q5_1: {  // quants | d, m | (Q5_1) the 32 high bits
                 const uint8_t *src = raw + b * (type == T_Q4_1 ? 20 : 24);
@@ -211,6 +225,14 @@ __global__ void k_unpack(WDev w, uint8_t *raw, uint64_t nblk) {
             case T_Q5_K:
                 for (int i = 0; i < 176; i++) raw[b * 176 + i] = w.q[b * 176 + i];
                 break;
+            case T_Q5_0: {
+                uint8_t *dst = raw + b * 22;
+                dst[0] = w.d[b] & 0xFF;
+                dst[1] = w.d[b] >> 8;
+                for (int i = 0; i < 4; i++) dst[2 + i] = w.sc[b * 4 + i];
+                for (int i = 0; i < 16; i++) dst[6 + i] = w.q[b * 16 + i];
+                break;
+            }
             case T_Q4_1:
             case T_Q5_1: {
                 const bool q5 = w.type == T_Q5_1;
@@ -316,6 +338,14 @@ __global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
                 }
                 const float s = fmul(d, (float)scs[8 * n + l / 16 + 2 * g]);
                 v = fmul(s, fsub((float)q, 32.0f));
+                break;
+            }
+            case T_Q5_0: {  // dequantRow :1772: (q - 16) * d
+                const uint8_t byte = w.q[gb * 16 + (i & 15)];
+                const uint32_t qh = (uint32_t)w.sc[gb * 4] | ((uint32_t)w.sc[gb * 4 + 1] << 8) |
+                                    ((uint32_t)w.sc[gb * 4 + 2] << 16) | ((uint32_t)w.sc[gb * 4 + 3] << 24);
+                const int q = (i < 16 ? (byte & 0x0F) : (byte >> 4)) | (int)((qh >> i) & 1) << 4;
+                v = fmul((float)(q - 16), f16_to_f32(w.d[gb]));
                 break;
             }
             case T_Q4_1:
@@ -448,6 +478,56 @@ void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x,
     if (rows == 0 || ntok == 0) return;
     const int nb = cols / block_elems(w.type);
     k_mm<<<cdiv(rows, 8), 256, 0, st>>>(w, gb_base, rows, nb, x, ntok, out);
+    count_launch();
+}
+
+// matvecQ50 (ggml.zig:1673-1704): one warp per (row, token); lane b takes
+// block b's partial (j = 0..15: partial += w0*x[j] + w1*x[j+16], in order),
+// a zero-scale block contributes nothing (the reference skips it, so its
+// non-finite activations never reach the sum), and the block terms
+// partial*scale are added in block order from +0.
+__global__ void __launch_bounds__(256) k_mm_q50(WDev w, uint64_t gb_base, int rows, int nb, const float *xs, int ntok,
+                                                float *out) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const int cols = nb * 32;
+    for (int t = 0; t < ntok; t++) {
+        const float *x = xs + (size_t)t * cols;
+        float acc = 0.0f;
+        for (int b0 = 0; b0 < nb; b0 += 32) {
+            const int b = b0 + lane;
+            float term = 0.0f;
+            if (b < nb) {
+                const uint64_t gb = gb_base + (uint64_t)r * nb + b;
+                const float scale = f16_to_f32(__ldg(w.d + gb));
+                if (scale != 0.0f) {
+                    const uint4 qv = ld_stream_v4(w.q + gb * 16);
+                    const uint32_t qh = __ldg(reinterpret_cast<const uint32_t *>(w.sc) + gb);
+                    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+                    const float *xb = x + (size_t)b * 32;
+                    float partial = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const uint32_t byte = (qw[j >> 2] >> (8 * (j & 3))) & 0xFF;
+                        const int q0 = (int)((byte & 0x0F) | (((qh >> j) << 4) & 0x10)) - 16;
+                        const int q1 = (int)((byte >> 4) | ((qh >> (j + 12)) & 0x10)) - 16;
+                        partial = fadd(partial, fadd(fmul((float)q0, __ldg(xb + j)), fmul((float)q1, __ldg(xb + j + 16))));
+                    }
+                    term = fmul(partial, scale);
+                }
+            }
+            const int lim = min(32, nb - b0);
+            for (int g = 0; g < lim; g++) acc = fadd(acc, __shfl_sync(0xffffffffu, term, g));
+        }
+        if (lane == 0) out[(size_t)t * rows + r] = acc;
+    }
+}
+
+void launch_mm_q50(const WDev &w, uint64_t gb_base, int rows, int cols, const float *xs, int ntok, float *out,
+                   cudaStream_t st) {
+    if (rows == 0 || ntok == 0) return;
+    k_mm_q50<<<cdiv(rows, 8), 256, 0, st>>>(w, gb_base, rows, cols / 32, xs, ntok, out);
     count_launch();
 }
 

@@ -47,6 +47,9 @@ void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind2
 void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x, int ntok, float *out,
                cudaStream_t st);
 void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out, cudaStream_t st);
+// Q5_0 on f32 activations (matvecQ50, ggml.zig:1673), out[k*rows + r]
+void launch_mm_q50(const WDev &w, uint64_t gb_base, int rows, int cols, const float *xs, int ntok, float *out,
+                   cudaStream_t st);
 void launch_route(const float *logits, const float *bias, int T, int n_expert, int n_used, int gating,
                   int weights_norm, float weights_scale, int *ids, float *gates, cudaStream_t st,
                   int n_group = 1, int topk_group = 1);

@@ -46,7 +46,9 @@ int decline(const char *why) {
     } while (0)
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
-bool type_ok(int t) { return t == T_F32 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_1 || t == T_Q8_0 || is_kquant(t); }
+bool type_ok(int t) {
+    return t == T_F32 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_1 || t == T_Q8_0 || is_kquant(t);
+}
 // types stored as their GGUF blocks unchanged (16-byte multiples)
 bool raw_layout(int t) { return t == T_F32 || t == T_Q4_K || t == T_Q5_K; }
 
@@ -133,8 +135,9 @@ int alloc_tensor(int type, uint64_t nblk, Tensor &t) {
     t.nblk = nblk;
     const size_t qb = align256(nblk * (size_t)layout_qbytes(type));
     const size_t scb = (type == T_Q6_K || type == T_Q3_K) ? align256(nblk * 16)
-                     : type == T_Q5_1 ? align256(nblk * 4) : 0;  // Q5_1: the 32 high bits
-    const size_t db = (type == T_Q6_K || type == T_Q8_0 || type == T_Q4_0 || type == T_Q3_K) ? align256(nblk * 2)
+                     : (type == T_Q5_1 || type == T_Q5_0) ? align256(nblk * 4) : 0;  // Q5_x: the 32 high bits
+    const size_t db = (type == T_Q6_K || type == T_Q8_0 || type == T_Q4_0 || type == T_Q3_K || type == T_Q5_0)
+                        ? align256(nblk * 2)
                     : (type == T_Q2_K || type == T_Q4_1 || type == T_Q5_1) ? align256(nblk * 4) : 0;  // d and dmin / m
     t.dev_bytes = qb + scb + db;
     cudaError_t e = cudaMalloc(&t.base, std::max<size_t>(t.dev_bytes, 256));
@@ -282,7 +285,8 @@ void quantize_inputs(const float *d_x, size_t T, size_t dim, bool need256, bool 
 
 int check_moe_types(const Tensor *g, const Tensor *u, const Tensor *d) {
     for (const Tensor *t : {g, u, d})
-        if (!t || t->type == T_F32) return decline("MoE expert tensors must be Q4_0, Q8_0, Q4_K or Q6_K");
+        if (!t || t->type == T_F32 || t->type == T_Q5_0)  // Q5_0 runs on f32 activations (matvecQ50)
+            return decline("MoE expert tensors must be a quantized type on int8 activations (not F32 or Q5_0)");
     return 0;
 }
 
@@ -674,6 +678,8 @@ int loom_cuda_matmul(int type, float *out, const void *w, size_t w_bytes, const 
     if (type == T_F32) {
         launch_mm_f32(reinterpret_cast<const float *>(t->base), (int)rows, (int)cols, S.io_in.as<float>(), (int)n,
                       S.io_out.as<float>(), g_stream);
+    } else if (type == T_Q5_0) {
+        launch_mm_q50(t->w, 0, (int)rows, (int)cols, S.io_in.as<float>(), (int)n, S.io_out.as<float>(), g_stream);
     } else {
         if (int rc = ensure_xq(n, cols)) return rc;
         quantize_into(S.io_in.as<float>(), n, cols, act256(type), g_stream);
@@ -1168,6 +1174,8 @@ int loom_cuda_tensor_matmul(loom_tensor h, size_t rows, size_t cols, const float
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
     if (t->type == T_F32) {
         launch_mm_f32(reinterpret_cast<const float *>(t->base), (int)rows, (int)cols, d_xs, (int)n, d_out, st);
+    } else if (t->type == T_Q5_0) {
+        launch_mm_q50(t->w, 0, (int)rows, (int)cols, d_xs, (int)n, d_out, st);
     } else {
         if (int rc = ensure_xq(n, cols)) return rc;
         quantize_into(d_xs, n, cols, act256(t->type), st);

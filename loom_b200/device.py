@@ -13,7 +13,7 @@ import numpy as np
 from . import _lib
 
 BLOCK_ELEMS = {0: 1, 2: 32, 8: 32, 12: 256, 14: 256}
-BLOCK_BYTES = {0: 4, 2: 18, 3: 20, 7: 24, 8: 34, 10: 84, 11: 110, 12: 144, 13: 176, 14: 210}
+BLOCK_BYTES = {0: 4, 2: 18, 3: 20, 6: 22, 7: 24, 8: 34, 10: 84, 11: 110, 12: 144, 13: 176, 14: 210}
 
 
 def _ptr(t) -> Optional[int]:

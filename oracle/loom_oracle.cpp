@@ -28,6 +28,7 @@ constexpr size_t Q8_0_BLOCK = 34;
 constexpr size_t Q4_K_BLOCK = 144;
 constexpr size_t Q4_1_BLOCK = 20;   // ggml.zig:89: d, m, qs[16]
 constexpr size_t Q5_1_BLOCK = 24;   // ggml.zig:91: d, m, qh (u32), qs[16]
+constexpr size_t Q5_0_BLOCK = 22;   // ggml.zig:90: d, qh (u32), qs[16]
 constexpr size_t Q5_K_BLOCK = 176;  // ggml.zig:87-159: d, dmin, scales[12], qh[32], qs[128]
 constexpr size_t Q2_K_BLOCK = 84;   // scales[16], qs[64], d, dmin
 constexpr size_t Q3_K_BLOCK = 110;  // hmask[32], qs[64], scales[12], d
@@ -473,7 +474,7 @@ extern "C" {
 size_t or_block_elems(int t) {
     switch (t) {
         case OR_F32: case OR_F16: return 1;
-        case OR_Q4_0: case OR_Q4_1: case OR_Q5_1: case OR_Q8_0: return QK_0;
+        case OR_Q4_0: case OR_Q4_1: case OR_Q5_0: case OR_Q5_1: case OR_Q8_0: return QK_0;
         case OR_Q2_K: case OR_Q3_K: case OR_Q4_K: case OR_Q5_K: case OR_Q6_K: return QK_K;
     }
     return 0;
@@ -492,6 +493,7 @@ size_t or_block_bytes(int t) {
         case OR_Q5_K: return Q5_K_BLOCK;
         case OR_Q4_1: return Q4_1_BLOCK;
         case OR_Q5_1: return Q5_1_BLOCK;
+        case OR_Q5_0: return Q5_0_BLOCK;
     }
     return 0;
 }
@@ -664,6 +666,19 @@ int or_dequant_row(int t, float *out, const uint8_t *data, size_t r, size_t cols
                     }
             }
             return 0;
+        case OR_Q5_0:  // dequantRow :1772-1793: (q - 16) * d
+            for (size_t b = 0; b < cols / QK_0; b++) {
+                const uint8_t *blk = row + b * Q5_0_BLOCK;
+                const float s = f16at(blk);
+                uint32_t qh;
+                std::memcpy(&qh, blk + 2, 4);
+                for (int j = 0; j < 16; j++) {
+                    const int xh0 = (int)(((qh >> j) << 4) & 0x10), xh1 = (int)((qh >> (j + 12)) & 0x10);
+                    out[b * 32 + j] = (float)(((blk[6 + j] & 0x0F) | xh0) - 16) * s;
+                    out[b * 32 + j + 16] = (float)(((blk[6 + j] >> 4) | xh1) - 16) * s;
+                }
+            }
+            return 0;
         case OR_Q4_1:
         case OR_Q5_1:  // dequantRow :1795-1819: q * d + m
             for (size_t b = 0; b < cols / QK_0; b++) {
@@ -704,7 +719,39 @@ int or_dequant_row(int t, float *out, const uint8_t *data, size_t r, size_t cols
 // ggml.zig:602-659 matvec/dispatch: the activation is quantized once per call
 // (matvecK256 :1024, matvecQ40Int :1196, matvecQ80Int :1277); rows are
 // independent dots, split over the pool.
+// ggml.zig:1673-1704 matvecQ50: q5_0 stays on f32 activations. Per block the
+// partial runs j = 0..15 as partial += w0*x[j] + w1*x[j+16]; blocks whose
+// scale is 0 are skipped; acc += partial * scale in block order.
+static float q50_row(const uint8_t *row, const float *x, size_t cols) {
+    float acc = 0.0f;
+    for (size_t b = 0; b < cols / QK_0; b++) {
+        const uint8_t *blk = row + b * Q5_0_BLOCK;
+        const float scale = f16at(blk);
+        if (scale == 0.0f) continue;
+        uint32_t qh;
+        std::memcpy(&qh, blk + 2, 4);
+        const float *xb = x + b * QK_0;
+        float partial = 0.0f;
+        for (int j = 0; j < 16; j++) {
+            const int xh0 = (int)(((qh >> j) << 4) & 0x10), xh1 = (int)((qh >> (j + 12)) & 0x10);
+            const float w0 = (float)(((blk[6 + j] & 0xF) | xh0) - 16);
+            const float w1 = (float)(((blk[6 + j] >> 4) | xh1) - 16);
+            partial += w0 * xb[j] + w1 * xb[j + 16];
+        }
+        acc += partial * scale;
+    }
+    return acc;
+}
+
 int or_matvec(int t, float *out, const uint8_t *data, const float *x, size_t rows, size_t cols) {
+    if (t == OR_Q5_0) {
+        if (cols % QK_0) return -1;
+        const size_t rb = or_row_bytes(t, cols);
+        parallel_rows(rows, [&](size_t r0, size_t r1) {
+            for (size_t r = r0; r < r1; r++) out[r] = q50_row(data + r * rb, x, cols);
+        });
+        return 0;
+    }
     if (t == OR_F32) {
         const float *w = (const float *)data;
         parallel_rows(rows, [&](size_t r0, size_t r1) {
@@ -727,7 +774,7 @@ int or_matvec(int t, float *out, const uint8_t *data, const float *x, size_t row
 // (the reference's own invariant, test ggml.zig:2132). Each token's activation
 // is quantized once; every row is decoded against all n tokens.
 int or_matmul(int t, float *out, const uint8_t *data, const float *xs, size_t n, size_t rows, size_t cols) {
-    if (t == OR_F32) {
+    if (t == OR_F32 || t == OR_Q5_0) {  // q5_0 has no batched kernel: n matvecs (ggml.zig:516-526)
         for (size_t k = 0; k < n; k++) or_matvec(t, out + k * rows, data, xs + k * cols, rows, cols);
         return 0;
     }
@@ -1020,6 +1067,13 @@ void or_synth(int type, void *out, uint64_t blk0, uint64_t nblk, uint64_t seed, 
                 for (int k = 0; k < 16; k++) blk[192 + k] = (uint8_t)(int8_t)((int)(sc[k] % 64) - 32);
                 uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
                 blk[208] = d & 0xFF; blk[209] = d >> 8;
+                break;
+            }
+            case OR_Q5_0: {  // f16 d ~U(1e-3, 1e-2), random high bits and nibbles
+                uint8_t *blk = o + i * Q5_0_BLOCK;
+                uint16_t d = rand_scale(word(seed, w0), 1e-3f, 9e-3f);
+                blk[0] = d & 0xFF; blk[1] = d >> 8;
+                put_bytes(blk + 2, 20, seed, w0 + 2);
                 break;
             }
             case OR_Q4_1:

@@ -24,7 +24,7 @@ extern "C" {
 #endif
 
 /* ggml type ids, src/gguf/ggml.zig:23-45 */
-enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q5_1 = 7, OR_Q8_0 = 8, OR_Q2_K = 10, OR_Q3_K = 11, OR_Q4_K = 12, OR_Q5_K = 13, OR_Q6_K = 14 };
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q5_0 = 6, OR_Q5_1 = 7, OR_Q8_0 = 8, OR_Q2_K = 10, OR_Q3_K = 11, OR_Q4_K = 12, OR_Q5_K = 13, OR_Q6_K = 14 };
 
 size_t or_row_bytes(int type, size_t n);          /* ggml.zig:103 rowBytes */
 size_t or_block_elems(int type);                  /* ggml.zig:128 blockElems */

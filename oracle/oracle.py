@@ -17,10 +17,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libloom_oracle.so")
 
-F32, F16, Q4_0, Q4_1, Q5_1, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 0, 1, 2, 3, 7, 8, 10, 11, 12, 13, 14
-BLOCK_ELEMS = {F32: 1, Q4_0: 32, Q4_1: 32, Q5_1: 32, Q8_0: 32, Q2_K: 256, Q3_K: 256, Q4_K: 256, Q5_K: 256,
+F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 0, 1, 2, 3, 6, 7, 8, 10, 11, 12, 13, 14
+BLOCK_ELEMS = {F32: 1, Q4_0: 32, Q4_1: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q2_K: 256, Q3_K: 256, Q4_K: 256, Q5_K: 256,
                Q6_K: 256}
-BLOCK_BYTES = {F32: 4, Q4_0: 18, Q4_1: 20, Q5_1: 24, Q8_0: 34, Q2_K: 84, Q3_K: 110, Q4_K: 144, Q5_K: 176,
+BLOCK_BYTES = {F32: 4, Q4_0: 18, Q4_1: 20, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q2_K: 84, Q3_K: 110, Q4_K: 144, Q5_K: 176,
                Q6_K: 210}
 
 

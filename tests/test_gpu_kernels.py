@@ -14,7 +14,7 @@ from tests.conftest import bits
 pytestmark = pytest.mark.gpu
 
 GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "known_answers.json")))
-QTYPES = [2, 3, 7, 8, 10, 11, 12, 13, 14]
+QTYPES = [2, 3, 6, 7, 8, 10, 11, 12, 13, 14]
 
 
 def _data(rng, t, rows, cols):
@@ -54,7 +54,7 @@ def test_dequant_row_bitexact(be, orc, t):
     (12, 257, 256), (12, 768, 2048), (12, 64, 7168), (14, 257, 256), (14, 2048, 768), (14, 33, 1536),
     (8, 257, 288), (8, 100, 1408), (8, 64, 2048), (2, 257, 288), (2, 96, 768), (2, 40, 2048),
     (0, 128, 2048), (0, 37, 300), (0, 5, 7), (0, 9, 40),
-    (3, 257, 288), (3, 100, 1408), (7, 257, 288), (7, 100, 1408),
+    (3, 257, 288), (3, 100, 1408), (7, 257, 288), (7, 100, 1408), (6, 257, 288), (6, 100, 1408),
     (10, 257, 256), (10, 96, 2048), (11, 257, 256), (11, 96, 2048), (13, 257, 256), (13, 768, 2048)])
 def test_matvec_bitexact(be, orc, t, rows, cols):
     rng = np.random.default_rng(rows * 31 + cols + t)
@@ -93,7 +93,11 @@ def test_matvec_nonfinite_activations(be, orc):
         x[256:288] = np.nan  # an all-non-finite 32 block
         got = np.empty(rows, np.float32)
         be.matvec(t, got, data, x, rows, cols)
-        assert np.array_equal(bits(got), bits(orc.matvec(t, data, x, rows, cols)))
+        want = orc.matvec(t, data, x, rows, cols)
+        if t == 6:  # q5_0 stays on f32 activations: non-finite values reach the sums (NaN payloads differ by host)
+            assert np.array_equal(np.isnan(got), np.isnan(want))
+            got, want = np.nan_to_num(got, nan=0.0), np.nan_to_num(want, nan=0.0)
+        assert np.array_equal(bits(got), bits(want))
 
 
 @pytest.mark.parametrize("case", GOLDEN["route"], ids=lambda c: c["name"])

@@ -285,7 +285,7 @@ def test_q5k_high_bit_adds_16(orc):
     assert abs(v[0] - 16.0) < 1e-4 and abs(v[1]) < 1e-4
 
 
-@pytest.mark.parametrize("t", [3, 7, 10, 11, 13])
+@pytest.mark.parametrize("t", [3, 6, 7, 10, 11, 13])
 def test_new_k_types_matvec_agrees_with_dequant(orc, t):
     """ggml.zig:2021-2087 for q4_1 / q5_1 / q2_k / q3_k / q5_k: random bytes (one f16 exponent
     bit cleared so no scale is NaN/Inf), int8-activation matvec within
@@ -362,3 +362,30 @@ def test_q51_matches_numpy_restatement(orc):
         want[j] = np.float32(np.float32(lo) * d) + m
         want[j + 16] = np.float32(np.float32(hi) * d) + m
     assert np.array_equal(want.view(np.uint32), orc.dequant_row(7, blk, 0, 32).view(np.uint32))
+
+
+def test_q50_f32_path_matches_numpy(orc):
+    """matvecQ50 (:1673): f32 activations, per block partial += w0*x[j] + w1*x[j+16]
+    in order, zero-scale blocks skipped (even with non-finite activations)."""
+    rng = np.random.default_rng(6)
+    cols = 96
+    data = rng.integers(0, 256, 3 * 22, dtype=np.uint8)
+    data[1::2] &= 0xFB
+    data[44:46] = 0  # block 2: scale 0
+    x = rng.standard_normal(cols).astype(np.float32)
+    x[70] = np.inf  # inside the zero-scale block: skipped, so no NaN
+    acc = np.float32(0)
+    for b in range(3):
+        blk = data[b * 22:(b + 1) * 22]
+        s = np.float32(np.frombuffer(blk[0:2].tobytes(), np.float16)[0])
+        if s == 0:
+            continue
+        qh = int(np.frombuffer(blk[2:6].tobytes(), np.uint32)[0])
+        part = np.float32(0)
+        for j in range(16):
+            w0 = np.float32(((int(blk[6 + j]) & 15) | (((qh >> j) << 4) & 0x10)) - 16)
+            w1 = np.float32(((int(blk[6 + j]) >> 4) | ((qh >> (j + 12)) & 0x10)) - 16)
+            part = np.float32(part + np.float32(np.float32(w0 * x[b * 32 + j]) + np.float32(w1 * x[b * 32 + j + 16])))
+        acc = np.float32(acc + np.float32(part * s))
+    got = orc.matvec(6, data, x, 1, cols)
+    assert got.view(np.uint32)[0] == np.float32(acc).view(np.uint32)
