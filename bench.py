@@ -529,18 +529,28 @@ def run_e2e(args, B):
         s = 1000 + l
         host.append((host_bytes(Q4K, NE * FFN * DIM // 256, s * 10 + 1), host_bytes(Q4K, NE * FFN * DIM // 256, s * 10 + 2),
                      host_bytes(Q6K, NE * DIM * FFN // 256, s * 10 + 3), host_bytes(F32, NE * DIM, s * 10 + 4, 0.02)))
-    cfg = B.RoutedCfg(NE, NK, False, True, 1.0)
+    import ctypes as C
+    from loom_b200 import _lib
+    # the C ABI called the way the reference's Zig arm would: argument structs built
+    # once, the host buffers reused, one matvec + one moe_ffn_routed per layer
+    lib = _lib.lib()
+    mv, fr = lib.loom_cuda_matvec, lib.loom_cuda_moe_ffn_routed
+    cfg = _lib.RoutedCfg(NE, NK, 0, 1, 1.0)
     x = np.random.default_rng(0).standard_normal(DIM).astype(np.float32)
     logits = np.empty(NE, np.float32)
     out = np.empty(DIM, np.float32)
+    xp, lp, op = (C.c_void_p(a.ctypes.data) for a in (x, logits, out))
+    args_l = [(C.c_void_p(r.ctypes.data), r.nbytes, _lib.Weight(Q4K, g.ctypes.data, g.nbytes),
+               _lib.Weight(Q4K, u.ctypes.data, u.nbytes), _lib.Weight(Q6K, d.ctypes.data, d.nbytes))
+              for (g, u, d, r) in host]
 
-    def token(x):
-        for (g, u, d, r) in host:
-            B.matvec(F32, logits, r, x, NE, DIM)
-            ok = B.moeFfnBlockRouted(x, logits, None, B.WeightRef(Q4K, g), B.WeightRef(Q4K, u), B.WeightRef(Q6K, d),
-                                     None, FFN, 0, cfg, out)
-            assert ok
-            x = x + out
+    def token(_x):
+        for (rp, rn, wg, wu, wd) in args_l:
+            if mv(F32, lp, rp, rn, xp, NE, DIM) != 0:
+                raise RuntimeError("matvec declined")
+            if fr(xp, DIM, lp, None, wg, wu, wd, None, FFN, 0, cfg, op) != 0:
+                raise RuntimeError("moe_ffn_routed declined")
+            np.add(x, out, out=x)  # the residual, on the host as the reference's engine does
         return x
 
     for _ in range(max(args.warmup, 1)):
@@ -548,7 +558,7 @@ def run_e2e(args, B):
     reps = max(args.steps, 3)
     t0 = time.perf_counter()
     for _ in range(reps):
-        x = token(x)
+        token(x)
     dt = (time.perf_counter() - t0) / reps / nl * LAYERS
     h2d = LAYERS * (DIM * 4 + DIM * 4 + NE * 4)
     d2h = LAYERS * (NE * 4 + DIM * 4)

@@ -11,6 +11,7 @@ namespace loom {
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launches() { return g_launches.load(); }
 void count_launch() { g_launches.fetch_add(1); }
+void count_launches(uint64_t n) { g_launches.fetch_add(n); }
 
 static inline unsigned cdiv(uint64_t a, uint64_t b) { return (unsigned)((a + b - 1) / b); }
 

@@ -69,5 +69,6 @@ void launch_argmax(const float *v, int n, unsigned long long *slot, unsigned *co
 // number of kernel launches issued by this library (host-side count)
 uint64_t launches();
 void count_launch();
+void count_launches(uint64_t n);
 
 }  // namespace loom

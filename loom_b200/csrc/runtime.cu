@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -74,6 +75,10 @@ struct Arena {
 };
 std::vector<Arena> g_arenas;
 
+// Bumped whenever a scratch or staging buffer moves or a cached weight is
+// freed: seam graphs captured before then point at stale memory.
+uint64_t g_buf_gen = 1;
+
 // growable device buffer
 struct DBuf {
     void *p = nullptr;
@@ -87,6 +92,7 @@ struct DBuf {
             cap = 0;
         }
         size_t want = std::max<size_t>(align256(n + n / 4), 256);
+        g_buf_gen++;
         cudaError_t e = cudaMalloc(&p, want);
         if (e != cudaSuccess) return fail("cudaMalloc(scratch)", e);
         if (zero) {
@@ -110,6 +116,7 @@ struct HBuf {  // pinned host staging
             cap = 0;
         }
         size_t want = std::max<size_t>(align256(n + n / 4), 4096);
+        g_buf_gen++;
         cudaError_t e = cudaHostAlloc(&p, want, cudaHostAllocDefault);
         if (e != cudaSuccess) return fail("cudaHostAlloc(staging)", e);
         cap = want;
@@ -225,6 +232,28 @@ Tensor *lookup(loom_tensor h) {
 }
 
 int need_init() { return g_inited ? 0 : decline("loom_cuda_init has not been called"); }
+
+// The seam calls return with their outputs on the host. Waiting on the stream
+// with cudaStreamSynchronize wakes the host tens of microseconds after the
+// copy lands under the default (yielding) scheduling; a seam call is a few
+// kernels of ~10 us, so the wake-up dominated. Instead the host polls an event
+// it recorded after the last copy (bounded to ~2 s of polling, then a blocking
+// wait), which returns within a microsecond or two of completion.
+cudaEvent_t g_seam_ev = nullptr;
+
+cudaError_t seam_wait() {
+    if (!g_seam_ev) {
+        cudaError_t e = cudaEventCreateWithFlags(&g_seam_ev, cudaEventDisableTiming);
+        if (e != cudaSuccess) return e;
+    }
+    cudaError_t e = cudaEventRecord(g_seam_ev, g_stream);
+    if (e != cudaSuccess) return e;
+    const auto t0 = std::chrono::steady_clock::now();
+    while ((e = cudaEventQuery(g_seam_ev)) == cudaErrorNotReady) {
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(2)) return cudaEventSynchronize(g_seam_ev);
+    }
+    return e;
+}
 
 // Scratch for quantizing T activation vectors of width `cols`.
 int ensure_xq(size_t T, size_t cols) {
@@ -427,6 +456,88 @@ DecodeArgs decode_args(const RoutedLayerDev &L, size_t T, const float *router, c
 
 // Device-side forward of a routed MoE layer (routing on the device). `router`
 // (f32 [n_expert][dim]) computes the logits; otherwise d_logits holds them.
+// Seam calls repeat the same few shapes on the same weights every token, so
+// each (operation, weights, shape, configuration) gets a CUDA graph of its
+// copies and kernels: the first call runs eagerly (sizing every buffer), the
+// second captures and instantiates, later calls are one graph launch. A graph
+// is dropped when a buffer it points at moves or a weight is freed
+// (g_buf_gen). The host side of a call (staging the inputs in pinned memory,
+// reading the result back after seam_wait) stays outside the graph.
+struct SeamGraph {
+    uint64_t gen = 0;
+    cudaGraphExec_t exec = nullptr;
+    bool seen = false, bad = false;  // bad: capture failed once, always run eagerly
+    uint64_t launches = 0;
+    int last_path = 0;
+};
+std::map<std::vector<uint64_t>, SeamGraph> g_seam_graphs;
+
+template <class F>
+int seam_run(const std::vector<uint64_t> &key, F &&body) {
+    if (g_trace) return body();  // traced kernels record into a buffer that is re-armed per call
+    SeamGraph &G = g_seam_graphs[key];
+    if (G.exec && G.gen == g_buf_gen) {
+        cudaError_t e = cudaGraphLaunch(G.exec, g_stream);
+        if (e != cudaSuccess) return fail("cudaGraphLaunch(seam)", e);
+        count_launches(G.launches);
+        g_last_path = G.last_path;
+        return 0;
+    }
+    if (G.exec) {
+        cudaGraphExecDestroy(G.exec);
+        G.exec = nullptr;
+    }
+    if (G.bad) return body();
+    if (!G.seen || G.gen != g_buf_gen) {  // first sighting at this buffer generation: eager
+        const int rc = body();
+        G.seen = rc == 0;
+        G.gen = g_buf_gen;  // after the eager run's allocations
+        return rc;
+    }
+    cudaError_t e = cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeRelaxed);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        G.bad = true;
+        return body();
+    }
+    const uint64_t l0 = launches();
+    const int rc = body();
+    cudaGraph_t graph = nullptr;
+    e = cudaStreamEndCapture(g_stream, &graph);
+    G.launches = launches() - l0;
+    G.last_path = g_last_path;
+    if (rc || e != cudaSuccess || !graph || G.gen != g_buf_gen) {  // nothing ran: run eagerly
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        G.bad = G.gen == g_buf_gen;  // a buffer move is retried, anything else is not
+        G.seen = false;
+        return body();
+    }
+    e = cudaGraphInstantiate(&G.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+        G.exec = nullptr;
+        G.bad = true;
+        cudaGetLastError();
+        return body();
+    }
+    e = cudaGraphLaunch(G.exec, g_stream);
+    if (e != cudaSuccess) return fail("cudaGraphLaunch(seam)", e);
+    return 0;
+}
+
+void seam_graphs_clear() {
+    for (auto &kv : g_seam_graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    g_seam_graphs.clear();
+}
+
+inline uint64_t fbits(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+
 int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const float *d_x, const float *d_logits,
                    const float *d_bias, float *d_out, const float *d_residual, uint32_t *d_ids_out, cudaStream_t st) {
     const size_t max_ffn = std::max<size_t>(L.ffn, L.has_shared ? L.shexp_ffn : 0);
@@ -494,6 +605,7 @@ int loom_cuda_init(int device) {
 void loom_cuda_clear_weight_cache(void) {
     if (!g_inited) return;
     cudaStreamSynchronize(g_stream);
+    g_buf_gen++;
     for (auto &kv : g_cache) {
         auto it = g_tensors.find(kv.second);
         if (it != g_tensors.end()) {
@@ -507,6 +619,7 @@ void loom_cuda_clear_weight_cache(void) {
 void loom_cuda_shutdown(void) {
     if (!g_inited) return;
     cudaStreamSynchronize(g_stream);
+    seam_graphs_clear();
     for (auto &kv : g_tensors) cudaFree(kv.second.base);
     g_tensors.clear();
     g_cache.clear();
@@ -525,6 +638,8 @@ void loom_cuda_shutdown(void) {
         b->p = nullptr;
         b->cap = 0;
     }
+    if (g_seam_ev) cudaEventDestroy(g_seam_ev);
+    g_seam_ev = nullptr;
     cudaStreamDestroy(g_stream);
     g_stream = nullptr;
     g_inited = false;
@@ -674,20 +789,27 @@ int loom_cuda_matmul(int type, float *out, const void *w, size_t w_bytes, const 
     if (int rc = S.io_in.ensure(in_b)) return rc;
     if (int rc = S.io_out.ensure(out_b)) return rc;
     memcpy(S.h_in.p, xs, in_b);
-    CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
-    if (type == T_F32) {
-        launch_mm_f32(reinterpret_cast<const float *>(t->base), (int)rows, (int)cols, S.io_in.as<float>(), (int)n,
-                      S.io_out.as<float>(), g_stream);
-    } else if (type == T_Q5_0) {
-        launch_mm_q50(t->w, 0, (int)rows, (int)cols, S.io_in.as<float>(), (int)n, S.io_out.as<float>(), g_stream);
-    } else {
-        if (int rc = ensure_xq(n, cols)) return rc;
-        quantize_into(S.io_in.as<float>(), n, cols, act256(type), g_stream);
-        launch_mm(t->w, 0, (int)rows, (int)cols, make_xq(act256(type), cols), (int)n, S.io_out.as<float>(), g_stream);
-    }
-    CK(cudaGetLastError());
-    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, out_b, cudaMemcpyDeviceToHost, g_stream));
-    CK(cudaStreamSynchronize(g_stream));
+    const std::vector<uint64_t> key = {1, (uint64_t)type, (uint64_t)(uintptr_t)t->base, n, rows, cols};
+    if (int rc = seam_run(key, [&]() -> int {
+            CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
+            if (type == T_F32) {
+                launch_mm_f32(reinterpret_cast<const float *>(t->base), (int)rows, (int)cols, S.io_in.as<float>(),
+                              (int)n, S.io_out.as<float>(), g_stream);
+            } else if (type == T_Q5_0) {
+                launch_mm_q50(t->w, 0, (int)rows, (int)cols, S.io_in.as<float>(), (int)n, S.io_out.as<float>(),
+                              g_stream);
+            } else {
+                if (int rc = ensure_xq(n, cols)) return rc;
+                quantize_into(S.io_in.as<float>(), n, cols, act256(type), g_stream);
+                launch_mm(t->w, 0, (int)rows, (int)cols, make_xq(act256(type), cols), (int)n, S.io_out.as<float>(),
+                          g_stream);
+            }
+            CK(cudaGetLastError());
+            CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, out_b, cudaMemcpyDeviceToHost, g_stream));
+            return 0;
+        }))
+        return rc;
+    CK(seam_wait());  // the seam returns with `out` written
     memcpy(out, S.h_out.p, out_b);
     g_cmdbufs++;
     return LOOM_CUDA_OK;
@@ -707,7 +829,7 @@ int loom_cuda_dequant_row(int type, float *out, const void *w, size_t w_bytes, s
     launch_dequant(t->w, (uint64_t)r * (cols / be), cols / be, S.io_out.as<float>(), g_stream);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, cols * 4, cudaMemcpyDeviceToHost, g_stream));
-    CK(cudaStreamSynchronize(g_stream));
+    CK(seam_wait());  // the seam returns with `out` written
     memcpy(out, S.h_out.p, cols * 4);
     g_cmdbufs++;
     return LOOM_CUDA_OK;
@@ -732,7 +854,7 @@ int loom_cuda_moe_route(const float *logits, const float *bias, size_t n_expert,
                  gating_sigmoid ? 2 : 1, weights_norm, weights_scale, d_ids, d_g, g_stream);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, out_b, cudaMemcpyDeviceToHost, g_stream));
-    CK(cudaStreamSynchronize(g_stream));
+    CK(seam_wait());  // the seam returns with `out` written
     memcpy(ids_out, S.h_out.p, n_used * 4);
     memcpy(gates_out, S.h_out.as<float>() + n_used, n_used * 4);
     g_cmdbufs++;
@@ -789,7 +911,7 @@ int loom_cuda_moe_ffn_block(const float *normed, size_t dim, const loom_expert *
                         g_stream);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
-    CK(cudaStreamSynchronize(g_stream));
+    CK(seam_wait());  // the seam returns with `out` written
     memcpy(out, S.h_out.p, dim * 4);
     g_cmdbufs++;
     return LOOM_CUDA_OK;
@@ -833,13 +955,23 @@ int loom_cuda_moe_ffn_routed(const float *normed, size_t dim, const float *logit
     memcpy(hin, normed, dim * 4);
     memcpy(hin + dim, logits, cfg.n_expert * 4);
     if (bias) memcpy(hin + dim + cfg.n_expert, bias, cfg.n_expert * 4);
-    CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
-    const float *dx = S.io_in.as<float>();
-    if (int rc = moe_routed_dev(L, 1, nullptr, dx, dx + dim, bias ? dx + dim + cfg.n_expert : nullptr,
-                                S.io_out.as<float>(), nullptr, nullptr, g_stream))
+    auto base = [](const Tensor *t) -> uint64_t { return t ? (uint64_t)(uintptr_t)t->base : 0; };
+    const std::vector<uint64_t> key = {2, (uint64_t)g->type, base(g), (uint64_t)u->type, base(u), (uint64_t)d->type,
+                                       base(d), base(sh[0]), base(sh[1]), base(sh[2]), dim, ffn, shexp_ffn,
+                                       cfg.n_expert, cfg.n_used, (uint64_t)cfg.gating_sigmoid,
+                                       (uint64_t)cfg.weights_norm, fbits(cfg.weights_scale), bias ? 1u : 0u,
+                                       (uint64_t)g_force_generic};
+    if (int rc = seam_run(key, [&]() -> int {
+            CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
+            const float *dx = S.io_in.as<float>();
+            if (int rc = moe_routed_dev(L, 1, nullptr, dx, dx + dim, bias ? dx + dim + cfg.n_expert : nullptr,
+                                        S.io_out.as<float>(), nullptr, nullptr, g_stream))
+                return rc;
+            CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
+            return 0;
+        }))
         return rc;
-    CK(cudaMemcpyAsync(S.h_out.p, S.io_out.p, dim * 4, cudaMemcpyDeviceToHost, g_stream));
-    CK(cudaStreamSynchronize(g_stream));
+    CK(seam_wait());  // the seam returns with `out` written
     memcpy(out, S.h_out.p, dim * 4);
     g_cmdbufs++;
     return LOOM_CUDA_OK;
@@ -923,6 +1055,7 @@ int loom_cuda_tensor_free(loom_tensor h) {
     if (!t) return decline("unknown tensor");
     CK(cudaStreamSynchronize(g_stream));
     cudaFree(t->base);
+    g_buf_gen++;
     for (auto it = g_cache.begin(); it != g_cache.end();)
         it = it->second == h ? g_cache.erase(it) : std::next(it);
     g_tensors.erase(h);

@@ -218,3 +218,20 @@ def test_lm_head_argmax_q6k(be, orc):
         assert int(tok.item()) == orc.argmax(want)
     finally:
         W.free()
+
+
+@pytest.mark.parametrize("t", [12, 14, 6, 0])
+def test_repeated_seam_calls_replay_exactly(be, orc, t):
+    """Repeated calls on the same weights and shape (eager, captured, then
+    replayed as one graph) stay bit-exact with fresh inputs every call and
+    still count their kernel launches."""
+    rng = np.random.default_rng(70 + t)
+    rows, cols = 96, 512
+    data = _data(rng, t, rows, cols)
+    for _ in range(5):
+        x = rng.standard_normal(cols).astype(np.float32)
+        got = np.full(rows, np.nan, np.float32)
+        k0 = be.kernelLaunches()
+        be.matvec(t, got, data, x, rows, cols)
+        assert be.kernelLaunches() > k0
+        assert np.array_equal(bits(got), bits(orc.matvec(t, data, x, rows, cols)))
