@@ -209,6 +209,7 @@ __device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int ga
         for (int k = 0; k < nk; k++) sum = fadd(sum, gates[k]);
         denom = fmaxf(sum, 6.103515625e-5f);
     }
+    __syncwarp();  // every lane has read the gates before they are rewritten
     for (int k = lane; k < nk; k += 32) {
         float g = gates[k];
         if (weights_norm) g = fdiv(g, denom);
@@ -238,13 +239,12 @@ __device__ __forceinline__ uint32_t f32_order_key(float x) {
 // grid (read with ld.global.cg) or shared memory.
 constexpr int RW_MAX = 8;
 
-// The route on logits already in registers: v[t] = logit of expert lane + 32t
-// (-inf past ne).
+// Scores of the route on logits in registers (v[t] = logit of expert
+// lane + 32t, -inf past ne): sigmoid, softmax (its sum in route_block's order:
+// per 128-thread stride, then per warp, then the four warp partials in order)
+// or the raw logits.
 template <int RW>
-__device__ __forceinline__ void route_warp_vals(float (&v)[RW], const float *bias, int ne, int nk, int gating,
-                                                int weights_norm, float weights_scale, float *scores, float *choice,
-                                                int *ids, float *gates, int *ids_out, float *gates_out, int lane) {
-    float sc[RW];
+__device__ __forceinline__ void route_warp_sc(const float (&v)[RW], int ne, int gating, float (&sc)[RW], int lane) {
     if (gating == 2) {
 #pragma unroll
         for (int t = 0; t < RW; t++) sc[t] = fdiv(1.0f, fadd(1.0f, expf(-v[t])));
@@ -275,6 +275,16 @@ __device__ __forceinline__ void route_warp_vals(float (&v)[RW], const float *bia
 #pragma unroll
         for (int t = 0; t < RW; t++) sc[t] = v[t];
     }
+}
+
+// The route on logits already in registers: v[t] = logit of expert lane + 32t
+// (-inf past ne).
+template <int RW>
+__device__ __forceinline__ void route_warp_vals(float (&v)[RW], const float *bias, int ne, int nk, int gating,
+                                                int weights_norm, float weights_scale, float *scores, float *choice,
+                                                int *ids, float *gates, int *ids_out, float *gates_out, int lane) {
+    float sc[RW];
+    route_warp_sc<RW>(v, ne, gating, sc, lane);
     bool fin = true;
     uint32_t key[RW];
     int ei[RW];
