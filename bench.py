@@ -206,7 +206,8 @@ def run_gpu(args):
     B.init(local)
     T = args.tokens
     ep = args.ep and world > 1
-    a2a = ep and args.ep_mode == "a2a"
+    a2a = ep and args.ep_mode in ("a2a", "a2a-counted")
+    a2a_cap = T if args.ep_mode == "a2a" else 0  # fixed-capacity runs: every rank decodes T tokens
     ex0, nloc = D.expert_range(NE, rank, world) if ep else (0, NE)
     if ep:
         D.ep_init(rank, world, dist)
@@ -241,7 +242,7 @@ def run_gpu(args):
         for l, L in enumerate(layers):
             nxt = bufs[l % 2]
             if a2a:
-                L.forward_a2a(cur, nxt, residual=cur, ids=ids[l], stream=sh)
+                L.forward_a2a(cur, nxt, residual=cur, ids=ids[l], stream=sh, t_cap=a2a_cap, desc=descs[l])
             else:
                 L.forward(cur, nxt, residual=cur, ids=ids[l], stream=sh, desc=descs[l])
             cur = nxt
@@ -250,7 +251,7 @@ def run_gpu(args):
         step(stream.cuda_stream)  # sizes all scratch before capture
     torch.cuda.synchronize()
     k0 = B.kernelLaunches()
-    if a2a:  # the receive counts go to the host every layer: no graph, eager launches
+    if a2a and not a2a_cap:  # the receive counts go to the host every layer: no graph, eager launches
         class _Eager:
             def replay(self):
                 step(stream.cuda_stream)
@@ -338,6 +339,8 @@ def run_gpu(args):
                                    f"ep{world} (experts sharded, NCCL all-reduce combine)" if ep else
                                    f"replicas x{world}" if world > 1 else "1 gpu"),
                    "engine": engine,
+                   **({"a2a_exchange": "fixed capacity (T*n_used rows per rank), graph-captured" if a2a_cap else
+                       "counted (host sync per layer)"} if a2a else {}),
                    "l2": "inputs > L2 (48 distinct layers, ~1.2 GB touched per token)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -586,9 +589,11 @@ def main():
     ap.add_argument("--ep", action="store_true",
                     help="with torchrun: shard each layer's experts over the ranks (expert parallel) instead of "
                          "running independent replicas")
-    ap.add_argument("--ep-mode", default="allreduce", choices=["allreduce", "a2a"],
+    ap.add_argument("--ep-mode", default="allreduce", choices=["allreduce", "a2a", "a2a-counted"],
                     help="allreduce: every rank runs the same tokens, partial outputs summed; a2a: every rank owns "
-                         "its own T tokens, routed rows travel to the experts' ranks and back (NCCL send/recv)")
+                         "its own T tokens, routed rows travel to the experts' ranks and back (NCCL send/recv) in fixed "
+                         "runs of T*n_used rows per rank, captured in a CUDA graph; a2a-counted: the same with "
+                         "exactly the routed rows (their counts go to the host each layer, eager launches)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers in the stack (default 48; smaller only for profiling captures)")
     args = ap.parse_args()

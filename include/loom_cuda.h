@@ -262,6 +262,17 @@ int loom_cuda_ep_size(void);
  * counts go to the host). Without loom_cuda_ep_init it runs as one rank. */
 int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
                              const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream);
+/* The same layer with fixed-capacity exchanges: every rank passes the same
+ * t_cap >= its T, and every rank sends every other rank a run of exactly
+ * t_cap * n_used rows (the unused entries carry no expert and are skipped).
+ * No size depends on the routing, so nothing goes to the host and the call
+ * can be captured in a CUDA graph with the NCCL exchanges (after one eager
+ * call has sized the buffers). Output bit-identical to
+ * loom_cuda_ep_a2a_forward. The exchange carries world * t_cap * n_used rows
+ * each way, so size t_cap to the decode batch, not to a prefill. Engine-level
+ * API: no counterpart in the reference's seam. */
+int loom_cuda_ep_a2a_forward_cap(const loom_moe_desc *desc, const float *d_x, size_t T, size_t t_cap, float *d_out,
+                                 const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream);
 /* Greedy sampling (sampler.zig:7-15 argmax) of device logits into *d_index
  * (device u32): the first maximum; NaN never taken; 0 when nothing is above
  * -inf. Asynchronous on `stream`; calls on one device share a 16-byte scratch,

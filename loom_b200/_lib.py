@@ -107,6 +107,7 @@ def lib() -> C.CDLL:
         "loom_cuda_ep_rank": (i, []),
         "loom_cuda_ep_size": (i, []),
         "loom_cuda_ep_a2a_forward": (i, [C.POINTER(MoeDesc), vp, sz, vp, vp, vp, vp, vp]),
+        "loom_cuda_ep_a2a_forward_cap": (i, [C.POINTER(MoeDesc), vp, sz, sz, vp, vp, vp, vp, vp]),
         "loom_cuda_argmax": (i, [vp, sz, vp, vp]),
         "loom_cuda_lm_head_argmax": (i, [C.c_uint64, sz, sz, vp, vp, vp, vp]),
         "loom_cuda_trace_enable": (i, [sz]),

@@ -33,10 +33,13 @@ __device__ __forceinline__ int a2a_owner(int e, int ne, int world) {
 constexpr int PACK_THREADS = 1024;
 
 // One CTA. cnt[world]: slots per destination; send_eid/send_tok/slot_pos as
-// described above.
+// described above. cap > 0 (fixed-capacity form): destination r's run starts
+// at r*cap instead of after the runs before it, and its cap - cnt[r] unused
+// entries get expert -1 and token -1 (no row: the receiver's grouping skips
+// ids outside its shard, and nothing is gathered for them).
 __global__ void __launch_bounds__(PACK_THREADS) k_a2a_pack(const int *ids, int n_slots, int n_used, int n_expert,
-                                                           int world, int *send_eid, int *send_tok, int *slot_pos,
-                                                           int *cnt) {
+                                                           int world, int cap, int *send_eid, int *send_tok,
+                                                           int *slot_pos, int *cnt) {
     __shared__ int s_cnt[A2A_MAX_RANKS], s_base[A2A_MAX_RANKS], s_wsum[PACK_THREADS / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid < world) s_cnt[tid] = 0;
@@ -46,12 +49,18 @@ __global__ void __launch_bounds__(PACK_THREADS) k_a2a_pack(const int *ids, int n
     if (tid == 0) {
         int b = 0;
         for (int r = 0; r < world; r++) {
-            s_base[r] = b;
+            s_base[r] = cap > 0 ? r * cap : b;
             b += s_cnt[r];
             cnt[r] = s_cnt[r];
         }
     }
     __syncthreads();
+    if (cap > 0)
+        for (int i = tid; i < world * cap; i += PACK_THREADS)
+            if (i % cap >= s_cnt[i / cap]) {
+                send_eid[i] = -1;
+                send_tok[i] = -1;
+            }
     for (int c = 0; c < n_slots; c += PACK_THREADS) {
         const int i = c + tid;
         const int e = i < n_slots ? ids[i] : 0;
@@ -81,6 +90,7 @@ __global__ void __launch_bounds__(PACK_THREADS) k_a2a_pack(const int *ids, int n
 
 __global__ void k_a2a_gather(const float *x, const int *send_tok, int dim, float *send_x) {
     const int p = blockIdx.x;
+    if (send_tok[p] < 0) return;  // an unused entry of a fixed-capacity run
     const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)send_tok[p] * dim);
     float4 *dst = reinterpret_cast<float4 *>(send_x + (size_t)p * dim);
     for (int c = threadIdx.x; c < dim / 4; c += blockDim.x) dst[c] = src[c];
@@ -107,13 +117,14 @@ __global__ void k_a2a_combine(const float *y_back, const int *slot_pos, const fl
 
 static inline unsigned cdiv_u(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 
-void launch_a2a_pack(const int *ids, int T, int n_used, int n_expert, int world, const float *x, int dim,
+void launch_a2a_pack(const int *ids, int T, int n_used, int n_expert, int world, int cap, const float *x, int dim,
                      int *send_eid, int *send_tok, int *slot_pos, int *cnt, float *send_x, cudaStream_t st) {
     const int n = T * n_used;
-    k_a2a_pack<<<1, PACK_THREADS, 0, st>>>(ids, n, n_used, n_expert, world, send_eid, send_tok, slot_pos, cnt);
+    k_a2a_pack<<<1, PACK_THREADS, 0, st>>>(ids, n, n_used, n_expert, world, cap, send_eid, send_tok, slot_pos, cnt);
     count_launch();
+    const int np = cap > 0 ? world * cap : n;
     if (n == 0) return;
-    k_a2a_gather<<<n, 128, 0, st>>>(x, send_tok, dim, send_x);
+    k_a2a_gather<<<np, 128, 0, st>>>(x, send_tok, dim, send_x);
     count_launch();
 }
 

@@ -27,7 +27,9 @@ constexpr int A2A_MAX_RANKS = 64;
 // Route-ordered slots [T][n_used] -> destination-ordered send lists:
 // send_eid/send_tok [T*n_used], slot_pos [T*n_used] (position of each slot in
 // the send order), cnt [world] (slots per destination), send_x [T*n_used][dim].
-void launch_a2a_pack(const int *ids, int T, int n_used, int n_expert, int world, const float *x, int dim,
+// cap > 0: fixed-capacity runs of cap entries per destination (send lists of
+// world*cap entries, unused ones with expert and token -1).
+void launch_a2a_pack(const int *ids, int T, int n_used, int n_expert, int world, int cap, const float *x, int dim,
                      int *send_eid, int *send_tok, int *slot_pos, int *cnt, float *send_x, cudaStream_t st);
 void launch_a2a_fill(float *v, int n, float val, cudaStream_t st);
 // out[t] = residual[t] + (sum_k gates[t,k] * y_back[slot_pos[t,k]] + y_sh[t])

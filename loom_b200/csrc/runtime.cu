@@ -1145,8 +1145,15 @@ int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T,
 // All-to-all expert parallelism (a2a.cu): route this rank's own tokens, send
 // each routed row to the expert's owner, run the rows that arrive through
 // this rank's experts, send the outputs back, combine in selection order.
-int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
-                             const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream) {
+}  // extern "C"
+
+namespace {
+
+// Both all-to-all forms: t_cap == 0 sends exactly the routed rows (their
+// counts go to the host once per layer); t_cap > 0 sends fixed runs of
+// t_cap * n_used rows to every rank (no host synchronisation).
+int ep_a2a(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, const float *d_residual,
+           const float *d_logits, uint32_t *d_ids, void *stream, size_t t_cap) {
     if (int rc = need_init()) return rc;
     if (!desc) return decline("no layer description");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
@@ -1191,14 +1198,17 @@ int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t
         router = reinterpret_cast<const float *>(r->base);
     }
     const size_t dim = D.dim, k = D.n_used, ns = T * k;
+    if (t_cap && T > t_cap) return decline("more tokens than the all-to-all capacity");
+    if (t_cap && (size_t)world * t_cap * k > (1u << 24)) return decline("all-to-all capacity out of range");
+    const size_t cap = t_cap * k, nsend = std::max(ns, (size_t)world * cap);  // send-list entries
     const size_t max_ffn = std::max<size_t>(D.ffn, sh[0] ? D.shexp_ffn : 0), act_stride = align256(max_ffn);
     // home side: route, then the destination-ordered send lists
     if (int rc = ensure_moe_scratch(std::max<size_t>(T, 1), dim, max_ffn, D.n_expert, std::max<size_t>(T, 1) * (k + 1)))
         return rc;
-    const size_t ni = align256(ns + 1);
+    const size_t ni = align256(nsend + 1);
     if (int rc = S.a2a_i.ensure((4 * ni + 2 * A2A_MAX_RANKS) * 4)) return rc;
-    if (int rc = S.a2a_sx.ensure(std::max<size_t>(ns, 1) * dim * 4)) return rc;
-    if (int rc = S.a2a_yb.ensure(std::max<size_t>(ns, 1) * dim * 4)) return rc;
+    if (int rc = S.a2a_sx.ensure(std::max<size_t>(nsend, 1) * dim * 4)) return rc;
+    if (int rc = S.a2a_yb.ensure(std::max<size_t>(nsend, 1) * dim * 4)) return rc;
     if (int rc = S.a2a_ysh.ensure(std::max<size_t>(T, 1) * dim * 4)) return rc;
     if (int rc = S.h_cnt.ensure(2 * A2A_MAX_RANKS * 4)) return rc;
     int *send_eid = S.a2a_i.as<int>(), *send_tok = send_eid + ni, *slot_pos = send_tok + ni;
@@ -1214,27 +1224,36 @@ int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t
         CK(cudaMemcpyAsync(home_gates, S.gates.p, ns * 4, cudaMemcpyDeviceToDevice, st));
         if (d_ids) CK(cudaMemcpyAsync(d_ids, S.ids.p, ns * 4, cudaMemcpyDeviceToDevice, st));
     }
-    launch_a2a_pack(S.ids.as<int>(), (int)T, (int)k, (int)D.n_expert, world, d_x, (int)dim, send_eid, send_tok,
-                    slot_pos, cnt, S.a2a_sx.as<float>(), st);
-    // counts: one int to and from every rank, then to the host
-    std::vector<size_t> one(world, 1), idx(world), scnt(world), soff(world), rcnt(world), roff(world);
-    for (int r = 0; r < world; r++) idx[r] = r;
-    if (int e = ep_alltoallv(cnt, idx.data(), one.data(), cnt + A2A_MAX_RANKS, idx.data(), one.data(), 4, st, g_err))
-        return e;
-    CK(cudaMemcpyAsync(S.h_cnt.p, cnt, 2 * A2A_MAX_RANKS * 4, cudaMemcpyDeviceToHost, st));
-    CK(cudaStreamSynchronize(st));
-    const int *hc = S.h_cnt.as<int>();
-    size_t so = 0, ro = 0;
-    for (int r = 0; r < world; r++) {
-        scnt[r] = (size_t)hc[r];
-        rcnt[r] = (size_t)hc[A2A_MAX_RANKS + r];
-        soff[r] = so;
-        roff[r] = ro;
-        so += scnt[r];
-        ro += rcnt[r];
+    launch_a2a_pack(S.ids.as<int>(), (int)T, (int)k, (int)D.n_expert, world, (int)cap, d_x, (int)dim, send_eid,
+                    send_tok, slot_pos, cnt, S.a2a_sx.as<float>(), st);
+    std::vector<size_t> scnt(world), soff(world), rcnt(world), roff(world);
+    size_t nr = 0;
+    if (cap) {  // fixed runs: every size is known without looking at the routing
+        for (int r = 0; r < world; r++) {
+            scnt[r] = rcnt[r] = cap;
+            soff[r] = roff[r] = (size_t)r * cap;
+        }
+        nr = (size_t)world * cap;
+    } else {  // counts: one int to and from every rank, then to the host
+        std::vector<size_t> one(world, 1), idx(world);
+        for (int r = 0; r < world; r++) idx[r] = r;
+        if (int e = ep_alltoallv(cnt, idx.data(), one.data(), cnt + A2A_MAX_RANKS, idx.data(), one.data(), 4, st,
+                                 g_err))
+            return e;
+        CK(cudaMemcpyAsync(S.h_cnt.p, cnt, 2 * A2A_MAX_RANKS * 4, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        const int *hc = S.h_cnt.as<int>();
+        size_t so = 0;
+        for (int r = 0; r < world; r++) {
+            scnt[r] = (size_t)hc[r];
+            rcnt[r] = (size_t)hc[A2A_MAX_RANKS + r];
+            soff[r] = so;
+            roff[r] = nr;
+            so += scnt[r];
+            nr += rcnt[r];
+        }
+        if (so != ns) return fail("all-to-all pack", cudaErrorUnknown);
     }
-    if (so != ns) return fail("all-to-all pack", cudaErrorUnknown);
-    const size_t nr = ro;
     // receive side buffers (sized now that the counts are known)
     if (int rc = S.a2a_rx.ensure(std::max<size_t>(nr, 1) * dim * 4)) return rc;
     if (int rc = S.a2a_re.ensure(std::max<size_t>(nr, 1) * 4)) return rc;
@@ -1295,6 +1314,21 @@ int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t
                        st);
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int loom_cuda_ep_a2a_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
+                             const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream) {
+    return ep_a2a(desc, d_x, T, d_out, d_residual, d_logits, d_ids, stream, 0);
+}
+
+int loom_cuda_ep_a2a_forward_cap(const loom_moe_desc *desc, const float *d_x, size_t T, size_t t_cap, float *d_out,
+                                 const float *d_residual, const float *d_logits, uint32_t *d_ids, void *stream) {
+    if (t_cap == 0) return decline("the fixed-capacity all-to-all needs t_cap >= 1");
+    return ep_a2a(desc, d_x, T, d_out, d_residual, d_logits, d_ids, stream, t_cap);
 }
 
 int loom_cuda_tensor_matmul(loom_tensor h, size_t rows, size_t cols, const float *d_xs, size_t n, float *d_out,

@@ -91,11 +91,17 @@ class MoeLayer:
                             h(self.down), h(sh[0]), h(sh[1]), h(sh[2]), self.shexp_ffn, self.expert0,
                             self.n_local or self.n_expert, h(self.next_router), self.n_group, self.topk_group)
 
-    def forward_a2a(self, x, out, residual=None, logits=None, ids=None, stream=None) -> None:
+    def forward_a2a(self, x, out, residual=None, logits=None, ids=None, stream=None, t_cap=0, desc=None) -> None:
         """All-to-all expert parallelism: x/out are THIS rank's tokens [T, dim]
-        (T may be 0); collective over the ranks of ep_init."""
-        d = self.desc()
+        (T may be 0); collective over the ranks of ep_init. t_cap > 0 (the same
+        on every rank, >= T): fixed-capacity exchanges, no host synchronisation."""
+        d = desc if desc is not None else self.desc()
         T = x.shape[0]
+        if t_cap:
+            rc = _lib.lib().loom_cuda_ep_a2a_forward_cap(C.byref(d), _ptr(x), T, t_cap, _ptr(out), _ptr(residual),
+                                                         _ptr(logits), _ptr(ids), stream)
+            _lib.must(rc, "ep_a2a_forward_cap")
+            return
         rc = _lib.lib().loom_cuda_ep_a2a_forward(C.byref(d), _ptr(x), T, _ptr(out), _ptr(residual), _ptr(logits),
                                                  _ptr(ids), stream)
         _lib.must(rc, "ep_a2a_forward")

@@ -1,8 +1,9 @@
 """Worker for the 2-GPU all-to-all expert-parallel test (launched by torchrun
 from tests/test_gpu_ep.py): each rank holds its contiguous half of the
 experts and its own tokens (different counts per rank, one round with no
-tokens on one rank); the all-to-all layer must equal, bit for bit, the
-unsharded layer each rank also runs on its own tokens."""
+tokens on one rank), in both exchange forms (counted, and fixed capacity with
+and without unused entries); the all-to-all layer must equal, bit for bit,
+the unsharded layer each rank also runs on its own tokens."""
 import os
 import sys
 
@@ -35,14 +36,15 @@ def main():
     full = MoeLayer(dim, ffn, ne, k, DeviceTensor.synth(12, ne * pg, 51), DeviceTensor.synth(12, ne * pg, 52),
                     DeviceTensor.synth(8, ne * pd, 53), router=router, shexp=shexp, shexp_ffn=sffn)
     ok = 1
-    for rnd, counts in enumerate([(5, 3), (1, 1), (40, 0), (0, 17)]):
+    for rnd, (counts, t_cap) in enumerate([((5, 3), 0), ((1, 1), 0), ((40, 0), 0), ((0, 17), 0),
+                                            ((5, 3), 5), ((1, 1), 1), ((2, 0), 4), ((0, 3), 3)]):
         T = counts[rank % 2]
         g = torch.Generator("cuda").manual_seed(1000 * rnd + rank)
         x = torch.randn((T, dim), device="cuda", generator=g)
         res = torch.randn((T, dim), device="cuda", generator=g)
         out = torch.full((T, dim), float("nan"), device="cuda")
         ids = torch.zeros((T, k), dtype=torch.int32, device="cuda")
-        shard.forward_a2a(x, out, residual=res, ids=ids)
+        shard.forward_a2a(x, out, residual=res, ids=ids, t_cap=t_cap)
         if T:
             want = torch.empty((T, dim), device="cuda")
             wids = torch.zeros((T, k), dtype=torch.int32, device="cuda")

@@ -31,10 +31,13 @@ def test_two_rank_expert_parallel_layer():
 ], ids=["qwen3", "v2lite", "v3grouped"])
 @pytest.mark.parametrize("T", [0, 1, 7, 64])
 @pytest.mark.parametrize("mode", [0, 1, 3], ids=["auto", "slot", "mma"])
-def test_a2a_single_rank_bitexact(be, orc, cfg, T, mode):
+@pytest.mark.parametrize("cap", [0, 1, 5], ids=["counted", "cap_exact", "cap_padded"])
+def test_a2a_single_rank_bitexact(be, orc, cfg, T, mode, cap):
     """The all-to-all layer as one rank (every row goes to itself through the
     pack, the self copy, the per-row expert run and the ordered combine) is
-    bit-identical to the ordinary layer, shared expert and groups included."""
+    bit-identical to the ordinary layer, shared expert and groups included;
+    so is the fixed-capacity form, with a run exactly T*n_used long and one
+    padded with unused entries."""
     from tests.test_gpu_moe import _layer_case
     from tests.conftest import bits
     import numpy as np
@@ -51,7 +54,7 @@ def test_a2a_single_rank_bitexact(be, orc, cfg, T, mode):
     from loom_b200 import device as D
     prev = D.force_generic(mode)  # how the arriving rows run: batch / slot kernels / tensor cores
     try:
-        L.forward_a2a(x, got, residual=res, ids=gids)
+        L.forward_a2a(x, got, residual=res, ids=gids, t_cap=0 if cap == 0 else max(T, 1) + (cap - 1))
     finally:
         D.force_generic(prev)
     torch.cuda.synchronize()
