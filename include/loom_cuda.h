@@ -4,8 +4,7 @@
  *
  * The backend slots in behind Loom's comptime backend seam
  * (src/compute/backend.zig:28-49) as a `cuda` arm, next to cpu/metal/vulkan.
- * Each seam entry below cites the reference declaration it replaces; the Zig
- * binding a maintainer adds is shown in INTEGRATION.md.
+ * Each seam entry below cites the reference declaration it replaces.
  *
  * Conventions (the seam's, src/compute/backend.zig and src/vulkan/backend.zig):
  *  - Host slices are borrowed for the duration of the call; `out` is written
@@ -19,6 +18,11 @@
  *    message is in loom_cuda_last_error). No CPU fallback exists inside the
  *    backend.
  *  - One generation thread calls the backend; it is not reentrant.
+ *  - Streams: entries that take `void *stream` run on that cudaStream_t. NULL
+ *    means the backend's own stream, a blocking stream: it is ordered after
+ *    and before work on the legacy default stream (stream 0), but not with
+ *    other non-blocking streams -- a caller that queues inputs on its own
+ *    stream passes that stream.
  *
  * ggml type ids (src/gguf/ggml.zig:23-45): F32 0, Q4_0 2, Q8_0 8, Q4_K 12, Q6_K 14.
  */
@@ -322,6 +326,16 @@ int loom_cuda_device_error(void);
 int loom_cuda_sync(void);
 /* The backend's stream (cudaStream_t). */
 void *loom_cuda_stream(void);
+/* Diagnostic (no counterpart in the reference): enable >= 0 turns the
+ * tensor-core kernels' cycle profile of CTA 0 on (1) or off (0) and zeroes it;
+ * enable < 0 synchronizes the device and copies min(n, 32) counters (gate/up
+ * then down, 16 each) to out. */
+int loom_cuda_tc_profile(int enable, unsigned long long *out, size_t n);
+/* Diagnostic (no counterpart in the reference): a bf16 tcgen05 GEMM
+ * D[M][N] = A[M][K] . B[N][K]^T on host arrays (bf16 bit patterns in, f32
+ * out). M a multiple of 128, N in 16..256 in steps of 16, K a multiple of 64.
+ * 0 ok, 1 bad arguments, 2 CUDA error, 3 an MMA completion wait gave up. */
+int loom_cuda_umma_selftest(const uint16_t *A, const uint16_t *B, float *D, int M, int N, int K);
 
 #ifdef __cplusplus
 }

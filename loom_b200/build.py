@@ -35,14 +35,18 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
     os.makedirs(os.path.join(LIBDIR, "obj"), exist_ok=True)
-    objs = []
-    for src in sources():
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(src):
         obj = os.path.join(LIBDIR, "obj", os.path.basename(src) + ".o")
-        cmd = [NVCC, *ARCH, *FLAGS, "-dc" if False else "-c", src, "-o", obj]
+        cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
         subprocess.run(cmd, check=True)
-        objs.append(obj)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
+        objs = list(pool.map(compile_one, sources()))
     subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"],
                    check=True)
     return LIB

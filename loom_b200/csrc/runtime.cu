@@ -596,7 +596,9 @@ int loom_cuda_init(int device) {
     cudaDeviceProp p;
     CK(cudaGetDeviceProperties(&p, device));
     if (p.major != 10) return decline("this backend is built for sm_100a (B200)");
-    CK(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking));
+    // A blocking stream: work on the legacy default stream (where torch and most
+    // C callers queue their copies) is ordered before and after it.
+    CK(cudaStreamCreateWithFlags(&g_stream, cudaStreamDefault));
     g_device = device;
     g_inited = true;
     return LOOM_CUDA_OK;

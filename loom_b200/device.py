@@ -20,6 +20,16 @@ def _ptr(t) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def _st(stream) -> int:
+    """The stream a call runs on: the caller's, else torch's current stream, so
+    the backend's kernels are ordered after the copies and fills that torch
+    queued for their inputs and before torch's reads of their outputs."""
+    if stream is not None:
+        return stream
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
 class DeviceTensor:
     def __init__(self, handle: int, ty: int, nblk: int):
         self.handle, self.ty, self.nblk = handle, ty, nblk
@@ -99,11 +109,11 @@ class MoeLayer:
         T = x.shape[0]
         if t_cap:
             rc = _lib.lib().loom_cuda_ep_a2a_forward_cap(C.byref(d), _ptr(x), T, t_cap, _ptr(out), _ptr(residual),
-                                                         _ptr(logits), _ptr(ids), stream)
+                                                         _ptr(logits), _ptr(ids), _st(stream))
             _lib.must(rc, "ep_a2a_forward_cap")
             return
         rc = _lib.lib().loom_cuda_ep_a2a_forward(C.byref(d), _ptr(x), T, _ptr(out), _ptr(residual), _ptr(logits),
-                                                 _ptr(ids), stream)
+                                                 _ptr(ids), _st(stream))
         _lib.must(rc, "ep_a2a_forward")
 
     def forward(self, x, out, residual=None, logits=None, ids=None, stream=None, desc=None) -> None:
@@ -111,7 +121,7 @@ class MoeLayer:
         d = desc if desc is not None else self.desc()
         T = x.shape[0]
         rc = _lib.lib().loom_cuda_moe_forward(C.byref(d), _ptr(x), T, _ptr(out), _ptr(residual), _ptr(logits),
-                                              _ptr(ids), stream)
+                                              _ptr(ids), _st(stream))
         _lib.must(rc, "moe_forward")
 
 
@@ -126,7 +136,7 @@ class Stack:
         self.n_layers = len(layers)
 
     def forward(self, x, out, ids=None, stream=None) -> None:
-        _lib.must(_lib.lib().loom_cuda_stack_forward(self.handle, _ptr(x), _ptr(out), _ptr(ids), stream), "stack_forward")
+        _lib.must(_lib.lib().loom_cuda_stack_forward(self.handle, _ptr(x), _ptr(out), _ptr(ids), _st(stream)), "stack_forward")
 
     def error(self) -> int:
         return int(_lib.lib().loom_cuda_stack_error(self.handle))
@@ -172,7 +182,7 @@ def argmax(logits, out=None, stream=None):
     """sampler.zig:7-15 argmax of a cuda float32 vector; returns a cuda int32 [1] (the index)."""
     import torch
     out = torch.zeros(1, dtype=torch.int32, device=logits.device) if out is None else out
-    _lib.must(_lib.lib().loom_cuda_argmax(_ptr(logits), logits.numel(), _ptr(out), stream), "argmax")
+    _lib.must(_lib.lib().loom_cuda_argmax(_ptr(logits), logits.numel(), _ptr(out), _st(stream)), "argmax")
     return out
 
 
@@ -180,7 +190,7 @@ def lm_head_argmax(w: DeviceTensor, vocab: int, dim: int, x, logits=None, out=No
     """Output head + greedy sample of one token: (logits W x, their argmax)."""
     import torch
     out = torch.zeros(1, dtype=torch.int32, device=x.device) if out is None else out
-    _lib.must(_lib.lib().loom_cuda_lm_head_argmax(w.handle, vocab, dim, _ptr(x), _ptr(logits), _ptr(out), stream),
+    _lib.must(_lib.lib().loom_cuda_lm_head_argmax(w.handle, vocab, dim, _ptr(x), _ptr(logits), _ptr(out), _st(stream)),
               "lm_head_argmax")
     return out
 
@@ -190,7 +200,7 @@ def reserve(T: int, dim: int, ffn: int, n_expert: int, n_used: int) -> None:
 
 
 def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -> None:
-    _lib.must(_lib.lib().loom_cuda_tensor_matmul(w.handle, rows, cols, _ptr(xs), xs.shape[0], _ptr(out), stream),
+    _lib.must(_lib.lib().loom_cuda_tensor_matmul(w.handle, rows, cols, _ptr(xs), xs.shape[0], _ptr(out), _st(stream)),
               "tensor_matmul")
 
 

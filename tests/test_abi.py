@@ -15,6 +15,16 @@ def test_library_exports_every_header_symbol():
     assert not missing, missing
 
 
+def test_every_exported_symbol_is_declared():
+    """The library exports no loom_cuda_* entry that the header leaves out."""
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.split() and ln.split()[-1].startswith("loom_cuda_")}
+    undeclared = sorted(exported - set(_lib.header_symbols()))
+    assert not undeclared, undeclared
+
+
 def test_seam_declines_before_init():
     L = _lib.lib()
     out = np.zeros(4, np.float32)

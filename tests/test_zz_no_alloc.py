@@ -27,7 +27,7 @@ TOL = 2e-3
 def _noalloc(layer, x, out, residual):
     d = layer.desc()
     rc = _lib.lib().loom_cuda_moe_forward_noalloc(C.byref(d), x.data_ptr(), x.shape[0], out.data_ptr(),
-                                                   residual.data_ptr(), None)
+                                                   residual.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _lib.must(rc, "moe_forward_noalloc")
 
 
