@@ -1127,3 +1127,104 @@ void or_synth(int type, void *out, uint64_t blk0, uint64_t nblk, uint64_t seed, 
 }
 
 }  // extern "C"
+
+// ---- llama.zig:1111-1228 step ---------------------------------------------------
+
+// llama.zig:821-826 ropeTheta
+static void rope_theta(size_t i, size_t rope_dim, size_t pos, float base, float &c, float &s) {
+    const float exponent = (float)i / (float)rope_dim;
+    const float freq = std::pow(base, -exponent);
+    const float angle = (float)pos * freq;
+    c = std::cos(angle);
+    s = std::sin(angle);
+}
+
+// llama.zig:830-839 ropeNorm (adjacent pairs) and :845-856 ropeNeox (split halves)
+static void rope_apply(int neox, float *vec, size_t rope_dim, size_t pos, float base) {
+    if (neox) {
+        const size_t half = rope_dim / 2;
+        for (size_t i = 0; i < half; i++) {
+            float c, s;
+            rope_theta(2 * i, rope_dim, pos, base, c, s);
+            const float a = vec[i], b = vec[i + half];
+            vec[i] = a * c - b * s;
+            vec[i + half] = a * s + b * c;
+        }
+    } else {
+        for (size_t i = 0; i + 1 < rope_dim; i += 2) {
+            float c, s;
+            rope_theta(i, rope_dim, pos, base, c, s);
+            const float a = vec[i], b = vec[i + 1];
+            vec[i] = a * c - b * s;
+            vec[i + 1] = a * s + b * c;
+        }
+    }
+}
+
+// llama.zig:938-950 headNorm
+static void head_norm(float *vec, const float *g, size_t n_heads, size_t hd, float eps) {
+    if (!g) return;
+    for (size_t h = 0; h < n_heads; h++) {
+        float *head = vec + h * hd;
+        float ss = 0.0f;
+        for (size_t i = 0; i < hd; i++) ss += head[i] * head[i];
+        const float inv = 1.0f / std::sqrt(ss / (float)hd + eps);
+        for (size_t i = 0; i < hd; i++) head[i] = head[i] * inv * g[i];
+    }
+}
+
+// ggml.zig:222-231 axpy (elementwise, no contraction)
+static void axpy(float *out, const float *v, float w, size_t n) {
+    for (size_t i = 0; i < n; i++) out[i] = out[i] + w * v[i];
+}
+
+int or_llama_step(const or_llama_model *m, float *k_cache, float *v_cache, uint32_t token, size_t pos,
+                  float *logits) {
+    const size_t dim = m->dim, hd = m->head_dim, nh = m->n_heads, nkv = m->n_kv_heads;
+    if (token >= m->vocab || pos >= m->ctx_len || nkv == 0 || nh % nkv) return -1;
+    const size_t kvd = nkv * hd, qd = nh * hd, q_per_kv = nh / nkv;
+    const float scale = m->attn_logit_mul / std::sqrt((float)hd);
+    std::vector<float> x(dim), normed(dim), q(qd), k(kvd), v(kvd), att(qd), proj(dim), scores(pos + 1), acc(dim);
+    if (or_dequant_row(m->embd_type, x.data(), m->token_embd, token, dim)) return -1;  // :1122
+    for (size_t li = 0; li < m->n_layers; li++) {
+        const or_llama_layer &l = m->layers[li];
+        or_rmsnorm(normed.data(), x.data(), l.attn_norm, dim, m->eps);               // :1139
+        if (or_matvec(l.wq_type, q.data(), l.wq, normed.data(), qd, dim)) return -1;  // :1140-1142
+        if (or_matvec(l.wk_type, k.data(), l.wk, normed.data(), kvd, dim)) return -1;
+        if (or_matvec(l.wv_type, v.data(), l.wv, normed.data(), kvd, dim)) return -1;
+        head_norm(q.data(), l.q_norm, nh, hd, m->eps);                               // :1148-1149
+        head_norm(k.data(), l.k_norm, nkv, hd, m->eps);
+        for (size_t h = 0; h < nh; h++) rope_apply(m->rope_neox, q.data() + h * hd, m->rope_dim, pos, m->rope_base);
+        for (size_t h = 0; h < nkv; h++) rope_apply(m->rope_neox, k.data() + h * hd, m->rope_dim, pos, m->rope_base);
+        const size_t base = (li * m->ctx_len + pos) * kvd;                            // :1157
+        std::memcpy(k_cache + base, k.data(), kvd * 4);
+        std::memcpy(v_cache + base, v.data(), kvd * 4);
+        const size_t seq = pos + 1;
+        for (size_t h = 0; h < nh; h++) {                                             // :1171-1191
+            const size_t kvh = h / q_per_kv;
+            const float *qh = q.data() + h * hd;
+            for (size_t t = 0; t < seq; t++)
+                scores[t] = or_dot_f32(qh, k_cache + (li * m->ctx_len + t) * kvd + kvh * hd, hd) * scale;
+            or_softmax(scores.data(), seq);
+            float *oh = att.data() + h * hd;
+            for (size_t i = 0; i < hd; i++) oh[i] = 0.0f;
+            for (size_t t = 0; t < seq; t++) axpy(oh, v_cache + (li * m->ctx_len + t) * kvd + kvh * hd, scores[t], hd);
+        }
+        if (or_matvec(l.wo_type, proj.data(), l.wo, att.data(), dim, qd)) return -1;  // :1193
+        for (size_t i = 0; i < dim; i++) x[i] += proj[i];                             // :1195
+        or_rmsnorm(normed.data(), x.data(), l.ffn_norm, dim, m->eps);                 // :1216/:1222
+        if (!l.router) {  // :1212-1218 denseFFN then add
+            or_expert e{l.gate_type, l.up_type, l.down_type, l.gate, l.up, l.down, 1.0f, l.ffn};
+            std::vector<float> g, u;
+            if (dense_ffn(e, normed.data(), dim, acc.data(), g, u)) return -1;
+        } else {  // :1224 moeLayer, then add(x, moe_acc)
+            if (or_moe_layer(normed.data(), 1, dim, l.router, l.gate_type, l.gate, l.up_type, l.up, l.down_type,
+                             l.down, l.ffn, m->n_expert, m->n_used, m->gating, m->weights_norm, m->weights_scale,
+                             acc.data(), nullptr))
+                return -1;
+        }
+        for (size_t i = 0; i < dim; i++) x[i] += acc[i];
+    }
+    or_rmsnorm(normed.data(), x.data(), m->output_norm, dim, m->eps);                 // :1226-1227
+    return or_matvec(m->output_type, logits, m->output, normed.data(), m->vocab, dim);
+}

@@ -96,6 +96,43 @@ int or_moe_layer(const float *x, size_t T, size_t dim, const float *router_w, in
                  const uint8_t *down3d, size_t ffn, size_t n_expert, size_t n_used, int gating,
                  int weights_norm, float weights_scale, float *out, uint32_t *ids_out);
 
+/* One decoder layer of llama.zig's model (Model.layers, llama.zig:136-200):
+ * attention weights, optional per-head Q/K RMSNorm weights (qwen3moe), and
+ * either a dense SwiGLU FFN (router == NULL) or a routed MoE FFN whose f32
+ * router is [n_expert][dim] and whose gate/up/down are 3D expert tensors. */
+typedef struct {
+    const float *attn_norm, *ffn_norm;   /* f32 [dim] */
+    int wq_type, wk_type, wv_type, wo_type;
+    const uint8_t *wq, *wk, *wv, *wo;    /* [n_heads*hd][dim], [n_kv*hd][dim] x2, [dim][n_heads*hd] */
+    const float *q_norm, *k_norm;        /* f32 [hd] or NULL */
+    int gate_type, up_type, down_type;
+    const uint8_t *gate, *up, *down;     /* dense [ffn][dim].. or 3D [n_expert][ffn][dim].. */
+    size_t ffn;
+    const float *router;                 /* f32 [n_expert][dim]; NULL = dense FFN */
+} or_llama_layer;
+typedef struct {
+    size_t dim, n_layers, n_heads, n_kv_heads, head_dim, rope_dim, vocab, ctx_len;
+    float eps, rope_base, attn_logit_mul;
+    int rope_neox;                        /* 1: ropeNeox (qwen3moe), 0: ropeNorm (llama) */
+    size_t n_expert, n_used;              /* routed layers */
+    int gating, weights_norm;
+    float weights_scale;
+    int embd_type;
+    const uint8_t *token_embd;            /* [vocab][dim] */
+    const float *output_norm;             /* f32 [dim] */
+    int output_type;
+    const uint8_t *output;                /* [vocab][dim] */
+    const or_llama_layer *layers;
+} or_llama_model;
+/* llama.zig:1111-1228 step (the per-operation path, no frame): embedding
+ * row, per layer RMSNorm -> q/k/v matvecs -> headNorm (:938) -> RoPE (:830-858)
+ * -> KV append -> per-head softmax attention over positions 0..pos (dotF32,
+ * softmax, axpy) -> output projection -> residual; RMSNorm -> dense FFN or
+ * moeLayer -> residual; final RMSNorm -> output head. k_cache / v_cache:
+ * f32 [n_layers][ctx_len][n_kv*hd], the caller's. logits: f32 [vocab]. */
+int or_llama_step(const or_llama_model *m, float *k_cache, float *v_cache, uint32_t token, size_t pos,
+                  float *logits);
+
 /* Seeded synthetic tensors (counter-based, the same generator the CUDA backend
  * runs on the device): blocks [blk0, blk0+nblk) of a tensor of `type`. For
  * OR_F32, "blocks" are elements ~ sigma * IrwinHall12. */

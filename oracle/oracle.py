@@ -61,6 +61,7 @@ def lib() -> C.CDLL:
                                         vp, vp, sz, sz, sz, C.c_int, C.c_int, fp, vp]
         L.or_moe_layer.argtypes = [vp, sz, sz, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, sz, sz,
                                    sz, C.c_int, C.c_int, fp, vp, vp]
+        L.or_llama_step.argtypes = [vp, vp, vp, C.c_uint32, sz, vp]
         L.or_synth.argtypes = [C.c_int, vp, C.c_uint64, C.c_uint64, C.c_uint64, fp]
         L.or_f32_to_f16_rne.restype = C.c_uint16
         L.or_f32_to_f16_rne.argtypes = [fp]
@@ -240,3 +241,74 @@ def synth(t, nblk, seed, blk0=0, sigma=1.0):
 
 def f32_to_f16_rne(v):
     return int(lib().or_f32_to_f16_rne(v))
+
+
+class LlamaLayer(C.Structure):
+    """or_llama_layer: one decoder layer (llama.zig:136-200)."""
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p),
+                ("wq_type", C.c_int), ("wk_type", C.c_int), ("wv_type", C.c_int), ("wo_type", C.c_int),
+                ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+                ("ffn", C.c_size_t), ("router", C.c_void_p)]
+
+
+class LlamaModel(C.Structure):
+    """or_llama_model."""
+    _fields_ = [("dim", C.c_size_t), ("n_layers", C.c_size_t), ("n_heads", C.c_size_t), ("n_kv_heads", C.c_size_t),
+                ("head_dim", C.c_size_t), ("rope_dim", C.c_size_t), ("vocab", C.c_size_t), ("ctx_len", C.c_size_t),
+                ("eps", C.c_float), ("rope_base", C.c_float), ("attn_logit_mul", C.c_float),
+                ("rope_neox", C.c_int), ("n_expert", C.c_size_t), ("n_used", C.c_size_t),
+                ("gating", C.c_int), ("weights_norm", C.c_int), ("weights_scale", C.c_float),
+                ("embd_type", C.c_int), ("token_embd", C.c_void_p), ("output_norm", C.c_void_p),
+                ("output_type", C.c_int), ("output", C.c_void_p), ("layers", C.POINTER(LlamaLayer))]
+
+
+class LlamaRunner:
+    """llama.zig:1111-1228 step on host tensors, with its own f32 KV cache.
+
+    `tensors` maps the GGUF tensor names of a model spec (loom_b200.model.ModelSpec)
+    to (type, numpy bytes or floats)."""
+
+    def __init__(self, spec, tensors):
+        self.spec, self.t = spec, tensors  # keep the arrays alive
+        c = spec
+        self._layers = (LlamaLayer * c.n_layers)()
+        for i in range(c.n_layers):
+            L = self._layers[i]
+            g = lambda n: tensors.get(f"blk.{i}.{n}")  # noqa: E731
+            L.attn_norm, L.ffn_norm = _p(g("attn_norm")[1]), _p(g("ffn_norm")[1])
+            for nm, tn in (("q", "attn_q"), ("k", "attn_k"), ("v", "attn_v"), ("o", "attn_output")):
+                ty, data = g(tn)
+                setattr(L, f"w{nm}_type", ty)
+                setattr(L, f"w{nm}", _p(data))
+            L.q_norm = _p(g("attn_q_norm")[1]) if g("attn_q_norm") else None
+            L.k_norm = _p(g("attn_k_norm")[1]) if g("attn_k_norm") else None
+            moe = g("ffn_gate_inp") is not None
+            sfx = "_exps" if moe else ""
+            for nm in ("gate", "up", "down"):
+                ty, data = g(f"ffn_{nm}{sfx}")
+                setattr(L, f"{nm}_type", ty)
+                setattr(L, nm, _p(data))
+            L.ffn = c.moe_ffn if moe else c.ffn
+            L.router = _p(g("ffn_gate_inp")[1]) if moe else None
+        M = LlamaModel()
+        M.dim, M.n_layers, M.n_heads, M.n_kv_heads = c.dim, c.n_layers, c.n_heads, c.n_kv_heads
+        M.head_dim, M.rope_dim, M.vocab, M.ctx_len = c.head_dim, c.rope_dim, c.vocab, c.ctx_len
+        M.eps, M.rope_base, M.attn_logit_mul, M.rope_neox = c.eps, c.rope_base, 1.0, int(c.rope_neox)
+        M.n_expert, M.n_used, M.gating, M.weights_norm, M.weights_scale = c.n_expert, c.n_used, 1, 1, 1.0
+        M.embd_type, M.token_embd = tensors["token_embd"][0], _p(tensors["token_embd"][1])
+        M.output_norm = _p(tensors["output_norm"][1])
+        M.output_type, M.output = tensors["output"][0], _p(tensors["output"][1])
+        M.layers = self._layers
+        self.m = M
+        kvd = c.n_kv_heads * c.head_dim
+        self.kc = np.zeros(c.n_layers * c.ctx_len * kvd, np.float32)
+        self.vc = np.zeros_like(self.kc)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.spec.vocab, np.float32)
+        rc = lib().or_llama_step(C.byref(self.m), _p(self.kc), _p(self.vc), token, pos, _p(logits))
+        assert rc == 0
+        return logits
