@@ -1,0 +1,234 @@
+"""Whole-model decode on the device (include/loom_cuda.h, loom_cuda_model_*).
+
+`ModelSpec` describes a decoder in the reference's tensor naming (GGUF names,
+src/gguf/llama.zig:136-200) and shapes; `DeviceModel` holds its tensors on the
+GPU and runs the reference's token step (llama.zig:1111-1228) there. The
+weights are seeded synthetic tensors generated on the device by the backend's
+counter-based generator (the same bytes `oracle.synth` makes on the host), so a
+test can build the identical model on both sides.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import zlib
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+
+from . import _lib
+from .device import BLOCK_BYTES, DeviceTensor
+
+F32, Q4_0, Q8_0, Q4_K, Q6_K = 0, 2, 8, 12, 14
+BLOCK_ELEMS = {0: 1, 2: 32, 3: 32, 6: 32, 7: 32, 8: 32, 10: 256, 11: 256, 12: 256, 13: 256, 14: 256}
+
+
+@dataclass
+class TensorPlan:
+    name: str
+    type: int
+    rows: int
+    cols: int
+    planes: int = 1         # 3D expert tensors: [planes][rows][cols]
+    fill: str = "synth"     # synth | ones | near_ones
+    sigma: float = 1.0      # f32 synth standard deviation
+    seed: int = 0
+
+    @property
+    def nblk(self) -> int:
+        return self.planes * self.rows * self.cols // BLOCK_ELEMS[self.type]
+
+    @property
+    def nbytes(self) -> int:
+        return self.nblk * BLOCK_BYTES[self.type]
+
+
+@dataclass
+class ModelSpec:
+    name: str
+    dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    ctx_len: int
+    eps: float = 1e-5
+    rope_base: float = 10000.0
+    rope_neox: bool = False
+    rope_dim: int = 0            # 0: head_dim
+    qk_norm: bool = False
+    ffn: int = 0                 # dense FFN width (n_expert == 0)
+    n_expert: int = 0
+    n_used: int = 0
+    moe_ffn: int = 0
+    types: Dict[str, int] = field(default_factory=dict)
+    norms: str = "ones"          # ones | near_ones
+    seed: int = 1
+
+    def __post_init__(self):
+        if not self.rope_dim:
+            self.rope_dim = self.head_dim
+
+    def ty(self, key: str) -> int:
+        return self.types[key]
+
+    def plan(self) -> List[TensorPlan]:
+        """Every tensor of the model, in a fixed order (the seeds follow the names)."""
+        d, qd, kvd = self.dim, self.n_heads * self.head_dim, self.n_kv_heads * self.head_dim
+        out = [TensorPlan("token_embd", self.ty("embd"), self.vocab, d, sigma=0.02),
+               TensorPlan("output_norm", F32, 1, d, fill=self.norms),
+               TensorPlan("output", self.ty("output"), self.vocab, d)]
+        for i in range(self.n_layers):
+            p = f"blk.{i}."
+            out += [TensorPlan(p + "attn_norm", F32, 1, d, fill=self.norms),
+                    TensorPlan(p + "attn_q", self.ty("attn_q"), qd, d),
+                    TensorPlan(p + "attn_k", self.ty("attn_k"), kvd, d),
+                    TensorPlan(p + "attn_v", self.ty("attn_v"), kvd, d),
+                    TensorPlan(p + "attn_output", self.ty("attn_output"), d, qd),
+                    TensorPlan(p + "ffn_norm", F32, 1, d, fill=self.norms)]
+            if self.qk_norm:
+                out += [TensorPlan(p + "attn_q_norm", F32, 1, self.head_dim, fill="near_ones"),
+                        TensorPlan(p + "attn_k_norm", F32, 1, self.head_dim, fill="near_ones")]
+            if self.n_expert:
+                ne, f = self.n_expert, self.moe_ffn
+                out += [TensorPlan(p + "ffn_gate_inp", F32, ne, d, sigma=0.02),
+                        TensorPlan(p + "ffn_gate_exps", self.ty("ffn_gate"), f, d, planes=ne),
+                        TensorPlan(p + "ffn_up_exps", self.ty("ffn_up"), f, d, planes=ne),
+                        TensorPlan(p + "ffn_down_exps", self.ty("ffn_down"), d, f, planes=ne)]
+            else:
+                out += [TensorPlan(p + "ffn_gate", self.ty("ffn_gate"), self.ffn, d),
+                        TensorPlan(p + "ffn_up", self.ty("ffn_up"), self.ffn, d),
+                        TensorPlan(p + "ffn_down", self.ty("ffn_down"), d, self.ffn)]
+        for t in out:
+            t.seed = (self.seed * 0x9E3779B1 + zlib.crc32(t.name.encode())) & 0xFFFFFFFF
+        return out
+
+    def weight_bytes(self) -> int:
+        return sum(t.nbytes for t in self.plan())
+
+
+def fill_values(t: TensorPlan) -> np.ndarray:
+    """The f32 values of a non-synthetic tensor (norm weights)."""
+    n = t.planes * t.rows * t.cols
+    if t.fill == "ones":
+        return np.ones(n, np.float32)
+    rng = np.random.default_rng(t.seed)
+    return (1.0 + rng.uniform(-0.25, 0.25, n)).astype(np.float32)
+
+
+def tiny_llama(ctx_len: int = 256, seed: int = 1) -> ModelSpec:
+    """llama-arch, dim 288, 6 layers, 6 heads of 48, FFN 768,
+    vocab 32000, every matrix Q4_0, f32 embeddings ~N(0, 0.02), norms 1.0."""
+    q = Q4_0
+    return ModelSpec("tiny-llama-q4_0", dim=288, n_layers=6, n_heads=6, n_kv_heads=6, head_dim=48, vocab=32000,
+                     ctx_len=ctx_len, eps=1e-5, rope_base=10000.0, rope_neox=False, ffn=768,
+                     types=dict(embd=F32, output=q, attn_q=q, attn_k=q, attn_v=q, attn_output=q, ffn_gate=q,
+                                ffn_up=q, ffn_down=q), seed=seed)
+
+
+def qwen3_moe(n_layers: int = 48, ctx_len: int = 2048, n_expert: int = 128, vocab: int = 151936,
+              seed: int = 3) -> ModelSpec:
+    """Qwen3-30B-A3B shape (48 layers, hidden 2048, 32 query /
+    4 KV heads of 128, QK-RMSNorm, RoPE NEOX base 1e6, 128 experts top-8 of
+    FFN 768, vocab 151936) in the Q4_K_M mix: attn_q/k/output, gate/up and the
+    embeddings Q4_K; attn_v, ffn_down and output Q6_K; router and norms f32."""
+    return ModelSpec("qwen3-30b-a3b-q4_k_m", dim=2048, n_layers=n_layers, n_heads=32, n_kv_heads=4, head_dim=128,
+                     vocab=vocab, ctx_len=ctx_len, eps=1e-6, rope_base=1e6, rope_neox=True, qk_norm=True,
+                     n_expert=n_expert, n_used=8, moe_ffn=768,
+                     types=dict(embd=Q4_K, output=Q6_K, attn_q=Q4_K, attn_k=Q4_K, attn_v=Q6_K, attn_output=Q4_K,
+                                ffn_gate=Q4_K, ffn_up=Q4_K, ffn_down=Q6_K), norms="near_ones", seed=seed)
+
+
+class DeviceModel:
+    """A ModelSpec's tensors on the GPU plus the backend's model handle."""
+
+    def __init__(self, spec: ModelSpec, host: Optional[Dict[str, np.ndarray]] = None):
+        self.spec = spec
+        self.t: Dict[str, DeviceTensor] = {}
+        for p in spec.plan():
+            if host is not None and p.name in host:
+                self.t[p.name] = DeviceTensor.upload(p.type, host[p.name])
+            elif p.fill == "synth":
+                self.t[p.name] = DeviceTensor.synth(p.type, p.nblk, p.seed, p.sigma)
+            else:
+                self.t[p.name] = DeviceTensor.upload(F32, fill_values(p))
+        self._layers = (_lib.ModelLayer * spec.n_layers)()
+        h = lambda n: self.t[n].handle if n in self.t else 0  # noqa: E731
+        for i in range(spec.n_layers):
+            L, p = self._layers[i], f"blk.{i}."
+            L.attn_norm, L.ffn_norm = h(p + "attn_norm"), h(p + "ffn_norm")
+            L.wq, L.wk, L.wv, L.wo = h(p + "attn_q"), h(p + "attn_k"), h(p + "attn_v"), h(p + "attn_output")
+            L.q_norm, L.k_norm = h(p + "attn_q_norm"), h(p + "attn_k_norm")
+            if spec.n_expert:
+                m = L.moe
+                m.dim, m.ffn, m.n_expert, m.n_used = spec.dim, spec.moe_ffn, spec.n_expert, spec.n_used
+                m.gating, m.weights_norm, m.weights_scale = 1, 1, 1.0
+                m.router = h(p + "ffn_gate_inp")
+                m.gate, m.up, m.down = h(p + "ffn_gate_exps"), h(p + "ffn_up_exps"), h(p + "ffn_down_exps")
+                m.n_local = spec.n_expert
+                m.n_group = m.topk_group = 1
+                if i + 1 < spec.n_layers:
+                    m.next_router = h(f"blk.{i + 1}.ffn_gate_inp")
+            else:
+                L.ffn_gate, L.ffn_up, L.ffn_down = h(p + "ffn_gate"), h(p + "ffn_up"), h(p + "ffn_down")
+                L.ffn = spec.ffn
+        d = _lib.ModelDesc()
+        d.dim, d.n_layers, d.n_heads, d.n_kv_heads = spec.dim, spec.n_layers, spec.n_heads, spec.n_kv_heads
+        d.head_dim, d.rope_dim, d.vocab, d.ctx_len = spec.head_dim, spec.rope_dim, spec.vocab, spec.ctx_len
+        d.eps, d.rope_base, d.attn_logit_mul, d.rope_neox = spec.eps, spec.rope_base, 1.0, int(spec.rope_neox)
+        d.token_embd, d.output_norm, d.output = h("token_embd"), h("output_norm"), h("output")
+        d.layers = self._layers
+        self.desc = d
+        hh = C.c_uint64(0)
+        _lib.must(_lib.lib().loom_cuda_model_create(C.byref(d), C.byref(hh)), "model_create")
+        self.handle = hh.value
+
+    def decode(self, token: int, pos: int, logits: bool = False):
+        """One token through the host entry point: returns (next token, logits or None)."""
+        nxt = C.c_uint32(0)
+        lg = np.empty(self.spec.vocab, np.float32) if logits else None
+        _lib.must(_lib.lib().loom_cuda_model_decode(self.handle, token, pos,
+                                                    lg.ctypes.data_as(C.c_void_p) if logits else None,
+                                                    C.byref(nxt)), "model_decode")
+        return nxt.value, lg
+
+    def step(self, d_token, d_pos, d_logits=None, d_next=None, stream=None) -> None:
+        """The step on device buffers (torch cuda tensors: int32 [1])."""
+        from .device import _st
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        _lib.must(_lib.lib().loom_cuda_model_step(self.handle, p(d_token), p(d_pos), p(d_logits), p(d_next),
+                                                  _st(stream)), "model_step")
+
+    def read_kv(self, layer: int, pos: int):
+        kvd = self.spec.n_kv_heads * self.spec.head_dim
+        k, v = np.empty(kvd, np.float32), np.empty(kvd, np.float32)
+        _lib.must(_lib.lib().loom_cuda_model_read_kv(self.handle, layer, pos, k.ctypes.data_as(C.c_void_p),
+                                                     v.ctypes.data_as(C.c_void_p)), "model_read_kv")
+        return k, v
+
+    def free(self) -> None:
+        if self.handle:
+            _lib.lib().loom_cuda_model_free(self.handle)
+            self.handle = 0
+        for t in self.t.values():
+            t.free()
+        self.t.clear()
+
+
+def greedy(step, prompt: List[int], n_new: int) -> List[int]:
+    """The generation loop: feed the prompt at positions 0..len-1, then take the
+    argmax token and feed it back (sampler.zig:7-15 greedy), n_new tokens.
+    `step(token, pos)` returns the next token."""
+    out: List[int] = []
+    nxt = None
+    for pos, tok in enumerate(prompt):
+        nxt = step(tok, pos)
+    pos = len(prompt)
+    for _ in range(n_new):
+        out.append(nxt)
+        if len(out) == n_new:
+            break
+        nxt = step(nxt, pos)
+        pos += 1
+    return out
