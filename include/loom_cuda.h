@@ -212,6 +212,66 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
 #define LOOM_CUDA_NOALLOC_SCRATCH_BYTES (1u << 20)
 int loom_cuda_moe_forward_noalloc(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out,
                                   const float *d_residual, void *stream);
+/* ---- whole-model decode on the device ----------------------------------------
+ * The reference's decode step (llama.zig:1111-1228 `step`; the seam's frame
+ * path beginFrame/layerBlock/endFrame, src/compute/backend.zig:146-156, with
+ * attnInit/kvAppend/attnHeads, :121-160) kept on the device for a whole token:
+ * embedding row (dequantRow), then per layer RMSNorm -> q/k/v matvecs ->
+ * per-head Q/K RMSNorm when given (headNorm, :938) -> RoPE (ropeNorm or
+ * ropeNeox, :830-858) -> append to the f32 KV cache [layer][ctx][n_kv*hd] ->
+ * softmax attention of every query head over positions 0..pos (GQA) -> output
+ * projection -> residual add -> RMSNorm -> dense SwiGLU FFN or routed MoE
+ * layer -> residual add; final RMSNorm -> output head -> argmax (sampler.zig:7).
+ * The residual stream never leaves the device. Every tensor is a device tensor
+ * (loom_tensor); norms are f32. */
+typedef struct {
+    loom_tensor attn_norm;            /* f32 [dim] */
+    loom_tensor wq, wk, wv, wo;       /* [n_heads*hd][dim], [n_kv*hd][dim] (x2), [dim][n_heads*hd] */
+    loom_tensor q_norm, k_norm;       /* f32 [hd] each, or 0 (no per-head norm) */
+    loom_tensor ffn_norm;             /* f32 [dim] */
+    /* FFN: routed when moe.n_expert > 0 (moe.dim must equal the model's dim),
+     * else dense: ffn_gate/ffn_up [ffn][dim], ffn_down [dim][ffn] */
+    loom_tensor ffn_gate, ffn_up, ffn_down;
+    size_t ffn;
+    loom_moe_desc moe;
+} loom_model_layer;
+typedef struct {
+    size_t dim, n_layers, n_heads, n_kv_heads, head_dim, rope_dim, vocab, ctx_len;
+    float eps, rope_base, attn_logit_mul; /* scores = q.k * attn_logit_mul / sqrt(head_dim) */
+    int rope_neox;                        /* 1 ropeNeox (qwen3moe, qwen2moe), 0 ropeNorm (llama) */
+    loom_tensor token_embd;               /* [vocab][dim], any supported type */
+    loom_tensor output_norm;              /* f32 [dim] */
+    loom_tensor output;                   /* [vocab][dim] */
+    const loom_model_layer *layers;       /* [n_layers], copied by create */
+} loom_model_desc;
+/* Build the model: checks every tensor's type and size, allocates the KV
+ * cache (2 x n_layers x ctx_len x n_kv*hd f32), the RoPE table and the step's
+ * buffers. Limits: head_dim even and <= 256, rope_dim <= head_dim, n_heads a
+ * multiple of n_kv_heads with at most 16 query heads per KV head. Contexts up
+ * to 512 positions use the attention kernel that keeps the reference's exact
+ * operation order (dotF32 scores, serial softmax sum, axpy in position order);
+ * longer contexts split the positions across CTAs and merge. */
+int loom_cuda_model_create(const loom_model_desc *desc, uint64_t *handle);
+/* One decode step on device memory (graph-capturable after the first call):
+ * d_token / d_pos: device u32 [1] (the token at position pos < ctx_len);
+ * d_logits: optional device f32 [vocab]; d_next: optional device u32 [1]
+ * receiving the greedy token. The caller keeps token < vocab and
+ * pos < ctx_len; out-of-range values only stay inside the model's buffers
+ * (the token is clamped, a position >= ctx_len skips the cache write and the
+ * attention) and give a meaningless result. */
+int loom_cuda_model_step(uint64_t handle, const uint32_t *d_token, const uint32_t *d_pos, float *d_logits,
+                         uint32_t *d_next, void *stream);
+/* The same step with host values: one host->device copy of (token, pos), the
+ * step replayed from a CUDA graph (captured on the second call), one
+ * device->host copy of the greedy token (and of the logits when logits !=
+ * NULL), then a wait for completion. */
+int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *logits, uint32_t *next);
+/* Copy one cache row (layer, pos) of keys and values (n_kv*hd f32 each) to the
+ * host -- the read-back that keeps a host copy authoritative (mlaReadCache,
+ * backend.zig:191). */
+int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k, float *v);
+int loom_cuda_model_free(uint64_t handle);
+
 /* A decode step (one token) through a whole stack of MoE layers as ONE
  * persistent cooperative kernel: x_{l+1} = x_l + MoE_l(x_l) for every layer,
  * the phases of each layer separated by grid barriers instead of kernel

@@ -44,6 +44,21 @@ class MoeDesc(C.Structure):  # loom_moe_desc
                 ("next_router", C.c_uint64), ("n_group", C.c_size_t), ("topk_group", C.c_size_t)]
 
 
+class ModelLayer(C.Structure):  # loom_model_layer
+    _fields_ = [("attn_norm", C.c_uint64), ("wq", C.c_uint64), ("wk", C.c_uint64), ("wv", C.c_uint64),
+                ("wo", C.c_uint64), ("q_norm", C.c_uint64), ("k_norm", C.c_uint64), ("ffn_norm", C.c_uint64),
+                ("ffn_gate", C.c_uint64), ("ffn_up", C.c_uint64), ("ffn_down", C.c_uint64), ("ffn", C.c_size_t),
+                ("moe", MoeDesc)]
+
+
+class ModelDesc(C.Structure):  # loom_model_desc
+    _fields_ = [("dim", C.c_size_t), ("n_layers", C.c_size_t), ("n_heads", C.c_size_t), ("n_kv_heads", C.c_size_t),
+                ("head_dim", C.c_size_t), ("rope_dim", C.c_size_t), ("vocab", C.c_size_t), ("ctx_len", C.c_size_t),
+                ("eps", C.c_float), ("rope_base", C.c_float), ("attn_logit_mul", C.c_float), ("rope_neox", C.c_int),
+                ("token_embd", C.c_uint64), ("output_norm", C.c_uint64), ("output", C.c_uint64),
+                ("layers", C.POINTER(ModelLayer))]
+
+
 def header_symbols() -> list[str]:
     """Every function the public header declares."""
     src = open(HEADER).read()
@@ -114,6 +129,11 @@ def lib() -> C.CDLL:
         "loom_cuda_trace_reset": (i, []),
         "loom_cuda_trace_read": (sz, [vp, sz]),
         "loom_cuda_stream": (vp, []),
+        "loom_cuda_model_create": (i, [C.POINTER(ModelDesc), C.POINTER(u64)]),
+        "loom_cuda_model_step": (i, [u64, vp, vp, vp, vp, vp]),
+        "loom_cuda_model_decode": (i, [u64, C.c_uint32, sz, vp, C.POINTER(C.c_uint32)]),
+        "loom_cuda_model_read_kv": (i, [u64, sz, sz, vp, vp]),
+        "loom_cuda_model_free": (i, [u64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -1,0 +1,45 @@
+// attn.cuh -- the attention half of a decoder layer on the device (attn.cu):
+// RMSNorm with the activation quantization fused in, per-head Q/K norm + RoPE
+// + KV-cache append, and softmax attention over an f32 cache.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "decode.cuh"
+
+namespace loom {
+
+// x (+)= add (when add != null, written back to x); normed = rmsnorm(x) * w
+// (tensor.zig:9-15); then normed quantized per 256 (q256.q != null, dim a
+// multiple of 256) and/or per 32 (q32.q != null) for the matvecs that read it.
+// The sum of squares is the reference's serial sum for dim <= RN_SERIAL_MAX,
+// a tree sum above.
+constexpr int RN_SERIAL_MAX = 1024;
+void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float eps, float *normed, XQW q256,
+                      XQW q32, cudaStream_t st);
+
+// Per head: optional RMSNorm over head_dim (headNorm, llama.zig:938-950, serial
+// sum), then RoPE at position *pos (ropeNeox / ropeNorm, llama.zig:830-858)
+// with the (cos, sin) of pair j at rope[(pos * rope_dim / 2 + j) * 2], in
+// place on q [n_heads][hd] and k [n_kv][hd]; k and v are stored at row *pos of
+// this layer's caches kc / vc ([ctx][n_kv*hd]). Nothing is written when
+// *pos >= ctx.
+void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const float *kn, int n_heads, int n_kv,
+                    int hd, int rope_dim, int neox, const float *rope, float eps, const uint32_t *pos, int ctx,
+                    float *kc, float *vc, cudaStream_t st);
+
+// Softmax attention of every query head over cache rows 0..*pos
+// (llama.zig:1171-1191), out [n_heads][hd].
+// Ordered form (ctx <= ATT_ORDERED_MAX): one CTA per query head keeps the
+// reference's order of operations (dotF32 scores times the scale, serial
+// softmax sum and 1/sum, axpy over positions in order).
+// Split form: the rows are split in chunks of ATT_CH across CTAs (one CTA
+// per KV head and chunk, all its query heads against one read of each row),
+// each with a running maximum and sum; a merge kernel combines the chunks.
+// `part` holds attn_part_floats(...) floats (split form only).
+constexpr int ATT_CH = 64;
+constexpr int ATT_ORDERED_MAX = 512;
+size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx);
+void launch_attention(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, float scale,
+                      const uint32_t *pos, int ctx, float *part, float *out, cudaStream_t st);
+
+}  // namespace loom

@@ -301,108 +301,126 @@ void launch_unpack(int type, const WDev &w, uint8_t *raw, uint64_t nblk, cudaStr
 
 // ---- dequant (bit-exact with dequantRow, ggml.zig:1739-1857) -----------------------
 
-__global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
-    const int be = block_elems(w.type);
-    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < nelem; e += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t gb = gb0 + e / be;
-        const int i = (int)(e % be);
-        float v = 0.0f;
-        switch (w.type) {
-            case T_F32:
-                v = reinterpret_cast<const float *>(w.q)[gb];
-                break;
-            case T_Q4_K: {  // dequantBlockQ4K :1342: (d*sc)*q - (dmin*m)
-                const uint8_t *blk = w.q + gb * 144;
-                const float d = f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
-                const float dmin = f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
-                const int j = i / 64, l = i % 64;
-                const int sb = 2 * j + (l >= 32);
-                const uint8_t byte = blk[16 + 32 * j + (l & 31)];
-                const int q = l < 32 ? (byte & 0x0F) : (byte >> 4);
-                int sc, mn;
-                scale_min_k4(sb, blk + 4, sc, mn);
-                v = fsub(fmul(fmul(d, (float)sc), (float)q), fmul(dmin, (float)mn));
-                break;
+// element i of global block gb (bit-exact with dequantRow)
+__device__ __forceinline__ float dequant_at(const WDev &w, uint64_t gb, int i) {
+    float v = 0.0f;
+    switch (w.type) {
+        case T_F32:
+            v = reinterpret_cast<const float *>(w.q)[gb];
+            break;
+        case T_Q4_K: {  // dequantBlockQ4K :1342: (d*sc)*q - (dmin*m)
+            const uint8_t *blk = w.q + gb * 144;
+            const float d = f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            const float dmin = f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+            const int j = i / 64, l = i % 64;
+            const int sb = 2 * j + (l >= 32);
+            const uint8_t byte = blk[16 + 32 * j + (l & 31)];
+            const int q = l < 32 ? (byte & 0x0F) : (byte >> 4);
+            int sc, mn;
+            scale_min_k4(sb, blk + 4, sc, mn);
+            v = fsub(fmul(fmul(d, (float)sc), (float)q), fmul(dmin, (float)mn));
+            break;
+        }
+        case T_Q6_K: {  // dequantBlockQ6K :1420: (d*sc)*(q-32)
+            const uint8_t *qb = w.q + gb * 192;
+            const int8_t *scs = reinterpret_cast<const int8_t *>(w.sc + gb * 16);
+            const float d = f16_to_f32(w.d[gb]);
+            const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
+            const uint8_t a = qb[64 * n + l], bb = qb[64 * n + 32 + l], h = qb[128 + 32 * n + l];
+            int q;
+            switch (g) {
+                case 0: q = (a & 0x0F) | ((h & 3) << 4); break;
+                case 1: q = (bb & 0x0F) | (((h >> 2) & 3) << 4); break;
+                case 2: q = (a >> 4) | (((h >> 4) & 3) << 4); break;
+                default: q = (bb >> 4) | (((h >> 6) & 3) << 4); break;
             }
-            case T_Q6_K: {  // dequantBlockQ6K :1420: (d*sc)*(q-32)
-                const uint8_t *qb = w.q + gb * 192;
-                const int8_t *scs = reinterpret_cast<const int8_t *>(w.sc + gb * 16);
-                const float d = f16_to_f32(w.d[gb]);
-                const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
-                const uint8_t a = qb[64 * n + l], bb = qb[64 * n + 32 + l], h = qb[128 + 32 * n + l];
-                int q;
-                switch (g) {
-                    case 0: q = (a & 0x0F) | ((h & 3) << 4); break;
-                    case 1: q = (bb & 0x0F) | (((h >> 2) & 3) << 4); break;
-                    case 2: q = (a >> 4) | (((h >> 4) & 3) << 4); break;
-                    default: q = (bb >> 4) | (((h >> 6) & 3) << 4); break;
-                }
-                const float s = fmul(d, (float)scs[8 * n + l / 16 + 2 * g]);
-                v = fmul(s, fsub((float)q, 32.0f));
-                break;
-            }
-            case T_Q5_0: {  // dequantRow :1772: (q - 16) * d
-                const uint8_t byte = w.q[gb * 16 + (i & 15)];
+            const float s = fmul(d, (float)scs[8 * n + l / 16 + 2 * g]);
+            v = fmul(s, fsub((float)q, 32.0f));
+            break;
+        }
+        case T_Q5_0: {  // dequantRow :1772: (q - 16) * d
+            const uint8_t byte = w.q[gb * 16 + (i & 15)];
+            const uint32_t qh = (uint32_t)w.sc[gb * 4] | ((uint32_t)w.sc[gb * 4 + 1] << 8) |
+                                ((uint32_t)w.sc[gb * 4 + 2] << 16) | ((uint32_t)w.sc[gb * 4 + 3] << 24);
+            const int q = (i < 16 ? (byte & 0x0F) : (byte >> 4)) | (int)((qh >> i) & 1) << 4;
+            v = fmul((float)(q - 16), f16_to_f32(w.d[gb]));
+            break;
+        }
+        case T_Q4_1:
+        case T_Q5_1: {  // dequantRow :1795: q*d + m
+            const uint8_t byte = w.q[gb * 16 + (i & 15)];
+            int q = i < 16 ? (byte & 0x0F) : (byte >> 4);
+            if (w.type == T_Q5_1) {
                 const uint32_t qh = (uint32_t)w.sc[gb * 4] | ((uint32_t)w.sc[gb * 4 + 1] << 8) |
                                     ((uint32_t)w.sc[gb * 4 + 2] << 16) | ((uint32_t)w.sc[gb * 4 + 3] << 24);
-                const int q = (i < 16 ? (byte & 0x0F) : (byte >> 4)) | (int)((qh >> i) & 1) << 4;
-                v = fmul((float)(q - 16), f16_to_f32(w.d[gb]));
-                break;
+                q |= (int)((qh >> i) & 1) << 4;  // value i < 16: bit i; value 16 + j: bit 16 + j
             }
-            case T_Q4_1:
-            case T_Q5_1: {  // dequantRow :1795: q*d + m
-                const uint8_t byte = w.q[gb * 16 + (i & 15)];
-                int q = i < 16 ? (byte & 0x0F) : (byte >> 4);
-                if (w.type == T_Q5_1) {
-                    const uint32_t qh = (uint32_t)w.sc[gb * 4] | ((uint32_t)w.sc[gb * 4 + 1] << 8) |
-                                        ((uint32_t)w.sc[gb * 4 + 2] << 16) | ((uint32_t)w.sc[gb * 4 + 3] << 24);
-                    q |= (int)((qh >> i) & 1) << 4;  // value i < 16: bit i; value 16 + j: bit 16 + j
-                }
-                v = fadd(fmul((float)q, f16_to_f32(w.d[2 * gb])), f16_to_f32(w.d[2 * gb + 1]));
-                break;
-            }
-            case T_Q5_K: {  // dequantBlockQ5K :1376: (d*sc)*(q + 16 h) - (dmin*m)
-                const uint8_t *blk = w.q + gb * 176;
-                const float d = f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
-                const float dmin = f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
-                const int j = i / 64, l = i % 64, sb = 2 * j + (l >= 32);
-                const uint8_t byte = blk[48 + 32 * j + (l & 31)];
-                const int q = l < 32 ? (byte & 0x0F) : (byte >> 4);
-                const bool hb = (blk[16 + (l & 31)] >> sb) & 1;
-                int sc, mn;
-                scale_min_k4(sb, blk + 4, sc, mn);
-                v = fsub(fmul(fmul(d, (float)sc), fadd((float)q, hb ? 16.0f : 0.0f)), fmul(dmin, (float)mn));
-                break;
-            }
-            case T_Q2_K: {  // dequantBlockQ2K :1476: (d*sc)*q - (dmin*m), sub-block j = i / 16
-                const uint8_t *qb = w.q + gb * 80;
-                const float d = f16_to_f32(w.d[2 * gb]), dmin = f16_to_f32(w.d[2 * gb + 1]);
-                const int g = i / 32, l = i % 32, j = i / 16;
-                const uint8_t sc = qb[j];
-                const int q = (qb[16 + 32 * (g / 4) + l] >> (2 * (g % 4))) & 3;
-                v = fsub(fmul(fmul(d, (float)(sc & 0xF)), (float)q), fmul(dmin, (float)(sc >> 4)));
-                break;
-            }
-            case T_Q3_K: {  // dequantBlockQ3K :1508: (d*(sc-32))*(q - 4 [high bit clear])
-                const uint8_t *qb = w.q + gb * 96;
-                const int g = i / 32, l = i % 32, j = i / 16;
-                const int q2 = (qb[32 + 32 * (g / 4) + l] >> (2 * (g % 4))) & 3;
-                const int off = (qb[l] >> g) & 1 ? 0 : 4;
-                v = fmul(fmul(f16_to_f32(w.d[gb]), (float)(q3k_scale(w.sc + gb * 16, j) - 32)), (float)(q2 - off));
-                break;
-            }
-            case T_Q4_0: {
-                const uint8_t byte = w.q[gb * 16 + (i & 15)];
-                const int q = i < 16 ? (byte & 0x0F) : (byte >> 4);
-                v = fmul((float)(q - 8), f16_to_f32(w.d[gb]));
-                break;
-            }
-            case T_Q8_0:
-                v = fmul((float)(int8_t)w.q[gb * 32 + i], f16_to_f32(w.d[gb]));
-                break;
+            v = fadd(fmul((float)q, f16_to_f32(w.d[2 * gb])), f16_to_f32(w.d[2 * gb + 1]));
+            break;
         }
-        out[e] = v;
+        case T_Q5_K: {  // dequantBlockQ5K :1376: (d*sc)*(q + 16 h) - (dmin*m)
+            const uint8_t *blk = w.q + gb * 176;
+            const float d = f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            const float dmin = f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+            const int j = i / 64, l = i % 64, sb = 2 * j + (l >= 32);
+            const uint8_t byte = blk[48 + 32 * j + (l & 31)];
+            const int q = l < 32 ? (byte & 0x0F) : (byte >> 4);
+            const bool hb = (blk[16 + (l & 31)] >> sb) & 1;
+            int sc, mn;
+            scale_min_k4(sb, blk + 4, sc, mn);
+            v = fsub(fmul(fmul(d, (float)sc), fadd((float)q, hb ? 16.0f : 0.0f)), fmul(dmin, (float)mn));
+            break;
+        }
+        case T_Q2_K: {  // dequantBlockQ2K :1476: (d*sc)*q - (dmin*m), sub-block j = i / 16
+            const uint8_t *qb = w.q + gb * 80;
+            const float d = f16_to_f32(w.d[2 * gb]), dmin = f16_to_f32(w.d[2 * gb + 1]);
+            const int g = i / 32, l = i % 32, j = i / 16;
+            const uint8_t sc = qb[j];
+            const int q = (qb[16 + 32 * (g / 4) + l] >> (2 * (g % 4))) & 3;
+            v = fsub(fmul(fmul(d, (float)(sc & 0xF)), (float)q), fmul(dmin, (float)(sc >> 4)));
+            break;
+        }
+        case T_Q3_K: {  // dequantBlockQ3K :1508: (d*(sc-32))*(q - 4 [high bit clear])
+            const uint8_t *qb = w.q + gb * 96;
+            const int g = i / 32, l = i % 32, j = i / 16;
+            const int q2 = (qb[32 + 32 * (g / 4) + l] >> (2 * (g % 4))) & 3;
+            const int off = (qb[l] >> g) & 1 ? 0 : 4;
+            v = fmul(fmul(f16_to_f32(w.d[gb]), (float)(q3k_scale(w.sc + gb * 16, j) - 32)), (float)(q2 - off));
+            break;
+        }
+        case T_Q4_0: {
+            const uint8_t byte = w.q[gb * 16 + (i & 15)];
+            const int q = i < 16 ? (byte & 0x0F) : (byte >> 4);
+            v = fmul((float)(q - 8), f16_to_f32(w.d[gb]));
+            break;
+        }
+        case T_Q8_0:
+            v = fmul((float)(int8_t)w.q[gb * 32 + i], f16_to_f32(w.d[gb]));
+            break;
     }
+    return v;
+}
+
+__global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
+    const int be = block_elems(w.type);
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < nelem; e += (uint64_t)gridDim.x * blockDim.x)
+        out[e] = dequant_at(w, gb0 + e / be, (int)(e % be));
+}
+
+// Embedding lookup (llama.zig:1122 dequantRow of token_embd) of the token held
+// in device memory; an id >= vocab reads row vocab - 1 (the caller's contract
+// is id < vocab; this only keeps the read inside the tensor).
+__global__ void k_embed(WDev w, int dim, const uint32_t *tok, int vocab, float *x) {
+    const uint32_t t = min(*tok, (uint32_t)(vocab - 1));
+    const int be = block_elems(w.type);
+    const uint64_t gb0 = (uint64_t)t * (dim / be);
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x)
+        x[e] = dequant_at(w, gb0 + e / be, e % be);
+}
+
+void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st) {
+    k_embed<<<cdiv(dim, 256), 256, 0, st>>>(w, dim, tok, vocab, x);
+    count_launch();
 }
 
 void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cudaStream_t st) {

@@ -42,6 +42,8 @@ void launch_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, uint64_t
 void launch_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, uint16_t *d, uint64_t nblk, cudaStream_t st);
 void launch_unpack(int type, const WDev &w, uint8_t *raw, uint64_t nblk, cudaStream_t st);
 void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cudaStream_t st);
+// row *tok of a [vocab][dim] tensor into x (embedding lookup)
+void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st);
 void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d,
                       int32_t *s, int dstride, int sstride, cudaStream_t st);
 void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x, int ntok, float *out,

@@ -1,0 +1,426 @@
+// model.cu -- whole-model decode on the device (include/loom_cuda.h,
+// loom_cuda_model_*): the reference's token step (src/gguf/llama.zig:1111-1228)
+// with the residual stream, the KV cache and every layer resident in HBM.
+//
+// Per layer (llama.zig:1138-1225):
+//   k_rmsnorm_q        attention RMSNorm + quantization of the normed vector
+//   k_mm x3            q, k, v matvecs (bit-exact with ggml.matvec)
+//   k_qk_rope          headNorm + RoPE, k/v appended to the cache at pos
+//   k_attn_*           softmax attention over rows 0..pos
+//   k_quant_act, k_mm  output projection
+//   k_rmsnorm_q        residual add + FFN RMSNorm
+//   MoE layer          loom_cuda_moe_forward (routed, or a dense FFN run as one
+//                      expert of weight 1.0, which adds exactly y: 0 + 1*y = y),
+//                      residual included
+// then the final RMSNorm, the output head and the argmax.
+// The step reads token and position from device memory, so one CUDA graph
+// replays every step; loom_cuda_model_decode wraps it with one host->device
+// and one device->host copy.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/loom_cuda.h"
+#include "attn.cuh"
+#include "kernels.cuh"
+
+namespace loom {
+bool rt_tensor(uint64_t h, WDev *w, int *type, uint64_t *nblk);
+cudaStream_t rt_stream(void *s);
+int rt_need_init();
+int rt_decline(const char *why);
+int rt_fail(const char *what, cudaError_t e);
+uint64_t rt_buf_gen();
+cudaError_t rt_wait();
+}  // namespace loom
+
+using namespace loom;
+
+namespace {
+
+#define MCK(call)                                         \
+    do {                                                  \
+        cudaError_t e_ = (call);                          \
+        if (e_ != cudaSuccess) return rt_fail(#call, e_); \
+    } while (0)
+
+struct Mat {
+    WDev w{};
+    int type = 0;
+    int rows = 0, cols = 0;
+};
+
+struct LayerRt {
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *qn = nullptr, *kn = nullptr;
+    Mat wq, wk, wv, wo;
+    loom_moe_desc moe{};
+    bool dense = false;
+};
+
+struct Model {
+    size_t dim = 0, n_layers = 0, nh = 0, nkv = 0, hd = 0, rope_dim = 0, vocab = 0, ctx = 0;
+    float eps = 0, scale = 0;
+    int neox = 0;
+    Mat embd, out;
+    const float *out_norm = nullptr;
+    std::vector<LayerRt> L;
+    bool need256 = false, need32 = false;  // kinds the normed vector is quantized to
+    bool att256 = false, att32 = false;    // kinds of the attention output
+    std::vector<void *> allocs;
+    float *kc = nullptr, *vc = nullptr, *rope = nullptr;
+    float *x[2] = {nullptr, nullptr}, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+          *proj = nullptr, *part = nullptr, *logits = nullptr, *zero_logit = nullptr;
+    XQW n256{}, n32{}, a256{}, a32{};
+    uint32_t *io_dev = nullptr;   // token, pos, next (graph path)
+    uint32_t *io_host = nullptr;  // pinned mirror
+    float *h_logits = nullptr;    // pinned
+    cudaGraphExec_t exec = nullptr;
+    uint64_t exec_gen = 0;
+    int calls = 0;
+};
+
+std::unordered_map<uint64_t, Model *> g_models;
+uint64_t g_next_model = 1;
+
+template <class T> int dalloc(Model &m, T *&p, size_t n, bool zero = false) {
+    void *v = nullptr;
+    const size_t bytes = std::max<size_t>(n * sizeof(T), 256);
+    MCK(cudaMalloc(&v, bytes));
+    m.allocs.push_back(v);
+    if (zero) MCK(cudaMemset(v, 0, bytes));
+    p = static_cast<T *>(v);
+    return 0;
+}
+
+void free_model(Model *m) {
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->io_host) cudaFreeHost(m->io_host);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    delete m;
+}
+
+bool mm_type_ok(int t) {
+    return t == T_F32 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_1 || t == T_Q8_0 || is_kquant(t);
+}
+
+// A [rows][cols] matrix view of a tensor; false when the tensor is unknown, of
+// an unsupported type or too small.
+bool mat(loom_tensor h, size_t rows, size_t cols, Mat &m) {
+    uint64_t nblk = 0;
+    if (!rt_tensor(h, &m.w, &m.type, &nblk)) return false;
+    if (!mm_type_ok(m.type)) return false;
+    const size_t be = block_elems(m.type);
+    if (cols % be || nblk < rows * (cols / be)) return false;
+    m.rows = (int)rows;
+    m.cols = (int)cols;
+    return true;
+}
+
+const float *f32_vec(loom_tensor h, size_t n, bool &ok) {
+    WDev w;
+    int type = 0;
+    uint64_t nblk = 0;
+    if (!rt_tensor(h, &w, &type, &nblk) || type != T_F32 || nblk < n) {
+        ok = false;
+        return nullptr;
+    }
+    return reinterpret_cast<const float *>(w.q);
+}
+
+// the activation kinds a matvec of type t reads
+void need_kind(int t, bool &k256, bool &k32) {
+    if (t == T_F32 || t == T_Q5_0) return;  // f32 activations
+    if (act256(t))
+        k256 = true;
+    else
+        k32 = true;
+}
+
+void matvec(const Mat &m, const float *xf, const XQW &x256, const XQW &x32, float *out, cudaStream_t st) {
+    if (m.type == T_F32) {
+        launch_mm_f32(reinterpret_cast<const float *>(m.w.q), m.rows, m.cols, xf, 1, out, st);
+    } else if (m.type == T_Q5_0) {
+        launch_mm_q50(m.w, 0, m.rows, m.cols, xf, 1, out, st);
+    } else if (act256(m.type)) {
+        XQ x{x256.q, x256.d, x256.s, m.cols, m.cols / 256, m.cols / 16, 1};
+        launch_mm(m.w, 0, m.rows, m.cols, x, 1, out, st);
+    } else {
+        XQ x{x32.q, x32.d, x32.s, m.cols, m.cols / 32, m.cols / 32, 0};
+        launch_mm(m.w, 0, m.rows, m.cols, x, 1, out, st);
+    }
+}
+
+int alloc_xq(Model &m, XQW &q, size_t cols, bool k256) {
+    if (int rc = dalloc(m, q.q, cols)) return rc;
+    if (int rc = dalloc(m, q.d, cols / (k256 ? 256 : 32) + 1)) return rc;
+    return dalloc(m, q.s, cols / (k256 ? 16 : 32) + 1);
+}
+
+// The step on device memory: token id at tok[0], position at pos[0].
+int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, uint32_t *next, cudaStream_t st) {
+    const int dim = (int)m.dim, nh = (int)m.nh, nkv = (int)m.nkv, hd = (int)m.hd, qd = nh * hd;
+    const size_t layer_stride = m.ctx * m.nkv * m.hd;
+    const XQW none{};
+    launch_embed(m.embd.w, dim, tok, (int)m.vocab, m.x[0], st);
+    int cur = 0;
+    for (size_t li = 0; li < m.n_layers; li++) {
+        const LayerRt &l = m.L[li];
+        float *x = m.x[cur];
+        launch_rmsnorm_q(x, nullptr, l.attn_norm, dim, m.eps, m.normed, m.need256 ? m.n256 : none,
+                         m.need32 ? m.n32 : none, st);
+        matvec(l.wq, m.normed, m.n256, m.n32, m.q, st);
+        matvec(l.wk, m.normed, m.n256, m.n32, m.k, st);
+        matvec(l.wv, m.normed, m.n256, m.n32, m.v, st);
+        float *kc = m.kc + li * layer_stride, *vc = m.vc + li * layer_stride;
+        launch_qk_rope(m.q, m.k, m.v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps, pos,
+                       (int)m.ctx, kc, vc, st);
+        launch_attention(m.q, kc, vc, nh, nkv, hd, m.scale, pos, (int)m.ctx, m.part, m.att, st);
+        if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
+            const bool k256 = act256(l.wo.type);
+            const XQW &a = k256 ? m.a256 : m.a32;
+            launch_quant_act(m.att, 1, qd, qd, k256, a.q, a.d, a.s, k256 ? qd / 256 : qd / 32,
+                             k256 ? qd / 16 : qd / 32, st);
+        }
+        matvec(l.wo, m.att, m.a256, m.a32, m.proj, st);
+        // x += proj (llama.zig:1195), then the FFN norm; the MoE layer quantizes normed itself
+        launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, none, none, st);
+        float *xn = m.x[cur ^ 1];
+        if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr, st))
+            return rc;
+        cur ^= 1;
+    }
+    XQW o256 = none, o32 = none;
+    if (m.out.type != T_F32 && m.out.type != T_Q5_0) {
+        if (act256(m.out.type))
+            o256 = m.n256;
+        else
+            o32 = m.n32;
+    }
+    launch_rmsnorm_q(m.x[cur], nullptr, m.out_norm, dim, m.eps, m.normed, o256, o32, st);
+    float *lg = logits ? logits : m.logits;
+    matvec(m.out, m.normed, m.n256, m.n32, lg, st);
+    if (next) {
+        if (int rc = loom_cuda_argmax(lg, m.vocab, next, st)) return rc;
+    }
+    MCK(cudaGetLastError());
+    return LOOM_CUDA_OK;
+}
+
+Model *find(uint64_t h) {
+    auto it = g_models.find(h);
+    return it == g_models.end() ? nullptr : it->second;
+}
+
+// (cos, sin) of every rotation pair j at every position, in the reference's
+// theta progression (llama.zig:821-826 ropeTheta with index 2j: exponent =
+// 2j / rope_dim, freq = base^-exponent, angle = pos * freq), in f32.
+std::vector<float> rope_table(size_t ctx, size_t rope_dim, float base) {
+    const size_t half = rope_dim / 2;
+    std::vector<float> t(ctx * half * 2);
+    for (size_t j = 0; j < half; j++) {
+        const float exponent = (float)(2 * j) / (float)rope_dim;
+        const float freq = std::pow(base, -exponent);
+        for (size_t p = 0; p < ctx; p++) {
+            const float angle = (float)p * freq;
+            t[(p * half + j) * 2] = std::cos(angle);
+            t[(p * half + j) * 2 + 1] = std::sin(angle);
+        }
+    }
+    return t;
+}
+
+}  // namespace
+
+extern "C" {
+
+int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
+    if (int rc = rt_need_init()) return rc;
+    if (!d || !handle || !d->layers) return rt_decline("no model description");
+    if (d->dim == 0 || d->n_layers == 0 || d->n_heads == 0 || d->n_kv_heads == 0 || d->vocab == 0 || d->ctx_len == 0)
+        return rt_decline("empty model shape");
+    if (d->n_heads % d->n_kv_heads || d->n_heads / d->n_kv_heads > 16)
+        return rt_decline("n_heads must be a multiple of n_kv_heads, at most 16 query heads per KV head");
+    if (d->head_dim == 0 || d->head_dim % 2 || d->head_dim > 256) return rt_decline("head_dim must be even and <= 256");
+    if (d->rope_dim > d->head_dim || d->rope_dim % 2) return rt_decline("rope_dim must be even and <= head_dim");
+    if (d->dim > 16384 || d->ctx_len > (1u << 20) || d->vocab > 0x7FFFFFFFu) return rt_decline("model shape too large");
+    Model *m = new Model();
+    auto bail = [&](int rc) {
+        free_model(m);
+        return rc;
+    };
+    m->dim = d->dim;
+    m->n_layers = d->n_layers;
+    m->nh = d->n_heads;
+    m->nkv = d->n_kv_heads;
+    m->hd = d->head_dim;
+    m->rope_dim = d->rope_dim;
+    m->vocab = d->vocab;
+    m->ctx = d->ctx_len;
+    m->eps = d->eps;
+    m->neox = d->rope_neox;
+    m->scale = d->attn_logit_mul / std::sqrt((float)d->head_dim);  // llama.zig:1116
+    const size_t dim = d->dim, qd = d->n_heads * d->head_dim, kvd = d->n_kv_heads * d->head_dim;
+    if (!mat(d->token_embd, d->vocab, dim, m->embd)) return bail(rt_decline("token_embd: unknown tensor or wrong size"));
+    if (!mat(d->output, d->vocab, dim, m->out)) return bail(rt_decline("output: unknown tensor or wrong size"));
+    bool ok = true;
+    m->out_norm = f32_vec(d->output_norm, dim, ok);
+    if (!ok) return bail(rt_decline("output_norm must be f32 [dim]"));
+    size_t max_ffn = 0, max_ne = 1, max_nu = 1;
+    for (size_t li = 0; li < d->n_layers; li++) {
+        const loom_model_layer &s = d->layers[li];
+        LayerRt l;
+        l.attn_norm = f32_vec(s.attn_norm, dim, ok);
+        l.ffn_norm = f32_vec(s.ffn_norm, dim, ok);
+        if (s.q_norm) l.qn = f32_vec(s.q_norm, d->head_dim, ok);
+        if (s.k_norm) l.kn = f32_vec(s.k_norm, d->head_dim, ok);
+        if (!ok) return bail(rt_decline("layer norms must be f32 [dim] / [head_dim]"));
+        if (!mat(s.wq, qd, dim, l.wq) || !mat(s.wk, kvd, dim, l.wk) || !mat(s.wv, kvd, dim, l.wv) ||
+            !mat(s.wo, dim, qd, l.wo))
+            return bail(rt_decline("attention weights: unknown tensor, unsupported type or wrong size"));
+        if (s.moe.n_expert) {
+            l.moe = s.moe;
+            if (l.moe.dim != dim) return bail(rt_decline("MoE layer dim differs from the model's"));
+            max_ffn = std::max(max_ffn, std::max(l.moe.ffn, l.moe.shexp_ffn));
+            max_ne = std::max(max_ne, l.moe.n_expert);
+            max_nu = std::max(max_nu, l.moe.n_used);
+        } else {
+            if (!s.ffn_gate || !s.ffn_up || !s.ffn_down || !s.ffn) return bail(rt_decline("dense FFN tensors missing"));
+            l.dense = true;
+            loom_moe_desc &e = l.moe;
+            e.dim = dim;
+            e.ffn = s.ffn;
+            e.n_expert = 1;
+            e.n_used = 1;
+            e.gating = 1;
+            e.weights_norm = 1;
+            e.weights_scale = 1.0f;
+            e.gate = s.ffn_gate;
+            e.up = s.ffn_up;
+            e.down = s.ffn_down;
+            max_ffn = std::max(max_ffn, s.ffn);
+        }
+        need_kind(l.wq.type, m->need256, m->need32);
+        need_kind(l.wk.type, m->need256, m->need32);
+        need_kind(l.wv.type, m->need256, m->need32);
+        need_kind(l.wo.type, m->att256, m->att32);
+        m->L.push_back(l);
+    }
+    need_kind(m->out.type, m->need256, m->need32);
+    if ((m->need256 && dim % 256) || (m->att256 && qd % 256))
+        return bail(rt_decline("a K-quant projection needs a width that is a multiple of 256"));
+    if ((m->need32 && dim % 32) || (m->att32 && qd % 32)) return bail(rt_decline("width not a multiple of 32"));
+    // the MoE scratch, sized now so the step never allocates (graph capture)
+    if (int rc = loom_cuda_reserve(1, dim, max_ffn, max_ne, max_nu)) return bail(rc);
+    int rc = 0;
+    const size_t cache = d->n_layers * d->ctx_len * kvd;
+    if ((rc = dalloc(*m, m->kc, cache, true)) || (rc = dalloc(*m, m->vc, cache, true)) ||
+        (rc = dalloc(*m, m->rope, d->ctx_len * d->rope_dim)) || (rc = dalloc(*m, m->x[0], dim)) ||
+        (rc = dalloc(*m, m->x[1], dim)) || (rc = dalloc(*m, m->normed, dim)) || (rc = dalloc(*m, m->q, qd)) ||
+        (rc = dalloc(*m, m->k, kvd)) || (rc = dalloc(*m, m->v, kvd)) || (rc = dalloc(*m, m->att, qd)) ||
+        (rc = dalloc(*m, m->proj, dim)) ||
+        (rc = dalloc(*m, m->part, attn_part_floats((int)m->nh, (int)m->nkv, (int)m->hd, (int)m->ctx))) ||
+        (rc = dalloc(*m, m->logits, d->vocab)) || (rc = dalloc(*m, m->zero_logit, 1, true)) ||
+        (rc = dalloc(*m, m->io_dev, 4, true)) || (rc = alloc_xq(*m, m->n256, dim, true)) ||
+        (rc = alloc_xq(*m, m->n32, dim, false)) || (rc = alloc_xq(*m, m->a256, qd, true)) ||
+        (rc = alloc_xq(*m, m->a32, qd, false)))
+        return bail(rc);
+    if (d->rope_dim) {
+        const std::vector<float> tab = rope_table(d->ctx_len, d->rope_dim, d->rope_base);
+        cudaError_t e = cudaMemcpy(m->rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(rt_fail("rope table upload", e));
+    }
+    cudaError_t e = cudaHostAlloc(&m->io_host, 16, cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaHostAlloc(&m->h_logits, d->vocab * 4, cudaHostAllocDefault);
+    if (e != cudaSuccess) return bail(rt_fail("cudaHostAlloc(model staging)", e));
+    const uint64_t h = g_next_model++;
+    g_models[h] = m;
+    *handle = h;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_model_step(uint64_t handle, const uint32_t *d_token, const uint32_t *d_pos, float *d_logits,
+                         uint32_t *d_next, void *stream) {
+    if (int rc = rt_need_init()) return rc;
+    Model *m = find(handle);
+    if (!m) return rt_decline("unknown model handle");
+    if (!d_token || !d_pos) return rt_decline("token and position pointers are required");
+    return run_step(*m, d_token, d_pos, d_logits, d_next, rt_stream(stream));
+}
+
+int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *logits, uint32_t *next) {
+    if (int rc = rt_need_init()) return rc;
+    Model *m = find(handle);
+    if (!m) return rt_decline("unknown model handle");
+    if (token >= m->vocab) return rt_decline("token id out of range (llama.zig:1121)");
+    if (pos >= m->ctx) return rt_decline("position beyond the context length");
+    cudaStream_t st = rt_stream(nullptr);
+    m->io_host[0] = token;
+    m->io_host[1] = (uint32_t)pos;
+    // one H2D copy of (token, pos), the step, one D2H copy of the token
+    auto record = [&]() -> int {
+        MCK(cudaMemcpyAsync(m->io_dev, m->io_host, 8, cudaMemcpyHostToDevice, st));
+        if (int rc = run_step(*m, m->io_dev, m->io_dev + 1, m->logits, m->io_dev + 2, st)) return rc;
+        MCK(cudaMemcpyAsync(m->io_host + 2, m->io_dev + 2, 4, cudaMemcpyDeviceToHost, st));
+        return 0;
+    };
+    if (m->exec && m->exec_gen != rt_buf_gen()) {  // a scratch buffer the graph points at has moved
+        cudaGraphExecDestroy(m->exec);
+        m->exec = nullptr;
+    }
+    if (!m->exec && m->calls++ > 0) {  // the first call runs eagerly (sizes every buffer); then capture
+        const uint64_t gen = rt_buf_gen();
+        MCK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+        const int rc = record();
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(st, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return rt_fail("cudaStreamEndCapture(model)", e);
+        e = cudaGraphInstantiate(&m->exec, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+            m->exec = nullptr;
+            return rt_fail("cudaGraphInstantiate(model)", e);
+        }
+        m->exec_gen = gen;
+    }
+    if (m->exec) {
+        MCK(cudaGraphLaunch(m->exec, st));
+    } else if (int rc = record()) {
+        return rc;
+    }
+    if (logits) MCK(cudaMemcpyAsync(m->h_logits, m->logits, m->vocab * 4, cudaMemcpyDeviceToHost, st));
+    MCK(rt_wait());
+    if (next) *next = m->io_host[2];
+    if (logits) std::memcpy(logits, m->h_logits, m->vocab * 4);
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k, float *v) {
+    if (int rc = rt_need_init()) return rc;
+    Model *m = find(handle);
+    if (!m) return rt_decline("unknown model handle");
+    if (layer >= m->n_layers || pos >= m->ctx) return rt_decline("cache row out of range");
+    const size_t kvd = m->nkv * m->hd, off = (layer * m->ctx + pos) * kvd;
+    MCK(cudaStreamSynchronize(rt_stream(nullptr)));
+    if (k) MCK(cudaMemcpy(k, m->kc + off, kvd * 4, cudaMemcpyDeviceToHost));
+    if (v) MCK(cudaMemcpy(v, m->vc + off, kvd * 4, cudaMemcpyDeviceToHost));
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_model_free(uint64_t handle) {
+    Model *m = find(handle);
+    if (!m) return LOOM_CUDA_DECLINED;
+    cudaDeviceSynchronize();
+    g_models.erase(handle);
+    free_model(m);
+    return LOOM_CUDA_OK;
+}
+
+}  // extern "C"

@@ -584,6 +584,24 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
 
 }  // namespace
 
+// Internal hooks for the other host files of the library (model.cu).
+namespace loom {
+bool rt_tensor(uint64_t h, WDev *w, int *type, uint64_t *nblk) {
+    Tensor *t = lookup(h);
+    if (!t) return false;
+    *w = t->w;
+    *type = t->type;
+    *nblk = t->nblk;
+    return true;
+}
+cudaStream_t rt_stream(void *s) { return s ? static_cast<cudaStream_t>(s) : g_stream; }
+int rt_need_init() { return need_init(); }
+int rt_decline(const char *why) { return decline(why); }
+int rt_fail(const char *what, cudaError_t e) { return fail(what, e); }
+uint64_t rt_buf_gen() { return g_buf_gen; }
+cudaError_t rt_wait() { return seam_wait(); }  // completion of the backend's stream, polled
+}  // namespace loom
+
 extern "C" {
 
 int loom_cuda_init(int device) {
