@@ -239,6 +239,11 @@ typedef struct {
     size_t dim, n_layers, n_heads, n_kv_heads, head_dim, rope_dim, vocab, ctx_len;
     float eps, rope_base, attn_logit_mul; /* scores = q.k * attn_logit_mul / sqrt(head_dim) */
     int rope_neox;                        /* 1 ropeNeox (qwen3moe, qwen2moe), 0 ropeNorm (llama) */
+    /* 1: keep the reference's summation order at every width -- RMSNorm's
+     * serial sum of squares (a few microseconds per norm at dim 2048) and the
+     * ordered attention at any context; 0: tree sums for RMSNorm wider than
+     * 1024 and split attention beyond 512 positions (faster, within rounding) */
+    int exact_order;
     loom_tensor token_embd;               /* [vocab][dim], any supported type */
     loom_tensor output_norm;              /* f32 [dim] */
     loom_tensor output;                   /* [vocab][dim] */
@@ -247,10 +252,11 @@ typedef struct {
 /* Build the model: checks every tensor's type and size, allocates the KV
  * cache (2 x n_layers x ctx_len x n_kv*hd f32), the RoPE table and the step's
  * buffers. Limits: head_dim even and <= 256, rope_dim <= head_dim, n_heads a
- * multiple of n_kv_heads with at most 16 query heads per KV head. Contexts up
- * to 512 positions use the attention kernel that keeps the reference's exact
- * operation order (dotF32 scores, serial softmax sum, axpy in position order);
- * longer contexts split the positions across CTAs and merge. */
+ * multiple of n_kv_heads with at most 16 query heads per KV head, ctx_len up
+ * to 32768 with exact_order. Contexts up to 512 positions (any, with
+ * exact_order) use the attention kernel that keeps the reference's operation
+ * order (dotF32 scores, serial softmax sum, axpy in position order); longer
+ * contexts split the positions across CTAs and merge. */
 int loom_cuda_model_create(const loom_model_desc *desc, uint64_t *handle);
 /* One decode step on device memory (graph-capturable after the first call):
  * d_token / d_pos: device u32 [1] (the token at position pos < ctx_len);

@@ -55,7 +55,7 @@ class ModelDesc(C.Structure):  # loom_model_desc
     _fields_ = [("dim", C.c_size_t), ("n_layers", C.c_size_t), ("n_heads", C.c_size_t), ("n_kv_heads", C.c_size_t),
                 ("head_dim", C.c_size_t), ("rope_dim", C.c_size_t), ("vocab", C.c_size_t), ("ctx_len", C.c_size_t),
                 ("eps", C.c_float), ("rope_base", C.c_float), ("attn_logit_mul", C.c_float), ("rope_neox", C.c_int),
-                ("token_embd", C.c_uint64), ("output_norm", C.c_uint64), ("output", C.c_uint64),
+                ("exact_order", C.c_int), ("token_embd", C.c_uint64), ("output_norm", C.c_uint64), ("output", C.c_uint64),
                 ("layers", C.POINTER(ModelLayer))]
 
 

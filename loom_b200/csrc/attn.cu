@@ -54,11 +54,11 @@ __device__ __forceinline__ float dot_f32_ordered(const float *a, const float *b,
 constexpr int RN_THREADS = 1024;
 
 __global__ void __launch_bounds__(RN_THREADS) k_rmsnorm_q(float *x, const float *add, const float *w, int dim,
-                                                          float eps, float *normed, XQW q256, XQW q32) {
+                                                          float eps, float *normed, XQW q256, XQW q32,
+                                                          int serial) {
     extern __shared__ float sx[];  // [dim]
     __shared__ float red[RN_THREADS / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool serial = dim <= RN_SERIAL_MAX;
     float ss = 0.0f;
     for (int i = tid; i < dim; i += RN_THREADS) {
         float v = x[i];
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
                                                             int n_heads, int n_kv, int hd, float scale,
                                                             const uint32_t *pos_p, int ctx, float *out) {
     __shared__ float qs[MAX_HD];
-    __shared__ float sc[ATT_ORDERED_MAX];
+    extern __shared__ float sc[];  // [ctx]
     __shared__ float inv_s;
     const int h = blockIdx.x, tid = threadIdx.x;
     const int pos = (int)*pos_p;
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
         float m = -INFINITY;
         for (int t = tid; t < seq; t += 32) m = fmaxf(m, sc[t]);
         m = warp_max(m);
-        for (int t = tid; t < seq; t += 32) sc[t] = expf(fsub(sc[t], m));
+        for (int t = tid; t < seq; t += 32) sc[t] = exp_f(fsub(sc[t], m));
         __syncwarp();
         if (tid == 0) {
             float sum = 0.0f;
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_part(const float *q, const 
         m = warp_max(m);
         float l = 0.0f;
         for (int j = lane; j < n; j += 32) {
-            const float e = expf(fsub(sc[hh * ATT_CH + j], m));
+            const float e = exp_f(fsub(sc[hh * ATT_CH + j], m));
             sc[hh * ATT_CH + j] = e;
             l = fadd(l, e);
         }
@@ -298,10 +298,10 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_merge(const float *part, in
     float M = -INFINITY;
     for (int s = 0; s < live; s++) M = fmaxf(M, rec[s * stride + hd]);
     float L = 0.0f;
-    for (int s = 0; s < live; s++) L = fadd(L, fmul(rec[s * stride + hd + 1], expf(fsub(rec[s * stride + hd], M))));
+    for (int s = 0; s < live; s++) L = fadd(L, fmul(rec[s * stride + hd + 1], exp_f(fsub(rec[s * stride + hd], M))));
     for (int d = threadIdx.x; d < hd; d += AT_THREADS) {
         float o = 0.0f;
-        for (int s = 0; s < live; s++) o = fadd(o, fmul(rec[s * stride + d], expf(fsub(rec[s * stride + hd], M))));
+        for (int s = 0; s < live; s++) o = fadd(o, fmul(rec[s * stride + d], exp_f(fsub(rec[s * stride + hd], M))));
         out[(size_t)h * hd + d] = fdiv(o, L);
     }
 }
@@ -311,8 +311,8 @@ unsigned cdiv_u(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 }  // namespace
 
 void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float eps, float *normed, XQW q256,
-                      XQW q32, cudaStream_t st) {
-    k_rmsnorm_q<<<1, RN_THREADS, (size_t)dim * 4, st>>>(x, add, w, dim, eps, normed, q256, q32);
+                      XQW q32, bool serial, cudaStream_t st) {
+    k_rmsnorm_q<<<1, RN_THREADS, (size_t)dim * 4, st>>>(x, add, w, dim, eps, normed, q256, q32, (int)serial);
     count_launch();
 }
 
@@ -330,9 +330,15 @@ size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx) {
 }
 
 void launch_attention(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, float scale,
-                      const uint32_t *pos, int ctx, float *part, float *out, cudaStream_t st) {
-    if (ctx <= ATT_ORDERED_MAX) {
-        k_attn_ordered<<<n_heads, AT_THREADS, 0, st>>>(q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx, out);
+                      const uint32_t *pos, int ctx, float *part, float *out, bool ordered, cudaStream_t st) {
+    if (ordered) {
+        static bool smem_set = false;  // the scores of up to ATT_ORDERED_LIMIT positions
+        if (!smem_set) {
+            cudaFuncSetAttribute(k_attn_ordered, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_ORDERED_LIMIT * 4);
+            smem_set = true;
+        }
+        k_attn_ordered<<<n_heads, AT_THREADS, (size_t)ctx * 4, st>>>(q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx,
+                                                                      out);
         count_launch();
         return;
     }

@@ -11,11 +11,11 @@ namespace loom {
 // x (+)= add (when add != null, written back to x); normed = rmsnorm(x) * w
 // (tensor.zig:9-15); then normed quantized per 256 (q256.q != null, dim a
 // multiple of 256) and/or per 32 (q32.q != null) for the matvecs that read it.
-// The sum of squares is the reference's serial sum for dim <= RN_SERIAL_MAX,
-// a tree sum above.
-constexpr int RN_SERIAL_MAX = 1024;
+// The sum of squares is the reference's serial sum when `serial`, else a
+// tree sum.
+constexpr int RN_SERIAL_MAX = 1024;  // default: serial up to this width
 void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float eps, float *normed, XQW q256,
-                      XQW q32, cudaStream_t st);
+                      XQW q32, bool serial, cudaStream_t st);
 
 // Per head: optional RMSNorm over head_dim (headNorm, llama.zig:938-950, serial
 // sum), then RoPE at position *pos (ropeNeox / ropeNorm, llama.zig:830-858)
@@ -29,7 +29,7 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 
 // Softmax attention of every query head over cache rows 0..*pos
 // (llama.zig:1171-1191), out [n_heads][hd].
-// Ordered form (ctx <= ATT_ORDERED_MAX): one CTA per query head keeps the
+// Ordered form (`ordered`): one CTA per query head keeps the
 // reference's order of operations (dotF32 scores times the scale, serial
 // softmax sum and 1/sum, axpy over positions in order).
 // Split form: the rows are split in chunks of ATT_CH across CTAs (one CTA
@@ -37,9 +37,10 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 // each with a running maximum and sum; a merge kernel combines the chunks.
 // `part` holds attn_part_floats(...) floats (split form only).
 constexpr int ATT_CH = 64;
-constexpr int ATT_ORDERED_MAX = 512;
+constexpr int ATT_ORDERED_MAX = 512;      // default: ordered up to this context
+constexpr int ATT_ORDERED_LIMIT = 32768;  // largest context of the ordered form
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx);
 void launch_attention(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, float scale,
-                      const uint32_t *pos, int ctx, float *part, float *out, cudaStream_t st);
+                      const uint32_t *pos, int ctx, float *part, float *out, bool ordered, cudaStream_t st);
 
 }  // namespace loom

@@ -103,6 +103,14 @@ __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b)
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 
+// e^x in f32 for the softmax, sigmoid and SiLU (tensor.zig:18-35): the double
+// precision exp rounded once to f32. That is the correctly rounded result
+// except within ~2^-29 of a rounding boundary; the reference's f32 exp
+// (within ~0.5 ulp) agrees with it nearly everywhere, CUDA's single-precision
+// expf (within 2 ulp) often does not, and one ulp there can move an int8
+// activation of the next matvec.
+__device__ __forceinline__ float exp_f(float x) { return (float)exp((double)x); }
+
 // ggml.zig:1067-1074 toI8Saturating
 __device__ __forceinline__ int to_i8_sat(float v) {
     if (!isfinite(v)) return 0;

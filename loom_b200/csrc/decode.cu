@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
             const int r = rl + i;
             if (r >= r0 && r < si.ffn) {
                 const float g = acc[i], u = acc[GU_NR + i];
-                act[r] = fmul(fdiv(g, fadd(1.0f, expf(-g))), u);  // silu(g) * u (tensor.zig:30,53)
+                act[r] = fmul(fdiv(g, fadd(1.0f, exp_f(-g))), u);  // silu(g) * u (tensor.zig:30,53)
             }
         }
     }
@@ -921,7 +921,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_grp(DecodeArgs A) {
 #pragma unroll
             for (int k = 0; k < GU_NR; k++) {
                 const int r = rl + k;
-                if (r >= r0 && r < ffn) act[r] = fmul(fdiv(acc[k], fadd(1.0f, expf(-acc[k]))), acc[GU_NR + k]);
+                if (r >= r0 && r < ffn) act[r] = fmul(fdiv(acc[k], fadd(1.0f, exp_f(-acc[k]))), acc[GU_NR + k]);
             }
         }
     }
@@ -1645,7 +1645,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
                 const float u = __shfl_down_sync(0xffffffffu, dotv, NR);  // lane i < NR: up row i
                 if (lane < NR)  // lane i: silu(gate row i) * up row i
                     A.act[(size_t)k * A.act_stride + rl + lane] =
-                        tagged(fmul(fdiv(dotv, fadd(1.0f, expf(-dotv))), u), tag);
+                        tagged(fmul(fdiv(dotv, fadd(1.0f, exp_f(-dotv))), u), tag);
                 if (TRACE && g == 0) cy.mark(14);  // warp 0's activations stored
             }
         }

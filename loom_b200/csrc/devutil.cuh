@@ -68,14 +68,14 @@ __device__ __forceinline__ void quant_lane8(const float *src, bool live, int gro
 __device__ __forceinline__ bool route_scores(const float *logits, const float *bias, int ne, int gating,
                                              float *scores, float *choice, int lane) {
     if (gating == 2) {
-        for (int e = lane; e < ne; e += 32) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
+        for (int e = lane; e < ne; e += 32) scores[e] = fdiv(1.0f, fadd(1.0f, exp_f(-logits[e])));
     } else if (gating == 1) {
         float m = -INFINITY;
         for (int e = lane; e < ne; e += 32) m = fmaxf(m, logits[e]);
         m = warp_max(m);
         float sum = 0.0f;
         for (int e = lane; e < ne; e += 32) {
-            const float v = expf(fsub(logits[e], m));
+            const float v = exp_f(fsub(logits[e], m));
             scores[e] = v;
             sum = fadd(sum, v);
         }
@@ -196,7 +196,7 @@ __device__ __forceinline__ void route_finish(bool ranked, int ne, int nk, int ga
         for (int k = 0; k < nk; k++) m = fmaxf(m, gates[k]);
         float sum = 0.0f;
         for (int k = 0; k < nk; k++) {
-            gates[k] = expf(fsub(gates[k], m));
+            gates[k] = exp_f(fsub(gates[k], m));
             sum = fadd(sum, gates[k]);
         }
         const float inv = fdiv(1.0f, sum);
@@ -247,7 +247,7 @@ template <int RW>
 __device__ __forceinline__ void route_warp_sc(const float (&v)[RW], int ne, int gating, float (&sc)[RW], int lane) {
     if (gating == 2) {
 #pragma unroll
-        for (int t = 0; t < RW; t++) sc[t] = fdiv(1.0f, fadd(1.0f, expf(-v[t])));
+        for (int t = 0; t < RW; t++) sc[t] = fdiv(1.0f, fadd(1.0f, exp_f(-v[t])));
     } else if (gating == 1) {
         float m = -INFINITY;  // fmaxf skips NaN, so the lane maximum is never NaN
 #pragma unroll
@@ -260,7 +260,7 @@ __device__ __forceinline__ void route_warp_sc(const float (&v)[RW], int ne, int 
         float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // route_block's warp w sums experts 32w + l + 128j
 #pragma unroll
         for (int t = 0; t < RW; t++) {
-            sc[t] = expf(fsub(v[t], m));
+            sc[t] = exp_f(fsub(v[t], m));
             if (lane + 32 * t < ne) part[t & 3] = fadd(part[t & 3], sc[t]);
         }
 #pragma unroll
@@ -414,7 +414,7 @@ __device__ __forceinline__ void route_block(const float *logits, const float *bi
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = ROUTE_THREADS / 32;
     if (gating == 2) {
-        for (int e = tid; e < ne; e += ROUTE_THREADS) scores[e] = fdiv(1.0f, fadd(1.0f, expf(-logits[e])));
+        for (int e = tid; e < ne; e += ROUTE_THREADS) scores[e] = fdiv(1.0f, fadd(1.0f, exp_f(-logits[e])));
     } else if (gating == 1) {
         float m = -INFINITY;
         for (int e = tid; e < ne; e += ROUTE_THREADS) m = fmaxf(m, logits[e]);
@@ -426,7 +426,7 @@ __device__ __forceinline__ void route_block(const float *logits, const float *bi
         for (int w = 1; w < NW; w++) m = fmaxf(m, red[w]);
         float sum = 0.0f;
         for (int e = tid; e < ne; e += ROUTE_THREADS) {
-            const float v = expf(fsub(logits[e], m));
+            const float v = exp_f(fsub(logits[e], m));
             scores[e] = v;
             sum = fadd(sum, v);
         }

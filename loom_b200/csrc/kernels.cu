@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(256) k_gateup(Src src, int dim, XQ x256, XQ x3
     rowdot<1>(s.g, s.gb_g + (uint64_t)r * nbg, nbg, act256(s.g.type) ? x256 : x32, s.token, 1, g, lane);
     rowdot<1>(s.u, s.gb_u + (uint64_t)r * nbu, nbu, act256(s.u.type) ? x256 : x32, s.token, 1, u, lane);
     if (lane == 0) {
-        const float sl = fdiv(g[0], fadd(1.0f, expf(-g[0])));
+        const float sl = fdiv(g[0], fadd(1.0f, exp_f(-g[0])));
         act[s.act_off + r] = fmul(sl, u[0]);
     }
 }

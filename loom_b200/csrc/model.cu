@@ -64,6 +64,7 @@ struct Model {
     size_t dim = 0, n_layers = 0, nh = 0, nkv = 0, hd = 0, rope_dim = 0, vocab = 0, ctx = 0;
     float eps = 0, scale = 0;
     int neox = 0;
+    bool serial_norm = false, ordered_attn = false;
     Mat embd, out;
     const float *out_norm = nullptr;
     std::vector<LayerRt> L;
@@ -171,14 +172,14 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
         const LayerRt &l = m.L[li];
         float *x = m.x[cur];
         launch_rmsnorm_q(x, nullptr, l.attn_norm, dim, m.eps, m.normed, m.need256 ? m.n256 : none,
-                         m.need32 ? m.n32 : none, st);
+                         m.need32 ? m.n32 : none, m.serial_norm, st);
         matvec(l.wq, m.normed, m.n256, m.n32, m.q, st);
         matvec(l.wk, m.normed, m.n256, m.n32, m.k, st);
         matvec(l.wv, m.normed, m.n256, m.n32, m.v, st);
         float *kc = m.kc + li * layer_stride, *vc = m.vc + li * layer_stride;
         launch_qk_rope(m.q, m.k, m.v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps, pos,
                        (int)m.ctx, kc, vc, st);
-        launch_attention(m.q, kc, vc, nh, nkv, hd, m.scale, pos, (int)m.ctx, m.part, m.att, st);
+        launch_attention(m.q, kc, vc, nh, nkv, hd, m.scale, pos, (int)m.ctx, m.part, m.att, m.ordered_attn, st);
         if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
             const bool k256 = act256(l.wo.type);
             const XQW &a = k256 ? m.a256 : m.a32;
@@ -187,7 +188,7 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
         }
         matvec(l.wo, m.att, m.a256, m.a32, m.proj, st);
         // x += proj (llama.zig:1195), then the FFN norm; the MoE layer quantizes normed itself
-        launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, none, none, st);
+        launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, none, none, m.serial_norm, st);
         float *xn = m.x[cur ^ 1];
         if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr, st))
             return rc;
@@ -200,7 +201,7 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
         else
             o32 = m.n32;
     }
-    launch_rmsnorm_q(m.x[cur], nullptr, m.out_norm, dim, m.eps, m.normed, o256, o32, st);
+    launch_rmsnorm_q(m.x[cur], nullptr, m.out_norm, dim, m.eps, m.normed, o256, o32, m.serial_norm, st);
     float *lg = logits ? logits : m.logits;
     matvec(m.out, m.normed, m.n256, m.n32, lg, st);
     if (next) {
@@ -262,6 +263,12 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
     m->ctx = d->ctx_len;
     m->eps = d->eps;
     m->neox = d->rope_neox;
+    m->serial_norm = d->exact_order || d->dim <= (size_t)RN_SERIAL_MAX;
+    m->ordered_attn = d->exact_order || d->ctx_len <= (size_t)ATT_ORDERED_MAX;
+    if (m->ordered_attn && d->ctx_len > (size_t)ATT_ORDERED_LIMIT) {
+        delete m;
+        return rt_decline("exact_order takes contexts up to 32768 positions");
+    }
     m->scale = d->attn_logit_mul / std::sqrt((float)d->head_dim);  // llama.zig:1116
     const size_t dim = d->dim, qd = d->n_heads * d->head_dim, kvd = d->n_kv_heads * d->head_dim;
     if (!mat(d->token_embd, d->vocab, dim, m->embd)) return bail(rt_decline("token_embd: unknown tensor or wrong size"));

@@ -664,7 +664,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
                 if (r < rows) {
                     if (FMT == 0) {
                         const float g = acc[0][i], u = acc[MATS - 1][i];
-                        A.act[(size_t)slot * stride + row0 + r] = fmul(fdiv(g, fadd(1.0f, expf(-g))), u);
+                        A.act[(size_t)slot * stride + row0 + r] = fmul(fdiv(g, fadd(1.0f, exp_f(-g))), u);
                     } else {
                         A.y[(size_t)slot * dim + row0 + r] = acc[0][i];
                     }
@@ -1127,7 +1127,7 @@ __global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const 
                         if (i >= tl.nc) break;
                         const int slot = tc_slot(A, tl, i);
                         const float g = xchg[i * 256 + r], u = xchg[i * 256 + 128 + r];
-                        A.act[(size_t)slot * stride + row0 + r] = fmul(fdiv(g, fadd(1.0f, expf(-g))), u);
+                        A.act[(size_t)slot * stride + row0 + r] = fmul(fdiv(g, fadd(1.0f, exp_f(-g))), u);
                     }
                 asm volatile("bar.sync 1, %0;" ::"r"(DP_CWARPS * 32) : "memory");  // xchg zeroed by the next tile
             } else if (r < rows) {

@@ -143,7 +143,7 @@ def qwen3_moe(n_layers: int = 48, ctx_len: int = 2048, n_expert: int = 128, voca
 class DeviceModel:
     """A ModelSpec's tensors on the GPU plus the backend's model handle."""
 
-    def __init__(self, spec: ModelSpec, host: Optional[Dict[str, np.ndarray]] = None):
+    def __init__(self, spec: ModelSpec, host: Optional[Dict[str, np.ndarray]] = None, exact_order: bool = False):
         self.spec = spec
         self.t: Dict[str, DeviceTensor] = {}
         for p in spec.plan():
@@ -177,6 +177,7 @@ class DeviceModel:
         d.dim, d.n_layers, d.n_heads, d.n_kv_heads = spec.dim, spec.n_layers, spec.n_heads, spec.n_kv_heads
         d.head_dim, d.rope_dim, d.vocab, d.ctx_len = spec.head_dim, spec.rope_dim, spec.vocab, spec.ctx_len
         d.eps, d.rope_base, d.attn_logit_mul, d.rope_neox = spec.eps, spec.rope_base, 1.0, int(spec.rope_neox)
+        d.exact_order = int(exact_order)
         d.token_embd, d.output_norm, d.output = h("token_embd"), h("output_norm"), h("output")
         d.layers = self._layers
         self.desc = d

@@ -789,21 +789,28 @@ int or_matmul(int t, float *out, const uint8_t *data, const float *xs, size_t n,
     return 0;
 }
 
+// f32 e^x, correctly rounded (a double-precision exp rounded once; exact to
+// f32 except within ~2^-29 of a rounding boundary). Zig's f32 @exp and glibc's
+// expf are both within ~0.5 ulp of this and differ from it, and from each
+// other, in rare last-bit cases; the correctly rounded value is the common
+// definition the oracle and the device kernels share.
+static inline float exp_f(float x) { return (float)std::exp((double)x); }
+
 // tensor.zig:18-28
 void or_softmax(float *x, size_t n) {
     float m = -INFINITY;
     for (size_t i = 0; i < n; i++) m = std::fmax(m, x[i]);
     float sum = 0.0f;
     for (size_t i = 0; i < n; i++) {
-        x[i] = std::exp(x[i] - m);
+        x[i] = exp_f(x[i] - m);
         sum += x[i];
     }
     const float inv = 1.0f / sum;
     for (size_t i = 0; i < n; i++) x[i] *= inv;
 }
 
-float or_silu(float x) { return x / (1.0f + std::exp(-x)); }      // tensor.zig:30
-float or_sigmoid(float x) { return 1.0f / (1.0f + std::exp(-x)); }  // tensor.zig:34
+float or_silu(float x) { return x / (1.0f + exp_f(-x)); }      // tensor.zig:30
+float or_sigmoid(float x) { return 1.0f / (1.0f + exp_f(-x)); }  // tensor.zig:34
 
 // tensor.zig:9-15
 void or_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps) {

@@ -46,15 +46,21 @@ def test_tiny_llama_64_greedy_tokens_match_oracle(be, orc):
         dev.free()
 
 
-@pytest.mark.parametrize("spec", [tiny_llama(ctx_len=160),
-                                  qwen3_moe(n_layers=2, ctx_len=160, n_expert=16, vocab=4096),
-                                  qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096)],
-                         ids=["tiny_llama", "qwen3_reduced_ordered", "qwen3_reduced_split"])
-def test_model_logits_match_oracle_over_positions(be, orc, spec):
-    """Teacher-forced: both sides get the same tokens. ctx 640 takes the split
-    attention (chunks of 64 rows, merged); positions run past two chunks."""
+@pytest.mark.parametrize("spec,exact,tol", [
+    (tiny_llama(ctx_len=160), False, TOL),
+    (qwen3_moe(n_layers=2, ctx_len=160, n_expert=16, vocab=4096), True, TOL),
+    (qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096), True, TOL),
+    (qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096), False, 2e-2)],
+    ids=["tiny_llama", "qwen3_exact", "qwen3_exact_long_ctx", "qwen3_fast_split"])
+def test_model_logits_match_oracle_over_positions(be, orc, spec, exact, tol):
+    """Teacher-forced: both sides get the same tokens. Tiny llama (dim 288,
+    ctx 160) keeps the reference's order by default; the Qwen3 shape keeps it
+    with exact_order. The fast form (tree-summed RMSNorm at dim 2048, split
+    attention at ctx 640: chunks of 64 rows, merged) differs by rounding, which
+    can move int8 activations of the next matvec: its logits are held to
+    2e-2 relative L2."""
     ref = _runner(spec, orc)
-    dev = DeviceModel(spec)
+    dev = DeviceModel(spec, exact_order=exact)
     rng = np.random.default_rng(7)
     try:
         for pos in range(140):
@@ -62,9 +68,9 @@ def test_model_logits_match_oracle_over_positions(be, orc, spec):
             want = ref.step(tok, pos)
             nxt, got = dev.decode(tok, pos, logits=True)
             assert np.all(np.isfinite(got))
-            assert rel_l2(got, want) < TOL, (pos, rel_l2(got, want))
+            assert rel_l2(got, want) < tol, (pos, rel_l2(got, want))
             top = np.sort(want)[-2:]
-            if top[1] - top[0] > 1e-3 * max(1.0, abs(top[1])):
+            if top[1] - top[0] > 50 * tol * max(1.0, abs(top[1])):
                 assert nxt == int(np.argmax(want)), pos
     finally:
         dev.free()
