@@ -1,7 +1,28 @@
 """Benchmark of the B200 CUDA backend on BASELINE's headline metric:
 decode tok/s + expert-matvec HBM GB/s at Qwen3-30B-A3B Q4_K.
 
-Workload (one "step"): one decode token (T=1 by default, --tokens T for a
+Default workload (--workload model; one "step"): one decode token at batch 1
+through the FULL Qwen3-30B-A3B-shaped model (48 layers,
+hidden 2048, 32/4 heads of 128, QK-RMSNorm, RoPE NEOX, 128 experts top-8 of
+768, vocab 151936, Q4_K_M mix) at position 2047 of a 2048-token context whose
+KV cache the run first fills by decoding: embedding, per layer RMSNorm +
+q/k/v + QK-norm + RoPE + KV append + attention over 2048 positions + output
+projection + MoE FFN, final norm, lm_head and argmax (loom_cuda_model_*).
+~2.5 GB is read per token, far more than the 126 MB L2.
+  value      tok/s of loom_cuda_model_step replayed from a CUDA graph
+  e2e        loom_cuda_model_decode: host token in, host token out (one
+             8-byte H2D and one 4-byte D2H copy per step), wall clock
+  roofline   algorithmic bytes of the token (every weight byte read once,
+             8 experts per layer, the KV cache rows, the head) / step time
+  moe_stack  the MoE-only measurement below (expert-matvec GB/s)
+  cpu_baseline  the oracle's token step (oracle/ restatement of llama.zig
+             step) on sampled layers of the same model, extrapolated
+With torchrun (N > 1) the model runs expert-parallel: experts of every layer
+sharded contiguously over the ranks, attention/norms/router/head replicated,
+the MoE partial outputs summed by an NCCL all-reduce (strong scaling: the
+same token on every rank).
+
+--workload moe (one "step"): one decode token (T=1 by default, --tokens T for a
 batch) through the 48 MoE layers of a Qwen3-30B-A3B-shaped model with
 distinct random-init weights per layer: router f32 [128x2048] -> softmax top-8
 with renorm -> gate/up Q4_K [768x2048] + SwiGLU -> down Q6_K [2048x768] ->
@@ -193,14 +214,14 @@ def build_model(T: int, seed_base: int = 1000, e0: int = 0, nl: int = NE):
     return layers
 
 
-def run_gpu(args):
+def run_gpu(args, emit=True):
     import torch
     import torch.distributed as dist
     from loom_b200 import backend as B
     from loom_b200 import device as D
 
     rank, world, local = dist_env()
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     B.init(local)
@@ -363,7 +384,14 @@ def run_gpu(args):
         line["batch"] = batch
     if cpu:
         line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    if stack is not None:
+        stack.free()
+    for L in layers:
+        for t in (L.gate, L.up, L.down, L.router):
+            t.free()
+    return line
 
 
 def trace_stack(stack, step, stream, torch):
@@ -569,6 +597,223 @@ def run_e2e(args, B):
             "path": f"seam calls with host buffers, {nl} distinct layers cycled to {LAYERS}"}
 
 
+# ---- full-model decode (--workload model) -------------------------------------------
+
+MODEL_METRIC = "decode tok/s (Qwen3-30B-A3B full model, Q4_K_M, batch 1, ctx 2048)"
+
+
+def model_bytes(spec, pos: int, n_local: int = None) -> int:
+    """Algorithmic HBM bytes of one decode token at position pos: every
+    replicated weight once (attention, norms, router, head, the embedding
+    row), the n_used selected experts' gate/up/down planes (on a shard: the
+    expected share n_used * n_local / n_expert), the KV rows read (pos + 1 per
+    layer, keys and values) and written (one)."""
+    n_local = spec.n_expert if n_local is None else n_local
+    kvd = spec.n_kv_heads * spec.head_dim
+    b = 0
+    for t in spec.plan():
+        if t.name == "token_embd":
+            b += t.nbytes // spec.vocab
+        elif t.planes > 1:
+            b += t.nbytes // t.planes * spec.n_used * n_local / spec.n_expert
+        else:
+            b += t.nbytes
+    b += spec.n_layers * (pos + 2) * kvd * 4 * 2
+    return int(b)
+
+
+def cpu_model_time(spec, threads: int, reps: int, pos: int):
+    """Seconds per token of the oracle's token step (llama.zig:1111-1228
+    restated) for `spec`, measured on 2- and 4-layer cuts of the model (same
+    shapes, KV cache filled with synthetic rows up to pos) and extrapolated:
+    head = t2 - 2 * layer, layer = (t4 - t2) / 2. Medians of `reps` runs."""
+    import copy
+    from oracle import oracle as orc
+    from oracle.oracle import LlamaRunner
+    from tests.modelref import host_tensors
+    if threads > 1:
+        orc.parallel_begin(threads)
+    try:
+        med = {}
+        for nl in (2, 4):
+            sp = copy.copy(spec)
+            sp.n_layers = nl
+            sp.ctx_len = pos + 1
+            run = LlamaRunner(sp, host_tensors(sp, orc))
+            rng = np.random.default_rng(0)
+            run.kc[:] = rng.standard_normal(run.kc.size).astype(np.float32)
+            run.vc[:] = rng.standard_normal(run.vc.size).astype(np.float32)
+            run.step(1, pos)  # warm-up
+            ts = []
+            for r in range(reps):
+                t0 = time.perf_counter()
+                run.step(1 + r, pos)
+                ts.append(time.perf_counter() - t0)
+            med[nl] = statistics.median(ts)
+    finally:
+        if threads > 1:
+            orc.parallel_end()
+    layer = max((med[4] - med[2]) / 2, 1e-9)
+    head = max(med[2] - 2 * layer, 0.0)
+    return head + spec.n_layers * layer
+
+
+def cpu_model_baseline(spec, pos, reps=9):
+    """The reference CPU path's own policy: nproc - 2 worker threads
+    (generator.zig:265-304), plus the single-thread figure."""
+    n = max(1, (os.cpu_count() or 1) - 2)
+    t_n = cpu_model_time(spec, n, reps, pos)
+    t_1 = cpu_model_time(spec, 1, max(3, reps // 3), pos)
+    try:
+        import cpuinfo
+        model = cpuinfo.get_cpu_info().get("brand_raw", "?")
+    except Exception:  # noqa: BLE001
+        model = "?"
+    return {"value": round(1.0 / t_n, 3), "unit": "tok/s", "cores": n, "kind": "port",
+            "value_1_thread": round(1.0 / t_1, 3), "host_cores": os.cpu_count(), "cpu_model": model,
+            "sample": (f"oracle token step at position {pos} on 2- and 4-layer cuts of the model (KV cache "
+                       f"synthetic), medians of {reps} runs ({max(3, reps // 3)} at 1 thread), extrapolated to "
+                       f"{spec.n_layers} layers")}
+
+
+def run_model(args):
+    import torch
+    import torch.distributed as dist
+    from loom_b200 import backend as B
+    from loom_b200 import device as D
+    from loom_b200.model import DeviceModel, qwen3_moe
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    B.init(local)
+    spec = qwen3_moe(n_layers=args.layers, ctx_len=args.ctx)
+    shard = D.expert_range(spec.n_expert, rank, world) if world > 1 else None
+    if world > 1:
+        D.ep_init(rank, world, dist)
+    dev = DeviceModel(spec, expert_shard=shard)
+    pos = spec.ctx_len - 1
+    # fill the KV cache: greedy decode of positions 0 .. ctx-2 (every rank the same tokens)
+    tok = 1
+    t0 = time.perf_counter()
+    for p in range(pos):
+        tok, _ = dev.decode(tok, p)
+    fill_s = time.perf_counter() - t0
+
+    stream = torch.cuda.Stream()
+    d_tok = torch.tensor([tok], dtype=torch.int32, device="cuda")
+    d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    d_next = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d_logits = torch.empty(spec.vocab, dtype=torch.float32, device="cuda")
+    with torch.cuda.stream(stream):
+        dev.step(d_tok, d_pos, d_logits, d_next, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    k0 = B.kernelLaunches()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        dev.step(d_tok, d_pos, d_logits, d_next, stream=torch.cuda.current_stream().cuda_stream)
+    launches_per_step = B.kernelLaunches() - k0
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as ck:
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # e2e: the host entry point, host token in and out, wall clock per token
+    for _ in range(args.warmup):
+        dev.decode(tok, pos)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dev.decode(tok, pos)
+    e2e_ms = (time.perf_counter() - t0) / args.steps * 1e3
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = (float(v) for v in t.tolist())
+        dist.barrier()
+    n_local = shard[1] if shard else spec.n_expert
+    bytes_step = model_bytes(spec, pos, n_local)
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    dev.free()
+
+    moe = None
+    if world == 1 and not args.no_moe_stack:
+        margs = argparse.Namespace(**vars(args))
+        margs.tokens, margs.ep, margs.engine, margs.trace = 1, False, "auto", False
+        margs.layers = args.layers
+        moe = run_gpu(margs, emit=False)
+    if rank != 0:
+        return
+    cpu = None
+    if not args.no_cpu and world == 1:
+        cpu = cpu_model_baseline(spec, pos)
+    line = {
+        "metric": MODEL_METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "int8xq4/q6 matvecs (f32 accum), f32 attention and KV",
+        "data": "synthetic (seeded generator), random-init weights",
+        "config": {"workload": f"qwen3-30b-a3b full-model decode, batch 1, position {pos} of a {spec.ctx_len}-token "
+                               f"context", "model": spec.name, "layers": spec.n_layers, "batch": 1,
+                   "ctx": spec.ctx_len, "dim": spec.dim, "n_heads": spec.n_heads, "n_kv_heads": spec.n_kv_heads,
+                   "n_expert": spec.n_expert, "n_used": spec.n_used, "vocab": spec.vocab,
+                   "parallelism": (f"ep{world} (experts sharded, attention replicated, NCCL all-reduce combine)"
+                                   if world > 1 else "1 gpu"),
+                   "engine": "loom_cuda_model_step in a CUDA graph",
+                   "l2": f"inputs > L2 ({bytes_step / 1e9:.2f} GB read per token)",
+                   "kv_fill_s": round(fill_s, 2)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "whole decode step (all kernels of the token, CUDA-event timed)",
+                     "peak_kind": peak_kind, "bytes_per_step": bytes_step},
+        "e2e": {"value": round(1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                "path": "loom_cuda_model_decode (graph replay, host token in/out), wall clock"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": ck.summary(),
+    }
+    if moe:
+        line["moe_stack"] = {k: moe[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "config",
+                                                 "e2e", "e2e_device", "prefill", "batch", "gpu_launches")
+                             if k in moe}
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_model(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from loom_b200.model import qwen3_moe
+    spec = qwen3_moe(n_layers=args.layers, ctx_len=args.ctx)
+    pos = spec.ctx_len - 1
+    cpu = cpu_model_baseline(spec, pos, reps=max(args.steps, 9))
+    v = cpu["value"]
+    line = {"impl": "reference", "metric": MODEL_METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4/q6 matvecs (f32 accum), f32 attention and KV",
+            "data": "synthetic (seeded generator), random-init weights",
+            "config": {"workload": f"qwen3-30b-a3b full-model decode, batch 1, position {pos} of a {spec.ctx_len}-"
+                                   f"token context", "model": spec.name, "layers": spec.n_layers, "batch": 1,
+                       "ctx": spec.ctx_len, "parallelism": "host threads"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -596,9 +841,15 @@ def main():
                          "exactly the routed rows (their counts go to the host each layer, eager launches)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers in the stack (default 48; smaller only for profiling captures)")
+    ap.add_argument("--workload", default="model", choices=["model", "moe"],
+                    help="model: full Qwen3-30B-A3B decode (the headline); moe: the 48 MoE layers only")
+    ap.add_argument("--ctx", type=int, default=2048, help="context length of the model workload")
+    ap.add_argument("--no-moe-stack", action="store_true", help="model workload: skip the MoE-only sub-measurement")
     args = ap.parse_args()
     globals()["LAYERS"] = args.layers
-    if args.impl == "reference":
+    if args.workload == "model":
+        run_reference_model(args) if args.impl == "reference" else run_model(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

@@ -143,12 +143,20 @@ def qwen3_moe(n_layers: int = 48, ctx_len: int = 2048, n_expert: int = 128, voca
 class DeviceModel:
     """A ModelSpec's tensors on the GPU plus the backend's model handle."""
 
-    def __init__(self, spec: ModelSpec, host: Optional[Dict[str, np.ndarray]] = None, exact_order: bool = False):
+    def __init__(self, spec: ModelSpec, host: Optional[Dict[str, np.ndarray]] = None, exact_order: bool = False,
+                 expert_shard: Optional[tuple] = None):
+        """expert_shard = (expert0, n_local): this rank holds only those experts of
+        every routed layer (expert parallelism after ep_init; the layer's partial
+        outputs are summed over the ranks); everything else is replicated."""
         self.spec = spec
         self.t: Dict[str, DeviceTensor] = {}
+        e0, nl = expert_shard if expert_shard else (0, spec.n_expert)
         for p in spec.plan():
             if host is not None and p.name in host:
                 self.t[p.name] = DeviceTensor.upload(p.type, host[p.name])
+            elif p.planes > 1 and expert_shard:
+                per = p.nblk // p.planes
+                self.t[p.name] = DeviceTensor.synth_range(p.type, e0 * per, nl * per, p.seed, p.sigma)
             elif p.fill == "synth":
                 self.t[p.name] = DeviceTensor.synth(p.type, p.nblk, p.seed, p.sigma)
             else:
@@ -166,7 +174,7 @@ class DeviceModel:
                 m.gating, m.weights_norm, m.weights_scale = 1, 1, 1.0
                 m.router = h(p + "ffn_gate_inp")
                 m.gate, m.up, m.down = h(p + "ffn_gate_exps"), h(p + "ffn_up_exps"), h(p + "ffn_down_exps")
-                m.n_local = spec.n_expert
+                m.expert0, m.n_local = e0, nl
                 m.n_group = m.topk_group = 1
                 if i + 1 < spec.n_layers:
                     m.next_router = h(f"blk.{i + 1}.ffn_gate_inp")
