@@ -276,6 +276,11 @@ int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *l
  * host -- the read-back that keeps a host copy authoritative (mlaReadCache,
  * backend.zig:191). */
 int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k, float *v);
+/* The device error word of the model's cooperative attention kernel (1 = a
+ * grid barrier gave up waiting; the kernel left without finishing the step);
+ * synchronizes, and re-arms the barrier counters after an error. 0 when
+ * none, -1 on an unknown handle or a failed stream. */
+int loom_cuda_model_error(uint64_t handle);
 int loom_cuda_model_free(uint64_t handle);
 
 /* A decode step (one token) through a whole stack of MoE layers as ONE

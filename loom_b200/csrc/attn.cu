@@ -9,6 +9,7 @@
 // order); the wide RMSNorm and the split attention use tree / chunked sums.
 #include "attn.cuh"
 #include "devutil.cuh"
+#include "pdl.cuh"
 
 namespace loom {
 
@@ -59,6 +60,8 @@ __global__ void __launch_bounds__(RN_THREADS) k_rmsnorm_q(float *x, const float 
     extern __shared__ float sx[];  // [dim]
     __shared__ float red[RN_THREADS / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait_();
+    pdl_trigger_();
     float ss = 0.0f;
     for (int i = tid; i < dim; i += RN_THREADS) {
         float v = x[i];
@@ -126,6 +129,8 @@ __global__ void __launch_bounds__(QR_WARPS * 32) k_qk_rope(float *q, float *k, c
     __shared__ float inv_all[QR_WARPS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int head = blockIdx.x * QR_WARPS + warp;
+    pdl_wait_();
+    pdl_trigger_();
     if (head >= n_heads + n_kv) return;
     const int pos = (int)*pos_p;
     if (pos >= ctx) return;
@@ -180,6 +185,8 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
     extern __shared__ float sc[];  // [ctx]
     __shared__ float inv_s;
     const int h = blockIdx.x, tid = threadIdx.x;
+    pdl_wait_();
+    pdl_trigger_();
     const int pos = (int)*pos_p;
     if (pos >= ctx) return;
     const int seq = pos + 1, kvd = n_kv * hd;
@@ -213,72 +220,109 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
     }
 }
 
-// Split form: one CTA per (KV head g, chunk sp of ATT_CH cache rows). Partial
-// record per query head: o[hd] = sum_t e^(s_t - m) v_t, then m, l = sum_t e^(s_t - m).
+// Split form: one CTA per (KV head g, chunk sp of ATT_CH cache rows). The
+// chunk's key and value rows are staged into shared memory with cp.async (all
+// of them in flight at once; keys at a padded row stride so a warp's rows fall
+// on distinct banks), then each thread scores one row against two query heads
+// of the group. Partial record per query head: o[hd] = sum_t e^(s_t - m) v_t,
+// then m and l = sum_t e^(s_t - m). The split form does not follow the
+// reference's summation order, so it uses fused multiply-adds.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+__host__ __device__ constexpr int att_kstride(int hd) { return hd + 4; }
+
 __global__ void __launch_bounds__(AT_THREADS) k_attn_part(const float *q, const float *kc, const float *vc,
                                                          int n_heads, int n_kv, int hd, float scale,
                                                          const uint32_t *pos_p, int ctx, int nsplit, float *part) {
-    extern __shared__ float sm[];
-    const int G = n_heads / n_kv, kvd = n_kv * hd;
-    float *qs = sm;             // [G][hd]
-    float *sc = sm + G * hd;    // [G][ATT_CH]
+    extern __shared__ __align__(16) float sm[];
+    const int G = n_heads / n_kv, kvd = n_kv * hd, KS = att_kstride(hd);
+    float *sK = sm;                      // [ATT_CH][KS]
+    float *sV = sK + ATT_CH * KS;        // [ATT_CH][hd]
+    float *qs = sV + ATT_CH * hd;        // [G][hd]
+    float *sc = qs + G * hd;             // [G][ATT_CH]
     const int g = blockIdx.x, sp = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait_();
+    pdl_trigger_();
     const int pos = (int)*pos_p;
     if (pos >= ctx) return;
     const int seq = pos + 1, t0 = sp * ATT_CH;
     if (t0 >= seq) return;
     const int n = min(ATT_CH, seq - t0);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < G * hd; i += AT_THREADS) qs[i] = q[(size_t)g * G * hd + i];
-    __syncthreads();
-    // scores: one warp per cache row, every query head of the group against one read of the key
-    for (int j = warp; j < n; j += AT_WARPS) {
-        const float *kr = kc + (size_t)(t0 + j) * kvd + (size_t)g * hd;
-        float kv[MAX_HD / 32];
-#pragma unroll
-        for (int c = 0; c < MAX_HD / 32; c++) {
-            const int d = lane + 32 * c;
-            kv[c] = d < hd ? kr[d] : 0.0f;
+    const float *kb = kc + (size_t)t0 * kvd + (size_t)g * hd, *vb = vc + (size_t)t0 * kvd + (size_t)g * hd;
+    const bool vec4 = (hd & 3) == 0;
+    if (vec4) {
+        const int q4 = hd / 4;
+        for (int i = tid; i < n * q4; i += AT_THREADS) {
+            const int j = i / q4, c = (i % q4) * 4;
+            cp_async16(sK + j * KS + c, kb + (size_t)j * kvd + c);
+            cp_async16(sV + j * hd + c, vb + (size_t)j * kvd + c);
         }
-        for (int hh = 0; hh < G; hh++) {
-            float p = 0.0f;
-#pragma unroll
-            for (int c = 0; c < MAX_HD / 32; c++) {
-                const int d = lane + 32 * c;
-                if (d < hd) p = fadd(p, fmul(qs[hh * hd + d], kv[c]));
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    } else {
+#pragma unroll 4
+        for (int i = tid; i < n * hd; i += AT_THREADS) {
+            const int j = i / hd, c = i % hd;
+            sK[j * KS + c] = kb[(size_t)j * kvd + c];
+            sV[i] = vb[(size_t)j * kvd + c];
+        }
+    }
+    for (int i = tid; i < G * hd; i += AT_THREADS) qs[i] = q[(size_t)g * G * hd + i];
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    // scores: lane = cache row, warp = pair of query heads
+    const int HP = (G + 1) / 2;
+    for (int hp = warp; hp < HP; hp += AT_WARPS) {
+        const int j = lane, ha = 2 * hp, hb = min(2 * hp + 1, G - 1);
+        if (j < n) {
+            const float *kr = sK + j * KS, *qa = qs + ha * hd, *qb = qs + hb * hd;
+            float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+            if (vec4) {
+                for (int d = 0; d < hd; d += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+                    const float4 x4 = *reinterpret_cast<const float4 *>(qa + d);
+                    const float4 y4 = *reinterpret_cast<const float4 *>(qb + d);
+                    a0 = fmaf(k4.x, x4.x, a0); a1 = fmaf(k4.y, x4.y, a1);
+                    a0 = fmaf(k4.z, x4.z, a0); a1 = fmaf(k4.w, x4.w, a1);
+                    b0 = fmaf(k4.x, y4.x, b0); b1 = fmaf(k4.y, y4.y, b1);
+                    b0 = fmaf(k4.z, y4.z, b0); b1 = fmaf(k4.w, y4.w, b1);
+                }
+            } else {
+                for (int d = 0; d < hd; d++) {
+                    a0 = fmaf(kr[d], qa[d], a0);
+                    b0 = fmaf(kr[d], qb[d], b0);
+                }
             }
-            p = warp_sum_f(p);
-            if (lane == 0) sc[hh * ATT_CH + j] = fmul(p, scale);
+            sc[ha * ATT_CH + j] = (a0 + a1) * scale;
+            sc[hb * ATT_CH + j] = (b0 + b1) * scale;
         }
     }
     __syncthreads();
     float *rec = part + ((size_t)g * nsplit + sp) * G * (hd + 2);
-    for (int hh = warp; hh < G; hh += AT_WARPS) {  // chunk max, exponentials, sum
-        float m = -INFINITY;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[hh * ATT_CH + j]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int j = lane; j < n; j += 32) {
-            const float e = exp_f(fsub(sc[hh * ATT_CH + j], m));
-            sc[hh * ATT_CH + j] = e;
-            l = fadd(l, e);
-        }
-        l = warp_sum_f(l);
+    for (int hh = warp; hh < G; hh += AT_WARPS) {  // chunk max, exponentials, sum (one row per lane)
+        const float v = lane < n ? sc[hh * ATT_CH + lane] : -INFINITY;
+        const float m = warp_max(v);
+        const float e = lane < n ? exp_f(v - m) : 0.0f;
+        if (lane < n) sc[hh * ATT_CH + lane] = e;
+        const float l = warp_sum_f(e);
         if (lane == 0) {
             rec[hh * (hd + 2) + hd] = m;
             rec[hh * (hd + 2) + hd + 1] = l;
         }
     }
     __syncthreads();
-    for (int d = tid; d < hd; d += AT_THREADS) {  // o = sum_t e_t v_t, one read of each value row
+    for (int d = tid; d < hd; d += AT_THREADS) {  // o = sum_t e_t v_t
         float acc[MAX_GQA];
 #pragma unroll
         for (int hh = 0; hh < MAX_GQA; hh++) acc[hh] = 0.0f;
         for (int j = 0; j < n; j++) {
-            const float vv = vc[(size_t)(t0 + j) * kvd + (size_t)g * hd + d];
+            const float vv = sV[j * hd + d];
 #pragma unroll
             for (int hh = 0; hh < MAX_GQA; hh++)
-                if (hh < G) acc[hh] = fadd(acc[hh], fmul(sc[hh * ATT_CH + j], vv));
+                if (hh < G) acc[hh] = fmaf(sc[hh * ATT_CH + j], vv, acc[hh]);
         }
 #pragma unroll
         for (int hh = 0; hh < MAX_GQA; hh++)
@@ -286,23 +330,68 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_part(const float *q, const 
     }
 }
 
-// One CTA per query head: out = (sum_s o_s e^(m_s - M)) / (sum_s l_s e^(m_s - M)).
-__global__ void __launch_bounds__(AT_THREADS) k_attn_merge(const float *part, int n_heads, int n_kv, int hd,
-                                                          const uint32_t *pos_p, int ctx, int nsplit, float *out) {
-    const int h = blockIdx.x, G = n_heads / n_kv, g = h / G, hh = h % G;
+// Merge: one CTA per 256 consecutive outputs (ATT_MG_HEADS query heads of
+// 256 / ATT_MG_HEADS values): out = (sum_s o_s e^(m_s - M)) / (sum_s l_s
+// e^(m_s - M)), the weights e^(m_s - M) computed once per head and split;
+// then, when q256 / q32 are given, the 256 outputs are quantized for the
+// output projection (quantizeX256 / quantizeX), so no separate pass reads them.
+__global__ void __launch_bounds__(256) k_attn_merge(const float *part, int n_heads, int n_kv, int hd,
+                                                   const uint32_t *pos_p, int ctx, int nsplit, float *out, XQW q256,
+                                                   XQW q32) {
+    extern __shared__ float wsm[];  // [heads in CTA][nsplit] weights
+    __shared__ float Ls[40];  // heads per CTA <= 256 / 8 + 1 (head_dim >= 8)
+    __shared__ __align__(16) float val[256];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait_();
+    pdl_trigger_();
     const int pos = (int)*pos_p;
     if (pos >= ctx) return;
+    const int G = n_heads / n_kv, qd = n_heads * hd;
     const int live = (pos + 1 + ATT_CH - 1) / ATT_CH;
     const size_t stride = (size_t)G * (hd + 2);
-    const float *rec = part + (size_t)g * nsplit * stride + (size_t)hh * (hd + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < live; s++) M = fmaxf(M, rec[s * stride + hd]);
-    float L = 0.0f;
-    for (int s = 0; s < live; s++) L = fadd(L, fmul(rec[s * stride + hd + 1], exp_f(fsub(rec[s * stride + hd], M))));
-    for (int d = threadIdx.x; d < hd; d += AT_THREADS) {
-        float o = 0.0f;
-        for (int s = 0; s < live; s++) o = fadd(o, fmul(rec[s * stride + d], exp_f(fsub(rec[s * stride + hd], M))));
-        out[(size_t)h * hd + d] = fdiv(o, L);
+    const int e0 = blockIdx.x * 256;
+    const int h0 = e0 / hd, h1 = min((e0 + 256 - 1) / hd, n_heads - 1);
+    // per head of this CTA (one warp each): M, weights, L (splits in order)
+    for (int lh = warp; lh <= h1 - h0; lh += 8) {  // per-head smem: (h1 - h0 + 1) x nsplit floats
+        const int h = h0 + lh, g = h / G, hh = h % G;
+        const float *rec = part + (size_t)g * nsplit * stride + (size_t)hh * (hd + 2);
+        float *w = wsm + (size_t)lh * nsplit;
+        float M = -INFINITY;
+        for (int s = lane; s < live; s += 32) M = fmaxf(M, rec[s * stride + hd]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int s = lane; s < live; s += 32) {
+            const float ws = exp_f(rec[s * stride + hd] - M);
+            w[s] = ws;
+            L = fmaf(rec[s * stride + hd + 1], ws, L);
+        }
+        L = warp_sum_f(L);
+        if (lane == 0) Ls[lh] = L;
+    }
+    __syncthreads();
+    const int e = e0 + tid;
+    float o = 0.0f;
+    if (e < qd) {
+        const int h = e / hd, d = e % hd, g = h / G, hh = h % G, lh = h - h0;
+        const float *rec = part + (size_t)g * nsplit * stride + (size_t)hh * (hd + 2) + d;
+        const float *w = wsm + (size_t)lh * nsplit;
+#pragma unroll 8
+        for (int s = 0; s < live; s++) o = fmaf(rec[s * stride], w[s], o);
+        o = o / Ls[lh];
+        out[e] = o;
+    }
+    val[tid] = o;
+    __syncthreads();
+    if (q256.q && warp == 0 && e0 + 256 <= qd) {
+        const int off = lane * 8;
+        quant_lane8(val + off, true, 32, q256.q + e0 + off, q256.d + blockIdx.x, q256.s + e0 / 16 + lane / 2,
+                    nullptr, lane);
+    }
+    if (q32.q && warp == 0) {
+        const int b = e0 / 32 + lane / 4, nb = qd / 32;
+        const bool live_b = b < nb;
+        const int off = (lane / 4) * 32 + (lane & 3) * 8;
+        quant_lane8(val + (live_b ? off : 0), live_b, 4, q32.q + e0 + off, q32.d + b, nullptr, q32.s + b, lane);
     }
 }
 
@@ -312,16 +401,15 @@ unsigned cdiv_u(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 
 void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float eps, float *normed, XQW q256,
                       XQW q32, bool serial, cudaStream_t st) {
-    k_rmsnorm_q<<<1, RN_THREADS, (size_t)dim * 4, st>>>(x, add, w, dim, eps, normed, q256, q32, (int)serial);
-    count_launch();
+    launch_pdl_(k_rmsnorm_q, dim3(1), dim3(RN_THREADS), (size_t)dim * 4, st, x, add, w, dim, eps, normed, q256, q32,
+                (int)serial);
 }
 
 void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const float *kn, int n_heads, int n_kv,
                     int hd, int rope_dim, int neox, const float *rope, float eps, const uint32_t *pos, int ctx,
                     float *kc, float *vc, cudaStream_t st) {
-    k_qk_rope<<<cdiv_u(n_heads + n_kv, QR_WARPS), QR_WARPS * 32, 0, st>>>(q, k, v, qn, kn, n_heads, n_kv, hd,
-                                                                          rope_dim, neox, rope, eps, pos, ctx, kc, vc);
-    count_launch();
+    launch_pdl_(k_qk_rope, dim3(cdiv_u(n_heads + n_kv, QR_WARPS)), dim3(QR_WARPS * 32), 0, st, q, k, v, qn, kn,
+                n_heads, n_kv, hd, rope_dim, neox, rope, eps, pos, ctx, kc, vc);
 }
 
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx) {
@@ -329,26 +417,40 @@ size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx) {
     return (size_t)n_kv * nsplit * (n_heads / n_kv) * (hd + 2);
 }
 
+bool attn_merge_quantizes(int n_heads, int hd, int ctx) {
+    const int qd = n_heads * hd, nsplit = (ctx + ATT_CH - 1) / ATT_CH;
+    return qd % 256 == 0 && (256 % hd == 0 || hd % 256 == 0) && (size_t)(256 / hd + 1) * nsplit * 4 <= 96 * 1024;
+}
+
 void launch_attention(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, float scale,
-                      const uint32_t *pos, int ctx, float *part, float *out, bool ordered, cudaStream_t st) {
+                      const uint32_t *pos, int ctx, float *part, float *out, bool ordered, XQW q256, XQW q32,
+                      cudaStream_t st) {
     if (ordered) {
         static bool smem_set = false;  // the scores of up to ATT_ORDERED_LIMIT positions
         if (!smem_set) {
             cudaFuncSetAttribute(k_attn_ordered, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_ORDERED_LIMIT * 4);
             smem_set = true;
         }
-        k_attn_ordered<<<n_heads, AT_THREADS, (size_t)ctx * 4, st>>>(q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx,
-                                                                      out);
-        count_launch();
+        launch_pdl_(k_attn_ordered, dim3(n_heads), dim3(AT_THREADS), (size_t)ctx * 4, st, q, kc, vc, n_heads, n_kv,
+                    hd, scale, pos, ctx, out);
         return;
     }
     const int nsplit = (ctx + ATT_CH - 1) / ATT_CH;
     const int G = n_heads / n_kv;
-    const size_t smem = ((size_t)G * hd + (size_t)G * ATT_CH) * 4;
-    k_attn_part<<<dim3(n_kv, nsplit), AT_THREADS, smem, st>>>(q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx, nsplit,
-                                                               part);
-    k_attn_merge<<<n_heads, AT_THREADS, 0, st>>>(part, n_heads, n_kv, hd, pos, ctx, nsplit, out);
-    count_launches(2);
+    const size_t smem = ((size_t)ATT_CH * att_kstride(hd) + (size_t)ATT_CH * hd + (size_t)G * hd + (size_t)G * ATT_CH) * 4;
+    static bool part_smem_set = false;
+    if (!part_smem_set) {
+        cudaFuncSetAttribute(k_attn_part, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (ATT_CH * att_kstride(MAX_HD) + ATT_CH * MAX_HD + MAX_GQA * MAX_HD + MAX_GQA * ATT_CH) * 4);
+        cudaFuncSetAttribute(k_attn_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        part_smem_set = true;
+    }
+    launch_pdl_(k_attn_part, dim3(n_kv, nsplit), dim3(AT_THREADS), smem, st, q, kc, vc, n_heads, n_kv, hd, scale, pos,
+                ctx, nsplit, part);
+    const int qd = n_heads * hd;
+    const int heads_per_cta = 256 / hd + 1 < n_heads ? 256 / hd + 1 : n_heads;
+    launch_pdl_(k_attn_merge, dim3(cdiv_u(qd, 256)), dim3(256), (size_t)heads_per_cta * nsplit * 4, st, part, n_heads,
+                n_kv, hd, pos, ctx, nsplit, out, q256, q32);
 }
 
 }  // namespace loom

@@ -35,12 +35,16 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 // Split form: the rows are split in chunks of ATT_CH across CTAs (one CTA
 // per KV head and chunk, all its query heads against one read of each row),
 // each with a running maximum and sum; a merge kernel combines the chunks.
-// `part` holds attn_part_floats(...) floats (split form only).
-constexpr int ATT_CH = 64;
+// `part` holds attn_part_floats(...) floats (split form only). With the split
+// form the merge also quantizes the output (q256 / q32 non-null) when
+// attn_merge_quantizes(); otherwise the caller quantizes `out` itself.
+constexpr int ATT_CH = 32;
 constexpr int ATT_ORDERED_MAX = 512;      // default: ordered up to this context
 constexpr int ATT_ORDERED_LIMIT = 32768;  // largest context of the ordered form
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx);
+bool attn_merge_quantizes(int n_heads, int hd, int ctx);
 void launch_attention(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, float scale,
-                      const uint32_t *pos, int ctx, float *part, float *out, bool ordered, cudaStream_t st);
+                      const uint32_t *pos, int ctx, float *part, float *out, bool ordered, XQW q256, XQW q32,
+                      cudaStream_t st);
 
 }  // namespace loom

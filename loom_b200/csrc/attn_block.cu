@@ -1,0 +1,565 @@
+// attn_block.cu -- the attention half of one decoder layer (llama.zig:1138-1216)
+// as ONE cooperative launch: RMSNorm -> q/k/v matvecs -> headNorm + RoPE + KV
+// append -> split-position softmax attention -> merge + quantization -> output
+// projection + residual -> FFN RMSNorm, the phases separated by bounded grid
+// barriers instead of kernel boundaries (the separate-kernel path of
+// model.cu costs ~8 launches of a few microseconds each per layer at batch 1).
+//
+// One CTA per SM, 16 warps. Phases (W = all warps of the grid):
+//   P1  every CTA: x -> RMSNorm -> int8 quantization into shared memory (each
+//       CTA its own copy); warps hold 4 q/k/v rows each, their weight loads
+//       issued before the norm (warp engine, warpdot.cuh), then the
+//       reference's integer block dots; q, k, v rows to global.      barrier
+//   P2  one warp per head: headNorm + RoPE; k, v appended to the cache. barrier
+//   P3  groups of 4 warps: one (KV head, 32-row chunk) each, rows staged by
+//       cp.async, running max / sum per query head (as k_attn_part). barrier
+//   P4  CTA c < q_dim/256: merge of 256 outputs + their quantization; the
+//       output-projection warps issue their weight loads first.      barrier
+//   P5  output-projection rows (2 or 4 per warp): x[r] += W_o[r] . att. barrier
+//   P6  CTA 0: FFN RMSNorm of the new x -> normed (the MoE layer's input).
+// Every wait is bounded; on a time-out the kernel raises a bit of the error
+// word and leaves (the host re-arms the counters). The arrival counter is
+// monotonic: launch e of the kernel expects G * (5e + b) arrivals at barrier
+// b, e being the epoch the last CTA to exit advances.
+#include "attn.cuh"
+#include "attn_block.cuh"
+#include "devutil.cuh"
+#include "warpdot.cuh"
+
+#include <algorithm>
+
+namespace loom {
+
+namespace {
+
+constexpr int AB_WARPS = 12, AB_THREADS = AB_WARPS * 32;  // 12 warps: up to 168 registers a thread
+constexpr int AB_GRP_WARPS = 4;                       // warps of an attention group
+constexpr int AB_NBAR = 5;                            // grid barriers per launch
+constexpr uint32_t AB_POLLS = 1u << 21;               // bounded grid-barrier wait (~1 s)
+
+__device__ __forceinline__ unsigned long long ab_ld_acquire(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void ab_red_release(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ float ab_warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// bar[0]: u64 arrival counter; bar[1]: (u32 epoch, u32 exit count); bar[2]: u32 error word
+__device__ __forceinline__ bool ab_barrier(unsigned long long *ctr, unsigned long long target, unsigned *err) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ab_red_release(ctr, 1ull);
+        uint32_t i = 0;
+        for (; i < AB_POLLS; i++) {
+            if (ab_ld_acquire(ctr) >= target) break;
+            if ((i & 1023) == 1023 && *reinterpret_cast<volatile unsigned *>(err)) i = AB_POLLS;
+        }
+        if (i >= AB_POLLS) atomicOr(err, 1u);
+        s_ok = i < AB_POLLS;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+__device__ __forceinline__ void ab_cp16(void *smem, const void *gmem) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+// L2 prefetch of bytes [0, n) at p, 128-byte lines, spread over the grid's threads
+__device__ __forceinline__ void ab_prefetch(const void *p, size_t n, size_t gt, size_t nt) {
+    const uint8_t *b = static_cast<const uint8_t *>(p);
+    for (size_t off = gt * 128; off < n; off += nt * 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(b + off));
+}
+// every region of the first nblk blocks of a device tensor
+__device__ __forceinline__ void ab_prefetch_w(const WDev &w, uint64_t nblk, size_t gt, size_t nt) {
+    ab_prefetch(w.q, nblk * (size_t)layout_qbytes(w.type), gt, nt);
+    if (w.sc) ab_prefetch(w.sc, nblk * 16, gt, nt);
+    if (w.d) ab_prefetch(w.d, nblk * 2, gt, nt);
+}
+
+// rows [r0, r0 + S) of one matrix against one activation view
+struct AbRows {
+    WDev w;
+    int r0, nb;
+    XV x;
+    __device__ __forceinline__ void at(int s, WDev &ww, uint64_t &gb, XV &xv) const {
+        ww = w;
+        gb = (uint64_t)(r0 + s) * nb;
+        xv = x;
+    }
+};
+
+__host__ __device__ constexpr size_t ab_al16(size_t n) { return (n + 15) & ~size_t(15); }
+
+template <int TY> constexpr int ab_maxu() { return TY == T_Q4_K ? 8 : TY == T_Q6_K ? 4 : TY == T_Q8_0 ? 4 : 2; }
+
+// RMSNorm of x (dim floats) by the whole CTA into sx (shared): the sum of
+// squares serial (thread 0, the reference's order) or a tree; then
+// out = x * scale * w. Returns after a __syncthreads with sx holding the result.
+__device__ void ab_rmsnorm(const float *x, const float *w, int dim, float eps, bool serial, float *sx, float *red) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float ss = 0.0f;
+    for (int i = tid; i < dim; i += AB_THREADS) {
+        const float v = x[i];
+        sx[i] = v;
+        if (!serial) ss = fadd(ss, fmul(v, v));
+    }
+    __syncthreads();
+    if (serial) {
+        if (tid == 0) {
+            float s = 0.0f;
+            for (int i = 0; i < dim; i++) s = fadd(s, fmul(sx[i], sx[i]));
+            red[0] = s;
+        }
+    } else {
+        ss = ab_warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.0f;
+            for (int i = 0; i < AB_WARPS; i++) t = fadd(t, red[i]);
+            red[0] = t;
+        }
+    }
+    __syncthreads();
+    const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(red[0], (float)dim), eps)));
+    for (int i = tid; i < dim; i += AB_THREADS) sx[i] = fmul(fmul(sx[i], scale), w[i]);
+    __syncthreads();
+}
+
+// quantize sx (n floats) per 256 (k256) or per 32 into q/d/s
+__device__ void ab_quant(const float *sx, int n, bool k256, int8_t *q, float *d, int32_t *s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (k256) {
+        for (int b = warp; b < n / 256; b += AB_WARPS) {
+            const int off = b * 256 + lane * 8;
+            quant_lane8(sx + off, true, 32, q + off, d + b, s + b * 16 + lane / 2, nullptr, lane);
+        }
+    } else {
+        const int nb = n / 32, ng = (nb + 7) / 8;
+        for (int g = warp; g < ng; g += AB_WARPS) {
+            const int b = g * 8 + lane / 4;
+            const bool live = b < nb;
+            const int off = b * 32 + (lane & 3) * 8;
+            quant_lane8(sx + (live ? off : 0), live, 4, q + off, d + b, nullptr, s + b, lane);
+        }
+    }
+}
+
+template <int TA, int TV, int TO, int SO>
+__global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
+    extern __shared__ __align__(16) uint8_t ab_smem[];
+    __shared__ float red[AB_WARPS];
+    __shared__ float Ls[40];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, c = blockIdx.x, gw = c * AB_WARPS + warp, W = G * AB_WARPS;
+    const int dim = A.dim, nh = A.n_heads, nkv = A.n_kv, hd = A.hd, qd = nh * hd, kvd = nkv * hd;
+    const int GQ = nh / nkv;
+    unsigned long long *ctr = A.bar;
+    unsigned *ep = reinterpret_cast<unsigned *>(A.bar + 1);
+    unsigned *err = reinterpret_cast<unsigned *>(A.bar + 2);
+    const unsigned long long base = (unsigned long long)G * AB_NBAR * *reinterpret_cast<volatile unsigned *>(ep);
+    int nbar = 0;
+    auto mark = [&](int i) {
+        if (A.trace && c == 0 && tid == 0) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            A.trace[i] = t;
+        }
+    };
+    mark(0);
+    const int pos = (int)*A.pos;
+    const bool pos_ok = pos < A.ctx;
+    {  // every byte the layer will read from HBM, requested into L2 up front: the phases then
+       // wait on L2 round trips only, and HBM streams at full rate underneath them
+        const size_t gt = (size_t)c * AB_THREADS + tid, nt = (size_t)G * AB_THREADS;
+        const int qd0 = A.n_heads * A.hd, kvd0 = A.n_kv * A.hd;
+        ab_prefetch_w(A.wq, (uint64_t)qd0 * (A.dim / block_elems(TA)), gt, nt);
+        ab_prefetch_w(A.wk, (uint64_t)kvd0 * (A.dim / block_elems(TA)), gt, nt);
+        ab_prefetch_w(A.wv, (uint64_t)kvd0 * (A.dim / block_elems(TV)), gt, nt);
+        ab_prefetch_w(A.wo, (uint64_t)A.dim * (qd0 / block_elems(TO)), gt, nt);
+        if (pos_ok) {
+            ab_prefetch(A.kc, (size_t)pos * kvd0 * 4, gt, nt);
+            ab_prefetch(A.vc, (size_t)pos * kvd0 * 4, gt, nt);
+        }
+    }
+
+    // ---- shared memory map -----------------------------------------------------------
+    // (regions on 16-byte boundaries: ab_fixed_smem)
+    float *sx = reinterpret_cast<float *>(ab_smem);                                 // [dim] (norms)
+    int8_t *xq = reinterpret_cast<int8_t *>(ab_smem + ab_al16((size_t)dim * 4));                              // [dim] quantized normed x
+    float *xd = reinterpret_cast<float *>(xq + ab_al16(dim));                       // [dim / 32] scales
+    int32_t *xs = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(xd) + ab_al16((size_t)dim / 32 * 4));
+    float *att_sm = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xs) + ab_al16((size_t)dim / 16 * 4));
+
+    // ---- P1: q/k/v rows ---------------------------------------------------------------
+    constexpr int SA = 4;
+    const int nbA = dim / QT<TA>::BE, nbV = dim / QT<TV>::BE;
+    const int gq = qd / SA, gk = kvd / SA, gv = kvd / SA;
+    const bool k256A = QT<TA>::BE == 256, k256V = QT<TV>::BE == 256;
+    int role = -1, r0 = 0;  // 0 q, 1 k, 2 v
+    if (gw < gq) role = 0, r0 = gw * SA;
+    else if (gw < gq + gk) role = 1, r0 = (gw - gq) * SA;
+    else if (gw < gq + gk + gv) role = 2, r0 = (gw - gq - gk) * SA;
+    // q/k rows (and v rows of the same type) hold their fragments in registers
+    // across the norm; v rows of another type are prefetched into L2 and
+    // loaded after it (one fragment array live at a time)
+    constexpr bool same = TA == TV;
+    WFrags<TA, ab_maxu<TA>()> fa;
+    const XV xv{xq, xd, xs};
+    if (role == 0 || role == 1 || (same && role == 2)) {
+        const AbRows st{role == 0 ? A.wq : role == 1 ? A.wk : A.wv, r0, nbA, xv};
+        wd_load<TA, SA, ab_maxu<TA>()>(st, nbA, SA, fa, lane);
+    } else if (role == 2) {
+        const int be = block_elems(TV);
+        const uint64_t gb0 = (uint64_t)r0 * nbV, nblk = (uint64_t)SA * nbV;
+        const size_t qb = (size_t)layout_qbytes(TV);
+        const uint8_t *q0 = A.wv.q + gb0 * qb;
+        for (size_t off = (size_t)lane * 128; off < nblk * qb; off += 32 * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(q0 + off));
+        if (A.wv.sc && lane == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(A.wv.sc + gb0 * 16));
+        if (A.wv.d && lane == 1) asm volatile("prefetch.global.L2 [%0];" ::"l"(A.wv.d + gb0));
+        (void)be;
+    }
+    ab_rmsnorm(A.x, A.attn_norm, dim, A.eps, A.serial, sx, red);
+    // the rows reading per-256 activations first, then (one buffer) those reading per-32 ones
+    for (int pass = 0; pass < 2; pass++) {
+        const bool k256 = pass == 0;
+        if (k256 ? !(k256A || k256V) : (k256A && k256V)) continue;
+        __syncthreads();
+        ab_quant(sx, dim, k256, xq, xd, xs);
+        __syncthreads();
+        const bool mine = role >= 0 && ((role <= 1 && k256A == k256) || (role == 2 && k256V == k256));
+        if (mine) {
+            float acc[SA];
+            if (role <= 1 || same) {
+                const AbRows st{role == 0 ? A.wq : role == 1 ? A.wk : A.wv, r0, nbA, xv};
+                wd_finish<TA, SA, ab_maxu<TA>()>(st, nbA, SA, fa, acc, lane);
+            } else {
+                const AbRows st{A.wv, r0, nbV, xv};
+                WFrags<TV, ab_maxu<TV>()> fv;
+                wd_load<TV, SA, ab_maxu<TV>()>(st, nbV, SA, fv, lane);
+                wd_finish<TV, SA, ab_maxu<TV>()>(st, nbV, SA, fv, acc, lane);
+            }
+            float *dst = role == 0 ? A.q : role == 1 ? A.k : A.v;
+            if (lane == 0)
+#pragma unroll
+                for (int s = 0; s < SA; s++) dst[r0 + s] = acc[s];
+        }
+    }
+    if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
+    mark(1);
+
+    // ---- P2: head norm + RoPE + append -------------------------------------------------
+    for (int head = gw; head < nh + nkv && pos_ok; head += W) {
+        const bool isk = head >= nh;
+        const int kh = head - nh;
+        float *vec = isk ? A.k + (size_t)kh * hd : A.q + (size_t)head * hd;
+        const float *g = isk ? A.k_norm : A.q_norm;
+        float *hv = att_sm + warp * MAX_AB_HD;  // this warp's head, in shared memory
+        for (int i = lane; i < hd; i += 32) hv[i] = vec[i];
+        __syncwarp();
+        if (g) {  // headNorm (llama.zig:938): serial sum of squares, inv = 1 / sqrt(ss / hd + eps)
+            float inv = 0.0f;
+            if (lane == 0) {
+                float ss = 0.0f;
+                for (int i = 0; i < hd; i++) ss = fadd(ss, fmul(hv[i], hv[i]));
+                inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)hd), A.eps)));
+            }
+            inv = __shfl_sync(0xffffffffu, inv, 0);
+            for (int i = lane; i < hd; i += 32) hv[i] = fmul(fmul(hv[i], inv), g[i]);
+            __syncwarp();
+        }
+        for (int i = lane; i < hd; i += 32) vec[i] = hv[i];
+        __syncwarp();
+        const float *cs = A.rope + (size_t)pos * A.rope_dim;
+        const int half = A.rope_dim / 2;
+        for (int j = lane; j < half; j += 32) {
+            const int ia = A.neox ? j : 2 * j, ib = A.neox ? j + half : 2 * j + 1;
+            const float co = cs[2 * j], si = cs[2 * j + 1];
+            const float a = vec[ia], b = vec[ib];
+            vec[ia] = fsub(fmul(a, co), fmul(b, si));
+            vec[ib] = fadd(fmul(a, si), fmul(b, co));
+        }
+        __syncwarp();
+        if (isk) {
+            const size_t row = (size_t)pos * kvd + (size_t)kh * hd;
+            for (int i = lane; i < hd; i += 32) {
+                A.kc[row + i] = vec[i];
+                A.vc[row + i] = A.v[(size_t)kh * hd + i];
+            }
+        }
+    }
+    if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
+    mark(2);
+
+    // ---- P3: attention chunks ------------------------------------------------------------
+    if (pos_ok) {
+        const int grp = warp / AB_GRP_WARPS, gl = tid % (AB_GRP_WARPS * 32), gwarp = warp % AB_GRP_WARPS;
+        const int ngrp = A.groups;  // groups per CTA that fit in shared memory
+        const int KS = hd + 4;
+        const size_t per = (size_t)ATT_CH * KS + (size_t)ATT_CH * hd + (size_t)GQ * hd + (size_t)GQ * ATT_CH;
+        const int live = (pos + 1 + ATT_CH - 1) / ATT_CH, items = nkv * live;
+        if (grp < ngrp) {
+            float *sK = att_sm + grp * per, *sV = sK + ATT_CH * KS, *qs = sV + ATT_CH * hd, *sc = qs + GQ * hd;
+            for (int it = c * ngrp + grp; it < items; it += G * ngrp) {
+                const int g = it / live, sp = it % live;
+                const int t0 = sp * ATT_CH, n = min(ATT_CH, pos + 1 - t0);
+                const float *kb = A.kc + (size_t)t0 * kvd + (size_t)g * hd;
+                const float *vb = A.vc + (size_t)t0 * kvd + (size_t)g * hd;
+                const int q4 = hd / 4;
+                for (int i = gl; i < n * q4; i += AB_GRP_WARPS * 32) {
+                    const int j = i / q4, c4 = (i % q4) * 4;
+                    ab_cp16(sK + j * KS + c4, kb + (size_t)j * kvd + c4);
+                    ab_cp16(sV + j * hd + c4, vb + (size_t)j * kvd + c4);
+                }
+                asm volatile("cp.async.commit_group;\n" ::: "memory");
+                for (int i = gl; i < GQ * hd; i += AB_GRP_WARPS * 32) qs[i] = A.q[(size_t)g * GQ * hd + i];
+                asm volatile("cp.async.wait_all;\n" ::: "memory");
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
+                const int HP = (GQ + 1) / 2;
+                for (int hp = gwarp; hp < HP; hp += AB_GRP_WARPS) {
+                    const int j = lane, ha = 2 * hp, hb = min(2 * hp + 1, GQ - 1);
+                    if (j < n) {
+                        const float *kr = sK + j * KS, *qa = qs + ha * hd, *qb = qs + hb * hd;
+                        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+                        for (int d = 0; d < hd; d += 4) {
+                            const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+                            const float4 x4 = *reinterpret_cast<const float4 *>(qa + d);
+                            const float4 y4 = *reinterpret_cast<const float4 *>(qb + d);
+                            a0 = fmaf(k4.x, x4.x, a0); a1 = fmaf(k4.y, x4.y, a1);
+                            a0 = fmaf(k4.z, x4.z, a0); a1 = fmaf(k4.w, x4.w, a1);
+                            b0 = fmaf(k4.x, y4.x, b0); b1 = fmaf(k4.y, y4.y, b1);
+                            b0 = fmaf(k4.z, y4.z, b0); b1 = fmaf(k4.w, y4.w, b1);
+                        }
+                        sc[ha * ATT_CH + j] = (a0 + a1) * A.scale;
+                        sc[hb * ATT_CH + j] = (b0 + b1) * A.scale;
+                    }
+                }
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
+                float *rec = A.part + ((size_t)g * A.nsplit + sp) * GQ * (hd + 2);
+                for (int hh = gwarp; hh < GQ; hh += AB_GRP_WARPS) {
+                    const float v = lane < n ? sc[hh * ATT_CH + lane] : -INFINITY;
+                    const float m = warp_max(v);
+                    const float e = lane < n ? exp_f(v - m) : 0.0f;
+                    if (lane < n) sc[hh * ATT_CH + lane] = e;
+                    const float l = ab_warp_sum(e);
+                    if (lane == 0) {
+                        rec[hh * (hd + 2) + hd] = m;
+                        rec[hh * (hd + 2) + hd + 1] = l;
+                    }
+                }
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
+                for (int d = gl; d < hd; d += AB_GRP_WARPS * 32) {
+                    float acc[16];
+#pragma unroll
+                    for (int hh = 0; hh < 16; hh++) acc[hh] = 0.0f;
+                    for (int j = 0; j < n; j++) {
+                        const float vv = sV[j * hd + d];
+#pragma unroll
+                        for (int hh = 0; hh < 16; hh++)
+                            if (hh < GQ) acc[hh] = fmaf(sc[hh * ATT_CH + j], vv, acc[hh]);
+                    }
+#pragma unroll
+                    for (int hh = 0; hh < 16; hh++)
+                        if (hh < GQ) rec[hh * (hd + 2) + d] = acc[hh];
+                }
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
+            }
+        }
+    }
+    if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
+    mark(3);
+
+    {
+        // ---- P4: output-projection loads, merge + quantization ----------------------------
+        const int nbO = qd / QT<TO>::BE, go = dim / SO;
+        const bool ow = gw < go;
+        const int ro = gw * SO;
+        WFrags<TO, ab_maxu<TO>()> fo;
+        const XV av{A.aq, A.ad, A.as};
+        if (ow) {
+            const AbRows st{A.wo, ro, nbO, av};
+            wd_load<TO, SO, ab_maxu<TO>()>(st, nbO, SO, fo, lane);
+        }
+        const bool k256O = QT<TO>::BE == 256;
+        if (pos_ok && c < (qd + 255) / 256) {
+            const int live = (pos + 1 + ATT_CH - 1) / ATT_CH;
+            const size_t stride = (size_t)GQ * (hd + 2);
+            const int e0 = c * 256, h0 = e0 / hd, h1 = min((e0 + 255) / hd, nh - 1);
+            float *wsm = att_sm;                       // [heads][live]
+            float *val = att_sm + (h1 - h0 + 1) * live;  // [256]
+            for (int lh = warp; lh <= h1 - h0; lh += AB_WARPS) {
+                const int h = h0 + lh, g = h / GQ, hh = h % GQ;
+                const float *rec = A.part + (size_t)g * A.nsplit * stride + (size_t)hh * (hd + 2);
+                float *w = wsm + lh * live;
+                float M = -INFINITY;
+                for (int s = lane; s < live; s += 32) M = fmaxf(M, rec[s * stride + hd]);
+                M = warp_max(M);
+                float L = 0.0f;
+                for (int s = lane; s < live; s += 32) {
+                    const float ws = exp_f(rec[s * stride + hd] - M);
+                    w[s] = ws;
+                    L = fmaf(rec[s * stride + hd + 1], ws, L);
+                }
+                L = ab_warp_sum(L);
+                if (lane == 0) Ls[lh] = L;
+            }
+            __syncthreads();
+            if (tid < 256) {
+                const int e = e0 + tid;
+                float o = 0.0f;
+                if (e < qd) {
+                    const int h = e / hd, d = e % hd, g = h / GQ, hh = h % GQ, lh = h - h0;
+                    const float *rec = A.part + (size_t)g * A.nsplit * stride + (size_t)hh * (hd + 2) + d;
+                    const float *w = wsm + lh * live;
+#pragma unroll 8
+                    for (int s = 0; s < live; s++) o = fmaf(rec[s * stride], w[s], o);
+                    o = o / Ls[lh];
+                }
+                val[tid] = o;
+            }
+            __syncthreads();
+            if (warp == 0) {
+                if (k256O) {
+                    const int off = lane * 8;
+                    quant_lane8(val + off, true, 32, A.aq + e0 + off, A.ad + c, A.as + e0 / 16 + lane / 2, nullptr,
+                                lane);
+                } else {
+                    const int b = e0 / 32 + lane / 4, nb = qd / 32;
+                    const bool lb = b < nb;
+                    const int off = (lane / 4) * 32 + (lane & 3) * 8;
+                    quant_lane8(val + (lb ? off : 0), lb, 4, A.aq + e0 + off, A.ad + b, nullptr, A.as + b, lane);
+                }
+            }
+        }
+        if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
+    mark(4);
+
+        // ---- P5: output projection + residual ------------------------------------------
+        if (ow) {
+            float acc[SO];
+            const AbRows st{A.wo, ro, nbO, av};
+            wd_finish<TO, SO, ab_maxu<TO>()>(st, nbO, SO, fo, acc, lane);
+            if (lane == 0)
+#pragma unroll
+                for (int s = 0; s < SO; s++)
+                    if (ro + s < dim) A.x[ro + s] = fadd(A.x[ro + s], acc[s]);  // llama.zig:1195 add
+        }
+    }
+    if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
+    mark(5);
+
+    // ---- P6: FFN RMSNorm -> the MoE layer's input ----------------------------------------
+    if (c == 0) {
+        ab_rmsnorm(A.x, A.ffn_norm, dim, A.eps, A.serial, sx, red);
+        for (int i = tid; i < dim; i += AB_THREADS) A.normed[i] = sx[i];
+    }
+out:
+    mark(7);
+    __syncthreads();
+    if (tid == 0) {  // the last CTA out advances the epoch (counters stay consistent only without errors)
+        __threadfence();
+        unsigned *ex = ep + 1;
+        if (atomicAdd(ex, 1u) == (unsigned)G - 1) {
+            *ex = 0;
+            __threadfence();
+            atomicAdd(ep, 1u);
+        }
+    }
+}
+
+using AbFn = void (*)(AttnBlockArgs);
+
+template <int TA, int TV, int TO> AbFn ab_pick(int so) {
+    return so == 4 ? k_attn_block<TA, TV, TO, 4> : so == 2 ? k_attn_block<TA, TV, TO, 2> : k_attn_block<TA, TV, TO, 1>;
+}
+
+AbFn ab_fn(int ta, int tv, int to, int so) {
+    if (ta == T_Q4_K && tv == T_Q6_K && to == T_Q4_K) return ab_pick<T_Q4_K, T_Q6_K, T_Q4_K>(so);
+    if (ta == T_Q4_K && tv == T_Q4_K && to == T_Q4_K) return ab_pick<T_Q4_K, T_Q4_K, T_Q4_K>(so);
+    if (ta == T_Q4_0 && tv == T_Q4_0 && to == T_Q4_0) return ab_pick<T_Q4_0, T_Q4_0, T_Q4_0>(so);
+    if (ta == T_Q8_0 && tv == T_Q8_0 && to == T_Q8_0) return ab_pick<T_Q8_0, T_Q8_0, T_Q8_0>(so);
+    return nullptr;
+}
+
+int ab_units(int t) { return t == T_Q4_K ? 32 : t == T_Q6_K ? 32 : t == T_Q8_0 ? 64 : t == T_Q4_0 ? 64 : 0; }
+
+int ab_so(int to, int qd) {  // output-projection rows per warp
+    const int nb = qd / block_elems(to), u = ab_units(to);
+    return nb * 4 <= u ? 4 : nb * 2 <= u ? 2 : nb <= u ? 1 : 0;
+}
+
+size_t ab_fixed_smem(int dim) {
+    return ab_al16((size_t)dim * 4) + ab_al16(dim) + ab_al16((size_t)dim / 32 * 4) + ab_al16((size_t)dim / 16 * 4);
+}
+
+int sm_count_ab() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+}  // namespace
+
+int attn_block_plan(AttnBlockArgs &A, int ta, int tk, int tv, int to, size_t ctx) {
+    if (ta != tk) return 0;
+    const int qd = A.n_heads * A.hd, kvd = A.n_kv * A.hd, GQ = A.n_heads / A.n_kv;
+    const int so = ab_so(to, qd);
+    if (!ab_fn(ta, tv, to, so) || so == 0) return 0;
+    if (A.hd % 4 || A.hd > MAX_AB_HD || GQ > 16 || qd % 4 || kvd % 4 || A.dim % 4) return 0;
+    if (A.dim % block_elems(ta) || A.dim % block_elems(tv) || qd % block_elems(to)) return 0;
+    if ((A.dim / block_elems(ta)) * 4 > ab_units(ta) || (A.dim / block_elems(tv)) * 4 > ab_units(tv)) return 0;
+    if (block_elems(to) == 256 && qd % 256) return 0;
+    const int G = sm_count_ab();
+    if ((qd + 2 * kvd) / 4 > G * AB_WARPS || A.dim / so > G * AB_WARPS || A.n_heads + A.n_kv > G * AB_WARPS) return 0;
+    if ((qd + 255) / 256 > G) return 0;
+    const size_t per = ((size_t)ATT_CH * (A.hd + 4) + (size_t)ATT_CH * A.hd + (size_t)GQ * A.hd + (size_t)GQ * ATT_CH) * 4;
+    const size_t nsplit = (ctx + ATT_CH - 1) / ATT_CH;
+    const size_t merge = ((size_t)(256 / A.hd + 2) * nsplit + 256) * 4;
+    const size_t budget = 220 * 1024 - ab_fixed_smem(A.dim);
+    int groups = (int)std::min<size_t>(AB_WARPS / AB_GRP_WARPS, budget / per);
+    if (groups < 1 || merge > budget) return 0;
+    A.groups = groups;
+    A.smem = ab_fixed_smem(A.dim) + std::max(std::max((size_t)groups * per, merge), (size_t)AB_WARPS * MAX_AB_HD * 4);
+    A.so = so;
+    A.ta = ta;
+    A.tv = tv;
+    A.to = to;
+    return 1;
+}
+
+cudaError_t launch_attn_block(const AttnBlockArgs &A, cudaStream_t st) {
+    AbFn fn = ab_fn(A.ta, A.tv, A.to, A.so);
+    if (!fn) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A.smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, AB_THREADS, A.smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sm_count_ab());
+    cfg.blockDim = dim3(AB_THREADS);
+    cfg.dynamicSmemBytes = A.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, fn, A);
+}
+
+}  // namespace loom

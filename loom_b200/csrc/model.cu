@@ -19,12 +19,16 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <unordered_map>
 #include <vector>
 
 #include "../../include/loom_cuda.h"
 #include "attn.cuh"
+#include "attn_block.cuh"
+#include "gemv.cuh"
 #include "kernels.cuh"
 
 namespace loom {
@@ -58,6 +62,8 @@ struct LayerRt {
     Mat wq, wk, wv, wo;
     loom_moe_desc moe{};
     bool dense = false;
+    bool fused = false;       // the attention half runs as one cooperative launch (attn_block.cu)
+    AttnBlockArgs blk{};
 };
 
 struct Model {
@@ -75,6 +81,7 @@ struct Model {
     float *x[2] = {nullptr, nullptr}, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
           *proj = nullptr, *part = nullptr, *logits = nullptr, *zero_logit = nullptr;
     XQW n256{}, n32{}, a256{}, a32{};
+    unsigned long long *ab_bar = nullptr;  // grid-barrier state of the fused attention kernel
     uint32_t *io_dev = nullptr;   // token, pos, next (graph path)
     uint32_t *io_host = nullptr;  // pinned mirror
     float *h_logits = nullptr;    // pinned
@@ -146,12 +153,13 @@ void matvec(const Mat &m, const float *xf, const XQW &x256, const XQW &x32, floa
         launch_mm_f32(reinterpret_cast<const float *>(m.w.q), m.rows, m.cols, xf, 1, out, st);
     } else if (m.type == T_Q5_0) {
         launch_mm_q50(m.w, 0, m.rows, m.cols, xf, 1, out, st);
-    } else if (act256(m.type)) {
-        XQ x{x256.q, x256.d, x256.s, m.cols, m.cols / 256, m.cols / 16, 1};
-        launch_mm(m.w, 0, m.rows, m.cols, x, 1, out, st);
     } else {
-        XQ x{x32.q, x32.d, x32.s, m.cols, m.cols / 32, m.cols / 32, 0};
-        launch_mm(m.w, 0, m.rows, m.cols, x, 1, out, st);
+        const XQ x = act256(m.type) ? XQ{x256.q, x256.d, x256.s, m.cols, m.cols / 256, m.cols / 16, 1}
+                                    : XQ{x32.q, x32.d, x32.s, m.cols, m.cols / 32, m.cols / 32, 0};
+        if (gemv_supported(m.type, m.cols))
+            launch_gemv(m.w, m.rows, m.cols, x, out, st);  // warp engine, weights loaded ahead of the wait
+        else
+            launch_mm(m.w, 0, m.rows, m.cols, x, 1, out, st);
     }
 }
 
@@ -171,6 +179,18 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
     for (size_t li = 0; li < m.n_layers; li++) {
         const LayerRt &l = m.L[li];
         float *x = m.x[cur];
+        if (l.fused) {  // one cooperative launch: norm, q/k/v, RoPE, attention, output projection, FFN norm
+            AttnBlockArgs a = l.blk;
+            a.x = x;
+            a.pos = pos;
+            MCK(launch_attn_block(a, st));
+            float *xn = m.x[cur ^ 1];
+            if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr,
+                                               st))
+                return rc;
+            cur ^= 1;
+            continue;
+        }
         launch_rmsnorm_q(x, nullptr, l.attn_norm, dim, m.eps, m.normed, m.need256 ? m.n256 : none,
                          m.need32 ? m.n32 : none, m.serial_norm, st);
         matvec(l.wq, m.normed, m.n256, m.n32, m.q, st);
@@ -179,9 +199,12 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
         float *kc = m.kc + li * layer_stride, *vc = m.vc + li * layer_stride;
         launch_qk_rope(m.q, m.k, m.v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps, pos,
                        (int)m.ctx, kc, vc, st);
-        launch_attention(m.q, kc, vc, nh, nkv, hd, m.scale, pos, (int)m.ctx, m.part, m.att, m.ordered_attn, st);
-        if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
-            const bool k256 = act256(l.wo.type);
+        const bool wq_kind = l.wo.type != T_F32 && l.wo.type != T_Q5_0;
+        const bool k256 = wq_kind && act256(l.wo.type);
+        const bool fused_q = wq_kind && !m.ordered_attn && attn_merge_quantizes(nh, hd, (int)m.ctx);
+        launch_attention(m.q, kc, vc, nh, nkv, hd, m.scale, pos, (int)m.ctx, m.part, m.att, m.ordered_attn,
+                         fused_q && k256 ? m.a256 : none, fused_q && !k256 ? m.a32 : none, st);
+        if (wq_kind && !fused_q) {
             const XQW &a = k256 ? m.a256 : m.a32;
             launch_quant_act(m.att, 1, qd, qd, k256, a.q, a.d, a.s, k256 ? qd / 256 : qd / 32,
                              k256 ? qd / 16 : qd / 32, st);
@@ -245,9 +268,16 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         return rt_decline("empty model shape");
     if (d->n_heads % d->n_kv_heads || d->n_heads / d->n_kv_heads > 16)
         return rt_decline("n_heads must be a multiple of n_kv_heads, at most 16 query heads per KV head");
-    if (d->head_dim == 0 || d->head_dim % 2 || d->head_dim > 256) return rt_decline("head_dim must be even and <= 256");
+    if (d->head_dim < 8 || d->head_dim % 2 || d->head_dim > 256)
+        return rt_decline("head_dim must be even, >= 8 and <= 256");
     if (d->rope_dim > d->head_dim || d->rope_dim % 2) return rt_decline("rope_dim must be even and <= head_dim");
-    if (d->dim > 16384 || d->ctx_len > (1u << 20) || d->vocab > 0x7FFFFFFFu) return rt_decline("model shape too large");
+    if (d->dim > 16384 || d->ctx_len > (1u << 18) || d->vocab > 0x7FFFFFFFu) return rt_decline("model shape too large");
+    {  // the split attention's merge keeps (256 / hd + 1) x chunks weights in shared memory
+        const size_t hpc = std::min<size_t>(256 / d->head_dim + 1, d->n_heads);
+        const size_t nsplit = (d->ctx_len + ATT_CH - 1) / ATT_CH;
+        if (!d->exact_order && d->ctx_len > (size_t)ATT_ORDERED_MAX && hpc * nsplit * 4 > 200 * 1024)
+            return rt_decline("context too long for this head_dim");
+    }
     Model *m = new Model();
     auto bail = [&](int rc) {
         free_model(m);
@@ -335,6 +365,47 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         (rc = alloc_xq(*m, m->n32, dim, false)) || (rc = alloc_xq(*m, m->a256, qd, true)) ||
         (rc = alloc_xq(*m, m->a32, qd, false)))
         return bail(rc);
+    if ((rc = dalloc(*m, m->ab_bar, 16, true))) return bail(rc);
+    if (!m->ordered_attn && !getenv("LOOM_CUDA_NO_ATTN_BLOCK")) {
+        for (size_t li = 0; li < d->n_layers; li++) {
+            LayerRt &l = m->L[li];
+            AttnBlockArgs &a = l.blk;
+            a.normed = m->normed;
+            a.attn_norm = l.attn_norm;
+            a.ffn_norm = l.ffn_norm;
+            a.q_norm = l.qn;
+            a.k_norm = l.kn;
+            a.eps = m->eps;
+            a.serial = m->serial_norm;
+            a.wq = l.wq.w;
+            a.wk = l.wk.w;
+            a.wv = l.wv.w;
+            a.wo = l.wo.w;
+            a.dim = (int)dim;
+            a.n_heads = (int)m->nh;
+            a.n_kv = (int)m->nkv;
+            a.hd = (int)m->hd;
+            a.rope_dim = (int)m->rope_dim;
+            a.neox = m->neox;
+            a.rope = m->rope;
+            a.scale = m->scale;
+            a.ctx = (int)m->ctx;
+            a.kc = m->kc + li * d->ctx_len * kvd;
+            a.vc = m->vc + li * d->ctx_len * kvd;
+            a.q = m->q;
+            a.k = m->k;
+            a.v = m->v;
+            a.part = m->part;
+            a.nsplit = (int)((m->ctx + ATT_CH - 1) / ATT_CH);
+            const bool o256 = act256(l.wo.type);
+            a.aq = o256 ? m->a256.q : m->a32.q;
+            a.ad = o256 ? m->a256.d : m->a32.d;
+            a.as = o256 ? m->a256.s : m->a32.s;
+            a.bar = m->ab_bar;
+            a.trace = li == 1 && getenv("LOOM_CUDA_AB_TRACE") ? m->ab_bar + 4 : nullptr;  // diagnostic
+            l.fused = attn_block_plan(a, l.wq.type, l.wk.type, l.wv.type, l.wo.type, m->ctx) != 0;
+        }
+    }
     if (d->rope_dim) {
         const std::vector<float> tab = rope_table(d->ctx_len, d->rope_dim, d->rope_base);
         cudaError_t e = cudaMemcpy(m->rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
@@ -419,6 +490,23 @@ int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k,
     if (k) MCK(cudaMemcpy(k, m->kc + off, kvd * 4, cudaMemcpyDeviceToHost));
     if (v) MCK(cudaMemcpy(v, m->vc + off, kvd * 4, cudaMemcpyDeviceToHost));
     return LOOM_CUDA_OK;
+}
+
+int loom_cuda_model_error(uint64_t handle) {
+    Model *m = find(handle);
+    if (!m) return -1;
+    if (cudaStreamSynchronize(rt_stream(nullptr)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return -1;
+    unsigned long long h[4] = {};
+    if (cudaMemcpy(h, m->ab_bar, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (getenv("LOOM_CUDA_AB_TRACE")) {  // diagnostic: phase times of layer 1's fused attention kernel
+        unsigned long long t[8];
+        if (cudaMemcpy(t, m->ab_bar + 4, sizeof t, cudaMemcpyDeviceToHost) == cudaSuccess)
+            fprintf(stderr, "attn_block phases (ns from start): %llu %llu %llu %llu %llu %llu %llu\n", t[1] - t[0],
+                    t[2] - t[0], t[3] - t[0], t[4] - t[0], t[5] - t[0], t[6] - t[0], t[7] - t[0]);
+    }
+    const int e = (int)(unsigned)h[2];
+    if (e && cudaMemset(m->ab_bar, 0, sizeof h) != cudaSuccess) return -1;  // re-arm the barrier counters
+    return e;
 }
 
 int loom_cuda_model_free(uint64_t handle) {

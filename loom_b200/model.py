@@ -216,6 +216,10 @@ class DeviceModel:
                                                      v.ctypes.data_as(C.c_void_p)), "model_read_kv")
         return k, v
 
+    def error(self) -> int:
+        """The fused attention kernel's error word (0: none); re-arms after an error."""
+        return int(_lib.lib().loom_cuda_model_error(self.handle))
+
     def free(self) -> None:
         if self.handle:
             _lib.lib().loom_cuda_model_free(self.handle)

@@ -72,6 +72,7 @@ def test_model_logits_match_oracle_over_positions(be, orc, spec, exact, tol):
             top = np.sort(want)[-2:]
             if top[1] - top[0] > 50 * tol * max(1.0, abs(top[1])):
                 assert nxt == int(np.argmax(want)), pos
+        assert dev.error() == 0
     finally:
         dev.free()
 
@@ -116,3 +117,25 @@ def test_model_declines_bad_arguments(be):
         assert L.loom_cuda_model_decode(dev.handle + 999, 1, 0, None, C.byref(nxt)) == _lib.DECLINED
     finally:
         dev.free()
+
+
+def test_fused_attention_block_equals_separate_kernels(be, monkeypatch):
+    """The cooperative attention kernel (one launch per layer) against the
+    separate kernels on the same weights, over positions that cross several
+    attention chunks. The two RMSNorm trees (dim 2048) round differently, which
+    can move an int8 activation: logits within the fast form's 2e-2."""
+    spec = qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096)
+    a = DeviceModel(spec)
+    monkeypatch.setenv("LOOM_CUDA_NO_ATTN_BLOCK", "1")
+    b = DeviceModel(spec)
+    try:
+        rng = np.random.default_rng(3)
+        for pos in range(100):
+            tok = int(rng.integers(0, spec.vocab))
+            na, la = a.decode(tok, pos, logits=True)
+            nb, lb = b.decode(tok, pos, logits=True)
+            assert rel_l2(la, lb) < 2e-2, (pos, rel_l2(la, lb))
+        assert a.error() == 0
+    finally:
+        a.free()
+        b.free()
