@@ -24,6 +24,7 @@
 #include "attn.cuh"
 #include "attn_block.cuh"
 #include "devutil.cuh"
+#include "tma.cuh"
 #include "warpdot.cuh"
 
 #include <algorithm>
@@ -51,7 +52,10 @@ __device__ __forceinline__ float ab_warp_sum(float v) {
     return v;
 }
 
-// bar[0]: u64 arrival counter; bar[1]: (u32 epoch, u32 exit count); bar[2]: u32 error word
+// bar[0]: u64 arrival counter; bar[1]: (u32 epoch, u32 exit count); bar[2]: u32 error word.
+// Each CTA adds one arrival (release) and polls until the counter reaches the
+// barrier's target (acquire); ~1.2 us for 148 CTAs on B200 (measured; a
+// variant with a separate release flag written by the last arriver was slower).
 __device__ __forceinline__ bool ab_barrier(unsigned long long *ctr, unsigned long long target, unsigned *err) {
     __shared__ int s_ok;
     __syncthreads();
@@ -99,6 +103,8 @@ struct AbRows {
 };
 
 __host__ __device__ constexpr size_t ab_al16(size_t n) { return (n + 15) & ~size_t(15); }
+__host__ __device__ constexpr size_t ab_al128(size_t n) { return (n + 127) & ~size_t(127); }
+constexpr uint32_t STAGE_POLLS_AB = 1u << 22;  // bounded wait on the staged rows
 
 template <int TY> constexpr int ab_maxu() { return TY == T_Q4_K ? 8 : TY == T_Q6_K ? 4 : TY == T_Q8_0 ? 4 : 2; }
 
@@ -155,11 +161,91 @@ __device__ void ab_quant(const float *sx, int n, bool k256, int8_t *q, float *d,
     }
 }
 
+// A matrix's rows [ra, rb) staged in shared memory in the device layout's
+// regions (quants / Q4_K blocks, Q6_K scales, f16 scales); block gb of the
+// slice is global block ra * nb + gb.
+struct AbStage {
+    const uint8_t *q, *sc;
+    const uint16_t *d;
+    int ra, rb, nb;
+};
+
+__device__ __forceinline__ uint4 ab_ld16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+
+// the fragment QT<TY>::load reads from global memory, read from a staged slice
+template <int TY> __device__ __forceinline__ typename QT<TY>::Frag ab_frag(const AbStage &s, int gb, int sub);
+template <> __device__ __forceinline__ QT<T_Q4_K>::Frag ab_frag<T_Q4_K>(const AbStage &s, int gb, int sub) {
+    const uint8_t *blk = s.q + (size_t)gb * 144;
+    return QT<T_Q4_K>::Frag{ab_ld16(blk), ab_ld16(blk + 16 + 16 * sub)};
+}
+template <> __device__ __forceinline__ QT<T_Q6_K>::Frag ab_frag<T_Q6_K>(const AbStage &s, int gb, int sub) {
+    const int n = sub >> 1, hh = sub & 1;
+    const uint8_t *qb = s.q + (size_t)gb * 192;
+    QT<T_Q6_K>::Frag f;
+    f.a = ab_ld16(qb + 64 * n + 16 * hh);
+    f.b = ab_ld16(qb + 64 * n + 32 + 16 * hh);
+    f.h = ab_ld16(qb + 128 + 32 * n + 16 * hh);
+    f.s = ab_ld16(s.sc + (size_t)gb * 16);
+    f.d = s.d[gb];
+    return f;
+}
+template <> __device__ __forceinline__ QT<T_Q8_0>::Frag ab_frag<T_Q8_0>(const AbStage &s, int gb, int sub) {
+    return QT<T_Q8_0>::Frag{ab_ld16(s.q + (size_t)gb * 32 + 16 * sub), (uint32_t)s.d[gb]};
+}
+template <> __device__ __forceinline__ QT<T_Q4_0>::Frag ab_frag<T_Q4_0>(const AbStage &s, int gb, int) {
+    return QT<T_Q4_0>::Frag{ab_ld16(s.q + (size_t)gb * 16), (uint32_t)s.d[gb]};
+}
+
+// rows [r0, r0 + nS) of a staged slice (r0 local) against activations xv:
+// the warp engine's unit order (wd_load) and finish (wd_finish)
+template <int TY, int S>
+__device__ __forceinline__ void ab_rows(const AbStage &st, int r0, int nS, const XV &xv, float (&acc)[S], int lane) {
+    using Q = QT<TY>;
+    constexpr int MAXU = ab_maxu<TY>(), GG = 32 / Q::LPB;
+    const int NB = st.nb, U = nS * NB, grp = lane / Q::LPB, sub = lane % Q::LPB;
+    WFrags<TY, MAXU> fr;
+#pragma unroll
+    for (int j = 0; j < MAXU; j++) {
+        const int u = j * GG + grp;
+        if (u < U) {
+            const int s2 = u / NB, b = u - s2 * NB;
+            fr.f[j] = ab_frag<TY>(st, (r0 + s2) * NB + b, sub);
+        }
+    }
+    const AbRows rows{WDev{}, 0, NB, xv};
+    wd_finish<TY, S, MAXU>(rows, NB, nS, fr, acc, lane);
+}
+
+// Issue the staging of rows [ra, rb) of w (nb blocks a row): the quant and
+// Q6_K-scale regions by bulk copies on mbarrier bar (returns their bytes; the
+// caller's expect_tx covers them), the f16 scales by this CTA's threads.
+__device__ __forceinline__ uint32_t ab_stage_bulk(const WDev &w, int ra, int rb, int nb, uint8_t *dq, uint8_t *dsc,
+                                                  uint64_t *bar) {
+    const uint64_t gb0 = (uint64_t)ra * nb, n = (uint64_t)(rb - ra) * nb;
+    const uint32_t qb = (uint32_t)layout_qbytes(w.type);
+    uint32_t bytes = 0;
+    if (n) {
+        bulk_g2s(dq, w.q + gb0 * qb, (uint32_t)(n * qb), bar);
+        bytes += (uint32_t)(n * qb);
+        if (w.sc) {
+            bulk_g2s(dsc, w.sc + gb0 * 16, (uint32_t)(n * 16), bar);
+            bytes += (uint32_t)(n * 16);
+        }
+    }
+    return bytes;
+}
+__device__ __forceinline__ void ab_stage_d(const WDev &w, int ra, int rb, int nb, uint16_t *dd) {
+    if (!w.d) return;
+    const uint64_t gb0 = (uint64_t)ra * nb, n = (uint64_t)(rb - ra) * nb;
+    for (uint64_t i = threadIdx.x; i < n; i += AB_THREADS) dd[i] = w.d[gb0 + i];
+}
+
 template <int TA, int TV, int TO, int SO>
 __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
-    extern __shared__ __align__(16) uint8_t ab_smem[];
+    extern __shared__ __align__(128) uint8_t ab_smem[];
     __shared__ float red[AB_WARPS];
     __shared__ float Ls[40];
+    __shared__ __align__(8) uint64_t mb[2];  // staged q/k/v rows, staged output-projection rows
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, c = blockIdx.x, gw = c * AB_WARPS + warp, W = G * AB_WARPS;
     const int dim = A.dim, nh = A.n_heads, nkv = A.n_kv, hd = A.hd, qd = nh * hd, kvd = nkv * hd;
@@ -179,94 +265,130 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     mark(0);
     const int pos = (int)*A.pos;
     const bool pos_ok = pos < A.ctx;
-    {  // every byte the layer will read from HBM, requested into L2 up front: the phases then
-       // wait on L2 round trips only, and HBM streams at full rate underneath them
-        const size_t gt = (size_t)c * AB_THREADS + tid, nt = (size_t)G * AB_THREADS;
-        const int qd0 = A.n_heads * A.hd, kvd0 = A.n_kv * A.hd;
-        ab_prefetch_w(A.wq, (uint64_t)qd0 * (A.dim / block_elems(TA)), gt, nt);
-        ab_prefetch_w(A.wk, (uint64_t)kvd0 * (A.dim / block_elems(TA)), gt, nt);
-        ab_prefetch_w(A.wv, (uint64_t)kvd0 * (A.dim / block_elems(TV)), gt, nt);
-        ab_prefetch_w(A.wo, (uint64_t)A.dim * (qd0 / block_elems(TO)), gt, nt);
-        if (pos_ok) {
-            ab_prefetch(A.kc, (size_t)pos * kvd0 * 4, gt, nt);
-            ab_prefetch(A.vc, (size_t)pos * kvd0 * 4, gt, nt);
-        }
-    }
 
-    // ---- shared memory map -----------------------------------------------------------
-    // (regions on 16-byte boundaries: ab_fixed_smem)
-    float *sx = reinterpret_cast<float *>(ab_smem);                                 // [dim] (norms)
-    int8_t *xq = reinterpret_cast<int8_t *>(ab_smem + ab_al16((size_t)dim * 4));                              // [dim] quantized normed x
-    float *xd = reinterpret_cast<float *>(xq + ab_al16(dim));                       // [dim / 32] scales
+    // ---- shared memory map (offsets from attn_block_plan, 128-byte aligned) -----------
+    float *sx = reinterpret_cast<float *>(ab_smem);
+    int8_t *xq = reinterpret_cast<int8_t *>(ab_smem + ab_al16((size_t)dim * 4));
+    float *xd = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xq) + ab_al16(dim));
     int32_t *xs = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(xd) + ab_al16((size_t)dim / 32 * 4));
-    float *att_sm = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xs) + ab_al16((size_t)dim / 16 * 4));
+    uint8_t *o_stage = ab_smem + A.off_o;       // output-projection rows (live until P5)
+    uint8_t *u_area = ab_smem + A.off_u;        // q/k/v rows (P1), then head scratch, attention, merge
+    float *att_sm = reinterpret_cast<float *>(u_area);
 
-    // ---- P1: q/k/v rows ---------------------------------------------------------------
-    constexpr int SA = 4;
-    const int nbA = dim / QT<TA>::BE, nbV = dim / QT<TV>::BE;
-    const int gq = qd / SA, gk = kvd / SA, gv = kvd / SA;
-    const bool k256A = QT<TA>::BE == 256, k256V = QT<TV>::BE == 256;
-    int role = -1, r0 = 0;  // 0 q, 1 k, 2 v
-    if (gw < gq) role = 0, r0 = gw * SA;
-    else if (gw < gq + gk) role = 1, r0 = (gw - gq) * SA;
-    else if (gw < gq + gk + gv) role = 2, r0 = (gw - gq - gk) * SA;
-    // q/k rows (and v rows of the same type) hold their fragments in registers
-    // across the norm; v rows of another type are prefetched into L2 and
-    // loaded after it (one fragment array live at a time)
-    constexpr bool same = TA == TV;
-    WFrags<TA, ab_maxu<TA>()> fa;
-    const XV xv{xq, xd, xs};
-    if (role == 0 || role == 1 || (same && role == 2)) {
-        const AbRows st{role == 0 ? A.wq : role == 1 ? A.wk : A.wv, r0, nbA, xv};
-        wd_load<TA, SA, ab_maxu<TA>()>(st, nbA, SA, fa, lane);
-    } else if (role == 2) {
-        const int be = block_elems(TV);
-        const uint64_t gb0 = (uint64_t)r0 * nbV, nblk = (uint64_t)SA * nbV;
-        const size_t qb = (size_t)layout_qbytes(TV);
-        const uint8_t *q0 = A.wv.q + gb0 * qb;
-        for (size_t off = (size_t)lane * 128; off < nblk * qb; off += 32 * 128)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(q0 + off));
-        if (A.wv.sc && lane == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(A.wv.sc + gb0 * 16));
-        if (A.wv.d && lane == 1) asm volatile("prefetch.global.L2 [%0];" ::"l"(A.wv.d + gb0));
-        (void)be;
+    // ---- this CTA's row slices -------------------------------------------------------
+    const int nbA = dim / QT<TA>::BE, nbV = dim / QT<TV>::BE, nbO = qd / QT<TO>::BE;
+    const int qa = qd * c / G, qb = qd * (c + 1) / G, ka = kvd * c / G, kb = kvd * (c + 1) / G;
+    const int oa = dim * c / G, ob = dim * (c + 1) / G;
+    AbStage sq, sk, sv, so;
+    {
+        uint8_t *p = u_area;
+        auto carve = [&](AbStage &st, const WDev &w, int ra, int rb, int nb) -> uint8_t * {
+            const size_t n = (size_t)(rb - ra) * nb;
+            st.ra = ra;
+            st.rb = rb;
+            st.nb = nb;
+            st.q = p;
+            p += ab_al128(n * layout_qbytes(w.type));
+            st.sc = p;
+            if (w.sc) p += ab_al128(n * 16);
+            st.d = reinterpret_cast<const uint16_t *>(p);
+            if (w.d) p += ab_al128(n * 2);
+            return p;
+        };
+        carve(sq, A.wq, qa, qb, nbA);
+        carve(sk, A.wk, ka, kb, nbA);
+        carve(sv, A.wv, ka, kb, nbV);
+        p = o_stage;
+        carve(so, A.wo, oa, ob, nbO);
     }
-    ab_rmsnorm(A.x, A.attn_norm, dim, A.eps, A.serial, sx, red);
-    // the rows reading per-256 activations first, then (one buffer) those reading per-32 ones
-    for (int pass = 0; pass < 2; pass++) {
-        const bool k256 = pass == 0;
-        if (k256 ? !(k256A || k256V) : (k256A && k256V)) continue;
-        __syncthreads();
-        ab_quant(sx, dim, k256, xq, xd, xs);
-        __syncthreads();
-        const bool mine = role >= 0 && ((role <= 1 && k256A == k256) || (role == 2 && k256V == k256));
-        if (mine) {
-            float acc[SA];
-            if (role <= 1 || same) {
-                const AbRows st{role == 0 ? A.wq : role == 1 ? A.wk : A.wv, r0, nbA, xv};
-                wd_finish<TA, SA, ab_maxu<TA>()>(st, nbA, SA, fa, acc, lane);
-            } else {
-                const AbRows st{A.wv, r0, nbV, xv};
-                WFrags<TV, ab_maxu<TV>()> fv;
-                wd_load<TV, SA, ab_maxu<TV>()>(st, nbV, SA, fv, lane);
-                wd_finish<TV, SA, ab_maxu<TV>()>(st, nbV, SA, fv, acc, lane);
-            }
-            float *dst = role == 0 ? A.q : role == 1 ? A.k : A.v;
-            if (lane == 0)
+    if (tid == 0) {  // every weight byte of the layer this CTA needs, in flight at once
+        mbar_init(&mb[0], 1);
+        mbar_init(&mb[1], 1);
+        const uint32_t bq = (uint32_t)((size_t)(qb - qa) * nbA * layout_qbytes(TA) + (size_t)(kb - ka) * nbA * layout_qbytes(TA) +
+                                       (size_t)(kb - ka) * nbV * (layout_qbytes(TV) + (A.wv.sc ? 16 : 0)) +
+                                       (size_t)(qb - qa + kb - ka) * nbA * (A.wq.sc ? 16 : 0));
+        mbar_expect_tx(&mb[0], bq);
+        ab_stage_bulk(A.wq, qa, qb, nbA, const_cast<uint8_t *>(sq.q), const_cast<uint8_t *>(sq.sc), &mb[0]);
+        ab_stage_bulk(A.wk, ka, kb, nbA, const_cast<uint8_t *>(sk.q), const_cast<uint8_t *>(sk.sc), &mb[0]);
+        ab_stage_bulk(A.wv, ka, kb, nbV, const_cast<uint8_t *>(sv.q), const_cast<uint8_t *>(sv.sc), &mb[0]);
+        const uint32_t bo = (uint32_t)((size_t)(ob - oa) * nbO * (layout_qbytes(TO) + (A.wo.sc ? 16 : 0)));
+        mbar_expect_tx(&mb[1], bo);
+        ab_stage_bulk(A.wo, oa, ob, nbO, const_cast<uint8_t *>(so.q), const_cast<uint8_t *>(so.sc), &mb[1]);
+    }
+    ab_stage_d(A.wq, qa, qb, nbA, const_cast<uint16_t *>(sq.d));
+    ab_stage_d(A.wk, ka, kb, nbA, const_cast<uint16_t *>(sk.d));
+    ab_stage_d(A.wv, ka, kb, nbV, const_cast<uint16_t *>(sv.d));
+    ab_stage_d(A.wo, oa, ob, nbO, const_cast<uint16_t *>(so.d));
+    if (pos_ok) {  // this layer's cache rows, requested into L2 for the attention phase
+        const size_t gt = (size_t)c * AB_THREADS + tid, nt = (size_t)G * AB_THREADS;
+        ab_prefetch(A.kc, (size_t)pos * kvd * 4, gt, nt);
+        ab_prefetch(A.vc, (size_t)pos * kvd * 4, gt, nt);
+    }
+
+    // ---- P1: RMSNorm + quantization, then the q/k/v rows from shared memory ---------------
+    mark(8);
+    ab_rmsnorm(A.x, A.attn_norm, dim, A.eps, A.serial, sx, red);  // (its barriers publish mb init and d regions)
+    mark(9);
+    {
+        bool staged = mbar_wait(&mb[0], 0, STAGE_POLLS_AB);
+        if (!staged && lane == 0) atomicOr(err, 2u);
+        const bool k256A = QT<TA>::BE == 256, k256V = QT<TV>::BE == 256;
+        const XV xv{xq, xd, xs};
+        constexpr int SA = 4;
+        const int cq = (qb - qa + SA - 1) / SA, ck = (kb - ka + SA - 1) / SA;
+        const int nchunk = cq + 2 * ck;
+        for (int pass = 0; pass < 2; pass++) {
+            const bool k256 = pass == 0;
+            if (k256 ? !(k256A || k256V) : (k256A && k256V)) continue;
+            __syncthreads();
+            ab_quant(sx, dim, k256, xq, xd, xs);
+            __syncthreads();
+            for (int ch = warp; ch < nchunk && staged; ch += AB_WARPS) {
+                const int m = ch < cq ? 0 : ch < cq + ck ? 1 : 2;
+                const int lc = m == 0 ? ch : m == 1 ? ch - cq : ch - cq - ck;
+                const AbStage &st = m == 0 ? sq : m == 1 ? sk : sv;
+                if ((m <= 1 ? k256A : k256V) != k256) continue;
+                const int r0 = lc * SA, nS = min(SA, st.rb - st.ra - r0);
+                float acc[SA];
+                if (m <= 1)
+                    ab_rows<TA, SA>(st, r0, nS, xv, acc, lane);
+                else
+                    ab_rows<TV, SA>(st, r0, nS, xv, acc, lane);
+                float *dst = (m == 0 ? A.q : m == 1 ? A.k : A.v) + st.ra + r0;
+                if (lane == 0)
 #pragma unroll
-                for (int s = 0; s < SA; s++) dst[r0 + s] = acc[s];
+                    for (int s2 = 0; s2 < SA; s2++)
+                        if (s2 < nS) dst[s2] = acc[s2];
+            }
         }
     }
+    mark(10);
     if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
     mark(1);
 
-    // ---- P2: head norm + RoPE + append -------------------------------------------------
+    // ---- P2: head norm + RoPE + append (one warp per head, in shared memory) -------------
     for (int head = gw; head < nh + nkv && pos_ok; head += W) {
         const bool isk = head >= nh;
         const int kh = head - nh;
         float *vec = isk ? A.k + (size_t)kh * hd : A.q + (size_t)head * hd;
         const float *g = isk ? A.k_norm : A.q_norm;
-        float *hv = att_sm + warp * MAX_AB_HD;  // this warp's head, in shared memory
-        for (int i = lane; i < hd; i += 32) hv[i] = vec[i];
+        float *hv = att_sm + warp * MAX_AB_HD;
+        const float *cs = A.rope + (size_t)pos * A.rope_dim;
+        const int half = A.rope_dim / 2;
+        float cj[MAX_AB_HD / 64][2], vv[MAX_AB_HD / 32], gg[MAX_AB_HD / 32];
+#pragma unroll
+        for (int t = 0; t < MAX_AB_HD / 64; t++) {  // (cos, sin) of the pairs this lane rotates
+            const int j = lane + 32 * t;
+            cj[t][0] = j < half ? cs[2 * j] : 0.0f;
+            cj[t][1] = j < half ? cs[2 * j + 1] : 0.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < MAX_AB_HD / 32; t++) {
+            const int i = lane + 32 * t;
+            vv[t] = isk && i < hd ? A.v[(size_t)kh * hd + i] : 0.0f;
+            gg[t] = g && i < hd ? g[i] : 0.0f;
+            if (i < hd) hv[i] = vec[i];
+        }
         __syncwarp();
         if (g) {  // headNorm (llama.zig:938): serial sum of squares, inv = 1 / sqrt(ss / hd + eps)
             float inv = 0.0f;
@@ -276,28 +398,37 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
                 inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)hd), A.eps)));
             }
             inv = __shfl_sync(0xffffffffu, inv, 0);
-            for (int i = lane; i < hd; i += 32) hv[i] = fmul(fmul(hv[i], inv), g[i]);
+#pragma unroll
+            for (int t = 0; t < MAX_AB_HD / 32; t++) {
+                const int i = lane + 32 * t;
+                if (i < hd) hv[i] = fmul(fmul(hv[i], inv), gg[t]);
+            }
             __syncwarp();
         }
-        for (int i = lane; i < hd; i += 32) vec[i] = hv[i];
-        __syncwarp();
-        const float *cs = A.rope + (size_t)pos * A.rope_dim;
-        const int half = A.rope_dim / 2;
-        for (int j = lane; j < half; j += 32) {
-            const int ia = A.neox ? j : 2 * j, ib = A.neox ? j + half : 2 * j + 1;
-            const float co = cs[2 * j], si = cs[2 * j + 1];
-            const float a = vec[ia], b = vec[ib];
-            vec[ia] = fsub(fmul(a, co), fmul(b, si));
-            vec[ib] = fadd(fmul(a, si), fmul(b, co));
-        }
-        __syncwarp();
-        if (isk) {
-            const size_t row = (size_t)pos * kvd + (size_t)kh * hd;
-            for (int i = lane; i < hd; i += 32) {
-                A.kc[row + i] = vec[i];
-                A.vc[row + i] = A.v[(size_t)kh * hd + i];
+#pragma unroll
+        for (int t = 0; t < MAX_AB_HD / 64; t++) {  // RoPE (llama.zig:830-858) on the pairs
+            const int j = lane + 32 * t;
+            if (j < half) {
+                const int ia = A.neox ? j : 2 * j, ib = A.neox ? j + half : 2 * j + 1;
+                const float a = hv[ia], b = hv[ib];
+                hv[ia] = fsub(fmul(a, cj[t][0]), fmul(b, cj[t][1]));
+                hv[ib] = fadd(fmul(a, cj[t][1]), fmul(b, cj[t][0]));
             }
         }
+        __syncwarp();
+        const size_t row = (size_t)pos * kvd + (size_t)kh * hd;
+#pragma unroll
+        for (int t = 0; t < MAX_AB_HD / 32; t++) {
+            const int i = lane + 32 * t;
+            if (i < hd) {
+                vec[i] = hv[i];
+                if (isk) {  // llama.zig:1157-1159 cache append
+                    A.kc[row + i] = hv[i];
+                    A.vc[row + i] = vv[t];
+                }
+            }
+        }
+        __syncwarp();
     }
     if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
     mark(2);
@@ -381,35 +512,26 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     mark(3);
 
     {
-        // ---- P4: output-projection loads, merge + quantization ----------------------------
-        const int nbO = qd / QT<TO>::BE, go = dim / SO;
-        const bool ow = gw < go;
-        const int ro = gw * SO;
-        WFrags<TO, ab_maxu<TO>()> fo;
-        const XV av{A.aq, A.ad, A.as};
-        if (ow) {
-            const AbRows st{A.wo, ro, nbO, av};
-            wd_load<TO, SO, ab_maxu<TO>()>(st, nbO, SO, fo, lane);
-        }
+        // ---- P4: merge + quantization ----------------------------------------------------
         const bool k256O = QT<TO>::BE == 256;
         if (pos_ok && c < (qd + 255) / 256) {
             const int live = (pos + 1 + ATT_CH - 1) / ATT_CH;
             const size_t stride = (size_t)GQ * (hd + 2);
             const int e0 = c * 256, h0 = e0 / hd, h1 = min((e0 + 255) / hd, nh - 1);
-            float *wsm = att_sm;                       // [heads][live]
+            float *wsm = att_sm;                         // [heads][live]
             float *val = att_sm + (h1 - h0 + 1) * live;  // [256]
             for (int lh = warp; lh <= h1 - h0; lh += AB_WARPS) {
                 const int h = h0 + lh, g = h / GQ, hh = h % GQ;
                 const float *rec = A.part + (size_t)g * A.nsplit * stride + (size_t)hh * (hd + 2);
                 float *w = wsm + lh * live;
                 float M = -INFINITY;
-                for (int s = lane; s < live; s += 32) M = fmaxf(M, rec[s * stride + hd]);
+                for (int s2 = lane; s2 < live; s2 += 32) M = fmaxf(M, rec[s2 * stride + hd]);
                 M = warp_max(M);
                 float L = 0.0f;
-                for (int s = lane; s < live; s += 32) {
-                    const float ws = exp_f(rec[s * stride + hd] - M);
-                    w[s] = ws;
-                    L = fmaf(rec[s * stride + hd + 1], ws, L);
+                for (int s2 = lane; s2 < live; s2 += 32) {
+                    const float ws = exp_f(rec[s2 * stride + hd] - M);
+                    w[s2] = ws;
+                    L = fmaf(rec[s2 * stride + hd + 1], ws, L);
                 }
                 L = ab_warp_sum(L);
                 if (lane == 0) Ls[lh] = L;
@@ -422,8 +544,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
                     const int h = e / hd, d = e % hd, g = h / GQ, hh = h % GQ, lh = h - h0;
                     const float *rec = A.part + (size_t)g * A.nsplit * stride + (size_t)hh * (hd + 2) + d;
                     const float *w = wsm + lh * live;
-#pragma unroll 8
-                    for (int s = 0; s < live; s++) o = fmaf(rec[s * stride], w[s], o);
+#pragma unroll 32
+                    for (int s2 = 0; s2 < live; s2++) o = fmaf(rec[s2 * stride], w[s2], o);
                     o = o / Ls[lh];
                 }
                 val[tid] = o;
@@ -443,17 +565,21 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
             }
         }
         if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
-    mark(4);
+        mark(4);
 
-        // ---- P5: output projection + residual ------------------------------------------
-        if (ow) {
+        // ---- P5: output projection from the staged rows + residual ------------------------
+        const bool staged = mbar_wait(&mb[1], 0, STAGE_POLLS_AB);
+        if (!staged && lane == 0) atomicOr(err, 2u);
+        const XV av{A.aq, A.ad, A.as};
+        const int nco = (ob - oa + SO - 1) / SO;
+        for (int ch = warp; ch < nco && staged; ch += AB_WARPS) {
+            const int r0 = ch * SO, nS = min(SO, ob - oa - r0);
             float acc[SO];
-            const AbRows st{A.wo, ro, nbO, av};
-            wd_finish<TO, SO, ab_maxu<TO>()>(st, nbO, SO, fo, acc, lane);
+            ab_rows<TO, SO>(so, r0, nS, av, acc, lane);
             if (lane == 0)
 #pragma unroll
-                for (int s = 0; s < SO; s++)
-                    if (ro + s < dim) A.x[ro + s] = fadd(A.x[ro + s], acc[s]);  // llama.zig:1195 add
+                for (int s2 = 0; s2 < SO; s2++)
+                    if (s2 < nS) A.x[oa + r0 + s2] = fadd(A.x[oa + r0 + s2], acc[s2]);  // llama.zig:1195 add
         }
     }
     if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
@@ -512,6 +638,12 @@ int sm_count_ab() {
 
 }  // namespace
 
+// bytes a CTA's slice of `rows` rows (nb blocks each) of a type takes in the staging area
+static size_t ab_stage_bytes(int type, size_t rows, int nb, bool sc, bool d) {
+    const size_t n = rows * nb;
+    return ab_al128(n * layout_qbytes(type)) + (sc ? ab_al128(n * 16) : 0) + (d ? ab_al128(n * 2) : 0);
+}
+
 int attn_block_plan(AttnBlockArgs &A, int ta, int tk, int tv, int to, size_t ctx) {
     if (ta != tk) return 0;
     const int qd = A.n_heads * A.hd, kvd = A.n_kv * A.hd, GQ = A.n_heads / A.n_kv;
@@ -522,16 +654,27 @@ int attn_block_plan(AttnBlockArgs &A, int ta, int tk, int tv, int to, size_t ctx
     if ((A.dim / block_elems(ta)) * 4 > ab_units(ta) || (A.dim / block_elems(tv)) * 4 > ab_units(tv)) return 0;
     if (block_elems(to) == 256 && qd % 256) return 0;
     const int G = sm_count_ab();
-    if ((qd + 2 * kvd) / 4 > G * AB_WARPS || A.dim / so > G * AB_WARPS || A.n_heads + A.n_kv > G * AB_WARPS) return 0;
-    if ((qd + 255) / 256 > G) return 0;
+    if (A.n_heads + A.n_kv > G * AB_WARPS || (qd + 255) / 256 > G) return 0;
+    auto has_sc = [](int t) { return t == T_Q6_K; };
+    auto has_d = [](int t) { return t == T_Q6_K || t == T_Q8_0 || t == T_Q4_0; };
+    const int nbA = A.dim / block_elems(ta), nbV = A.dim / block_elems(tv), nbO = qd / block_elems(to);
+    const size_t rq = (qd + G - 1) / G, rk = (kvd + G - 1) / G, ro = (A.dim + G - 1) / G;
+    const size_t qkv = ab_stage_bytes(ta, rq, nbA, has_sc(ta), has_d(ta)) + ab_stage_bytes(ta, rk, nbA, has_sc(ta), has_d(ta)) +
+                       ab_stage_bytes(tv, rk, nbV, has_sc(tv), has_d(tv));
+    const size_t ost = ab_stage_bytes(to, ro, nbO, has_sc(to), has_d(to));
     const size_t per = ((size_t)ATT_CH * (A.hd + 4) + (size_t)ATT_CH * A.hd + (size_t)GQ * A.hd + (size_t)GQ * ATT_CH) * 4;
     const size_t nsplit = (ctx + ATT_CH - 1) / ATT_CH;
     const size_t merge = ((size_t)(256 / A.hd + 2) * nsplit + 256) * 4;
-    const size_t budget = 220 * 1024 - ab_fixed_smem(A.dim);
-    int groups = (int)std::min<size_t>(AB_WARPS / AB_GRP_WARPS, budget / per);
-    if (groups < 1 || merge > budget) return 0;
+    const size_t fixed = ab_al128(ab_fixed_smem(A.dim));
+    const size_t limit = 225 * 1024;
+    if (fixed + ost + std::max(qkv, merge) > limit) return 0;
+    const size_t room = limit - fixed - ost;
+    const int groups = (int)std::min<size_t>(AB_WARPS / AB_GRP_WARPS, room / per);
+    if (groups < 1) return 0;
     A.groups = groups;
-    A.smem = ab_fixed_smem(A.dim) + std::max(std::max((size_t)groups * per, merge), (size_t)AB_WARPS * MAX_AB_HD * 4);
+    A.off_o = fixed;
+    A.off_u = fixed + ost;
+    A.smem = A.off_u + std::max(std::max(qkv, (size_t)groups * per), std::max(merge, (size_t)AB_WARPS * MAX_AB_HD * 4));
     A.so = so;
     A.ta = ta;
     A.tv = tv;

@@ -31,7 +31,7 @@ struct AttnBlockArgs {
     unsigned long long *trace; // optional [8]: %globaltimer ns of CTA 0 at the phase boundaries (diagnostic)
     // set by attn_block_plan
     int groups, so, ta, tv, to;
-    size_t smem;
+    size_t smem, off_o, off_u;  // dynamic shared memory: total, staged output-projection rows, union area
 };
 
 // Fills the plan fields; 0 when the fused kernel does not take these types or
