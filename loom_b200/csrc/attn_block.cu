@@ -196,24 +196,46 @@ template <> __device__ __forceinline__ QT<T_Q4_0>::Frag ab_frag<T_Q4_0>(const Ab
     return QT<T_Q4_0>::Frag{ab_ld16(s.q + (size_t)gb * 16), (uint32_t)s.d[gb]};
 }
 
-// rows [r0, r0 + nS) of a staged slice (r0 local) against activations xv:
-// the warp engine's unit order (wd_load) and finish (wd_finish)
-template <int TY, int S>
-__device__ __forceinline__ void ab_rows(const AbStage &st, int r0, int nS, const XV &xv, float (&acc)[S], int lane) {
+// rows [r0, r0 + nS) of a staged slice (r0 local) against activations xv,
+// kept compact (no unrolling: this code runs once per launch, so instruction
+// fetch, not issue, sets its speed): per round each lane group forms one
+// unit's integer dot (QT<TY>::part, the warp engine's arithmetic) and its
+// float term into the warp's term buffer tsm (>= nS * nb floats); then lane s
+// adds stream s's block terms in block order from +0 (kBlockDot / matvecK256,
+// ggml.zig:1002-1042). Bit-identical to wd_load + wd_finish. acc[s] for
+// s < nS is valid in lane s.
+template <int TY>
+__device__ __noinline__ float ab_rows(const AbStage &st, int r0, int nS, const XV &xv, float *tsm, int lane) {
     using Q = QT<TY>;
-    constexpr int MAXU = ab_maxu<TY>(), GG = 32 / Q::LPB;
+    constexpr int GG = 32 / Q::LPB;
     const int NB = st.nb, U = nS * NB, grp = lane / Q::LPB, sub = lane % Q::LPB;
-    WFrags<TY, MAXU> fr;
-#pragma unroll
-    for (int j = 0; j < MAXU; j++) {
-        const int u = j * GG + grp;
+#pragma unroll 1
+    for (int u0 = 0; u0 < U; u0 += GG) {
+        const int u = u0 + grp;
+        int I = 0, M = 0;
+        float xdv = 0.0f;
+        typename Q::Frag f{};
         if (u < U) {
             const int s2 = u / NB, b = u - s2 * NB;
-            fr.f[j] = ab_frag<TY>(st, (r0 + s2) * NB + b, sub);
+            f = ab_frag<TY>(st, (r0 + s2) * NB + b, sub);
+            Q::part(f, sub, xv.q + b * Q::BE, xv.s + b * Q::SPB, I, M);
+            xdv = xv.d[b];
         }
+#pragma unroll
+        for (int o = 1; o < Q::LPB; o <<= 1) {
+            I += __shfl_xor_sync(0xffffffffu, I, o);
+            M += __shfl_xor_sync(0xffffffffu, M, o);
+        }
+        if (u < U && sub == 0) tsm[u] = Q::term(f, I, M, xdv);
     }
-    const AbRows rows{WDev{}, 0, NB, xv};
-    wd_finish<TY, S, MAXU>(rows, NB, nS, fr, acc, lane);
+    __syncwarp();
+    float a = 0.0f;
+    if (lane < nS) {
+#pragma unroll 1
+        for (int b = 0; b < NB; b++) a = fadd(b == 0 ? 0.0f : a, tsm[lane * NB + b]);  // from +0, block order
+    }
+    __syncwarp();
+    return a;
 }
 
 // Issue the staging of rows [ra, rb) of w (nb blocks a row): the quant and
@@ -246,10 +268,12 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     __shared__ float red[AB_WARPS];
     __shared__ float Ls[40];
     __shared__ __align__(8) uint64_t mb[2];  // staged q/k/v rows, staged output-projection rows
+    __shared__ float tsm_all[AB_WARPS][64];  // per-warp unit terms of ab_rows (<= 4 rows x 16 blocks)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, c = blockIdx.x, gw = c * AB_WARPS + warp, W = G * AB_WARPS;
     const int dim = A.dim, nh = A.n_heads, nkv = A.n_kv, hd = A.hd, qd = nh * hd, kvd = nkv * hd;
     const int GQ = nh / nkv;
+    float *tsm = tsm_all[threadIdx.x >> 5];
     unsigned long long *ctr = A.bar;
     unsigned *ep = reinterpret_cast<unsigned *>(A.bar + 1);
     unsigned *err = reinterpret_cast<unsigned *>(A.bar + 2);
@@ -263,6 +287,11 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         }
     };
     mark(0);
+    if (A.trace && tid == 0) {  // diagnostic: the latest CTA start
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        atomicMax(A.trace + 12, t);
+    }
     const int pos = (int)*A.pos;
     const bool pos_ok = pos < A.ctx;
 
@@ -319,7 +348,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     ab_stage_d(A.wk, ka, kb, nbA, const_cast<uint16_t *>(sk.d));
     ab_stage_d(A.wv, ka, kb, nbV, const_cast<uint16_t *>(sv.d));
     ab_stage_d(A.wo, oa, ob, nbO, const_cast<uint16_t *>(so.d));
-    if (pos_ok) {  // this layer's cache rows, requested into L2 for the attention phase
+    if (pos_ok && !(A.diag & 64)) {  // this layer's cache rows, requested into L2 for the attention phase
         const size_t gt = (size_t)c * AB_THREADS + tid, nt = (size_t)G * AB_THREADS;
         ab_prefetch(A.kc, (size_t)pos * kvd * 4, gt, nt);
         ab_prefetch(A.vc, (size_t)pos * kvd * 4, gt, nt);
@@ -332,6 +361,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     {
         bool staged = mbar_wait(&mb[0], 0, STAGE_POLLS_AB);
         if (!staged && lane == 0) atomicOr(err, 2u);
+        mark(11);
         const bool k256A = QT<TA>::BE == 256, k256V = QT<TV>::BE == 256;
         const XV xv{xq, xd, xs};
         constexpr int SA = 4;
@@ -343,22 +373,15 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
             __syncthreads();
             ab_quant(sx, dim, k256, xq, xd, xs);
             __syncthreads();
-            for (int ch = warp; ch < nchunk && staged; ch += AB_WARPS) {
+            for (int ch = warp; ch < nchunk && staged && !(A.diag & 1); ch += AB_WARPS) {
                 const int m = ch < cq ? 0 : ch < cq + ck ? 1 : 2;
                 const int lc = m == 0 ? ch : m == 1 ? ch - cq : ch - cq - ck;
                 const AbStage &st = m == 0 ? sq : m == 1 ? sk : sv;
                 if ((m <= 1 ? k256A : k256V) != k256) continue;
                 const int r0 = lc * SA, nS = min(SA, st.rb - st.ra - r0);
-                float acc[SA];
-                if (m <= 1)
-                    ab_rows<TA, SA>(st, r0, nS, xv, acc, lane);
-                else
-                    ab_rows<TV, SA>(st, r0, nS, xv, acc, lane);
+                const float a = m <= 1 ? ab_rows<TA>(st, r0, nS, xv, tsm, lane) : ab_rows<TV>(st, r0, nS, xv, tsm, lane);
                 float *dst = (m == 0 ? A.q : m == 1 ? A.k : A.v) + st.ra + r0;
-                if (lane == 0)
-#pragma unroll
-                    for (int s2 = 0; s2 < SA; s2++)
-                        if (s2 < nS) dst[s2] = acc[s2];
+                if (lane < nS) dst[lane] = a;
             }
         }
     }
@@ -367,7 +390,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     mark(1);
 
     // ---- P2: head norm + RoPE + append (one warp per head, in shared memory) -------------
-    for (int head = gw; head < nh + nkv && pos_ok; head += W) {
+    for (int head = gw; head < nh + nkv && pos_ok && !(A.diag & 2); head += W) {
         const bool isk = head >= nh;
         const int kh = head - nh;
         float *vec = isk ? A.k + (size_t)kh * hd : A.q + (size_t)head * hd;
@@ -434,7 +457,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     mark(2);
 
     // ---- P3: attention chunks ------------------------------------------------------------
-    if (pos_ok) {
+    if (pos_ok && !(A.diag & 4)) {
         const int grp = warp / AB_GRP_WARPS, gl = tid % (AB_GRP_WARPS * 32), gwarp = warp % AB_GRP_WARPS;
         const int ngrp = A.groups;  // groups per CTA that fit in shared memory
         const int KS = hd + 4;
@@ -514,7 +537,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     {
         // ---- P4: merge + quantization ----------------------------------------------------
         const bool k256O = QT<TO>::BE == 256;
-        if (pos_ok && c < (qd + 255) / 256) {
+        if (pos_ok && c < (qd + 255) / 256 && !(A.diag & 8)) {
             const int live = (pos + 1 + ATT_CH - 1) / ATT_CH;
             const size_t stride = (size_t)GQ * (hd + 2);
             const int e0 = c * 256, h0 = e0 / hd, h1 = min((e0 + 255) / hd, nh - 1);
@@ -572,21 +595,17 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         if (!staged && lane == 0) atomicOr(err, 2u);
         const XV av{A.aq, A.ad, A.as};
         const int nco = (ob - oa + SO - 1) / SO;
-        for (int ch = warp; ch < nco && staged; ch += AB_WARPS) {
+        for (int ch = warp; ch < nco && staged && !(A.diag & 16); ch += AB_WARPS) {
             const int r0 = ch * SO, nS = min(SO, ob - oa - r0);
-            float acc[SO];
-            ab_rows<TO, SO>(so, r0, nS, av, acc, lane);
-            if (lane == 0)
-#pragma unroll
-                for (int s2 = 0; s2 < SO; s2++)
-                    if (s2 < nS) A.x[oa + r0 + s2] = fadd(A.x[oa + r0 + s2], acc[s2]);  // llama.zig:1195 add
+            const float a = ab_rows<TO>(so, r0, nS, av, tsm, lane);
+            if (lane < nS) A.x[oa + r0 + lane] = fadd(A.x[oa + r0 + lane], a);  // llama.zig:1195 add
         }
     }
     if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
     mark(5);
 
     // ---- P6: FFN RMSNorm -> the MoE layer's input ----------------------------------------
-    if (c == 0) {
+    if (c == 0 && !(A.diag & 32)) {
         ab_rmsnorm(A.x, A.ffn_norm, dim, A.eps, A.serial, sx, red);
         for (int i = tid; i < dim; i += AB_THREADS) A.normed[i] = sx[i];
     }

@@ -184,6 +184,7 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
             a.x = x;
             a.pos = pos;
             MCK(launch_attn_block(a, st));
+            if (getenv("LOOM_CUDA_DIAG_SKIP_MOE")) continue;  // TEMP diagnostic
             float *xn = m.x[cur ^ 1];
             if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr,
                                                st))
@@ -365,7 +366,7 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         (rc = alloc_xq(*m, m->n32, dim, false)) || (rc = alloc_xq(*m, m->a256, qd, true)) ||
         (rc = alloc_xq(*m, m->a32, qd, false)))
         return bail(rc);
-    if ((rc = dalloc(*m, m->ab_bar, 32, true))) return bail(rc);
+    if ((rc = dalloc(*m, m->ab_bar, 64, true))) return bail(rc);
     if (!m->ordered_attn && !getenv("LOOM_CUDA_NO_ATTN_BLOCK")) {
         for (size_t li = 0; li < d->n_layers; li++) {
             LayerRt &l = m->L[li];
@@ -402,6 +403,7 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
             a.ad = o256 ? m->a256.d : m->a32.d;
             a.as = o256 ? m->a256.s : m->a32.s;
             a.bar = m->ab_bar;
+            a.diag = getenv("LOOM_CUDA_AB_DIAG") ? atoi(getenv("LOOM_CUDA_AB_DIAG")) : 0;  // TEMP
             a.trace = li == 1 && getenv("LOOM_CUDA_AB_TRACE") ? m->ab_bar + 4 : nullptr;  // diagnostic (words 4..11)
             l.fused = attn_block_plan(a, l.wq.type, l.wk.type, l.wv.type, l.wo.type, m->ctx) != 0;
         }
@@ -499,11 +501,11 @@ int loom_cuda_model_error(uint64_t handle) {
     unsigned long long h[4] = {};
     if (cudaMemcpy(h, m->ab_bar, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
     if (getenv("LOOM_CUDA_AB_TRACE")) {  // diagnostic: phase times of layer 1's fused attention kernel
-        unsigned long long t[12];
+        unsigned long long t[13];
         if (cudaMemcpy(t, m->ab_bar + 4, sizeof t, cudaMemcpyDeviceToHost) == cudaSuccess)
-            fprintf(stderr, "attn_block (ns from start): B1 %llu B2 %llu B3 %llu B4 %llu B5 %llu end %llu | loads %llu norm %llu dots %llu\n",
+            fprintf(stderr, "attn_block (ns from start): B1 %llu B2 %llu B3 %llu B4 %llu B5 %llu end %llu | loads %llu norm %llu dots %llu staged %llu last_start %lld\n",
                     t[1] - t[0], t[2] - t[0], t[3] - t[0], t[4] - t[0], t[5] - t[0], t[7] - t[0], t[8] - t[0],
-                    t[9] - t[0], t[10] - t[0]);
+                    t[9] - t[0], t[10] - t[0], t[11] - t[0], (long long)(t[12] - t[0]));
     }
     const int e = (int)(unsigned)h[2];
     if (e && cudaMemset(m->ab_bar, 0, 32 * sizeof(unsigned long long)) != cudaSuccess) return -1;  // re-arm (counter, flag)
