@@ -295,6 +295,11 @@ int loom_cuda_model_free(uint64_t handle);
  * in the reference's seam. */
 int loom_cuda_stack_prepare(const loom_moe_desc *descs, size_t n_layers, uint64_t *handle);
 int loom_cuda_stack_forward(uint64_t handle, const float *d_x, float *d_out, uint32_t *d_ids, void *stream);
+/* The same launch, the last layer adding its experts to d_residual instead of
+ * its own input: for a one-layer stack, d_out = d_residual + MoE(d_x) -- a
+ * decoder layer's FFN on its normed input (llama.zig:1222-1225). */
+int loom_cuda_stack_forward_residual(uint64_t handle, const float *d_x, const float *d_residual, float *d_out,
+                                     uint32_t *d_ids, void *stream);
 /* The stack kernel's device error word (2 = a grid barrier gave up waiting);
  * synchronizes, and re-arms the barrier after an error. -1 on an unknown handle or a failed stream. */
 int loom_cuda_stack_error(uint64_t handle);

@@ -112,6 +112,7 @@ def lib() -> C.CDLL:
         "loom_cuda_stack_prepare": (i, [vp, sz, C.POINTER(u64)]),
         "loom_cuda_stack_forward": (i, [u64, vp, vp, vp, vp]),
         "loom_cuda_stack_error": (i, [u64]),
+        "loom_cuda_stack_forward_residual": (i, [u64, vp, vp, vp, vp, vp]),
         "loom_cuda_stack_free": (i, [u64]),
         "loom_cuda_stack_trace": (i, [u64, i, vp, sz]),
         "loom_cuda_umma_selftest": (i, [vp, vp, vp, i, i, i]),

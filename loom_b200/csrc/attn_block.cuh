@@ -28,7 +28,6 @@ struct AttnBlockArgs {
     float *ad;
     int32_t *as;
     unsigned long long *bar;   // zeroed 32 bytes: arrival counter, epoch + exit count, error word
-    int diag;                  // diagnostic: phases to skip (bit mask), 0 normally
     unsigned long long *trace; // optional [8]: %globaltimer ns of CTA 0 at the phase boundaries (diagnostic)
     // set by attn_block_plan
     int groups, so, ta, tv, to;

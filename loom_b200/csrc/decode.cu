@@ -1721,7 +1721,7 @@ __global__ void __launch_bounds__(PS_WARPS * 32, 1) k_stack(StackArgs A) {
         for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
             float acc = 0.0f;
             for (int k = 0; k < nk; k++) acc = fadd(acc, __ldcg(pl + (size_t)k * dim + r));
-            A.out[r] = fadd(S.xs[r], acc);
+            A.out[r] = fadd(A.residual ? __ldcg(A.residual + r) : S.xs[r], acc);
         }
     }
     stack_exit(A);

@@ -101,6 +101,7 @@ struct StackArgs {
     int gating, weights_norm;
     float weights_scale;
     const float *x_in;
+    const float *residual;     // optional: the last layer's output adds its experts to this instead of its x
     float *part;               // [2][n_used][dim] gate-weighted expert outputs (by layer parity)
     float *out;                // [dim] output of the last layer
     unsigned long long *logits; // [LOGIT_REPLICAS][n_expert + 32] tagged words (float bits | layer tag << 32)

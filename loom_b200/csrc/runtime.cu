@@ -1608,6 +1608,23 @@ extern "C" int loom_cuda_stack_forward(uint64_t handle, const float *d_x, float 
     if (it == g_stacks.end()) return decline("unknown stack");
     StackArgs A = it->second.args;
     A.x_in = d_x;
+    A.residual = nullptr;
+    A.out = d_out;
+    A.ids_out = d_ids;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
+    CK(launch_stack(A, it->second.gty, it->second.dty, st));
+    return LOOM_CUDA_OK;
+}
+
+extern "C" int loom_cuda_stack_forward_residual(uint64_t handle, const float *d_x, const float *d_residual,
+                                                float *d_out, uint32_t *d_ids, void *stream) {
+    if (int rc = need_init()) return rc;
+    auto it = g_stacks.find(handle);
+    if (it == g_stacks.end()) return decline("unknown stack");
+    if (!d_residual) return decline("no residual");
+    StackArgs A = it->second.args;
+    A.x_in = d_x;
+    A.residual = d_residual;
     A.out = d_out;
     A.ids_out = d_ids;
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;

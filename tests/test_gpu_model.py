@@ -139,3 +139,29 @@ def test_fused_attention_block_equals_separate_kernels(be, monkeypatch):
     finally:
         a.free()
         b.free()
+
+
+def test_persistent_model_kernel_equals_per_layer_path(be, monkeypatch):
+    """Every layer in one persistent launch (model_kernel.cu) against the
+    per-layer launches on the same weights: the same kernels' arithmetic, so the
+    logits agree to the RMSNorm tree's rounding (held to the fast form's 2e-2),
+    over positions that cross several attention chunks, with the routing equal."""
+    spec = qwen3_moe(n_layers=3, ctx_len=640, n_expert=16, vocab=4096)
+    monkeypatch.setenv("LOOM_CUDA_PERSISTENT", "1")
+    a = DeviceModel(spec)
+    monkeypatch.delenv("LOOM_CUDA_PERSISTENT")
+    b = DeviceModel(spec)
+    try:
+        rng = np.random.default_rng(11)
+        worst = 0.0
+        for pos in range(100):
+            tok = int(rng.integers(0, spec.vocab))
+            na, la = a.decode(tok, pos, logits=True)
+            nb, lb = b.decode(tok, pos, logits=True)
+            worst = max(worst, rel_l2(la, lb))
+            assert rel_l2(la, lb) < 2e-2, (pos, rel_l2(la, lb))
+        assert worst < 2e-2
+        assert a.error() == 0
+    finally:
+        a.free()
+        b.free()
