@@ -64,7 +64,6 @@ struct LayerRt {
     loom_moe_desc moe{};
     bool dense = false;
     bool fused = false;       // the attention half runs as one cooperative launch (attn_block.cu)
-    uint64_t stack = 0;       // the MoE half as a one-layer persistent stack launch (0: per-layer kernels)
     AttnBlockArgs blk{};
 };
 
@@ -111,8 +110,6 @@ template <class T> int dalloc(Model &m, T *&p, size_t n, bool zero = false) {
 
 void free_model(Model *m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
-    for (auto &l : m->L)
-        if (l.stack) loom_cuda_stack_free(l.stack);
     for (void *p : m->allocs) cudaFree(p);
     if (m->io_host) cudaFreeHost(m->io_host);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -199,9 +196,7 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
             a.pos = pos;
             MCK(launch_attn_block(a, st));
             float *xn = m.x[cur ^ 1];
-            if (l.stack) {
-                if (int rc = loom_cuda_stack_forward_residual(l.stack, m.normed, x, xn, nullptr, st)) return rc;
-            } else if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr,
+            if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr,
                                                st))
                 return rc;
             cur ^= 1;
@@ -517,12 +512,6 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
                 m->persistent = true;
             }
         }
-    }
-    for (size_t li = 0; li < d->n_layers && !m->persistent && !getenv("LOOM_CUDA_NO_MOE_STACK"); li++) {
-        LayerRt &l = m->L[li];
-        if (!l.fused || l.dense) continue;
-        uint64_t h = 0;
-        if (loom_cuda_stack_prepare(&l.moe, 1, &h) == LOOM_CUDA_OK) l.stack = h;  // else: per-layer kernels
     }
     if (d->rope_dim) {
         const std::vector<float> tab = rope_table(d->ctx_len, d->rope_dim, d->rope_base);

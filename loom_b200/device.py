@@ -138,6 +138,11 @@ class Stack:
     def forward(self, x, out, ids=None, stream=None) -> None:
         _lib.must(_lib.lib().loom_cuda_stack_forward(self.handle, _ptr(x), _ptr(out), _ptr(ids), _st(stream)), "stack_forward")
 
+    def forward_residual(self, x, residual, out, ids=None, stream=None) -> None:
+        """out = residual + MoE(x) for a one-layer stack (the last layer adds to residual)."""
+        _lib.must(_lib.lib().loom_cuda_stack_forward_residual(self.handle, _ptr(x), _ptr(residual), _ptr(out),
+                                                              _ptr(ids), _st(stream)), "stack_forward_residual")
+
     def error(self) -> int:
         return int(_lib.lib().loom_cuda_stack_error(self.handle))
 

@@ -63,3 +63,26 @@ def test_stack_declines_shared_expert(be, orc):
     L = _layer_case(orc, 5, ne=64, k=6, dim=2048, ffn=1408, gt=12, dt=8, shared=2816)
     with pytest.raises(RuntimeError):
         Stack([L])
+
+
+def test_one_layer_stack_with_residual_bitexact(be, orc):
+    """loom_cuda_stack_forward_residual: out = residual + MoE(x), a decoder
+    layer's FFN on its normed input, bit for bit the per-layer path's."""
+    layers = _qwen_layers(orc, 1)
+    L, dim = layers[0], layers[0].dim
+    x = torch.from_numpy(orc.synth(0, dim, seed=611, sigma=1.0).reshape(1, dim)).cuda()
+    res = torch.from_numpy(orc.synth(0, dim, seed=612, sigma=1.0).reshape(1, dim)).cuda()
+    want = torch.empty_like(x)
+    L.forward(x, want, residual=res)
+    st = Stack(layers)
+    try:
+        for _ in range(2):
+            got = torch.full_like(x, float("nan"))
+            st.forward_residual(x, res, got)
+            torch.cuda.synchronize()
+            assert np.array_equal(bits(got.cpu().numpy()), bits(want.cpu().numpy()))
+        assert st.error() == 0
+    finally:
+        st.free()
+        for t in (L.gate, L.up, L.down, L.router):
+            t.free()
