@@ -65,10 +65,33 @@ class ModelSpec:
     types: Dict[str, int] = field(default_factory=dict)
     norms: str = "ones"          # ones | near_ones
     seed: int = 1
+    # DeepSeek-V2/V3 (deepseek2 arch): multi-head latent attention and MoE extras
+    mla: bool = False
+    kv_lora: int = 0
+    q_lora: int = 0
+    nope: int = 0
+    v_head: int = 0
+    n_dense: int = 0             # leading dense-FFN layers (ffn wide)
+    shexp_ffn: int = 0           # shared expert width (0: none)
+    gating: int = 1              # 1 softmax, 2 sigmoid
+    weights_norm: bool = True
+    weights_scale: float = 1.0
+    router_bias: bool = False
+    n_group: int = 1
+    topk_group: int = 1
 
     def __post_init__(self):
         if not self.rope_dim:
             self.rope_dim = self.head_dim
+
+    @property
+    def attn_scale(self) -> float:
+        """MLA softmax scale 1 / sqrt(nope + rope) (deepseek.zig:360, no YaRN)."""
+        import math
+        return float(np.float32(1.0) / np.float32(math.sqrt(float(self.nope + self.rope_dim))))
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.n_expert > 0 and i >= self.n_dense
 
     def ty(self, key: str) -> int:
         return self.types[key]
@@ -81,25 +104,47 @@ class ModelSpec:
                TensorPlan("output", self.ty("output"), self.vocab, d)]
         for i in range(self.n_layers):
             p = f"blk.{i}."
-            out += [TensorPlan(p + "attn_norm", F32, 1, d, fill=self.norms),
-                    TensorPlan(p + "attn_q", self.ty("attn_q"), qd, d),
-                    TensorPlan(p + "attn_k", self.ty("attn_k"), kvd, d),
-                    TensorPlan(p + "attn_v", self.ty("attn_v"), kvd, d),
-                    TensorPlan(p + "attn_output", self.ty("attn_output"), d, qd),
-                    TensorPlan(p + "ffn_norm", F32, 1, d, fill=self.norms)]
+            out += [TensorPlan(p + "attn_norm", F32, 1, d, fill=self.norms)]
+            if self.mla:
+                kd = self.nope + self.rope_dim
+                if self.q_lora:
+                    out += [TensorPlan(p + "attn_q_a", self.ty("attn_q_a"), self.q_lora, d),
+                            TensorPlan(p + "attn_q_a_norm", F32, 1, self.q_lora, fill=self.norms),
+                            TensorPlan(p + "attn_q_b", self.ty("attn_q_b"), self.n_heads * kd, self.q_lora)]
+                else:
+                    out += [TensorPlan(p + "attn_q", self.ty("attn_q"), self.n_heads * kd, d)]
+                out += [TensorPlan(p + "attn_kv_a_mqa", self.ty("attn_kv_a_mqa"), self.kv_lora + self.rope_dim, d),
+                        TensorPlan(p + "attn_kv_a_norm", F32, 1, self.kv_lora, fill=self.norms),
+                        TensorPlan(p + "attn_kv_b", self.ty("attn_kv_b"), self.n_heads * (self.nope + self.v_head),
+                                   self.kv_lora),
+                        TensorPlan(p + "attn_output", self.ty("attn_output"), d, self.n_heads * self.v_head)]
+            else:
+                out += [TensorPlan(p + "attn_q", self.ty("attn_q"), qd, d),
+                        TensorPlan(p + "attn_k", self.ty("attn_k"), kvd, d),
+                        TensorPlan(p + "attn_v", self.ty("attn_v"), kvd, d),
+                        TensorPlan(p + "attn_output", self.ty("attn_output"), d, qd)]
+            out += [TensorPlan(p + "ffn_norm", F32, 1, d, fill=self.norms)]
             if self.qk_norm:
                 out += [TensorPlan(p + "attn_q_norm", F32, 1, self.head_dim, fill="near_ones"),
                         TensorPlan(p + "attn_k_norm", F32, 1, self.head_dim, fill="near_ones")]
-            if self.n_expert:
+            if self.is_moe_layer(i):
                 ne, f = self.n_expert, self.moe_ffn
                 out += [TensorPlan(p + "ffn_gate_inp", F32, ne, d, sigma=0.02),
                         TensorPlan(p + "ffn_gate_exps", self.ty("ffn_gate"), f, d, planes=ne),
                         TensorPlan(p + "ffn_up_exps", self.ty("ffn_up"), f, d, planes=ne),
                         TensorPlan(p + "ffn_down_exps", self.ty("ffn_down"), d, f, planes=ne)]
+                if self.router_bias:
+                    out += [TensorPlan(p + "exp_probs_b.bias", F32, 1, ne, sigma=0.05)]
+                if self.shexp_ffn:
+                    sf = self.shexp_ffn
+                    out += [TensorPlan(p + "ffn_gate_shexp", self.ty("ffn_gate"), sf, d),
+                            TensorPlan(p + "ffn_up_shexp", self.ty("ffn_up"), sf, d),
+                            TensorPlan(p + "ffn_down_shexp", self.ty("ffn_down_shexp"), d, sf)]
             else:
                 out += [TensorPlan(p + "ffn_gate", self.ty("ffn_gate"), self.ffn, d),
                         TensorPlan(p + "ffn_up", self.ty("ffn_up"), self.ffn, d),
-                        TensorPlan(p + "ffn_down", self.ty("ffn_down"), d, self.ffn)]
+                        TensorPlan(p + "ffn_down", self.types.get("ffn_down_dense", self.ty("ffn_down")), d,
+                                   self.ffn)]
         for t in out:
             t.seed = (self.seed * 0x9E3779B1 + zlib.crc32(t.name.encode())) & 0xFFFFFFFF
         return out
@@ -138,6 +183,39 @@ def qwen3_moe(n_layers: int = 48, ctx_len: int = 2048, n_expert: int = 128, voca
                      n_expert=n_expert, n_used=8, moe_ffn=768,
                      types=dict(embd=Q4_K, output=Q6_K, attn_q=Q4_K, attn_k=Q4_K, attn_v=Q6_K, attn_output=Q4_K,
                                 ffn_gate=Q4_K, ffn_up=Q4_K, ffn_down=Q6_K), norms="near_ones", seed=seed)
+
+
+def deepseek_v2_lite(n_layers: int = 27, ctx_len: int = 4096, n_expert: int = 64, vocab: int = 102400,
+                     seed: int = 5) -> ModelSpec:
+    """DeepSeek-V2-Lite (deepseek2 / MLA): 27 layers, hidden
+    2048, 16 heads, kv_lora 512, rope 64, nope 128, v 128, no q_lora; layer 0
+    dense (FFN 10944), then 64 routed experts top-6 of FFN 1408 plus 2 shared
+    (one shared FFN of 2816), vocab 102400; softmax gating with renorm.
+    Q4_K wherever the width is a multiple of 256; the down projections of
+    width 1408 / 10944 / 2816 are Q8_0 (as real Q4_K_M files put them)."""
+    return ModelSpec("deepseek-v2-lite-q4_k", dim=2048, n_layers=n_layers, n_heads=16, n_kv_heads=16, head_dim=192,
+                     vocab=vocab, ctx_len=ctx_len, eps=1e-6, rope_base=10000.0, rope_neox=False, rope_dim=64,
+                     mla=True, kv_lora=512, q_lora=0, nope=128, v_head=128, n_dense=1, ffn=10944,
+                     n_expert=n_expert, n_used=6, moe_ffn=1408, shexp_ffn=2816, gating=1, weights_norm=True,
+                     types=dict(embd=Q4_K, output=Q6_K, attn_q=Q4_K, attn_kv_a_mqa=Q4_K, attn_kv_b=Q4_K,
+                                attn_output=Q4_K, ffn_gate=Q4_K, ffn_up=Q4_K, ffn_down=Q8_0,
+                                ffn_down_dense=Q8_0, ffn_down_shexp=Q8_0), seed=seed)
+
+
+def deepseek_v3(n_layers: int = 61, ctx_len: int = 4096, n_expert: int = 256, vocab: int = 129280, dim: int = 7168,
+                n_heads: int = 128, n_dense: int = 3, seed: int = 7) -> ModelSpec:
+    """DeepSeek-V3 shape: 61 layers (3 dense, FFN 18432),
+    hidden 7168, MLA with 128 heads, q_lora 1536, kv_lora 512; 256 routed
+    experts top-8 of FFN 2048, sigmoid gating with selection bias and renorm,
+    grouped top-k (8 groups, 4 kept), 1 shared expert; vocab 129280; Q4_K."""
+    return ModelSpec("deepseek-v3-q4_k", dim=dim, n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_heads,
+                     head_dim=192, vocab=vocab, ctx_len=ctx_len, eps=1e-6, rope_base=10000.0, rope_neox=False,
+                     rope_dim=64, mla=True, kv_lora=512, q_lora=1536, nope=128, v_head=128, n_dense=n_dense,
+                     ffn=18432, n_expert=n_expert, n_used=8, moe_ffn=2048, shexp_ffn=2048, gating=2,
+                     weights_norm=True, weights_scale=2.5, router_bias=True, n_group=8, topk_group=4,
+                     types=dict(embd=Q4_K, output=Q4_K, attn_q_a=Q4_K, attn_q_b=Q4_K, attn_kv_a_mqa=Q4_K,
+                                attn_kv_b=Q4_K, attn_output=Q4_K, ffn_gate=Q4_K, ffn_up=Q4_K, ffn_down=Q4_K,
+                                ffn_down_dense=Q4_K, ffn_down_shexp=Q4_K), seed=seed)
 
 
 class DeviceModel:

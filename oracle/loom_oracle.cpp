@@ -1235,3 +1235,104 @@ int or_llama_step(const or_llama_model *m, float *k_cache, float *v_cache, uint3
     or_rmsnorm(normed.data(), x.data(), m->output_norm, dim, m->eps);                 // :1226-1227
     return or_matvec(m->output_type, logits, m->output, normed.data(), m->vocab, dim);
 }
+
+// ---- deepseek.zig:1275-1537 step, attnLayer :851-1049 -----------------------------
+
+// deepseek.zig:615-629 ropeNormPlain (adjacent pairs over the whole vector)
+static void rope_norm_plain(float *vec, size_t n, size_t pos, float base) {
+    for (size_t i = 0; 2 * i + 1 < n; i++) {
+        float c, s;
+        rope_theta(2 * i, n, pos, base, c, s);
+        const float a = vec[2 * i], b = vec[2 * i + 1];
+        vec[2 * i] = a * c - b * s;
+        vec[2 * i + 1] = a * s + b * c;
+    }
+}
+
+int or_deepseek_step(const or_ds_model *m, float *c_cache, float *r_cache, uint32_t token, size_t pos,
+                     float *logits) {
+    const size_t dim = m->dim, nh = m->n_heads, nope = m->nope, rope = m->rope, kvr = m->kv_lora, vd = m->v_head;
+    const size_t kd = nope + rope;
+    if (token >= m->vocab || pos >= m->ctx_len) return -1;
+    std::vector<float> x(dim), normed(dim), q(nh * kd), qa_lat(m->q_lora ? m->q_lora : 1), kv_a(kvr + rope),
+        qabs(nh * kvr), row(kvr), scores(pos + 1), c_acc(kvr), head_out(nh * vd), proj(dim), acc(dim), v(dim);
+    if (or_dequant_row(m->embd_type, x.data(), m->token_embd, token, dim)) return -1;  // :1292
+    for (size_t li = 0; li < m->n_layers; li++) {
+        const or_ds_layer &l = m->layers[li];
+        or_rmsnorm(normed.data(), x.data(), l.attn_norm, dim, m->eps);  // :860
+        if (m->q_lora) {                                                // :862-865
+            if (or_matvec(l.q_a_type, qa_lat.data(), l.q_a, normed.data(), m->q_lora, dim)) return -1;
+            or_rmsnorm(qa_lat.data(), qa_lat.data(), l.q_a_norm, m->q_lora, m->eps);
+            if (or_matvec(l.q_b_type, q.data(), l.q_b, qa_lat.data(), nh * kd, m->q_lora)) return -1;
+        } else if (or_matvec(l.wq_type, q.data(), l.wq, normed.data(), nh * kd, dim)) {
+            return -1;
+        }
+        if (or_matvec(l.kv_a_type, kv_a.data(), l.kv_a, normed.data(), kvr + rope, dim)) return -1;  // :870
+        float *c_kv = c_cache + (li * m->ctx_len + pos) * kvr;
+        or_rmsnorm(c_kv, kv_a.data(), l.kv_a_norm, kvr, m->eps);                                    // :872
+        float *k_rope = r_cache + (li * m->ctx_len + pos) * rope;
+        std::memcpy(k_rope, kv_a.data() + kvr, rope * 4);
+        rope_norm_plain(k_rope, rope, pos, m->rope_base);                                           // :875
+        for (size_t h = 0; h < nh; h++) rope_norm_plain(q.data() + h * kd + nope, rope, pos, m->rope_base);
+        const size_t seq = pos + 1;
+        const size_t kb_rb = or_row_bytes(l.kv_b_type, kvr);
+        for (size_t h = 0; h < nh; h++) {  // :944-958 absorb: qa = sum_r q_nope[r] * W_k row r
+            float *qa = qabs.data() + h * kvr;
+            for (size_t j = 0; j < kvr; j++) qa[j] = 0.0f;
+            const uint8_t *k_rows = l.kv_b + h * (nope + vd) * kb_rb;
+            for (size_t r = 0; r < nope; r++) {
+                if (or_dequant_row(l.kv_b_type, row.data(), k_rows, r, kvr)) return -1;
+                axpy(qa, row.data(), q[h * kd + r], kvr);
+            }
+        }
+        for (size_t h = 0; h < nh; h++) {  // :966-986 scores, softmax, weighted sum in compressed space
+            const float *qa = qabs.data() + h * kvr, *qr = q.data() + h * kd + nope;
+            for (size_t t = 0; t < seq; t++) {
+                const float *c_t = c_cache + (li * m->ctx_len + t) * kvr;
+                const float *kr_t = r_cache + (li * m->ctx_len + t) * rope;
+                scores[t] = (or_dot_f32(qa, c_t, kvr) + or_dot_f32(qr, kr_t, rope)) * m->attn_scale;
+            }
+            or_softmax(scores.data(), seq);
+            for (size_t j = 0; j < kvr; j++) c_acc[j] = 0.0f;
+            for (size_t t = 0; t < seq; t++) axpy(c_acc.data(), c_cache + (li * m->ctx_len + t) * kvr, scores[t], kvr);
+            // :988 W_v applied once per head
+            if (or_matvec(l.kv_b_type, head_out.data() + h * vd, l.kv_b + (h * (nope + vd) + nope) * kb_rb,
+                          c_acc.data(), vd, kvr))
+                return -1;
+        }
+        if (or_matvec(l.wo_type, proj.data(), l.wo, head_out.data(), dim, nh * vd)) return -1;  // :991
+        for (size_t i = 0; i < dim; i++) x[i] += proj[i];
+        or_rmsnorm(normed.data(), x.data(), l.ffn_norm, dim, m->eps);  // :1326
+        if (!l.router) {                                               // :1328-1330 dense
+            or_expert e{l.gate_type, l.up_type, l.down_type, l.gate, l.up, l.down, 1.0f, l.ffn};
+            std::vector<float> g, u;
+            if (dense_ffn(e, normed.data(), dim, acc.data(), g, u)) return -1;
+        } else {  // :1332-1507 router, route, experts in selection order, shared expert added
+            std::vector<float> lg(m->n_expert);
+            if (or_matvec(OR_F32, lg.data(), (const uint8_t *)l.router, normed.data(), m->n_expert, dim)) return -1;
+            uint32_t ids[64];
+            float gates[64];
+            if (or_route_grouped(lg.data(), l.router_bias, m->n_expert, m->n_used, m->gating_sigmoid ? 2 : 1,
+                                 m->weights_norm, m->weights_scale, m->n_group ? m->n_group : 1,
+                                 m->topk_group ? m->topk_group : 1, ids, gates))
+                return -1;
+            const size_t gp = l.ffn * or_row_bytes(l.gate_type, dim), upb = l.ffn * or_row_bytes(l.up_type, dim);
+            const size_t dp = dim * or_row_bytes(l.down_type, l.ffn);
+            std::vector<or_expert> ex(m->n_used);
+            for (size_t k = 0; k < m->n_used; k++)
+                ex[k] = or_expert{l.gate_type, l.up_type, l.down_type, l.gate + ids[k] * gp, l.up + ids[k] * upb,
+                                  l.down + ids[k] * dp, gates[k], l.ffn};
+            if (or_moe_ffn_block(normed.data(), dim, ex.data(), m->n_used, acc.data())) return -1;
+            if (l.sh_gate) {  // deepseek.zig:1498-1508: shared expert added plainly
+                or_expert se{l.sh_gate_type, l.sh_up_type, l.sh_down_type, l.sh_gate, l.sh_up, l.sh_down, 1.0f,
+                             l.sh_ffn};
+                std::vector<float> g, u;
+                if (dense_ffn(se, normed.data(), dim, v.data(), g, u)) return -1;
+                for (size_t i = 0; i < dim; i++) acc[i] += v[i];
+            }
+        }
+        for (size_t i = 0; i < dim; i++) x[i] += acc[i];
+    }
+    or_rmsnorm(normed.data(), x.data(), m->output_norm, dim, m->eps);
+    return or_matvec(m->output_type, logits, m->output, normed.data(), m->vocab, dim);
+}

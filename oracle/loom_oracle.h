@@ -133,6 +133,44 @@ typedef struct {
 int or_llama_step(const or_llama_model *m, float *k_cache, float *v_cache, uint32_t token, size_t pos,
                   float *logits);
 
+/* One DeepSeek-V2/V3 decoder layer (deepseek.zig Model.layers): MLA attention
+ * weights (q either from wq, or q_a -> RMSNorm(q_a_norm) -> q_b when
+ * q_lora_rank > 0), then a dense FFN (router == NULL) or a routed MoE with
+ * optional bias and optional shared expert (shexp_gate != NULL). */
+typedef struct {
+    const float *attn_norm, *ffn_norm;
+    int wq_type; const uint8_t *wq;                 /* [n_heads*(nope+rope)][dim] (q_lora_rank == 0) */
+    int q_a_type; const uint8_t *q_a; const float *q_a_norm;  /* [q_lora][dim], f32 [q_lora] */
+    int q_b_type; const uint8_t *q_b;               /* [n_heads*(nope+rope)][q_lora] */
+    int kv_a_type; const uint8_t *kv_a;             /* [kv_lora+rope][dim] (attn_kv_a_mqa) */
+    const float *kv_a_norm;                         /* f32 [kv_lora] */
+    int kv_b_type; const uint8_t *kv_b;             /* [n_heads*(nope+v_head)][kv_lora] */
+    int wo_type; const uint8_t *wo;                 /* [dim][n_heads*v_head] */
+    int gate_type, up_type, down_type;
+    const uint8_t *gate, *up, *down;                /* dense or 3D expert tensors */
+    size_t ffn;
+    const float *router, *router_bias;              /* f32 [n_expert][dim], [n_expert] or NULL */
+    int sh_gate_type, sh_up_type, sh_down_type;
+    const uint8_t *sh_gate, *sh_up, *sh_down;       /* shared expert or NULL */
+    size_t sh_ffn;
+} or_ds_layer;
+typedef struct {
+    size_t dim, n_layers, n_heads, nope, rope, kv_lora, q_lora, v_head, vocab, ctx_len;
+    float eps, rope_base, attn_scale;
+    size_t n_expert, n_used;
+    int gating_sigmoid, weights_norm;
+    float weights_scale;
+    int embd_type; const uint8_t *token_embd;
+    const float *output_norm;
+    int output_type; const uint8_t *output;
+    const or_ds_layer *layers;
+    size_t n_group, topk_group;   /* DeepSeek-V3 group-limited routing (1, 1: moe.zig route) */
+} or_ds_model;
+/* deepseek.zig:1275-1537 step (host path) with attnLayer (:851-1049):
+ * c_cache f32 [n_layers][ctx][kv_lora], r_cache f32 [n_layers][ctx][rope]. */
+int or_deepseek_step(const or_ds_model *m, float *c_cache, float *r_cache, uint32_t token, size_t pos,
+                     float *logits);
+
 /* Seeded synthetic tensors (counter-based, the same generator the CUDA backend
  * runs on the device): blocks [blk0, blk0+nblk) of a tensor of `type`. For
  * OR_F32, "blocks" are elements ~ sigma * IrwinHall12. */

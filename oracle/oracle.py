@@ -62,6 +62,7 @@ def lib() -> C.CDLL:
         L.or_moe_layer.argtypes = [vp, sz, sz, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, sz, sz,
                                    sz, C.c_int, C.c_int, fp, vp, vp]
         L.or_llama_step.argtypes = [vp, vp, vp, C.c_uint32, sz, vp]
+        L.or_deepseek_step.argtypes = [vp, vp, vp, C.c_uint32, sz, vp]
         L.or_synth.argtypes = [C.c_int, vp, C.c_uint64, C.c_uint64, C.c_uint64, fp]
         L.or_f32_to_f16_rne.restype = C.c_uint16
         L.or_f32_to_f16_rne.argtypes = [fp]
@@ -310,5 +311,90 @@ class LlamaRunner:
     def step(self, token: int, pos: int) -> np.ndarray:
         logits = np.empty(self.spec.vocab, np.float32)
         rc = lib().or_llama_step(C.byref(self.m), _p(self.kc), _p(self.vc), token, pos, _p(logits))
+        assert rc == 0
+        return logits
+
+
+class DsLayer(C.Structure):
+    """or_ds_layer: one DeepSeek-V2/V3 decoder layer."""
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p),
+                ("wq_type", C.c_int), ("wq", C.c_void_p),
+                ("q_a_type", C.c_int), ("q_a", C.c_void_p), ("q_a_norm", C.c_void_p),
+                ("q_b_type", C.c_int), ("q_b", C.c_void_p),
+                ("kv_a_type", C.c_int), ("kv_a", C.c_void_p), ("kv_a_norm", C.c_void_p),
+                ("kv_b_type", C.c_int), ("kv_b", C.c_void_p), ("wo_type", C.c_int), ("wo", C.c_void_p),
+                ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p), ("ffn", C.c_size_t),
+                ("router", C.c_void_p), ("router_bias", C.c_void_p),
+                ("sh_gate_type", C.c_int), ("sh_up_type", C.c_int), ("sh_down_type", C.c_int),
+                ("sh_gate", C.c_void_p), ("sh_up", C.c_void_p), ("sh_down", C.c_void_p), ("sh_ffn", C.c_size_t)]
+
+
+class DsModel(C.Structure):
+    """or_ds_model."""
+    _fields_ = [("dim", C.c_size_t), ("n_layers", C.c_size_t), ("n_heads", C.c_size_t), ("nope", C.c_size_t),
+                ("rope", C.c_size_t), ("kv_lora", C.c_size_t), ("q_lora", C.c_size_t), ("v_head", C.c_size_t),
+                ("vocab", C.c_size_t), ("ctx_len", C.c_size_t), ("eps", C.c_float), ("rope_base", C.c_float),
+                ("attn_scale", C.c_float), ("n_expert", C.c_size_t), ("n_used", C.c_size_t),
+                ("gating_sigmoid", C.c_int), ("weights_norm", C.c_int), ("weights_scale", C.c_float),
+                ("embd_type", C.c_int), ("token_embd", C.c_void_p), ("output_norm", C.c_void_p),
+                ("output_type", C.c_int), ("output", C.c_void_p), ("layers", C.POINTER(DsLayer)),
+                ("n_group", C.c_size_t), ("topk_group", C.c_size_t)]
+
+
+class DeepseekRunner:
+    """deepseek.zig:1275-1537 step (attnLayer :851-1049) on host tensors, with
+    its own compressed caches (c: [layers][ctx][kv_lora], r: [layers][ctx][rope])."""
+
+    def __init__(self, spec, tensors):
+        self.spec, self.t = spec, tensors
+        c = spec
+        self._layers = (DsLayer * c.n_layers)()
+        for i in range(c.n_layers):
+            L = self._layers[i]
+
+            def g(n, i=i):
+                return tensors.get(f"blk.{i}.{n}")
+
+            def tp(n):
+                return g(n)[0] if g(n) else 0
+
+            def pp(n):
+                return _p(g(n)[1]) if g(n) else None
+            L.attn_norm, L.ffn_norm = pp("attn_norm"), pp("ffn_norm")
+            L.wq_type, L.wq = tp("attn_q"), pp("attn_q")
+            L.q_a_type, L.q_a, L.q_a_norm = tp("attn_q_a"), pp("attn_q_a"), pp("attn_q_a_norm")
+            L.q_b_type, L.q_b = tp("attn_q_b"), pp("attn_q_b")
+            L.kv_a_type, L.kv_a, L.kv_a_norm = tp("attn_kv_a_mqa"), pp("attn_kv_a_mqa"), pp("attn_kv_a_norm")
+            L.kv_b_type, L.kv_b = tp("attn_kv_b"), pp("attn_kv_b")
+            L.wo_type, L.wo = tp("attn_output"), pp("attn_output")
+            moe = g("ffn_gate_inp") is not None
+            sfx = "_exps" if moe else ""
+            L.gate_type, L.up_type, L.down_type = tp("ffn_gate" + sfx), tp("ffn_up" + sfx), tp("ffn_down" + sfx)
+            L.gate, L.up, L.down = pp("ffn_gate" + sfx), pp("ffn_up" + sfx), pp("ffn_down" + sfx)
+            L.ffn = c.moe_ffn if moe else c.ffn
+            L.router, L.router_bias = pp("ffn_gate_inp"), pp("exp_probs_b.bias")
+            L.sh_gate_type, L.sh_up_type = tp("ffn_gate_shexp"), tp("ffn_up_shexp")
+            L.sh_down_type = tp("ffn_down_shexp")
+            L.sh_gate, L.sh_up, L.sh_down = pp("ffn_gate_shexp"), pp("ffn_up_shexp"), pp("ffn_down_shexp")
+            L.sh_ffn = c.shexp_ffn
+        M = DsModel()
+        M.dim, M.n_layers, M.n_heads, M.nope, M.rope = c.dim, c.n_layers, c.n_heads, c.nope, c.rope_dim
+        M.kv_lora, M.q_lora, M.v_head, M.vocab, M.ctx_len = c.kv_lora, c.q_lora, c.v_head, c.vocab, c.ctx_len
+        M.eps, M.rope_base, M.attn_scale = c.eps, c.rope_base, c.attn_scale
+        M.n_expert, M.n_used, M.gating_sigmoid = c.n_expert, c.n_used, int(c.gating == 2)
+        M.weights_norm, M.weights_scale = int(c.weights_norm), c.weights_scale
+        M.embd_type, M.token_embd = tensors["token_embd"][0], _p(tensors["token_embd"][1])
+        M.output_norm = _p(tensors["output_norm"][1])
+        M.output_type, M.output = tensors["output"][0], _p(tensors["output"][1])
+        M.layers = self._layers
+        M.n_group, M.topk_group = c.n_group, c.topk_group
+        self.m = M
+        self.cc = np.zeros(c.n_layers * c.ctx_len * c.kv_lora, np.float32)
+        self.rc = np.zeros(c.n_layers * c.ctx_len * c.rope_dim, np.float32)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.spec.vocab, np.float32)
+        rc = lib().or_deepseek_step(C.byref(self.m), _p(self.cc), _p(self.rc), token, pos, _p(logits))
         assert rc == 0
         return logits

@@ -88,3 +88,71 @@ def numpy_step(spec: ModelSpec, T: dict, orc, kc, vc, token: int, pos: int) -> n
         x = (x + y).astype(np.float32)
     h = _rmsnorm(x, T["output_norm"][1], spec.eps).astype(np.float32)
     return mv("output", h, spec.vocab, d)
+
+
+def numpy_ds_step(spec: ModelSpec, T: dict, orc, cc, rc, token: int, pos: int) -> np.ndarray:
+    """deepseek.zig:1275-1537 / attnLayer :851-1049 in numpy (float64 sums)
+    around the oracle's matvecs and dequant: q (direct or q_a -> norm -> q_b),
+    kv_a -> normed compressed row + RoPE'd rope row into the caches, W_k
+    absorbed into q, softmax over positions in compressed space, W_v once per
+    head, output projection; dense FFN or routed MoE + shared expert."""
+    d, nh, nope, rope, kvr, vd = spec.dim, spec.n_heads, spec.nope, spec.rope_dim, spec.kv_lora, spec.v_head
+    kd = nope + rope
+    mv = lambda n, x, rows, cols: orc.matvec(T[n][0], T[n][1], np.asarray(x, np.float32), rows, cols)  # noqa: E731
+    x = orc.dequant_row(T["token_embd"][0], T["token_embd"][1], token, d).astype(np.float32)
+    for li in range(spec.n_layers):
+        p = f"blk.{li}."
+        h = _rmsnorm(x, T[p + "attn_norm"][1], spec.eps).astype(np.float32)
+        if spec.q_lora:
+            qa = _rmsnorm(mv(p + "attn_q_a", h, spec.q_lora, d), T[p + "attn_q_a_norm"][1], spec.eps)
+            q = mv(p + "attn_q_b", qa, nh * kd, spec.q_lora)
+        else:
+            q = mv(p + "attn_q", h, nh * kd, d)
+        kv = mv(p + "attn_kv_a_mqa", h, kvr + rope, d)
+        cc[li, pos] = _rmsnorm(kv[:kvr], T[p + "attn_kv_a_norm"][1], spec.eps)
+        kr = kv[kvr:].copy()
+        _rope(kr, rope, pos, spec.rope_base, False)
+        rc[li, pos] = kr
+        kvb = orc.dequant(T[p + "attn_kv_b"][0], T[p + "attn_kv_b"][1], nh * (nope + vd), kvr).reshape(nh, nope + vd, kvr)
+        head_out = np.zeros(nh * vd, np.float32)
+        for hh in range(nh):
+            qh = q[hh * kd:(hh + 1) * kd].copy()
+            qr = qh[nope:].copy()
+            _rope(qr, rope, pos, spec.rope_base, False)
+            qabs = qh[:nope].astype(np.float64) @ kvb[hh, :nope].astype(np.float64)
+            s = (cc[li, :pos + 1].astype(np.float64) @ qabs + rc[li, :pos + 1].astype(np.float64) @ qr) * spec.attn_scale
+            e = np.exp(s - s.max())
+            cacc = ((e / e.sum()) @ cc[li, :pos + 1].astype(np.float64)).astype(np.float32)
+            rows = T[p + "attn_kv_b"][1].reshape(nh * (nope + vd), -1)[hh * (nope + vd) + nope:(hh + 1) * (nope + vd)]
+            head_out[hh * vd:(hh + 1) * vd] = orc.matvec(T[p + "attn_kv_b"][0], np.ascontiguousarray(rows), cacc, vd, kvr)
+        x = (x + mv(p + "attn_output", head_out, d, nh * vd)).astype(np.float32)
+        h = _rmsnorm(x, T[p + "ffn_norm"][1], spec.eps).astype(np.float32)
+        if spec.is_moe_layer(li):
+            lg = orc.matvec(0, T[p + "ffn_gate_inp"][1], h, spec.n_expert, d)
+            bias = T[p + "exp_probs_b.bias"][1] if spec.router_bias else None
+            ids, gates = orc.route(lg, spec.n_used, spec.gating, spec.weights_norm, spec.weights_scale, bias=bias,
+                                   n_group=spec.n_group, topk_group=spec.topk_group)
+            f = spec.moe_ffn
+            acc = np.zeros(d, np.float64)
+            for e_, gt in zip(ids, gates):
+                def plane(n, rows, cols):
+                    ty, b = T[p + n]
+                    nb = b.size // spec.n_expert
+                    return ty, b[int(e_) * nb:(int(e_) + 1) * nb]
+                gty, gb = plane("ffn_gate_exps", f, d)
+                uty, ub = plane("ffn_up_exps", f, d)
+                dty, db = plane("ffn_down_exps", d, f)
+                g_ = orc.matvec(gty, gb, h, f, d)
+                u_ = orc.matvec(uty, ub, h, f, d)
+                acc += float(gt) * orc.matvec(dty, db, ((g_ / (1 + np.exp(-g_))) * u_).astype(np.float32), d, f)
+            if spec.shexp_ffn:
+                sf = spec.shexp_ffn
+                g_, u_ = mv(p + "ffn_gate_shexp", h, sf, d), mv(p + "ffn_up_shexp", h, sf, d)
+                acc += mv(p + "ffn_down_shexp", ((g_ / (1 + np.exp(-g_))) * u_).astype(np.float32), d, sf)
+            y = acc.astype(np.float32)
+        else:
+            g_, u_ = mv(p + "ffn_gate", h, spec.ffn, d), mv(p + "ffn_up", h, spec.ffn, d)
+            y = mv(p + "ffn_down", ((g_ / (1 + np.exp(-g_))) * u_).astype(np.float32), d, spec.ffn)
+        x = (x + y).astype(np.float32)
+    h = _rmsnorm(x, T["output_norm"][1], spec.eps).astype(np.float32)
+    return mv("output", h, spec.vocab, d)

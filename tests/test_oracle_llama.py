@@ -46,3 +46,35 @@ def test_oracle_rejects_bad_token_and_position(orc):
         run.step(spec.vocab, 0)  # llama.zig:1121 TokenOutOfRange
     with pytest.raises(AssertionError):
         run.step(1, spec.ctx_len)
+
+
+def _compare_ds(spec, orc, steps, tol):
+    from oracle.oracle import DeepseekRunner
+    from tests.modelref import numpy_ds_step
+    T = host_tensors(spec, orc)
+    run = DeepseekRunner(spec, T)
+    cc = np.zeros((spec.n_layers, spec.ctx_len, spec.kv_lora), np.float32)
+    rc = np.zeros((spec.n_layers, spec.ctx_len, spec.rope_dim), np.float32)
+    rng = np.random.default_rng(9)
+    for pos in range(steps):
+        tok = int(rng.integers(0, spec.vocab))
+        got = run.step(tok, pos)
+        want = numpy_ds_step(spec, T, orc, cc, rc, tok, pos)
+        assert np.all(np.isfinite(got))
+        assert rel_l2(got, want) < tol, (pos, rel_l2(got, want))
+        oc = run.cc.reshape(spec.n_layers, spec.ctx_len, spec.kv_lora)[:, pos]
+        assert rel_l2(oc, cc[:, pos]) < tol
+
+
+def test_oracle_deepseek_v2_lite_reduced(orc):
+    """MLA without q_lora, dense first layer, routed layer with shared experts."""
+    from loom_b200.model import deepseek_v2_lite
+    _compare_ds(deepseek_v2_lite(n_layers=2, ctx_len=8, n_expert=8, vocab=512), orc, steps=5, tol=2e-3)
+
+
+def test_oracle_deepseek_v3_shape_reduced(orc):
+    """MLA with q_lora, sigmoid + bias gating, grouped top-k, one shared expert."""
+    from loom_b200.model import deepseek_v3
+    spec = deepseek_v3(n_layers=2, ctx_len=8, n_expert=16, dim=1024, n_heads=8, vocab=512, n_dense=1)
+    spec.n_used, spec.n_group, spec.topk_group = 4, 4, 2
+    _compare_ds(spec, orc, steps=4, tol=2e-3)
