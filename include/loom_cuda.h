@@ -234,6 +234,11 @@ typedef struct {
     loom_tensor ffn_gate, ffn_up, ffn_down;
     size_t ffn;
     loom_moe_desc moe;
+    /* multi-head latent attention (desc.mla = 1; deepseek.zig:851-1049), in place
+     * of wq/wk/wv: q = wq . x (q_lora_rank 0) or q_b . RMSNorm(q_a . x) *
+     * q_a_norm; kv_a [kv_lora + rope][dim] (attn_kv_a_mqa); kv_a_norm f32
+     * [kv_lora]; kv_b [n_heads*(nope + v_head)][kv_lora]; wo [dim][n_heads*v_head] */
+    loom_tensor q_a, q_a_norm, q_b, kv_a, kv_a_norm, kv_b;
 } loom_model_layer;
 typedef struct {
     size_t dim, n_layers, n_heads, n_kv_heads, head_dim, rope_dim, vocab, ctx_len;
@@ -248,6 +253,13 @@ typedef struct {
     loom_tensor output_norm;              /* f32 [dim] */
     loom_tensor output;                   /* [vocab][dim] */
     const loom_model_layer *layers;       /* [n_layers], copied by create */
+    /* multi-head latent attention (DeepSeek-V2/V3): head_dim = nope + rope_dim
+     * per query head; the cache holds [ctx][kv_lora] compressed rows and
+     * [ctx][rope_dim] rope rows per layer; scores scale by mla_scale
+     * (deepseek.zig:360: mscale^2 / sqrt(nope + rope)). n_kv_heads is ignored. */
+    int mla;
+    size_t kv_lora, q_lora, nope, v_head;
+    float mla_scale;
 } loom_model_desc;
 /* Build the model: checks every tensor's type and size, allocates the KV
  * cache (2 x n_layers x ctx_len x n_kv*hd f32), the RoPE table and the step's
@@ -272,7 +284,8 @@ int loom_cuda_model_step(uint64_t handle, const uint32_t *d_token, const uint32_
  * device->host copy of the greedy token (and of the logits when logits !=
  * NULL), then a wait for completion. */
 int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *logits, uint32_t *next);
-/* Copy one cache row (layer, pos) of keys and values (n_kv*hd f32 each) to the
+/* Copy one cache row (layer, pos) of keys and values (n_kv*hd f32 each; with
+ * MLA the compressed row, kv_lora f32, and the rope row, rope_dim f32) to the
  * host -- the read-back that keeps a host copy authoritative (mlaReadCache,
  * backend.zig:191). */
 int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k, float *v);

@@ -48,7 +48,8 @@ class ModelLayer(C.Structure):  # loom_model_layer
     _fields_ = [("attn_norm", C.c_uint64), ("wq", C.c_uint64), ("wk", C.c_uint64), ("wv", C.c_uint64),
                 ("wo", C.c_uint64), ("q_norm", C.c_uint64), ("k_norm", C.c_uint64), ("ffn_norm", C.c_uint64),
                 ("ffn_gate", C.c_uint64), ("ffn_up", C.c_uint64), ("ffn_down", C.c_uint64), ("ffn", C.c_size_t),
-                ("moe", MoeDesc)]
+                ("moe", MoeDesc), ("q_a", C.c_uint64), ("q_a_norm", C.c_uint64), ("q_b", C.c_uint64),
+                ("kv_a", C.c_uint64), ("kv_a_norm", C.c_uint64), ("kv_b", C.c_uint64)]
 
 
 class ModelDesc(C.Structure):  # loom_model_desc
@@ -56,7 +57,8 @@ class ModelDesc(C.Structure):  # loom_model_desc
                 ("head_dim", C.c_size_t), ("rope_dim", C.c_size_t), ("vocab", C.c_size_t), ("ctx_len", C.c_size_t),
                 ("eps", C.c_float), ("rope_base", C.c_float), ("attn_logit_mul", C.c_float), ("rope_neox", C.c_int),
                 ("exact_order", C.c_int), ("token_embd", C.c_uint64), ("output_norm", C.c_uint64), ("output", C.c_uint64),
-                ("layers", C.POINTER(ModelLayer))]
+                ("layers", C.POINTER(ModelLayer)), ("mla", C.c_int), ("kv_lora", C.c_size_t), ("q_lora", C.c_size_t),
+                ("nope", C.c_size_t), ("v_head", C.c_size_t), ("mla_scale", C.c_float)]
 
 
 def header_symbols() -> list[str]:

@@ -395,6 +395,92 @@ __global__ void __launch_bounds__(256) k_attn_merge(const float *part, int n_hea
     }
 }
 
+// ---- MLA (deepseek.zig:851-1049) --------------------------------------------------------
+
+// CTA 0: the compressed row c = RMSNorm(kv_a[0..kvr]) * kv_a_norm (serial sum
+// of squares) and the rope row (kv_a[kvr..], RoPE at pos) into the caches.
+// CTAs 1..: one warp per head, RoPE of the head's q rope part in place.
+__global__ void __launch_bounds__(256) k_mla_front(const float *kv_a, const float *kv_norm, int kvr, int rope,
+                                                  float eps, float *q, int n_heads, int kd, int nope,
+                                                  const float *rope_tab, const uint32_t *pos_p, int ctx,
+                                                  float *c_cache, float *r_cache) {
+    __shared__ float red;
+    pdl_wait_();
+    pdl_trigger_();
+    const int pos = (int)*pos_p;
+    if (pos >= ctx) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *cs = rope_tab + (size_t)pos * rope;
+    if (blockIdx.x == 0) {
+        if (tid == 0) {
+            float ss = 0.0f;
+            for (int i = 0; i < kvr; i++) ss = fadd(ss, fmul(kv_a[i], kv_a[i]));
+            red = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)kvr), eps)));
+        }
+        __syncthreads();
+        float *c = c_cache + (size_t)pos * kvr;
+        for (int i = tid; i < kvr; i += blockDim.x) c[i] = fmul(fmul(kv_a[i], red), kv_norm[i]);
+        float *r = r_cache + (size_t)pos * rope;
+        for (int j = tid; 2 * j + 1 < rope; j += blockDim.x) {  // ropeNormPlain: adjacent pairs
+            const float a = kv_a[kvr + 2 * j], b = kv_a[kvr + 2 * j + 1], co = cs[2 * j], si = cs[2 * j + 1];
+            r[2 * j] = fsub(fmul(a, co), fmul(b, si));
+            r[2 * j + 1] = fadd(fmul(a, si), fmul(b, co));
+        }
+        return;
+    }
+    const int h = (blockIdx.x - 1) * (blockDim.x >> 5) + warp;
+    if (h >= n_heads) return;
+    float *v = q + (size_t)h * kd + nope;
+    for (int j = lane; 2 * j + 1 < rope; j += 32) {
+        const float a = v[2 * j], b = v[2 * j + 1], co = cs[2 * j], si = cs[2 * j + 1];
+        v[2 * j] = fsub(fmul(a, co), fmul(b, si));
+        v[2 * j + 1] = fadd(fmul(a, si), fmul(b, co));
+    }
+}
+
+// One CTA per head, the reference's order: score_t = (dotF32(qa, c_t) +
+// dotF32(q_rope, r_t)) * scale, softmax (max, exp, serial sum, 1/sum), then
+// c_acc = sum_t p_t c_t in position order from +0 (axpy).
+__global__ void __launch_bounds__(AT_THREADS) k_mla_attn(const float *qa, const float *q, int kvr, int rope, int kd,
+                                                        int nope, float scale, const uint32_t *pos_p, int ctx,
+                                                        const float *c_cache, const float *r_cache, float *c_acc) {
+    extern __shared__ float sc[];  // [ctx]
+    __shared__ float inv_s;
+    const int h = blockIdx.x, tid = threadIdx.x;
+    pdl_wait_();
+    pdl_trigger_();
+    const int pos = (int)*pos_p;
+    if (pos >= ctx) return;
+    const int seq = pos + 1;
+    const float *qh = qa + (size_t)h * kvr, *qr = q + (size_t)h * kd + nope;
+    for (int t = tid; t < seq; t += AT_THREADS)
+        sc[t] = fmul(fadd(dot_f32_ordered(qh, c_cache + (size_t)t * kvr, kvr),
+                          dot_f32_ordered(qr, r_cache + (size_t)t * rope, rope)),
+                     scale);
+    __syncthreads();
+    if (tid < 32) {
+        float m = -INFINITY;
+        for (int t = tid; t < seq; t += 32) m = fmaxf(m, sc[t]);
+        m = warp_max(m);
+        for (int t = tid; t < seq; t += 32) sc[t] = exp_f(fsub(sc[t], m));
+        __syncwarp();
+        if (tid == 0) {
+            float sum = 0.0f;
+            for (int t = 0; t < seq; t++) sum = fadd(sum, sc[t]);
+            inv_s = fdiv(1.0f, sum);
+        }
+        __syncwarp();
+        const float inv = inv_s;
+        for (int t = tid; t < seq; t += 32) sc[t] = fmul(sc[t], inv);
+    }
+    __syncthreads();
+    for (int j = tid; j < kvr; j += AT_THREADS) {
+        float o = 0.0f;
+        for (int t = 0; t < seq; t++) o = fadd(o, fmul(sc[t], c_cache[(size_t)t * kvr + j]));
+        c_acc[(size_t)h * kvr + j] = o;
+    }
+}
+
 unsigned cdiv_u(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 
 }  // namespace
@@ -410,6 +496,25 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
                     float *kc, float *vc, cudaStream_t st) {
     launch_pdl_(k_qk_rope, dim3(cdiv_u(n_heads + n_kv, QR_WARPS)), dim3(QR_WARPS * 32), 0, st, q, k, v, qn, kn,
                 n_heads, n_kv, hd, rope_dim, neox, rope, eps, pos, ctx, kc, vc);
+}
+
+void launch_mla_front(const float *kv_a, const float *kv_norm, int kvr, int rope, float eps, float *q, int n_heads,
+                      int kd, int nope, const float *rope_tab, const uint32_t *pos, int ctx, float *c_cache,
+                      float *r_cache, cudaStream_t st) {
+    launch_pdl_(k_mla_front, dim3(1 + cdiv_u(n_heads, 8)), dim3(256), 0, st, kv_a, kv_norm, kvr, rope, eps, q,
+                n_heads, kd, nope, rope_tab, pos, ctx, c_cache, r_cache);
+}
+
+void launch_mla_attn(const float *qa, const float *q, int kvr, int rope, int kd, int nope, int n_heads, float scale,
+                     const uint32_t *pos, int ctx, const float *c_cache, const float *r_cache, float *c_acc,
+                     cudaStream_t st) {
+    static bool smem_set = false;
+    if (!smem_set) {
+        cudaFuncSetAttribute(k_mla_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_ORDERED_LIMIT * 4);
+        smem_set = true;
+    }
+    launch_pdl_(k_mla_attn, dim3(n_heads), dim3(AT_THREADS), (size_t)ctx * 4, st, qa, q, kvr, rope, kd, nope, scale,
+                pos, ctx, c_cache, r_cache, c_acc);
 }
 
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx) {

@@ -47,4 +47,16 @@ void launch_attention(const float *q, const float *kc, const float *vc, int n_he
                       const uint32_t *pos, int ctx, float *part, float *out, bool ordered, XQW q256, XQW q32,
                       cudaStream_t st);
 
+// MLA (deepseek.zig:851-1049). front: the compressed and rope cache rows at
+// *pos from kv_a [kvr + rope] (RMSNorm with kv_norm; RoPE adjacent pairs) and
+// the RoPE of every head's q rope part (q [n_heads][kd], rope part at nope).
+void launch_mla_front(const float *kv_a, const float *kv_norm, int kvr, int rope, float eps, float *q, int n_heads,
+                      int kd, int nope, const float *rope_tab, const uint32_t *pos, int ctx, float *c_cache,
+                      float *r_cache, cudaStream_t st);
+// attention in compressed space over rows 0..*pos: c_acc [n_heads][kvr]
+// (ctx <= ATT_ORDERED_LIMIT)
+void launch_mla_attn(const float *qa, const float *q, int kvr, int rope, int kd, int nope, int n_heads, float scale,
+                     const uint32_t *pos, int ctx, const float *c_cache, const float *r_cache, float *c_acc,
+                     cudaStream_t st);
+
 }  // namespace loom

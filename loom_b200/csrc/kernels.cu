@@ -423,6 +423,46 @@ void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float 
     count_launch();
 }
 
+// MLA absorption (deepseek.zig:944-958): for head h and latent column j,
+// qa[h][j] = sum over r < nope, in order from +0, of q[h*kd + r] * W[h*(nope+vd) + r][j]
+// (axpy of each dequantized W_k row, exact dequantRow values), W = attn_kv_b [nh*(nope+vd)][kvr].
+__global__ void k_mla_absorb(WDev w, int kvr, int nope, int vd, int kd, const float *q, float *qa) {
+    const int h = blockIdx.y, j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= kvr) return;
+    const int be = block_elems(w.type), nb = kvr / be;
+    float a = 0.0f;
+    for (int r = 0; r < nope; r++) {
+        const uint64_t row = (uint64_t)h * (nope + vd) + r;
+        a = fadd(a, fmul(q[(size_t)h * kd + r], dequant_at(w, row * nb + j / be, j % be)));
+    }
+    qa[(size_t)h * kvr + j] = a;
+}
+
+// W_v per head (deepseek.zig:988): out[h*vd + r] = W[h*(nope+vd) + nope + r] . c_h, the
+// bit-exact quantized row dot of the tensor's type against head h's activation
+// (token h of x).
+__global__ void __launch_bounds__(256) k_mla_wv(WDev w, int nope, int vd, int nb, int n_heads, XQ x, float *out) {
+    const int lane = threadIdx.x & 31;
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (i >= n_heads * vd) return;
+    const int h = i / vd, r = i % vd;
+    float acc[1] = {0.0f};
+    rowdot<1>(w, ((uint64_t)h * (nope + vd) + nope + r) * nb, nb, x, h, 1, acc, lane);
+    if (lane == 0) out[i] = acc[0];
+}
+
+void launch_mla_absorb(const WDev &w, int kvr, int nope, int vd, int kd, int n_heads, const float *q, float *qa,
+                       cudaStream_t st) {
+    k_mla_absorb<<<dim3(cdiv(kvr, 128), n_heads), 128, 0, st>>>(w, kvr, nope, vd, kd, q, qa);
+    count_launch();
+}
+
+void launch_mla_wv(const WDev &w, int kvr, int nope, int vd, int n_heads, const XQ &x, float *out, cudaStream_t st) {
+    const int nb = kvr / block_elems(w.type);
+    k_mla_wv<<<cdiv((uint64_t)n_heads * vd, 8), 256, 0, st>>>(w, nope, vd, nb, n_heads, x, out);
+    count_launch();
+}
+
 void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cudaStream_t st) {
     const uint64_t n = nblk * (uint64_t)block_elems(w.type);
     if (n == 0) return;

@@ -42,6 +42,11 @@ void launch_synth(int type, uint8_t *raw, uint64_t blk0, uint64_t nblk, uint64_t
 void launch_repack(int type, const uint8_t *raw, uint8_t *q, uint8_t *sc, uint16_t *d, uint64_t nblk, cudaStream_t st);
 void launch_unpack(int type, const WDev &w, uint8_t *raw, uint64_t nblk, cudaStream_t st);
 void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cudaStream_t st);
+// MLA (deepseek.zig attnLayer): W_k absorbed into q per head, qa [n_heads][kvr];
+// and W_v applied per head to head h's quantized activation (token h of x), out [n_heads][vd]
+void launch_mla_absorb(const WDev &w, int kvr, int nope, int vd, int kd, int n_heads, const float *q, float *qa,
+                       cudaStream_t st);
+void launch_mla_wv(const WDev &w, int kvr, int nope, int vd, int n_heads, const XQ &x, float *out, cudaStream_t st);
 // row *tok of a [vocab][dim] tensor into x (embedding lookup)
 void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st);
 void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d,

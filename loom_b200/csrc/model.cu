@@ -64,6 +64,8 @@ struct LayerRt {
     loom_moe_desc moe{};
     bool dense = false;
     bool fused = false;       // the attention half runs as one cooperative launch (attn_block.cu)
+    Mat q_a, q_b, kv_a, kv_b;  // multi-head latent attention
+    const float *q_a_norm = nullptr, *kv_a_norm = nullptr;
     AttnBlockArgs blk{};
 };
 
@@ -71,7 +73,11 @@ struct Model {
     size_t dim = 0, n_layers = 0, nh = 0, nkv = 0, hd = 0, rope_dim = 0, vocab = 0, ctx = 0;
     float eps = 0, scale = 0;
     int neox = 0;
-    bool serial_norm = false, ordered_attn = false;
+    bool serial_norm = false, ordered_attn = false, exact = false;
+    bool mla = false;  // DeepSeek multi-head latent attention
+    size_t kvr = 0, qlora = 0, nope = 0, vd = 0, kd = 0;
+    float *qa_lat = nullptr, *qa_n = nullptr, *kva = nullptr, *qabs = nullptr, *cacc = nullptr;
+    XQW l256{}, l32{}, c256{}, c32{};  // q_a output quantized for q_b; per-head compressed results for W_v
     Mat embd, out;
     const float *out_norm = nullptr;
     std::vector<LayerRt> L;
@@ -190,6 +196,48 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
     for (size_t li = 0; li < m.n_layers && !m.persistent; li++) {
         const LayerRt &l = m.L[li];
         float *x = m.x[cur];
+        if (m.mla) {  // deepseek.zig:851-1049 attnLayer, then the FFN
+            launch_rmsnorm_q(x, nullptr, l.attn_norm, dim, m.eps, m.normed, m.need256 ? m.n256 : none,
+                             m.need32 ? m.n32 : none, m.serial_norm, st);
+            if (m.qlora) {
+                matvec(l.q_a, m.normed, m.n256, m.n32, m.qa_lat, st);
+                const bool k256 = act256(l.q_b.type), kq = l.q_b.type != T_F32 && l.q_b.type != T_Q5_0;
+                launch_rmsnorm_q(m.qa_lat, nullptr, l.q_a_norm, (int)m.qlora, m.eps, m.qa_n, kq && k256 ? m.l256 : none,
+                                 kq && !k256 ? m.l32 : none, m.exact || m.qlora <= (size_t)RN_SERIAL_MAX, st);
+                matvec(l.q_b, m.qa_n, m.l256, m.l32, m.q, st);
+            } else {
+                matvec(l.wq, m.normed, m.n256, m.n32, m.q, st);
+            }
+            matvec(l.kv_a, m.normed, m.n256, m.n32, m.kva, st);
+            const int kvr = (int)m.kvr, rope = (int)m.rope_dim;
+            float *cc = m.kc + li * m.ctx * m.kvr, *rc = m.vc + li * m.ctx * m.rope_dim;
+            launch_mla_front(m.kva, l.kv_a_norm, kvr, rope, m.eps, m.q, nh, (int)m.kd, (int)m.nope, m.rope, pos,
+                             (int)m.ctx, cc, rc, st);
+            launch_mla_absorb(l.kv_b.w, kvr, (int)m.nope, (int)m.vd, (int)m.kd, nh, m.q, m.qabs, st);
+            launch_mla_attn(m.qabs, m.q, kvr, rope, (int)m.kd, (int)m.nope, nh, m.scale, pos, (int)m.ctx, cc, rc,
+                            m.cacc, st);
+            const bool ck = act256(l.kv_b.type);
+            const XQW &cq = ck ? m.c256 : m.c32;
+            launch_quant_act(m.cacc, nh, kvr, kvr, ck, cq.q, cq.d, cq.s, ck ? kvr / 256 : kvr / 32, ck ? kvr / 16 : kvr / 32,
+                             st);
+            launch_mla_wv(l.kv_b.w, kvr, (int)m.nope, (int)m.vd, nh,
+                          XQ{cq.q, cq.d, cq.s, kvr, ck ? kvr / 256 : kvr / 32, ck ? kvr / 16 : kvr / 32, ck ? 1 : 0},
+                          m.att, st);
+            const int hv = nh * (int)m.vd;
+            if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
+                const bool k256 = act256(l.wo.type);
+                const XQW &a = k256 ? m.a256 : m.a32;
+                launch_quant_act(m.att, 1, hv, hv, k256, a.q, a.d, a.s, k256 ? hv / 256 : hv / 32, k256 ? hv / 16 : hv / 32,
+                                 st);
+            }
+            matvec(l.wo, m.att, m.a256, m.a32, m.proj, st);
+            launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, none, none, m.serial_norm, st);
+            float *xn = m.x[cur ^ 1];
+            if (int rc2 = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr, st))
+                return rc2;
+            cur ^= 1;
+            continue;
+        }
         if (l.fused) {  // one cooperative launch: norm, q/k/v, RoPE, attention, output projection, FFN norm
             AttnBlockArgs a = l.blk;
             a.x = x;
@@ -283,7 +331,10 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         return rt_decline("head_dim must be even, >= 8 and <= 256");
     if (d->rope_dim > d->head_dim || d->rope_dim % 2) return rt_decline("rope_dim must be even and <= head_dim");
     if (d->dim > 16384 || d->ctx_len > (1u << 18) || d->vocab > 0x7FFFFFFFu) return rt_decline("model shape too large");
-    {  // the split attention's merge keeps (256 / hd + 1) x chunks weights in shared memory
+    if (d->mla && (!d->kv_lora || !d->nope || !d->v_head || d->nope + d->rope_dim != d->head_dim ||
+                   d->ctx_len > (size_t)ATT_ORDERED_LIMIT))
+        return rt_decline("MLA: head_dim must be nope + rope_dim, kv_lora/v_head nonzero, ctx_len <= 32768");
+    if (!d->mla) {  // the split attention's merge keeps (256 / hd + 1) x chunks weights in shared memory
         const size_t hpc = std::min<size_t>(256 / d->head_dim + 1, d->n_heads);
         const size_t nsplit = (d->ctx_len + ATT_CH - 1) / ATT_CH;
         if (!d->exact_order && d->ctx_len > (size_t)ATT_ORDERED_MAX && hpc * nsplit * 4 > 200 * 1024)
@@ -311,7 +362,19 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         return rt_decline("exact_order takes contexts up to 32768 positions");
     }
     m->scale = d->attn_logit_mul / std::sqrt((float)d->head_dim);  // llama.zig:1116
+    m->exact = d->exact_order != 0;
+    if (d->mla) {
+        m->mla = true;
+        m->kvr = d->kv_lora;
+        m->qlora = d->q_lora;
+        m->nope = d->nope;
+        m->vd = d->v_head;
+        m->kd = d->nope + d->rope_dim;
+        m->scale = d->mla_scale;
+        m->ordered_attn = true;  // the compressed-space attention keeps the reference's order
+    }
     const size_t dim = d->dim, qd = d->n_heads * d->head_dim, kvd = d->n_kv_heads * d->head_dim;
+    const size_t hv = m->mla ? d->n_heads * d->v_head : qd;  // attention output width (the output projection's input)
     if (!mat(d->token_embd, d->vocab, dim, m->embd)) return bail(rt_decline("token_embd: unknown tensor or wrong size"));
     if (!mat(d->output, d->vocab, dim, m->out)) return bail(rt_decline("output: unknown tensor or wrong size"));
     bool ok = true;
@@ -326,9 +389,28 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         if (s.q_norm) l.qn = f32_vec(s.q_norm, d->head_dim, ok);
         if (s.k_norm) l.kn = f32_vec(s.k_norm, d->head_dim, ok);
         if (!ok) return bail(rt_decline("layer norms must be f32 [dim] / [head_dim]"));
-        if (!mat(s.wq, qd, dim, l.wq) || !mat(s.wk, kvd, dim, l.wk) || !mat(s.wv, kvd, dim, l.wv) ||
-            !mat(s.wo, dim, qd, l.wo))
+        if (m->mla) {  // deepseek.zig:860-875 tensors
+            const bool qok = m->qlora ? mat(s.q_a, m->qlora, dim, l.q_a) && mat(s.q_b, qd, m->qlora, l.q_b) &&
+                                            (l.q_a_norm = f32_vec(s.q_a_norm, m->qlora, ok)) != nullptr
+                                      : mat(s.wq, qd, dim, l.wq);
+            l.kv_a_norm = f32_vec(s.kv_a_norm, m->kvr, ok);
+            if (!qok || !ok || !mat(s.kv_a, m->kvr + d->rope_dim, dim, l.kv_a) ||
+                !mat(s.kv_b, d->n_heads * (m->nope + m->vd), m->kvr, l.kv_b) || !mat(s.wo, dim, hv, l.wo))
+                return bail(rt_decline("MLA weights: unknown tensor, unsupported type or wrong size"));
+            if (l.kv_b.type == T_F32 || l.kv_b.type == T_Q5_0)
+                return bail(rt_decline("MLA: kv_b must be a quantized type with int8 activations"));
+            if (m->qlora) {
+                need_kind(l.q_a.type, m->need256, m->need32);
+                if ((act256(l.q_b.type) && m->qlora % 256) || m->qlora % 32)
+                    return bail(rt_decline("MLA: q_lora width does not fit q_b's blocks"));
+            } else {
+                need_kind(l.wq.type, m->need256, m->need32);
+            }
+            need_kind(l.kv_a.type, m->need256, m->need32);
+        } else if (!mat(s.wq, qd, dim, l.wq) || !mat(s.wk, kvd, dim, l.wk) || !mat(s.wv, kvd, dim, l.wv) ||
+                   !mat(s.wo, dim, qd, l.wo)) {
             return bail(rt_decline("attention weights: unknown tensor, unsupported type or wrong size"));
+        }
         if (s.moe.n_expert) {
             l.moe = s.moe;
             if (l.moe.dim != dim) return bail(rt_decline("MoE layer dim differs from the model's"));
@@ -351,21 +433,33 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
             e.down = s.ffn_down;
             max_ffn = std::max(max_ffn, s.ffn);
         }
-        need_kind(l.wq.type, m->need256, m->need32);
-        need_kind(l.wk.type, m->need256, m->need32);
-        need_kind(l.wv.type, m->need256, m->need32);
+        if (!m->mla) {
+            need_kind(l.wq.type, m->need256, m->need32);
+            need_kind(l.wk.type, m->need256, m->need32);
+            need_kind(l.wv.type, m->need256, m->need32);
+        }
         need_kind(l.wo.type, m->att256, m->att32);
         m->L.push_back(l);
     }
     need_kind(m->out.type, m->need256, m->need32);
-    if ((m->need256 && dim % 256) || (m->att256 && qd % 256))
+    if ((m->need256 && dim % 256) || (m->att256 && hv % 256))
         return bail(rt_decline("a K-quant projection needs a width that is a multiple of 256"));
-    if ((m->need32 && dim % 32) || (m->att32 && qd % 32)) return bail(rt_decline("width not a multiple of 32"));
+    if ((m->need32 && dim % 32) || (m->att32 && hv % 32)) return bail(rt_decline("width not a multiple of 32"));
     // the MoE scratch, sized now so the step never allocates (graph capture)
     if (int rc = loom_cuda_reserve(1, dim, max_ffn, max_ne, max_nu)) return bail(rc);
     int rc = 0;
-    const size_t cache = d->n_layers * d->ctx_len * kvd;
-    if ((rc = dalloc(*m, m->kc, cache, true)) || (rc = dalloc(*m, m->vc, cache, true)) ||
+    // caches: k/v rows [layers][ctx][n_kv*hd]; MLA: compressed rows [..][kv_lora] and rope rows [..][rope]
+    const size_t cache_k = d->n_layers * d->ctx_len * (m->mla ? m->kvr : kvd);
+    const size_t cache_v = d->n_layers * d->ctx_len * (m->mla ? d->rope_dim : kvd);
+    if (m->mla) {
+        const size_t ql = m->qlora ? m->qlora : 1, lat = d->n_heads * m->kvr;
+        if ((rc = dalloc(*m, m->qa_lat, ql)) || (rc = dalloc(*m, m->qa_n, ql)) || (rc = alloc_xq(*m, m->l256, ql, true)) ||
+            (rc = alloc_xq(*m, m->l32, ql, false)) || (rc = dalloc(*m, m->kva, m->kvr + d->rope_dim)) ||
+            (rc = dalloc(*m, m->qabs, lat)) || (rc = dalloc(*m, m->cacc, lat)) || (rc = alloc_xq(*m, m->c256, lat, true)) ||
+            (rc = alloc_xq(*m, m->c32, lat, false)))
+            return bail(rc);
+    }
+    if ((rc = dalloc(*m, m->kc, cache_k, true)) || (rc = dalloc(*m, m->vc, cache_v, true)) ||
         (rc = dalloc(*m, m->rope, d->ctx_len * d->rope_dim)) || (rc = dalloc(*m, m->x[0], dim)) ||
         (rc = dalloc(*m, m->x[1], dim)) || (rc = dalloc(*m, m->normed, dim)) || (rc = dalloc(*m, m->q, qd)) ||
         (rc = dalloc(*m, m->k, kvd)) || (rc = dalloc(*m, m->v, kvd)) || (rc = dalloc(*m, m->att, qd)) ||
@@ -373,11 +467,11 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         (rc = dalloc(*m, m->part, attn_part_floats((int)m->nh, (int)m->nkv, (int)m->hd, (int)m->ctx))) ||
         (rc = dalloc(*m, m->logits, d->vocab)) || (rc = dalloc(*m, m->zero_logit, 1, true)) ||
         (rc = dalloc(*m, m->io_dev, 4, true)) || (rc = alloc_xq(*m, m->n256, dim, true)) ||
-        (rc = alloc_xq(*m, m->n32, dim, false)) || (rc = alloc_xq(*m, m->a256, qd, true)) ||
-        (rc = alloc_xq(*m, m->a32, qd, false)))
+        (rc = alloc_xq(*m, m->n32, dim, false)) || (rc = alloc_xq(*m, m->a256, std::max(qd, hv), true)) ||
+        (rc = alloc_xq(*m, m->a32, std::max(qd, hv), false)))
         return bail(rc);
     if ((rc = dalloc(*m, m->ab_bar, 64, true))) return bail(rc);
-    if (!m->ordered_attn && !getenv("LOOM_CUDA_NO_ATTN_BLOCK")) {
+    if (!m->ordered_attn && !m->mla && !getenv("LOOM_CUDA_NO_ATTN_BLOCK")) {
         for (size_t li = 0; li < d->n_layers; li++) {
             LayerRt &l = m->L[li];
             AttnBlockArgs &a = l.blk;
@@ -592,10 +686,11 @@ int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k,
     Model *m = find(handle);
     if (!m) return rt_decline("unknown model handle");
     if (layer >= m->n_layers || pos >= m->ctx) return rt_decline("cache row out of range");
-    const size_t kvd = m->nkv * m->hd, off = (layer * m->ctx + pos) * kvd;
+    // GQA: key and value rows (n_kv*hd each); MLA: compressed row (kv_lora) and rope row (rope_dim)
+    const size_t kw = m->mla ? m->kvr : m->nkv * m->hd, vw = m->mla ? m->rope_dim : m->nkv * m->hd;
     MCK(cudaStreamSynchronize(rt_stream(nullptr)));
-    if (k) MCK(cudaMemcpy(k, m->kc + off, kvd * 4, cudaMemcpyDeviceToHost));
-    if (v) MCK(cudaMemcpy(v, m->vc + off, kvd * 4, cudaMemcpyDeviceToHost));
+    if (k) MCK(cudaMemcpy(k, m->kc + (layer * m->ctx + pos) * kw, kw * 4, cudaMemcpyDeviceToHost));
+    if (v) MCK(cudaMemcpy(v, m->vc + (layer * m->ctx + pos) * vw, vw * 4, cudaMemcpyDeviceToHost));
     return LOOM_CUDA_OK;
 }
 

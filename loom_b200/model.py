@@ -246,15 +246,20 @@ class DeviceModel:
             L.attn_norm, L.ffn_norm = h(p + "attn_norm"), h(p + "ffn_norm")
             L.wq, L.wk, L.wv, L.wo = h(p + "attn_q"), h(p + "attn_k"), h(p + "attn_v"), h(p + "attn_output")
             L.q_norm, L.k_norm = h(p + "attn_q_norm"), h(p + "attn_k_norm")
-            if spec.n_expert:
+            L.q_a, L.q_a_norm, L.q_b = h(p + "attn_q_a"), h(p + "attn_q_a_norm"), h(p + "attn_q_b")
+            L.kv_a, L.kv_a_norm, L.kv_b = h(p + "attn_kv_a_mqa"), h(p + "attn_kv_a_norm"), h(p + "attn_kv_b")
+            if spec.is_moe_layer(i):
                 m = L.moe
                 m.dim, m.ffn, m.n_expert, m.n_used = spec.dim, spec.moe_ffn, spec.n_expert, spec.n_used
-                m.gating, m.weights_norm, m.weights_scale = 1, 1, 1.0
-                m.router = h(p + "ffn_gate_inp")
+                m.gating, m.weights_norm, m.weights_scale = spec.gating, int(spec.weights_norm), spec.weights_scale
+                m.router, m.router_bias = h(p + "ffn_gate_inp"), h(p + "exp_probs_b.bias")
                 m.gate, m.up, m.down = h(p + "ffn_gate_exps"), h(p + "ffn_up_exps"), h(p + "ffn_down_exps")
+                if spec.shexp_ffn:
+                    m.shexp_gate, m.shexp_up = h(p + "ffn_gate_shexp"), h(p + "ffn_up_shexp")
+                    m.shexp_down, m.shexp_ffn = h(p + "ffn_down_shexp"), spec.shexp_ffn
                 m.expert0, m.n_local = e0, nl
-                m.n_group = m.topk_group = 1
-                if i + 1 < spec.n_layers:
+                m.n_group, m.topk_group = spec.n_group, spec.topk_group
+                if i + 1 < spec.n_layers and spec.is_moe_layer(i + 1):
                     m.next_router = h(f"blk.{i + 1}.ffn_gate_inp")
             else:
                 L.ffn_gate, L.ffn_up, L.ffn_down = h(p + "ffn_gate"), h(p + "ffn_up"), h(p + "ffn_down")
@@ -264,6 +269,9 @@ class DeviceModel:
         d.head_dim, d.rope_dim, d.vocab, d.ctx_len = spec.head_dim, spec.rope_dim, spec.vocab, spec.ctx_len
         d.eps, d.rope_base, d.attn_logit_mul, d.rope_neox = spec.eps, spec.rope_base, 1.0, int(spec.rope_neox)
         d.exact_order = int(exact_order)
+        if spec.mla:
+            d.mla, d.kv_lora, d.q_lora, d.nope, d.v_head = 1, spec.kv_lora, spec.q_lora, spec.nope, spec.v_head
+            d.mla_scale = spec.attn_scale
         d.token_embd, d.output_norm, d.output = h("token_embd"), h("output_norm"), h("output")
         d.layers = self._layers
         self.desc = d
@@ -288,8 +296,10 @@ class DeviceModel:
                                                   _st(stream)), "model_step")
 
     def read_kv(self, layer: int, pos: int):
-        kvd = self.spec.n_kv_heads * self.spec.head_dim
-        k, v = np.empty(kvd, np.float32), np.empty(kvd, np.float32)
+        sp = self.spec
+        kw = sp.kv_lora if sp.mla else sp.n_kv_heads * sp.head_dim
+        vw = sp.rope_dim if sp.mla else sp.n_kv_heads * sp.head_dim
+        k, v = np.empty(kw, np.float32), np.empty(vw, np.float32)
         _lib.must(_lib.lib().loom_cuda_model_read_kv(self.handle, layer, pos, k.ctypes.data_as(C.c_void_p),
                                                      v.ctypes.data_as(C.c_void_p)), "model_read_kv")
         return k, v

@@ -37,3 +37,23 @@ def test_seam_declines_before_init():
     assert L.loom_cuda_register_arena(w.ctypes.data_as(C.c_void_p), w.nbytes) == _lib.DECLINED
     assert L.loom_cuda_materialize_arenas() == 0
     assert L.loom_cuda_take_cmdbuf_count() == 0
+
+
+def test_ctypes_structs_match_the_header(tmp_path):
+    """Every ctypes mirror of a header struct has the C size (a field missing on
+    either side would otherwise pass silently)."""
+    import shutil
+    import subprocess
+    import pytest
+    if not shutil.which("gcc"):
+        pytest.skip("no C compiler")
+    names = {"loom_moe_desc": _lib.MoeDesc, "loom_model_layer": _lib.ModelLayer, "loom_model_desc": _lib.ModelDesc,
+             "loom_weight": _lib.Weight, "loom_routed_cfg": _lib.RoutedCfg}
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include "%s"\nint main(void){%s return 0;}\n' % (
+        _lib.HEADER, " ".join('printf("%%zu\\n", sizeof(%s));' % n for n in names)))
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    for (n, cls), want in zip(names.items(), sizes):
+        assert C.sizeof(cls) == want, (n, C.sizeof(cls), want)

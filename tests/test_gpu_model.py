@@ -165,3 +165,43 @@ def test_persistent_model_kernel_equals_per_layer_path(be, monkeypatch):
     finally:
         a.free()
         b.free()
+
+
+def _ds_runner(spec, orc):
+    from oracle.oracle import DeepseekRunner
+    return DeepseekRunner(spec, host_tensors(spec, orc))
+
+
+def _v3_small():
+    from loom_b200.model import deepseek_v3
+    spec = deepseek_v3(n_layers=3, ctx_len=96, n_expert=16, dim=1024, n_heads=8, vocab=2048, n_dense=1)
+    spec.n_used, spec.n_group, spec.topk_group = 4, 4, 2
+    return spec
+
+
+@pytest.mark.parametrize("which,exact,tol", [("v2_lite", True, TOL), ("v2_lite", False, 2e-2), ("v3", True, TOL)],
+                         ids=["v2_lite_exact", "v2_lite_fast", "v3_qlora_grouped_exact"])
+def test_mla_model_matches_oracle(be, orc, which, exact, tol):
+    """MLA decode (deepseek.zig:851-1049) on the device against the oracle:
+    DeepSeek-V2-Lite shape (no q_lora, dense first layer, 2 shared experts,
+    Q8_0 down projections) and a reduced V3 shape (q_lora, sigmoid + bias,
+    grouped top-k, one shared expert); logits every step, the compressed and
+    rope cache rows."""
+    from loom_b200.model import deepseek_v2_lite
+    spec = deepseek_v2_lite(n_layers=2, ctx_len=96, n_expert=8, vocab=2048) if which == "v2_lite" else _v3_small()
+    ref = _ds_runner(spec, orc)
+    dev = DeviceModel(spec, exact_order=exact)
+    rng = np.random.default_rng(13)
+    try:
+        for pos in range(40):
+            tok = int(rng.integers(0, spec.vocab))
+            want = ref.step(tok, pos)
+            nxt, got = dev.decode(tok, pos, logits=True)
+            assert np.all(np.isfinite(got))
+            assert rel_l2(got, want) < tol, (pos, rel_l2(got, want))
+        c, r = dev.read_kv(1, 39)
+        cc = ref.cc.reshape(spec.n_layers, spec.ctx_len, spec.kv_lora)[1, 39]
+        rc = ref.rc.reshape(spec.n_layers, spec.ctx_len, spec.rope_dim)[1, 39]
+        assert rel_l2(c, cc) < tol and rel_l2(r, rc) < tol
+    finally:
+        dev.free()
