@@ -100,6 +100,117 @@ int loom_cuda_register_arena(const void *mem, size_t bytes);
 size_t loom_cuda_materialize_arenas(void);
 /* arena_error (src/compute/backend.zig:118). NULL when none. */
 const char *loom_cuda_arena_error(void);
+
+/* ---- GGUF tensor table (host side, no device needed) -----------------------
+ *
+ * gguf.parse (src/gguf/gguf.zig:251-325) over a file image, and the engine's
+ * checked tensor resolve (src/gguf/llama.zig:259-273, sizes by
+ * src/gguf/ggml.zig:143-153). A failed call leaves the reference's error name
+ * in loom_gguf_error(): NotGguf, UnsupportedGgufVersion, TruncatedGguf,
+ * BadTensorDims, BadAlignment, ArrayNestingTooDeep, UnknownValueType;
+ * resolve adds MissingTensor, UnsupportedTensorType, BadTensorShape. Names,
+ * strings and tensor data are views into the image, which must outlive the
+ * handle. */
+typedef struct loom_gguf loom_gguf;
+
+enum {
+    LOOM_GGUF_META_INT = 1,
+    LOOM_GGUF_META_UINT = 2,
+    LOOM_GGUF_META_FLOAT = 3,
+    LOOM_GGUF_META_BOOL = 4,
+    LOOM_GGUF_META_STRING = 5,
+    LOOM_GGUF_META_ARRAY_STR = 6,  /* `array` -> first string's u64 length */
+    LOOM_GGUF_META_ARRAY_F32 = 7,  /* `array` -> count little-endian f32 */
+    LOOM_GGUF_META_ARRAY_I32 = 8,
+    LOOM_GGUF_META_ARRAY = 9       /* other element types: only type and count kept */
+};
+
+/* TensorInfo (src/gguf/gguf.zig:36-47); dims past n_dims read 1. */
+typedef struct {
+    const char *name;
+    size_t name_len;
+    uint32_t n_dims;
+    uint64_t dims[8];
+    uint32_t ggml_type;
+    uint64_t offset; /* relative to the data section */
+} loom_gguf_tensor;
+
+/* MetaKV / MetaValue (src/gguf/gguf.zig:49-72). */
+typedef struct {
+    const char *key;
+    size_t key_len;
+    int kind;
+    int64_t i;
+    uint64_t u; /* UINT, and BOOL as 0/1 */
+    double f;
+    const char *str;
+    size_t str_len;
+    uint32_t elem_type;
+    uint64_t count;
+    const void *array;
+    uint64_t span_start, span_end; /* byte span of the whole pair in the file */
+} loom_gguf_value;
+
+/* Model.resolve's Tensor (src/gguf/llama.zig:259-273): a checked byte view. */
+typedef struct {
+    int ggml_type;
+    const void *data;
+    size_t bytes;
+    uint64_t ne0, ne1, ne2;
+} loom_gguf_view;
+
+loom_gguf *loom_gguf_parse(const void *image, size_t bytes);
+/* parse of a file mapped read-only (the mapping is released by close). */
+loom_gguf *loom_gguf_open(const char *path);
+const char *loom_gguf_error(void);
+void loom_gguf_close(loom_gguf *g);
+uint32_t loom_gguf_version(const loom_gguf *g);
+uint64_t loom_gguf_alignment(const loom_gguf *g);
+uint64_t loom_gguf_data_offset(const loom_gguf *g);
+uint64_t loom_gguf_file_size(const loom_gguf *g);
+const void *loom_gguf_image(const loom_gguf *g);
+size_t loom_gguf_n_tensors(const loom_gguf *g);
+size_t loom_gguf_n_meta(const loom_gguf *g);
+int loom_gguf_tensor_info(const loom_gguf *g, size_t i, loom_gguf_tensor *out);
+/* findTensor / findMeta (src/gguf/gguf.zig:92,120): DECLINED when absent. */
+int loom_gguf_find_tensor(const loom_gguf *g, const char *name, loom_gguf_tensor *out);
+int loom_gguf_meta(const loom_gguf *g, size_t i, loom_gguf_value *out);
+int loom_gguf_find_meta(const loom_gguf *g, const char *key, loom_gguf_value *out);
+/* getUint / getFloat / getString / getBool (src/gguf/gguf.zig:99-126),
+ * with the same kind conversions; DECLINED where the reference gives null. */
+int loom_gguf_get_uint(const loom_gguf *g, const char *key, uint64_t *out);
+int loom_gguf_get_float(const loom_gguf *g, const char *key, double *out);
+int loom_gguf_get_string(const loom_gguf *g, const char *key, const char **s, size_t *len);
+int loom_gguf_get_bool(const loom_gguf *g, const char *key, int *out);
+int loom_gguf_resolve(const loom_gguf *g, const char *name, loom_gguf_view *out);
+
+/* ---- verified upload ---------------------------------------------------------
+ *
+ * A content-addressed shard: the host byte ranges of one block of weights (an
+ * expert's gate, up and down planes) in order, and the SHA-256 of their
+ * concatenation -- the digest the reference keeps per range and checks
+ * before any read (src/core/hash.zig:12-23, src/p2p/weights.zig:862-879).
+ * Each extent must lie inside one weight tensor the backend holds (or it is
+ * uploaded as its own tensor) and start on a block boundary of it. */
+typedef struct {
+    loom_weight ext[4];
+    int n_ext;
+    uint8_t digest[32];
+} loom_shard;
+
+/* Compute each shard's SHA-256 on the device over the bytes the kernels will
+ * read (the device copy, its GGUF bytes rebuilt from the layout repack) and
+ * compare with `digest`. bad[i] (optional) = 1 on mismatch. A mismatching
+ * shard's tensors are dropped from the weight cache, so the next use uploads
+ * them again from the host -- the reference clears the range's holding bit
+ * (src/p2p/weights.zig:873-876). Returns OK and the mismatch count in
+ * *n_bad; DECLINED for an extent the backend cannot place. */
+int loom_cuda_verify_shards(const loom_shard *shards, size_t n, uint8_t *bad, size_t *n_bad);
+/* SHA-256 of device bytes (a test and manifest helper). */
+int loom_cuda_sha256_device(const void *d_bytes, size_t bytes, uint8_t digest[32]);
+/* SHA-256 of blocks [blk0, blk0 + nblk) of a device tensor, over their GGUF
+ * bytes (the layout repack undone). */
+int loom_cuda_tensor_sha256(uint64_t t, uint64_t blk0, uint64_t nblk, uint8_t digest[32]);
 /* takeCmdBufCount (src/compute/backend.zig:112): seam submissions since the
  * last call, then reset. */
 size_t loom_cuda_take_cmdbuf_count(void);
@@ -344,6 +455,17 @@ int loom_cuda_ep_init(int nranks, int rank, const void *id, size_t bytes);
 void loom_cuda_ep_shutdown(void);
 int loom_cuda_ep_rank(void);
 int loom_cuda_ep_size(void);
+/* 1 when the combine of small partials (T x dim <= 16384 floats) runs as the
+ * one-shot peer-memory kernel (every rank stores its partial into every rank's
+ * slot over NVLink, flags with release/acquire at system scope, rank-ordered
+ * sum: identical bits on every rank), 0 when it is NCCL's all-reduce
+ * (LOOM_CUDA_EP_NCCL set, more than 8 ranks, or setup failed on any rank).
+ * No counterpart in the reference (its experts stay on one host). */
+int loom_cuda_ep_peer_combine(void);
+/* The peer combine's error word (1 = a wait for a peer's flag gave up; the
+ * combine was skipped); synchronizes. After an error the backend stays on
+ * NCCL. 0 when none, -1 on a failed device. */
+int loom_cuda_ep_error(void);
 /* All-to-all form (token-sharded attention): each rank passes ITS OWN T
  * tokens (T may differ between ranks, and may be 0) and a descriptor of its
  * contiguous shard [r*E/R, (r+1)*E/R). The rank routes its tokens, sends each

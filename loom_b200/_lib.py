@@ -61,10 +61,31 @@ class ModelDesc(C.Structure):  # loom_model_desc
                 ("nope", C.c_size_t), ("v_head", C.c_size_t), ("mla_scale", C.c_float)]
 
 
+class GgufTensor(C.Structure):  # loom_gguf_tensor (TensorInfo, src/gguf/gguf.zig:36)
+    _fields_ = [("name", C.c_void_p), ("name_len", C.c_size_t), ("n_dims", C.c_uint32),
+                ("dims", C.c_uint64 * 8), ("ggml_type", C.c_uint32), ("offset", C.c_uint64)]
+
+
+class GgufValue(C.Structure):  # loom_gguf_value (MetaKV, src/gguf/gguf.zig:49-72)
+    _fields_ = [("key", C.c_void_p), ("key_len", C.c_size_t), ("kind", C.c_int), ("i", C.c_int64),
+                ("u", C.c_uint64), ("f", C.c_double), ("str", C.c_void_p), ("str_len", C.c_size_t),
+                ("elem_type", C.c_uint32), ("count", C.c_uint64), ("array", C.c_void_p),
+                ("span_start", C.c_uint64), ("span_end", C.c_uint64)]
+
+
+class GgufView(C.Structure):  # loom_gguf_view (Model.resolve's Tensor, src/gguf/llama.zig:259)
+    _fields_ = [("ggml_type", C.c_int), ("data", C.c_void_p), ("bytes", C.c_size_t),
+                ("ne0", C.c_uint64), ("ne1", C.c_uint64), ("ne2", C.c_uint64)]
+
+
+class Shard(C.Structure):  # loom_shard
+    _fields_ = [("ext", Weight * 4), ("n_ext", C.c_int), ("digest", C.c_uint8 * 32)]
+
+
 def header_symbols() -> list[str]:
     """Every function the public header declares."""
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"\b(loom_cuda_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(loom_(?:cuda|gguf)_\w+)\s*\(", src)))
 
 
 _lib = None
@@ -124,6 +145,8 @@ def lib() -> C.CDLL:
         "loom_cuda_ep_shutdown": (None, []),
         "loom_cuda_ep_rank": (i, []),
         "loom_cuda_ep_size": (i, []),
+        "loom_cuda_ep_peer_combine": (i, []),
+        "loom_cuda_ep_error": (i, []),
         "loom_cuda_ep_a2a_forward": (i, [C.POINTER(MoeDesc), vp, sz, vp, vp, vp, vp, vp]),
         "loom_cuda_ep_a2a_forward_cap": (i, [C.POINTER(MoeDesc), vp, sz, sz, vp, vp, vp, vp, vp]),
         "loom_cuda_argmax": (i, [vp, sz, vp, vp]),
@@ -138,6 +161,29 @@ def lib() -> C.CDLL:
         "loom_cuda_model_read_kv": (i, [u64, sz, sz, vp, vp]),
         "loom_cuda_model_free": (i, [u64]),
         "loom_cuda_model_error": (i, [u64]),
+        "loom_gguf_parse": (vp, [vp, sz]),
+        "loom_gguf_open": (vp, [C.c_char_p]),
+        "loom_gguf_error": (C.c_char_p, []),
+        "loom_gguf_close": (None, [vp]),
+        "loom_gguf_version": (C.c_uint32, [vp]),
+        "loom_gguf_alignment": (u64, [vp]),
+        "loom_gguf_data_offset": (u64, [vp]),
+        "loom_gguf_file_size": (u64, [vp]),
+        "loom_gguf_image": (vp, [vp]),
+        "loom_gguf_n_tensors": (sz, [vp]),
+        "loom_gguf_n_meta": (sz, [vp]),
+        "loom_gguf_tensor_info": (i, [vp, sz, C.POINTER(GgufTensor)]),
+        "loom_gguf_find_tensor": (i, [vp, C.c_char_p, C.POINTER(GgufTensor)]),
+        "loom_gguf_meta": (i, [vp, sz, C.POINTER(GgufValue)]),
+        "loom_gguf_find_meta": (i, [vp, C.c_char_p, C.POINTER(GgufValue)]),
+        "loom_gguf_get_uint": (i, [vp, C.c_char_p, C.POINTER(u64)]),
+        "loom_gguf_get_float": (i, [vp, C.c_char_p, C.POINTER(C.c_double)]),
+        "loom_gguf_get_string": (i, [vp, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(sz)]),
+        "loom_gguf_get_bool": (i, [vp, C.c_char_p, C.POINTER(i)]),
+        "loom_gguf_resolve": (i, [vp, C.c_char_p, C.POINTER(GgufView)]),
+        "loom_cuda_verify_shards": (i, [C.POINTER(Shard), sz, vp, C.POINTER(sz)]),
+        "loom_cuda_sha256_device": (i, [vp, sz, vp]),
+        "loom_cuda_tensor_sha256": (i, [u64, u64, u64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -600,6 +600,47 @@ int rt_decline(const char *why) { return decline(why); }
 int rt_fail(const char *what, cudaError_t e) { return fail(what, e); }
 uint64_t rt_buf_gen() { return g_buf_gen; }
 cudaError_t rt_wait() { return seam_wait(); }  // completion of the backend's stream, polled
+
+// A host weight range -> the cached device tensor that holds it (uploading it
+// as its own tensor when no cached tensor of that type contains it) and its
+// first block and block count there.
+int rt_place(int type, const void *data, size_t bytes, uint64_t *handle, uint64_t *blk0, uint64_t *nblk) {
+    const size_t bb = block_bytes(type);
+    if (!type_ok(type) || bb == 0) return decline("unsupported ggml type");
+    if (bytes == 0 || bytes % bb != 0) return decline("extent is not a whole number of blocks");
+    const uint8_t *p = static_cast<const uint8_t *>(data);
+    for (auto &kv : g_cache) {
+        const uint8_t *hp = static_cast<const uint8_t *>(std::get<0>(kv.first));
+        const size_t hb = std::get<1>(kv.first);
+        if (std::get<2>(kv.first) != type || p < hp || p + bytes > hp + hb) continue;
+        if ((size_t)(p - hp) % bb != 0) continue;
+        *handle = kv.second;
+        *blk0 = (size_t)(p - hp) / bb;
+        *nblk = bytes / bb;
+        return 0;
+    }
+    Tensor *t = nullptr;
+    if (int rc = resolve(type, data, bytes, t)) return rc;
+    *handle = g_cache[std::make_tuple(data, bytes, type)];
+    *blk0 = 0;
+    *nblk = bytes / bb;
+    return 0;
+}
+// Drop a cached weight tensor: the next seam call that names its bytes
+// uploads them again.
+void rt_evict(uint64_t handle) {
+    cudaStreamSynchronize(g_stream);
+    for (auto it = g_cache.begin(); it != g_cache.end();) {
+        if (it->second == handle) it = g_cache.erase(it);
+        else ++it;
+    }
+    auto it = g_tensors.find(handle);
+    if (it != g_tensors.end()) {
+        cudaFree(it->second.base);
+        g_tensors.erase(it);
+    }
+    g_buf_gen++;
+}
 }  // namespace loom
 
 extern "C" {

@@ -42,12 +42,29 @@ def main():
         torch.cuda.synchronize()
         err = float((out - want).norm() / want.norm())
         worst = max(worst, err)
-    t = torch.tensor([worst], device="cuda")
+    from loom_b200 import _lib
+    lib = _lib.lib()
+    assert lib.loom_cuda_ep_error() == 0
+    # the whole-token model, experts sharded, against the same model unsharded (rank 0)
+    from loom_b200.model import DeviceModel, qwen3_moe
+    spec = qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096)
+    sharded = DeviceModel(spec, expert_shard=D.expert_range(spec.n_expert, rank, world))
+    single = DeviceModel(spec) if rank == 0 else None
+    mworst = 0.0
+    for pos in range(24):
+        tok = (37 * pos + 11) % spec.vocab
+        nxt, lg = sharded.decode(tok, pos, logits=True)
+        if single is not None:
+            n1, l1 = single.decode(tok, pos, logits=True)
+            mworst = max(mworst, float(np.linalg.norm(lg - l1) / np.linalg.norm(l1)))
+    assert lib.loom_cuda_ep_error() == 0
+    t = torch.tensor([worst, mworst], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     if rank == 0:
-        print(f"EP_MAX_REL_L2 {float(t.item()):.3e}", flush=True)
+        print(f"EP_MAX_REL_L2 {float(t[0].item()):.3e} MODEL_REL_L2 {float(t[1].item()):.3e} "
+              f"PEER_COMBINE {lib.loom_cuda_ep_peer_combine()}", flush=True)
     dist.destroy_process_group()
-    return 0 if float(t.item()) < 1e-5 else 1
+    return 0 if float(t[0].item()) < 1e-5 and float(t[1].item()) < 2e-2 else 1
 
 
 if __name__ == "__main__":

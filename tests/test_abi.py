@@ -20,7 +20,7 @@ def test_every_exported_symbol_is_declared():
     import subprocess
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,
                          check=True).stdout
-    exported = {ln.split()[-1] for ln in out.splitlines() if ln.split() and ln.split()[-1].startswith("loom_cuda_")}
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.split() and ln.split()[-1].startswith(("loom_cuda_", "loom_gguf_"))}
     undeclared = sorted(exported - set(_lib.header_symbols()))
     assert not undeclared, undeclared
 
@@ -48,7 +48,8 @@ def test_ctypes_structs_match_the_header(tmp_path):
     if not shutil.which("gcc"):
         pytest.skip("no C compiler")
     names = {"loom_moe_desc": _lib.MoeDesc, "loom_model_layer": _lib.ModelLayer, "loom_model_desc": _lib.ModelDesc,
-             "loom_weight": _lib.Weight, "loom_routed_cfg": _lib.RoutedCfg}
+             "loom_weight": _lib.Weight, "loom_routed_cfg": _lib.RoutedCfg, "loom_gguf_tensor": _lib.GgufTensor,
+             "loom_gguf_value": _lib.GgufValue, "loom_gguf_view": _lib.GgufView, "loom_shard": _lib.Shard}
     src = tmp_path / "sz.c"
     src.write_text('#include <stdio.h>\n#include "%s"\nint main(void){%s return 0;}\n' % (
         _lib.HEADER, " ".join('printf("%%zu\\n", sizeof(%s));' % n for n in names)))

@@ -13,14 +13,21 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_rank_expert_parallel_layer():
+@pytest.mark.parametrize("combine", ["peer", "nccl"])
+def test_two_rank_expert_parallel_layer(combine):
+    """Sharded layers (T = 1, 5 through the peer-memory combine unless NCCL is
+    forced; T = 40 through NCCL) against the unsharded layer, and the
+    whole-token model sharded over 2 GPUs against the same model on one."""
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    if combine == "nccl":
+        env["LOOM_CUDA_EP_NCCL"] = "1"
     p = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
                         "--master-addr", "127.0.0.1", "--master-port", str(29600 + os.getpid() % 300),
                         os.path.join(ROOT, "tests", "ep_worker.py")], env=env, capture_output=True, text=True,
                        timeout=600)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-3000:]
     assert "EP_MAX_REL_L2" in p.stdout
+    assert f"PEER_COMBINE {1 if combine == 'peer' else 0}" in p.stdout
 
 
 @pytest.mark.parametrize("cfg", [
