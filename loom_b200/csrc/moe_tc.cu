@@ -4,7 +4,8 @@
 // Arithmetic (unchanged from the reference, ggml.zig kBlockDot :1002): each
 // MMA carries integer sub-block products that fp16 holds exactly,
 //   A = the weight's folded sub-block values   Q4_K  sc * q        (<= 945)
-//                                              Q6_K  sc * (q - 32) (|.| <= 2048 when |sc| <= 64)
+//                                              Q6_K  sc * (q - 32) (|.| <= 1024 when |sc| <= 32;
+//                                                    any int8 sc: split in two tiles, FMT 2)
 //   B = the int8 activations of quantizeX256 (ggml.zig:776),
 // accumulated in f32 in TMEM over half a super-block (128 products, every
 // partial sum an integer below 2^24, so exact). The epilogue adds the two
@@ -56,12 +57,20 @@ constexpr uint32_t TC_POLLS = 1u << 21;   // suspending polls (drains)
 constexpr int TC_XPITCH = 272;      // token row pitch in a raw stage: 16-byte reads by consecutive rows are conflict-free
 
 // FMT 0: gate and up, Q4_K (two matrices); FMT 1: down, Q6_K (one matrix).
+// FMT 2: down, Q6_K with any int8 sub-block scale: q - 32 = 8 (qh - 4) + ql
+// (qh = q >> 3, ql = q & 7) splits the folded value into two operand tiles,
+//   hi = sc * (qh - 4) (|.| <= 512) and lo = sc * ql (|.| <= 896),
+// each exact in fp16 with 128-product partial sums below 2^24; the epilogue
+// forms the integer 8 I_hi + I_lo. One raw matrix, two operand matrices.
 template <int FMT> struct TcFmt;
 template <> struct TcFmt<0> {
-    static constexpr int MATS = 2, WPITCH = 144;  // raw Q4_K block
+    static constexpr int MATS = 2, RMATS = 2, WPITCH = 144;  // raw Q4_K block
 };
 template <> struct TcFmt<1> {
-    static constexpr int MATS = 1, WPITCH = 208;  // Q6_K quants [128][192], then int8 scales [128][16]
+    static constexpr int MATS = 1, RMATS = 1, WPITCH = 208;  // Q6_K quants [128][192], then int8 scales [128][16]
+};
+template <> struct TcFmt<2> {
+    static constexpr int MATS = 2, RMATS = 1, WPITCH = 208;
 };
 
 // 2D tensor maps of the weights, rows x bytes: FMT 0 gate, up, shared gate,
@@ -81,7 +90,7 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 
 template <int FMT> struct TcLayout {
     static constexpr int MATS = TcFmt<FMT>::MATS, WPITCH = TcFmt<FMT>::WPITCH;
-    static constexpr size_t RAW_W = (size_t)MATS * 128 * WPITCH, RAW_X = (size_t)TC_N * TC_XPITCH;
+    static constexpr size_t RAW_W = (size_t)TcFmt<FMT>::RMATS * 128 * WPITCH, RAW_X = (size_t)TC_N * TC_XPITCH;
     static constexpr size_t RAW = RAW_W + RAW_X;
     static constexpr size_t OP_A = (size_t)8 * 128 * 16, OP = MATS * OP_A + (size_t)8 * TC_N * 16;
     static constexpr size_t HDR = (size_t)MATS * 128 * 16;      // per row: d, dmin, mins (2 words)
@@ -211,7 +220,7 @@ __device__ int g_tc_prof_on = 0;
 __device__ unsigned long long g_tc_prof[2][TC_PROF_SLOTS];  // by FMT
 // `on`: the CTA's copy of (g_tc_prof_on && blockIdx.x == 0), read once at kernel start
 __device__ __forceinline__ void tc_prof_add(int on, int fmt, int slot, long long cyc) {
-    if (on) atomicAdd(&g_tc_prof[fmt][slot], (unsigned long long)cyc);
+    if (on) atomicAdd(&g_tc_prof[fmt != 0][slot], (unsigned long long)cyc);
 }
 
 // bounded wait by one thread; a timeout raises the CTA's error flag
@@ -245,7 +254,7 @@ __device__ __forceinline__ void tc_pf_load(const DecodeArgs &A, const TcTile &t,
             xd = A.ad[(size_t)slot * (stride / 32) + blk];
         }
     }
-    if (FMT == 1) {
+    if (FMT != 0) {
         const int r0 = t.rt * 128;
         if (ct < 128 && r0 + ct < R) {
             const WDev w = t.shared ? A.sdn : A.dn;
@@ -490,18 +499,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
                                 const __half2 sc2 = __half2half2(__int2half_rn(sc));
                                 const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
                                 uint32_t o[8];
+                                uint32_t o2[8];  // FMT 2: the lo tile (o holds hi)
 #pragma unroll
                                 for (int w = 0; w < 4; w++) {
                                     const uint32_t lo4 = (p ? lw[w] >> 4 : lw[w]) & 0x0F0F0F0Fu;
                                     const uint32_t qb = lo4 | (((hw[w] >> (2 * gg)) & 0x03030303u) << 4);
-                                    o[2 * w] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), sc2));
-                                    o[2 * w + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), sc2));
+                                    if (FMT == 1) {
+                                        o[2 * w] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), sc2));
+                                        o[2 * w + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), sc2));
+                                    } else {
+                                        const __half2 k1028 = tc_u2h(0x64046404u), k1024 = tc_u2h(0x64006400u);
+                                        const uint32_t qh = (qb >> 3) & 0x07070707u, ql = qb & 0x07070707u;
+                                        o[2 * w] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qh, 0x64646464u, 0x7170)), k1028), sc2));
+                                        o[2 * w + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qh, 0x64646464u, 0x7372)), k1028), sc2));
+                                        o2[2 * w] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(ql, 0x64646464u, 0x7170)), k1024), sc2));
+                                        o2[2 * w + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(ql, 0x64646464u, 0x7372)), k1024), sc2));
+                                    }
                                 }
                                 *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0)) = make_uint4(o[0], o[1], o[2], o[3]);
                                 *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                                if (FMT == 2) {
+                                    uint8_t *tL = tA + Ly::OP_A;
+                                    *reinterpret_cast<uint4 *>(tL + tc_sw(r, c0)) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+                                    *reinterpret_cast<uint4 *>(tL + tc_sw(r, c0 + 1)) = make_uint4(o2[4], o2[5], o2[6], o2[7]);
+                                }
                             } else {
-                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0)) = make_uint4(0, 0, 0, 0);
-                                *reinterpret_cast<uint4 *>(tA + tc_sw(r, c0 + 1)) = make_uint4(0, 0, 0, 0);
+#pragma unroll
+                                for (int m = 0; m < MATS; m++) {
+                                    *reinterpret_cast<uint4 *>(tA + m * Ly::OP_A + tc_sw(r, c0)) = make_uint4(0, 0, 0, 0);
+                                    *reinterpret_cast<uint4 *>(tA + m * Ly::OP_A + tc_sw(r, c0 + 1)) = make_uint4(0, 0, 0, 0);
+                                }
                             }
                         }
                     }
@@ -620,6 +647,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
                 for (int j = 0; j < 4; j++) {  // token groups of 8, alternating between the two warp halves
                     const int t0 = 8 * (2 * j + th);
                     if (t0 >= tl.nc) break;  // warp-uniform
+                    if (FMT == 2) {  // one output: I = 8 I_hi + I_lo, every part an exact integer
+                        float h0[8], h1[8], l0[8], l1[8];
+                        const uint32_t col = (uint32_t)b * (MATS * 2 * TC_N) + (uint32_t)t0;
+                        tmem_f8(tmem, qq, col, h0);
+                        tmem_f8(tmem, qq, col + TC_N, h1);
+                        tmem_f8(tmem, qq, col + 2 * TC_N, l0);
+                        tmem_f8(tmem, qq, col + 3 * TC_N, l1);
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const int ti2 = t0 + i;
+                            if (ti2 < tl.nc) {
+                                const int I = 8 * (__float2int_rn(h0[i]) + __float2int_rn(h1[i])) + __float2int_rn(l0[i]) +
+                                              __float2int_rn(l1[i]);
+                                acc[0][8 * j + i] = fadd(acc[0][8 * j + i],
+                                                         fmul(fmul(txd[ti2], __uint_as_float(hr[0].x)), __int2float_rn(I)));
+                            }
+                        }
+                        continue;
+                    }
 #pragma unroll
                     for (int m = 0; m < MATS; m++) {
                         float v0[8], v1[8];
@@ -732,24 +778,26 @@ static TcFn tc_gu_fn(int nb) {
     }
     return nullptr;
 }
-static TcFn tc_dn_fn(int nb) {
+static TcFn tc_dn_fn(int nb, bool split) {
     switch (nb) {
-        case 2: return k_moe_tc<1, 2>;
-        case 3: return k_moe_tc<1, 3>;
-        case 4: return k_moe_tc<1, 4>;
-        case 8: return k_moe_tc<1, 8>;
+        case 2: return split ? k_moe_tc<2, 2> : k_moe_tc<1, 2>;
+        case 3: return split ? k_moe_tc<2, 3> : k_moe_tc<1, 3>;
+        case 4: return split ? k_moe_tc<2, 4> : k_moe_tc<1, 4>;
+        case 8: return split ? k_moe_tc<2, 8> : k_moe_tc<1, 8>;
     }
     return nullptr;
+}
+// Small Q6_K scales (every |sc| <= 32) take the one-tile fold; others the split.
+static bool tc_dn_split(const DecodeArgs &A) {
+    return !(A.dn.pad_ & WDEV_Q6K_SMALL_SCALES) || (A.has_shared && !(A.sdn.pad_ & WDEV_Q6K_SMALL_SCALES));
 }
 
 bool moe_mma_supported(const DecodeArgs &A) {
     if (A.g.type != T_Q4_K || A.u.type != T_Q4_K || A.dn.type != T_Q6_K) return false;
     if (A.dim % 256 || A.ffn % 256 || A.n_local + 1 > 1024) return false;
-    if (!tc_gu_fn(A.dim / 256) || !tc_dn_fn(A.ffn / 256)) return false;
-    if (!(A.dn.pad_ & WDEV_Q6K_SMALL_SCALES)) return false;  // the fold sc*(q-32) must stay exact in fp16
+    if (!tc_gu_fn(A.dim / 256) || !tc_dn_fn(A.ffn / 256, false)) return false;
     if (!tc_encoder()) return false;
-    if (A.has_shared && (A.sg.type != T_Q4_K || A.su.type != T_Q4_K || A.sdn.type != T_Q6_K || A.shexp_ffn != A.ffn ||
-                         !(A.sdn.pad_ & WDEV_Q6K_SMALL_SCALES)))
+    if (A.has_shared && (A.sg.type != T_Q4_K || A.su.type != T_Q4_K || A.sdn.type != T_Q6_K || A.shexp_ffn != A.ffn))
         return false;
     return true;
 }
@@ -765,7 +813,8 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
         if (n_sm <= 0) n_sm = 148;
     }
-    TcFn gf = tc_gu_fn(A.dim / 256), df = tc_dn_fn(A.ffn / 256);
+    const bool split = tc_dn_split(A);
+    TcFn gf = tc_gu_fn(A.dim / 256), df = tc_dn_fn(A.ffn / 256, split);
     const int nbg = A.dim / 256, nbd = A.ffn / 256;
     TcMaps mg, md;
     memset(&mg, 0, sizeof mg);
@@ -779,7 +828,8 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
              tc_map(md.m[2], A.sdn.q, nbd * 192ull, (uint64_t)A.dim, 192) &&
              tc_map(md.m[3], A.sdn.sc, nbd * 16ull, (uint64_t)A.dim, 16);
     if (!ok) return cudaErrorInvalidValue;
-    constexpr size_t gs = TcLayout<0>::SMEM, ds = TcLayout<1>::SMEM;
+    constexpr size_t gs = TcLayout<0>::SMEM;
+    const size_t ds = split ? TcLayout<2>::SMEM : TcLayout<1>::SMEM;
     cudaError_t e = cudaFuncSetAttribute(gf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(df, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ds);
     if (e != cudaSuccess) return e;

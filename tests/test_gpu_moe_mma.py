@@ -102,21 +102,66 @@ def test_mma_token_counts(be, orc, T):
     assert np.array_equal(bits(mma), bits(ref)), rel_l2(mma, ref)
 
 
-def test_mma_declines_large_q6k_scales(be, orc):
-    """Q6_K down weights with a sub-block scale beyond +-32 (the fp16 fold and
-    its f32 sums would no longer be exact): the layer stays on the int8
-    kernels and still matches them."""
-    ne, k, dim, ffn, T = 16, 4, 1024, 512, 128
+def _full_range_scales(d, seed, extreme):
+    """Q6_K blocks with int8 sub-block scales over the whole range real GGUF
+    files use (llama.cpp maps each super-block's largest sub-block to -128 or
+    127); `extreme`: every scale -128 and every quant 0, the largest folded
+    values (sc * (q - 32) = 4096) the format allows."""
+    d = d.copy().reshape(-1, 210)
+    rng = np.random.default_rng(seed)
+    if extreme:
+        d[:, :192] = 0
+        d[:, 192:208] = np.uint8(0x80)
+    else:
+        d[:, 192:208] = rng.integers(0, 256, (d.shape[0], 16), dtype=np.uint8)
+        d[:, 192] = np.where(rng.random(d.shape[0]) < 0.5, 0x80, 0x7F)  # -128 / 127 in every block
+    return d.reshape(-1)
+
+
+@pytest.mark.parametrize("extreme", [False, True], ids=["random", "extreme"])
+@pytest.mark.parametrize("shared", [False, True], ids=["routed", "shared"])
+def test_mma_full_range_q6k_scales(be, orc, extreme, shared):
+    """Q6_K down weights with scales beyond +-32 run on the tensor cores (the
+    split fold: two fp16 tiles, 8 I_hi + I_lo) and equal the int8 kernels,
+    which are the reference's integer arithmetic, bit for bit."""
+    ne, k, dim, ffn, T = 16, 4, 1024, 512, 160
     g, u, d = synth_layer(orc, 51, ne, dim, ffn, 12, 12, 14)
-    d = d.copy()
-    d[192 + 3] = 100  # block 0, scale 3 (int8 100)
+    d = _full_range_scales(d, 54, extreme)
     rw = orc.synth(0, ne * dim, seed=52, sigma=0.02)
+    kw = {}
+    if shared:
+        sg, su, sd = synth_layer(orc, 55, 1, dim, ffn, 12, 12, 14)
+        kw = dict(shexp=(D.DeviceTensor.upload(12, sg), D.DeviceTensor.upload(12, su),
+                         D.DeviceTensor.upload(14, _full_range_scales(sd, 56, extreme))), shexp_ffn=ffn)
+    L = D.MoeLayer(dim, ffn, ne, k, D.DeviceTensor.upload(12, g), D.DeviceTensor.upload(12, u),
+                   D.DeviceTensor.upload(14, d), router=D.DeviceTensor.upload(0, rw), **kw)
+    x = torch.from_numpy(orc.synth(0, T * dim, seed=53, sigma=1.0).reshape(T, dim)).cuda()
+    a, ia = _run(L, x, 3, k, path=3)
+    b, ib = _run(L, x, 2, k, path=2)
+    assert np.array_equal(ia, ib)
+    assert np.array_equal(bits(a), bits(b)), rel_l2(a, b)
+    assert np.isfinite(a).all()
+
+
+def test_mma_full_range_q6k_vs_oracle(be, orc):
+    """The split fold against the CPU oracle's moeLayer directly."""
+    ne, k, dim, ffn, T = 16, 4, 1024, 512, 64
+    g, u, d = synth_layer(orc, 61, ne, dim, ffn, 12, 12, 14)
+    d = _full_range_scales(d, 62, False)
+    rw = orc.synth(0, ne * dim, seed=63, sigma=0.02)
+    x = orc.synth(0, T * dim, seed=64, sigma=1.0).reshape(T, dim)
     L = D.MoeLayer(dim, ffn, ne, k, D.DeviceTensor.upload(12, g), D.DeviceTensor.upload(12, u),
                    D.DeviceTensor.upload(14, d), router=D.DeviceTensor.upload(0, rw))
-    x = torch.from_numpy(orc.synth(0, T * dim, seed=53, sigma=1.0).reshape(T, dim)).cuda()
-    a, ia = _run(L, x, 3, k, path=2)
-    b, ib = _run(L, x, 2, k, path=2)
-    assert np.array_equal(ia, ib) and np.array_equal(bits(a), bits(b))
+    got, gids = _run(L, torch.from_numpy(x).cuda(), 3, k, path=3)
+    want, wids = orc.moe_layer(x, rw, (12, g), (12, u), (14, d), ffn, ne, k)
+    logits = orc.matmul(0, rw.view(np.uint8), x, ne, dim)
+    compared = 0
+    for t in range(T):
+        if _route_gaps_ok(logits[t], k):
+            assert list(gids[t]) == list(wids[t]), t
+            assert rel_l2(got[t], want[t]) < TOL, (t, rel_l2(got[t], want[t]))
+            compared += 1
+    assert compared >= T * 3 // 4
 
 
 @pytest.mark.parametrize("cfg", [
