@@ -406,6 +406,11 @@ int loom_cuda_model_read_kv(uint64_t handle, size_t layer, size_t pos, float *k,
  * none, -1 on an unknown handle or a failed stream. */
 int loom_cuda_model_error(uint64_t handle);
 int loom_cuda_model_free(uint64_t handle);
+/* Diagnostic (no counterpart in the reference; the spirit of LOOM_PROFILE,
+ * deepseek.zig:705-850): layer >= 0 makes that layer's fused attention
+ * launch record %globaltimer ns of CTA 0 at its phase boundaries (zeroed
+ * now); layer < 0 copies min(n, 32) recorded words to out. */
+int loom_cuda_model_trace(uint64_t handle, int layer, unsigned long long *out, size_t n);
 
 /* A decode step (one token) through a whole stack of MoE layers as ONE
  * persistent cooperative kernel: x_{l+1} = x_l + MoE_l(x_l) for every layer,

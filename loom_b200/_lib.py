@@ -161,6 +161,7 @@ def lib() -> C.CDLL:
         "loom_cuda_model_read_kv": (i, [u64, sz, sz, vp, vp]),
         "loom_cuda_model_free": (i, [u64]),
         "loom_cuda_model_error": (i, [u64]),
+        "loom_cuda_model_trace": (i, [u64, i, vp, sz]),
         "loom_gguf_parse": (vp, [vp, sz]),
         "loom_gguf_open": (vp, [C.c_char_p]),
         "loom_gguf_error": (C.c_char_p, []),

@@ -519,7 +519,7 @@ void launch_mla_attn(const float *qa, const float *q, int kvr, int rope, int kd,
 
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx) {
     const size_t nsplit = (ctx + ATT_CH - 1) / ATT_CH;
-    return (size_t)n_kv * nsplit * (n_heads / n_kv) * (hd + 2);
+    return (size_t)n_kv * nsplit * (n_heads / n_kv) * (hd + 4);  // records of hd + 2 floats, or hd + 4 (16-byte rows)
 }
 
 bool attn_merge_quantizes(int n_heads, int hd, int ctx) {

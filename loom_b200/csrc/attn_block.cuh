@@ -11,7 +11,7 @@ constexpr int MAX_AB_HD = 256;
 
 struct AttnBlockArgs {
     float *x;                  // [dim] residual stream: x += W_o . attention (in place)
-    float *normed;             // [dim] out: RMSNorm(x) * ffn_norm, the FFN's input
+    float *normed;             // [dim] out: RMSNorm(x) * ffn_norm, the FFN's input; null: not computed
     const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
     float eps;
     int serial;                // RMSNorm sum of squares in the reference's serial order
@@ -31,6 +31,7 @@ struct AttnBlockArgs {
     unsigned long long *trace; // optional [8]: %globaltimer ns of CTA 0 at the phase boundaries (diagnostic)
     // set by attn_block_plan
     int groups, so, ta, tv, to;
+    int merge_bulk;             // the merge CTAs bulk-copy their heads' partial records into shared memory
     size_t smem, off_o, off_u;  // dynamic shared memory: total, staged output-projection rows, union area
 };
 

@@ -134,6 +134,30 @@ __device__ __forceinline__ void load_row_chunk(float (&w)[RR_CHUNK], const float
 // CTA 0 of a token's router cluster, once every logit is in `choice`:
 // route (moe.zig:106) and quantize the token's activation (smx) for the expert
 // kernels. nw = warps in the CTA.
+// The FFN RMSNorm of the layer folded into the router kernel's prologue
+// (llama.zig:1198 before the MoE block): sx holds the raw residual row; every
+// CTA of the cluster normalizes its own copy, sums of squares as a tree (per
+// thread, then warps in order), out = x * (1 / sqrt(ss / dim + eps)) * w.
+__device__ __noinline__ void prenorm_smem(float *sx, const float *w, int dim, float eps) {
+    __shared__ float red[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    float ss = 0.0f;
+    for (int i = tid; i < dim; i += blockDim.x) ss = fadd(ss, fmul(sx[i], sx[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = fadd(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < nw; i++) t = fadd(t, red[i]);
+        red[0] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(t, (float)dim), eps)));
+    }
+    __syncthreads();
+    const float scale = red[0];
+    for (int i = tid; i < dim; i += blockDim.x) sx[i] = fmul(fmul(sx[i], scale), __ldg(w + i));
+    __syncthreads();
+}
+
 __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const float *smx, float *scores, float *choice,
                                             int nw) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -195,6 +219,7 @@ __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
     trace_begin(A, 3);
     for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = xt[i];
     __syncthreads();
+    if (A.prenorm_w) prenorm_smem(smx, A.prenorm_w, dim, A.prenorm_eps);
     if (A.router) {
         for (int row = gw; row < ne; row += RR_WARPS_ALL) {
             const float *wr = A.router + (size_t)row * dim;
@@ -251,6 +276,7 @@ __global__ void __launch_bounds__(RR2_WARPS * 32) k_router_tma(DecodeArgs A) {
     trace_begin(A, 3);
     for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = xt[i];
     __syncthreads();
+    if (A.prenorm_w) prenorm_smem(smx, A.prenorm_w, dim, A.prenorm_eps);
     const long long c0 = clock64();
     if (nrows > 0 && !mbar_wait(&bar, 0, WAIT_POLLS)) {
         if (threadIdx.x == 0 && A.err) atomicOr(A.err, 1);

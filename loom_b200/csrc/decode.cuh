@@ -24,6 +24,8 @@ struct DecodeArgs {
     const int *ids_in;       // optional routing decided elsewhere [T][n_used] (then no router, no route) ...
     const float *gates_in;   // ... with these gates (null: 1.0)
     const float *x;          // [T][dim]
+    const float *prenorm_w;  // T = 1 router kernels: x is the raw residual stream, normed in the
+    float prenorm_eps;       // prologue as RMSNorm(x) * prenorm_w (null: x is already the FFN input)
     float *out;              // [T][dim]
     const float *residual;   // [T][dim] or null
     float *logits;           // scratch [T][n_expert]

@@ -40,6 +40,7 @@ int rt_decline(const char *why);
 int rt_fail(const char *what, cudaError_t e);
 uint64_t rt_buf_gen();
 cudaError_t rt_wait();
+void rt_moe_prenorm(const float *w, float eps);
 }  // namespace loom
 
 using namespace loom;
@@ -74,6 +75,7 @@ struct Model {
     float eps = 0, scale = 0;
     int neox = 0;
     bool serial_norm = false, ordered_attn = false, exact = false;
+    bool fold_ffn_norm = false;  // fused layers: the MoE router kernel applies the FFN RMSNorm
     bool mla = false;  // DeepSeek multi-head latent attention
     size_t kvr = 0, qlora = 0, nope = 0, vd = 0, kd = 0;
     float *qa_lat = nullptr, *qa_n = nullptr, *kva = nullptr, *qabs = nullptr, *cacc = nullptr;
@@ -89,6 +91,7 @@ struct Model {
           *proj = nullptr, *part = nullptr, *logits = nullptr, *zero_logit = nullptr;
     XQW n256{}, n32{}, a256{}, a32{};
     unsigned long long *ab_bar = nullptr;  // grid-barrier state of the fused attention kernel
+    unsigned long long *ab_trace = nullptr;  // diagnostic: phase timestamps of one layer's fused attention
     bool persistent = false;  // every layer in one persistent launch (model_kernel.cu)
     MkArgs mk{};
     MkLayer *mk_layers = nullptr;
@@ -116,6 +119,7 @@ template <class T> int dalloc(Model &m, T *&p, size_t n, bool zero = false) {
 
 void free_model(Model *m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->ab_trace) cudaFree(m->ab_trace);
     for (void *p : m->allocs) cudaFree(p);
     if (m->io_host) cudaFreeHost(m->io_host);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -244,8 +248,9 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
             a.pos = pos;
             MCK(launch_attn_block(a, st));
             float *xn = m.x[cur ^ 1];
-            if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr,
-                                               st))
+            if (m.fold_ffn_norm) rt_moe_prenorm(l.ffn_norm, m.eps);  // the router kernel normalizes x itself
+            if (int rc = loom_cuda_moe_forward(&l.moe, m.fold_ffn_norm ? x : m.normed, 1, xn, x,
+                                               l.dense ? m.zero_logit : nullptr, nullptr, st))
                 return rc;
             cur ^= 1;
             continue;
@@ -471,11 +476,14 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         (rc = alloc_xq(*m, m->a32, std::max(qd, hv), false)))
         return bail(rc);
     if ((rc = dalloc(*m, m->ab_bar, 64, true))) return bail(rc);
+    // The FFN RMSNorm moves into the MoE layer's router kernel (one grid barrier
+    // and one single-CTA phase less per layer) where the tree-order norm is used.
+    m->fold_ffn_norm = !m->serial_norm && !getenv("LOOM_CUDA_NO_NORM_FOLD");
     if (!m->ordered_attn && !m->mla && !getenv("LOOM_CUDA_NO_ATTN_BLOCK")) {
         for (size_t li = 0; li < d->n_layers; li++) {
             LayerRt &l = m->L[li];
             AttnBlockArgs &a = l.blk;
-            a.normed = m->normed;
+            a.normed = m->fold_ffn_norm ? nullptr : m->normed;
             a.attn_norm = l.attn_norm;
             a.ffn_norm = l.ffn_norm;
             a.q_norm = l.qn;
@@ -703,6 +711,28 @@ int loom_cuda_model_error(uint64_t handle) {
     const int e = (int)(unsigned)h[2];
     if (e && cudaMemset(m->ab_bar, 0, 32 * sizeof(unsigned long long)) != cudaSuccess) return -1;  // re-arm (counter, flag)
     return e;
+}
+
+int loom_cuda_model_trace(uint64_t handle, int layer, unsigned long long *out, size_t n) {
+    if (int rc = rt_need_init()) return rc;
+    Model *m = find(handle);
+    if (!m) return rt_decline("unknown model handle");
+    if (layer >= 0) {
+        if ((size_t)layer >= m->n_layers) return rt_decline("layer out of range");
+        if (!m->ab_trace) MCK(cudaMalloc(&m->ab_trace, 32 * sizeof(unsigned long long)));
+        MCK(cudaMemset(m->ab_trace, 0, 32 * sizeof(unsigned long long)));
+        for (auto &l : m->L) l.blk.trace = nullptr;
+        m->L[layer].blk.trace = m->ab_trace;
+        if (m->exec) {  // a captured graph holds the old arguments
+            cudaGraphExecDestroy(m->exec);
+            m->exec = nullptr;
+        }
+        return LOOM_CUDA_OK;
+    }
+    if (!m->ab_trace) return rt_decline("tracing was not enabled");
+    MCK(cudaDeviceSynchronize());
+    MCK(cudaMemcpy(out, m->ab_trace, std::min<size_t>(n, 32) * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    return LOOM_CUDA_OK;
 }
 
 int loom_cuda_model_free(uint64_t handle) {

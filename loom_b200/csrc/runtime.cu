@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "../../include/loom_cuda.h"
+#include "attn.cuh"
 #include "decode.cuh"
 #include "ep.cuh"
 #include "kernels.cuh"
@@ -131,6 +132,7 @@ struct Scratch {
     DBuf io_in, io_out, io_aux, raw;
     // all-to-all expert parallelism: home-side lists and rows, receive-side rows
     DBuf tmp;  // small synchronous scratch (tensor scans)
+    DBuf prenormed;  // the FFN input when a layer's RMSNorm is not folded into its router kernel
     DBuf amax;  // argmax slot + counter (zeroed once, left zeroed by the kernel); lm_head logits
     DBuf head_logits;
     DBuf a2a_i, a2a_sx, a2a_yb, a2a_ysh, a2a_rx, a2a_re, a2a_yr, a2a_g1;
@@ -538,19 +540,49 @@ inline uint64_t fbits(float f) {
     return u;
 }
 
+// The layer's FFN RMSNorm weight for the next moe_routed_dev call (model.cu):
+// x is then the raw residual stream. One-token decode folds the norm into the
+// router kernel; every other path normalizes into a scratch row first.
+const float *g_prenorm_w = nullptr;
+float g_prenorm_eps = 0.0f;
+
 int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const float *d_x, const float *d_logits,
                    const float *d_bias, float *d_out, const float *d_residual, uint32_t *d_ids_out, cudaStream_t st) {
     const size_t max_ffn = std::max<size_t>(L.ffn, L.has_shared ? L.shexp_ffn : 0);
     const size_t n_slots = T * L.n_used + (L.has_shared ? T : 0);
     if (int rc = ensure_moe_scratch(T, L.dim, max_ffn, L.n_expert, n_slots)) return rc;
     const size_t act_stride = align256(max_ffn);
+    const float *pre_w = g_prenorm_w;
+    g_prenorm_w = nullptr;
+    auto prenorm_scratch = [&]() -> int {  // the unfolded form: RMSNorm rows into scratch
+        if (int rc = S.prenormed.ensure(T * (size_t)L.dim * 4)) return rc;
+        const XQW none{nullptr, nullptr, nullptr};
+        for (size_t t = 0; t < T; t++)
+            launch_rmsnorm_q(const_cast<float *>(d_x) + t * L.dim, nullptr, pre_w, L.dim, g_prenorm_eps,
+                             S.prenormed.as<float>() + t * L.dim, none, none, false, st);
+        CK(cudaGetLastError());
+        d_x = S.prenormed.as<float>();
+        pre_w = nullptr;
+        return 0;
+    };
     if (g_force_generic != 1) {
         DecodeArgs A = decode_args(L, T, router, d_x, d_logits, d_bias, d_out, d_residual, d_ids_out, act_stride);
         const bool batch_ok = router && batch_supported(A);
         if (g_force_generic == 0 && (T <= DECODE_AUTO_T || (!batch_ok && T <= DECODE_MAX_T)) && decode_supported(A)) {
             g_last_path = 0;
+            if (pre_w && T == 1) {
+                A.prenorm_w = pre_w;
+                A.prenorm_eps = g_prenorm_eps;
+            } else if (pre_w) {
+                if (int rc = prenorm_scratch()) return rc;
+                A.x = d_x;
+            }
             CK(launch_decode(A, st));
             return 0;
+        }
+        if (pre_w) {
+            if (int rc = prenorm_scratch()) return rc;
+            A.x = d_x;
         }
         if (batch_ok) {
             const int path = batch_path(A, T * L.n_used, L.n_local);
@@ -566,6 +598,8 @@ int moe_routed_dev(const RoutedLayerDev &L, size_t T, const float *router, const
             return 0;
         }
     }
+    if (pre_w)
+        if (int rc = prenorm_scratch()) return rc;
     if (router) {
         launch_mm_f32(router, L.n_expert, L.dim, d_x, (int)T, S.logits.as<float>(), st);
         d_logits = S.logits.as<float>();
@@ -600,6 +634,12 @@ int rt_decline(const char *why) { return decline(why); }
 int rt_fail(const char *what, cudaError_t e) { return fail(what, e); }
 uint64_t rt_buf_gen() { return g_buf_gen; }
 cudaError_t rt_wait() { return seam_wait(); }  // completion of the backend's stream, polled
+// The next loom_cuda_moe_forward takes the raw residual row and applies the
+// layer's FFN RMSNorm (weight w, f32 [dim]) itself.
+void rt_moe_prenorm(const float *w, float eps) {
+    g_prenorm_w = w;
+    g_prenorm_eps = eps;
+}
 
 // A host weight range -> the cached device tensor that holds it (uploading it
 // as its own tensor when no cached tensor of that type contains it) and its
@@ -689,7 +729,7 @@ void loom_cuda_shutdown(void) {
     g_arenas.clear();
     for (DBuf *b : {&S.xq256_q, &S.xq256_d, &S.xq256_s, &S.xq32_q, &S.xq32_d, &S.xq32_s, &S.logits, &S.ids, &S.gates,
                     &S.slots, &S.act, &S.aq, &S.ad, &S.as, &S.counters, &S.grp, &S.ybuf, &S.io_in, &S.io_out, &S.io_aux, &S.raw, &S.a2a_i, &S.a2a_sx,
-                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1, &S.tmp, &S.amax, &S.head_logits}) {
+                    &S.a2a_yb, &S.a2a_ysh, &S.a2a_rx, &S.a2a_re, &S.a2a_yr, &S.a2a_g1, &S.tmp, &S.amax, &S.head_logits, &S.prenormed}) {
         if (b->p) cudaFree(b->p);
         b->p = nullptr;
         b->cap = 0;
@@ -1140,6 +1180,9 @@ int loom_cuda_reserve(size_t T, size_t dim, size_t ffn, size_t n_expert, size_t 
 
 int loom_cuda_moe_forward(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, const float *d_residual,
                           const float *d_logits, uint32_t *d_ids, void *stream) {
+    struct PrenormOnce {  // a pending FFN-norm fold applies to this call only, whatever it returns
+        ~PrenormOnce() { g_prenorm_w = nullptr; }
+    } prenorm_once;
     if (int rc = need_init()) return rc;
     if (!desc || T == 0) return decline("empty forward");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;

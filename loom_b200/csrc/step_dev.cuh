@@ -14,7 +14,7 @@ namespace {
 
 constexpr int AB_WARPS = 12, AB_THREADS = AB_WARPS * 32;  // 12 warps: up to 168 registers a thread
 constexpr int AB_GRP_WARPS = 4;                       // warps of an attention group
-constexpr int AB_NBAR = 5;                            // grid barriers per launch
+constexpr int AB_NBAR = 4;                            // grid barriers per launch (with the FFN norm)
 constexpr uint32_t AB_POLLS = 1u << 21;               // bounded grid-barrier wait (~1 s)
 
 __device__ __forceinline__ unsigned long long ab_ld_acquire(const unsigned long long *p) {
@@ -93,6 +93,17 @@ template <int TY> constexpr int ab_maxu() { return TY == T_Q4_K ? 8 : TY == T_Q6
 __device__ void ab_rmsnorm(const float *x, const float *w, int dim, float eps, bool serial, float *sx, float *red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float ss = 0.0f;
+    // the weights are requested with the row (one round trip for both), kept in registers
+    constexpr int WE = 24;
+    float wr[WE];
+    const bool wreg = dim <= WE * AB_THREADS;
+    if (wreg) {
+#pragma unroll
+        for (int k = 0; k < WE; k++) {
+            const int i = tid + k * AB_THREADS;
+            wr[k] = i < dim ? __ldg(w + i) : 0.0f;
+        }
+    }
     for (int i = tid; i < dim; i += AB_THREADS) {
         const float v = x[i];
         sx[i] = v;
@@ -117,7 +128,97 @@ __device__ void ab_rmsnorm(const float *x, const float *w, int dim, float eps, b
     }
     __syncthreads();
     const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(red[0], (float)dim), eps)));
-    for (int i = tid; i < dim; i += AB_THREADS) sx[i] = fmul(fmul(sx[i], scale), w[i]);
+    if (wreg) {
+#pragma unroll
+        for (int k = 0; k < WE; k++) {
+            const int i = tid + k * AB_THREADS;
+            if (i < dim) sx[i] = fmul(fmul(sx[i], scale), wr[k]);
+        }
+    } else {
+        for (int i = tid; i < dim; i += AB_THREADS) sx[i] = fmul(fmul(sx[i], scale), w[i]);
+    }
+    __syncthreads();
+}
+
+// One head row in shared memory by one warp: optional headNorm with weight
+// gamma (shared; llama.zig:938-950: inv = 1 / sqrt(ss / hd + eps), ss serial
+// in the reference's order when `serial`, else a lane-strided tree), optional
+// RoPE on the (cos, sin) pairs cs (shared; llama.zig:830-858; NEOX pairs j,
+// j + half, else 2j, 2j + 1), and a copy to `cache` (global) when given.
+__device__ __noinline__ void ab_head_smem(float *v, const float *gamma, bool rope, const float *cs, int half, int neox,
+                                          int hd, float eps, int serial, float *cache, int lane) {
+    if (gamma) {
+        float ss = 0.0f;
+        if (serial) {
+            if (lane == 0)
+                for (int i = 0; i < hd; i++) ss = fadd(ss, fmul(v[i], v[i]));
+            ss = __shfl_sync(0xffffffffu, ss, 0);
+        } else {
+            for (int i = lane; i < hd; i += 32) ss = fadd(ss, fmul(v[i], v[i]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss = fadd(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        }
+        const float inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)hd), eps)));
+        __syncwarp();
+        for (int i = lane; i < hd; i += 32) v[i] = fmul(fmul(v[i], inv), gamma[i]);
+        __syncwarp();
+    }
+    if (rope) {
+        for (int j = lane; j < half; j += 32) {
+            const int ia = neox ? j : 2 * j, ib = neox ? j + half : 2 * j + 1;
+            const float a = v[ia], b = v[ib], co = cs[2 * j], si = cs[2 * j + 1];
+            v[ia] = fsub(fmul(a, co), fmul(b, si));
+            v[ib] = fadd(fmul(a, si), fmul(b, co));
+        }
+        __syncwarp();
+    }
+    if (cache)
+        for (int i = lane; i < hd; i += 32) cache[i] = v[i];
+}
+
+// RMSNorm of the row already in sx (dim floats, shared), in place: the sum of
+// squares serial (thread 0, the reference's order) or a tree (per thread, then
+// warps in order); out = x * scale * w. Ends with a __syncthreads.
+__device__ void ab_rmsnorm_sx(const float *w, int dim, float eps, bool serial, float *sx, float *red) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int WE = 24;
+    float wr[WE];
+    const bool wreg = dim <= WE * AB_THREADS;
+    if (wreg) {
+#pragma unroll
+        for (int k = 0; k < WE; k++) {
+            const int i = tid + k * AB_THREADS;
+            wr[k] = i < dim ? __ldg(w + i) : 0.0f;
+        }
+    }
+    float ss = 0.0f;
+    if (serial) {
+        if (tid == 0) {
+            for (int i = 0; i < dim; i++) ss = fadd(ss, fmul(sx[i], sx[i]));
+            red[0] = ss;
+        }
+    } else {
+        for (int i = tid; i < dim; i += AB_THREADS) ss = fadd(ss, fmul(sx[i], sx[i]));
+        ss = ab_warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.0f;
+            for (int i = 0; i < AB_WARPS; i++) t = fadd(t, red[i]);
+            red[0] = t;
+        }
+    }
+    __syncthreads();
+    const float scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(red[0], (float)dim), eps)));
+    if (wreg) {
+#pragma unroll
+        for (int k = 0; k < WE; k++) {
+            const int i = tid + k * AB_THREADS;
+            if (i < dim) sx[i] = fmul(fmul(sx[i], scale), wr[k]);
+        }
+    } else {
+        for (int i = tid; i < dim; i += AB_THREADS) sx[i] = fmul(fmul(sx[i], scale), w[i]);
+    }
     __syncthreads();
 }
 
@@ -136,6 +237,39 @@ __device__ void ab_quant(const float *sx, int n, bool k256, int8_t *q, float *d,
             const bool live = b < nb;
             const int off = b * 32 + (lane & 3) * 8;
             quant_lane8(sx + (live ? off : 0), live, 4, q + off, d + b, nullptr, s + b, lane);
+        }
+    }
+}
+
+// Floats of one attention group's shared memory: K rows (padded stride hd + 4)
+// and V rows of a chunk, the group's query heads, their scores, and the
+// head-norm weights and (cos, sin) pairs of the head preparation.
+__host__ __device__ constexpr size_t ab_att_per(int hd, int gq) {
+    return (size_t)ATT_CH * (hd + 4) + (size_t)ATT_CH * hd + (size_t)gq * hd + (size_t)gq * ATT_CH + 3 * (size_t)hd;
+}
+
+// Padded activation layout (shared memory): a 256-value block's quants 272
+// bytes apart and its 16 sums 20 words apart (80 bytes: bulk-copy rows); a 32-value block's quants 48
+// bytes apart, one sum word each. ab_quant_pad writes it; ab_rows reads it
+// with these strides.
+__host__ __device__ constexpr int ab_pad_qs(bool k256) { return k256 ? 272 : 48; }
+__host__ __device__ constexpr int ab_pad_ss(bool k256) { return k256 ? 20 : 1; }
+__host__ __device__ constexpr size_t ab_pad_qbytes(size_t n) { return n / 32 * 48; }           // >= n / 256 * 272
+__host__ __device__ constexpr size_t ab_pad_sbytes(size_t n) { return (n / 256 + 1) * 20 * 4 + n / 32 * 4; }
+__device__ void ab_quant_pad(const float *sx, int n, bool k256, int8_t *q, float *d, int32_t *s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (k256) {
+        for (int b = warp; b < n / 256; b += AB_WARPS)
+            quant_lane8(sx + b * 256 + lane * 8, true, 32, q + b * 272 + lane * 8, d + b, s + b * 20 + lane / 2,
+                        nullptr, lane);
+    } else {
+        const int nb = n / 32, ng = (nb + 7) / 8;
+        for (int g = warp; g < ng; g += AB_WARPS) {
+            const int b = g * 8 + lane / 4;
+            const bool live = b < nb;
+            const int off = (lane & 3) * 8;
+            quant_lane8(sx + (live ? b * 32 + off : 0), live, 4, q + (live ? b : 0) * 48 + off, d + b, nullptr, s + b,
+                        lane);
         }
     }
 }
@@ -178,36 +312,38 @@ template <> __device__ __forceinline__ QT<T_Q4_0>::Frag ab_frag<T_Q4_0>(const Ab
 }
 
 // rows [r0, r0 + nS) of a staged slice (r0 local) against activations xv,
-// kept compact (no unrolling: this code runs once per launch, so instruction
-// fetch, not issue, sets its speed): per round each lane group forms one
-// unit's integer dot (QT<TY>::part, the warp engine's arithmetic) and its
-// float term into the warp's term buffer tsm (>= nS * nb floats); then lane s
-// adds stream s's block terms in block order from +0 (kBlockDot / matvecK256,
-// ggml.zig:1002-1042). Bit-identical to wd_load + wd_finish. acc[s] for
-// s < nS is valid in lane s.
+// one lane per unit (row, block): the lane walks the block's LPB fragments
+// (QT<TY>::part, the warp engine's arithmetic; the integer sums I and M are
+// the same integers the lane groups' shuffle trees form) and writes the
+// block's float term into the warp's term buffer tsm (>= nS * nb floats);
+// then lane s adds stream s's block terms in block order from +0 (kBlockDot /
+// matvecK256, ggml.zig:1002-1042). Bit-identical to wd_load + wd_finish.
+// One lane per unit needs no cross-lane reduction per block, so a warp
+// issues about a quarter of the instructions of lane groups, with the
+// fragments' shared-memory loads independent of each other.
+// acc[s] for s < nS is valid in lane s.
+// Activation blocks sit qs bytes (quants) and ss words (per-16 sums) apart:
+// the packed layout (qs = BE, ss = SPB) or the padded shared-memory layout of
+// ab_quant_pad, in which the lanes of one 8-lane phase, reading the same
+// offset of eight consecutive blocks, hit eight different bank groups.
 template <int TY>
-__device__ __noinline__ float ab_rows(const AbStage &st, int r0, int nS, const XV &xv, float *tsm, int lane) {
+__device__ __noinline__ float ab_rows(const AbStage &st, int r0, int nS, const XV &xv, float *tsm, int lane,
+                                      int qs = QT<TY>::BE, int ss = QT<TY>::SPB) {
     using Q = QT<TY>;
-    constexpr int GG = 32 / Q::LPB;
-    const int NB = st.nb, U = nS * NB, grp = lane / Q::LPB, sub = lane % Q::LPB;
-#pragma unroll 4
-    for (int u0 = 0; u0 < U; u0 += GG) {
-        const int u = u0 + grp;
+    const int NB = st.nb, U = nS * NB;
+    for (int u = lane; u < U; u += 32) {
+        const int s2 = u / NB, b = u - s2 * NB, gb = (r0 + s2) * NB + b;
         int I = 0, M = 0;
-        float xdv = 0.0f;
         typename Q::Frag f{};
-        if (u < U) {
-            const int s2 = u / NB, b = u - s2 * NB;
-            f = ab_frag<TY>(st, (r0 + s2) * NB + b, sub);
-            Q::part(f, sub, xv.q + b * Q::BE, xv.s + b * Q::SPB, I, M);
-            xdv = xv.d[b];
+#pragma unroll 2
+        for (int sub = 0; sub < Q::LPB; sub++) {
+            f = ab_frag<TY>(st, gb, sub);
+            int i = 0, m = 0;
+            Q::part(f, sub, xv.q + b * qs, xv.s + b * ss, i, m);
+            I += i;
+            M += m;
         }
-#pragma unroll
-        for (int o = 1; o < Q::LPB; o <<= 1) {
-            I += __shfl_xor_sync(0xffffffffu, I, o);
-            M += __shfl_xor_sync(0xffffffffu, M, o);
-        }
-        if (u < U && sub == 0) tsm[u] = Q::term(f, I, M, xdv);
+        tsm[u] = Q::term(f, I, M, xv.d[b]);
     }
     __syncwarp();
     float a = 0.0f;
