@@ -106,10 +106,11 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         carve(so, A.wo, oa, ob, nbO);
     }
     if (tid == 0) {  // every weight byte of the layer this CTA needs, in flight at once
-        mbar_init(&mb[0], 1);
-        mbar_init(&mb[1], 1);
-        for (int i = 0; i < AB_WARPS / AB_GRP_WARPS; i++) mbar_init(&mbh[i], 1);
-        for (int i = 0; i < 3; i++) mbar_init(&mbm[i], 1);
+        mbar_init_nf(&mb[0], 1);
+        mbar_init_nf(&mb[1], 1);
+        for (int i = 0; i < AB_WARPS / AB_GRP_WARPS; i++) mbar_init_nf(&mbh[i], 1);
+        for (int i = 0; i < 3; i++) mbar_init_nf(&mbm[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         // the residual row first: the norm waits for it
         asm volatile("fence.proxy.async.global;" ::: "memory");
         mbar_expect_tx(&mbm[2], (uint32_t)dim * 4);
@@ -127,6 +128,11 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     mark(8);
     __syncthreads();  // publishes the mbarrier init
     if (!mbar_wait(&mbm[2], 0, STAGE_POLLS_AB) && lane == 0) atomicOr(err, 2u);
+    // this CTA's output rows of the residual, kept for the output projection's add
+    constexpr int XRES = 64;
+    __shared__ float xres[XRES];
+    const bool xres_ok = ob - oa <= XRES;
+    if (xres_ok && tid < ob - oa) xres[tid] = sx[oa + tid];
     ab_rmsnorm_sx(A.attn_norm, dim, A.eps, A.serial, sx, red);
     mark(9);
     // the f16 scale regions (published by the barriers before the dots and before P5)
@@ -237,13 +243,67 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
                 }
                 asm volatile("cp.async.commit_group;\n" ::: "memory");
                 if (grp == 0) mark(12);
-                for (int hh = gwarp; hh < nhp; hh += AB_GRP_WARPS) {
-                    const bool isq = hh < GQ, isk = hh == GQ;
-                    float *v = isq ? qs + hh * hd : isk ? sK + (n - 1) * KS : sV + (n - 1) * hd;
-                    const bool norm = isq ? A.q_norm != nullptr : isk && A.k_norm != nullptr;
-                    float *cache = isq ? nullptr : (isk ? A.kc : A.vc) + (size_t)pos * kvd + (size_t)g * hd;
-                    ab_head_smem(v, norm ? (isq ? gqs : gks) : nullptr, hh <= GQ, css, A.rope_dim / 2, A.neox, hd, A.eps,
-                                 A.serial, cache, lane);
+                if (A.serial) {
+                    for (int hh = gwarp; hh < nhp; hh += AB_GRP_WARPS) {
+                        const bool isq = hh < GQ, isk = hh == GQ;
+                        float *v = isq ? qs + hh * hd : isk ? sK + (n - 1) * KS : sV + (n - 1) * hd;
+                        const bool norm = isq ? A.q_norm != nullptr : isk && A.k_norm != nullptr;
+                        float *cache = isq ? nullptr : (isk ? A.kc : A.vc) + (size_t)pos * kvd + (size_t)g * hd;
+                        ab_head_smem(v, norm ? (isq ? gqs : gks) : nullptr, hh <= GQ, css, A.rope_dim / 2, A.neox, hd,
+                                     A.eps, A.serial, cache, lane);
+                    }
+                } else {  // this warp's heads side by side (independent chains interleaved)
+                    constexpr int HW = (16 + 2 + AB_GRP_WARPS - 1) / AB_GRP_WARPS;
+                    float *vr[HW];
+                    float ss[HW];
+#pragma unroll
+                    for (int t = 0; t < HW; t++) {
+                        const int hh = gwarp + AB_GRP_WARPS * t;
+                        vr[t] = hh < GQ ? qs + hh * hd : hh == GQ ? sK + (n - 1) * KS : sV + (n - 1) * hd;
+                        const bool norm = hh < nhp && (hh < GQ ? A.q_norm != nullptr : hh == GQ && A.k_norm != nullptr);
+                        ss[t] = 0.0f;
+                        if (norm)
+                            for (int i = lane; i < hd; i += 32) ss[t] = fadd(ss[t], fmul(vr[t][i], vr[t][i]));
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                        for (int t = 0; t < HW; t++) ss[t] = fadd(ss[t], __shfl_xor_sync(0xffffffffu, ss[t], o));
+                    __syncwarp();
+                    const int half = A.rope_dim / 2;
+#pragma unroll
+                    for (int t = 0; t < HW; t++) {
+                        const int hh = gwarp + AB_GRP_WARPS * t;
+                        if (hh >= nhp) continue;
+                        const bool norm = hh < GQ ? A.q_norm != nullptr : hh == GQ && A.k_norm != nullptr;
+                        float *v = vr[t];
+                        if (norm) {
+                            const float inv = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss[t], (float)hd), A.eps)));
+                            const float *gm = hh < GQ ? gqs : gks;
+                            for (int i = lane; i < hd; i += 32) v[i] = fmul(fmul(v[i], inv), gm[i]);
+                        }
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int t = 0; t < HW; t++) {
+                        const int hh = gwarp + AB_GRP_WARPS * t;
+                        if (hh >= nhp || hh > GQ) continue;  // RoPE on queries and the key
+                        float *v = vr[t];
+                        for (int j = lane; j < half; j += 32) {
+                            const int ia = A.neox ? j : 2 * j, ib = A.neox ? j + half : 2 * j + 1;
+                            const float a = v[ia], b = v[ib], co = css[2 * j], si = css[2 * j + 1];
+                            v[ia] = fsub(fmul(a, co), fmul(b, si));
+                            v[ib] = fadd(fmul(a, si), fmul(b, co));
+                        }
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int t = 0; t < HW; t++) {
+                        const int hh = gwarp + AB_GRP_WARPS * t;
+                        if (hh < GQ || hh >= nhp) continue;  // the new key and value rows -> the cache
+                        float *cache = (hh == GQ ? A.kc : A.vc) + (size_t)pos * kvd + (size_t)g * hd;
+                        for (int i = lane; i < hd; i += 32) cache[i] = vr[t][i];
+                    }
                 }
                 if (grp == 0) mark(13);
                 asm volatile("cp.async.wait_all;\n" ::: "memory");
@@ -432,7 +492,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         for (int ch = warp; ch < nco && staged; ch += AB_WARPS) {
             const int r0 = ch * SO, nS = min(SO, ob - oa - r0);
             const float a = ab_rows<TO>(so, r0, nS, av, tsm, lane, ab_pad_qs(k256O), ab_pad_ss(k256O));
-            if (lane < nS) A.x[oa + r0 + lane] = fadd(A.x[oa + r0 + lane], a);  // llama.zig:1195 add
+            if (lane < nS)  // llama.zig:1195 add
+                A.x[oa + r0 + lane] = fadd(xres_ok ? xres[r0 + lane] : A.x[oa + r0 + lane], a);
         }
     }
     if (!A.normed) goto out;  // the MoE layer's router kernel applies the FFN norm itself
