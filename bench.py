@@ -618,7 +618,10 @@ def model_bytes(spec, pos: int, n_local: int = None) -> int:
             b += t.nbytes // t.planes * spec.n_used * n_local / spec.n_expert
         else:
             b += t.nbytes
-    b += spec.n_layers * (pos + 2) * kvd * 4 * 2
+    if getattr(spec, "mla", False):  # compressed row + rope row per position
+        b += spec.n_layers * (pos + 2) * (spec.kv_lora + spec.rope_dim) * 4
+    else:
+        b += spec.n_layers * (pos + 2) * kvd * 4 * 2
     return int(b)
 
 
@@ -749,6 +752,12 @@ def run_model(args):
     peak, peak_kind = peaks()
     dev.free()
 
+    ds = None
+    if world == 1 and not args.no_deepseek:
+        try:
+            ds = run_model_deepseek(args, peak, peak_kind)
+        except Exception as e:  # reported in the line, never fatal to the headline
+            ds = {"error": f"{type(e).__name__}: {e}"[:300]}
     moe = None
     if world == 1 and not args.no_moe_stack:
         margs = argparse.Namespace(**vars(args))
@@ -788,9 +797,75 @@ def run_model(args):
         line["moe_stack"] = {k: moe[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "config",
                                                  "e2e", "e2e_device", "prefill", "batch", "gpu_launches")
                              if k in moe}
+    if ds:
+        line["deepseek_v2_lite"] = ds
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def run_model_deepseek(args, peak, peak_kind):
+    """The DeepSeek-V2-Lite-shaped model (MLA attention,
+    layer 0 dense, 64 routed experts top-6 + 2 shared): one decode token at
+    position ctx - 1 after filling the cache by decoding, graph-replayed and
+    event-timed like the headline; e2e through loom_cuda_model_decode."""
+    import torch
+    from loom_b200.model import DeviceModel, deepseek_v2_lite
+    spec = deepseek_v2_lite(ctx_len=args.ctx)
+    dev = DeviceModel(spec)
+    try:
+        pos = spec.ctx_len - 1
+        tok = 1
+        t0 = time.perf_counter()
+        for p in range(pos):
+            tok, _ = dev.decode(tok, p)
+        fill_s = time.perf_counter() - t0
+        stream = torch.cuda.Stream()
+        d_tok = torch.tensor([tok], dtype=torch.int32, device="cuda")
+        d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        d_next = torch.zeros(1, dtype=torch.int32, device="cuda")
+        d_logits = torch.empty(spec.vocab, dtype=torch.float32, device="cuda")
+        with torch.cuda.stream(stream):
+            dev.step(d_tok, d_pos, d_logits, d_next, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            dev.step(d_tok, d_pos, d_logits, d_next, stream=torch.cuda.current_stream().cuda_stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        for _ in range(args.warmup):
+            dev.decode(tok, pos)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            dev.decode(tok, pos)
+        e2e_ms = (time.perf_counter() - t0) / args.steps * 1e3
+        err = dev.error()
+    finally:
+        dev.free()
+    bytes_step = model_bytes(spec, pos)
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    return {"metric": "decode tok/s (DeepSeek-V2-Lite-shaped full model, Q4_K/Q8_0, batch 1)",
+            "value": round(1e3 / ms, 2), "unit": "tok/s", "ms_per_step": round(ms, 4),
+            "config": {"workload": f"deepseek-v2-lite full-model decode, batch 1, position {pos} of a "
+                                   f"{spec.ctx_len}-token context", "model": spec.name, "layers": spec.n_layers,
+                       "dim": spec.dim, "n_heads": spec.n_heads, "kv_lora": spec.kv_lora, "n_expert": spec.n_expert,
+                       "n_used": spec.n_used, "shared_ffn": spec.shexp_ffn, "vocab": spec.vocab,
+                       "engine": "loom_cuda_model_step (MLA kernels + fused MoE) in a CUDA graph",
+                       "kv_fill_s": round(fill_s, 2)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "bytes_per_step": bytes_step},
+            "e2e": {"value": round(1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4, "path": "loom_cuda_model_decode, wall clock"},
+            "device_error": err}
 
 
 def run_reference_model(args):
@@ -845,6 +920,8 @@ def main():
                     help="model: full Qwen3-30B-A3B decode (the headline); moe: the 48 MoE layers only")
     ap.add_argument("--ctx", type=int, default=2048, help="context length of the model workload")
     ap.add_argument("--no-moe-stack", action="store_true", help="model workload: skip the MoE-only sub-measurement")
+    ap.add_argument("--no-deepseek", action="store_true",
+                    help="model workload: skip the DeepSeek-V2-Lite full-model sub-measurement")
     args = ap.parse_args()
     globals()["LAYERS"] = args.layers
     if args.workload == "model":
