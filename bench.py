@@ -700,7 +700,7 @@ def run_model(args):
     # fill the KV cache: greedy decode of positions 0 .. ctx-2 (every rank the same tokens)
     tok = 1
     t0 = time.perf_counter()
-    for p in range(pos):
+    for p in range(0 if args.no_fill else pos):
         tok, _ = dev.decode(tok, p)
     fill_s = time.perf_counter() - t0
 
@@ -920,6 +920,9 @@ def main():
                     help="model: full Qwen3-30B-A3B decode (the headline); moe: the 48 MoE layers only")
     ap.add_argument("--ctx", type=int, default=2048, help="context length of the model workload")
     ap.add_argument("--no-moe-stack", action="store_true", help="model workload: skip the MoE-only sub-measurement")
+    ap.add_argument("--no-fill", action="store_true",
+                    help="model workload: leave the KV cache unfilled (profiling captures only; the kernels and "
+                         "bytes are the same, the cached values are zeros)")
     ap.add_argument("--no-deepseek", action="store_true",
                     help="model workload: skip the DeepSeek-V2-Lite full-model sub-measurement")
     args = ap.parse_args()

@@ -10,6 +10,7 @@
 #include "attn.cuh"
 #include "devutil.cuh"
 #include "pdl.cuh"
+#include "tma.cuh"
 
 namespace loom {
 
@@ -481,6 +482,131 @@ __global__ void __launch_bounds__(AT_THREADS) k_mla_attn(const float *qa, const 
     }
 }
 
+// Split-position MLA attention (the fast form; contexts past the ordered
+// limit): CTA (s, hg) takes positions [s*MLA_CH, +MLA_CH) for heads
+// [16 hg, +16). The chunk's compressed and rope rows and the heads' absorbed
+// queries come in by bulk copies; scores (warp per (head, position), lanes over
+// the 576 columns), the chunk's softmax max / sum per head, then the
+// chunk-weighted rows per head into a head-major record [head][split][REC]:
+// kvr outputs, running max, sum. k_mla_merge rescales and sums the records.
+constexpr int MLA_CH = 16, MLA_HG = 16, MLA_THREADS = 512;
+constexpr uint32_t MLA_POLLS = 1u << 22;
+
+__global__ void __launch_bounds__(MLA_THREADS) k_mla_part(const float *qa, const float *q, int kvr, int rope, int kd,
+                                                         int nope, int n_heads, float scale, const uint32_t *pos_p,
+                                                         int ctx, const float *c_cache, const float *r_cache,
+                                                         float *part, int nsplit, int *err) {
+    extern __shared__ __align__(16) float ms[];
+    __shared__ __align__(8) uint64_t bar;
+    pdl_wait_();
+    pdl_trigger_();
+    const int pos = (int)*pos_p;
+    const int s = blockIdx.x, h0 = blockIdx.y * MLA_HG;
+    const int t0 = s * MLA_CH;
+    if (pos >= ctx || t0 > pos) return;
+    const int n = min(MLA_CH, pos + 1 - t0), nh = min(MLA_HG, n_heads - h0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int REC = kvr + 4;
+    float *sc_c = ms;                               // [MLA_CH][kvr]
+    float *sc_r = sc_c + MLA_CH * kvr;              // [MLA_CH][rope]
+    float *sq = sc_r + MLA_CH * rope;               // [MLA_HG][kvr]
+    float *sqr = sq + MLA_HG * kvr;                 // [MLA_HG][rope]
+    float *sp = sqr + MLA_HG * rope;                // [MLA_HG][MLA_CH] scores, then weights
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        const uint32_t bytes = (uint32_t)(n * kvr + n * rope + nh * kvr) * 4;
+        mbar_expect_tx(&bar, bytes);
+        bulk_g2s(sc_c, c_cache + (size_t)t0 * kvr, (uint32_t)(n * kvr * 4), &bar);
+        bulk_g2s(sc_r, r_cache + (size_t)t0 * rope, (uint32_t)(n * rope * 4), &bar);
+        bulk_g2s(sq, qa + (size_t)h0 * kvr, (uint32_t)(nh * kvr * 4), &bar);
+    }
+    for (int i = tid; i < nh * rope; i += MLA_THREADS) {  // the heads' rope parts (strided rows)
+        const int hh = i / rope, j = i - hh * rope;
+        sqr[i] = __ldg(q + (size_t)(h0 + hh) * kd + nope + j);
+    }
+    __syncthreads();
+    if (!mbar_wait(&bar, 0, MLA_POLLS)) {
+        if (tid == 0 && err) atomicOr(err, 4);
+        return;
+    }
+    // scores: warp per (head, position)
+    for (int pr = warp; pr < nh * n; pr += MLA_THREADS / 32) {
+        const int hh = pr / n, t = pr - hh * n;
+        const float *qh = sq + hh * kvr, *ct = sc_c + t * kvr, *qr = sqr + hh * rope, *rt = sc_r + t * rope;
+        float a = 0.0f;
+        for (int j = lane; j < kvr; j += 32) a = fmaf(qh[j], ct[j], a);
+        for (int j = lane; j < rope; j += 32) a = fmaf(qr[j], rt[j], a);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) sp[hh * MLA_CH + t] = a * scale;
+    }
+    __syncthreads();
+    if (warp < nh) {  // chunk max and sum per head
+        const float v = lane < n ? sp[warp * MLA_CH + lane] : -INFINITY;
+        const float m = warp_max(v);
+        const float e = lane < n ? exp_f(v - m) : 0.0f;
+        if (lane < n) sp[warp * MLA_CH + lane] = e;
+        float l = e;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            float *rec = part + ((size_t)(h0 + warp) * nsplit + s) * REC;
+            rec[kvr] = m;
+            rec[kvr + 1] = l;
+        }
+    }
+    __syncthreads();
+    for (int j = tid; j < kvr; j += MLA_THREADS) {  // weighted rows: column j for every head
+        float cv[MLA_CH];
+#pragma unroll
+        for (int t = 0; t < MLA_CH; t++) cv[t] = t < n ? sc_c[t * kvr + j] : 0.0f;
+        for (int hh = 0; hh < nh; hh++) {
+            float o = 0.0f;
+#pragma unroll
+            for (int t = 0; t < MLA_CH; t++) o = fmaf(sp[hh * MLA_CH + t], cv[t], o);
+            part[((size_t)(h0 + hh) * nsplit + s) * REC + j] = o;
+        }
+    }
+}
+
+// c_acc[h][j] = sum_s rec_s[j] * exp(m_s - M) / sum_s l_s * exp(m_s - M), one
+// CTA per head (columns across threads: each split's record row is read once
+// and coalesced).
+__global__ void __launch_bounds__(MLA_THREADS) k_mla_merge(int kvr, const uint32_t *pos_p, int ctx, const float *part,
+                                                          int nsplit, float *c_acc) {
+    extern __shared__ float wts[];  // [live] weights
+    __shared__ float inv_l;
+    pdl_wait_();
+    pdl_trigger_();
+    const int pos = (int)*pos_p;
+    if (pos >= ctx) return;
+    const int h = blockIdx.x, tid = threadIdx.x, REC = kvr + 4;
+    const int live = (pos + 1 + MLA_CH - 1) / MLA_CH;
+    const float *rec = part + (size_t)h * nsplit * REC;
+    if (tid < 32) {
+        float M = -INFINITY;
+        for (int s2 = tid; s2 < live; s2 += 32) M = fmaxf(M, __ldcg(rec + (size_t)s2 * REC + kvr));
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int s2 = tid; s2 < live; s2 += 32) {
+            const float w = exp_f(__ldcg(rec + (size_t)s2 * REC + kvr) - M);
+            wts[s2] = w;
+            L = fmaf(__ldcg(rec + (size_t)s2 * REC + kvr + 1), w, L);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (tid == 0) inv_l = 1.0f / L;
+    }
+    __syncthreads();
+    for (int j = tid; j < kvr; j += MLA_THREADS) {
+        float o = 0.0f;
+#pragma unroll 16
+        for (int s2 = 0; s2 < live; s2++) o = fmaf(__ldcg(rec + (size_t)s2 * REC + j), wts[s2], o);
+        c_acc[(size_t)h * kvr + j] = o * inv_l;
+    }
+}
+
 unsigned cdiv_u(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 
 }  // namespace
@@ -515,6 +641,31 @@ void launch_mla_attn(const float *qa, const float *q, int kvr, int rope, int kd,
     }
     launch_pdl_(k_mla_attn, dim3(n_heads), dim3(AT_THREADS), (size_t)ctx * 4, st, qa, q, kvr, rope, kd, nope, scale,
                 pos, ctx, c_cache, r_cache, c_acc);
+}
+
+size_t mla_part_floats(int n_heads, int kvr, int ctx) {
+    return (size_t)n_heads * ((ctx + MLA_CH - 1) / MLA_CH) * (kvr + 4);
+}
+
+bool mla_split_supported(int kvr, int rope) {
+    const size_t smem = ((size_t)MLA_CH * (kvr + rope) + (size_t)MLA_HG * (kvr + rope) + MLA_HG * MLA_CH) * 4;
+    return kvr % 4 == 0 && rope % 4 == 0 && kvr <= 1024 && smem <= 200 * 1024;
+}
+
+void launch_mla_split(const float *qa, const float *q, int kvr, int rope, int kd, int nope, int n_heads, float scale,
+                      const uint32_t *pos, int ctx, const float *c_cache, const float *r_cache, float *part,
+                      float *c_acc, int *err, cudaStream_t st) {
+    const int nsplit = (ctx + MLA_CH - 1) / MLA_CH;
+    const size_t smem = ((size_t)MLA_CH * (kvr + rope) + (size_t)MLA_HG * (kvr + rope) + MLA_HG * MLA_CH) * 4;
+    static size_t set = 0;
+    if (smem > set) {
+        cudaFuncSetAttribute(k_mla_part, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_mla_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, nsplit * 4 > 48 * 1024 ? nsplit * 4 : 48 * 1024);
+        set = smem;
+    }
+    launch_pdl_(k_mla_part, dim3(nsplit, cdiv_u(n_heads, MLA_HG)), dim3(MLA_THREADS), smem, st, qa, q, kvr, rope, kd,
+                nope, n_heads, scale, pos, ctx, c_cache, r_cache, part, nsplit, err);
+    launch_pdl_(k_mla_merge, dim3(n_heads), dim3(MLA_THREADS), (size_t)nsplit * 4, st, kvr, pos, ctx, part, nsplit, c_acc);
 }
 
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx) {

@@ -42,6 +42,14 @@ constexpr int ATT_CH = 32;
 constexpr int ATT_ORDERED_MAX = 512;      // default: ordered up to this context
 constexpr int ATT_ORDERED_LIMIT = 32768;  // largest context of the ordered form
 size_t attn_part_floats(int n_heads, int n_kv, int hd, int ctx);
+// Split-position MLA attention (contexts past the ordered limit, not exact_order):
+// records [n_heads][ctx / 16][kvr + 4] in `part` (mla_part_floats), then c_acc.
+// err (optional) gets bit 4 when a chunk's bulk copies time out.
+size_t mla_part_floats(int n_heads, int kvr, int ctx);
+bool mla_split_supported(int kvr, int rope);
+void launch_mla_split(const float *qa, const float *q, int kvr, int rope, int kd, int nope, int n_heads, float scale,
+                      const uint32_t *pos, int ctx, const float *c_cache, const float *r_cache, float *part,
+                      float *c_acc, int *err, cudaStream_t st);
 bool attn_merge_quantizes(int n_heads, int hd, int ctx);
 void launch_attention(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, float scale,
                       const uint32_t *pos, int ctx, float *part, float *out, bool ordered, XQW q256, XQW q32,

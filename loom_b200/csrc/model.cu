@@ -79,6 +79,7 @@ struct Model {
     bool mla = false;  // DeepSeek multi-head latent attention
     size_t kvr = 0, qlora = 0, nope = 0, vd = 0, kd = 0;
     float *qa_lat = nullptr, *qa_n = nullptr, *kva = nullptr, *qabs = nullptr, *cacc = nullptr;
+    float *mla_part = nullptr;  // split-position MLA attention records
     XQW l256{}, l32{}, c256{}, c32{};  // q_a output quantized for q_b; per-head compressed results for W_v
     Mat embd, out;
     const float *out_norm = nullptr;
@@ -218,8 +219,12 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
             launch_mla_front(m.kva, l.kv_a_norm, kvr, rope, m.eps, m.q, nh, (int)m.kd, (int)m.nope, m.rope, pos,
                              (int)m.ctx, cc, rc, st);
             launch_mla_absorb(l.kv_b.w, kvr, (int)m.nope, (int)m.vd, (int)m.kd, nh, m.q, m.qabs, st);
-            launch_mla_attn(m.qabs, m.q, kvr, rope, (int)m.kd, (int)m.nope, nh, m.scale, pos, (int)m.ctx, cc, rc,
-                            m.cacc, st);
+            if (m.ordered_attn)
+                launch_mla_attn(m.qabs, m.q, kvr, rope, (int)m.kd, (int)m.nope, nh, m.scale, pos, (int)m.ctx, cc, rc,
+                                m.cacc, st);
+            else
+                launch_mla_split(m.qabs, m.q, kvr, rope, (int)m.kd, (int)m.nope, nh, m.scale, pos, (int)m.ctx, cc, rc,
+                                 m.mla_part, m.cacc, reinterpret_cast<int *>(m.ab_bar + 2), st);
             const bool ck = act256(l.kv_b.type);
             const XQW &cq = ck ? m.c256 : m.c32;
             launch_quant_act(m.cacc, nh, kvr, kvr, ck, cq.q, cq.d, cq.s, ck ? kvr / 256 : kvr / 32, ck ? kvr / 16 : kvr / 32,
@@ -376,7 +381,10 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         m->vd = d->v_head;
         m->kd = d->nope + d->rope_dim;
         m->scale = d->mla_scale;
-        m->ordered_attn = true;  // the compressed-space attention keeps the reference's order
+        // the reference's order up to the ordered limit (and with exact_order); past it the
+        // split-position form
+        m->ordered_attn = d->exact_order || d->ctx_len <= (size_t)ATT_ORDERED_MAX ||
+                          !mla_split_supported((int)d->kv_lora, (int)d->rope_dim);
     }
     const size_t dim = d->dim, qd = d->n_heads * d->head_dim, kvd = d->n_kv_heads * d->head_dim;
     const size_t hv = m->mla ? d->n_heads * d->v_head : qd;  // attention output width (the output projection's input)
@@ -476,6 +484,8 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         (rc = alloc_xq(*m, m->a32, std::max(qd, hv), false)))
         return bail(rc);
     if ((rc = dalloc(*m, m->ab_bar, 64, true))) return bail(rc);
+    if (m->mla && !m->ordered_attn && (rc = dalloc(*m, m->mla_part, mla_part_floats((int)m->nh, (int)m->kvr, (int)m->ctx))))
+        return bail(rc);
     // The FFN RMSNorm moves into the MoE layer's router kernel (one grid barrier
     // and one single-CTA phase less per layer) where the tree-order norm is used.
     m->fold_ffn_norm = !m->serial_norm && !getenv("LOOM_CUDA_NO_NORM_FOLD");

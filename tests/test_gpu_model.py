@@ -179,29 +179,33 @@ def _v3_small():
     return spec
 
 
-@pytest.mark.parametrize("which,exact,tol", [("v2_lite", True, TOL), ("v2_lite", False, 2e-2), ("v3", True, TOL)],
-                         ids=["v2_lite_exact", "v2_lite_fast", "v3_qlora_grouped_exact"])
-def test_mla_model_matches_oracle(be, orc, which, exact, tol):
+@pytest.mark.parametrize("which,exact,tol,ctx,steps", [
+    ("v2_lite", True, TOL, 96, 40), ("v2_lite", False, 2e-2, 96, 40), ("v3", True, TOL, 96, 40),
+    ("v2_lite", False, 2e-2, 640, 100), ("v3", False, 2e-2, 640, 100)],
+    ids=["v2_lite_exact", "v2_lite_fast", "v3_qlora_grouped_exact", "v2_lite_split", "v3_split"])
+def test_mla_model_matches_oracle(be, orc, which, exact, tol, ctx, steps):
     """MLA decode (deepseek.zig:851-1049) on the device against the oracle:
     DeepSeek-V2-Lite shape (no q_lora, dense first layer, 2 shared experts,
     Q8_0 down projections) and a reduced V3 shape (q_lora, sigmoid + bias,
     grouped top-k, one shared expert); logits every step, the compressed and
-    rope cache rows."""
+    rope cache rows. Contexts past 512 without exact_order take the
+    split-position attention (16-position chunks, merged records)."""
     from loom_b200.model import deepseek_v2_lite
-    spec = deepseek_v2_lite(n_layers=2, ctx_len=96, n_expert=8, vocab=2048) if which == "v2_lite" else _v3_small()
+    spec = deepseek_v2_lite(n_layers=2, ctx_len=ctx, n_expert=8, vocab=2048) if which == "v2_lite" else _v3_small()
+    spec.ctx_len = ctx
     ref = _ds_runner(spec, orc)
     dev = DeviceModel(spec, exact_order=exact)
     rng = np.random.default_rng(13)
     try:
-        for pos in range(40):
+        for pos in range(steps):
             tok = int(rng.integers(0, spec.vocab))
             want = ref.step(tok, pos)
             nxt, got = dev.decode(tok, pos, logits=True)
             assert np.all(np.isfinite(got))
             assert rel_l2(got, want) < tol, (pos, rel_l2(got, want))
-        c, r = dev.read_kv(1, 39)
-        cc = ref.cc.reshape(spec.n_layers, spec.ctx_len, spec.kv_lora)[1, 39]
-        rc = ref.rc.reshape(spec.n_layers, spec.ctx_len, spec.rope_dim)[1, 39]
+        c, r = dev.read_kv(1, steps - 1)
+        cc = ref.cc.reshape(spec.n_layers, spec.ctx_len, spec.kv_lora)[1, steps - 1]
+        rc = ref.rc.reshape(spec.n_layers, spec.ctx_len, spec.rope_dim)[1, steps - 1]
         assert rel_l2(c, cc) < tol and rel_l2(r, rc) < tol
     finally:
         dev.free()
