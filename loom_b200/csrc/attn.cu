@@ -406,6 +406,7 @@ __global__ void __launch_bounds__(256) k_mla_front(const float *kv_a, const floa
                                                   const float *rope_tab, const uint32_t *pos_p, int ctx,
                                                   float *c_cache, float *r_cache) {
     __shared__ float red;
+    extern __shared__ float kva_s[];  // [kvr] the compressed row, loaded by every thread at once
     pdl_wait_();
     pdl_trigger_();
     const int pos = (int)*pos_p;
@@ -413,14 +414,16 @@ __global__ void __launch_bounds__(256) k_mla_front(const float *kv_a, const floa
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float *cs = rope_tab + (size_t)pos * rope;
     if (blockIdx.x == 0) {
-        if (tid == 0) {
+        for (int i = tid; i < kvr; i += blockDim.x) kva_s[i] = kv_a[i];
+        __syncthreads();
+        if (tid == 0) {  // serial sum of squares (the reference's order), from shared memory
             float ss = 0.0f;
-            for (int i = 0; i < kvr; i++) ss = fadd(ss, fmul(kv_a[i], kv_a[i]));
+            for (int i = 0; i < kvr; i++) ss = fadd(ss, fmul(kva_s[i], kva_s[i]));
             red = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)kvr), eps)));
         }
         __syncthreads();
         float *c = c_cache + (size_t)pos * kvr;
-        for (int i = tid; i < kvr; i += blockDim.x) c[i] = fmul(fmul(kv_a[i], red), kv_norm[i]);
+        for (int i = tid; i < kvr; i += blockDim.x) c[i] = fmul(fmul(kva_s[i], red), kv_norm[i]);
         float *r = r_cache + (size_t)pos * rope;
         for (int j = tid; 2 * j + 1 < rope; j += blockDim.x) {  // ropeNormPlain: adjacent pairs
             const float a = kv_a[kvr + 2 * j], b = kv_a[kvr + 2 * j + 1], co = cs[2 * j], si = cs[2 * j + 1];
@@ -601,8 +604,15 @@ __global__ void __launch_bounds__(MLA_THREADS) k_mla_merge(int kvr, const uint32
     __syncthreads();
     for (int j = tid; j < kvr; j += MLA_THREADS) {
         float o = 0.0f;
-#pragma unroll 16
-        for (int s2 = 0; s2 < live; s2++) o = fmaf(__ldcg(rec + (size_t)s2 * REC + j), wts[s2], o);
+        int s2 = 0;
+        for (; s2 + 32 <= live; s2 += 32) {  // 32 record loads in flight, then added in order
+            float v[32];
+#pragma unroll
+            for (int k = 0; k < 32; k++) v[k] = __ldcg(rec + (size_t)(s2 + k) * REC + j);
+#pragma unroll
+            for (int k = 0; k < 32; k++) o = fmaf(v[k], wts[s2 + k], o);
+        }
+        for (; s2 < live; s2++) o = fmaf(__ldcg(rec + (size_t)s2 * REC + j), wts[s2], o);
         c_acc[(size_t)h * kvr + j] = o * inv_l;
     }
 }
@@ -627,7 +637,8 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 void launch_mla_front(const float *kv_a, const float *kv_norm, int kvr, int rope, float eps, float *q, int n_heads,
                       int kd, int nope, const float *rope_tab, const uint32_t *pos, int ctx, float *c_cache,
                       float *r_cache, cudaStream_t st) {
-    launch_pdl_(k_mla_front, dim3(1 + cdiv_u(n_heads, 8)), dim3(256), 0, st, kv_a, kv_norm, kvr, rope, eps, q,
+    if (kvr * 4 > 48 * 1024) cudaFuncSetAttribute(k_mla_front, cudaFuncAttributeMaxDynamicSharedMemorySize, kvr * 4);
+    launch_pdl_(k_mla_front, dim3(1 + cdiv_u(n_heads, 8)), dim3(256), (size_t)kvr * 4, st, kv_a, kv_norm, kvr, rope, eps, q,
                 n_heads, kd, nope, rope_tab, pos, ctx, c_cache, r_cache);
 }
 

@@ -426,16 +426,27 @@ void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float 
 // MLA absorption (deepseek.zig:944-958): for head h and latent column j,
 // qa[h][j] = sum over r < nope, in order from +0, of q[h*kd + r] * W[h*(nope+vd) + r][j]
 // (axpy of each dequantized W_k row, exact dequantRow values), W = attn_kv_b [nh*(nope+vd)][kvr].
-__global__ void k_mla_absorb(WDev w, int kvr, int nope, int vd, int kd, const float *q, float *qa) {
-    const int h = blockIdx.y, j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= kvr) return;
-    const int be = block_elems(w.type), nb = kvr / be;
-    float a = 0.0f;
-    for (int r = 0; r < nope; r++) {
+constexpr int MLA_AB_COLS = 64;  // latent columns per CTA of k_mla_absorb
+__global__ void __launch_bounds__(512) k_mla_absorb(WDev w, int kvr, int nope, int vd, int kd, const float *q, float *qa) {
+    // this CTA: head h, latent columns [j0, j0 + 64); every W_k value it needs dequantized into
+    // shared memory by all threads at once, then each column's sum over the rows in order
+    extern __shared__ float wk_s[];  // [nope][64], then the head's q rows [nope]
+    const int h = blockIdx.y, j0 = blockIdx.x * MLA_AB_COLS, tid = threadIdx.x;
+    const int be = block_elems(w.type), nb = kvr / be, nc = min(MLA_AB_COLS, kvr - j0);
+    float *qs = wk_s + nope * MLA_AB_COLS;
+    for (int i = tid; i < nope * MLA_AB_COLS; i += blockDim.x) {
+        const int r = i / MLA_AB_COLS, jj = i % MLA_AB_COLS, j = j0 + jj;
         const uint64_t row = (uint64_t)h * (nope + vd) + r;
-        a = fadd(a, fmul(q[(size_t)h * kd + r], dequant_at(w, row * nb + j / be, j % be)));
+        wk_s[i] = jj < nc ? dequant_at(w, row * nb + j / be, j % be) : 0.0f;
     }
-    qa[(size_t)h * kvr + j] = a;
+    for (int r = tid; r < nope; r += blockDim.x) qs[r] = __ldg(q + (size_t)h * kd + r);
+    __syncthreads();
+    if (tid < nc) {
+        float a = 0.0f;
+#pragma unroll 8
+        for (int r = 0; r < nope; r++) a = fadd(a, fmul(qs[r], wk_s[r * MLA_AB_COLS + tid]));
+        qa[(size_t)h * kvr + j0 + tid] = a;
+    }
 }
 
 // W_v per head (deepseek.zig:988): out[h*vd + r] = W[h*(nope+vd) + nope + r] . c_h, the
@@ -453,7 +464,9 @@ __global__ void __launch_bounds__(256) k_mla_wv(WDev w, int nope, int vd, int nb
 
 void launch_mla_absorb(const WDev &w, int kvr, int nope, int vd, int kd, int n_heads, const float *q, float *qa,
                        cudaStream_t st) {
-    k_mla_absorb<<<dim3(cdiv(kvr, 128), n_heads), 128, 0, st>>>(w, kvr, nope, vd, kd, q, qa);
+    const size_t smem = (size_t)nope * (MLA_AB_COLS + 1) * 4;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k_mla_absorb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_mla_absorb<<<dim3(cdiv(kvr, MLA_AB_COLS), n_heads), 512, smem, st>>>(w, kvr, nope, vd, kd, q, qa);
     count_launch();
 }
 
