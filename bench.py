@@ -69,6 +69,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 DIM, FFN, NE, NK, LAYERS = 2048, 768, 128, 8, 48
+LAYERS_DEFAULT = LAYERS
 Q4K, Q6K, F32 = 12, 14, 0
 METRIC = "decode tok/s (Qwen3-30B-A3B MoE stack, Q4_K/Q6_K, T=1)"
 
@@ -600,6 +601,7 @@ def run_e2e(args, B):
 # ---- full-model decode (--workload model) -------------------------------------------
 
 MODEL_METRIC = "decode tok/s (Qwen3-30B-A3B full model, Q4_K_M, batch 1, ctx 2048)"
+DS_METRIC = "decode tok/s (DeepSeek-V2-Lite-shaped full model, Q4_K/Q8_0, batch 1)"
 
 
 def model_bytes(spec, pos: int, n_local: int = None) -> int:
@@ -684,14 +686,16 @@ def run_model(args):
     import torch.distributed as dist
     from loom_b200 import backend as B
     from loom_b200 import device as D
-    from loom_b200.model import DeviceModel, qwen3_moe
+    from loom_b200.model import DeviceModel, deepseek_v2_lite, qwen3_moe
 
     rank, world, local = dist_env()
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     B.init(local)
-    spec = qwen3_moe(n_layers=args.layers, ctx_len=args.ctx)
+    ds_main = args.model == "ds-v2-lite"
+    spec = (deepseek_v2_lite(n_layers=args.layers if args.layers != LAYERS_DEFAULT else 27, ctx_len=args.ctx)
+            if ds_main else qwen3_moe(n_layers=args.layers, ctx_len=args.ctx))
     shard = D.expert_range(spec.n_expert, rank, world) if world > 1 else None
     if world > 1:
         D.ep_init(rank, world, dist)
@@ -753,13 +757,13 @@ def run_model(args):
     dev.free()
 
     ds = None
-    if world == 1 and not args.no_deepseek:
+    if world == 1 and not args.no_deepseek and not ds_main:
         try:
             ds = run_model_deepseek(args, peak, peak_kind)
         except Exception as e:  # reported in the line, never fatal to the headline
             ds = {"error": f"{type(e).__name__}: {e}"[:300]}
     moe = None
-    if world == 1 and not args.no_moe_stack:
+    if world == 1 and not args.no_moe_stack and not ds_main:
         margs = argparse.Namespace(**vars(args))
         margs.tokens, margs.ep, margs.engine, margs.trace = 1, False, "auto", False
         margs.layers = args.layers
@@ -767,15 +771,15 @@ def run_model(args):
     if rank != 0:
         return
     cpu = None
-    if not args.no_cpu and world == 1:
+    if not args.no_cpu and world == 1 and not ds_main:
         cpu = cpu_model_baseline(spec, pos)
     line = {
-        "metric": MODEL_METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": DS_METRIC if ds_main else MODEL_METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "int8xq4/q6 matvecs (f32 accum), f32 attention and KV",
         "data": "synthetic (seeded generator), random-init weights",
-        "config": {"workload": f"qwen3-30b-a3b full-model decode, batch 1, position {pos} of a {spec.ctx_len}-token "
+        "config": {"workload": f"{spec.name} full-model decode, batch 1, position {pos} of a {spec.ctx_len}-token "
                                f"context", "model": spec.name, "layers": spec.n_layers, "batch": 1,
                    "ctx": spec.ctx_len, "dim": spec.dim, "n_heads": spec.n_heads, "n_kv_heads": spec.n_kv_heads,
                    "n_expert": spec.n_expert, "n_used": spec.n_used, "vocab": spec.vocab,
@@ -853,7 +857,7 @@ def run_model_deepseek(args, peak, peak_kind):
         dev.free()
     bytes_step = model_bytes(spec, pos)
     achieved = bytes_step / (ms * 1e-3) / 1e9
-    return {"metric": "decode tok/s (DeepSeek-V2-Lite-shaped full model, Q4_K/Q8_0, batch 1)",
+    return {"metric": DS_METRIC,
             "value": round(1e3 / ms, 2), "unit": "tok/s", "ms_per_step": round(ms, 4),
             "config": {"workload": f"deepseek-v2-lite full-model decode, batch 1, position {pos} of a "
                                    f"{spec.ctx_len}-token context", "model": spec.name, "layers": spec.n_layers,
@@ -920,6 +924,8 @@ def main():
                     help="model: full Qwen3-30B-A3B decode (the headline); moe: the 48 MoE layers only")
     ap.add_argument("--ctx", type=int, default=2048, help="context length of the model workload")
     ap.add_argument("--no-moe-stack", action="store_true", help="model workload: skip the MoE-only sub-measurement")
+    ap.add_argument("--model", default="qwen3", choices=["qwen3", "ds-v2-lite"],
+                    help="model workload: the headline Qwen3-30B-A3B shape, or the DeepSeek-V2-Lite shape (MLA)")
     ap.add_argument("--no-fill", action="store_true",
                     help="model workload: leave the KV cache unfilled (profiling captures only; the kernels and "
                          "bytes are the same, the cached values are zeros)")
