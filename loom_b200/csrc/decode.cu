@@ -158,6 +158,13 @@ __device__ __noinline__ void prenorm_smem(float *sx, const float *w, int dim, fl
     __syncthreads();
 }
 
+// every expert of a pre-routed row is -1 (an unused fixed-capacity entry)
+__device__ __forceinline__ bool row_unused(const int *ids, int n) {
+    for (int k = 0; k < n; k++)
+        if (__ldcg(ids + k) >= 0) return false;
+    return true;
+}
+
 __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const float *smx, float *scores, float *choice,
                                             int nw) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -179,8 +186,9 @@ __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const fl
             for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS)
                 A.ids_out[(size_t)t * A.n_used + k] = sid[k];
         if (A.trace && threadIdx.x == 0) atomicMin(A.trace + 2 * (A.trace_slot + 6), gtimer());
-    } else {
-        // quantize x in the format(s) the expert types read
+    } else if (!(A.ids_in && row_unused(A.ids_in + (size_t)t * A.n_used, A.n_used))) {
+        // quantize x in the format(s) the expert types read (not for the unused
+        // entries of a fixed-capacity exchange: expert -1, no expert reads them)
         const int nwq = nw - ROUTE_THREADS / 32, wi = warp - ROUTE_THREADS / 32;
         if (A.need256)
             for (int b = wi; b < dim / 256; b += nwq)

@@ -214,6 +214,33 @@ bool ep_active() { return g_comm != nullptr && g_size > 1; }
 int ep_rank() { return g_rank; }
 int ep_size() { return g_size; }
 
+bool ep_agree(const int *vals, int n, std::string &err) {
+    if (!ep_active()) return true;
+    if (n > 16) return false;
+    // min and max of every value over the ranks: equal everywhere iff min == max
+    int h[32];
+    for (int i = 0; i < n; i++) {
+        h[i] = vals[i];
+        h[16 + i] = -vals[i];
+    }
+    int *d = nullptr;
+    cudaStream_t st = nullptr;
+    bool ok = cudaMalloc(&d, sizeof h) == cudaSuccess && cudaStreamCreate(&st) == cudaSuccess &&
+              cudaMemcpyAsync(d, h, sizeof h, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+              N.allReduce(d, d, 32, ncclInt32, ncclMin, g_comm, st) == ncclSuccess &&
+              cudaMemcpyAsync(h, d, sizeof h, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+              cudaStreamSynchronize(st) == cudaSuccess;
+    if (d) cudaFree(d);
+    if (st) cudaStreamDestroy(st);
+    if (!ok) {
+        err = "expert-parallel agreement failed";
+        return false;
+    }
+    for (int i = 0; i < n; i++)
+        if (h[i] != -h[16 + i]) return false;  // some rank's value differs
+    return true;
+}
+
 int ep_allreduce_sum(float *buf, size_t n, cudaStream_t st, std::string &err) {
     if (!ep_active()) return LOOM_CUDA_OK;
     if (P2.ready && n <= P2P_MAXN && n % 4 == 0 && (reinterpret_cast<uintptr_t>(buf) & 15) == 0) {

@@ -11,6 +11,10 @@ namespace loom {
 bool ep_active();
 int ep_rank();
 int ep_size();
+// Collective: true on every rank when every rank passed the same n ints
+// (host values; n <= 16), false on every rank otherwise. Synchronises the
+// host with one small NCCL exchange on a private stream.
+bool ep_agree(const int *vals, int n, std::string &err);
 // out[i] = sum over ranks of out[i] (in place), on stream st
 int ep_allreduce_sum(float *buf, size_t n, cudaStream_t st, std::string &err);
 

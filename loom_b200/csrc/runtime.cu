@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <set>
 #include <string>
 #include <tuple>
 #include <unordered_map>
@@ -1256,9 +1257,40 @@ namespace {
 // Both all-to-all forms: t_cap == 0 sends exactly the routed rows (their
 // counts go to the host once per layer); t_cap > 0 sends fixed runs of
 // t_cap * n_used rows to every rank (no host synchronisation).
+// The all-to-all layer is a collective: a rank that declined alone would leave
+// its peers blocked in the exchange. So every layer shape is agreed once
+// (every rank valid, the same t_cap and shapes) before its first exchange,
+// and declined on every rank otherwise; and a rank with more tokens than the
+// fixed capacity still takes part (it sends none of its rows, runs the rows
+// its peers send it) and then declines for its own tokens.
+std::set<std::vector<int>> g_a2a_agreed;
+
+int ep_a2a_checked(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, const float *d_residual,
+                   const float *d_logits, uint32_t *d_ids, void *stream, size_t t_cap);
+
 int ep_a2a(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, const float *d_residual,
            const float *d_logits, uint32_t *d_ids, void *stream, size_t t_cap) {
     if (int rc = need_init()) return rc;
+    if (!ep_active()) return ep_a2a_checked(desc, d_x, T, d_out, d_residual, d_logits, d_ids, stream, t_cap);
+    // this rank's verdict on the layer shape (the local checks, no work), then the agreement
+    const int local = ep_a2a_checked(desc, nullptr, 0, nullptr, nullptr, d_logits, nullptr, stream, t_cap | (1ull << 62));
+    std::vector<int> key{local == LOOM_CUDA_OK ? 1 : 0, (int)t_cap, desc ? (int)desc->n_expert : 0,
+                         desc ? (int)desc->n_used : 0, desc ? (int)desc->dim : 0, desc ? (int)desc->ffn : 0,
+                         desc && desc->shexp_gate ? (int)desc->shexp_ffn : -1, d_logits ? 1 : 0};
+    if (!g_a2a_agreed.count(key)) {
+        if (!ep_agree(key.data(), (int)key.size(), g_err)) return decline("the ranks disagree on the all-to-all layer (shape, t_cap or a local check)");
+        if (key[0] == 0) return local;  // every rank declined alike
+        g_a2a_agreed.insert(key);
+    }
+    if (local != LOOM_CUDA_OK) return local;
+    return ep_a2a_checked(desc, d_x, T, d_out, d_residual, d_logits, d_ids, stream, t_cap);
+}
+
+// t_cap's bit 62: validate only (no launches, no exchange).
+int ep_a2a_checked(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, const float *d_residual,
+                   const float *d_logits, uint32_t *d_ids, void *stream, size_t t_cap) {
+    const bool check_only = (t_cap >> 62) & 1;
+    t_cap &= ~(1ull << 62);
     if (!desc) return decline("no layer description");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g_stream;
     const loom_moe_desc &D = *desc;
@@ -1301,9 +1333,13 @@ int ep_a2a(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, 
         if (!r || r->type != T_F32 || r->nblk < D.n_expert * D.dim) return decline("router must be f32 [n_expert][dim]");
         router = reinterpret_cast<const float *>(r->base);
     }
-    const size_t dim = D.dim, k = D.n_used, ns = T * k;
-    if (t_cap && T > t_cap) return decline("more tokens than the all-to-all capacity");
+    const size_t dim = D.dim, k = D.n_used;
     if (t_cap && (size_t)world * t_cap * k > (1u << 24)) return decline("all-to-all capacity out of range");
+    if (check_only) return LOOM_CUDA_OK;
+    // more tokens than the capacity: take part without sending any of this rank's rows, then decline
+    const bool over = t_cap && T > t_cap;
+    if (over) T = 0;
+    const size_t ns = T * k;
     const size_t cap = t_cap * k, nsend = std::max(ns, (size_t)world * cap);  // send-list entries
     const size_t max_ffn = std::max<size_t>(D.ffn, sh[0] ? D.shexp_ffn : 0), act_stride = align256(max_ffn);
     // home side: route, then the destination-ordered send lists
@@ -1417,6 +1453,7 @@ int ep_a2a(const loom_moe_desc *desc, const float *d_x, size_t T, float *d_out, 
     launch_a2a_combine(S.a2a_yb.as<float>(), slot_pos, home_gates, y_sh, d_residual, d_out, (int)T, (int)k, (int)dim,
                        st);
     CK(cudaGetLastError());
+    if (over) return decline("more tokens than the all-to-all capacity (this rank's rows were not sent; its peers' were run)");
     return LOOM_CUDA_OK;
 }
 

@@ -55,6 +55,34 @@ def main():
             if not same:
                 print(f"rank {rank} round {rnd}: max diff {float((out - want).abs().max())}", flush=True)
                 ok = 0
+    # a collective that one rank cannot complete must not leave the other blocked:
+    # (a) rank 0 has more tokens than the capacity: it takes part, sends none of its
+    #     rows and declines; rank 1's tokens are still served, bit for bit;
+    # (b) the ranks pass different capacities: both decline, neither exchanges
+    import ctypes as C
+    from loom_b200 import _lib
+    from loom_b200.device import _ptr, _st
+    L = _lib.lib()
+    for name, counts, caps in [("over", (6, 3), (4, 4)), ("mismatch", (2, 2), (6, 7))]:
+        T = counts[rank % 2]
+        g = torch.Generator("cuda").manual_seed(77 + rank)
+        x = torch.randn((T, dim), device="cuda", generator=g)
+        res = torch.randn((T, dim), device="cuda", generator=g)
+        out = torch.full((T, dim), float("nan"), device="cuda")
+        d = shard.desc()
+        rc = L.loom_cuda_ep_a2a_forward_cap(C.byref(d), _ptr(x), T, caps[rank % 2], _ptr(out), _ptr(res), None,
+                                            None, _st(None))
+        want_rc = (_lib.DECLINED if rank == 0 else _lib.OK) if name == "over" else _lib.DECLINED
+        if rc != want_rc:
+            print(f"rank {rank} {name}: rc {rc}, expected {want_rc}", flush=True)
+            ok = 0
+        elif rc == _lib.OK:
+            want = torch.empty((T, dim), device="cuda")
+            full.forward(x, want, residual=res)
+            torch.cuda.synchronize()
+            if not np.array_equal(out.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32)):
+                print(f"rank {rank} {name}: served tokens differ", flush=True)
+                ok = 0
     t = torch.tensor([ok], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MIN)
     if rank == 0:
