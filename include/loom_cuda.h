@@ -511,8 +511,8 @@ int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float
  * kernels for T <= 2, expert-major batch kernels above, on the tensor cores
  * once the experts average >= 16 tokens), 1 the general slot kernels, 2 the
  * expert-major batch kernels at any T, 3 the expert-major batch kernels on
- * the tensor cores at any T (Q4_K gate/up with Q6_K down whose scales are
- * within +-32; other layers fall back to 2). Every family computes the same
+ * the tensor cores at any T (Q4_K gate/up with Q6_K down, any scales;
+ * other layers fall back to 2). Every family computes the same
  * numbers bit for bit. Returns the previous setting. */
 int loom_cuda_force_generic(int on);
 /* Kernel family the last routed layer ran: 0 fused decode, 1 slot kernels,

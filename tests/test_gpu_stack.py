@@ -86,3 +86,43 @@ def test_one_layer_stack_with_residual_bitexact(be, orc):
         st.free()
         for t in (L.gate, L.up, L.down, L.router):
             t.free()
+
+
+def test_stack_matches_oracle_layer_by_layer(be, orc):
+    """The persistent stack against the oracle directly: three Qwen3-shaped
+    layers, x_{l+1} = x_l + moeLayer_l(x_l) with the
+    oracle's moeLayer (moe.zig / ggml.zig restated in C); every layer's ids
+    equal where the router's top-k margins are clear, the output within the
+    path's tolerance."""
+    from tests.conftest import rel_l2
+    from tests.test_gpu_moe import _route_gaps_ok
+    n_layers, ne, k, dim, ffn = 3, 128, 8, 2048, 768
+    hosts = []
+    for i in range(n_layers):
+        g, u, d = synth_layer(orc, 100 + i, ne, dim, ffn)
+        rw = orc.synth(0, ne * dim, seed=300 + i, sigma=0.02)
+        hosts.append((g, u, d, rw))
+    layers = [MoeLayer(dim, ffn, ne, k, DeviceTensor.upload(12, g), DeviceTensor.upload(12, u),
+                       DeviceTensor.upload(14, d), router=DeviceTensor.upload(0, rw)) for g, u, d, rw in hosts]
+    x0 = orc.synth(0, dim, seed=777, sigma=1.0).reshape(1, dim)
+    S = Stack(layers)
+    try:
+        out = torch.full((1, dim), float("nan"), device="cuda")
+        ids = torch.zeros((n_layers, k), dtype=torch.int32, device="cuda")
+        S.forward(torch.from_numpy(x0).cuda(), out, ids)
+        torch.cuda.synchronize()
+        assert S.error() == 0
+        got_ids = ids.cpu().numpy()
+        x = x0.astype(np.float32)
+        for li, (g, u, d, rw) in enumerate(hosts):
+            y, wids = orc.moe_layer(x, rw, (12, g), (12, u), (14, d), ffn, ne, k)
+            logits = orc.matmul(0, rw.view(np.uint8), x, ne, dim)
+            if _route_gaps_ok(logits[0], k):
+                assert list(got_ids[li]) == list(wids[0]), li
+            x = (x + y).astype(np.float32)
+        assert rel_l2(out.cpu().numpy(), x) < 2e-3, rel_l2(out.cpu().numpy(), x)
+    finally:
+        S.free()
+    for L in layers:
+        for t in (L.gate, L.up, L.down, L.router):
+            t.free()
