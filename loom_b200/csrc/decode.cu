@@ -154,7 +154,7 @@ __device__ __noinline__ void prenorm_smem(float *sx, const float *w, int dim, fl
     }
     __syncthreads();
     const float scale = red[0];
-    for (int i = tid; i < dim; i += blockDim.x) sx[i] = fmul(fmul(sx[i], scale), __ldg(w + i));
+    for (int i = tid; i < dim; i += blockDim.x) sx[i] = fmul(fmul(sx[i], scale), w[i]);
     __syncthreads();
 }
 
@@ -258,8 +258,8 @@ constexpr int RR2_WARPS = 8;
 constexpr uint32_t WAIT_POLLS = 1u << 22;  // bounded mbarrier wait (far beyond any legitimate latency)
 
 __global__ void __launch_bounds__(RR2_WARPS * 32) k_router_tma(DecodeArgs A) {
-    extern __shared__ __align__(16) float smw[];  // W rows [rpc][dim] | x[dim] | scores | choice | ids | gates
-    __shared__ __align__(8) uint64_t bar;
+    extern __shared__ __align__(16) float smw[];  // W rows [rpc][dim] | x[dim] | scores | choice | ids | gates | norm w
+    __shared__ __align__(8) uint64_t bar, bar_x;
     const int t = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int dim = A.dim, ne = A.n_expert;
@@ -270,21 +270,35 @@ __global__ void __launch_bounds__(RR2_WARPS * 32) k_router_tma(DecodeArgs A) {
     const int nrows = row0 >= ne ? 0 : (ne - row0 < rpc ? ne - row0 : rpc);
     float *smx = smw + (size_t)rpc * dim;
     float *scores = smx + dim, *choice = scores + ne;
+    float *snw = choice + ne + 136;  // the FFN norm weights, bulk-copied when 16-byte aligned
+    const bool wbulk = A.prenorm_w && (size_t)(snw - smw) % 4 == 0;
     trace_begin(A, 0);
-    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init(&bar_x, 1);
+    }
     __syncthreads();
-    if (threadIdx.x == 0 && nrows > 0) {
-        mbar_expect_tx(&bar, (uint32_t)(nrows * dim * 4));
+    if (threadIdx.x == 0 && (nrows > 0 || wbulk)) {
+        // the router rows and the norm weights (neither depends on the previous kernel)
+        mbar_expect_tx(&bar, (uint32_t)(nrows * dim * 4) + (wbulk ? (uint32_t)dim * 4 : 0u));
         for (int r = 0; r < nrows; r++)
             bulk_g2s(smw + (size_t)r * dim, A.router + (size_t)(row0 + r) * dim, (uint32_t)(dim * 4), &bar);
+        if (wbulk) bulk_g2s(snw, A.prenorm_w, (uint32_t)dim * 4, &bar);
     }
     pdl_wait();
-    
+
     const float *xt = A.x + (size_t)t * dim;
     trace_begin(A, 3);
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) smx[i] = xt[i];
-    __syncthreads();
-    if (A.prenorm_w) prenorm_smem(smx, A.prenorm_w, dim, A.prenorm_eps);
+    if (threadIdx.x == 0) {  // the row the previous kernel wrote, as one bulk copy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_expect_tx(&bar_x, (uint32_t)dim * 4);
+        bulk_g2s(smx, xt, (uint32_t)dim * 4, &bar_x);
+    }
+    if (!mbar_wait(&bar_x, 0, WAIT_POLLS) && threadIdx.x == 0 && A.err) atomicOr(A.err, 1);
+    if (A.prenorm_w) {
+        if (wbulk && !mbar_wait(&bar, 0, WAIT_POLLS) && threadIdx.x == 0 && A.err) atomicOr(A.err, 1);
+        prenorm_smem(smx, wbulk ? snw : A.prenorm_w, dim, A.prenorm_eps);
+    }
     const long long c0 = clock64();
     if (nrows > 0 && !mbar_wait(&bar, 0, WAIT_POLLS)) {
         if (threadIdx.x == 0 && A.err) atomicOr(A.err, 1);
@@ -791,7 +805,7 @@ static int tma_cluster(const DecodeArgs &A, size_t &smem) {
     if (!ok) return 0;
     for (int c : {c16 ? 16 : 8, 8}) {
         const int rpc = (A.n_expert + c - 1) / c;
-        smem = ((size_t)rpc * A.dim + A.dim + 2 * A.n_expert + 136) * 4;
+        smem = ((size_t)rpc * A.dim + A.dim + 2 * A.n_expert + 136 + A.dim) * 4;
         if (A.dim % 4 == 0 && smem <= 200 * 1024) return c;
     }
     return 0;
