@@ -416,9 +416,23 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
     int8_t *xq = reinterpret_cast<int8_t *>(sm);
     float *xd = reinterpret_cast<float *>(sm + dim);
     int32_t *xs = reinterpret_cast<int32_t *>(sm + dim + NB * 4);
-    stage16(xq, A.x256.q + (size_t)si.token * dim, dim);
-    for (int i = threadIdx.x; i < NB; i += blockDim.x) xd[i] = __ldcg(A.x256.d + (size_t)si.token * NB + i);
-    for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) xs[i] = __ldcg(A.x256.s + (size_t)si.token * NB * 16 + i);
+    // (written by the router kernel: three bulk copies, landing while the weights load)
+    constexpr bool XBULK = NB % 4 == 0;  // 16-byte sizes and offsets
+    __shared__ __align__(8) uint64_t bx;
+    if (XBULK) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bx, 1);
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_expect_tx(&bx, (uint32_t)(dim + NB * 4 + NB * 64));
+            bulk_g2s(xq, A.x256.q + (size_t)si.token * dim, (uint32_t)dim, &bx);
+            bulk_g2s(xd, A.x256.d + (size_t)si.token * NB, (uint32_t)NB * 4, &bx);
+            bulk_g2s(xs, A.x256.s + (size_t)si.token * NB * 16, (uint32_t)NB * 64, &bx);
+        }
+    } else {
+        stage16(xq, A.x256.q + (size_t)si.token * dim, dim);
+        for (int i = threadIdx.x; i < NB; i += blockDim.x) xd[i] = __ldcg(A.x256.d + (size_t)si.token * NB + i);
+        for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) xs[i] = __ldcg(A.x256.s + (size_t)si.token * NB * 16 + i);
+    }
     const WDev wg = si.shared ? A.sg : A.g, wu = si.shared ? A.su : A.u;
     const uint64_t plane = si.shared ? 0 : (uint64_t)si.expert_local * si.ffn * NB;
     const int r0 = blockIdx.x * rows_cta + warp * GU_NR;
@@ -445,6 +459,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_gateup_dec(DecodeArgs A) {
         }
     }
     __syncthreads();
+    if (XBULK && !mbar_wait(&bx, 0, WAIT_POLLS) && threadIdx.x == 0 && A.err) atomicOr(A.err, 1);
     float acc[2 * GU_NR];
     E::finish(st, fr, acc, lane);
     float *act = A.act + (size_t)slot * A.act_stride;
