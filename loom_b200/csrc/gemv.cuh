@@ -11,5 +11,10 @@ bool gemv_supported(int type, int cols);
 // Launched with programmatic dependent launch: the weight loads are issued
 // before the wait for the kernel that wrote x. Bit-identical to launch_mm.
 cudaError_t launch_gemv(const WDev &w, int rows, int cols, const XQ &x, float *out, cudaStream_t st);
+// Large matrices (>= 4096 rows, Q4_K or Q6_K with nb % 8 == 0, up to 128 blocks
+// a row): tiles streamed through shared memory by bulk copies, one CTA per SM.
+// Bit-identical to launch_gemv / launch_mm.
+bool gemv_stream_supported(int type, int rows, int cols);
+cudaError_t launch_gemv_stream(const WDev &w, int rows, int cols, const XQ &x, float *out, cudaStream_t st);
 
 }  // namespace loom

@@ -164,6 +164,11 @@ void need_kind(int t, bool &k256, bool &k32) {
         k32 = true;
 }
 
+bool getenv_stream_off() {  // LOOM_CUDA_NO_GEMV_STREAM=1: the warp-engine matvec for every size (comparisons)
+    static const int off = getenv("LOOM_CUDA_NO_GEMV_STREAM") ? 1 : 0;
+    return off != 0;
+}
+
 void matvec(const Mat &m, const float *xf, const XQW &x256, const XQW &x32, float *out, cudaStream_t st) {
     if (m.type == T_F32) {
         launch_mm_f32(reinterpret_cast<const float *>(m.w.q), m.rows, m.cols, xf, 1, out, st);
@@ -172,7 +177,9 @@ void matvec(const Mat &m, const float *xf, const XQW &x256, const XQW &x32, floa
     } else {
         const XQ x = act256(m.type) ? XQ{x256.q, x256.d, x256.s, m.cols, m.cols / 256, m.cols / 16, 1}
                                     : XQ{x32.q, x32.d, x32.s, m.cols, m.cols / 32, m.cols / 32, 0};
-        if (gemv_supported(m.type, m.cols))
+        if (gemv_stream_supported(m.type, (int)m.rows, (int)m.cols) && !getenv_stream_off())
+            launch_gemv_stream(m.w, (int)m.rows, (int)m.cols, x, out, st);  // large: tiles streamed through smem
+        else if (gemv_supported(m.type, m.cols))
             launch_gemv(m.w, m.rows, m.cols, x, out, st);  // warp engine, weights loaded ahead of the wait
         else
             launch_mm(m.w, 0, m.rows, m.cols, x, 1, out, st);

@@ -17,6 +17,7 @@
 
 #include "../../include/loom_cuda.h"
 #include "attn.cuh"
+#include "gemv.cuh"
 #include "decode.cuh"
 #include "ep.cuh"
 #include "kernels.cuh"
@@ -1487,7 +1488,10 @@ int loom_cuda_tensor_matmul(loom_tensor h, size_t rows, size_t cols, const float
     } else {
         if (int rc = ensure_xq(n, cols)) return rc;
         quantize_into(d_xs, n, cols, act256(t->type), st);
-        launch_mm(t->w, 0, (int)rows, (int)cols, make_xq(act256(t->type), cols), (int)n, d_out, st);
+        if (n == 1 && gemv_stream_supported(t->type, (int)rows, (int)cols))  // one vector, a large matrix
+            CK(launch_gemv_stream(t->w, (int)rows, (int)cols, make_xq(act256(t->type), cols), d_out, st));
+        else
+            launch_mm(t->w, 0, (int)rows, (int)cols, make_xq(act256(t->type), cols), (int)n, d_out, st);
     }
     CK(cudaGetLastError());
     return LOOM_CUDA_OK;

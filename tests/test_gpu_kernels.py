@@ -235,3 +235,23 @@ def test_repeated_seam_calls_replay_exactly(be, orc, t):
         be.matvec(t, got, data, x, rows, cols)
         assert be.kernelLaunches() > k0
         assert np.array_equal(bits(got), bits(orc.matvec(t, data, x, rows, cols)))
+
+
+@pytest.mark.parametrize("t,rows,cols", [(12, 8195, 7168), (12, 4100, 16384), (14, 5003, 2048), (14, 4096, 4096)])
+def test_streamed_matvec_bitexact(be, orc, t, rows, cols):
+    """Large matrices take the streamed matvec (tiles bulk-copied through
+    shared memory, one CTA per SM; ragged last tiles): bit-identical to the
+    oracle's matvec (ggml.zig:602)."""
+    import torch
+    from loom_b200 import device as D
+    nblk = rows * cols // 256
+    W = D.DeviceTensor.synth(t, nblk, seed=911 + t, sigma=1.0)
+    try:
+        x = orc.synth(0, cols, seed=912, sigma=1.0)
+        out = torch.full((1, rows), float("nan"), device="cuda")
+        D.tensor_matmul(W, rows, cols, torch.from_numpy(x.reshape(1, cols)).cuda(), out)
+        torch.cuda.synchronize()
+        want = orc.matvec(t, orc.synth(t, nblk, seed=911 + t), x, rows, cols)
+        assert np.array_equal(bits(out.cpu().numpy().reshape(-1)), bits(want))
+    finally:
+        W.free()
