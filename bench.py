@@ -803,19 +803,28 @@ def run_model(args):
                              if k in moe}
     if ds:
         line["deepseek_v2_lite"] = ds
+    if world == 1 and not args.no_deepseek and not ds_main and args.v3_layers > 0:
+        try:
+            line["deepseek_v3_cut"] = run_model_deepseek(args, peak, peak_kind, which="v3")
+        except Exception as e:
+            line["deepseek_v3_cut"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
 
 
-def run_model_deepseek(args, peak, peak_kind):
-    """The DeepSeek-V2-Lite-shaped model (MLA attention,
-    layer 0 dense, 64 routed experts top-6 + 2 shared): one decode token at
-    position ctx - 1 after filling the cache by decoding, graph-replayed and
-    event-timed like the headline; e2e through loom_cuda_model_decode."""
+def run_model_deepseek(args, peak, peak_kind, which="v2-lite"):
+    """A DeepSeek-shaped model: V2-Lite (MLA attention,
+    layer 0 dense, 64 routed experts top-6 + 2 shared), or a cut of the V3
+    shape (config 5 at full width: dim 7168, 128 MLA heads with q-LoRA, 256
+    experts top-8 with sigmoid + bias and grouped top-k, one shared expert; the
+    first `layers` of its 61, three dense). One decode token at position
+    ctx - 1 after filling the cache by decoding, graph-replayed and event-timed
+    like the headline; e2e through loom_cuda_model_decode."""
     import torch
-    from loom_b200.model import DeviceModel, deepseek_v2_lite
-    spec = deepseek_v2_lite(ctx_len=args.ctx)
+    from loom_b200.model import DeviceModel, deepseek_v2_lite, deepseek_v3
+    spec = deepseek_v2_lite(ctx_len=args.ctx) if which == "v2-lite" else deepseek_v3(n_layers=args.v3_layers,
+                                                                                       ctx_len=args.ctx)
     dev = DeviceModel(spec)
     try:
         pos = spec.ctx_len - 1
@@ -857,10 +866,13 @@ def run_model_deepseek(args, peak, peak_kind):
         dev.free()
     bytes_step = model_bytes(spec, pos)
     achieved = bytes_step / (ms * 1e-3) / 1e9
-    return {"metric": DS_METRIC,
+    metric = DS_METRIC if which == "v2-lite" else (
+        f"decode tok/s (DeepSeek-V3-shaped model, first {spec.n_layers} of 61 layers at full width, Q4_K, batch 1)")
+    return {"metric": metric,
             "value": round(1e3 / ms, 2), "unit": "tok/s", "ms_per_step": round(ms, 4),
-            "config": {"workload": f"deepseek-v2-lite full-model decode, batch 1, position {pos} of a "
+            "config": {"workload": f"{spec.name} decode ({spec.n_layers} layers), batch 1, position {pos} of a "
                                    f"{spec.ctx_len}-token context", "model": spec.name, "layers": spec.n_layers,
+                       "ms_per_layer": round(ms / spec.n_layers, 4),
                        "dim": spec.dim, "n_heads": spec.n_heads, "kv_lora": spec.kv_lora, "n_expert": spec.n_expert,
                        "n_used": spec.n_used, "shared_ffn": spec.shexp_ffn, "vocab": spec.vocab,
                        "engine": "loom_cuda_model_step (MLA kernels + fused MoE) in a CUDA graph",
@@ -926,6 +938,8 @@ def main():
     ap.add_argument("--no-moe-stack", action="store_true", help="model workload: skip the MoE-only sub-measurement")
     ap.add_argument("--model", default="qwen3", choices=["qwen3", "ds-v2-lite"],
                     help="model workload: the headline Qwen3-30B-A3B shape, or the DeepSeek-V2-Lite shape (MLA)")
+    ap.add_argument("--v3-layers", type=int, default=8,
+                    help="model workload: layers of the DeepSeek-V3-shaped cut measured beside the headline (0: skip)")
     ap.add_argument("--no-fill", action="store_true",
                     help="model workload: leave the KV cache unfilled (profiling captures only; the kernels and "
                          "bytes are the same, the cached values are zeros)")
