@@ -835,7 +835,10 @@ static cudaError_t launch_router(const DecodeArgs &A, cudaStream_t st) {
             return e;
         return launch_pdl(k_route_batch, dim3(A.T), dim3(256), rs, st, A);
     }
-    if (A.router && A.T > 16 && A.dim % 32 == 0 && A.dim <= 8192 && !A.trace_reg) {  // batch router
+    // batch router: many tokens, or a router too large for one cluster's shared memory (DeepSeek-V3:
+    // 256 x 7168 f32 = 7.3 MB), tiled over experts across the GPU
+    const bool big_router = (size_t)A.n_expert * A.dim * 4 > (4u << 20) && !A.prenorm_w;
+    if (A.router && (A.T > 16 || big_router) && A.dim % 32 == 0 && A.dim <= 8192 && !A.trace_reg) {
         const int et = rb_experts(A.dim);
         const size_t smem = ((size_t)et + RB_TOK) * A.dim * 4;
         cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
