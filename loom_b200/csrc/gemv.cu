@@ -87,7 +87,8 @@ __host__ __device__ inline size_t gs_act_bytes(int nb) {
 }
 
 template <int TY>
-__global__ void __launch_bounds__(GS_WARPS * 32, 1) k_gemv_stream(WDev w, int rows, int nb, XQ x, float *out, int tr) {
+__global__ void __launch_bounds__(GS_WARPS * 32, 1) k_gemv_stream(WDev w, int rows, int nb, XQ x, float *out, int tr,
+                                                                  const float *res) {
     extern __shared__ __align__(128) uint8_t gs[];
     __shared__ __align__(8) uint64_t full[GS_STAGES];
     __shared__ float tsm_all[GS_WARPS][128];
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(GS_WARPS * 32, 1) k_gemv_stream(WDev w, int ro
         for (int rr = warp * nS; rr < n; rr += GS_WARPS * nS) {
             const int ns = min(nS, n - rr);
             const float a = ab_rows<TY>(sg, rr, ns, xv, tsm, lane, 272, 20);
-            if (lane < ns) out[r0 + rr + lane] = a;
+            if (lane < ns) out[r0 + rr + lane] = res ? fadd(res[r0 + rr + lane], a) : a;
         }
         __syncthreads();  // every warp is done with this stage
         if (tid == 0) {
@@ -179,15 +180,18 @@ int gs_tile_rows(int type, int nb) {
 
 }  // namespace
 
-bool gemv_stream_supported(int type, int rows, int cols) {
+bool gemv_stream_shape_ok(int type, int cols) {
     if (type != T_Q4_K && type != T_Q6_K) return false;
     if (cols % 256) return false;
     const int nb = cols / 256;
     if (nb > 128 || (type == T_Q6_K && nb % 8)) return false;
-    return rows >= 4096 && gs_tile_rows(type, nb) >= 8;
+    return gs_tile_rows(type, nb) >= 8;
 }
 
-cudaError_t launch_gemv_stream(const WDev &w, int rows, int cols, const XQ &x, float *out, cudaStream_t st) {
+bool gemv_stream_supported(int type, int rows, int cols) { return rows >= 4096 && gemv_stream_shape_ok(type, cols); }
+
+cudaError_t launch_gemv_stream(const WDev &w, int rows, int cols, const XQ &x, float *out, cudaStream_t st,
+                               const float *res) {
     static int n_sm = 0;
     if (!n_sm) {
         int dev = 0;
@@ -202,10 +206,10 @@ cudaError_t launch_gemv_stream(const WDev &w, int rows, int cols, const XQ &x, f
     const dim3 grid(tiles < n_sm ? tiles : n_sm);
     if (w.type == T_Q6_K) {
         cudaFuncSetAttribute(k_gemv_stream<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        return launch_pdl_(k_gemv_stream<T_Q6_K>, grid, dim3(GS_WARPS * 32), smem, st, w, rows, nb, x, out, tr);
+        return launch_pdl_(k_gemv_stream<T_Q6_K>, grid, dim3(GS_WARPS * 32), smem, st, w, rows, nb, x, out, tr, res);
     }
     cudaFuncSetAttribute(k_gemv_stream<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    return launch_pdl_(k_gemv_stream<T_Q4_K>, grid, dim3(GS_WARPS * 32), smem, st, w, rows, nb, x, out, tr);
+    return launch_pdl_(k_gemv_stream<T_Q4_K>, grid, dim3(GS_WARPS * 32), smem, st, w, rows, nb, x, out, tr, res);
 }
 
 bool gemv_supported(int type, int cols) {

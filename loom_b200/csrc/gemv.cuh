@@ -14,7 +14,10 @@ cudaError_t launch_gemv(const WDev &w, int rows, int cols, const XQ &x, float *o
 // Large matrices (>= 4096 rows, Q4_K or Q6_K with nb % 8 == 0, up to 128 blocks
 // a row): tiles streamed through shared memory by bulk copies, one CTA per SM.
 // Bit-identical to launch_gemv / launch_mm.
+// res (optional): out[r] = res[r] + W[r] . x (the residual add, llama.zig's x + ffn).
 bool gemv_stream_supported(int type, int rows, int cols);
-cudaError_t launch_gemv_stream(const WDev &w, int rows, int cols, const XQ &x, float *out, cudaStream_t st);
+bool gemv_stream_shape_ok(int type, int cols);  // any row count
+cudaError_t launch_gemv_stream(const WDev &w, int rows, int cols, const XQ &x, float *out, cudaStream_t st,
+                               const float *res = nullptr);
 
 }  // namespace loom

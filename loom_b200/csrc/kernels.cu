@@ -517,6 +517,17 @@ __global__ void k_quant_act(const float *x, int ntok, int cols, int xstride, int
     }
 }
 
+// act = silu(g) * u (tensor.zig:30,53; the fused kernels' order: g / (1 + e^-g), then * u)
+__global__ void k_swiglu(const float *g, const float *u, int n, float *act) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        act[i] = fmul(fdiv(g[i], fadd(1.0f, exp_f(-g[i]))), u[i]);
+}
+
+void launch_swiglu(const float *g, const float *u, int n, float *act, cudaStream_t st) {
+    k_swiglu<<<cdiv(n, 256), 256, 0, st>>>(g, u, n, act);
+    count_launch();
+}
+
 void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d, int32_t *s,
                       int dstride, int sstride, cudaStream_t st) {
     const int items = kind256 ? ntok * (cols / 256) : ntok * ((cols / 32 + 7) / 8);

@@ -66,6 +66,8 @@ struct LayerRt {
     bool dense = false;
     bool fused = false;       // the attention half runs as one cooperative launch (attn_block.cu)
     Mat q_a, q_b, kv_a, kv_b;  // multi-head latent attention
+    Mat fg, fu, fd;            // dense FFN on the streamed matvec (dense_stream)
+    bool dense_stream = false;
     const float *q_a_norm = nullptr, *kv_a_norm = nullptr;
     AttnBlockArgs blk{};
 };
@@ -80,6 +82,8 @@ struct Model {
     size_t kvr = 0, qlora = 0, nope = 0, vd = 0, kd = 0;
     float *qa_lat = nullptr, *qa_n = nullptr, *kva = nullptr, *qabs = nullptr, *cacc = nullptr;
     float *mla_part = nullptr;  // split-position MLA attention records
+    float *dg = nullptr, *du = nullptr, *dact_f = nullptr;  // dense FFN: gate, up, SwiGLU rows
+    XQW dact{};                                              // ... and the quantized activation
     XQW l256{}, l32{}, c256{}, c32{};  // q_a output quantized for q_b; per-head compressed results for W_v
     Mat embd, out;
     const float *out_norm = nullptr;
@@ -192,6 +196,18 @@ int alloc_xq(Model &m, XQW &q, size_t cols, bool k256) {
     return dalloc(m, q.s, cols / (k256 ? 16 : 32) + 1);
 }
 
+// A dense FFN on the streamed matvec: normed x already quantized in m.n256;
+// xn = x + W_down . (silu(W_gate . x) * (W_up . x)).
+void dense_ffn_stream(Model &m, const LayerRt &l, const float *x, float *xn, cudaStream_t st) {
+    const int dim = (int)m.dim, f = (int)l.moe.ffn;
+    const XQ xq{m.n256.q, m.n256.d, m.n256.s, dim, dim / 256, dim / 16, 1};
+    launch_gemv_stream(l.fg.w, f, dim, xq, m.dg, st);
+    launch_gemv_stream(l.fu.w, f, dim, xq, m.du, st);
+    launch_swiglu(m.dg, m.du, f, m.dact_f, st);
+    launch_quant_act(m.dact_f, 1, f, f, 1, m.dact.q, m.dact.d, m.dact.s, f / 256, f / 16, st);
+    launch_gemv_stream(l.fd.w, dim, f, XQ{m.dact.q, m.dact.d, m.dact.s, f, f / 256, f / 16, 1}, xn, st, x);
+}
+
 // The step on device memory: token id at tok[0], position at pos[0].
 int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, uint32_t *next, cudaStream_t st) {
     const int dim = (int)m.dim, nh = (int)m.nh, nkv = (int)m.nkv, hd = (int)m.hd, qd = nh * hd;
@@ -247,9 +263,13 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
                                  st);
             }
             matvec(l.wo, m.att, m.a256, m.a32, m.proj, st);
-            launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, none, none, m.serial_norm, st);
+            launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, l.dense_stream ? m.n256 : none, none,
+                             m.serial_norm, st);
             float *xn = m.x[cur ^ 1];
-            if (int rc2 = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr, st))
+            if (l.dense_stream)
+                dense_ffn_stream(m, l, x, xn, st);
+            else if (int rc2 = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr,
+                                                     nullptr, st))
                 return rc2;
             cur ^= 1;
             continue;
@@ -260,6 +280,12 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
             a.pos = pos;
             MCK(launch_attn_block(a, st));
             float *xn = m.x[cur ^ 1];
+            if (l.dense_stream) {
+                launch_rmsnorm_q(x, nullptr, l.ffn_norm, dim, m.eps, m.normed, m.n256, none, m.serial_norm, st);
+                dense_ffn_stream(m, l, x, xn, st);
+                cur ^= 1;
+                continue;
+            }
             if (m.fold_ffn_norm) rt_moe_prenorm(l.ffn_norm, m.eps);  // the router kernel normalizes x itself
             if (int rc = loom_cuda_moe_forward(&l.moe, m.fold_ffn_norm ? x : m.normed, 1, xn, x,
                                                l.dense ? m.zero_logit : nullptr, nullptr, st))
@@ -287,9 +313,12 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
         }
         matvec(l.wo, m.att, m.a256, m.a32, m.proj, st);
         // x += proj (llama.zig:1195), then the FFN norm; the MoE layer quantizes normed itself
-        launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, none, none, m.serial_norm, st);
+        launch_rmsnorm_q(x, m.proj, l.ffn_norm, dim, m.eps, m.normed, l.dense_stream ? m.n256 : none, none,
+                         m.serial_norm, st);
         float *xn = m.x[cur ^ 1];
-        if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr, st))
+        if (l.dense_stream)
+            dense_ffn_stream(m, l, x, xn, st);
+        else if (int rc = loom_cuda_moe_forward(&l.moe, m.normed, 1, xn, x, l.dense ? m.zero_logit : nullptr, nullptr, st))
             return rc;
         cur ^= 1;
     }
@@ -400,7 +429,7 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
     bool ok = true;
     m->out_norm = f32_vec(d->output_norm, dim, ok);
     if (!ok) return bail(rt_decline("output_norm must be f32 [dim]"));
-    size_t max_ffn = 0, max_ne = 1, max_nu = 1;
+    size_t max_ffn = 0, max_ne = 1, max_nu = 1, max_dense = 0;
     for (size_t li = 0; li < d->n_layers; li++) {
         const loom_model_layer &s = d->layers[li];
         LayerRt l;
@@ -452,6 +481,14 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
             e.up = s.ffn_up;
             e.down = s.ffn_down;
             max_ffn = std::max(max_ffn, s.ffn);
+            // large dense FFNs (DeepSeek's first layers) on the streamed matvec: gate, up, SwiGLU, down + residual
+            if (!getenv("LOOM_CUDA_NO_GEMV_STREAM") && mat(s.ffn_gate, s.ffn, dim, l.fg) && mat(s.ffn_up, s.ffn, dim, l.fu) &&
+                mat(s.ffn_down, dim, s.ffn, l.fd) && act256(l.fg.type) && l.fg.type == l.fu.type &&
+                act256(l.fd.type) && gemv_stream_shape_ok(l.fg.type, (int)dim) &&
+                gemv_stream_shape_ok(l.fd.type, (int)s.ffn)) {
+                l.dense_stream = true;
+                max_dense = std::max(max_dense, s.ffn);
+            }
         }
         if (!m->mla) {
             need_kind(l.wq.type, m->need256, m->need32);
@@ -491,6 +528,9 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         (rc = alloc_xq(*m, m->a32, std::max(qd, hv), false)))
         return bail(rc);
     if ((rc = dalloc(*m, m->ab_bar, 64, true))) return bail(rc);
+    if (max_dense && ((rc = dalloc(*m, m->dg, max_dense)) || (rc = dalloc(*m, m->du, max_dense)) ||
+                      (rc = dalloc(*m, m->dact_f, max_dense)) || (rc = alloc_xq(*m, m->dact, max_dense, true))))
+        return bail(rc);
     if (m->mla && !m->ordered_attn && (rc = dalloc(*m, m->mla_part, mla_part_floats((int)m->nh, (int)m->kvr, (int)m->ctx))))
         return bail(rc);
     // The FFN RMSNorm moves into the MoE layer's router kernel (one grid barrier
