@@ -693,9 +693,14 @@ def run_model(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     B.init(local)
-    ds_main = args.model == "ds-v2-lite"
-    spec = (deepseek_v2_lite(n_layers=args.layers if args.layers != LAYERS_DEFAULT else 27, ctx_len=args.ctx)
-            if ds_main else qwen3_moe(n_layers=args.layers, ctx_len=args.ctx))
+    from loom_b200.model import deepseek_v3
+    ds_main = args.model in ("ds-v2-lite", "ds-v3")
+    if args.model == "ds-v2-lite":
+        spec = deepseek_v2_lite(n_layers=args.layers if args.layers != LAYERS_DEFAULT else 27, ctx_len=args.ctx)
+    elif args.model == "ds-v3":
+        spec = deepseek_v3(n_layers=args.v3_layers, ctx_len=args.ctx)
+    else:
+        spec = qwen3_moe(n_layers=args.layers, ctx_len=args.ctx)
     shard = D.expert_range(spec.n_expert, rank, world) if world > 1 else None
     if world > 1:
         D.ep_init(rank, world, dist)
@@ -774,7 +779,9 @@ def run_model(args):
     if not args.no_cpu and world == 1 and not ds_main:
         cpu = cpu_model_baseline(spec, pos)
     line = {
-        "metric": DS_METRIC if ds_main else MODEL_METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": (MODEL_METRIC if not ds_main else DS_METRIC if args.model == "ds-v2-lite" else
+                   f"decode tok/s (DeepSeek-V3-shaped model, first {spec.n_layers} of 61 layers at full width, Q4_K, "
+                   f"batch 1)"), "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "int8xq4/q6 matvecs (f32 accum), f32 attention and KV",
@@ -936,7 +943,7 @@ def main():
                     help="model: full Qwen3-30B-A3B decode (the headline); moe: the 48 MoE layers only")
     ap.add_argument("--ctx", type=int, default=2048, help="context length of the model workload")
     ap.add_argument("--no-moe-stack", action="store_true", help="model workload: skip the MoE-only sub-measurement")
-    ap.add_argument("--model", default="qwen3", choices=["qwen3", "ds-v2-lite"],
+    ap.add_argument("--model", default="qwen3", choices=["qwen3", "ds-v2-lite", "ds-v3"],
                     help="model workload: the headline Qwen3-30B-A3B shape, or the DeepSeek-V2-Lite shape (MLA)")
     ap.add_argument("--v3-layers", type=int, default=8,
                     help="model workload: layers of the DeepSeek-V3-shaped cut measured beside the headline (0: skip)")
