@@ -602,6 +602,9 @@ def run_e2e(args, B):
 
 MODEL_METRIC = "decode tok/s (Qwen3-30B-A3B full model, Q4_K_M, batch 1, ctx 2048)"
 DS_METRIC = "decode tok/s (DeepSeek-V2-Lite-shaped full model, Q4_K/Q8_0, batch 1)"
+# DRAM bytes of one headline step (48 layers + head at position 2047), from the
+# 4-layer ncu capture of profiles/model_step_qwen3_ctx2048_dram.md: 48 x 56.43 MB + 257.7 MB
+MODEL_TRAFFIC = 2966436352
 
 
 def model_bytes(spec, pos: int, n_local: int = None) -> int:
@@ -796,7 +799,11 @@ def run_model(args):
                    "l2": f"inputs > L2 ({bytes_step / 1e9:.2f} GB read per token)",
                    "kv_fill_s": round(fill_s, 2)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4),
+                     "traffic": MODEL_TRAFFIC if (args.model == "qwen3" and spec.n_layers == 48 and spec.ctx_len == 2048)
+                     else None,
+                     "traffic_note": "DRAM bytes per step from an ncu capture of 4 layers + head (caches flushed per "
+                                     "kernel, scaled to 48 layers): profiles/model_step_qwen3_ctx2048_dram.md",
                      "kernel": "whole decode step (all kernels of the token, CUDA-event timed)",
                      "peak_kind": peak_kind, "bytes_per_step": bytes_step},
         "e2e": {"value": round(1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
