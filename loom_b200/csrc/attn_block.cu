@@ -111,10 +111,6 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         for (int i = 0; i < AB_WARPS / AB_GRP_WARPS; i++) mbar_init_nf(&mbh[i], 1);
         for (int i = 0; i < 3; i++) mbar_init_nf(&mbm[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        // the residual row first: the norm waits for it
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        mbar_expect_tx(&mbm[2], (uint32_t)dim * 4);
-        bulk_g2s(sx, A.x, (uint32_t)dim * 4, &mbm[2]);
         const uint32_t bq = (uint32_t)((size_t)(qb - qa) * nbA * layout_qbytes(TA) + (size_t)(kb - ka) * nbA * layout_qbytes(TA) +
                                        (size_t)(kb - ka) * nbV * (layout_qbytes(TV) + (A.wv.sc ? 16 : 0)) +
                                        (size_t)(qb - qa + kb - ka) * nbA * (A.wq.sc ? 16 : 0));
@@ -122,6 +118,15 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         ab_stage_bulk(A.wq, qa, qb, nbA, const_cast<uint8_t *>(sq.q), const_cast<uint8_t *>(sq.sc), &mb[0]);
         ab_stage_bulk(A.wk, ka, kb, nbA, const_cast<uint8_t *>(sk.q), const_cast<uint8_t *>(sk.sc), &mb[0]);
         ab_stage_bulk(A.wv, ka, kb, nbV, const_cast<uint8_t *>(sv.q), const_cast<uint8_t *>(sv.sc), &mb[0]);
+    }
+    // The weights do not depend on the previous kernel: they were requested above, before
+    // the wait for it (programmatic dependent launch; a no-op when launched without it).
+    // The residual row does: requested after.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (tid == 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_expect_tx(&mbm[2], (uint32_t)dim * 4);
+        bulk_g2s(sx, A.x, (uint32_t)dim * 4, &mbm[2]);
     }
 
     // ---- P1: RMSNorm + quantization, then the q/k/v rows from shared memory ---------------
@@ -496,6 +501,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
                 A.x[oa + r0 + lane] = fadd(xres_ok ? xres[r0 + lane] : A.x[oa + r0 + lane], a);
         }
     }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (!A.normed) goto out;  // the MoE layer's router kernel applies the FFN norm itself
     if (!ab_barrier(ctr, base + (unsigned long long)G * ++nbar, err)) goto out;
     mark(5);
@@ -619,12 +625,24 @@ cudaError_t launch_attn_block(const AttnBlockArgs &A, cudaStream_t st) {
     cfg.blockDim = dim3(AB_THREADS);
     cfg.dynamicSmemBytes = A.smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    // with programmatic dependent launch the q/k/v weight copies overlap the previous kernel's
+    // tail; if the runtime refuses the combination, the launch is cooperative only
+    static int pdl_ok = getenv("LOOM_CUDA_NO_AB_PDL") ? 0 : 1;
     count_launch();
+    if (pdl_ok) {
+        cfg.numAttrs = 2;
+        e = cudaLaunchKernelEx(&cfg, fn, A);
+        if (e == cudaSuccess) return e;
+        cudaGetLastError();
+        pdl_ok = 0;
+    }
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, fn, A);
 }
 
