@@ -332,6 +332,9 @@ def run_gpu(args, emit=True):
         if args.batch_tokens > 0:
             batch = run_prefill(args, layers, stream, torch, D, T=args.batch_tokens,
                                 label=f"decode batch {args.batch_tokens} (one step of {args.batch_tokens} streams)")
+            btc = run_prefill(args, layers, stream, torch, D, T=args.batch_tokens, force_tc=True, with_exact=False,
+                              label="the same step forced onto the tensor-core kernels")
+            batch["tensor_cores"] = {k: btc[k] for k in ("workload", "value", "unit", "ms_per_step", "engine")}
     e2e_device = None
     if args.e2e_layers > 0 and not ep:
         e2e = run_e2e(args, B)
@@ -454,7 +457,7 @@ def trace_phases(D, step, stream, torch):
     }
 
 
-def run_prefill(args, layers, stream, torch, D, T=None, label="prefill"):
+def run_prefill(args, layers, stream, torch, D, T=None, label="prefill", force_tc=False, with_exact=True):
     """T tokens (default --prefill-tokens) through the same layers on the
     expert-major batch path, captured in one CUDA graph: a prefill (the
     experts average >= 16 tokens, so gate/up and down run as tcgen05 MMAs) or
@@ -473,24 +476,45 @@ def run_prefill(args, layers, stream, torch, D, T=None, label="prefill"):
             L.forward(cur, nxt, residual=cur, ids=ids[l], stream=sh, desc=descs[l])
             cur = nxt
 
-    with torch.cuda.stream(stream):
-        step(stream.cuda_stream)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        step(torch.cuda.current_stream().cuda_stream)
     steps = max(2, min(args.steps, 5))
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            g.replay()
+
+    def timed():
+        with torch.cuda.stream(stream):
+            step(stream.cuda_stream)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            g.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(torch.cuda.current_stream().cuda_stream)
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 3)):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps, D.last_path()
+
+    extra = {}
+    if force_tc:  # the tensor-core kernels at this T (below their automatic threshold)
+        prev = D.force_generic(3)
+        try:
+            ms, last = timed()
+        finally:
+            D.force_generic(prev)
+    else:
+        ms, last = timed()
+    if last == 3 and with_exact:  # the integer-exact tensor-core form beside the default fp16 one
+        prev = D.tc_exact(1)
+        try:
+            ms_x, _ = timed()
+        finally:
+            D.tc_exact(prev)
+        extra["integer_exact"] = {"value": round(T / (ms_x * 1e-3), 1), "unit": "tok/s", "ms_per_step": round(ms_x, 3),
+                                  "engine": "tcgen05 kind::f16 on integer sub-block products (bit-identical to "
+                                            "the CPU), per-super-block float tail"}
     ids_np = ids.cpu().numpy()
     bytes_step = sum(layer_bytes_model(ids_np[l].reshape(-1)) for l in range(LAYERS))
     flops = 2.0 * T * NK * 3 * DIM * FFN * LAYERS  # gate, up, down per routed token
@@ -500,15 +524,16 @@ def run_prefill(args, layers, stream, torch, D, T=None, label="prefill"):
     gbs = bytes_step / (ms * 1e-3) / 1e9
     tfs = flops / (ms * 1e-3) / 1e12
     path = {0: "fused decode kernels", 1: "slot kernels", 2: "per-expert int8 dot kernels",
-            3: "tcgen05 kind::f16 gate/up and down (integer-exact), warp-specialized",
-            4: "tiled dp4a gate/up and down (TMA-staged rows, integer-exact)"}.get(D.last_path(), "?")
+            3: "tcgen05 kind::f16 gate/up and down on dequantized fp16 tiles (f32 accumulation over the row, "
+               "within 2e-3 of the reference), warp-specialized",
+            4: "tiled dp4a gate/up and down (TMA-staged rows, integer-exact)"}.get(last, "?")
     return {"workload": label, "tokens": T, "layers": LAYERS, "value": round(T / (ms * 1e-3), 1), "unit": "tok/s",
             "ms_per_step": round(ms, 3), "steps": steps,
             "engine": "expert-major batch: tiled router GEMV, " + path,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "bytes_per_step": bytes_step,
                          "tensor_tflops": round(tfs, 2), "tensor_peak": tpeak,
-                         "tensor_frac": round(tfs / tpeak, 5)}}
+                         "tensor_frac": round(tfs / tpeak, 5)}, **extra}
 
 
 def run_e2e_device(args, g, stream, x0, out, torch, dist, world, job_tokens=None):

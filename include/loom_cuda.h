@@ -513,8 +513,18 @@ int loom_cuda_tensor_matmul(loom_tensor w, size_t rows, size_t cols, const float
  * expert-major batch kernels at any T, 3 the expert-major batch kernels on
  * the tensor cores at any T (Q4_K gate/up with Q6_K down, any scales;
  * other layers fall back to 2). Every family computes the same
- * numbers bit for bit. Returns the previous setting. */
+ * numbers bit for bit, except the tensor cores in their default
+ * dequantized form (loom_cuda_tc_exact). Returns the previous setting. */
 int loom_cuda_force_generic(int on);
+/* Arithmetic of the tensor-core expert kernels (batched prefill, no
+ * counterpart in the reference's seam; its tensor-core path is specified by
+ * tolerance): 0 (default) dequantized fp16 weight tiles (Q4_K (d sc) q -
+ * dmin m, Q6_K (d sc)(q - 32)) against the int8 activations of
+ * quantizeX256 dequantized to fp16, f32 accumulation over the whole row,
+ * within 2e-3 relative L2 of the reference; 1 the integer-exact kernels,
+ * bit-identical to the CPU (ggml.zig:1002-1021), slower. Returns the previous
+ * setting. */
+int loom_cuda_tc_exact(int on);
 /* Kernel family the last routed layer ran: 0 fused decode, 1 slot kernels,
  * 2 expert-major int8 batch kernels, 3 tensor cores; -1 before the first. */
 int loom_cuda_last_path(void);

@@ -130,6 +130,7 @@ def lib() -> C.CDLL:
         "loom_cuda_tensor_matmul": (i, [u64, sz, sz, vp, sz, vp, vp]),
         "loom_cuda_sync": (i, []),
         "loom_cuda_force_generic": (i, [i]),
+        "loom_cuda_tc_exact": (i, [i]),
         "loom_cuda_last_path": (i, []),
         "loom_cuda_device_error": (i, []),
         "loom_cuda_stack_prepare": (i, [vp, sz, C.POINTER(u64)]),

@@ -74,6 +74,7 @@ bool batch_supported(const DecodeArgs &A);
 enum { BATCH_GRP = 2, BATCH_MMA = 3, BATCH_DP4A = 4 };
 cudaError_t launch_batch(const DecodeArgs &A, int path, cudaStream_t st);
 bool moe_mma_supported(const DecodeArgs &A);
+extern int g_tc_exact;  // tensor-core arithmetic: 1 integer-exact, 0 dequantized fp16 (default)
 bool moe_dp4a_supported(const DecodeArgs &A);
 constexpr int MOE_DP_CH = 16;  // slots per dp4a tile
 cudaError_t launch_moe_dp4a(const DecodeArgs &A, cudaStream_t st,

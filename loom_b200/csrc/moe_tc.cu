@@ -130,6 +130,48 @@ __device__ __forceinline__ int tc_slot(const DecodeArgs &A, const TcTile &tl, in
     return tl.shared ? A.T * A.n_used + tl.c0 + i : A.grp_list[A.grp_off[tl.e] + tl.c0 + i];
 }
 
+// The tile tables (tc_pre, grp_cnt, grp_off) copied into shared memory at
+// kernel start: the per-tile lookups (a binary search over tc_pre, then the
+// group offset) would otherwise be chains of dependent global loads that stall
+// the warps at every tile boundary.
+struct TileTab {
+    const int *pre, *cnt, *off;
+};
+__host__ __device__ constexpr size_t tc_tab_bytes(int n_local) { return ((size_t)3 * (n_local + 3) * 4 + 15) & ~(size_t)15; }
+// every thread of the CTA; a __syncthreads() must follow before the first use
+__device__ __forceinline__ TileTab tc_tab_load(const DecodeArgs &A, int *buf) {
+    const int nexp = A.n_local + (A.has_shared ? 1 : 0), n = A.n_local + 3;
+    for (int i = threadIdx.x; i <= nexp; i += blockDim.x) buf[i] = A.tc_pre[i];
+    for (int i = threadIdx.x; i < A.n_local; i += blockDim.x) {
+        buf[n + i] = A.grp_cnt[i];
+        buf[2 * n + i] = A.grp_off[i];
+    }
+    return TileTab{buf, buf + n, buf + 2 * n};
+}
+__device__ __forceinline__ bool tc_tile(const DecodeArgs &A, const TileTab &tt, int RT, int t, TcTile &o,
+                                        int CH = TC_N) {
+    const int nexp = A.n_local + (A.has_shared ? 1 : 0);
+    const int *pre = tt.pre;
+    if (t >= pre[nexp] * RT) return false;
+    int lo = 0, hi = nexp;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (pre[mid] * RT <= t) lo = mid;
+        else hi = mid;
+    }
+    const int nch = pre[lo + 1] - pre[lo], loc = t - pre[lo] * RT;
+    o.e = lo;
+    o.shared = lo == A.n_local;
+    o.rt = loc / nch;
+    o.c0 = (loc % nch) * CH;
+    const int n = o.shared ? A.T : tt.cnt[lo];
+    o.nc = n - o.c0 < CH ? n - o.c0 : CH;
+    return true;
+}
+__device__ __forceinline__ int tc_slot(const DecodeArgs &A, const TileTab &tt, const TcTile &tl, int i) {
+    return tl.shared ? A.T * A.n_used + tl.c0 + i : A.grp_list[tt.off[tl.e] + tl.c0 + i];
+}
+
 __device__ __forceinline__ void tc_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -272,6 +314,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ TcBars B;
     uint8_t *raw = sm, *ops = sm + TC_RS * Ly::RAW, *hdr = ops + TC_OS * Ly::OP, *tok = hdr + TC_HS * Ly::HDR;
+    const TileTab TT = tc_tab_load(A, reinterpret_cast<int *>(sm + Ly::SMEM));
     const int R = FMT == 0 ? A.ffn : A.dim;  // weight rows
     const int RT = (R + 127) / 128;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -313,14 +356,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
         uint32_t gb = 0;
         TcTile tl;
         bool run = true;
-        for (int ti = blockIdx.x; run && tc_tile(A, RT, ti, tl); ti += gridDim.x) {
+        for (int ti = blockIdx.x; run && tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) {
             const int row0 = tl.rt * 128;
             const int8_t *src[2] = {nullptr, nullptr};  // this lane's token rows (i = lane, lane + 32), block 0
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const int i = lane + 32 * u;
                 if (i < tl.nc) {
-                    const int slot = tc_slot(A, tl, i);
+                    const int slot = tc_slot(A, TT, tl, i);
                     src[u] = FMT == 0 ? A.x256.q + (size_t)(tl.shared ? tl.c0 + i : slot / A.n_used) * dim
                                       : A.aq + (size_t)slot * stride;
                 }
@@ -369,13 +412,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
         int slot_cur = 0, slot_nxt = 0;
 #define TC_PF_LOAD(t, blk, slot) tc_pf_load<FMT, NB>(A, (t), (blk), (slot), ct, R, stride, pf_xd, pf_d, pf_s)
         TcTile tl, tn;
-        if (tc_tile(A, RT, blockIdx.x, tl)) {
-            if (ct < tl.nc) slot_cur = tc_slot(A, tl, ct);
+        if (tc_tile(A, TT, RT, blockIdx.x, tl)) {
+            if (ct < tl.nc) slot_cur = tc_slot(A, TT, tl, ct);
             TC_PF_LOAD(tl, 0, slot_cur);
         }
-        for (int ti = blockIdx.x; tc_tile(A, RT, ti, tl); ti += gridDim.x) {
-            const bool has_next = tc_tile(A, RT, ti + gridDim.x, tn);
-            if (has_next && ct < tn.nc) slot_nxt = tc_slot(A, tn, ct);
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) {
+            const bool has_next = tc_tile(A, TT, RT, ti + gridDim.x, tn);
+            if (has_next && ct < tn.nc) slot_nxt = tc_slot(A, TT, tn, ct);
             const int row0 = tl.rt * 128, rows = R - row0 < 128 ? R - row0 : 128;
             const int N = (tl.nc + 15) & ~15;
             bool run = true;
@@ -570,7 +613,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
         if (lane == 0) {
             uint32_t gb = 0, gq = 0;
             TcTile tl;
-            for (int ti = blockIdx.x; tc_ok(B) && tc_tile(A, RT, ti, tl); ti += gridDim.x) {
+            for (int ti = blockIdx.x; tc_ok(B) && tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) {
                 const int N = (tl.nc + 15) & ~15;
                 const uint32_t idesc = tc_idesc(128, N);
                 bool run = true;
@@ -614,11 +657,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
         const int qq = warp & 3, th = warp >> 2, r = 32 * qq + lane;
         uint32_t gb = 0;
         TcTile tl;
-        for (int ti = blockIdx.x; tc_tile(A, RT, ti, tl); ti += gridDim.x) {
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) {
             const int row0 = tl.rt * 128, rows = R - row0 < 128 ? R - row0 : 128;
             // lane l: the slot of this warp's l-th token, for the stores at the end of the tile
             const int my_ti = 8 * (2 * (lane >> 3) + th) + (lane & 7);
-            const int my_slot = my_ti < tl.nc ? tc_slot(A, tl, my_ti) : 0;
+            const int my_slot = my_ti < tl.nc ? tc_slot(A, TT, tl, my_ti) : 0;
             float acc[MATS][32];
 #pragma unroll
             for (int m = 0; m < MATS; m++)
@@ -732,8 +775,375 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_moe_tc(DecodeArgs A, const __
         tc_prof_add(B.prof, FMT, 12, clock64() - t_start);
         int nt = 0;
         TcTile tl;
-        for (int ti = blockIdx.x; tc_tile(A, RT, ti, tl); ti += gridDim.x) nt++;
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) nt++;
         tc_prof_add(B.prof, FMT, 13, nt);
+    }
+    if (warp == 0) tmem_free(tmem, Ly::TMEM_COLS);
+}
+
+// ==== down projection on dequantized fp16 tiles (the default) ============================
+// The north star's form of the batched expert FFN, for the down projection:
+// the Q6_K weights dequantized to fp16 values (d sc)(q - 32) (the f32 product
+// of dequantBlockQ6K, ggml.zig:1420, rounded once), the activations the
+// reference's int8 quantization of quantizeX256 (ggml.zig:776) dequantized to
+// fp16 (xd * q), one f32 TMEM accumulator per (row, token) over the whole row,
+// and no per-block epilogue: the epilogue runs once per tile. The result stays
+// within ~3e-4 relative L2 of the reference's integer arithmetic (fp16 keeps
+// 11 significant bits of every operand; the int8 activations are reproduced
+// exactly before the rounding). Gate/up keep the integer-exact kernel: their
+// output is re-quantized to int8 for down, where operand rounding would move
+// int8 roundings. loom_cuda_tc_exact(1) runs down integer-exact too.
+//
+// Same tiles, producer and bounded waits as k_moe_tc, with more converter
+// warps (the conversion is the kernel's critical path) and a deeper operand
+// ring:
+//   warps 0-3    epilogue: TMEM lane quarter = warp, every token of the tile
+//   warp 4       producer
+//   warp 5       MMA issuer (one accumulator per tile, two tile buffers)
+//   warps 6-21   converters: thread = (row, 16-value quarter) of the weight
+//                tile, (token, 8-value chunk) of the activation tile
+// Operand values are limited to the fp16 range (|x| < 65504).
+constexpr int TCF_EPI_WARPS = 4, TCF_PRO_WARP = 4, TCF_MMA_WARP = 5, TCF_CVT_WARP0 = 6, TCF_CVT_WARPS = 16;
+constexpr int TCF_THREADS = (TCF_CVT_WARP0 + TCF_CVT_WARPS) * 32;
+constexpr int TCF_OS = 4;
+constexpr uint32_t TCF_POLLS = 1u << 20;  // suspending polls of up to 4 us each
+constexpr int TCF_ACC = 4;  // accumulators per tile (one per K step of a sub-stage), summed by the epilogue
+struct TcfLayout {
+    static constexpr size_t RAW_W = (size_t)128 * 208, RAW_X = (size_t)TC_N * TC_XPITCH;
+    static constexpr size_t RAW = RAW_W + RAW_X;
+    static constexpr size_t OP_A = (size_t)8 * 128 * 16, OP = OP_A + (size_t)8 * TC_N * 16;
+    static constexpr size_t SMEM = TC_RS * RAW + TCF_OS * OP;
+    static constexpr uint32_t TMEM_COLS = 2 * TCF_ACC * TC_N;  // 2 tile buffers x TCF_ACC x TC_N
+};
+struct TcfBars {
+    uint64_t raw_full[TC_RS], raw_empty[TC_RS], op_full[TCF_OS], op_empty[TCF_OS];
+    uint64_t acc_full[2], acc_empty[2], drain;
+    uint32_t tmem;
+    int err;
+    int prof;
+};
+
+__device__ __forceinline__ uint32_t tcf_h2(float a) {  // f32 -> fp16 pair (a, a)
+    const __half h = __float2half_rn(a);
+    return tc_h2u(__halves2half2(h, h));
+}
+
+// bounded wait by one thread; a timeout raises the CTA's error flag (as tc_wait)
+__device__ __forceinline__ bool tcf_wait(TcfBars &B, uint64_t *bar, uint32_t parity, int *gerr, int slot = -1) {
+    if (*reinterpret_cast<volatile int *>(&B.err)) return false;
+    const long long c0 = B.prof ? clock64() : 0;
+    const bool ok = mbar_wait_hint(bar, parity, TCF_POLLS, 4000);
+    if (slot >= 0) tc_prof_add(B.prof, 1, slot, clock64() - c0);
+    if (ok) return true;
+    *reinterpret_cast<volatile int *>(&B.err) = 1;
+    if (gerr) atomicOr(gerr, 64);
+    return false;
+}
+
+// Power-of-two exponent E of a down-projection token: its largest block scale
+// xd times 127 lies in [2^(E-1), 2^E), so its operand values xd q 2^-E lie
+// below 1 in magnitude (far inside fp16's range); the epilogue multiplies by
+// 2^E, which is exact.
+template <int NB>
+__device__ __forceinline__ int tcf_exp_of(const float (&xd)[NB]) {
+    float m = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NB; b++) m = fmaxf(m, fabsf(xd[b]));
+    int e = 0;
+    if (m > 0.0f && m < 1e30f) frexpf(m * 127.0f, &e);
+    return max(-100, min(100, e));
+}
+template <int NB>
+__device__ __forceinline__ int tcf_tok_exp(const DecodeArgs &A, int slot) {
+    float xd[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) xd[b] = A.ad[(size_t)slot * (A.act_stride / 32) + b];
+    return tcf_exp_of<NB>(xd);
+}
+__device__ __forceinline__ float tcf_pow2(int e) { return __int_as_float((127 + e) << 23); }
+
+template <int NB>
+__global__ void __launch_bounds__(TCF_THREADS, 1) k_moe_tcf(DecodeArgs A, const __grid_constant__ TcMaps M) {
+    using Ly = TcfLayout;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    extern __shared__ __align__(1024) uint8_t sm[];
+    __shared__ TcfBars B;
+    uint8_t *raw = sm, *ops = sm + TC_RS * Ly::RAW;
+    const TileTab TT = tc_tab_load(A, reinterpret_cast<int *>(sm + Ly::SMEM));
+    const int R = A.dim;  // weight rows
+    const int RT = (R + 127) / 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    {
+        TcTile t0;
+        if (!tc_tile(A, RT, blockIdx.x, t0)) return;  // no work for this CTA
+    }
+    if (warp == 0) tmem_alloc(&B.tmem, Ly::TMEM_COLS);
+    if (tid == 0) {
+        for (int i = 0; i < TC_RS; i++) {
+            mbar_init(&B.raw_full[i], 1);
+            mbar_init(&B.raw_empty[i], TCF_CVT_WARPS);
+        }
+        for (int i = 0; i < TCF_OS; i++) {
+            mbar_init(&B.op_full[i], TCF_CVT_WARPS);
+            mbar_init(&B.op_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&B.acc_full[i], 1);
+            mbar_init(&B.acc_empty[i], TCF_EPI_WARPS);
+        }
+        mbar_init(&B.drain, 1);
+        B.err = 0;
+        B.prof = g_tc_prof_on && blockIdx.x == 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = B.tmem;
+    const int dim = A.dim, stride = A.act_stride;
+    const long long t_start = clock64();
+
+    if (warp == TCF_PRO_WARP) {
+        // ---- producer (as k_moe_tc) ------------------------------------------------------------
+        uint32_t gb = 0;
+        TcTile tl;
+        bool run = true;
+        for (int ti = blockIdx.x; run && tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) {
+            const int row0 = tl.rt * 128;
+            const int8_t *src[2] = {nullptr, nullptr};
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int i = lane + 32 * u;
+                if (i < tl.nc) src[u] = A.aq + (size_t)tc_slot(A, TT, tl, i) * stride;
+            }
+            for (int blk = 0; blk < NB; blk++, gb++) {
+                const int s = gb % TC_RS;
+                int ok = 1;
+                if (lane == 0) ok = gb >= TC_RS ? tcf_wait(B, &B.raw_empty[s], ((gb / TC_RS) - 1) & 1, A.err, 0) : 1;
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    run = false;
+                    break;
+                }
+                uint8_t *W = raw + (size_t)s * Ly::RAW, *X = W + Ly::RAW_W;
+                if (lane == 0) {
+                    mbar_expect_tx(&B.raw_full[s], (uint32_t)Ly::RAW_W + (uint32_t)tl.nc * 256);
+                    const int y = (tl.shared ? 0 : tl.e * R) + row0, m0 = tl.shared ? 2 : 0;
+                    tma_load_2d(W, &M.m[m0], blk * 192, y, &B.raw_full[s]);
+                    tma_load_2d(W + 128 * 192, &M.m[m0 + 1], blk * 16, y, &B.raw_full[s]);
+                }
+                __syncwarp();
+#pragma unroll
+                for (int u = 0; u < 2; u++)
+                    if (src[u]) bulk_g2s(X + (size_t)(lane + 32 * u) * TC_XPITCH, src[u] + blk * 256, 256, &B.raw_full[s]);
+            }
+        }
+        if (lane == 0 && !run)
+            for (uint32_t g = gb > TC_RS ? gb - TC_RS : 0; g < gb; g++)
+                mbar_wait(&B.raw_full[g % TC_RS], (g / TC_RS) & 1, TC_POLLS);
+    } else if (warp >= TCF_CVT_WARP0) {
+        // ---- converters: raw stage -> dequantized fp16 operand tiles ---------------------------
+        const int ct = tid - TCF_CVT_WARP0 * 32;
+        const int r = ct >> 2, j = ct & 3;          // weight row, 16-value quarter of the 64-value sub-stage
+        const int ti_tok = ct & 63, ch = ct >> 6;   // activation token, 8-value chunk
+        const int gp = j >> 1, hl = j & 1, c0 = 4 * gp + 2 * hl;
+        uint32_t gb = 0, gq = 0;
+        // read a block ahead: the converted token's scale xd and the row's f16 d
+        float pf_xd = 0.0f, pf_d = 0.0f;
+        int slot_cur = 0, slot_nxt = 0;  // the slot of token ti_tok in this / the next tile
+        float inv_cur = 1.0f;            // 2^-E of that token (tcf_tok_exp)
+        float nxd[NB];                   // the next tile's token: its block scales, loaded a tile ahead
+#pragma unroll
+        for (int b = 0; b < NB; b++) nxd[b] = 0.0f;
+        auto pf = [&](const TcTile &t, int blk, int slot) {
+            if (ti_tok < t.nc) pf_xd = A.ad[(size_t)slot * (stride / 32) + blk];
+            const WDev &w = t.shared ? A.sdn : A.dn;
+            const uint64_t pl = t.shared ? 0 : (uint64_t)t.e * R * NB;
+            const int rr = t.rt * 128 + r;
+            pf_d = rr < R ? f16_to_f32(w.d[pl + (uint64_t)rr * NB + blk]) : 0.0f;
+        };
+        TcTile tl, tn;
+        if (tc_tile(A, TT, RT, blockIdx.x, tl)) {
+            if (ti_tok < tl.nc) {
+                slot_cur = tc_slot(A, TT, tl, ti_tok);
+                inv_cur = tcf_pow2(-tcf_tok_exp<NB>(A, slot_cur));
+            }
+            pf(tl, 0, slot_cur);
+        }
+        const __half2 k1056 = tc_u2h(0x64206420u);  // 1024 + 32
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) {
+            const bool has_next = tc_tile(A, TT, RT, ti + gridDim.x, tn);
+            if (has_next && ti_tok < tn.nc) {
+                slot_nxt = tc_slot(A, TT, tn, ti_tok);
+#pragma unroll
+                for (int b = 0; b < NB; b++) nxd[b] = A.ad[(size_t)slot_nxt * (stride / 32) + b];
+            }
+            const int row0 = tl.rt * 128, rows = R - row0 < 128 ? R - row0 : 128;
+            const int N = (tl.nc + 15) & ~15;
+            bool run = true;
+            for (int blk = 0; blk < NB && run; blk++, gb++) {
+                const int s = gb % TC_RS;
+                int ok = 1;
+                if (lane == 0) ok = tcf_wait(B, &B.raw_full[s], (gb / TC_RS) & 1, A.err, ct == 0 ? 1 : -1);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    run = false;
+                    break;
+                }
+                const uint8_t *W = raw + (size_t)s * Ly::RAW, *X = W + Ly::RAW_W;
+                const float xd = pf_xd, dr = pf_d;
+                if (blk + 1 < NB) pf(tl, blk + 1, slot_cur);
+                else if (has_next) pf(tn, 0, slot_nxt);
+                const __half2 xd2 = tc_u2h(tcf_h2(fmul(xd, inv_cur)));
+                const uint8_t *wr = W + (size_t)r * 192;
+                const int8_t *scr = reinterpret_cast<const int8_t *>(W + 128 * 192 + (size_t)r * 16);
+                for (int q = 0; q < 4; q++, gq++) {
+                    const long long c_0 = clock64();
+                    const int os = gq % TCF_OS;
+                    const int h = q >> 1, p = q & 1, gg = 2 * p + gp;
+                    int ok2 = 1;
+                    if (lane == 0) ok2 = gq >= TCF_OS ? tcf_wait(B, &B.op_empty[os], ((gq / TCF_OS) - 1) & 1, A.err, ct == 0 ? 3 : -1) : 1;
+                    if (!__shfl_sync(0xffffffffu, ok2, 0)) {
+                        run = false;
+                        break;
+                    }
+                    uint4 l4 = make_uint4(0, 0, 0, 0), h4 = l4;
+                    int sc = 0;
+                    if (r < rows) {
+                        l4 = *reinterpret_cast<const uint4 *>(wr + 64 * h + 16 * j);
+                        h4 = *reinterpret_cast<const uint4 *>(wr + 128 + 32 * h + 16 * hl);
+                        sc = scr[8 * h + 2 * gg + hl];
+                    }
+                    uint2 xv = make_uint2(0, 0);
+                    if (ti_tok < tl.nc) xv = *reinterpret_cast<const uint2 *>(X + (size_t)ti_tok * TC_XPITCH + 64 * q + 8 * ch);
+                    uint8_t *O = ops + (size_t)os * Ly::OP;
+                    const long long c_1 = clock64();
+                    {   // weights: (d sc)(q - 32), the f32 product of dequantBlockQ6K rounded to fp16
+                        const __half2 S = tc_u2h(tcf_h2(fmul(dr, (float)sc)));
+                        const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+                        uint32_t o[8];
+#pragma unroll
+                        for (int w = 0; w < 4; w++) {
+                            const uint32_t lo4 = (p ? lw[w] >> 4 : lw[w]) & 0x0F0F0F0Fu;
+                            const uint32_t qb = lo4 | (((hw[w] >> (2 * gg)) & 0x03030303u) << 4);
+                            o[2 * w] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7170)), k1056), S));
+                            o[2 * w + 1] = tc_h2u(__hmul2(__hsub2(tc_u2h(__byte_perm(qb, 0x64646464u, 0x7372)), k1056), S));
+                        }
+                        *reinterpret_cast<uint4 *>(O + tc_sw(r, c0)) = make_uint4(o[0], o[1], o[2], o[3]);
+                        *reinterpret_cast<uint4 *>(O + tc_sw(r, c0 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                    const long long c_2 = clock64();
+                    if (ti_tok < N) {  // activations: xd * q of the int8 values, in fp16
+                        uint4 o = tc_h8(xv.x, xv.y);
+                        o = make_uint4(tc_h2u(__hmul2(tc_u2h(o.x), xd2)), tc_h2u(__hmul2(tc_u2h(o.y), xd2)),
+                                       tc_h2u(__hmul2(tc_u2h(o.z), xd2)), tc_h2u(__hmul2(tc_u2h(o.w), xd2)));
+                        *reinterpret_cast<uint4 *>(O + Ly::OP_A + tc_sw(ti_tok, ch)) = o;  // zero past nc
+                    }
+                    const long long c_3 = clock64();
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tc_arrive(&B.op_full[os]);
+                    if (ct == 0) {
+                        tc_prof_add(B.prof, 1, 17, c_1 - c_0);
+                        tc_prof_add(B.prof, 1, 14, c_2 - c_1);
+                        tc_prof_add(B.prof, 1, 15, c_3 - c_2);
+                        tc_prof_add(B.prof, 1, 18, clock64() - c_3);
+                    }
+                }
+                if (run) {
+                    __syncwarp();
+                    if (lane == 0) tc_arrive(&B.raw_empty[s]);
+                }
+            }
+            if (!run) break;
+            slot_cur = slot_nxt;
+            inv_cur = tcf_pow2(-tcf_exp_of<NB>(nxd));
+        }
+    } else if (warp == TCF_MMA_WARP) {
+        // ---- MMA issuer: one accumulator over the whole row, two tile buffers -------------------
+        if (lane == 0) {
+            uint32_t gt = 0, gq = 0;
+            TcTile tl;
+            bool run = true;
+            for (int ti = blockIdx.x; run && tc_tile(A, TT, RT, ti, tl); ti += gridDim.x, gt++) {
+                const int N = (tl.nc + 15) & ~15;
+                const uint32_t idesc = tc_idesc(128, N);
+                const int b = gt & 1;
+                if (gt >= 2 && !tcf_wait(B, &B.acc_empty[b], ((gt >> 1) - 1) & 1, A.err, 4)) break;
+                for (int blk = 0; blk < NB && run; blk++) {
+                    for (int q = 0; q < 4; q++, gq++) {
+                        const int os = gq % TCF_OS;
+                        if (!tcf_wait(B, &B.op_full[os], (gq / TCF_OS) & 1, A.err, 5)) {
+                            run = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint8_t *O = ops + (size_t)os * Ly::OP;
+                        const uint64_t ad = tc_desc_sw128(O), bd = tc_desc_sw128(O + Ly::OP_A);
+#pragma unroll
+                        for (int k = 0; k < 4; k++)  // four independent accumulators: no MMA waits on the previous
+                            umma_bf16(tmem + (uint32_t)(b * TCF_ACC + k) * TC_N, ad + (uint64_t)(2 * k),
+                                      bd + (uint64_t)(2 * k), idesc, (blk | q) != 0);
+                        umma_commit(&B.op_empty[os]);
+                    }
+                }
+                if (run) umma_commit(&B.acc_full[b]);
+            }
+            umma_commit(&B.drain);
+            mbar_wait(&B.drain, 0, TC_POLLS);
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue (warps 0-3): once per tile, every token -----------------------------------
+        const int r = 32 * warp + lane;
+        uint32_t gt = 0;
+        TcTile tl;
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl); ti += gridDim.x, gt++) {
+            const int row0 = tl.rt * 128, rows = R - row0 < 128 ? R - row0 : 128;
+            const int slot_a = lane < tl.nc ? tc_slot(A, TT, tl, lane) : 0;        // token lane
+            const int slot_b = lane + 32 < tl.nc ? tc_slot(A, TT, tl, lane + 32) : 0;  // token lane + 32
+            const float sc_a = lane < tl.nc ? tcf_pow2(tcf_tok_exp<NB>(A, slot_a)) : 1.0f;
+            const float sc_b = lane + 32 < tl.nc ? tcf_pow2(tcf_tok_exp<NB>(A, slot_b)) : 1.0f;
+            const int b = gt & 1;
+            int ok = 1;
+            if (lane == 0) ok = tcf_wait(B, &B.acc_full[b], (gt >> 1) & 1, A.err, tid == 0 ? 6 : -1);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            tc_fence_after();
+            for (int t0 = 0; t0 < tl.nc; t0 += 8) {  // warp-uniform
+                float v[8], w[8];
+                tmem_f8(tmem, warp, (uint32_t)(b * TCF_ACC) * TC_N + (uint32_t)t0, v);
+#pragma unroll
+                for (int c = 1; c < TCF_ACC; c++) {
+                    tmem_f8(tmem, warp, (uint32_t)(b * TCF_ACC + c) * TC_N + (uint32_t)t0, w);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = fadd(v[i], w[i]);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int t = t0 + i;
+                    const int slot = __shfl_sync(0xffffffffu, t < 32 ? slot_a : slot_b, t & 31);
+                    const float sc = __shfl_sync(0xffffffffu, t < 32 ? sc_a : sc_b, t & 31);
+                    if (t < tl.nc && r < rows) A.y[(size_t)slot * dim + row0 + r] = fmul(v[i], sc);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc_arrive(&B.acc_empty[b]);
+        }
+    }
+    {   // role spans: producer 8, converters 9, MMA 10, epilogue 11; whole CTA 12; tiles 13
+        const long long span = clock64() - t_start;
+        if (tid == TCF_PRO_WARP * 32) tc_prof_add(B.prof, 1, 8, span);
+        if (tid == TCF_CVT_WARP0 * 32) tc_prof_add(B.prof, 1, 9, span);
+        if (tid == TCF_MMA_WARP * 32) tc_prof_add(B.prof, 1, 10, span);
+        if (tid == 0) tc_prof_add(B.prof, 1, 11, span);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+        tc_prof_add(B.prof, 1, 12, clock64() - t_start);
+        int nt = 0;
+        TcTile tl;
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl); ti += gridDim.x) nt++;
+        tc_prof_add(B.prof, 1, 13, nt);
     }
     if (warp == 0) tmem_free(tmem, Ly::TMEM_COLS);
 }
@@ -778,6 +1188,15 @@ static TcFn tc_gu_fn(int nb) {
     }
     return nullptr;
 }
+static TcFn tcf_dn_fn(int nb) {
+    switch (nb) {
+        case 2: return k_moe_tcf<2>;
+        case 3: return k_moe_tcf<3>;
+        case 4: return k_moe_tcf<4>;
+        case 8: return k_moe_tcf<8>;
+    }
+    return nullptr;
+}
 static TcFn tc_dn_fn(int nb, bool split) {
     switch (nb) {
         case 2: return split ? k_moe_tc<2, 2> : k_moe_tc<1, 2>;
@@ -791,6 +1210,9 @@ static TcFn tc_dn_fn(int nb, bool split) {
 static bool tc_dn_split(const DecodeArgs &A) {
     return !(A.dn.pad_ & WDEV_Q6K_SMALL_SCALES) || (A.has_shared && !(A.sdn.pad_ & WDEV_Q6K_SMALL_SCALES));
 }
+
+// 1: the bit-exact integer kernels (k_moe_tc); 0: the dequantized fp16 kernels (k_moe_tcf)
+int g_tc_exact = 0;
 
 bool moe_mma_supported(const DecodeArgs &A) {
     if (A.g.type != T_Q4_K || A.u.type != T_Q4_K || A.dn.type != T_Q6_K) return false;
@@ -813,8 +1235,11 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
         if (n_sm <= 0) n_sm = 148;
     }
-    const bool split = tc_dn_split(A);
-    TcFn gf = tc_gu_fn(A.dim / 256), df = tc_dn_fn(A.ffn / 256, split);
+    // gate/up stay integer-exact in every mode: their output is re-quantized to int8 for down, and
+    // fp16 operand rounding there moves int8 roundings (one moved step is ~1e-3 of the layer output)
+    const bool split = tc_dn_split(A), exact = g_tc_exact != 0;
+    TcFn gf = tc_gu_fn(A.dim / 256);
+    TcFn df = exact ? tc_dn_fn(A.ffn / 256, split) : tcf_dn_fn(A.ffn / 256);
     const int nbg = A.dim / 256, nbd = A.ffn / 256;
     TcMaps mg, md;
     memset(&mg, 0, sizeof mg);
@@ -828,8 +1253,8 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
              tc_map(md.m[2], A.sdn.q, nbd * 192ull, (uint64_t)A.dim, 192) &&
              tc_map(md.m[3], A.sdn.sc, nbd * 16ull, (uint64_t)A.dim, 16);
     if (!ok) return cudaErrorInvalidValue;
-    constexpr size_t gs = TcLayout<0>::SMEM;
-    const size_t ds = split ? TcLayout<2>::SMEM : TcLayout<1>::SMEM;
+    const size_t gs = TcLayout<0>::SMEM + tc_tab_bytes(A.n_local);
+    const size_t ds = (!exact ? TcfLayout::SMEM : split ? TcLayout<2>::SMEM : TcLayout<1>::SMEM) + tc_tab_bytes(A.n_local);
     cudaError_t e = cudaFuncSetAttribute(gf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(df, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ds);
     if (e != cudaSuccess) return e;
@@ -838,7 +1263,7 @@ cudaError_t launch_moe_mma(const DecodeArgs &A, cudaStream_t st, cudaError_t (*q
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = quant(A, st)) != cudaSuccess) return e;
     count_launch();
-    df<<<n_sm, TC_THREADS, ds, st>>>(A, md);
+    df<<<n_sm, exact ? TC_THREADS : TCF_THREADS, ds, st>>>(A, md);
     return cudaGetLastError();
 }
 
@@ -870,6 +1295,13 @@ int q6k_max_scale(const uint8_t *sc, uint64_t nblk, int *d_tmp, cudaStream_t st)
 using namespace loom;
 
 extern "C" int loom_cuda_tc_profile(int enable, unsigned long long *out, size_t n);
+extern "C" int loom_cuda_tc_exact(int on);
+
+int loom_cuda_tc_exact(int on) {
+    const int prev = g_tc_exact;
+    g_tc_exact = on ? 1 : 0;
+    return prev;
+}
 
 // Diagnostic entry (no counterpart in the reference): enable (1) / disable (0)
 // the tensor-core kernels' cycle profile of CTA 0, zeroing it; then (any

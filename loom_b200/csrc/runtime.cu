@@ -1063,7 +1063,7 @@ int loom_cuda_moe_ffn_routed(const float *normed, size_t dim, const float *logit
                                        base(d), base(sh[0]), base(sh[1]), base(sh[2]), dim, ffn, shexp_ffn,
                                        cfg.n_expert, cfg.n_used, (uint64_t)cfg.gating_sigmoid,
                                        (uint64_t)cfg.weights_norm, fbits(cfg.weights_scale), bias ? 1u : 0u,
-                                       (uint64_t)g_force_generic};
+                                       (uint64_t)g_force_generic | (uint64_t)g_tc_exact << 8};
     if (int rc = seam_run(key, [&]() -> int {
             CK(cudaMemcpyAsync(S.io_in.p, S.h_in.p, in_b, cudaMemcpyHostToDevice, g_stream));
             const float *dx = S.io_in.as<float>();

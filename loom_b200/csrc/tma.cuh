@@ -45,6 +45,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     return false;
 }
 
+// As mbar_wait, with a suspend-time hint: a waiting thread sleeps until the
+// phase completes or about `ns` nanoseconds pass, instead of re-polling (a
+// polling warp takes issue slots from the warps doing the work).
+__device__ __forceinline__ bool mbar_wait_hint(uint64_t *bar, uint32_t parity, uint32_t max_polls, uint32_t ns) {
+    for (uint32_t i = 0; i < max_polls; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // Wait for phase `parity` with non-blocking tests (mbarrier.test_wait) and a
 // short sleep between them: for barriers several warps wait on at once, where
 // a suspended try_wait may not be woken promptly. Gives up after `max_polls`.

@@ -211,8 +211,14 @@ def tensor_matmul(w: DeviceTensor, rows: int, cols: int, xs, out, stream=None) -
 
 def force_generic(mode) -> int:
     """Kernel family for MoE layers: 0 automatic, 1 (True) slot kernels, 2 expert-major batch kernels
-    (int8 dots), 3 expert-major batch kernels on the tensor cores (integer-exact tcgen05 MMAs)."""
+    (int8 dots), 3 expert-major batch kernels on the tensor cores (tcgen05 MMAs; see tc_exact)."""
     return int(_lib.lib().loom_cuda_force_generic(int(mode)))
+
+
+def tc_exact(on) -> int:
+    """Tensor-core expert kernels: 0 (default) dequantized fp16 tiles, within 2e-3 relative L2 of the
+    reference; 1 integer-exact tiles, bit-identical to the CPU. Returns the previous setting."""
+    return int(_lib.lib().loom_cuda_tc_exact(int(on)))
 
 
 def last_path() -> int:

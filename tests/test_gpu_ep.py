@@ -60,10 +60,12 @@ def test_a2a_single_rank_bitexact(be, orc, cfg, T, mode, cap):
     gids = torch.zeros((T, k), dtype=torch.int32, device="cuda")
     from loom_b200 import device as D
     prev = D.force_generic(mode)  # how the arriving rows run: batch / slot kernels / tensor cores
+    prev_x = D.tc_exact(1)  # the integer-exact tensor-core form: bit-comparable
     try:
         L.forward_a2a(x, got, residual=res, ids=gids, t_cap=0 if cap == 0 else max(T, 1) + (cap - 1))
     finally:
         D.force_generic(prev)
+        D.tc_exact(prev_x)
     torch.cuda.synchronize()
     assert np.array_equal(gids.cpu().numpy(), wids.cpu().numpy())
     assert np.array_equal(bits(got.cpu().numpy()), bits(want.cpu().numpy()))
