@@ -19,8 +19,8 @@
 // share weights, which stay in L2), and CTA c takes tiles c, c + grid, ...
 //
 // Roles of one CTA (576 threads, one CTA per SM):
-//   warp 8       producer: per super-block, one 2D tensor copy (TMA, no
-//                multicast) of the tile's 128 raw weight rows per matrix and
+//   warp 8       producer: per super-block, one 2D tensor copy (TMA, into
+//                this CTA only) of the tile's 128 raw weight rows per matrix and
 //                one bulk copy per token row into a 2-stage ring, completion by
 //                mbarrier transaction count
 //   warps 10-17  converters: raw stage -> fp16 operand tiles (K = 64 per
