@@ -1361,6 +1361,7 @@ __global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const 
     __shared__ DpBars B;
     uint8_t *raw = sm, *tokb = sm + DP_RS * Ly::RAW;
     float *xchg = reinterpret_cast<float *>(tokb + DP_RS * Ly::TOK);
+    const TileTab TT = tc_tab_load(A, reinterpret_cast<int *>(sm + Ly::SMEM));
     const int R = FMT == 0 ? A.ffn : A.dim, RT = (R + 127) / 128;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int dim = A.dim, stride = A.act_stride;
@@ -1393,11 +1394,11 @@ __global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const 
         uint32_t gb = 0;
         bool run = true;
         TcTile tl;
-        for (int ti = blockIdx.x; run && tc_tile(A, RT, ti, tl, DP_CH); ti += gridDim.x) {
+        for (int ti = blockIdx.x; run && tc_tile(A, TT, RT, ti, tl, DP_CH); ti += gridDim.x) {
             const int row0 = tl.rt * 128;
             const int8_t *src = nullptr;  // this lane's token row (i = lane)
             if (lane < tl.nc) {
-                const int slot = tc_slot(A, tl, lane);
+                const int slot = tc_slot(A, TT, tl, lane);
                 src = FMT == 0 ? A.x256.q + (size_t)(tl.shared ? tl.c0 + lane : slot / A.n_used) * dim
                                : A.aq + (size_t)slot * stride;
             }
@@ -1431,10 +1432,10 @@ __global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const 
         const int r = tid & 127, hi = tid >> 7;  // FMT 0: hi = matrix; FMT 1: hi = token half
         uint32_t gb = 0;
         TcTile tl;
-        for (int ti = blockIdx.x; tc_tile(A, RT, ti, tl, DP_CH); ti += gridDim.x) {
+        for (int ti = blockIdx.x; tc_tile(A, TT, RT, ti, tl, DP_CH); ti += gridDim.x) {
             const int row0 = tl.rt * 128, rows = R - row0 < 128 ? R - row0 : 128;
             // this thread's token (tid < nc): its slot, for the per-block scalars and the stores
-            const int my_slot = tid < tl.nc ? tc_slot(A, tl, tid) : 0;
+            const int my_slot = tid < tl.nc ? tc_slot(A, TT, tl, tid) : 0;
             const size_t my_tok = tl.shared ? (size_t)(tl.c0 + tid) : (size_t)(my_slot / A.n_used);
             float acc[FMT == 0 ? 1 : DP_CH / 2];  // down: in registers; gate/up: in shared memory (xchg)
 #pragma unroll
@@ -1607,7 +1608,7 @@ __global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const 
 #pragma unroll
                     for (int i = 0; i < DP_CH; i++) {
                         if (i >= tl.nc) break;
-                        const int slot = tc_slot(A, tl, i);
+                        const int slot = tc_slot(A, TT, tl, i);
                         const float g = xchg[i * 256 + r], u = xchg[i * 256 + 128 + r];
                         A.act[(size_t)slot * stride + row0 + r] = fmul(fdiv(g, fadd(1.0f, exp_f(-g))), u);
                     }
@@ -1617,7 +1618,7 @@ __global__ void __launch_bounds__(DP_THREADS, 2) k_moe_dp4a(DecodeArgs A, const 
                 for (int k = 0; k < DP_CH / 2; k++) {
                     const int i = DP_CH / 2 * hi + k;
                     if (i >= tl.nc) break;
-                    A.y[(size_t)tc_slot(A, tl, i) * dim + row0 + r] = acc[k];
+                    A.y[(size_t)tc_slot(A, TT, tl, i) * dim + row0 + r] = acc[k];
                 }
             }
         }
@@ -1677,7 +1678,7 @@ cudaError_t launch_moe_dp4a(const DecodeArgs &A, cudaStream_t st, cudaError_t (*
              tc_map(md.m[2], A.sdn.q, nbd * 192ull, (uint64_t)A.dim, 192) &&
              tc_map(md.m[3], A.sdn.sc, nbd * 16ull, (uint64_t)A.dim, 16);
     if (!ok) return cudaErrorInvalidValue;
-    constexpr size_t gs = DpLayout<0>::SMEM, ds = DpLayout<1>::SMEM;
+    const size_t gs = DpLayout<0>::SMEM + tc_tab_bytes(A.n_local), ds = DpLayout<1>::SMEM + tc_tab_bytes(A.n_local);
     cudaError_t e = cudaFuncSetAttribute(gf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(df, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ds);
     if (e != cudaSuccess) return e;
