@@ -35,6 +35,10 @@ namespace loom {
 
 namespace {
 
+#ifndef AB_HEAD_COMPACT
+#define AB_HEAD_COMPACT 1
+#endif
+
 template <int TA, int TV, int TO, int SO>
 __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     extern __shared__ __align__(128) uint8_t ab_smem[];
@@ -42,6 +46,7 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     __shared__ float Ls[40];
     __shared__ __align__(8) uint64_t mb[2];  // staged q/k/v rows, staged output-projection rows
     __shared__ __align__(8) uint64_t mbh[AB_WARPS / AB_GRP_WARPS];  // per attention group: its head rows
+    __shared__ __align__(8) uint64_t mbkv[AB_WARPS / AB_GRP_WARPS];  // per attention group: its cache rows
     __shared__ __align__(8) uint64_t mbm[3];  // merge records; output-projection input; the residual row
     __shared__ float tsm_all[AB_WARPS][64];  // per-warp unit terms of ab_rows (<= 4 rows x 16 blocks)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -108,7 +113,10 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
     if (tid == 0) {  // every weight byte of the layer this CTA needs, in flight at once
         mbar_init_nf(&mb[0], 1);
         mbar_init_nf(&mb[1], 1);
-        for (int i = 0; i < AB_WARPS / AB_GRP_WARPS; i++) mbar_init_nf(&mbh[i], 1);
+        for (int i = 0; i < AB_WARPS / AB_GRP_WARPS; i++) {
+            mbar_init_nf(&mbh[i], 1);
+            mbar_init_nf(&mbkv[i], 1);
+        }
         for (int i = 0; i < 3; i++) mbar_init_nf(&mbm[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         const uint32_t bq = (uint32_t)((size_t)(qb - qa) * nbA * layout_qbytes(TA) + (size_t)(kb - ka) * nbA * layout_qbytes(TA) +
@@ -202,7 +210,8 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
         if (grp < ngrp) {
             float *sK = att_sm + grp * per, *sV = sK + ATT_CH * KS, *qs = sV + ATT_CH * hd, *sc = qs + GQ * hd;
             float *gqs = sc + GQ * ATT_CH, *gks = gqs + hd, *css = gks + hd;  // head-norm weights, (cos, sin) pairs
-            uint32_t hph = 0;  // phase of this group's head-row barrier
+            uint32_t hph = 0;  // phase of this group's head-row and cache-row barriers
+            const bool kv_bulk = hd % 4 == 0;  // 16-byte rows: one bulk copy per cache row
             for (int it = c * ngrp + grp; it < items; it += G * ngrp) {
                 const int g = it / live, sp = it % live;
                 const int t0 = sp * ATT_CH, n = min(ATT_CH, pos + 1 - t0);
@@ -238,17 +247,30 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
                 if ((A.rope_dim * 4) % 16 != 0)
                     for (int i = gl; i < A.rope_dim; i += AB_GRP_WARPS * 32) css[i] = __ldg(A.rope + (size_t)pos * A.rope_dim + i);
                 if (!mbar_wait(&mbh[grp], hph & 1, STAGE_POLLS_AB) && lane == 0) atomicOr(err, 2u);
-                hph++;
                 if (grp == 0) mark(28);
                 asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
-                for (int i = gl; i < nold * q4; i += AB_GRP_WARPS * 32) {
-                    const int j = i / q4, c4 = (i % q4) * 4;
-                    ab_cp16(sK + j * KS + c4, kb + (size_t)j * kvd + c4);
-                    ab_cp16(sV + j * hd + c4, vb + (size_t)j * kvd + c4);
+                if (kv_bulk) {
+                    // the cache rows by the copy engine (two requests per position): the head
+                    // preparation's shared-memory traffic does not queue behind them
+                    // (spread over the group's lanes: each issues at most a few, so no warp's own
+                    // head preparation waits long behind the issue)
+                    if (gl == 0) mbar_expect_tx(&mbkv[grp], (uint32_t)nold * 2 * hd * 4);
+                    asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
+                    for (int i = gl; i < 2 * nold; i += AB_GRP_WARPS * 32) {
+                        const int j = i >> 1;
+                        if (i & 1) bulk_g2s(sV + j * hd, vb + (size_t)j * kvd, (uint32_t)hd * 4, &mbkv[grp]);
+                        else bulk_g2s(sK + j * KS, kb + (size_t)j * kvd, (uint32_t)hd * 4, &mbkv[grp]);
+                    }
+                } else {
+                    for (int i = gl; i < nold * q4; i += AB_GRP_WARPS * 32) {
+                        const int j = i / q4, c4 = (i % q4) * 4;
+                        ab_cp16(sK + j * KS + c4, kb + (size_t)j * kvd + c4);
+                        ab_cp16(sV + j * hd + c4, vb + (size_t)j * kvd + c4);
+                    }
+                    asm volatile("cp.async.commit_group;\n" ::: "memory");
                 }
-                asm volatile("cp.async.commit_group;\n" ::: "memory");
                 if (grp == 0) mark(12);
-                if (A.serial) {
+                if (A.serial || AB_HEAD_COMPACT) {
                     for (int hh = gwarp; hh < nhp; hh += AB_GRP_WARPS) {
                         const bool isq = hh < GQ, isk = hh == GQ;
                         float *v = isq ? qs + hh * hd : isk ? sK + (n - 1) * KS : sV + (n - 1) * hd;
@@ -311,7 +333,12 @@ __global__ void __launch_bounds__(AB_THREADS, 1) k_attn_block(AttnBlockArgs A) {
                     }
                 }
                 if (grp == 0) mark(13);
-                asm volatile("cp.async.wait_all;\n" ::: "memory");
+                if (kv_bulk) {
+                    if (!mbar_wait(&mbkv[grp], hph & 1, STAGE_POLLS_AB) && lane == 0) atomicOr(err, 2u);
+                } else {
+                    asm volatile("cp.async.wait_all;\n" ::: "memory");
+                }
+                hph++;
                 asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(AB_GRP_WARPS * 32) : "memory");
                 if (grp == 0) mark(14);
                 const int HP = (GQ + 1) / 2;
