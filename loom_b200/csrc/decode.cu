@@ -165,13 +165,37 @@ __device__ __forceinline__ bool row_unused(const int *ids, int n) {
     return true;
 }
 
+// x quantization of token t's row smx into the format(s) the expert types read, 256-value blocks
+// b0, b0 + step, ... (and the 32-value groups likewise) by one warp each (warp index wi of nwq)
+__device__ __forceinline__ void quant_x_rows(const DecodeArgs &A, int t, const float *smx, int b0, int step, int wi,
+                                             int nwq, int lane) {
+    const int dim = A.dim;
+    if (A.need256)
+        for (int b = b0 + step * wi; b < dim / 256; b += step * nwq)
+            quant_lane8(smx + b * 256 + lane * 8, true, 32, A.x256.q + (size_t)t * dim + b * 256 + lane * 8,
+                        A.x256.d + (size_t)t * (dim / 256) + b, A.x256.s + (size_t)t * (dim / 16) + b * 16 + lane / 2,
+                        nullptr, lane);
+    if (A.need32) {
+        const int nb = dim / 32, ng = (nb + 7) / 8;
+        for (int g = b0 + step * wi; g < ng; g += step * nwq) {
+            const int b = g * 8 + lane / 4;
+            const int off = b * 32 + (lane & 3) * 8;
+            quant_lane8(smx + off, b < nb, 4, A.x32.q + (size_t)t * dim + off, A.x32.d + (size_t)t * (dim / 32) + b,
+                        nullptr, A.x32.s + (size_t)t * (dim / 32) + b, lane);
+        }
+    }
+}
+
+// quant: also quantize x here (false when the cluster's CTAs quantized it already)
 __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const float *smx, float *scores, float *choice,
-                                            int nw) {
+                                            int nw, bool quant = true) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int dim = A.dim, ne = A.n_expert;
     int *sid = reinterpret_cast<int *>(choice + ne);
     float *sg = choice + ne + 64;
     float *red = choice + ne + 128;
+    // the route by one warp (logits in registers) where the layer allows, else by ROUTE_THREADS threads
+    const bool wroute = !A.ids_in && (A.n_group <= 1 || A.topk_group >= A.n_group) && ne <= 32 * RW_MAX;
     if (threadIdx.x < ROUTE_THREADS && A.ids_in) {  // rows routed elsewhere: take their experts and gates
         for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS) {
             const size_t i = (size_t)t * A.n_used + k;
@@ -179,33 +203,37 @@ __device__ __forceinline__ void router_tail(const DecodeArgs &A, int t, const fl
             A.gates[i] = A.gates_in ? A.gates_in[i] : 1.0f;
             if (A.ids_out) A.ids_out[i] = A.ids_in[i];
         }
-    } else if (threadIdx.x < ROUTE_THREADS) {
-        route_block(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid, sg,
-                    red, A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, A.n_group, A.topk_group);
-        if (A.ids_out)
-            for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS)
-                A.ids_out[(size_t)t * A.n_used + k] = sid[k];
+    } else if (wroute ? warp == 0 : threadIdx.x < ROUTE_THREADS) {
+        if (wroute) {
+            // one warp on logits in registers (the stack kernel's route; same order, same results);
+            // the CTA's other warps quantize meanwhile
+            if (ne <= 128)
+                route_warp_regs<false, 4>(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale,
+                                          scores, choice, sid, sg, A.ids + (size_t)t * A.n_used,
+                                          A.gates + (size_t)t * A.n_used, lane);
+            else
+                route_warp_regs<false, RW_MAX>(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm,
+                                               A.weights_scale, scores, choice, sid, sg,
+                                               A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, lane);
+            __syncwarp();
+            if (A.ids_out)
+                for (int k = lane; k < A.n_used; k += 32) A.ids_out[(size_t)t * A.n_used + k] = sid[k];
+        } else {
+            route_block(choice, A.bias, ne, A.n_used, A.gating, A.weights_norm, A.weights_scale, scores, choice, sid,
+                        sg, red, A.ids + (size_t)t * A.n_used, A.gates + (size_t)t * A.n_used, A.n_group, A.topk_group);
+            if (A.ids_out)
+                for (int k = threadIdx.x; k < A.n_used; k += ROUTE_THREADS)
+                    A.ids_out[(size_t)t * A.n_used + k] = sid[k];
+        }
         if (A.trace && threadIdx.x == 0) atomicMin(A.trace + 2 * (A.trace_slot + 6), gtimer());
-    } else if (!(A.ids_in && row_unused(A.ids_in + (size_t)t * A.n_used, A.n_used))) {
+    } else if (quant && !(A.ids_in && row_unused(A.ids_in + (size_t)t * A.n_used, A.n_used))) {
         // quantize x in the format(s) the expert types read (not for the unused
         // entries of a fixed-capacity exchange: expert -1, no expert reads them)
-        const int nwq = nw - ROUTE_THREADS / 32, wi = warp - ROUTE_THREADS / 32;
-        if (A.need256)
-            for (int b = wi; b < dim / 256; b += nwq)
-                quant_lane8(smx + b * 256 + lane * 8, true, 32, A.x256.q + (size_t)t * dim + b * 256 + lane * 8,
-                            A.x256.d + (size_t)t * (dim / 256) + b,
-                            A.x256.s + (size_t)t * (dim / 16) + b * 16 + lane / 2, nullptr, lane);
-        if (A.need32) {
-            const int nb = dim / 32, ng = (nb + 7) / 8;
-            for (int g = wi; g < ng; g += nwq) {
-                const int b = g * 8 + lane / 4;
-                const int off = b * 32 + (lane & 3) * 8;
-                quant_lane8(smx + off, b < nb, 4, A.x32.q + (size_t)t * dim + off, A.x32.d + (size_t)t * (dim / 32) + b,
-                            nullptr, A.x32.s + (size_t)t * (dim / 32) + b, lane);
-            }
-        }
+        const int nrw = wroute ? 1 : ROUTE_THREADS / 32;  // warps routing
+        quant_x_rows(A, t, smx, 0, 1, warp - nrw, nw - nrw, lane);
         if (A.trace && lane == 0) atomicMax(A.trace + 2 * (A.trace_slot + 6) + 1, gtimer());
     }
+    (void)dim;
 }
 
 __global__ void __launch_bounds__(RR_WARPS * 32) k_router_route(DecodeArgs A) {
@@ -332,9 +360,19 @@ __global__ void __launch_bounds__(RR2_WARPS * 32) k_router_tma(DecodeArgs A) {
         atomicMax(A.trace + 2 * (A.trace_slot + 7), (unsigned long long)(c1 - c0));
         atomicMax(A.trace + 2 * (A.trace_slot + 7) + 1, (unsigned long long)(c2 - c1));
     }
-    if (rank != 0) return;
+    if (rank != 0) {
+        // the x quantization, split over the cluster's other CTAs (each holds the normalized row):
+        // block b by CTA 1 + b % (ncl - 1), one warp a block, while CTA 0 routes
+        if (ncl > 1 && !(A.ids_in && row_unused(A.ids_in + (size_t)t * A.n_used, A.n_used))) {
+            quant_x_rows(A, t, smx, (int)rank - 1, ncl - 1, warp, RR2_WARPS, lane);
+            if (A.trace && lane == 0) atomicMax(A.trace + 2 * (A.trace_slot + 6) + 1, gtimer());
+        }
+        __syncthreads();
+        pdl_trigger();
+        return;
+    }
     const long long c3 = clock64();
-    router_tail(A, t, smx, scores, choice, RR2_WARPS);
+    router_tail(A, t, smx, scores, choice, RR2_WARPS, ncl == 1);
     if (A.trace && threadIdx.x == 0) atomicMax(A.trace + 2 * (A.trace_slot + 8) + 1, (unsigned long long)(clock64() - c3));
     __syncthreads();
     pdl_trigger();  // late: the expert kernel's CTAs would only wait on this SM's issue slots
