@@ -395,6 +395,17 @@ int loom_cuda_model_step(uint64_t handle, const uint32_t *d_token, const uint32_
  * device->host copy of the greedy token (and of the logits when logits !=
  * NULL), then a wait for completion. */
 int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *logits, uint32_t *next);
+/* Batched prefill (llama.zig:1698-1825 stepBatch): the n host token ids at
+ * positions pos_base .. pos_base + n - 1 through every layer, each layer over
+ * all n rows before the next (matmuls bit-identical to per-token matvecs,
+ * each token attending causally to cache rows 0..its position in the
+ * reference's order, the FFN on the expert-major batch path), their K/V rows
+ * appended to the cache; then the last token's logits (host, vocab f32, or
+ * NULL) and greedy next token (or NULL). Synchronous. Declines MLA models and
+ * positions beyond the context; allocates its row buffers on first use of a
+ * larger n (not for use inside a stream capture). */
+int loom_cuda_model_prefill(uint64_t handle, const uint32_t *tokens, size_t n, size_t pos_base, float *logits,
+                            uint32_t *next);
 /* Copy one cache row (layer, pos) of keys and values (n_kv*hd f32 each; with
  * MLA the compressed row, kv_lora f32, and the rope row, rope_dim f32) to the
  * host -- the read-back that keeps a host copy authoritative (mlaReadCache,

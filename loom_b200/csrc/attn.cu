@@ -61,6 +61,22 @@ __global__ void __launch_bounds__(RN_THREADS) k_rmsnorm_q(float *x, const float 
     extern __shared__ float sx[];  // [dim]
     __shared__ float red[RN_THREADS / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (blockIdx.y) {  // row blockIdx.y of a batch: every vector advances by its row
+        const size_t y = blockIdx.y;
+        x += y * dim;
+        if (add) add += y * dim;
+        normed += y * dim;
+        if (q256.q) {
+            q256.q += y * dim;
+            q256.d += y * (dim / 256);
+            q256.s += y * (dim / 16);
+        }
+        if (q32.q) {
+            q32.q += y * dim;
+            q32.d += y * (dim / 32);
+            q32.s += y * (dim / 32);
+        }
+    }
     pdl_wait_();
     pdl_trigger_();
     float ss = 0.0f;
@@ -130,10 +146,14 @@ __global__ void __launch_bounds__(QR_WARPS * 32) k_qk_rope(float *q, float *k, c
     __shared__ float inv_all[QR_WARPS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int head = blockIdx.x * QR_WARPS + warp;
+    // token blockIdx.y of a batch at position *pos_p + blockIdx.y
+    q += (size_t)blockIdx.y * n_heads * hd;
+    k += (size_t)blockIdx.y * n_kv * hd;
+    v += (size_t)blockIdx.y * n_kv * hd;
     pdl_wait_();
     pdl_trigger_();
     if (head >= n_heads + n_kv) return;
-    const int pos = (int)*pos_p;
+    const int pos = (int)*pos_p + (int)blockIdx.y;
     if (pos >= ctx) return;
     const bool isk = head >= n_heads;
     const int kh = head - n_heads;
@@ -186,9 +206,12 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
     extern __shared__ float sc[];  // [ctx]
     __shared__ float inv_s;
     const int h = blockIdx.x, tid = threadIdx.x;
+    // token blockIdx.y of a batch at position *pos_p + blockIdx.y: causal, it sees rows 0..its position
+    q += (size_t)blockIdx.y * n_heads * hd;
+    out += (size_t)blockIdx.y * n_heads * hd;
     pdl_wait_();
     pdl_trigger_();
-    const int pos = (int)*pos_p;
+    const int pos = (int)*pos_p + (int)blockIdx.y;
     if (pos >= ctx) return;
     const int seq = pos + 1, kvd = n_kv * hd;
     const int kvh = h / (n_heads / n_kv);
@@ -622,16 +645,27 @@ unsigned cdiv_u(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
 }  // namespace
 
 void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float eps, float *normed, XQW q256,
-                      XQW q32, bool serial, cudaStream_t st) {
-    launch_pdl_(k_rmsnorm_q, dim3(1), dim3(RN_THREADS), (size_t)dim * 4, st, x, add, w, dim, eps, normed, q256, q32,
-                (int)serial);
+                      XQW q32, bool serial, cudaStream_t st, int rows) {
+    launch_pdl_(k_rmsnorm_q, dim3(1, rows), dim3(RN_THREADS), (size_t)dim * 4, st, x, add, w, dim, eps, normed, q256,
+                q32, (int)serial);
 }
 
 void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const float *kn, int n_heads, int n_kv,
                     int hd, int rope_dim, int neox, const float *rope, float eps, const uint32_t *pos, int ctx,
-                    float *kc, float *vc, cudaStream_t st) {
-    launch_pdl_(k_qk_rope, dim3(cdiv_u(n_heads + n_kv, QR_WARPS)), dim3(QR_WARPS * 32), 0, st, q, k, v, qn, kn,
+                    float *kc, float *vc, cudaStream_t st, int ntok) {
+    launch_pdl_(k_qk_rope, dim3(cdiv_u(n_heads + n_kv, QR_WARPS), ntok), dim3(QR_WARPS * 32), 0, st, q, k, v, qn, kn,
                 n_heads, n_kv, hd, rope_dim, neox, rope, eps, pos, ctx, kc, vc);
+}
+
+void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st) {
+    static bool smem_set = false;
+    if (!smem_set) {
+        cudaFuncSetAttribute(k_attn_ordered, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_ORDERED_LIMIT * 4);
+        smem_set = true;
+    }
+    launch_pdl_(k_attn_ordered, dim3(n_heads, ntok), dim3(AT_THREADS), (size_t)ctx * 4, st, q, kc, vc, n_heads, n_kv,
+                hd, scale, pos, ctx, out);
 }
 
 void launch_mla_front(const float *kv_a, const float *kv_norm, int kvr, int rope, float eps, float *q, int n_heads,

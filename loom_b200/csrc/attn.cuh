@@ -14,8 +14,10 @@ namespace loom {
 // The sum of squares is the reference's serial sum when `serial`, else a
 // tree sum.
 constexpr int RN_SERIAL_MAX = 1024;  // default: serial up to this width
+// rows > 1: rows consecutive vectors (x, add, normed and the quantized forms
+// advance by one row each), one CTA per row.
 void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float eps, float *normed, XQW q256,
-                      XQW q32, bool serial, cudaStream_t st);
+                      XQW q32, bool serial, cudaStream_t st, int rows = 1);
 
 // Per head: optional RMSNorm over head_dim (headNorm, llama.zig:938-950, serial
 // sum), then RoPE at position *pos (ropeNeox / ropeNorm, llama.zig:830-858)
@@ -23,9 +25,16 @@ void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float
 // place on q [n_heads][hd] and k [n_kv][hd]; k and v are stored at row *pos of
 // this layer's caches kc / vc ([ctx][n_kv*hd]). Nothing is written when
 // *pos >= ctx.
+// ntok > 1: token i of a batch (q, k, v advance by one token's heads) at
+// position *pos + i.
 void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const float *kn, int n_heads, int n_kv,
                     int hd, int rope_dim, int neox, const float *rope, float eps, const uint32_t *pos, int ctx,
-                    float *kc, float *vc, cudaStream_t st);
+                    float *kc, float *vc, cudaStream_t st, int ntok = 1);
+// The ordered attention for a batch of ntok tokens at positions *pos + i
+// (llama.zig:1749-1774 stepBatch: token i sees cache rows 0..*pos + i only),
+// q and out [ntok][n_heads * hd]; one CTA per (query head, token).
+void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st);
 
 // Softmax attention of every query head over cache rows 0..*pos
 // (llama.zig:1171-1191), out [n_heads][hd].

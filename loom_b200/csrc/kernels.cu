@@ -410,16 +410,18 @@ __global__ void k_dequant(WDev w, uint64_t gb0, uint64_t nelem, float *out) {
 // Embedding lookup (llama.zig:1122 dequantRow of token_embd) of the token held
 // in device memory; an id >= vocab reads row vocab - 1 (the caller's contract
 // is id < vocab; this only keeps the read inside the tensor).
+// row blockIdx.y: token tok[y] into x + y * dim (one row per token of a batch)
 __global__ void k_embed(WDev w, int dim, const uint32_t *tok, int vocab, float *x) {
-    const uint32_t t = min(*tok, (uint32_t)(vocab - 1));
+    x += (size_t)blockIdx.y * dim;
+    const uint32_t t = min(tok[blockIdx.y], (uint32_t)(vocab - 1));
     const int be = block_elems(w.type);
     const uint64_t gb0 = (uint64_t)t * (dim / be);
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < dim; e += gridDim.x * blockDim.x)
         x[e] = dequant_at(w, gb0 + e / be, e % be);
 }
 
-void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st) {
-    k_embed<<<cdiv(dim, 256), 256, 0, st>>>(w, dim, tok, vocab, x);
+void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st, int ntok) {
+    k_embed<<<dim3(cdiv(dim, 256), ntok), 256, 0, st>>>(w, dim, tok, vocab, x);
     count_launch();
 }
 

@@ -47,8 +47,8 @@ void launch_dequant(const WDev &w, uint64_t gb0, uint64_t nblk, float *out, cuda
 void launch_mla_absorb(const WDev &w, int kvr, int nope, int vd, int kd, int n_heads, const float *q, float *qa,
                        cudaStream_t st);
 void launch_mla_wv(const WDev &w, int kvr, int nope, int vd, int n_heads, const XQ &x, float *out, cudaStream_t st);
-// row *tok of a [vocab][dim] tensor into x (embedding lookup)
-void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st);
+// row tok[i] of a [vocab][dim] tensor into x + i * dim, i < ntok (embedding lookup)
+void launch_embed(const WDev &w, int dim, const uint32_t *tok, int vocab, float *x, cudaStream_t st, int ntok = 1);
 // act[i] = silu(g[i]) * u[i]
 void launch_swiglu(const float *g, const float *u, int n, float *act, cudaStream_t st);
 void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind256, int8_t *q, float *d,

@@ -107,6 +107,13 @@ struct Model {
     cudaGraphExec_t exec = nullptr;
     uint64_t exec_gen = 0;
     int calls = 0;
+    size_t max_ffn = 0, max_ne = 1, max_nu = 1;  // the MoE layers' largest shape (scratch sizing)
+    // batched prefill (loom_cuda_model_prefill): row buffers for up to pf_cap tokens
+    size_t pf_cap = 0;
+    float *pf_x[2] = {nullptr, nullptr}, *pf_normed = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr,
+          *pf_att = nullptr, *pf_proj = nullptr, *pf_zero = nullptr;
+    XQW pf_n256{}, pf_n32{}, pf_a256{}, pf_a32{};
+    uint32_t *pf_tok = nullptr, *pf_pos = nullptr;
 };
 
 std::unordered_map<uint64_t, Model *> g_models;
@@ -339,6 +346,82 @@ int run_step(Model &m, const uint32_t *tok, const uint32_t *pos, float *logits, 
     return LOOM_CUDA_OK;
 }
 
+// A matrix times ntok token rows: out[k * rows + r] (ggml.matmul, ggml.zig:504: bit-identical to
+// ntok matvecs); xf are the f32 rows, x256 / x32 their quantized forms (token stride = one row).
+void matmul_rows(const Mat &m, const float *xf, const XQW &x256, const XQW &x32, int ntok, float *out,
+                 cudaStream_t st) {
+    if (m.type == T_F32) {
+        launch_mm_f32(reinterpret_cast<const float *>(m.w.q), m.rows, m.cols, xf, ntok, out, st);
+    } else if (m.type == T_Q5_0) {
+        launch_mm_q50(m.w, 0, m.rows, m.cols, xf, ntok, out, st);
+    } else {
+        const XQ x = act256(m.type) ? XQ{x256.q, x256.d, x256.s, m.cols, m.cols / 256, m.cols / 16, 1}
+                                    : XQ{x32.q, x32.d, x32.s, m.cols, m.cols / 32, m.cols / 32, 0};
+        launch_mm(m.w, 0, m.rows, m.cols, x, ntok, out, st);
+    }
+}
+
+int alloc_prefill(Model &m, size_t n) {
+    if (n <= m.pf_cap) return 0;
+    const size_t dim = m.dim, qd = m.nh * m.hd, kvd = m.nkv * m.hd;
+    int rc = 0;
+    if ((rc = dalloc(m, m.pf_x[0], n * dim)) || (rc = dalloc(m, m.pf_x[1], n * dim)) ||
+        (rc = dalloc(m, m.pf_normed, n * dim)) || (rc = dalloc(m, m.pf_q, n * qd)) || (rc = dalloc(m, m.pf_k, n * kvd)) ||
+        (rc = dalloc(m, m.pf_v, n * kvd)) || (rc = dalloc(m, m.pf_att, n * qd)) || (rc = dalloc(m, m.pf_proj, n * dim)) ||
+        (rc = dalloc(m, m.pf_zero, n, true)) || (rc = dalloc(m, m.pf_tok, n)) || (rc = dalloc(m, m.pf_pos, 1)) ||
+        (rc = alloc_xq(m, m.pf_n256, n * dim, true)) || (rc = alloc_xq(m, m.pf_n32, n * dim, false)) ||
+        (rc = alloc_xq(m, m.pf_a256, n * qd, true)) || (rc = alloc_xq(m, m.pf_a32, n * qd, false)))
+        return rc;
+    m.pf_cap = n;
+    return 0;
+}
+
+// llama.zig:1698-1825 stepBatch: n tokens at positions pos_base .. pos_base + n - 1 through the
+// model layer by layer (every token's row through a layer before the next layer), the KV cache
+// rows appended, each token attending causally to rows 0..its position; the last token's logits.
+// Per layer: RMSNorm of every row (+ quantization), q/k/v as matmuls over the rows (bit-identical
+// to per-row matvecs), headNorm + RoPE + cache append per token, the ordered attention per
+// (head, token), the output projection as a matmul, the residual add and the FFN RMSNorm, then
+// the MoE (or dense) FFN on all rows through the expert-major batch path (the reference runs it
+// token by token through the single-token path: the same integer arithmetic, except the
+// tensor cores' fp16 down projection when the experts average >= 16 tokens).
+int run_prefill(Model &m, int n, cudaStream_t st) {
+    const int dim = (int)m.dim, nh = (int)m.nh, nkv = (int)m.nkv, hd = (int)m.hd, qd = nh * hd;
+    const size_t layer_stride = m.ctx * m.nkv * m.hd;
+    const XQW none{};
+    launch_embed(m.embd.w, dim, m.pf_tok, (int)m.vocab, m.pf_x[0], st, n);
+    int cur = 0;
+    for (size_t li = 0; li < m.n_layers; li++) {
+        const LayerRt &l = m.L[li];
+        float *x = m.pf_x[cur];
+        launch_rmsnorm_q(x, nullptr, l.attn_norm, dim, m.eps, m.pf_normed, m.need256 ? m.pf_n256 : none,
+                         m.need32 ? m.pf_n32 : none, m.serial_norm, st, n);
+        matmul_rows(l.wq, m.pf_normed, m.pf_n256, m.pf_n32, n, m.pf_q, st);
+        matmul_rows(l.wk, m.pf_normed, m.pf_n256, m.pf_n32, n, m.pf_k, st);
+        matmul_rows(l.wv, m.pf_normed, m.pf_n256, m.pf_n32, n, m.pf_v, st);
+        float *kc = m.kc + li * layer_stride, *vc = m.vc + li * layer_stride;
+        launch_qk_rope(m.pf_q, m.pf_k, m.pf_v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps,
+                       m.pf_pos, (int)m.ctx, kc, vc, st, n);
+        launch_attention_ordered_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.pf_pos, (int)m.ctx, m.pf_att, n, st);
+        if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
+            const bool k256 = act256(l.wo.type);
+            const XQW &a = k256 ? m.pf_a256 : m.pf_a32;
+            launch_quant_act(m.pf_att, n, qd, qd, k256, a.q, a.d, a.s, k256 ? qd / 256 : qd / 32, k256 ? qd / 16 : qd / 32,
+                             st);
+        }
+        matmul_rows(l.wo, m.pf_att, m.pf_a256, m.pf_a32, n, m.pf_proj, st);
+        // x += proj (llama.zig:1781), then the FFN norm of every row
+        launch_rmsnorm_q(x, m.pf_proj, l.ffn_norm, dim, m.eps, m.pf_normed, none, none, m.serial_norm, st, n);
+        float *xn = m.pf_x[cur ^ 1];
+        if (int rc = loom_cuda_moe_forward(&l.moe, m.pf_normed, (size_t)n, xn, x, l.dense ? m.pf_zero : nullptr, nullptr,
+                                           st))
+            return rc;
+        cur ^= 1;
+    }
+    MCK(cudaGetLastError());
+    return cur;  // the buffer holding the final rows
+}
+
 Model *find(uint64_t h) {
     auto it = g_models.find(h);
     return it == g_models.end() ? nullptr : it->second;
@@ -498,6 +581,9 @@ int loom_cuda_model_create(const loom_model_desc *d, uint64_t *handle) {
         need_kind(l.wo.type, m->att256, m->att32);
         m->L.push_back(l);
     }
+    m->max_ffn = max_ffn;
+    m->max_ne = max_ne;
+    m->max_nu = max_nu;
     need_kind(m->out.type, m->need256, m->need32);
     if ((m->need256 && dim % 256) || (m->att256 && hv % 256))
         return bail(rt_decline("a K-quant projection needs a width that is a multiple of 256"));
@@ -743,6 +829,48 @@ int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *l
     MCK(rt_wait());
     if (next) *next = m->io_host[2];
     if (logits) std::memcpy(logits, m->h_logits, m->vocab * 4);
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_model_prefill(uint64_t handle, const uint32_t *tokens, size_t n, size_t pos_base, float *logits,
+                            uint32_t *next) {
+    if (int rc = rt_need_init()) return rc;
+    Model *mp = find(handle);
+    if (!mp) return rt_decline("unknown model handle");
+    Model &m = *mp;
+    if (m.mla) return rt_decline("prefill: multi-head latent attention models decode token by token");
+    if (m.persistent) return rt_decline("prefill: not with the persistent whole-token kernel");
+    if (!tokens || n == 0) return rt_decline("prefill: no tokens");
+    if (pos_base + n > m.ctx) return rt_decline("prefill: positions beyond the context");
+    for (size_t i = 0; i < n; i++)
+        if (tokens[i] >= m.vocab) return rt_decline("prefill: token id out of range");
+    if ((size_t)ATT_ORDERED_LIMIT < m.ctx) return rt_decline("prefill: context beyond the ordered attention's limit");
+    if (int rc = alloc_prefill(m, n)) return rc;
+    if (int rc = loom_cuda_reserve(n, m.dim, std::max<size_t>(m.max_ffn, 1), m.max_ne, m.max_nu)) return rc;
+    cudaStream_t st = rt_stream(nullptr);
+    const uint32_t pb = (uint32_t)pos_base;
+    MCK(cudaMemcpyAsync(m.pf_tok, tokens, n * 4, cudaMemcpyHostToDevice, st));
+    MCK(cudaMemcpyAsync(m.pf_pos, &pb, 4, cudaMemcpyHostToDevice, st));
+    const int cur = run_prefill(m, (int)n, st);
+    if (cur < 0 || cur > 1) return cur;
+    // the last token: final RMSNorm, the head, the argmax (llama.zig:1820-1824)
+    const XQW none{};
+    XQW o256 = none, o32 = none;
+    if (m.out.type != T_F32 && m.out.type != T_Q5_0) {
+        if (act256(m.out.type))
+            o256 = m.n256;
+        else
+            o32 = m.n32;
+    }
+    launch_rmsnorm_q(m.pf_x[cur] + (n - 1) * m.dim, nullptr, m.out_norm, (int)m.dim, m.eps, m.normed, o256, o32,
+                     m.serial_norm, st);
+    matvec(m.out, m.normed, m.n256, m.n32, m.logits, st);
+    if (int rc = loom_cuda_argmax(m.logits, m.vocab, m.io_dev + 2, st)) return rc;
+    if (logits) MCK(cudaMemcpyAsync(logits, m.logits, m.vocab * 4, cudaMemcpyDeviceToHost, st));
+    uint32_t nx = 0;
+    MCK(cudaMemcpyAsync(&nx, m.io_dev + 2, 4, cudaMemcpyDeviceToHost, st));
+    MCK(cudaStreamSynchronize(st));
+    if (next) *next = nx;
     return LOOM_CUDA_OK;
 }
 

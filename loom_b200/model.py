@@ -288,6 +288,17 @@ class DeviceModel:
                                                     C.byref(nxt)), "model_decode")
         return nxt.value, lg
 
+    def prefill(self, tokens, pos_base: int = 0, logits: bool = False):
+        """Batched prefill of `tokens` at positions pos_base.. (llama.zig stepBatch): returns
+        (greedy next token, the last token's logits or None)."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        nxt = C.c_uint32(0)
+        lg = np.empty(self.spec.vocab, np.float32) if logits else None
+        _lib.must(_lib.lib().loom_cuda_model_prefill(self.handle, t.ctypes.data_as(C.c_void_p), t.size, pos_base,
+                                                     lg.ctypes.data_as(C.c_void_p) if logits else None,
+                                                     C.byref(nxt)), "model_prefill")
+        return nxt.value, lg
+
     def step(self, d_token, d_pos, d_logits=None, d_next=None, stream=None) -> None:
         """The step on device buffers (torch cuda tensors: int32 [1])."""
         from .device import _st

@@ -209,3 +209,99 @@ def test_mla_model_matches_oracle(be, orc, which, exact, tol, ctx, steps):
         assert rel_l2(c, cc) < tol and rel_l2(r, rc) < tol
     finally:
         dev.free()
+
+
+# ---- batched prefill (loom_cuda_model_prefill, llama.zig:1698 stepBatch) ----------------
+
+def _kv_rows(dev, spec, n):
+    return [dev.read_kv(li, p) for li in range(spec.n_layers) for p in range(n)]
+
+
+def test_prefill_matches_token_by_token(be):
+    """The reference's own invariant (llama.zig:2206 "batched prefill matches
+    token-by-token prefill"): the tiny llama's 8-token prompt through the
+    batched prefill equals 8 decode steps bit for bit -- the last logits and
+    every cache row -- and both continue to the same 16 greedy tokens."""
+    spec = tiny_llama(ctx_len=256)
+    rng = np.random.default_rng(1)
+    prompt = [int(t) for t in rng.integers(1, 32000, size=8)]
+    a, b = DeviceModel(spec), DeviceModel(spec)
+    try:
+        na, la = a.prefill(prompt, 0, logits=True)
+        for p, t in enumerate(prompt):
+            nb, lb = b.decode(t, p, logits=True)
+        assert na == nb
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+        for (ka, va), (kb, vb) in zip(_kv_rows(a, spec, 8), _kv_rows(b, spec, 8)):
+            assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+        ta, tb, pos = na, nb, len(prompt)
+        for _ in range(16):
+            ta, _ = a.decode(ta, pos)
+            tb, _ = b.decode(tb, pos)
+            assert ta == tb
+            pos += 1
+    finally:
+        a.free()
+        b.free()
+
+
+def test_prefill_matches_oracle_and_greedy(be, orc):
+    """Prefill logits against the oracle fed the same prompt token by token
+    (2e-3), then 24 greedy tokens decoded after the prefill equal the
+    oracle's."""
+    spec = tiny_llama(ctx_len=256)
+    rng = np.random.default_rng(5)
+    prompt = [int(t) for t in rng.integers(1, 32000, size=12)]
+    ref = _runner(spec, orc)
+    for p, t in enumerate(prompt):
+        want = ref.step(t, p)
+    dev = DeviceModel(spec)
+    try:
+        nxt, got = dev.prefill(prompt, 0, logits=True)
+        assert rel_l2(got, want) < TOL
+        assert nxt == int(np.argmax(want))
+        seq_ref, seq_dev, pos = [int(np.argmax(want))], [nxt], len(prompt)
+        for _ in range(24):
+            seq_ref.append(int(np.argmax(ref.step(seq_ref[-1], pos))))
+            seq_dev.append(dev.decode(seq_dev[-1], pos)[0])
+            pos += 1
+        assert seq_dev == seq_ref
+    finally:
+        dev.free()
+
+
+@pytest.mark.parametrize("arith", ["exact", "fp16"])
+def test_prefill_qwen3_shape(be, arith):
+    """Qwen3-30B-A3B shape (2 layers, 16 experts, ctx 640) with the
+    reference's order (exact_order): 100 prompt tokens through the batched
+    prefill -- 50 tokens per expert on average, so the experts run on the
+    tensor cores -- against 100 decode steps. Integer-exact tensor cores: bit
+    for bit, logits and cache rows; the default fp16 down projection: logits
+    within 2e-2 (operand rounding can move an int8 rounding of the next
+    layer's activation). Chunked (60 then 40 tokens at position 60) equals one
+    batch bit for bit."""
+    from loom_b200 import device as D
+    spec = qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096)
+    rng = np.random.default_rng(11)
+    prompt = [int(t) for t in rng.integers(0, spec.vocab, size=100)]
+    prev = D.tc_exact(1 if arith == "exact" else 0)
+    a, b, c = DeviceModel(spec, exact_order=True), DeviceModel(spec, exact_order=True), DeviceModel(spec, exact_order=True)
+    try:
+        na, la = a.prefill(prompt, 0, logits=True)
+        for p, t in enumerate(prompt):
+            nb, lb = b.decode(t, p, logits=True)
+        c.prefill(prompt[:60], 0)
+        nc, lc = c.prefill(prompt[60:], 60, logits=True)
+        assert np.array_equal(la.view(np.uint32), lc.view(np.uint32)) and na == nc
+        if arith == "exact":
+            assert np.array_equal(la.view(np.uint32), lb.view(np.uint32)) and na == nb
+            for (ka, va), (kb, vb) in zip(_kv_rows(a, spec, 100)[::7], _kv_rows(b, spec, 100)[::7]):
+                assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+        else:
+            assert rel_l2(la, lb) < 2e-2, rel_l2(la, lb)
+        assert a.error() == 0 and c.error() == 0
+    finally:
+        D.tc_exact(prev)
+        a.free()
+        b.free()
+        c.free()
