@@ -709,6 +709,50 @@ def cpu_model_baseline(spec, pos, reps=9):
                        f"{spec.n_layers} layers")}
 
 
+def prefill_bytes(spec, T: int) -> int:
+    """Algorithmic HBM bytes of a T-token prefill: every replicated weight once
+    (attention, norms, router, the head for the last token; T embedding rows),
+    each routed layer's expected distinct experts (n_expert (1 - (1 - n_used /
+    n_expert)^T)) once, the T cache rows written per layer."""
+    kvd = spec.n_kv_heads * spec.head_dim
+    touched = spec.n_expert * (1.0 - (1.0 - spec.n_used / spec.n_expert) ** T)
+    b = 0
+    for t in spec.plan():
+        if t.name == "token_embd":
+            b += t.nbytes // spec.vocab * T
+        elif t.planes > 1:
+            b += t.nbytes // t.planes * touched
+        else:
+            b += t.nbytes
+    return int(b + spec.n_layers * T * kvd * 4 * 2)
+
+
+def run_model_prefill(args, dev, spec, peak, peak_kind):
+    """A T-token prompt through the whole model at position 0 by the batched
+    prefill (loom_cuda_model_prefill: host token ids in, the last token's next
+    token out), wall clock of the synchronous call, median of 3 after one
+    warm-up."""
+    T = args.model_prefill
+    rng = np.random.default_rng(3)
+    prompt = [int(t) for t in rng.integers(0, spec.vocab, size=T)]
+    dev.prefill(prompt, 0)
+    ts = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        dev.prefill(prompt, 0)
+        ts.append(time.perf_counter() - t0)
+    sec = statistics.median(ts)
+    b = prefill_bytes(spec, T)
+    return {"workload": f"prefill of a {T}-token prompt through the full model (batched, layer-major)",
+            "tokens": T, "value": round(T / sec, 1), "unit": "tok/s", "ms_per_step": round(sec * 1e3, 3),
+            "engine": "loom_cuda_model_prefill: row-batched norms, tiled q/k/v/output matmuls, causal ordered "
+                      "attention per (head, token), experts on the tensor cores",
+            "roofline": {"bound": "hbm", "achieved": round(b / sec / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(b / sec / 1e9 / peak, 4), "peak_kind": peak_kind, "bytes_per_step": b},
+            "e2e": {"value": round(T / sec, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * T + 4,
+                    "d2h_bytes_per_step": 4}}
+
+
 def run_model(args):
     import torch
     import torch.distributed as dist
@@ -787,6 +831,12 @@ def run_model(args):
     bytes_step = model_bytes(spec, pos, n_local)
     achieved = bytes_step / (ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
+    prefill = None
+    if world == 1 and not ds_main and args.model_prefill > 0:
+        try:
+            prefill = run_model_prefill(args, dev, spec, peak, peak_kind)
+        except Exception as e:  # reported in the line, never fatal to the headline
+            prefill = {"error": f"{type(e).__name__}: {e}"[:300]}
     dev.free()
 
     ds = None
@@ -842,6 +892,8 @@ def run_model(args):
                              if k in moe}
     if ds:
         line["deepseek_v2_lite"] = ds
+    if prefill is not None:
+        line["prefill"] = prefill
     if world == 1 and not args.no_deepseek and not ds_main and args.v3_layers > 0:
         try:
             line["deepseek_v3_cut"] = run_model_deepseek(args, peak, peak_kind, which="v3")
@@ -982,6 +1034,8 @@ def main():
     ap.add_argument("--no-fill", action="store_true",
                     help="model workload: leave the KV cache unfilled (profiling captures only; the kernels and "
                          "bytes are the same, the cached values are zeros)")
+    ap.add_argument("--model-prefill", type=int, default=512,
+                    help="model workload: also time a prefill of this many tokens through the full model (0: skip)")
     ap.add_argument("--no-deepseek", action="store_true",
                     help="model workload: skip the DeepSeek-V2-Lite full-model sub-measurement")
     args = ap.parse_args()

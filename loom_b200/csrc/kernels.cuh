@@ -56,6 +56,9 @@ void launch_quant_act(const float *x, int ntok, int cols, int xstride, int kind2
 void launch_mm(const WDev &w, uint64_t gb_base, int rows, int cols, const XQ &x, int ntok, float *out,
                cudaStream_t st);
 void launch_mm_f32(const float *W, int rows, int cols, const float *xs, int ntok, float *out, cudaStream_t st);
+// launch_mm for many token rows (prefill.cu): weight and token tiles staged in shared memory;
+// Q4_K / Q6_K / Q8_0 / Q4_0 only (false: not launched, use launch_mm). Bit-identical to launch_mm.
+bool launch_mm_tiled(const WDev &w, int rows, int cols, const XQ &x, int ntok, float *out, cudaStream_t st);
 // Q5_0 on f32 activations (matvecQ50, ggml.zig:1673), out[k*rows + r]
 void launch_mm_q50(const WDev &w, uint64_t gb_base, int rows, int cols, const float *xs, int ntok, float *out,
                    cudaStream_t st);

@@ -357,7 +357,8 @@ void matmul_rows(const Mat &m, const float *xf, const XQW &x256, const XQW &x32,
     } else {
         const XQ x = act256(m.type) ? XQ{x256.q, x256.d, x256.s, m.cols, m.cols / 256, m.cols / 16, 1}
                                     : XQ{x32.q, x32.d, x32.s, m.cols, m.cols / 32, m.cols / 32, 0};
-        launch_mm(m.w, 0, m.rows, m.cols, x, ntok, out, st);
+        if (ntok < 8 || !launch_mm_tiled(m.w, m.rows, m.cols, x, ntok, out, st))
+            launch_mm(m.w, 0, m.rows, m.cols, x, ntok, out, st);
     }
 }
 
