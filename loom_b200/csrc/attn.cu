@@ -244,6 +244,70 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
     }
 }
 
+// Prefill form (batched causal attention, llama.zig:1759-1774 in another
+// order): one CTA per (KV head, token), one warp per query head of the group.
+// Each lane scores keys lane, lane + 32, ... (float4 rows from L2, fused
+// multiply-adds), the warp takes the maximum and the sum of e^(s - max), then
+// lane l accumulates dims 4l..4l+3 of sum_t p_t v_t over the positions. The
+// group's warps read the same key and value rows (L1 hits after the first).
+constexpr int AP_MAX_GQ = 16;
+__global__ void __launch_bounds__(AP_MAX_GQ * 32) k_attn_prefill(const float *q, const float *kc, const float *vc,
+                                                                 int n_heads, int n_kv, int hd, float scale,
+                                                                 const uint32_t *pos_p, int ctx, float *out) {
+    extern __shared__ float ap_sm[];  // per warp: the query head [hd], the scores [ctx]
+    const int g = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int GQ = n_heads / n_kv, h = g * GQ + w, kvd = n_kv * hd;
+    q += (size_t)blockIdx.y * n_heads * hd;
+    out += (size_t)blockIdx.y * n_heads * hd;
+    pdl_wait_();
+    pdl_trigger_();
+    const int pos = (int)*pos_p + (int)blockIdx.y;
+    if (pos >= ctx || w >= GQ) return;
+    const int seq = pos + 1;
+    float *qs = ap_sm + (size_t)w * (hd + ctx), *sc = qs + hd;
+    for (int i = lane; i < hd; i += 32) qs[i] = q[(size_t)h * hd + i];
+    __syncwarp();
+    const float *kb = kc + (size_t)g * hd, *vb = vc + (size_t)g * hd;
+    float m = -INFINITY;
+    for (int t = lane; t < seq; t += 32) {
+        const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)t * kvd);
+        float a0 = 0.f, a1 = 0.f;
+        for (int d4 = 0; d4 < hd / 4; d4++) {
+            const float4 k4 = __ldg(kr + d4);
+            const float4 x4 = *reinterpret_cast<const float4 *>(qs + 4 * d4);
+            a0 = fmaf(k4.x, x4.x, a0);
+            a1 = fmaf(k4.y, x4.y, a1);
+            a0 = fmaf(k4.z, x4.z, a0);
+            a1 = fmaf(k4.w, x4.w, a1);
+        }
+        const float s2 = (a0 + a1) * scale;
+        sc[t] = s2;
+        m = fmaxf(m, s2);
+    }
+    m = warp_max(m);
+    float sum = 0.0f;
+    for (int t = lane; t < seq; t += 32) {
+        const float e = exp_f(sc[t] - m);
+        sc[t] = e;
+        sum += e;
+    }
+    sum = warp_sum_f(sum);
+    __syncwarp();
+    const float inv = 1.0f / sum;
+    for (int d4 = lane; d4 < hd / 4; d4 += 32) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < seq; t++) {
+            const float p = sc[t];
+            const float4 v4 = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)t * kvd) + d4);
+            o.x = fmaf(p, v4.x, o.x);
+            o.y = fmaf(p, v4.y, o.y);
+            o.z = fmaf(p, v4.z, o.z);
+            o.w = fmaf(p, v4.w, o.w);
+        }
+        reinterpret_cast<float4 *>(out + (size_t)h * hd)[d4] = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+    }
+}
+
 // Split form: one CTA per (KV head g, chunk sp of ATT_CH cache rows). The
 // chunk's key and value rows are staged into shared memory with cp.async (all
 // of them in flight at once; keys at a padded row stride so a warp's rows fall
@@ -655,6 +719,20 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
                     float *kc, float *vc, cudaStream_t st, int ntok) {
     launch_pdl_(k_qk_rope, dim3(cdiv_u(n_heads + n_kv, QR_WARPS), ntok), dim3(QR_WARPS * 32), 0, st, q, k, v, qn, kn,
                 n_heads, n_kv, hd, rope_dim, neox, rope, eps, pos, ctx, kc, vc);
+}
+
+bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st) {
+    const int gq = n_heads / n_kv;
+    const size_t smem = (size_t)gq * (hd + ctx) * 4;
+    if (gq > AP_MAX_GQ || hd % 4 || smem > 200 * 1024) return false;
+    static bool smem_set = false;
+    if (!smem_set) {
+        cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        smem_set = true;
+    }
+    return launch_pdl_(k_attn_prefill, dim3(n_kv, ntok), dim3(gq * 32), smem, st, q, kc, vc, n_heads, n_kv, hd, scale,
+                       pos, ctx, out) == cudaSuccess;
 }
 
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,

@@ -33,6 +33,12 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 // The ordered attention for a batch of ntok tokens at positions *pos + i
 // (llama.zig:1749-1774 stepBatch: token i sees cache rows 0..*pos + i only),
 // q and out [ntok][n_heads * hd]; one CTA per (query head, token).
+// The same batch in another summation order (fused multiply-adds, tree sums),
+// one CTA per (KV head, token) with one warp per query head: false when the
+// shape does not fit (query heads per KV head > 16, hd not a multiple of 4, or
+// scores of the context beyond 200 KB of shared memory).
+bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st);
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st);
 

@@ -403,7 +403,10 @@ int run_prefill(Model &m, int n, cudaStream_t st) {
         float *kc = m.kc + li * layer_stride, *vc = m.vc + li * layer_stride;
         launch_qk_rope(m.pf_q, m.pf_k, m.pf_v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps,
                        m.pf_pos, (int)m.ctx, kc, vc, st, n);
-        launch_attention_ordered_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.pf_pos, (int)m.ctx, m.pf_att, n, st);
+        // the reference's order where the model keeps it (exact_order, short contexts); else the batched form
+        if (m.ordered_attn || !launch_attention_prefill_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.pf_pos, (int)m.ctx,
+                                                             m.pf_att, n, st))
+            launch_attention_ordered_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.pf_pos, (int)m.ctx, m.pf_att, n, st);
         if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
             const bool k256 = act256(l.wo.type);
             const XQW &a = k256 ? m.pf_a256 : m.pf_a32;

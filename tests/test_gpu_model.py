@@ -305,3 +305,30 @@ def test_prefill_qwen3_shape(be, arith):
         a.free()
         b.free()
         c.free()
+
+
+def test_prefill_batched_attention_form(be):
+    """The default form (ctx 640: the batched prefill attention, fused
+    multiply-adds and tree sums, beside the decode path's split attention):
+    120 prompt tokens through the prefill against 120 decode steps, logits
+    within 2e-2 (rounding differences can move an int8 rounding of a later
+    activation), the same greedy token when the top two logits are apart, and
+    the cache rows within 2e-3."""
+    spec = qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096)
+    rng = np.random.default_rng(13)
+    prompt = [int(t) for t in rng.integers(0, spec.vocab, size=120)]
+    a, b = DeviceModel(spec), DeviceModel(spec)
+    try:
+        na, la = a.prefill(prompt, 0, logits=True)
+        for p, t in enumerate(prompt):
+            nb, lb = b.decode(t, p, logits=True)
+        assert np.all(np.isfinite(la)) and rel_l2(la, lb) < 2e-2, rel_l2(la, lb)
+        top = np.sort(lb)[-2:]
+        if top[1] - top[0] > 1e-2 * max(1.0, abs(top[1])):
+            assert na == nb
+        for (ka, va), (kb, vb) in zip(_kv_rows(a, spec, 120)[::11], _kv_rows(b, spec, 120)[::11]):
+            assert rel_l2(ka, kb) < 1e-2 and rel_l2(va, vb) < 1e-2
+        assert a.error() == 0
+    finally:
+        a.free()
+        b.free()
