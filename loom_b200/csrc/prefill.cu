@@ -55,6 +55,86 @@ MtPlan mt_plan(int ty, int nb) {
     return MtPlan{};
 }
 
+// Q4_K rows [r0, r0 + nS) of the staged tile against up to MT_NT tokens at once:
+// lane u = (row, block) unpacks each 32-byte nibble fragment and its two
+// sub-block scales/mins once (QT<T_Q4_K>::part's arithmetic) and runs the
+// dp4a dots of every token against them; per token the integer sums I and M
+// are exact, so the block terms and their block-order sums equal ab_rows'.
+constexpr int MT_NT = 16;
+__device__ __noinline__ void q4k_rows_multi(const uint8_t *wq, int r0, int nS, int NB, const uint8_t *xt, size_t tb,
+                                            size_t q_bytes, size_t s_bytes, int nt, float (*tsm)[32], int lane,
+                                            float *out, int rows, int t0) {
+    const int u = lane;
+    if (u < nS * NB) {
+        const int s2 = u / NB, b = u - s2 * NB;
+        const uint8_t *blk = wq + ((size_t)(r0 + s2) * NB + b) * 144;
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+        int I[MT_NT], M[MT_NT];
+#pragma unroll
+        for (int t = 0; t < MT_NT; t++) I[t] = M[t] = 0;
+#pragma unroll 1
+        for (int sub = 0; sub < 8; sub++) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(blk + 16 + 16 * sub);
+            const int j = sub >> 1, hh = sub & 1;
+            const int l0 = (int)(q.x & 0x0F0F0F0Fu), l1 = (int)(q.y & 0x0F0F0F0Fu), l2 = (int)(q.z & 0x0F0F0F0Fu),
+                      l3 = (int)(q.w & 0x0F0F0F0Fu);
+            const int h0 = (int)((q.x >> 4) & 0x0F0F0F0Fu), h1 = (int)((q.y >> 4) & 0x0F0F0F0Fu),
+                      h2 = (int)((q.z >> 4) & 0x0F0F0F0Fu), h3 = (int)((q.w >> 4) & 0x0F0F0F0Fu);
+            int sc0, mn0, sc1, mn1;  // scaleMinK4 (ggml.zig:1332) for sub-blocks 2j and 2j+1
+            if (j < 2) {
+                const uint32_t a = h.y >> (16 * j), c = h.z >> (16 * j);
+                sc0 = a & 63;
+                sc1 = (a >> 8) & 63;
+                mn0 = c & 63;
+                mn1 = (c >> 8) & 63;
+            } else {
+                const int jj = j - 2;
+                const uint32_t lo = h.w >> (16 * jj), hs = h.y >> (16 * jj), hm = h.z >> (16 * jj);
+                sc0 = (lo & 0xF) | (((hs >> 6) & 3) << 4);
+                mn0 = ((lo >> 4) & 0xF) | (((hm >> 6) & 3) << 4);
+                sc1 = ((lo >> 8) & 0xF) | (((hs >> 14) & 3) << 4);
+                mn1 = ((lo >> 12) & 0xF) | (((hm >> 14) & 3) << 4);
+            }
+#pragma unroll
+            for (int t = 0; t < MT_NT; t++) {
+                if (t < nt) {
+                    const uint8_t *xb = xt + (size_t)t * tb;
+                    const int8_t *xq = reinterpret_cast<const int8_t *>(xb) + (size_t)b * 272;
+                    const int4 xl = *reinterpret_cast<const int4 *>(xq + 64 * j + 16 * hh);
+                    const int4 xh = *reinterpret_cast<const int4 *>(xq + 64 * j + 32 + 16 * hh);
+                    int dl = dp4a(l0, xl.x, 0);
+                    dl = dp4a(l1, xl.y, dl);
+                    dl = dp4a(l2, xl.z, dl);
+                    dl = dp4a(l3, xl.w, dl);
+                    int dh = dp4a(h0, xh.x, 0);
+                    dh = dp4a(h1, xh.y, dh);
+                    dh = dp4a(h2, xh.z, dh);
+                    dh = dp4a(h3, xh.w, dh);
+                    const int32_t *xs = reinterpret_cast<const int32_t *>(xb + q_bytes) + b * 20;
+                    I[t] += sc0 * dl + sc1 * dh;
+                    M[t] += mn0 * xs[4 * j + hh] + mn1 * xs[4 * j + 2 + hh];
+                }
+            }
+        }
+        const float d = f16_to_f32((uint16_t)(h.x & 0xFFFF)), dmin = f16_to_f32((uint16_t)(h.x >> 16));
+#pragma unroll
+        for (int t = 0; t < MT_NT; t++)
+            if (t < nt) {
+                const float xd = reinterpret_cast<const float *>(xt + (size_t)t * tb + q_bytes + s_bytes)[b];
+                tsm[t][u] = fmul(xd, fsub(fmul(d, (float)I[t]), fmul(dmin, (float)M[t])));
+            }
+    }
+    __syncwarp();
+    if (lane < nS)
+        for (int t = 0; t < nt; t++) {
+            float a = 0.0f;
+#pragma unroll 1
+            for (int b = 0; b < NB; b++) a = fadd(b == 0 ? 0.0f : a, tsm[t][lane * NB + b]);  // from +0, block order
+            out[(size_t)(t0 + t) * rows + r0 + lane] = a;
+        }
+    __syncwarp();
+}
+
 template <int TY>
 __global__ void __launch_bounds__(MT_THREADS, 1) k_mm_tiled(WDev w, int rows, int nb, XQ x, int ntok, float *out,
                                                             int R, int NT, size_t w_off_sc, size_t w_off_d,
@@ -105,9 +185,18 @@ __global__ void __launch_bounds__(MT_THREADS, 1) k_mm_tiled(WDev w, int rows, in
     }
     __syncthreads();
     if (!mbar_wait(&bar, 0, 1u << 22)) return;  // a copy that never landed: the outputs stay unwritten
+    const int nS = max(1, min(4, 32 / nb)), nch = (nr + nS - 1) / nS;
+    if (TY == T_Q4_K && NT <= MT_NT) {  // fragments unpacked once for every token of the tile
+        __shared__ float tsm_nt[MT_WARPS][MT_NT][32];
+        for (int c = warp; c < nch; c += MT_WARPS) {
+            const int rc = c * nS;
+            q4k_rows_multi(sq, rc, min(nS, nr - rc), nb, xt, tb, q_bytes, s_bytes, nt, tsm_nt[warp], lane, out + r0, rows,
+                           t0);
+        }
+        return;
+    }
     const AbStage st{sq, TY == T_Q6_K ? ssc : nullptr, TY == T_Q4_K ? nullptr : sd, 0, nr, nb};
     // units: (token, chunk of rows) with at most 32 (row, block) lanes
-    const int nS = max(1, min(4, 32 / nb)), nch = (nr + nS - 1) / nS;
     for (int u = warp; u < nt * nch; u += MT_WARPS) {
         const int t = u / nch, rc = (u - t * nch) * nS, n = min(nS, nr - rc);
         const uint8_t *xb = xt + (size_t)t * tb;
