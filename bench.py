@@ -777,6 +777,12 @@ def run_model(args):
     if world > 1:
         D.ep_init(rank, world, dist)
     dev = DeviceModel(spec, expert_shard=shard)
+    if args.prefill_only:  # the batched prefill alone (profiling captures): its JSON object, then exit
+        if rank == 0:
+            peak, peak_kind = peaks()
+            print(json.dumps(run_model_prefill(args, dev, spec, peak, peak_kind)), flush=True)
+        dev.free()
+        return
     pos = spec.ctx_len - 1
     # fill the KV cache: greedy decode of positions 0 .. ctx-2 (every rank the same tokens)
     tok = 1
@@ -1036,6 +1042,8 @@ def main():
                          "bytes are the same, the cached values are zeros)")
     ap.add_argument("--model-prefill", type=int, default=512,
                     help="model workload: also time a prefill of this many tokens through the full model (0: skip)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="model workload: time only the --model-prefill prefill (profiling captures)")
     ap.add_argument("--no-deepseek", action="store_true",
                     help="model workload: skip the DeepSeek-V2-Lite full-model sub-measurement")
     args = ap.parse_args()
