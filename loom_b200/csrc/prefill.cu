@@ -19,7 +19,7 @@ namespace loom {
 namespace {
 
 constexpr int MT_WARPS = 8, MT_THREADS = MT_WARPS * 32;
-constexpr size_t MT_SMEM_MAX = 200 * 1024;
+constexpr size_t MT_SMEM_MAX = 200 * 1024, MT_SMEM_TWO = 92 * 1024;
 
 struct MtPlan {
     int R = 0, NT = 0;  // rows, tokens per tile
@@ -37,8 +37,11 @@ __host__ __device__ inline size_t mt_tok_bytes(int ty, int nb) {
            (((size_t)nb * 4 + 15) & ~size_t(15));
 }
 
+// The largest tile that lets two CTAs share an SM (16 warps to hide the dots' latencies), else
+// the largest that fits one.
 MtPlan mt_plan(int ty, int nb) {
     const size_t qb = layout_qbytes(ty);
+    for (size_t cap : {MT_SMEM_TWO, MT_SMEM_MAX})
     for (int R : {64, 32, 16}) {
         for (int NT : {16, 8}) {
             MtPlan c;
@@ -49,7 +52,7 @@ MtPlan mt_plan(int ty, int nb) {
             c.d_bytes = ty == T_Q4_K ? 0 : al128((size_t)R * nb * 2);
             c.x_bytes = al128((size_t)NT * mt_tok_bytes(ty, nb));
             c.smem = c.w_bytes + c.sc_bytes + c.d_bytes + c.x_bytes;
-            if (c.smem <= MT_SMEM_MAX) return c;
+            if (c.smem <= cap) return c;
         }
     }
     return MtPlan{};
@@ -136,7 +139,7 @@ __device__ __noinline__ void q4k_rows_multi(const uint8_t *wq, int r0, int nS, i
 }
 
 template <int TY>
-__global__ void __launch_bounds__(MT_THREADS, 1) k_mm_tiled(WDev w, int rows, int nb, XQ x, int ntok, float *out,
+__global__ void __launch_bounds__(MT_THREADS, 2) k_mm_tiled(WDev w, int rows, int nb, XQ x, int ntok, float *out,
                                                             int R, int NT, size_t w_off_sc, size_t w_off_d,
                                                             size_t x_off) {
     extern __shared__ __align__(128) uint8_t sm[];
