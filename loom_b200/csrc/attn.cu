@@ -250,11 +250,15 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
 // multiply-adds), the warp takes the maximum and the sum of e^(s - max), then
 // lane l accumulates dims 4l..4l+3 of sum_t p_t v_t over the positions. The
 // group's warps read the same key and value rows (L1 hits after the first).
+// HD > 0: the head width at compile time (loops unrolled, loads in flight together); 0: hd.
 constexpr int AP_MAX_GQ = 16;
+template <int HD>
 __global__ void __launch_bounds__(AP_MAX_GQ * 32) k_attn_prefill(const float *q, const float *kc, const float *vc,
-                                                                 int n_heads, int n_kv, int hd, float scale,
-                                                                 const uint32_t *pos_p, int ctx, float *out) {
-    extern __shared__ float ap_sm[];  // per warp: the query head [hd], the scores [ctx]
+                                                                 int n_heads, int n_kv, int hd_, float scale,
+                                                                 const uint32_t *pos_p, int ctx, float *out,
+                                                                 int smax) {
+    extern __shared__ float ap_sm[];  // per warp: the query head [hd], the scores [smax]
+    const int hd = HD > 0 ? HD : hd_;
     const int g = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int GQ = n_heads / n_kv, h = g * GQ + w, kvd = n_kv * hd;
     q += (size_t)blockIdx.y * n_heads * hd;
@@ -264,25 +268,50 @@ __global__ void __launch_bounds__(AP_MAX_GQ * 32) k_attn_prefill(const float *q,
     const int pos = (int)*pos_p + (int)blockIdx.y;
     if (pos >= ctx || w >= GQ) return;
     const int seq = pos + 1;
-    float *qs = ap_sm + (size_t)w * (hd + ctx), *sc = qs + hd;
+    if (seq > smax) return;  // (the launch sized the scores for the batch's last position)
+    float *qs = ap_sm + (size_t)w * (hd + smax), *sc = qs + hd;
     for (int i = lane; i < hd; i += 32) qs[i] = q[(size_t)h * hd + i];
     __syncwarp();
     const float *kb = kc + (size_t)g * hd, *vb = vc + (size_t)g * hd;
     float m = -INFINITY;
-    for (int t = lane; t < seq; t += 32) {
-        const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)t * kvd);
-        float a0 = 0.f, a1 = 0.f;
-        for (int d4 = 0; d4 < hd / 4; d4++) {
-            const float4 k4 = __ldg(kr + d4);
-            const float4 x4 = *reinterpret_cast<const float4 *>(qs + 4 * d4);
-            a0 = fmaf(k4.x, x4.x, a0);
-            a1 = fmaf(k4.y, x4.y, a1);
-            a0 = fmaf(k4.z, x4.z, a0);
-            a1 = fmaf(k4.w, x4.w, a1);
+    // scores of 512 keys at a time, key lane + 32 k in acc[k]; the query read from shared memory
+    // once per 32 dims (a broadcast) into registers, not once per key
+    for (int tb = 0; tb < seq; tb += 512) {
+        float acc[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) acc[k] = 0.0f;
+        for (int c = 0; c < hd; c += 32) {
+            const int cw = min(32, hd - c);
+            float4 qr[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                qr[i] = 4 * i < cw ? *reinterpret_cast<const float4 *>(qs + c + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int t = tb + lane + 32 * k;
+                if (t < seq) {
+                    const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)t * kvd + c);
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        if (4 * i < cw) {
+                            const float4 k4 = __ldg(kr + i);
+                            acc[k] = fmaf(k4.x, qr[i].x, acc[k]);
+                            acc[k] = fmaf(k4.y, qr[i].y, acc[k]);
+                            acc[k] = fmaf(k4.z, qr[i].z, acc[k]);
+                            acc[k] = fmaf(k4.w, qr[i].w, acc[k]);
+                        }
+                }
+            }
         }
-        const float s2 = (a0 + a1) * scale;
-        sc[t] = s2;
-        m = fmaxf(m, s2);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const int t = tb + lane + 32 * k;
+            if (t < seq) {
+                const float s2 = acc[k] * scale;
+                sc[t] = s2;
+                m = fmaxf(m, s2);
+            }
+        }
     }
     m = warp_max(m);
     float sum = 0.0f;
@@ -296,7 +325,21 @@ __global__ void __launch_bounds__(AP_MAX_GQ * 32) k_attn_prefill(const float *q,
     const float inv = 1.0f / sum;
     for (int d4 = lane; d4 < hd / 4; d4 += 32) {
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t = 0; t < seq; t++) {
+        const int seq4 = seq & ~3;
+#pragma unroll 2
+        for (int t = 0; t < seq4; t += 4) {  // four weights per shared-memory read
+            const float4 p4 = *reinterpret_cast<const float4 *>(sc + t);
+            const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 v4 = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)(t + u) * kvd) + d4);
+                o.x = fmaf(pp[u], v4.x, o.x);
+                o.y = fmaf(pp[u], v4.y, o.y);
+                o.z = fmaf(pp[u], v4.z, o.z);
+                o.w = fmaf(pp[u], v4.w, o.w);
+            }
+        }
+        for (int t = seq4; t < seq; t++) {
             const float p = sc[t];
             const float4 v4 = __ldg(reinterpret_cast<const float4 *>(vb + (size_t)t * kvd) + d4);
             o.x = fmaf(p, v4.x, o.x);
@@ -722,17 +765,20 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 }
 
 bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
-                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st) {
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, int max_pos,
+                                   cudaStream_t st) {
     const int gq = n_heads / n_kv;
-    const size_t smem = (size_t)gq * (hd + ctx) * 4;
+    const int smax = ((max_pos + 1 < ctx ? max_pos + 1 : ctx) + 3) & ~3;  // scores of the batch's last position at most
+    const size_t smem = (size_t)gq * (hd + smax) * 4;
     if (gq > AP_MAX_GQ || hd % 4 || smem > 200 * 1024) return false;
     static bool smem_set = false;
     if (!smem_set) {
-        cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_attn_prefill<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         smem_set = true;
     }
-    return launch_pdl_(k_attn_prefill, dim3(n_kv, ntok), dim3(gq * 32), smem, st, q, kc, vc, n_heads, n_kv, hd, scale,
-                       pos, ctx, out) == cudaSuccess;
+    return launch_pdl_(hd == 128 ? k_attn_prefill<128> : k_attn_prefill<0>, dim3(n_kv, ntok), dim3(gq * 32), smem, st,
+                       q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx, out, smax) == cudaSuccess;
 }
 
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,

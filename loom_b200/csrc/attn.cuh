@@ -37,8 +37,10 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 // one CTA per (KV head, token) with one warp per query head: false when the
 // shape does not fit (query heads per KV head > 16, hd not a multiple of 4, or
 // scores of the context beyond 200 KB of shared memory).
+// max_pos: the batch's last position (host-side bound of the scores' room).
 bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
-                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st);
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, int max_pos,
+                                   cudaStream_t st);
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st);
 

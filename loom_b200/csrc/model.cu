@@ -386,7 +386,7 @@ int alloc_prefill(Model &m, size_t n) {
 // the MoE (or dense) FFN on all rows through the expert-major batch path (the reference runs it
 // token by token through the single-token path: the same integer arithmetic, except the
 // tensor cores' fp16 down projection when the experts average >= 16 tokens).
-int run_prefill(Model &m, int n, cudaStream_t st) {
+int run_prefill(Model &m, int n, int pos_base, cudaStream_t st) {
     const int dim = (int)m.dim, nh = (int)m.nh, nkv = (int)m.nkv, hd = (int)m.hd, qd = nh * hd;
     const size_t layer_stride = m.ctx * m.nkv * m.hd;
     const XQW none{};
@@ -405,7 +405,7 @@ int run_prefill(Model &m, int n, cudaStream_t st) {
                        m.pf_pos, (int)m.ctx, kc, vc, st, n);
         // the reference's order where the model keeps it (exact_order, short contexts); else the batched form
         if (m.ordered_attn || !launch_attention_prefill_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.pf_pos, (int)m.ctx,
-                                                             m.pf_att, n, st))
+                                                             m.pf_att, n, pos_base + n - 1, st))
             launch_attention_ordered_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.pf_pos, (int)m.ctx, m.pf_att, n, st);
         if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
             const bool k256 = act256(l.wo.type);
@@ -855,7 +855,7 @@ int loom_cuda_model_prefill(uint64_t handle, const uint32_t *tokens, size_t n, s
     const uint32_t pb = (uint32_t)pos_base;
     MCK(cudaMemcpyAsync(m.pf_tok, tokens, n * 4, cudaMemcpyHostToDevice, st));
     MCK(cudaMemcpyAsync(m.pf_pos, &pb, 4, cudaMemcpyHostToDevice, st));
-    const int cur = run_prefill(m, (int)n, st);
+    const int cur = run_prefill(m, (int)n, (int)pos_base, st);
     if (cur < 0 || cur > 1) return cur;
     // the last token: final RMSNorm, the head, the argmax (llama.zig:1820-1824)
     const XQW none{};
