@@ -7,6 +7,8 @@
 // order where that is cheap (RMSNorm up to 1024 wide, head norms, the
 // ordered attention: dotF32 scores, serial softmax sum, axpy in position
 // order); the wide RMSNorm and the split attention use tree / chunked sums.
+#include <cstdlib>
+
 #include "attn.cuh"
 #include "devutil.cuh"
 #include "pdl.cuh"
@@ -348,6 +350,113 @@ __global__ void __launch_bounds__(AP_MAX_GQ * 32) k_attn_prefill(const float *q,
             o.w = fmaf(p, v4.w, o.w);
         }
         reinterpret_cast<float4 *>(out + (size_t)h * hd)[d4] = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+    }
+}
+
+// Prefill form for GQA groups of 8 heads of 128 (the Qwen3 shape), tiled:
+// one CTA per (KV head, 8 consecutive tokens), warp w = token t0 + w with all
+// 8 query heads of the group. Key and value rows go through shared memory in
+// chunks of 32 positions, read once for the tile's 64 query rows (instead of
+// once per warp of every token); per query row a running maximum and sum
+// (online softmax) and the output dims 4l..4l+3 of every head in lane l.
+constexpr int APT_TOK = 8, APT_GQ = 8, APT_HD = 128, APT_CH = 32, APT_KS = APT_HD + 4;
+constexpr size_t APT_SMEM = (size_t)(APT_CH * APT_KS + APT_CH * APT_HD + APT_TOK * APT_GQ * APT_HD + APT_TOK * APT_GQ * APT_CH) * 4;
+__global__ void __launch_bounds__(APT_TOK * 32) k_attn_prefill_tile(const float *q, const float *kc, const float *vc,
+                                                                    int n_heads, int n_kv, float scale,
+                                                                    const uint32_t *pos_p, int ctx, int ntok, float *out) {
+    extern __shared__ __align__(16) float apt[];
+    float *sK = apt, *sV = sK + APT_CH * APT_KS, *sQ = sV + APT_CH * APT_HD, *sP = sQ + APT_TOK * APT_GQ * APT_HD;
+    const int g = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int kvd = n_kv * APT_HD, t0 = blockIdx.y * APT_TOK;
+    pdl_wait_();
+    pdl_trigger_();
+    const int pos0 = (int)*pos_p;
+    const int tok = t0 + w, p = pos0 + tok;  // this warp's token and position
+    const bool live = tok < ntok && p < ctx;
+    const int last = min(pos0 + min(t0 + APT_TOK, ntok) - 1, ctx - 1);  // the tile's last position
+    // the tile's query rows: token t, head hh at sQ[(t * 8 + hh) * 128]
+    for (int i = tid; i < APT_TOK * APT_GQ * APT_HD / 4; i += APT_TOK * 32) {
+        const int t = i / (APT_GQ * APT_HD / 4), r = i - t * (APT_GQ * APT_HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + t < ntok)
+            v = reinterpret_cast<const float4 *>(q + (size_t)(t0 + t) * n_heads * APT_HD + (size_t)g * APT_GQ * APT_HD)[r];
+        reinterpret_cast<float4 *>(sQ)[i] = v;
+    }
+    float m[APT_GQ], l[APT_GQ];
+    float4 o[APT_GQ];
+#pragma unroll
+    for (int h = 0; h < APT_GQ; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.0f;
+        o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float *qw = sQ + (size_t)w * APT_GQ * APT_HD;
+    float *pw = sP + (size_t)w * APT_GQ * APT_CH;
+    for (int c0 = 0; c0 <= last; c0 += APT_CH) {
+        __syncthreads();  // the previous chunk's rows are no longer read
+        for (int i = tid; i < APT_CH * APT_HD / 4; i += APT_TOK * 32) {
+            const int j = i / (APT_HD / 4), d4 = i - j * (APT_HD / 4);
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (c0 + j <= last) {
+                kv = __ldg(reinterpret_cast<const float4 *>(kc + (size_t)(c0 + j) * kvd + (size_t)g * APT_HD) + d4);
+                vv = __ldg(reinterpret_cast<const float4 *>(vc + (size_t)(c0 + j) * kvd + (size_t)g * APT_HD) + d4);
+            }
+            *reinterpret_cast<float4 *>(sK + j * APT_KS + 4 * d4) = kv;
+            reinterpret_cast<float4 *>(sV)[i] = vv;
+        }
+        __syncthreads();
+        if (!live || c0 > p) continue;  // warp-uniform: every key of the chunk is past this token
+        // scores: lane = key c0 + lane, all 8 heads
+        float sc[APT_GQ];
+#pragma unroll
+        for (int h = 0; h < APT_GQ; h++) sc[h] = 0.0f;
+        const float *kr = sK + lane * APT_KS;
+#pragma unroll 4
+        for (int d = 0; d < APT_HD; d += 4) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+#pragma unroll
+            for (int h = 0; h < APT_GQ; h++) {
+                const float4 q4 = *reinterpret_cast<const float4 *>(qw + h * APT_HD + d);
+                sc[h] = fmaf(k4.x, q4.x, fmaf(k4.y, q4.y, fmaf(k4.z, q4.z, fmaf(k4.w, q4.w, sc[h]))));
+            }
+        }
+        const bool valid = c0 + lane <= p;
+#pragma unroll
+        for (int h = 0; h < APT_GQ; h++) {
+            const float s2 = valid ? sc[h] * scale : -INFINITY;
+            const float mc = warp_max(s2), mn = fmaxf(m[h], mc);
+            const float e = valid ? exp_f(s2 - mn) : 0.0f;
+            const float corr = m[h] == -INFINITY ? 0.0f : exp_f(m[h] - mn);
+            l[h] = l[h] * corr + warp_sum_f(e);
+            o[h].x *= corr;
+            o[h].y *= corr;
+            o[h].z *= corr;
+            o[h].w *= corr;
+            m[h] = mn;
+            pw[h * APT_CH + lane] = e;
+        }
+        __syncwarp();
+        // o[h] += sum_j e[h][j] v_j, dims 4 lane .. 4 lane + 3
+        const int jn = min(APT_CH, p - c0 + 1);
+        for (int j = 0; j < jn; j++) {
+            const float4 v4 = reinterpret_cast<const float4 *>(sV + j * APT_HD)[lane];
+#pragma unroll
+            for (int h = 0; h < APT_GQ; h++) {
+                const float e = pw[h * APT_CH + j];
+                o[h].x = fmaf(e, v4.x, o[h].x);
+                o[h].y = fmaf(e, v4.y, o[h].y);
+                o[h].z = fmaf(e, v4.z, o[h].z);
+                o[h].w = fmaf(e, v4.w, o[h].w);
+            }
+        }
+        __syncwarp();
+    }
+    if (!live) return;
+#pragma unroll
+    for (int h = 0; h < APT_GQ; h++) {
+        const float inv = 1.0f / l[h];
+        reinterpret_cast<float4 *>(out + (size_t)tok * n_heads * APT_HD + (size_t)(g * APT_GQ + h) * APT_HD)[lane] =
+            make_float4(o[h].x * inv, o[h].y * inv, o[h].z * inv, o[h].w * inv);
     }
 }
 
@@ -768,6 +877,15 @@ bool launch_attention_prefill_rows(const float *q, const float *kc, const float 
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, int max_pos,
                                    cudaStream_t st) {
     const int gq = n_heads / n_kv;
+    if (gq == APT_GQ && hd == APT_HD && !getenv("LOOM_CUDA_NO_ATT_TILE")) {
+        static bool set = false;
+        if (!set) {
+            cudaFuncSetAttribute(k_attn_prefill_tile, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)APT_SMEM);
+            set = true;
+        }
+        return launch_pdl_(k_attn_prefill_tile, dim3(n_kv, cdiv_u(ntok, APT_TOK)), dim3(APT_TOK * 32), APT_SMEM, st, q,
+                           kc, vc, n_heads, n_kv, scale, pos, ctx, ntok, out) == cudaSuccess;
+    }
     const int smax = ((max_pos + 1 < ctx ? max_pos + 1 : ctx) + 3) & ~3;  // scores of the batch's last position at most
     const size_t smem = (size_t)gq * (hd + smax) * 4;
     if (gq > AP_MAX_GQ || hd % 4 || smem > 200 * 1024) return false;
