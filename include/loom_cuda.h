@@ -406,6 +406,14 @@ int loom_cuda_model_decode(uint64_t handle, uint32_t token, size_t pos, float *l
  * larger n (not for use inside a stream capture). */
 int loom_cuda_model_prefill(uint64_t handle, const uint32_t *tokens, size_t n, size_t pos_base, float *logits,
                             uint32_t *next);
+/* Batched decode of B sequences (llama.zig:1939 decodeBatch): row b is
+ * sequence b's token at position positions[b], with its own KV cache (B
+ * caches, zeroed, allocated by the first call, which fixes the largest B;
+ * separate from the single-sequence cache of loom_cuda_model_decode). Every
+ * row's logits (host [B][vocab] f32, or NULL) and greedy next token (host
+ * [B], or NULL). Synchronous. Declines MLA models. */
+int loom_cuda_model_decode_batch(uint64_t handle, const uint32_t *tokens, const uint32_t *positions, size_t B,
+                                 float *logits, uint32_t *next);
 /* Copy one cache row (layer, pos) of keys and values (n_kv*hd f32 each; with
  * MLA the compressed row, kv_lora f32, and the rope row, rope_dim f32) to the
  * host -- the read-back that keeps a host copy authoritative (mlaReadCache,

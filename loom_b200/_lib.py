@@ -161,6 +161,7 @@ def lib() -> C.CDLL:
         "loom_cuda_model_decode": (i, [u64, C.c_uint32, sz, vp, C.POINTER(C.c_uint32)]),
         "loom_cuda_model_read_kv": (i, [u64, sz, sz, vp, vp]),
         "loom_cuda_model_prefill": (i, [u64, vp, sz, sz, vp, C.POINTER(C.c_uint32)]),
+        "loom_cuda_model_decode_batch": (i, [u64, vp, vp, sz, vp, vp]),
         "loom_cuda_model_free": (i, [u64]),
         "loom_cuda_model_error": (i, [u64]),
         "loom_cuda_model_trace": (i, [u64, i, vp, sz]),

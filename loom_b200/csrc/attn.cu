@@ -143,7 +143,8 @@ constexpr int MAX_HD = 256;
 __global__ void __launch_bounds__(QR_WARPS * 32) k_qk_rope(float *q, float *k, const float *v, const float *qn,
                                                           const float *kn, int n_heads, int n_kv, int hd,
                                                           int rope_dim, int neox, const float *rope, float eps,
-                                                          const uint32_t *pos_p, int ctx, float *kc, float *vc) {
+                                                          const uint32_t *pos_p, int ctx, float *kc, float *vc,
+                                                          int pos_rows, size_t cache_stride) {
     __shared__ float hv_all[QR_WARPS][MAX_HD];
     __shared__ float inv_all[QR_WARPS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -152,10 +153,13 @@ __global__ void __launch_bounds__(QR_WARPS * 32) k_qk_rope(float *q, float *k, c
     q += (size_t)blockIdx.y * n_heads * hd;
     k += (size_t)blockIdx.y * n_kv * hd;
     v += (size_t)blockIdx.y * n_kv * hd;
+    kc += blockIdx.y * cache_stride;
+    vc += blockIdx.y * cache_stride;
     pdl_wait_();
     pdl_trigger_();
     if (head >= n_heads + n_kv) return;
-    const int pos = (int)*pos_p + (int)blockIdx.y;
+    // row blockIdx.y: position pos_p[y] of its own cache (a batch of sequences, pos_rows) or *pos_p + y
+    const int pos = pos_rows ? (int)pos_p[blockIdx.y] : (int)*pos_p + (int)blockIdx.y;
     if (pos >= ctx) return;
     const bool isk = head >= n_heads;
     const int kh = head - n_heads;
@@ -203,7 +207,8 @@ constexpr int MAX_GQA = 16;
 // Ordered form: one CTA per query head.
 __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, const float *kc, const float *vc,
                                                             int n_heads, int n_kv, int hd, float scale,
-                                                            const uint32_t *pos_p, int ctx, float *out) {
+                                                            const uint32_t *pos_p, int ctx, float *out, int pos_rows,
+                                                            size_t cache_stride) {
     __shared__ float qs[MAX_HD];
     extern __shared__ float sc[];  // [ctx]
     __shared__ float inv_s;
@@ -211,9 +216,12 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_ordered(const float *q, con
     // token blockIdx.y of a batch at position *pos_p + blockIdx.y: causal, it sees rows 0..its position
     q += (size_t)blockIdx.y * n_heads * hd;
     out += (size_t)blockIdx.y * n_heads * hd;
+    kc += blockIdx.y * cache_stride;
+    vc += blockIdx.y * cache_stride;
     pdl_wait_();
     pdl_trigger_();
-    const int pos = (int)*pos_p + (int)blockIdx.y;
+    // row blockIdx.y: position pos_p[y] of its own cache (a batch of sequences, pos_rows) or *pos_p + y
+    const int pos = pos_rows ? (int)pos_p[blockIdx.y] : (int)*pos_p + (int)blockIdx.y;
     if (pos >= ctx) return;
     const int seq = pos + 1, kvd = n_kv * hd;
     const int kvh = h / (n_heads / n_kv);
@@ -258,16 +266,19 @@ template <int HD>
 __global__ void __launch_bounds__(AP_MAX_GQ * 32) k_attn_prefill(const float *q, const float *kc, const float *vc,
                                                                  int n_heads, int n_kv, int hd_, float scale,
                                                                  const uint32_t *pos_p, int ctx, float *out,
-                                                                 int smax) {
+                                                                 int smax, int pos_rows, size_t cache_stride) {
     extern __shared__ float ap_sm[];  // per warp: the query head [hd], the scores [smax]
     const int hd = HD > 0 ? HD : hd_;
     const int g = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int GQ = n_heads / n_kv, h = g * GQ + w, kvd = n_kv * hd;
     q += (size_t)blockIdx.y * n_heads * hd;
     out += (size_t)blockIdx.y * n_heads * hd;
+    kc += blockIdx.y * cache_stride;
+    vc += blockIdx.y * cache_stride;
     pdl_wait_();
     pdl_trigger_();
-    const int pos = (int)*pos_p + (int)blockIdx.y;
+    // row blockIdx.y: position pos_p[y] of its own cache (a batch of sequences, pos_rows) or *pos_p + y
+    const int pos = pos_rows ? (int)pos_p[blockIdx.y] : (int)*pos_p + (int)blockIdx.y;
     if (pos >= ctx || w >= GQ) return;
     const int seq = pos + 1;
     if (seq > smax) return;  // (the launch sized the scores for the batch's last position)
@@ -868,16 +879,16 @@ void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float
 
 void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const float *kn, int n_heads, int n_kv,
                     int hd, int rope_dim, int neox, const float *rope, float eps, const uint32_t *pos, int ctx,
-                    float *kc, float *vc, cudaStream_t st, int ntok) {
+                    float *kc, float *vc, cudaStream_t st, int ntok, int pos_rows, size_t cache_stride) {
     launch_pdl_(k_qk_rope, dim3(cdiv_u(n_heads + n_kv, QR_WARPS), ntok), dim3(QR_WARPS * 32), 0, st, q, k, v, qn, kn,
-                n_heads, n_kv, hd, rope_dim, neox, rope, eps, pos, ctx, kc, vc);
+                n_heads, n_kv, hd, rope_dim, neox, rope, eps, pos, ctx, kc, vc, pos_rows, cache_stride);
 }
 
 bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, int max_pos,
-                                   cudaStream_t st) {
+                                   cudaStream_t st, int pos_rows, size_t cache_stride) {
     const int gq = n_heads / n_kv;
-    if (gq == APT_GQ && hd == APT_HD && !getenv("LOOM_CUDA_NO_ATT_TILE")) {
+    if (!pos_rows && gq == APT_GQ && hd == APT_HD && !getenv("LOOM_CUDA_NO_ATT_TILE")) {
         static bool set = false;
         if (!set) {
             cudaFuncSetAttribute(k_attn_prefill_tile, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)APT_SMEM);
@@ -896,18 +907,19 @@ bool launch_attention_prefill_rows(const float *q, const float *kc, const float 
         smem_set = true;
     }
     return launch_pdl_(hd == 128 ? k_attn_prefill<128> : k_attn_prefill<0>, dim3(n_kv, ntok), dim3(gq * 32), smem, st,
-                       q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx, out, smax) == cudaSuccess;
+                       q, kc, vc, n_heads, n_kv, hd, scale, pos, ctx, out, smax, pos_rows, cache_stride) == cudaSuccess;
 }
 
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
-                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st) {
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st,
+                                   int pos_rows, size_t cache_stride) {
     static bool smem_set = false;
     if (!smem_set) {
         cudaFuncSetAttribute(k_attn_ordered, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_ORDERED_LIMIT * 4);
         smem_set = true;
     }
     launch_pdl_(k_attn_ordered, dim3(n_heads, ntok), dim3(AT_THREADS), (size_t)ctx * 4, st, q, kc, vc, n_heads, n_kv,
-                hd, scale, pos, ctx, out);
+                hd, scale, pos, ctx, out, pos_rows, cache_stride);
 }
 
 void launch_mla_front(const float *kv_a, const float *kv_norm, int kvr, int rope, float eps, float *q, int n_heads,
@@ -975,7 +987,7 @@ void launch_attention(const float *q, const float *kc, const float *vc, int n_he
             smem_set = true;
         }
         launch_pdl_(k_attn_ordered, dim3(n_heads), dim3(AT_THREADS), (size_t)ctx * 4, st, q, kc, vc, n_heads, n_kv,
-                    hd, scale, pos, ctx, out);
+                    hd, scale, pos, ctx, out, 0, (size_t)0);
         return;
     }
     const int nsplit = (ctx + ATT_CH - 1) / ATT_CH;

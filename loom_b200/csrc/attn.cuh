@@ -26,10 +26,12 @@ void launch_rmsnorm_q(float *x, const float *add, const float *w, int dim, float
 // this layer's caches kc / vc ([ctx][n_kv*hd]). Nothing is written when
 // *pos >= ctx.
 // ntok > 1: token i of a batch (q, k, v advance by one token's heads) at
-// position *pos + i.
+// position *pos + i; with pos_rows, token i is sequence i at position pos[i]
+// with its own cache rows at kc / vc + i * cache_stride (the same for the
+// attention launchers below).
 void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const float *kn, int n_heads, int n_kv,
                     int hd, int rope_dim, int neox, const float *rope, float eps, const uint32_t *pos, int ctx,
-                    float *kc, float *vc, cudaStream_t st, int ntok = 1);
+                    float *kc, float *vc, cudaStream_t st, int ntok = 1, int pos_rows = 0, size_t cache_stride = 0);
 // The ordered attention for a batch of ntok tokens at positions *pos + i
 // (llama.zig:1749-1774 stepBatch: token i sees cache rows 0..*pos + i only),
 // q and out [ntok][n_heads * hd]; one CTA per (query head, token).
@@ -40,9 +42,10 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 // max_pos: the batch's last position (host-side bound of the scores' room).
 bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, int max_pos,
-                                   cudaStream_t st);
+                                   cudaStream_t st, int pos_rows = 0, size_t cache_stride = 0);
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
-                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st);
+                                   float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st,
+                                   int pos_rows = 0, size_t cache_stride = 0);
 
 // Softmax attention of every query head over cache rows 0..*pos
 // (llama.zig:1171-1191), out [n_heads][hd].

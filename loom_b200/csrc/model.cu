@@ -114,6 +114,10 @@ struct Model {
           *pf_att = nullptr, *pf_proj = nullptr, *pf_zero = nullptr;
     XQW pf_n256{}, pf_n32{}, pf_a256{}, pf_a32{};
     uint32_t *pf_tok = nullptr, *pf_pos = nullptr;
+    // batched decode of many sequences (loom_cuda_model_decode_batch): their own caches
+    size_t bd_cap = 0;
+    float *bkc = nullptr, *bvc = nullptr, *bd_logits = nullptr;
+    uint32_t *bd_pos = nullptr, *bd_next = nullptr;
 };
 
 std::unordered_map<uint64_t, Model *> g_models;
@@ -424,6 +428,60 @@ int run_prefill(Model &m, int n, int pos_base, cudaStream_t st) {
     }
     MCK(cudaGetLastError());
     return cur;  // the buffer holding the final rows
+}
+
+// llama.zig:1939 decodeBatch: B sequences one token each, sequence b at position pos[b] with its
+// own KV cache (m.bkc / m.bvc: [B][layers][ctx][kv dim]); the prefill's row-batched kernels with
+// per-row positions and cache bases, the attention per (head or KV head, sequence), the FFN of
+// all B rows on the expert-major batch path, then every row's final norm, head and argmax.
+int run_decode_batch(Model &m, int B, cudaStream_t st) {
+    const int dim = (int)m.dim, nh = (int)m.nh, nkv = (int)m.nkv, hd = (int)m.hd, qd = nh * hd;
+    const size_t layer_stride = m.ctx * m.nkv * m.hd, seq_stride = m.n_layers * layer_stride;
+    const XQW none{};
+    launch_embed(m.embd.w, dim, m.pf_tok, (int)m.vocab, m.pf_x[0], st, B);
+    int cur = 0;
+    for (size_t li = 0; li < m.n_layers; li++) {
+        const LayerRt &l = m.L[li];
+        float *x = m.pf_x[cur];
+        launch_rmsnorm_q(x, nullptr, l.attn_norm, dim, m.eps, m.pf_normed, m.need256 ? m.pf_n256 : none,
+                         m.need32 ? m.pf_n32 : none, m.serial_norm, st, B);
+        matmul_rows(l.wq, m.pf_normed, m.pf_n256, m.pf_n32, B, m.pf_q, st);
+        matmul_rows(l.wk, m.pf_normed, m.pf_n256, m.pf_n32, B, m.pf_k, st);
+        matmul_rows(l.wv, m.pf_normed, m.pf_n256, m.pf_n32, B, m.pf_v, st);
+        float *kc = m.bkc + li * layer_stride, *vc = m.bvc + li * layer_stride;
+        launch_qk_rope(m.pf_q, m.pf_k, m.pf_v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps,
+                       m.bd_pos, (int)m.ctx, kc, vc, st, B, 1, seq_stride);
+        if (m.ordered_attn || !launch_attention_prefill_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.bd_pos, (int)m.ctx,
+                                                             m.pf_att, B, (int)m.ctx - 1, st, 1, seq_stride))
+            launch_attention_ordered_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.bd_pos, (int)m.ctx, m.pf_att, B, st, 1,
+                                          seq_stride);
+        if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
+            const bool k256 = act256(l.wo.type);
+            const XQW &a = k256 ? m.pf_a256 : m.pf_a32;
+            launch_quant_act(m.pf_att, B, qd, qd, k256, a.q, a.d, a.s, k256 ? qd / 256 : qd / 32, k256 ? qd / 16 : qd / 32,
+                             st);
+        }
+        matmul_rows(l.wo, m.pf_att, m.pf_a256, m.pf_a32, B, m.pf_proj, st);
+        launch_rmsnorm_q(x, m.pf_proj, l.ffn_norm, dim, m.eps, m.pf_normed, none, none, m.serial_norm, st, B);
+        float *xn = m.pf_x[cur ^ 1];
+        if (int rc = loom_cuda_moe_forward(&l.moe, m.pf_normed, (size_t)B, xn, x, l.dense ? m.pf_zero : nullptr, nullptr,
+                                           st))
+            return rc;
+        cur ^= 1;
+    }
+    XQW o256 = none, o32 = none;
+    if (m.out.type != T_F32 && m.out.type != T_Q5_0) {
+        if (act256(m.out.type))
+            o256 = m.pf_n256;
+        else
+            o32 = m.pf_n32;
+    }
+    launch_rmsnorm_q(m.pf_x[cur], nullptr, m.out_norm, dim, m.eps, m.pf_normed, o256, o32, m.serial_norm, st, B);
+    matmul_rows(m.out, m.pf_normed, m.pf_n256, m.pf_n32, B, m.bd_logits, st);
+    for (int b = 0; b < B; b++)
+        if (int rc = loom_cuda_argmax(m.bd_logits + (size_t)b * m.vocab, m.vocab, m.bd_next + b, st)) return rc;
+    MCK(cudaGetLastError());
+    return LOOM_CUDA_OK;
 }
 
 Model *find(uint64_t h) {
@@ -875,6 +933,39 @@ int loom_cuda_model_prefill(uint64_t handle, const uint32_t *tokens, size_t n, s
     MCK(cudaMemcpyAsync(&nx, m.io_dev + 2, 4, cudaMemcpyDeviceToHost, st));
     MCK(cudaStreamSynchronize(st));
     if (next) *next = nx;
+    return LOOM_CUDA_OK;
+}
+
+int loom_cuda_model_decode_batch(uint64_t handle, const uint32_t *tokens, const uint32_t *positions, size_t B,
+                                 float *logits, uint32_t *next) {
+    if (int rc = rt_need_init()) return rc;
+    Model *mp = find(handle);
+    if (!mp) return rt_decline("unknown model handle");
+    Model &m = *mp;
+    if (m.mla) return rt_decline("decode_batch: multi-head latent attention models decode one sequence");
+    if (m.persistent) return rt_decline("decode_batch: not with the persistent whole-token kernel");
+    if (!tokens || !positions || B == 0) return rt_decline("decode_batch: no sequences");
+    if (m.bd_cap && B > m.bd_cap) return rt_decline("decode_batch: more sequences than the first call's batch");
+    for (size_t i = 0; i < B; i++)
+        if (tokens[i] >= m.vocab || positions[i] >= m.ctx) return rt_decline("decode_batch: token or position out of range");
+    if ((size_t)ATT_ORDERED_LIMIT < m.ctx) return rt_decline("decode_batch: context beyond the ordered attention's limit");
+    if (int rc = alloc_prefill(m, B)) return rc;
+    if (!m.bd_cap) {  // the sequences' caches (zeroed), logits and next tokens, sized by the first call
+        const size_t cache = B * m.n_layers * m.ctx * m.nkv * m.hd;
+        int rc = 0;
+        if ((rc = dalloc(m, m.bkc, cache, true)) || (rc = dalloc(m, m.bvc, cache, true)) ||
+            (rc = dalloc(m, m.bd_logits, B * m.vocab)) || (rc = dalloc(m, m.bd_pos, B)) || (rc = dalloc(m, m.bd_next, B)))
+            return rc;
+        m.bd_cap = B;
+    }
+    if (int rc = loom_cuda_reserve(B, m.dim, std::max<size_t>(m.max_ffn, 1), m.max_ne, m.max_nu)) return rc;
+    cudaStream_t st = rt_stream(nullptr);
+    MCK(cudaMemcpyAsync(m.pf_tok, tokens, B * 4, cudaMemcpyHostToDevice, st));
+    MCK(cudaMemcpyAsync(m.bd_pos, positions, B * 4, cudaMemcpyHostToDevice, st));
+    if (int rc = run_decode_batch(m, (int)B, st)) return rc;
+    if (logits) MCK(cudaMemcpyAsync(logits, m.bd_logits, B * m.vocab * 4, cudaMemcpyDeviceToHost, st));
+    if (next) MCK(cudaMemcpyAsync(next, m.bd_next, B * 4, cudaMemcpyDeviceToHost, st));
+    MCK(cudaStreamSynchronize(st));
     return LOOM_CUDA_OK;
 }
 

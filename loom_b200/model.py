@@ -299,6 +299,20 @@ class DeviceModel:
                                                      C.byref(nxt)), "model_prefill")
         return nxt.value, lg
 
+    def decode_batch(self, tokens, positions, logits: bool = False):
+        """One token for each of B sequences (row b: sequence b at positions[b], its own cache;
+        llama.zig decodeBatch): returns (next tokens [B], logits [B][vocab] or None)."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.uint32))
+        assert t.size == p.size
+        nxt = np.zeros(t.size, np.uint32)
+        lg = np.empty((t.size, self.spec.vocab), np.float32) if logits else None
+        _lib.must(_lib.lib().loom_cuda_model_decode_batch(self.handle, t.ctypes.data_as(C.c_void_p),
+                                                          p.ctypes.data_as(C.c_void_p), t.size,
+                                                          lg.ctypes.data_as(C.c_void_p) if logits else None,
+                                                          nxt.ctypes.data_as(C.c_void_p)), "model_decode_batch")
+        return nxt, lg
+
     def step(self, d_token, d_pos, d_logits=None, d_next=None, stream=None) -> None:
         """The step on device buffers (torch cuda tensors: int32 [1])."""
         from .device import _st

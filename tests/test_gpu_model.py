@@ -332,3 +332,57 @@ def test_prefill_batched_attention_form(be):
     finally:
         a.free()
         b.free()
+
+
+# ---- batched decode of many sequences (loom_cuda_model_decode_batch, llama.zig:1939) --------
+
+def test_decode_batch_matches_single_sequences(be):
+    """Three sequences of the tiny llama decoded together, one token each per
+    call, sequence 2 starting 5 positions later (its earlier cache rows zero,
+    as in a fresh single-sequence model): every row's logits equal the same
+    sequence decoded alone, bit for bit, over 12 steps, and so does the
+    greedy token."""
+    spec = tiny_llama(ctx_len=256)
+    rng = np.random.default_rng(21)
+    off = [0, 0, 5]
+    toks = rng.integers(1, 32000, size=(12, 3))
+    batch = DeviceModel(spec)
+    singles = [DeviceModel(spec) for _ in range(3)]
+    try:
+        for s in range(12):
+            pos = [s + o for o in off]
+            nxt, lg = batch.decode_batch(toks[s], pos, logits=True)
+            for b in range(3):
+                n1, l1 = singles[b].decode(int(toks[s, b]), pos[b], logits=True)
+                assert np.array_equal(lg[b].view(np.uint32), l1.view(np.uint32)), (s, b)
+                assert int(nxt[b]) == n1
+    finally:
+        batch.free()
+        for m in singles:
+            m.free()
+
+
+def test_decode_batch_qwen3_shape(be):
+    """Qwen3 shape (2 layers, 16 experts, ctx 640), 4 sequences at different
+    positions: the batched form (per-row attention against each sequence's
+    cache, the experts of all rows together) within 2e-2 of each sequence
+    decoded alone (the single-sequence path's split attention and fused
+    kernels round differently)."""
+    spec = qwen3_moe(n_layers=2, ctx_len=640, n_expert=16, vocab=4096)
+    rng = np.random.default_rng(22)
+    off = [0, 3, 7, 11]
+    toks = rng.integers(0, spec.vocab, size=(16, 4))
+    batch = DeviceModel(spec)
+    singles = [DeviceModel(spec) for _ in range(4)]
+    try:
+        for s in range(16):
+            pos = [s + o for o in off]
+            nxt, lg = batch.decode_batch(toks[s], pos, logits=True)
+            for b in range(4):
+                n1, l1 = singles[b].decode(int(toks[s, b]), pos[b], logits=True)
+                assert np.all(np.isfinite(lg[b])) and rel_l2(lg[b], l1) < 2e-2, (s, b, rel_l2(lg[b], l1))
+        assert batch.error() == 0
+    finally:
+        batch.free()
+        for m in singles:
+            m.free()
