@@ -753,6 +753,46 @@ def run_model_prefill(args, dev, spec, peak, peak_kind):
                     "d2h_bytes_per_step": 4}}
 
 
+def run_model_batch(args, dev, spec, peak, peak_kind):
+    """One decode step of B sequences through the whole model
+    (loom_cuda_model_decode_batch: B host tokens and positions in, B next tokens
+    out), every sequence at position ctx - 1 of its own cache (zeroed rows:
+    the same kernels and bytes as a filled one), wall clock of the synchronous
+    call, median of 5 after two warm-ups."""
+    B = args.model_batch
+    pos = spec.ctx_len - 1
+    rng = np.random.default_rng(4)
+    toks = [int(t) for t in rng.integers(0, spec.vocab, size=B)]
+    for _ in range(2):
+        dev.decode_batch(toks, [pos] * B)
+    ts = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        dev.decode_batch(toks, [pos] * B)
+        ts.append(time.perf_counter() - t0)
+    sec = statistics.median(ts)
+    kvd = spec.n_kv_heads * spec.head_dim
+    touched = spec.n_expert * (1.0 - (1.0 - spec.n_used / spec.n_expert) ** B)
+    b = 0
+    for t in spec.plan():
+        if t.name == "token_embd":
+            b += t.nbytes // spec.vocab * B
+        elif t.planes > 1:
+            b += t.nbytes // t.planes * touched
+        else:
+            b += t.nbytes
+    b = int(b + B * spec.n_layers * (pos + 2) * kvd * 4 * 2)  # every sequence's cache rows read, one written
+    return {"workload": f"decode of {B} sequences, one token each, at position {pos} of a {spec.ctx_len}-token "
+                        f"context (each its own cache)",
+            "tokens": B, "value": round(B / sec, 1), "unit": "tok/s", "ms_per_step": round(sec * 1e3, 3),
+            "engine": "loom_cuda_model_decode_batch: row-batched norms, tiled matmuls, per-row attention over each "
+                      "sequence's cache, the experts of all rows on the expert-major path, every row's head",
+            "roofline": {"bound": "hbm", "achieved": round(b / sec / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(b / sec / 1e9 / peak, 4), "peak_kind": peak_kind, "bytes_per_step": b},
+            "e2e": {"value": round(B / sec, 1), "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
+                    "d2h_bytes_per_step": 4 * B}}
+
+
 def run_model(args):
     import torch
     import torch.distributed as dist
@@ -837,7 +877,12 @@ def run_model(args):
     bytes_step = model_bytes(spec, pos, n_local)
     achieved = bytes_step / (ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
-    prefill = None
+    prefill = mbatch = None
+    if world == 1 and not ds_main and args.model_batch > 0:
+        try:
+            mbatch = run_model_batch(args, dev, spec, peak, peak_kind)
+        except Exception as e:  # reported in the line, never fatal to the headline
+            mbatch = {"error": f"{type(e).__name__}: {e}"[:300]}
     if world == 1 and not ds_main and args.model_prefill > 0:
         try:
             prefill = run_model_prefill(args, dev, spec, peak, peak_kind)
@@ -900,6 +945,8 @@ def run_model(args):
         line["deepseek_v2_lite"] = ds
     if prefill is not None:
         line["prefill"] = prefill
+    if mbatch is not None:
+        line["batch"] = mbatch
     if world == 1 and not args.no_deepseek and not ds_main and args.v3_layers > 0:
         try:
             line["deepseek_v3_cut"] = run_model_deepseek(args, peak, peak_kind, which="v3")
@@ -1042,6 +1089,8 @@ def main():
                          "bytes are the same, the cached values are zeros)")
     ap.add_argument("--model-prefill", type=int, default=512,
                     help="model workload: also time a prefill of this many tokens through the full model (0: skip)")
+    ap.add_argument("--model-batch", type=int, default=32,
+                    help="model workload: also time one decode step of this many sequences (0: skip)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="model workload: time only the --model-prefill prefill (profiling captures)")
     ap.add_argument("--no-deepseek", action="store_true",

@@ -487,9 +487,15 @@ __host__ __device__ constexpr int att_kstride(int hd) { return hd + 4; }
 
 __global__ void __launch_bounds__(AT_THREADS) k_attn_part(const float *q, const float *kc, const float *vc,
                                                          int n_heads, int n_kv, int hd, float scale,
-                                                         const uint32_t *pos_p, int ctx, int nsplit, float *part) {
+                                                         const uint32_t *pos_p, int ctx, int nsplit, float *part,
+                                                         int pos_rows, size_t cache_stride, size_t part_stride) {
     extern __shared__ __align__(16) float sm[];
     const int G = n_heads / n_kv, kvd = n_kv * hd, KS = att_kstride(hd);
+    // row blockIdx.z of a batch of sequences (pos_rows): its query, its cache, its records
+    q += (size_t)blockIdx.z * n_heads * hd;
+    kc += blockIdx.z * cache_stride;
+    vc += blockIdx.z * cache_stride;
+    part += blockIdx.z * part_stride;
     float *sK = sm;                      // [ATT_CH][KS]
     float *sV = sK + ATT_CH * KS;        // [ATT_CH][hd]
     float *qs = sV + ATT_CH * hd;        // [G][hd]
@@ -498,7 +504,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_part(const float *q, const 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait_();
     pdl_trigger_();
-    const int pos = (int)*pos_p;
+    const int pos = pos_rows ? (int)pos_p[blockIdx.z] : (int)*pos_p;
     if (pos >= ctx) return;
     const int seq = pos + 1, t0 = sp * ATT_CH;
     if (t0 >= seq) return;
@@ -588,14 +594,16 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_part(const float *q, const 
 // output projection (quantizeX256 / quantizeX), so no separate pass reads them.
 __global__ void __launch_bounds__(256) k_attn_merge(const float *part, int n_heads, int n_kv, int hd,
                                                    const uint32_t *pos_p, int ctx, int nsplit, float *out, XQW q256,
-                                                   XQW q32) {
+                                                   XQW q32, int pos_rows, size_t part_stride) {
     extern __shared__ float wsm[];  // [heads in CTA][nsplit] weights
     __shared__ float Ls[40];  // heads per CTA <= 256 / 8 + 1 (head_dim >= 8)
     __shared__ __align__(16) float val[256];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait_();
     pdl_trigger_();
-    const int pos = (int)*pos_p;
+    part += blockIdx.z * part_stride;  // row blockIdx.z of a batch of sequences (pos_rows)
+    out += (size_t)blockIdx.z * n_heads * hd;
+    const int pos = pos_rows ? (int)pos_p[blockIdx.z] : (int)*pos_p;
     if (pos >= ctx) return;
     const int G = n_heads / n_kv, qd = n_heads * hd;
     const int live = (pos + 1 + ATT_CH - 1) / ATT_CH;
@@ -1001,11 +1009,32 @@ void launch_attention(const float *q, const float *kc, const float *vc, int n_he
         part_smem_set = true;
     }
     launch_pdl_(k_attn_part, dim3(n_kv, nsplit), dim3(AT_THREADS), smem, st, q, kc, vc, n_heads, n_kv, hd, scale, pos,
-                ctx, nsplit, part);
+                ctx, nsplit, part, 0, (size_t)0, (size_t)0);
     const int qd = n_heads * hd;
     const int heads_per_cta = 256 / hd + 1 < n_heads ? 256 / hd + 1 : n_heads;
     launch_pdl_(k_attn_merge, dim3(cdiv_u(qd, 256)), dim3(256), (size_t)heads_per_cta * nsplit * 4, st, part, n_heads,
-                n_kv, hd, pos, ctx, nsplit, out, q256, q32);
+                n_kv, hd, pos, ctx, nsplit, out, q256, q32, 0, (size_t)0);
+}
+
+void launch_attention_split_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
+                                 float scale, const uint32_t *pos, int ctx, float *part, float *out, int nrows,
+                                 size_t cache_stride, cudaStream_t st) {
+    const int nsplit = (int)cdiv_u(ctx, ATT_CH), G = n_heads / n_kv;
+    const size_t smem = ((size_t)ATT_CH * att_kstride(hd) + (size_t)ATT_CH * hd + (size_t)G * hd + (size_t)G * ATT_CH) * 4;
+    static bool set = false;
+    if (!set) {
+        cudaFuncSetAttribute(k_attn_part, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (ATT_CH * att_kstride(MAX_HD) + ATT_CH * MAX_HD + MAX_GQA * MAX_HD + MAX_GQA * ATT_CH) * 4);
+        cudaFuncSetAttribute(k_attn_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        set = true;
+    }
+    const size_t part_stride = attn_part_floats(n_heads, n_kv, hd, ctx);
+    launch_pdl_(k_attn_part, dim3(n_kv, nsplit, nrows), dim3(AT_THREADS), smem, st, q, kc, vc, n_heads, n_kv, hd, scale,
+                pos, ctx, nsplit, part, 1, cache_stride, part_stride);
+    const int qd = n_heads * hd;
+    const int heads_per_cta = 256 / hd + 1 < n_heads ? 256 / hd + 1 : n_heads;
+    launch_pdl_(k_attn_merge, dim3(cdiv_u(qd, 256), 1, nrows), dim3(256), (size_t)heads_per_cta * nsplit * 4, st, part,
+                n_heads, n_kv, hd, pos, ctx, nsplit, out, XQW{}, XQW{}, 1, part_stride);
 }
 
 }  // namespace loom

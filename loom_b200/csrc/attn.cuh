@@ -43,6 +43,12 @@ void launch_qk_rope(float *q, float *k, const float *v, const float *qn, const f
 bool launch_attention_prefill_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, int max_pos,
                                    cudaStream_t st, int pos_rows = 0, size_t cache_stride = 0);
+// The split form (k_attn_part + k_attn_merge) for nrows sequences: row i at
+// position pos[i] of its own cache (kc / vc + i * cache_stride); part holds
+// nrows * attn_part_floats(...) floats; out [nrows][n_heads * hd], not quantized.
+void launch_attention_split_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
+                                 float scale, const uint32_t *pos, int ctx, float *part, float *out, int nrows,
+                                 size_t cache_stride, cudaStream_t st);
 void launch_attention_ordered_rows(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd,
                                    float scale, const uint32_t *pos, int ctx, float *out, int ntok, cudaStream_t st,
                                    int pos_rows = 0, size_t cache_stride = 0);

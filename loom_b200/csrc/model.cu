@@ -116,7 +116,7 @@ struct Model {
     uint32_t *pf_tok = nullptr, *pf_pos = nullptr;
     // batched decode of many sequences (loom_cuda_model_decode_batch): their own caches
     size_t bd_cap = 0;
-    float *bkc = nullptr, *bvc = nullptr, *bd_logits = nullptr;
+    float *bkc = nullptr, *bvc = nullptr, *bd_logits = nullptr, *bd_part = nullptr;
     uint32_t *bd_pos = nullptr, *bd_next = nullptr;
 };
 
@@ -451,10 +451,12 @@ int run_decode_batch(Model &m, int B, cudaStream_t st) {
         float *kc = m.bkc + li * layer_stride, *vc = m.bvc + li * layer_stride;
         launch_qk_rope(m.pf_q, m.pf_k, m.pf_v, l.qn, l.kn, nh, nkv, hd, (int)m.rope_dim, m.neox, m.rope, m.eps,
                        m.bd_pos, (int)m.ctx, kc, vc, st, B, 1, seq_stride);
-        if (m.ordered_attn || !launch_attention_prefill_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.bd_pos, (int)m.ctx,
-                                                             m.pf_att, B, (int)m.ctx - 1, st, 1, seq_stride))
+        if (m.ordered_attn)
             launch_attention_ordered_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.bd_pos, (int)m.ctx, m.pf_att, B, st, 1,
                                           seq_stride);
+        else  // the single-sequence step's split form, one grid over every sequence's chunks
+            launch_attention_split_rows(m.pf_q, kc, vc, nh, nkv, hd, m.scale, m.bd_pos, (int)m.ctx, m.bd_part, m.pf_att, B,
+                                        seq_stride, st);
         if (l.wo.type != T_F32 && l.wo.type != T_Q5_0) {
             const bool k256 = act256(l.wo.type);
             const XQW &a = k256 ? m.pf_a256 : m.pf_a32;
@@ -954,7 +956,8 @@ int loom_cuda_model_decode_batch(uint64_t handle, const uint32_t *tokens, const 
         const size_t cache = B * m.n_layers * m.ctx * m.nkv * m.hd;
         int rc = 0;
         if ((rc = dalloc(m, m.bkc, cache, true)) || (rc = dalloc(m, m.bvc, cache, true)) ||
-            (rc = dalloc(m, m.bd_logits, B * m.vocab)) || (rc = dalloc(m, m.bd_pos, B)) || (rc = dalloc(m, m.bd_next, B)))
+            (rc = dalloc(m, m.bd_logits, B * m.vocab)) || (rc = dalloc(m, m.bd_pos, B)) || (rc = dalloc(m, m.bd_next, B)) ||
+            (rc = dalloc(m, m.bd_part, B * attn_part_floats((int)m.nh, (int)m.nkv, (int)m.hd, (int)m.ctx))))
             return rc;
         m.bd_cap = B;
     }

@@ -38,9 +38,24 @@ __host__ __device__ inline size_t mt_tok_bytes(int ty, int nb) {
 }
 
 // The largest tile that lets two CTAs share an SM (16 warps to hide the dots' latencies), else
-// the largest that fits one.
-MtPlan mt_plan(int ty, int nb) {
+// the largest that fits one. A matrix far beyond L2 (an output head) takes every token of the
+// batch (up to 32) in one tile instead, so its weights cross HBM once.
+MtPlan mt_plan(int ty, int nb, int rows, int ntok) {
     const size_t qb = layout_qbytes(ty);
+    const size_t wbytes = (size_t)rows * nb * (qb + (ty == T_Q6_K ? 16 : 0) + (ty == T_Q4_K ? 0 : 2));
+    if (wbytes > ((size_t)32 << 20) && ntok > 16) {
+        for (int R : {64, 32, 16}) {
+            MtPlan c;
+            c.R = R;
+            c.NT = 32;
+            c.w_bytes = al128((size_t)R * nb * qb);
+            c.sc_bytes = ty == T_Q6_K ? al128((size_t)R * nb * 16) : 0;
+            c.d_bytes = ty == T_Q4_K ? 0 : al128((size_t)R * nb * 2);
+            c.x_bytes = al128((size_t)32 * mt_tok_bytes(ty, nb));
+            c.smem = c.w_bytes + c.sc_bytes + c.d_bytes + c.x_bytes;
+            if (c.smem <= MT_SMEM_MAX) return c;
+        }
+    }
     for (size_t cap : {MT_SMEM_TWO, MT_SMEM_MAX})
     for (int R : {64, 32, 16}) {
         for (int NT : {16, 8}) {
@@ -236,7 +251,7 @@ bool launch_mm_tiled(const WDev &w, int rows, int cols, const XQ &x, int ntok, f
     if (cols % be || x.kind256 != (mt_k256(ty) ? 1 : 0)) return false;
     const int nb = cols / be;
     if (nb > 64) return false;  // the per-warp term buffer
-    const MtPlan p = mt_plan(ty, nb);
+    const MtPlan p = mt_plan(ty, nb, rows, ntok);
     if (!p.R) return false;
     cudaError_t e = cudaSuccess;
     switch (ty) {
