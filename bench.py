@@ -817,10 +817,11 @@ def run_model(args):
     if world > 1:
         D.ep_init(rank, world, dist)
     dev = DeviceModel(spec, expert_shard=shard)
-    if args.prefill_only:  # the batched prefill alone (profiling captures): its JSON object, then exit
+    if args.prefill_only or args.batch_only:  # one sub-measurement alone (profiling captures), then exit
         if rank == 0:
             peak, peak_kind = peaks()
-            print(json.dumps(run_model_prefill(args, dev, spec, peak, peak_kind)), flush=True)
+            run = run_model_prefill if args.prefill_only else run_model_batch
+            print(json.dumps(run(args, dev, spec, peak, peak_kind)), flush=True)
         dev.free()
         return
     pos = spec.ctx_len - 1
@@ -1091,6 +1092,8 @@ def main():
                     help="model workload: also time a prefill of this many tokens through the full model (0: skip)")
     ap.add_argument("--model-batch", type=int, default=32,
                     help="model workload: also time one decode step of this many sequences (0: skip)")
+    ap.add_argument("--batch-only", action="store_true",
+                    help="model workload: time only the --model-batch decode step (profiling captures)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="model workload: time only the --model-prefill prefill (profiling captures)")
     ap.add_argument("--no-deepseek", action="store_true",

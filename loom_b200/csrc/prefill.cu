@@ -20,6 +20,7 @@ namespace {
 
 constexpr int MT_WARPS = 8, MT_THREADS = MT_WARPS * 32;
 constexpr size_t MT_SMEM_MAX = 200 * 1024, MT_SMEM_TWO = 92 * 1024;
+constexpr int MT_NT = 16;  // tokens a lane dots against one unpacked weight fragment
 
 struct MtPlan {
     int R = 0, NT = 0;  // rows, tokens per tile
@@ -38,8 +39,8 @@ __host__ __device__ inline size_t mt_tok_bytes(int ty, int nb) {
 }
 
 // The largest tile that lets two CTAs share an SM (16 warps to hide the dots' latencies), else
-// the largest that fits one. A matrix far beyond L2 (an output head) takes every token of the
-// batch (up to 32) in one tile instead, so its weights cross HBM once.
+// the largest that fits one. A matrix far beyond L2 (an output head) takes 16 tokens a tile with
+// the largest row tile that fits one CTA, so its weights cross HBM as few times as that allows.
 MtPlan mt_plan(int ty, int nb, int rows, int ntok) {
     const size_t qb = layout_qbytes(ty);
     const size_t wbytes = (size_t)rows * nb * (qb + (ty == T_Q6_K ? 16 : 0) + (ty == T_Q4_K ? 0 : 2));
@@ -47,11 +48,11 @@ MtPlan mt_plan(int ty, int nb, int rows, int ntok) {
         for (int R : {64, 32, 16}) {
             MtPlan c;
             c.R = R;
-            c.NT = 32;
+            c.NT = MT_NT;
             c.w_bytes = al128((size_t)R * nb * qb);
             c.sc_bytes = ty == T_Q6_K ? al128((size_t)R * nb * 16) : 0;
             c.d_bytes = ty == T_Q4_K ? 0 : al128((size_t)R * nb * 2);
-            c.x_bytes = al128((size_t)32 * mt_tok_bytes(ty, nb));
+            c.x_bytes = al128((size_t)MT_NT * mt_tok_bytes(ty, nb));
             c.smem = c.w_bytes + c.sc_bytes + c.d_bytes + c.x_bytes;
             if (c.smem <= MT_SMEM_MAX) return c;
         }
@@ -78,7 +79,6 @@ MtPlan mt_plan(int ty, int nb, int rows, int ntok) {
 // sub-block scales/mins once (QT<T_Q4_K>::part's arithmetic) and runs the
 // dp4a dots of every token against them; per token the integer sums I and M
 // are exact, so the block terms and their block-order sums equal ab_rows'.
-constexpr int MT_NT = 16;
 __device__ __noinline__ void q4k_rows_multi(const uint8_t *wq, int r0, int nS, int NB, const uint8_t *xt, size_t tb,
                                             size_t q_bytes, size_t s_bytes, int nt, float (*tsm)[32], int lane,
                                             float *out, int rows, int t0) {
@@ -153,6 +153,74 @@ __device__ __noinline__ void q4k_rows_multi(const uint8_t *wq, int r0, int nS, i
     __syncwarp();
 }
 
+// Q6_K likewise (QT<T_Q6_K>::part's arithmetic): each lane's (row, block) fragment -- 6-bit
+// quants rebuilt from the low and high planes, four int8 sub-block scales -- unpacked once for
+// every token of the tile; per token I = sum sc (q . x - 32 sum x), exact.
+__device__ __noinline__ void q6k_rows_multi(const AbStage &st, int r0, int nS, int NB, const uint8_t *xt, size_t tb,
+                                            size_t q_bytes, size_t s_bytes, int nt, float (*tsm)[32], int lane,
+                                            float *out, int rows, int t0) {
+    const int u = lane;
+    if (u < nS * NB) {
+        const int s2 = u / NB, b = u - s2 * NB, gb = (r0 + s2) * NB + b;
+        int I[MT_NT];
+#pragma unroll
+        for (int t = 0; t < MT_NT; t++) I[t] = 0;
+        const uint4 sv = *reinterpret_cast<const uint4 *>(st.sc + (size_t)gb * 16);
+#pragma unroll 1
+        for (int sub = 0; sub < 4; sub++) {
+            const int n = sub >> 1, hh = sub & 1;
+            const uint8_t *qb = st.q + (size_t)gb * 192;
+            const uint4 a4 = *reinterpret_cast<const uint4 *>(qb + 64 * n + 16 * hh);
+            const uint4 b4 = *reinterpret_cast<const uint4 *>(qb + 64 * n + 32 + 16 * hh);
+            const uint4 h4 = *reinterpret_cast<const uint4 *>(qb + 128 + 32 * n + 16 * hh);
+            const uint32_t A[4] = {a4.x, a4.y, a4.z, a4.w}, Bq[4] = {b4.x, b4.y, b4.z, b4.w}, H[4] = {h4.x, h4.y, h4.z, h4.w};
+            int w0[4], w1[4], w2[4], w3[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                w0[k] = (int)((A[k] & 0x0F0F0F0Fu) | ((H[k] & 0x03030303u) << 4));
+                w1[k] = (int)((Bq[k] & 0x0F0F0F0Fu) | (((H[k] >> 2) & 0x03030303u) << 4));
+                w2[k] = (int)(((A[k] >> 4) & 0x0F0F0F0Fu) | (((H[k] >> 4) & 0x03030303u) << 4));
+                w3[k] = (int)(((Bq[k] >> 4) & 0x0F0F0F0Fu) | (((H[k] >> 6) & 0x03030303u) << 4));
+            }
+            const uint32_t sw0 = n ? sv.z : sv.x, sw1 = n ? sv.w : sv.y;
+            const int c0 = (int)(int8_t)(sw0 >> (8 * hh)), c1 = (int)(int8_t)(sw0 >> (8 * (hh + 2)));
+            const int c2 = (int)(int8_t)(sw1 >> (8 * hh)), c3 = (int)(int8_t)(sw1 >> (8 * (hh + 2)));
+#pragma unroll
+            for (int t = 0; t < MT_NT; t++) {
+                if (t < nt) {
+                    const uint8_t *xbt = xt + (size_t)t * tb;
+                    const int8_t *xb = reinterpret_cast<const int8_t *>(xbt) + (size_t)b * 272 + 128 * n + 16 * hh;
+                    const int4 x0 = *reinterpret_cast<const int4 *>(xb), x1 = *reinterpret_cast<const int4 *>(xb + 32);
+                    const int4 x2 = *reinterpret_cast<const int4 *>(xb + 64), x3 = *reinterpret_cast<const int4 *>(xb + 96);
+                    int d0 = dp4a(w0[0], x0.x, 0), d1 = dp4a(w1[0], x1.x, 0), d2 = dp4a(w2[0], x2.x, 0),
+                        d3 = dp4a(w3[0], x3.x, 0);
+                    d0 = dp4a(w0[1], x0.y, d0); d1 = dp4a(w1[1], x1.y, d1); d2 = dp4a(w2[1], x2.y, d2); d3 = dp4a(w3[1], x3.y, d3);
+                    d0 = dp4a(w0[2], x0.z, d0); d1 = dp4a(w1[2], x1.z, d1); d2 = dp4a(w2[2], x2.z, d2); d3 = dp4a(w3[2], x3.z, d3);
+                    d0 = dp4a(w0[3], x0.w, d0); d1 = dp4a(w1[3], x1.w, d1); d2 = dp4a(w2[3], x2.w, d2); d3 = dp4a(w3[3], x3.w, d3);
+                    const int32_t *bs = reinterpret_cast<const int32_t *>(xbt + q_bytes) + b * 20 + 8 * n + hh;
+                    I[t] += c0 * (d0 - 32 * bs[0]) + c1 * (d1 - 32 * bs[2]) + c2 * (d2 - 32 * bs[4]) + c3 * (d3 - 32 * bs[6]);
+                }
+            }
+        }
+        const float d = f16_to_f32(st.d[gb]);
+#pragma unroll
+        for (int t = 0; t < MT_NT; t++)
+            if (t < nt) {
+                const float xd = reinterpret_cast<const float *>(xt + (size_t)t * tb + q_bytes + s_bytes)[b];
+                tsm[t][u] = fmul(fmul(xd, d), (float)I[t]);
+            }
+    }
+    __syncwarp();
+    if (lane < nS)
+        for (int t = 0; t < nt; t++) {
+            float a = 0.0f;
+#pragma unroll 1
+            for (int b = 0; b < NB; b++) a = fadd(b == 0 ? 0.0f : a, tsm[t][lane * NB + b]);  // from +0, block order
+            out[(size_t)(t0 + t) * rows + r0 + lane] = a;
+        }
+    __syncwarp();
+}
+
 template <int TY>
 __global__ void __launch_bounds__(MT_THREADS, 2) k_mm_tiled(WDev w, int rows, int nb, XQ x, int ntok, float *out,
                                                             int R, int NT, size_t w_off_sc, size_t w_off_d,
@@ -204,16 +272,20 @@ __global__ void __launch_bounds__(MT_THREADS, 2) k_mm_tiled(WDev w, int rows, in
     __syncthreads();
     if (!mbar_wait(&bar, 0, 1u << 22)) return;  // a copy that never landed: the outputs stay unwritten
     const int nS = max(1, min(4, 32 / nb)), nch = (nr + nS - 1) / nS;
-    if (TY == T_Q4_K && NT <= MT_NT) {  // fragments unpacked once for every token of the tile
+    const AbStage st{sq, TY == T_Q6_K ? ssc : nullptr, TY == T_Q4_K ? nullptr : sd, 0, nr, nb};
+    if ((TY == T_Q4_K || TY == T_Q6_K) && NT <= MT_NT) {  // fragments unpacked once for every token of the tile
         __shared__ float tsm_nt[MT_WARPS][MT_NT][32];
         for (int c = warp; c < nch; c += MT_WARPS) {
             const int rc = c * nS;
-            q4k_rows_multi(sq, rc, min(nS, nr - rc), nb, xt, tb, q_bytes, s_bytes, nt, tsm_nt[warp], lane, out + r0, rows,
-                           t0);
+            if (TY == T_Q4_K)
+                q4k_rows_multi(sq, rc, min(nS, nr - rc), nb, xt, tb, q_bytes, s_bytes, nt, tsm_nt[warp], lane, out + r0,
+                               rows, t0);
+            else
+                q6k_rows_multi(st, rc, min(nS, nr - rc), nb, xt, tb, q_bytes, s_bytes, nt, tsm_nt[warp], lane, out + r0,
+                               rows, t0);
         }
         return;
     }
-    const AbStage st{sq, TY == T_Q6_K ? ssc : nullptr, TY == T_Q4_K ? nullptr : sd, 0, nr, nb};
     // units: (token, chunk of rows) with at most 32 (row, block) lanes
     for (int u = warp; u < nt * nch; u += MT_WARPS) {
         const int t = u / nch, rc = (u - t * nch) * nS, n = min(nS, nr - rc);
