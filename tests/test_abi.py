@@ -37,6 +37,14 @@ def test_seam_declines_before_init():
     assert L.loom_cuda_register_arena(w.ctypes.data_as(C.c_void_p), w.nbytes) == _lib.DECLINED
     assert L.loom_cuda_materialize_arenas() == 0
     assert L.loom_cuda_take_cmdbuf_count() == 0
+    # the whole-model batch entries decline the same way, having done nothing
+    t = np.array([1, 2, 3], np.uint32)
+    nxt = np.zeros(3, np.uint32)
+    assert L.loom_cuda_model_prefill(7, t.ctypes.data_as(C.c_void_p), 3, 0, None,
+                                     nxt.ctypes.data_as(C.POINTER(C.c_uint32))) == _lib.DECLINED
+    assert L.loom_cuda_model_decode_batch(7, t.ctypes.data_as(C.c_void_p), t.ctypes.data_as(C.c_void_p), 3, None,
+                                          nxt.ctypes.data_as(C.c_void_p)) == _lib.DECLINED
+    assert list(nxt) == [0, 0, 0]
 
 
 def test_ctypes_structs_match_the_header(tmp_path):
